@@ -1,0 +1,418 @@
+"""Benchmark of the QSA sparse-attention hot path on B200 (one JSON line on stdout, rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|3|5]
+
+Default workload: decode of one token on one sparse-attention layer at
+163,840-token context, q8_0 KV, 16 query / 2 KV heads, head_dim 256, one 128-dim indexer head,
+top-64 of 2560 blocks of 64 cells + a 128-token window (67 blocks, 4288 cells).  A step is the
+whole node: append of the token's K/V/raw key (+ the pooled key of the block it completes),
+indexer scores + top-k, and split-K attention.  Metric: microseconds per layer-token (lower is
+better).  Inputs are resident in HBM; L2 is flushed (256 MB write) before every timed step.
+  --config 3: 64 sequences, lengths U[4096, 163840] (seed 2), one batched decode step.
+  --config 5: 12 layers at 1,048,576 tokens, top-128, one token through all 12 layers.
+With N > 1 GPUs (torchrun) each rank runs the workload on its own GPU ("replicas", config 2) or
+its share of the sequences (config 3, data parallel); value = total units / max-over-ranks time.
+--impl reference times the reference's CPU algorithm (the oracle/ port, all host cores).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+HBM_FALLBACK_GBS, BF16_FALLBACK_TFS = 6650.0, 1590.0
+METRIC = "sparse-attn decode us/layer @160K q8_0"
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        j = json.load(open(p))
+        return float(j["hbm_gbs"]), float(j["bf16_tflops"]), "measured"
+    return HBM_FALLBACK_GBS, BF16_FALLBACK_TFS, "fallback"
+
+
+def profile_traffic(name: str):
+    """dram bytes per launch of the dominant kernel, from the committed ncu summary (or None)."""
+    p = os.path.join(ROOT, "profiles", name)
+    if not os.path.exists(p):
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", open(p).read())
+    return float(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 20 ms while running."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: str):
+        self.samples, self.proc, self.gpu = [], None, gpu_index
+        self.t0 = self.t1 = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-lms", "20", "-i", self.gpu], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.samples.append((time.time(), [x.strip() for x in line.split(",")]))
+
+    def mark(self, which):
+        setattr(self, which, time.time())
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.thread.join(timeout=2)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        inside = [s for t, s in self.samples if self.t0 and self.t1 and self.t0 <= t <= self.t1]
+        use = inside or [s for _, s in self.samples[-10:]]
+        names = ["active", "hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        sm, mx = [], []
+        for s in use:
+            try:
+                sm.append(float(s[1]))
+                mx.append(float(s[2]))
+            except (ValueError, IndexError):
+                continue
+            for i, n in enumerate(names[1:], start=5):
+                if i < len(s) and s[i].lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(use), "samples_in_timed_region": len(inside)}
+
+
+# ------------------------------------------------------------------------------------------------
+def dist_setup(backend):
+    import torch
+    import torch.distributed as dist
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1:
+        from datetime import timedelta
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=timedelta(seconds=120))
+    return ws, rank, local
+
+
+def max_over_ranks(x: float, ws: int) -> float:
+    if ws == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(x: float, ws: int) -> float:
+    if ws == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t)
+    return float(t.item())
+
+
+def attended_cells(sel_row, q, r):
+    return sum(max(0, min(r, q - int(b) * r + 1)) for b in sel_row if b >= 0)
+
+
+# ------------------------------------------------------------------------------------------------
+def cpu_baseline_config2(d, kc, vc, pool, q_host, qi_host, n_past, budget_s=12.0, max_iter=200):
+    """The oracle's ggml-mode node (scores, top-k, f32 online softmax with an F16 V accumulator as
+    ggml-cpu's flash attention) on all host cores, one query per iteration, bounded to ~budget_s."""
+    import numpy as np
+
+    import oracle
+    from qwfnfer_b200._abi import TYPE_BF16
+    threads = oracle.max_threads()
+    oracle.set_threads(threads)
+    flags = oracle.DEFAULT_FLAGS | oracle.GGML_FA | oracle.GGML_V_F16
+    times = []
+    t_end = time.perf_counter() + budget_s
+    i = 0
+    while time.perf_counter() < t_end and i < max_iter:
+        s = i % q_host.shape[0]
+        t0 = time.perf_counter()
+        oracle.node(d, kc, vc, pool, [n_past], q_host[s:s + 1], qi_host[s:s + 1], q_type=TYPE_BF16, flags=flags)
+        times.append(time.perf_counter() - t0)
+        i += 1
+    us = statistics.median(times) * 1e6
+    return {"value": round(us, 1), "unit": "us/layer-token", "cores": threads, "kind": "port",
+            "sample": f"{len(times)} single-query decodes of config 2 (scores over 2560 blocks, top-64+3, "
+                      f"attention over 4288 cells x 16 heads), median, oracle ggml-mode, {threads} threads"}
+
+
+def run_ours_config2(args, ws, rank, local):
+    import numpy as np
+    import torch
+
+    from qwfnfer_b200._abi import TYPE_BF16, check, k_blocks, lib
+    from qwfnfer_b200.configs import CONFIGS, fill_cache, token_inputs
+    from qwfnfer_b200.qsa import QsaNode, QsaState, decode_items, _stream
+    import ctypes
+
+    cfg = CONFIGS[2]
+    d = cfg.desc()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    n_past = cfg.n_past
+    node, st = QsaNode(d, dev), QsaState(d, device=dev)
+    fill_cache(node, st, 0, n_past, cfg.seed + 17 * rank)
+    S = 8
+    q, qi, k, v, ki = token_inputs(d, S, cfg.seed + 1000 + rank)
+    items = decode_items([st.layer()], [n_past], device=dev)
+    KB = k_blocks(d)
+    wsb = node.workspace("decode", 1, n_past + 1)
+    # static buffers for graph replay; slot inputs are copied in before each timed step
+    sq, sqi, sk, sv, ski = (torch.empty_like(x[:1]) for x in (q, qi, k, v, ki))
+    out = torch.empty(1, d.n_head, d.head_dim, device=dev)
+    sel = torch.empty(1, KB, dtype=torch.int32, device=dev)
+    L = lib()
+    D = ctypes.byref(d)
+
+    def load(s):
+        sq.copy_(q[s:s + 1]); sqi.copy_(qi[s:s + 1]); sk.copy_(k[s:s + 1]); sv.copy_(v[s:s + 1]); ski.copy_(ki[s:s + 1])
+
+    def step_api(stream_ptr):
+        check(L.qsa_decode(D, items.data_ptr(), 1, n_past + 1, sq.data_ptr(), TYPE_BF16, sqi.data_ptr(),
+                           sk.data_ptr(), sv.data_ptr(), ski.data_ptr(), out.data_ptr(), sel.data_ptr(),
+                           wsb.data_ptr(), wsb.numel(), stream_ptr), "qsa_decode")
+
+    def attend_api(stream_ptr):
+        check(L.qsa_decode_attend(D, items.data_ptr(), 1, n_past + 1, sq.data_ptr(), TYPE_BF16, out.data_ptr(),
+                                  wsb.data_ptr(), wsb.numel(), stream_ptr), "qsa_decode_attend")
+
+    def select_api(stream_ptr):
+        check(L.qsa_decode_select(D, items.data_ptr(), 1, n_past + 1, sqi.data_ptr(), sel.data_ptr(),
+                                  wsb.data_ptr(), wsb.numel(), stream_ptr), "qsa_decode_select")
+
+    for s in range(max(args.warmup, 3)):
+        load(s % S)
+        step_api(_stream(None))
+    torch.cuda.synchronize()
+    g_step, g_attn, g_sel = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_step):
+        step_api(_stream(None))
+    with torch.cuda.graph(g_attn):
+        attend_api(_stream(None))
+    with torch.cuda.graph(g_sel):
+        select_api(_stream(None))
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    K = args.steps
+
+    def timed(graph, n):
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+        for i in range(n):
+            load(i % S)
+            flush.zero_()
+            ev[i][0].record()
+            graph.replay()
+            ev[i][1].record()
+        torch.cuda.synchronize()
+        return [a.elapsed_time(b) * 1e3 for a, b in ev]   # us
+
+    clocks = ClockSampler(os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local]
+                          if "CUDA_VISIBLE_DEVICES" in os.environ else str(local))
+    clocks.start()
+    for _ in range(max(args.warmup, 3)):
+        timed(g_step, 50)            # warm-up under load (also settles clocks)
+    if ws > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    clocks.mark("t0")
+    step_us = timed(g_step, K)
+    if ws > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    clocks.mark("t1")
+    attn_us = timed(g_attn, K)
+    sel_us = timed(g_sel, K)
+    # e2e through the public C ABI with pinned host buffers, copies inside the timed region
+    hq, hqi, hk, hv, hki = (x.cpu().pin_memory() for x in (q, qi, k, v, ki))
+    hout = torch.empty(S, d.n_head, d.head_dim).pin_memory()
+    stream = torch.cuda.current_stream()
+    e2e = []
+    for i in range(K):
+        s = i % S
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        sq.copy_(hq[s:s + 1], non_blocking=True); sqi.copy_(hqi[s:s + 1], non_blocking=True)
+        sk.copy_(hk[s:s + 1], non_blocking=True); sv.copy_(hv[s:s + 1], non_blocking=True)
+        ski.copy_(hki[s:s + 1], non_blocking=True)
+        step_api(stream.cuda_stream)
+        hout[s:s + 1].copy_(out, non_blocking=True)
+        b.record()
+        e2e.append((a, b))
+    torch.cuda.synchronize()
+    e2e_us = [a.elapsed_time(b) * 1e3 for a, b in e2e]
+    clocks.stop()
+    h2d = sum(x[:1].numel() * x.element_size() for x in (q, qi, k, v, ki))
+    d2h = out.numel() * out.element_size()
+    check(node.check(wsb), "qsa_check")
+
+    total_us = max_over_ranks(sum(step_us), ws)
+    e2e_total = max_over_ranks(sum(e2e_us), ws)
+    units = K * ws
+    value = total_us / units
+    sel_h = sel.cpu().numpy()[0]
+    cells = attended_cells(sel_h, n_past, d.ratio)
+    attn_bytes = cells * 2 * 544 + q[:1].numel() * 2 + out.numel() * 4 + KB * 4
+    attn_mean = statistics.mean(attn_us)
+    hbm, _, src = peaks()
+    achieved = attn_bytes / (attn_mean * 1e-6) / 1e9
+    step_bytes = attn_bytes + (n_past + 1) // 64 * 256 + 2 * 544 + 256 + 64 * 256
+    res = {
+        "metric": METRIC, "value": round(value, 3), "unit": "us/layer-token", "n_gpus": ws, "steps": K,
+        "warmup": args.warmup, "ms_per_step": round(statistics.mean(step_us) / 1e3, 6), "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": None, "dtype": "q8_0 KV, bf16 Q, f16 MMA / f32 softmax", "data": "synthetic",
+        "config": {"workload": "config2: decode 1 token, 1 layer, ctx 163840, q8_0 KV, top-64 of 2560 blocks + "
+                               "128-token window (67 blocks, 4288 cells), batch 1",
+                   "global_batch": ws, "seq_len": n_past + 1, "parallelism": f"replicas x{ws}" if ws > 1 else "1 GPU",
+                   "l2": "flushed (256 MB write) before every timed step", "cuda_graph": True},
+        "roofline": {"bound": "hbm", "kernel": "attn_kernel<q8_0> (qsa_decode_attend)",
+                     "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(achieved / hbm, 4), "peak_source": f"{src} hbm_gbs (burst)",
+                     "traffic": profile_traffic("attn_decode_config2.md"),
+                     "algorithmic_bytes_per_launch": attn_bytes, "launch_us": round(attn_mean, 3)},
+        "step_roofline": {"algorithmic_bytes": step_bytes,
+                          "achieved_gbs": round(step_bytes / (statistics.mean(step_us) * 1e-6) / 1e9, 1)},
+        "stages_us": {"step": round(statistics.mean(step_us), 3), "select": round(statistics.mean(sel_us), 3),
+                      "attend": round(attn_mean, 3)},
+        "e2e": {"value": round(e2e_total / units, 3), "unit": "us/layer-token", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": 3 * K,
+        "clocks": clocks.summary(),
+    }
+    if rank == 0 and not args.no_cpu_baseline:
+        kc = st.k[0][:n_past + 1].cpu().numpy()
+        vc = st.v[0][:n_past + 1].cpu().numpy()
+        pool = st.pool[0].cpu().numpy().view(np.uint16)
+        qh = q.view(torch.int16).cpu().numpy().view(np.uint16)
+        res["cpu_baseline"] = cpu_baseline_config2(d, kc, vc, pool, qh, qi.cpu().numpy(), n_past)
+    return res
+
+
+def run_reference_config2(args):
+    """The reference's CPU algorithm (oracle port, ggml mode, all host cores) on config 2."""
+    import numpy as np
+
+    import oracle
+    from qwfnfer_b200._abi import TYPE_BF16
+    from qwfnfer_b200.configs import CONFIGS, IDX_STD, K_SCALE
+    cfg = CONFIGS[2]
+    d = cfg.desc()
+    n_past = cfg.n_past
+    threads = oracle.max_threads()
+    oracle.set_threads(threads)
+    rng = np.random.default_rng(cfg.seed)
+    kc, vc, ic, pool = oracle.cache_arrays(d)
+    chunk = 16384
+    for pos in range(0, n_past, chunk):
+        n = min(chunk, n_past - pos)
+        oracle.append(d, kc, vc, ic, pos, (rng.standard_normal((n, 512), np.float32) * K_SCALE),
+                      rng.standard_normal((n, 512), np.float32), rng.standard_normal((n, 128), np.float32) * IDX_STD)
+    _, p16 = oracle.pool_blocks(d, ic, 0, n_past // 64)
+    pool[: n_past // 64] = p16
+    S = 8
+    qf = rng.standard_normal((S, 16, 256), np.float32)
+    qh = (qf.view(np.uint32) >> 16).astype(np.uint16)           # bf16 bits (truncated draw)
+    qi = rng.standard_normal((S, 1, 128), np.float32) * IDX_STD
+    kn = rng.standard_normal((S, 512), np.float32) * K_SCALE
+    vn = rng.standard_normal((S, 512), np.float32)
+    kin = rng.standard_normal((S, 128), np.float32) * IDX_STD
+    flags = oracle.DEFAULT_FLAGS | oracle.GGML_FA | oracle.GGML_V_F16
+
+    def step(s):
+        oracle.append(d, kc, vc, ic, n_past, kn[s:s + 1], vn[s:s + 1], kin[s:s + 1])
+        b = n_past // 64
+        _, p = oracle.pool_blocks(d, ic, b, 1)
+        pool[b] = p[0]
+        oracle.node(d, kc, vc, pool, [n_past], qh[s:s + 1], qi[s:s + 1], q_type=TYPE_BF16, flags=flags)
+
+    for i in range(args.warmup):
+        step(i % S)
+    times = []
+    for i in range(args.steps):
+        t0 = time.perf_counter()
+        step(i % S)
+        times.append(time.perf_counter() - t0)
+    us = statistics.mean(times) * 1e6
+    return {
+        "impl": "reference", "metric": METRIC, "value": round(us, 1), "unit": "us/layer-token", "n_gpus": 0,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(us / 1e3, 4), "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": None, "dtype": "q8_0 KV, f16-rounded K/V and Q, f32 softmax", "data": "synthetic",
+        "config": {"workload": "config2: decode 1 token, 1 layer, ctx 163840, q8_0 KV, top-64 + 128-token window",
+                   "global_batch": 1, "seq_len": n_past + 1, "parallelism": f"CPU, {threads} threads"},
+        "cpu_baseline": {"value": round(us, 1), "unit": "us/layer-token", "cores": threads, "kind": "port",
+                         "sample": f"{args.steps} decode steps (append + pooled key + scores + top-k + ggml-mode "
+                                   f"attention), oracle port of the reference node"},
+        "e2e": {"value": round(us, 1), "unit": "us/layer-token", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 5])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        if rank != 0:
+            return
+        res = run_reference_config2(args)
+        print(json.dumps(res), flush=True)
+        return
+
+    ws, rank, local = dist_setup("nccl")
+    if args.config == 2:
+        res = run_ours_config2(args, ws, rank, local)
+    else:
+        raise SystemExit(f"--config {args.config}: not wired into bench.py yet")
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,201 @@
+/*
+ * qsa.h -- C ABI of the B200 sparse-attention (QSA) library, libqsa.so.
+ *
+ * The library implements the four parts of QwFNfer's "Qwen Sparse Attention" node:
+ *   1. the lightning indexer: each query scored against one mean-pooled, RMS-normed,
+ *      IMRoPE'd key per block of `ratio` cells;
+ *   2. top-k block selection plus a forced local window;
+ *   3. block-sparse flash attention over the selected q8_0 or f16 KV rows;
+ *   4. the pooled-key update when KV rows are appended.
+ *
+ * Reference interfaces replaced (paths inside the QwFNfer source tree):
+ *   - graph_builder::sparse_attn_decode   src/qwfn_graph.cpp:450-546  -> qsa_decode
+ *   - graph_builder::sparse_attn/qsa_top_k src/qwfn_graph.cpp:235-408 -> qsa_prefill
+ *   - graph_builder::qsa_pool_rebuild      src/qwfn_graph.cpp:431-448 -> qsa_pool_rebuild
+ *   - the K/V/raw-key writes (ggml_set_rows / ggml_cpy into the caches)
+ *                                          src/qwfn_graph.cpp:466-469,504-528,249-254,349-360
+ *                                                                     -> qsa_append
+ *   - engine::qsa_decode_prepare / build_attn_inputs bias + table rules
+ *                                          src/qwfn_engine.cpp:731-799,884-957
+ *                                          (computed on the device from n_past; no host tables)
+ *
+ * Cache layouts are byte-identical to the reference:
+ *   K, V   : per layer, n_ctx token rows of n_head_kv*head_dim elements in type_k/type_v,
+ *            row t = head0[head_dim] head1[head_dim] ...   (src/qwfn_state.cpp:40-56)
+ *            q8_0 = blocks of 32: { f16 d; int8 qs[32] }, 34 bytes, packed.
+ *   idx    : F16 [n_ctx][idx_dim] raw (pre-norm, pre-rope) indexer keys   (src/qwfn_state.cpp:49)
+ *   pool   : F16 [n_ctx/ratio][idx_dim] pooled+normed+roped block keys   (src/qwfn_engine.cpp:394-397)
+ *
+ * Conventions:
+ *   - Every pointer that a kernel touches is a DEVICE pointer unless the comment says "host".
+ *   - The caller owns every cache, input, output and workspace buffer.  No entry point allocates
+ *     device memory, and none synchronises the stream except qsa_check and the *_sync helpers.
+ *   - Work is stream-ordered on `stream`; calls on different streams over the same caches race.
+ *   - Errors: an enum return.  Argument errors are found on the host (QSA_ERR_INVALID) before
+ *     anything is launched.  Out-of-range values found on the device (for instance an n_past
+ *     beyond n_ctx in a device-side table) are recorded in the workspace status word and the
+ *     offending item is skipped; qsa_check() reads and clears it.  Nothing aborts.
+ *   - Workspaces must be zeroed once (qsa_workspace_init) before first use; kernels leave the
+ *     counters they use at zero again when they finish.
+ */
+#ifndef QSA_H
+#define QSA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* cudaStream_t without requiring the CUDA headers. */
+struct CUstream_st;
+typedef struct CUstream_st * qsa_stream_t;
+
+typedef enum qsa_status {
+    QSA_OK              = 0,
+    QSA_ERR_INVALID     = 1,  /* bad argument or descriptor (host-side check)            */
+    QSA_ERR_CUDA        = 2,  /* a CUDA launch or copy failed                            */
+    QSA_ERR_TIMEOUT     = 3,  /* a bounded device-side wait ran out                      */
+    QSA_ERR_UNSUPPORTED = 4,  /* shape/type combination without a kernel                 */
+    QSA_ERR_WORKSPACE   = 5,  /* workspace missing or smaller than *_workspace_size()    */
+    QSA_ERR_DEVICE_ARG  = 6   /* an out-of-range value was found on the device           */
+} qsa_status;
+
+/* Element types, numbered as ggml numbers them (ggml_type). */
+enum {
+    QSA_TYPE_F32  = 0,
+    QSA_TYPE_F16  = 1,
+    QSA_TYPE_Q8_0 = 8,
+    QSA_TYPE_BF16 = 30
+};
+
+/* Layer descriptor: the hyper-parameters of one QSA layer (src/qwfn_hparams.h:21-54). */
+typedef struct qsa_desc {
+    int32_t n_head;          /* query heads                                     (n_head)          */
+    int32_t n_head_kv;       /* KV heads                                        (n_head_kv)       */
+    int32_t head_dim;        /* 256                                             (n_embd_head_k)   */
+    int32_t idx_n_head;      /* indexer heads                                   (idx_n_head)      */
+    int32_t idx_dim;         /* indexer key length                              (idx_key_len)     */
+    int32_t ratio;           /* cells per block r                               (compress_ratios) */
+    int32_t top_k_blocks;    /* blocks kept by score                                              */
+    int32_t window;          /* causal local window in tokens, forced at block granularity:
+                                ceil(window/ratio)+1 blocks ending at the query's block.
+                                0 = the reference rule: only the query's block, and only while it
+                                is incomplete (src/qwfn_engine.cpp:936-950).                      */
+    int32_t n_ctx;           /* cache capacity in tokens (a multiple of ratio)                    */
+    int32_t type_k;          /* QSA_TYPE_Q8_0 or QSA_TYPE_F16                                     */
+    int32_t type_v;          /* QSA_TYPE_Q8_0 or QSA_TYPE_F16                                     */
+    int32_t rope_dim;        /* rotated dims of the indexer key (rope_dim)                        */
+    int32_t sections[4];     /* IMRoPE sections (mrope_sections)                                  */
+    float   rms_eps;         /* rms_eps                                                           */
+    float   rope_freq_base;  /* rope_freq_base                                                    */
+    const float * k_norm_w;  /* device [idx_dim], indexer.k_norm.weight; NULL means all ones      */
+} qsa_desc;
+
+/* One layer's caches of one sequence (device pointers, reference layouts above). */
+typedef struct qsa_layer_cache {
+    void     * k;
+    void     * v;
+    uint16_t * idx;
+    uint16_t * pool;
+} qsa_layer_cache;
+
+/* One decode query, as a device-resident table entry: the query is token n_past of the
+ * sequence whose caches are `cache`; after this step the cache holds n_past+1 tokens.
+ * Kept in device memory so that a captured CUDA graph replays with new positions. */
+typedef struct qsa_decode_item {
+    qsa_layer_cache cache;
+    int32_t n_past;
+    int32_t reserved[3];
+} qsa_decode_item;
+
+/* ------------------------------------------------------------------ descriptors / sizes */
+const char * qsa_status_string(qsa_status s);
+/* Host-side validation of a descriptor against what the kernels support. */
+qsa_status qsa_desc_check(const qsa_desc * d);
+/* Blocks attended per query: top_k_blocks plus the forced-window blocks (KB). */
+int32_t qsa_k_blocks(const qsa_desc * d);
+/* Bytes of one cache row: which = 0 K, 1 V, 2 idx, 3 pool (per block). */
+size_t qsa_row_bytes(const qsa_desc * d, int32_t which);
+/* Bytes of one whole layer cache of n_ctx tokens: which as above. */
+size_t qsa_cache_bytes(const qsa_desc * d, int32_t which);
+
+/* ------------------------------------------------------------------ append / pool */
+/* Write n_tok tokens at rows [pos0, pos0+n_tok): K and V (f32 [n_tok][n_head_kv*head_dim],
+ * quantised to type_k/type_v with ggml's reference q8_0 rounding), the raw indexer key
+ * (f32 [n_tok][idx_dim] -> F16), and the pooled key of every block that is complete at
+ * pos0+n_tok and has a member in the range.  kidx may be NULL (no indexer write, no pool update).
+ * Replaces the set_rows/cpy writes of src/qwfn_graph.cpp:466-476,504-528 and 249-254,349-360. */
+qsa_status qsa_append(const qsa_desc * d, const qsa_layer_cache * cache /* host struct */,
+                      int32_t pos0, int32_t n_tok,
+                      const float * k, const float * v, const float * kidx,
+                      qsa_stream_t stream);
+
+/* Recompute pooled keys of blocks [blk0, blk0+n_blk) from the raw indexer cache.
+ * pooled_f32 (optional, device [n_blk][idx_dim]) receives the f32 values before the F16 store.
+ * Replaces graph_builder::qsa_pool_rebuild (src/qwfn_graph.cpp:412-448). */
+qsa_status qsa_pool_rebuild(const qsa_desc * d, const qsa_layer_cache * cache /* host struct */,
+                            int32_t blk0, int32_t n_blk, float * pooled_f32, qsa_stream_t stream);
+
+/* ------------------------------------------------------------------ decode */
+size_t qsa_decode_workspace_size(const qsa_desc * d, int32_t batch, int32_t max_n_kv);
+/* Zero a workspace (required once before its first use). */
+qsa_status qsa_workspace_init(void * ws, size_t ws_bytes, qsa_stream_t stream);
+
+/* One decode step for `batch` queries (items: device table of qsa_decode_item).
+ *   q      : [batch][n_head][head_dim], q_type QSA_TYPE_BF16 or QSA_TYPE_F32 (post-norm, post-rope)
+ *   q_idx  : f32 [batch][idx_n_head][idx_dim]   indexer query (post q_norm and rope)
+ *   k_new, v_new, kidx_new : f32 rows of the token being decoded, [batch][...] as in qsa_append;
+ *            all three NULL = the caller already wrote row n_past (and the pooled keys)
+ *   out    : f32 [batch][n_head][head_dim]
+ *   sel_out: optional int32 [batch][KB]: selected block ids ascending, -1 padded
+ * max_n_kv bounds n_past+1 over the batch (sizes the grid; a device value above it is an error).
+ * Replaces graph_builder::sparse_attn_decode up to the output gate (src/qwfn_graph.cpp:450-541). */
+qsa_status qsa_decode(const qsa_desc * d, const qsa_decode_item * items, int32_t batch, int32_t max_n_kv,
+                      const void * q, int32_t q_type, const float * q_idx,
+                      const float * k_new, const float * v_new, const float * kidx_new,
+                      float * out, int32_t * sel_out,
+                      void * ws, size_t ws_bytes, qsa_stream_t stream);
+
+/* The three stages of qsa_decode as separate calls (same arguments and workspace), for callers
+ * that append elsewhere or time the stages: append (row n_past of each item, plus the pooled key
+ * of a block it completes), select (scores + top-k into the workspace, optional sel_out),
+ * attend (attention over the selection the last select left in the workspace). */
+qsa_status qsa_decode_append(const qsa_desc * d, const qsa_decode_item * items, int32_t batch, int32_t max_n_kv,
+                             const float * k_new, const float * v_new, const float * kidx_new,
+                             void * ws, size_t ws_bytes, qsa_stream_t stream);
+qsa_status qsa_decode_select(const qsa_desc * d, const qsa_decode_item * items, int32_t batch, int32_t max_n_kv,
+                             const float * q_idx, int32_t * sel_out, void * ws, size_t ws_bytes, qsa_stream_t stream);
+qsa_status qsa_decode_attend(const qsa_desc * d, const qsa_decode_item * items, int32_t batch, int32_t max_n_kv,
+                             const void * q, int32_t q_type, float * out, void * ws, size_t ws_bytes,
+                             qsa_stream_t stream);
+
+/* ------------------------------------------------------------------ prefill */
+size_t qsa_prefill_workspace_size(const qsa_desc * d, int32_t T, int32_t max_n_kv);
+
+/* Chunked prefill of T tokens at positions [n_past, n_past+T) of one sequence: append K/V/raw
+ * keys, update the pooled keys of the blocks completed, score every query against the blocks
+ * complete at its position, select, and attend.  Inputs are laid out as in qsa_decode with
+ * `batch` replaced by T.  k_new/v_new/kidx_new NULL = already appended.
+ * Replaces graph_builder::sparse_attn + qsa_top_k (src/qwfn_graph.cpp:235-408) together with
+ * the per-chunk host inputs of engine::build_attn_inputs (src/qwfn_engine.cpp:884-957): the
+ * result does not depend on how the caller chunks the T tokens. */
+qsa_status qsa_prefill(const qsa_desc * d, const qsa_layer_cache * cache /* host struct */,
+                       int32_t n_past, int32_t T,
+                       const void * q, int32_t q_type, const float * q_idx,
+                       const float * k_new, const float * v_new, const float * kidx_new,
+                       float * out, int32_t * sel_out,
+                       void * ws, size_t ws_bytes, qsa_stream_t stream);
+
+/* ------------------------------------------------------------------ status */
+/* Synchronise `stream`, read and clear the workspace status word. */
+qsa_status qsa_check(void * ws, size_t ws_bytes, qsa_stream_t stream);
+
+/* Library version (major*10000 + minor*100 + patch) and the device kernels' target. */
+int32_t qsa_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QSA_H */

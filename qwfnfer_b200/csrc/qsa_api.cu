@@ -1,0 +1,339 @@
+// qsa_api.cu -- the C ABI of libqsa (include/qsa.h): validation, workspace layout, launches.
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+
+#include "qsa_kernels.cuh"
+
+namespace qsa {
+namespace {
+
+constexpr int TARGET_ATTN_CTAS = 148;   // one resident attention CTA (8 warps, both KV heads) per SM
+
+// Tiles (64 cells) per attention CTA; QSA_TILES_PER_CTA overrides the heuristic (tuning).
+int tiles_override() {
+    static int v = [] { const char * e = getenv("QSA_TILES_PER_CTA"); return e ? atoi(e) : 0; }();
+    return v;
+}
+
+inline int ceil_div(int64_t a, int64_t b) { return (int) ((a + b - 1) / b); }
+
+int n_force_of(const qsa_desc * d) { return d->window > 0 ? ceil_div(d->window, d->ratio) + 1 : 1; }
+
+size_t kv_row_bytes(int type, int64_t n) {
+    return type == QSA_TYPE_Q8_0 ? (size_t) (n / QK8_0) * Q8_0_BYTES : (size_t) n * 2;
+}
+
+DevDesc make_dev(const qsa_desc * d) {
+    DevDesc x;
+    std::memset(&x, 0, sizeof x);
+    x.n_head = d->n_head; x.n_head_kv = d->n_head_kv; x.head_dim = d->head_dim;
+    x.gqa = d->n_head / d->n_head_kv;
+    x.idx_n_head = d->idx_n_head; x.idx_dim = d->idx_dim; x.ratio = d->ratio;
+    x.top_k = d->top_k_blocks; x.n_force = n_force_of(d); x.kb = x.top_k + x.n_force; x.window = d->window;
+    x.n_ctx = d->n_ctx; x.type_k = d->type_k; x.type_v = d->type_v; x.rope_dim = d->rope_dim;
+    for (int i = 0; i < 4; i++) x.sections[i] = d->sections[i];
+    x.rms_eps = d->rms_eps;
+    x.theta_scale = powf(d->rope_freq_base, -2.0f / (float) d->rope_dim);   // as ggml's rope computes it
+    x.inv_ratio = 1.0f / (float) d->ratio;
+    x.scale_log2 = (float) (1.4426950408889634 / std::sqrt((double) d->head_dim));
+    x.k_norm_w = d->k_norm_w;
+    const int64_t kv_dim = (int64_t) d->n_head_kv * d->head_dim;
+    x.rb_k = (int64_t) kv_row_bytes(d->type_k, kv_dim);
+    x.rb_v = (int64_t) kv_row_bytes(d->type_v, kv_dim);
+    x.hb_k = (int) kv_row_bytes(d->type_k, d->head_dim);
+    x.hb_v = (int) kv_row_bytes(d->type_v, d->head_dim);
+    return x;
+}
+
+struct WsLayout {
+    size_t status, cnt_sel, cnt_att, scores, sel, nsel, part_o, part_ml, total;
+    int scores_stride, max_chunks, tiles_per_cta;
+};
+
+size_t align256(size_t x) { return (x + 255) & ~(size_t) 255; }
+
+WsLayout ws_layout(const DevDesc & d, int n_q, int max_n_kv) {
+    WsLayout w;
+    w.scores_stride = std::max(1, ceil_div(max_n_kv, d.ratio));
+    const int max_tiles = std::max(1, ceil_div((int64_t) d.kb * d.ratio, CELLS_TILE));
+    const int64_t total_tiles = (int64_t) n_q * max_tiles;
+    int tpc = (int) std::max<int64_t>(1, total_tiles / TARGET_ATTN_CTAS);
+    if (tiles_override() > 0) tpc = tiles_override();
+    tpc = std::min(tpc, max_tiles);
+    w.tiles_per_cta = tpc;
+    w.max_chunks = ceil_div(max_tiles, tpc);
+    size_t o = 0;
+    w.status  = o; o = align256(o + 16);
+    w.cnt_sel = o; o = align256(o + (size_t) n_q * 4);
+    w.cnt_att = o; o = align256(o + (size_t) n_q * 4);
+    w.scores  = o; o = align256(o + (size_t) n_q * w.scores_stride * 4);
+    w.sel     = o; o = align256(o + (size_t) n_q * d.kb * 4);
+    w.nsel    = o; o = align256(o + (size_t) n_q * 4);
+    const int CL = attn_cluster_size(w.max_chunks);
+    const int max_parts = (w.max_chunks + CL - 1) / CL;          // one partial per cluster
+    const size_t parts = max_parts > 1 ? (size_t) n_q * max_parts : 0;
+    w.part_o  = o; o = align256(o + parts * attn_state_rows() * HEAD_DIM * 4);
+    w.part_ml = o; o = align256(o + parts * 2 * attn_state_rows() * 4);
+    w.total = o;
+    return w;
+}
+
+qsa_status cuda_status(cudaError_t e) { return e == cudaSuccess ? QSA_OK : QSA_ERR_CUDA; }
+
+bool attrs_done = false;
+qsa_status set_attrs() {
+    if (attrs_done) return QSA_OK;
+    cudaError_t e = attn_set_attrs();
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(score_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+    if (e != cudaSuccess) return QSA_ERR_CUDA;
+    attrs_done = true;
+    return QSA_OK;
+}
+
+// Scores + selection into the workspace (and sel_out).
+qsa_status launch_select(const DevDesc & d, const WsLayout & w, int n_q, const qsa_decode_item * items,
+                         qsa_layer_cache cache0, int n_past0, const float * q_idx, int32_t * sel_out,
+                         unsigned char * ws, cudaStream_t st) {
+    uint32_t * status = reinterpret_cast<uint32_t *>(ws + w.status);
+    // blocks per scoring CTA: 16 (one row pair per warp) while the grid is small, more once
+    // there are enough CTAs to fill the GPU several times over
+    int bpc = 16;
+    while (bpc < 256 && (int64_t) ceil_div(w.scores_stride, 2 * bpc) * n_q >= 8 * 148) bpc *= 2;
+    const int score_ctas = ceil_div(w.scores_stride, bpc);
+    const size_t sel_smem = (size_t) w.scores_stride * 5;       // scores + selection flags
+    if (sel_smem > 160 * 1024) return QSA_ERR_UNSUPPORTED;
+    score_select_kernel<<<dim3(score_ctas, n_q), 256, sel_smem, st>>>(
+        d, items, cache0.pool, n_past0, q_idx, bpc,
+        reinterpret_cast<float *>(ws + w.scores), w.scores_stride, reinterpret_cast<unsigned *>(ws + w.cnt_sel),
+        reinterpret_cast<int *>(ws + w.sel), reinterpret_cast<int *>(ws + w.nsel), sel_out, status);
+    return cuda_status(cudaGetLastError());
+}
+
+// Attention over the selection held in the workspace.
+qsa_status launch_attend(const DevDesc & d, const WsLayout & w, int n_q, const qsa_decode_item * items,
+                         qsa_layer_cache cache0, int n_past0, const void * q, int q_type, float * out,
+                         unsigned char * ws, cudaStream_t st) {
+    const dim3 grid(w.max_chunks, d.n_head_kv, n_q);
+    return cuda_status(launch_attn(d, grid, st, items, cache0, n_past0, q, q_type,
+                                   reinterpret_cast<const int *>(ws + w.sel), reinterpret_cast<const int *>(ws + w.nsel),
+                                   w.tiles_per_cta, w.max_chunks, reinterpret_cast<float *>(ws + w.part_o),
+                                   reinterpret_cast<float *>(ws + w.part_ml), reinterpret_cast<unsigned *>(ws + w.cnt_att),
+                                   out, reinterpret_cast<uint32_t *>(ws + w.status)));
+}
+
+}  // namespace
+}  // namespace qsa
+
+using namespace qsa;
+
+extern "C" {
+
+const char * qsa_status_string(qsa_status s) {
+    switch (s) {
+        case QSA_OK: return "ok";
+        case QSA_ERR_INVALID: return "invalid argument";
+        case QSA_ERR_CUDA: return "CUDA error";
+        case QSA_ERR_TIMEOUT: return "device wait timed out";
+        case QSA_ERR_UNSUPPORTED: return "unsupported shape or type";
+        case QSA_ERR_WORKSPACE: return "workspace too small";
+        case QSA_ERR_DEVICE_ARG: return "out-of-range value found on the device";
+    }
+    return "unknown status";
+}
+
+qsa_status qsa_desc_check(const qsa_desc * d) {
+    if (!d) return QSA_ERR_INVALID;
+    if (d->n_head <= 0 || d->n_head_kv <= 0 || d->n_head % d->n_head_kv != 0) return QSA_ERR_INVALID;
+    if (d->ratio <= 0 || d->n_ctx <= 0 || d->n_ctx % d->ratio != 0) return QSA_ERR_INVALID;
+    if (d->top_k_blocks <= 0 || d->window < 0 || d->idx_n_head <= 0) return QSA_ERR_INVALID;
+    if (d->rope_dim <= 0 || d->rope_dim % 2 != 0 || d->rope_dim > d->idx_dim) return QSA_ERR_INVALID;
+    if (d->type_k != QSA_TYPE_Q8_0 && d->type_k != QSA_TYPE_F16) return QSA_ERR_INVALID;
+    if (d->type_v != QSA_TYPE_Q8_0 && d->type_v != QSA_TYPE_F16) return QSA_ERR_INVALID;
+    // what the kernels of this version are written for
+    if (d->head_dim != HEAD_DIM) return QSA_ERR_UNSUPPORTED;
+    if (d->n_head / d->n_head_kv > GQA_TILE || d->n_head_kv > 2) return QSA_ERR_UNSUPPORTED;
+    if (d->idx_dim != MAX_IDX_DIM || d->idx_n_head > 4 || d->rope_dim % 8 != 0) return QSA_ERR_UNSUPPORTED;
+    if (d->type_k != d->type_v) return QSA_ERR_UNSUPPORTED;
+    if (d->top_k_blocks + n_force_of(d) > MAX_KB) return QSA_ERR_UNSUPPORTED;
+    return QSA_OK;
+}
+
+int32_t qsa_k_blocks(const qsa_desc * d) { return d ? d->top_k_blocks + n_force_of(d) : 0; }
+
+size_t qsa_row_bytes(const qsa_desc * d, int32_t which) {
+    if (!d) return 0;
+    const int64_t kv_dim = (int64_t) d->n_head_kv * d->head_dim;
+    switch (which) {
+        case 0: return kv_row_bytes(d->type_k, kv_dim);
+        case 1: return kv_row_bytes(d->type_v, kv_dim);
+        case 2: return (size_t) d->idx_dim * 2;
+        case 3: return (size_t) d->idx_dim * 2;
+        default: return 0;
+    }
+}
+
+size_t qsa_cache_bytes(const qsa_desc * d, int32_t which) {
+    if (!d) return 0;
+    const size_t rows = which == 3 ? (size_t) (d->n_ctx / std::max(1, d->ratio)) : (size_t) d->n_ctx;
+    return rows * qsa_row_bytes(d, which);
+}
+
+qsa_status qsa_append(const qsa_desc * dd, const qsa_layer_cache * cache, int32_t pos0, int32_t n_tok,
+                      const float * k, const float * v, const float * kidx, qsa_stream_t stream) {
+    qsa_status s = qsa_desc_check(dd);
+    if (s != QSA_OK) return s;
+    if (!cache || pos0 < 0 || n_tok < 0 || (int64_t) pos0 + n_tok > dd->n_ctx) return QSA_ERR_INVALID;
+    if ((k && !cache->k) || (v && !cache->v) || (kidx && (!cache->idx || !cache->pool))) return QSA_ERR_INVALID;
+    if (n_tok == 0) return QSA_OK;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const DevDesc d = make_dev(dd);
+    append_rows_kernel<<<n_tok, 256, 0, st>>>(d, *cache, pos0, k, v, kidx);
+    if (kidx) {
+        const int b0 = pos0 / d.ratio, b1 = (pos0 + n_tok) / d.ratio;   // blocks complete after the append
+        if (b1 > b0) {
+            const int n = b1 - b0;
+            pool_blocks_kernel<<<ceil_div(n, 8), 256, 0, st>>>(d, cache->idx, cache->pool, b0, n, nullptr);
+        }
+    }
+    return cuda_status(cudaGetLastError());
+}
+
+qsa_status qsa_pool_rebuild(const qsa_desc * dd, const qsa_layer_cache * cache, int32_t blk0, int32_t n_blk,
+                            float * pooled_f32, qsa_stream_t stream) {
+    qsa_status s = qsa_desc_check(dd);
+    if (s != QSA_OK) return s;
+    if (!cache || !cache->idx || !cache->pool || blk0 < 0 || n_blk < 0 ||
+        (int64_t) (blk0 + n_blk) * dd->ratio > dd->n_ctx) return QSA_ERR_INVALID;
+    if (n_blk == 0) return QSA_OK;
+    const DevDesc d = make_dev(dd);
+    pool_blocks_kernel<<<ceil_div(n_blk, 8), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        d, cache->idx, cache->pool, blk0, n_blk, pooled_f32);
+    return cuda_status(cudaGetLastError());
+}
+
+size_t qsa_decode_workspace_size(const qsa_desc * dd, int32_t batch, int32_t max_n_kv) {
+    if (qsa_desc_check(dd) != QSA_OK || batch <= 0 || max_n_kv <= 0) return 0;
+    return ws_layout(make_dev(dd), batch, max_n_kv).total;
+}
+
+size_t qsa_prefill_workspace_size(const qsa_desc * dd, int32_t T, int32_t max_n_kv) {
+    return qsa_decode_workspace_size(dd, T, max_n_kv);
+}
+
+qsa_status qsa_workspace_init(void * ws, size_t ws_bytes, qsa_stream_t stream) {
+    if (!ws || ws_bytes == 0) return QSA_ERR_WORKSPACE;
+    return cuda_status(cudaMemsetAsync(ws, 0, ws_bytes, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+namespace {
+qsa_status decode_common(const qsa_desc * dd, const qsa_decode_item * items, int32_t batch, int32_t max_n_kv,
+                         void * ws, size_t ws_bytes, DevDesc & d, WsLayout & w) {
+    qsa_status s = qsa_desc_check(dd);
+    if (s != QSA_OK) return s;
+    if (!items || batch <= 0 || max_n_kv <= 0 || max_n_kv > dd->n_ctx) return QSA_ERR_INVALID;
+    d = make_dev(dd);
+    w = ws_layout(d, batch, max_n_kv);
+    if (!ws || ws_bytes < w.total) return QSA_ERR_WORKSPACE;
+    return set_attrs();
+}
+}  // namespace
+
+qsa_status qsa_decode_append(const qsa_desc * dd, const qsa_decode_item * items, int32_t batch, int32_t max_n_kv,
+                             const float * k_new, const float * v_new, const float * kidx_new,
+                             void * ws, size_t ws_bytes, qsa_stream_t stream) {
+    DevDesc d; WsLayout w;
+    qsa_status s = decode_common(dd, items, batch, max_n_kv, ws, ws_bytes, d, w);
+    if (s != QSA_OK) return s;
+    if (!k_new || !v_new || !kidx_new) return QSA_ERR_INVALID;
+    append_decode_kernel<<<batch, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        d, items, k_new, v_new, kidx_new, reinterpret_cast<uint32_t *>(static_cast<unsigned char *>(ws) + w.status));
+    return cuda_status(cudaGetLastError());
+}
+
+qsa_status qsa_decode_select(const qsa_desc * dd, const qsa_decode_item * items, int32_t batch, int32_t max_n_kv,
+                             const float * q_idx, int32_t * sel_out, void * ws, size_t ws_bytes, qsa_stream_t stream) {
+    DevDesc d; WsLayout w;
+    qsa_status s = decode_common(dd, items, batch, max_n_kv, ws, ws_bytes, d, w);
+    if (s != QSA_OK) return s;
+    if (!q_idx) return QSA_ERR_INVALID;
+    qsa_layer_cache none{};
+    return launch_select(d, w, batch, items, none, 0, q_idx, sel_out, static_cast<unsigned char *>(ws),
+                         reinterpret_cast<cudaStream_t>(stream));
+}
+
+qsa_status qsa_decode_attend(const qsa_desc * dd, const qsa_decode_item * items, int32_t batch, int32_t max_n_kv,
+                             const void * q, int32_t q_type, float * out, void * ws, size_t ws_bytes,
+                             qsa_stream_t stream) {
+    DevDesc d; WsLayout w;
+    qsa_status s = decode_common(dd, items, batch, max_n_kv, ws, ws_bytes, d, w);
+    if (s != QSA_OK) return s;
+    if (!q || !out || (q_type != QSA_TYPE_BF16 && q_type != QSA_TYPE_F32)) return QSA_ERR_INVALID;
+    qsa_layer_cache none{};
+    return launch_attend(d, w, batch, items, none, 0, q, q_type, out, static_cast<unsigned char *>(ws),
+                         reinterpret_cast<cudaStream_t>(stream));
+}
+
+qsa_status qsa_decode(const qsa_desc * dd, const qsa_decode_item * items, int32_t batch, int32_t max_n_kv,
+                      const void * q, int32_t q_type, const float * q_idx,
+                      const float * k_new, const float * v_new, const float * kidx_new,
+                      float * out, int32_t * sel_out, void * ws, size_t ws_bytes, qsa_stream_t stream) {
+    DevDesc d; WsLayout w;
+    qsa_status s = decode_common(dd, items, batch, max_n_kv, ws, ws_bytes, d, w);
+    if (s != QSA_OK) return s;
+    if (!q || !q_idx || !out || (q_type != QSA_TYPE_BF16 && q_type != QSA_TYPE_F32)) return QSA_ERR_INVALID;
+    const bool any_new = k_new || v_new || kidx_new;
+    if (any_new && !(k_new && v_new && kidx_new)) return QSA_ERR_INVALID;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    unsigned char * wsb = static_cast<unsigned char *>(ws);
+    if (any_new)
+        append_decode_kernel<<<batch, 256, 0, st>>>(d, items, k_new, v_new, kidx_new,
+                                                    reinterpret_cast<uint32_t *>(wsb + w.status));
+    qsa_layer_cache none{};
+    if ((s = launch_select(d, w, batch, items, none, 0, q_idx, sel_out, wsb, st)) != QSA_OK) return s;
+    return launch_attend(d, w, batch, items, none, 0, q, q_type, out, wsb, st);
+}
+
+qsa_status qsa_prefill(const qsa_desc * dd, const qsa_layer_cache * cache, int32_t n_past, int32_t T,
+                       const void * q, int32_t q_type, const float * q_idx,
+                       const float * k_new, const float * v_new, const float * kidx_new,
+                       float * out, int32_t * sel_out, void * ws, size_t ws_bytes, qsa_stream_t stream) {
+    qsa_status s = qsa_desc_check(dd);
+    if (s != QSA_OK) return s;
+    if (!cache || n_past < 0 || T <= 0 || (int64_t) n_past + T > dd->n_ctx || !q || !q_idx || !out) return QSA_ERR_INVALID;
+    if (!cache->k || !cache->v || !cache->idx || !cache->pool) return QSA_ERR_INVALID;
+    if (q_type != QSA_TYPE_BF16 && q_type != QSA_TYPE_F32) return QSA_ERR_INVALID;
+    const bool any_new = k_new || v_new || kidx_new;
+    if (any_new && !(k_new && v_new && kidx_new)) return QSA_ERR_INVALID;
+    const DevDesc d = make_dev(dd);
+    const WsLayout w = ws_layout(d, T, n_past + T);
+    if (!ws || ws_bytes < w.total) return QSA_ERR_WORKSPACE;
+    if ((s = set_attrs()) != QSA_OK) return s;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (any_new) {
+        if ((s = qsa_append(dd, cache, n_past, T, k_new, v_new, kidx_new, stream)) != QSA_OK) return s;
+    }
+    unsigned char * wsb = static_cast<unsigned char *>(ws);
+    if ((s = launch_select(d, w, T, nullptr, *cache, n_past, q_idx, sel_out, wsb, st)) != QSA_OK) return s;
+    return launch_attend(d, w, T, nullptr, *cache, n_past, q, q_type, out, wsb, st);
+}
+
+qsa_status qsa_check(void * ws, size_t ws_bytes, qsa_stream_t stream) {
+    if (!ws || ws_bytes < 16) return QSA_ERR_WORKSPACE;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    uint32_t h = 0;
+    cudaError_t e = cudaMemcpyAsync(&h, ws, 4, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return QSA_ERR_CUDA;
+    if (h != 0) {
+        if (cudaMemsetAsync(ws, 0, 4, st) != cudaSuccess || cudaStreamSynchronize(st) != cudaSuccess) return QSA_ERR_CUDA;
+        if (h & DEV_TIMEOUT) return QSA_ERR_TIMEOUT;
+        return QSA_ERR_DEVICE_ARG;
+    }
+    return QSA_OK;
+}
+
+int32_t qsa_version(void) { return 100; }
+
+}  // extern "C"

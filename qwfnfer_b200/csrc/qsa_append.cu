@@ -1,0 +1,157 @@
+// qsa_append.cu -- KV append (q8_0/f16 quantisation), raw indexer-key append, pooled-key update.
+//
+// Reference: the cache writes of graph_builder::sparse_attn_decode (ggml_set_rows,
+// src/qwfn_graph.cpp:466-469, 504-528) and sparse_attn/qsa_top_k (ggml_cpy, :249-254, :349-360);
+// the pooled key of a block, qsa_pool_blocks (src/qwfn_graph.cpp:412-429), decode use (:470-476),
+// post-prefill rebuild qsa_pool_rebuild (:431-448) driven from src/qwfn_engine.cpp:761-798.
+#include "qsa_kernels.cuh"
+
+namespace qsa {
+
+// ---------------------------------------------------------------------------------------------
+// One q8_0 block (32 values) per warp, lane = element.  ggml's reference rounding
+// (quantize_row_q8_0_ref): d = amax/127, id = 1/d (0 when d == 0), q = roundf(x*id), d -> f16.
+__device__ __forceinline__ void quantize_q8_0_warp(const float * __restrict__ x, uint8_t * __restrict__ dst, int lane) {
+    const float v = x[lane];
+    float amax = fabsf(v);
+    #pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float d  = __fdiv_rn(amax, 127.0f);
+    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    const float q  = roundf(__fmul_rn(v, id));
+    dst[2 + lane] = (uint8_t) (int8_t) (int) q;
+    if (lane == 0) *reinterpret_cast<uint16_t *>(dst) = f32_to_f16_bits(d);   // q8_0 blocks are 2-byte aligned
+}
+
+// Write one token row of K (or V) with a whole CTA: kv_dim/32 q8_0 blocks, one per warp in turn.
+__device__ __forceinline__ void write_kv_row(const DevDesc & d, int type, const float * __restrict__ x,
+                                             uint8_t * __restrict__ row, int kv_dim) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    if (type == QSA_TYPE_Q8_0) {
+        for (int b = warp; b < kv_dim / QK8_0; b += nw)
+            quantize_q8_0_warp(x + b * QK8_0, row + (size_t) b * Q8_0_BYTES, lane);
+    } else {
+        uint16_t * h = reinterpret_cast<uint16_t *>(row);
+        for (int i = threadIdx.x; i < kv_dim; i += blockDim.x) h[i] = f32_to_f16_bits(x[i]);
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Pooled key of block b by one warp; lane owns dims 4*lane .. 4*lane+3 (idx_dim == 128).
+// Arithmetic as the oracle restates qsa_pool_blocks: sequential f32 sum of the r member rows,
+// times the f32 1/r; sum of squares of f32 products in double, mean rounded to f32,
+// scale = 1/sqrtf(mean + eps) (IEEE), times k_norm_w; IMRoPE at position b*r with the angle of
+// pair i obtained by i successive f32 multiplies by theta_scale (ggml's cache recurrence), cos and
+// sin of that f32 angle (evaluated in double and rounded), NEOX pairs (i, i + rope_dim/2).
+__device__ void pool_block_warp(const DevDesc & d, const uint16_t * __restrict__ idx, int64_t b,
+                                uint16_t * __restrict__ pool_row, float * __restrict__ out_f32) {
+    const int lane = threadIdx.x & 31;
+    const int r = d.ratio;
+    float x[4] = {0.f, 0.f, 0.f, 0.f};
+    const uint16_t * base = idx + (size_t) b * r * MAX_IDX_DIM + 4 * lane;
+    for (int i = 0; i < r; i++) {
+        const uint2 w = *reinterpret_cast<const uint2 *>(base + (size_t) i * MAX_IDX_DIM);
+        const float v0 = f16_bits_to_f32((uint16_t) (w.x & 0xffff)), v1 = f16_bits_to_f32((uint16_t) (w.x >> 16));
+        const float v2 = f16_bits_to_f32((uint16_t) (w.y & 0xffff)), v3 = f16_bits_to_f32((uint16_t) (w.y >> 16));
+        if (i == 0) { x[0] = v0; x[1] = v1; x[2] = v2; x[3] = v3; }
+        else { x[0] = __fadd_rn(x[0], v0); x[1] = __fadd_rn(x[1], v1); x[2] = __fadd_rn(x[2], v2); x[3] = __fadd_rn(x[3], v3); }
+    }
+    double ss = 0.0;
+    #pragma unroll
+    for (int e = 0; e < 4; e++) {
+        x[e] = __fmul_rn(x[e], d.inv_ratio);
+        ss += (double) __fmul_rn(x[e], x[e]);
+    }
+    #pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float mean  = (float) (ss / (double) d.idx_dim);
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, d.rms_eps)));
+    #pragma unroll
+    for (int e = 0; e < 4; e++) {
+        x[e] = __fmul_rn(x[e], scale);
+        if (d.k_norm_w) x[e] = __fmul_rn(x[e], d.k_norm_w[4 * lane + e]);
+    }
+    // IMRoPE: pair i rotates dims (i, i + rope_dim/2), i < rope_dim/2.
+    const int half = d.rope_dim / 2;
+    float y[4] = {x[0], x[1], x[2], x[3]};
+    const int sect_dims = d.sections[0] + d.sections[1] + d.sections[2] + d.sections[3];
+    const float p = (float) (b * r);
+    #pragma unroll
+    for (int e = 0; e < 4; e++) {
+        const int dim = 4 * lane + e;
+        const bool first = dim < half, second = dim >= half && dim < d.rope_dim;
+        const int i = first ? dim : dim - half;                 // pair index
+        float partner = __shfl_sync(0xffffffffu, x[e], first ? lane + half / 4 : (lane - half / 4) & 31);
+        if (first || second) {
+            float th = p;
+            for (int k = 0; k < i; k++) th = __fmul_rn(th, d.theta_scale);
+            const int sector = i % sect_dims;
+            const bool use_pos = (sector % 3 == 1 && sector < 3 * d.sections[1]) ||
+                                 (sector % 3 == 2 && sector < 3 * d.sections[2]) ||
+                                 (sector % 3 == 0 && sector < 3 * d.sections[0]);
+            if (!use_pos) th = 0.0f;                            // the 4th section's position is 0
+            double sd, cd;
+            sincos((double) th, &sd, &cd);
+            const float c = (float) cd, s = (float) sd;
+            if (first) y[e] = __fsub_rn(__fmul_rn(x[e], c), __fmul_rn(partner, s));     // x0*c - x1*s
+            else       y[e] = __fadd_rn(__fmul_rn(partner, s), __fmul_rn(x[e], c));     // x0*s + x1*c
+        }
+    }
+    uint2 o;
+    o.x = (uint32_t) f32_to_f16_bits(y[0]) | ((uint32_t) f32_to_f16_bits(y[1]) << 16);
+    o.y = (uint32_t) f32_to_f16_bits(y[2]) | ((uint32_t) f32_to_f16_bits(y[3]) << 16);
+    *reinterpret_cast<uint2 *>(pool_row + 4 * lane) = o;
+    if (out_f32) *reinterpret_cast<float4 *>(out_f32 + 4 * lane) = make_float4(y[0], y[1], y[2], y[3]);
+}
+
+// ---------------------------------------------------------------------------------------------
+// Append of n_tok rows at pos0 (one CTA per token).  Pool updates run afterwards (pool kernel).
+__global__ void __launch_bounds__(256) append_rows_kernel(DevDesc d, qsa_layer_cache c, int pos0,
+        const float * __restrict__ k, const float * __restrict__ v, const float * __restrict__ kidx) {
+    const int t = blockIdx.x, row = pos0 + t;
+    const int kv_dim = d.n_head_kv * d.head_dim;
+    if (k) write_kv_row(d, d.type_k, k + (size_t) t * kv_dim, (uint8_t *) c.k + (size_t) row * d.rb_k, kv_dim);
+    if (v) write_kv_row(d, d.type_v, v + (size_t) t * kv_dim, (uint8_t *) c.v + (size_t) row * d.rb_v, kv_dim);
+    if (kidx)
+        for (int i = threadIdx.x; i < d.idx_dim; i += blockDim.x)
+            c.idx[(size_t) row * d.idx_dim + i] = f32_to_f16_bits(kidx[(size_t) t * d.idx_dim + i]);
+}
+
+// Pooled keys of blocks [blk0, blk0+n_blk): one warp per block.
+__global__ void __launch_bounds__(256) pool_blocks_kernel(DevDesc d, const uint16_t * __restrict__ idx,
+        uint16_t * __restrict__ pool, int blk0, int n_blk, float * __restrict__ out_f32) {
+    const int j = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (j >= n_blk) return;
+    const int64_t b = blk0 + j;
+    pool_block_warp(d, idx, b, pool + (size_t) b * d.idx_dim, out_f32 ? out_f32 + (size_t) j * d.idx_dim : nullptr);
+}
+
+// Decode append for a batch: CTA s writes row n_past of sequence s (K, V, raw key) and, when
+// that row completes its block, the block's pooled key (as the reference recomputes the
+// current block every token and stores it, src/qwfn_graph.cpp:470-476; only a complete block's
+// pooled key is ever read, an incomplete block being forced by the bias).
+__global__ void __launch_bounds__(256) append_decode_kernel(DevDesc d, const qsa_decode_item * __restrict__ items,
+        const float * __restrict__ k, const float * __restrict__ v, const float * __restrict__ kidx,
+        uint32_t * __restrict__ status) {
+    const int s = blockIdx.x;
+    const qsa_decode_item it = items[s];
+    const int row = it.n_past;
+    if (row < 0 || row >= d.n_ctx) {
+        if (threadIdx.x == 0) set_status(status, DEV_BAD_POS);
+        return;
+    }
+    const int kv_dim = d.n_head_kv * d.head_dim;
+    if (k) write_kv_row(d, d.type_k, k + (size_t) s * kv_dim, (uint8_t *) it.cache.k + (size_t) row * d.rb_k, kv_dim);
+    if (v) write_kv_row(d, d.type_v, v + (size_t) s * kv_dim, (uint8_t *) it.cache.v + (size_t) row * d.rb_v, kv_dim);
+    if (kidx) {
+        for (int i = threadIdx.x; i < d.idx_dim; i += blockDim.x)
+            it.cache.idx[(size_t) row * d.idx_dim + i] = f32_to_f16_bits(kidx[(size_t) s * d.idx_dim + i]);
+        __syncthreads();
+        if ((row + 1) % d.ratio == 0 && threadIdx.x < 32) {
+            const int64_t b = row / d.ratio;
+            pool_block_warp(d, it.cache.idx, b, it.cache.pool + (size_t) b * d.idx_dim, nullptr);
+        }
+    }
+}
+
+}  // namespace qsa

@@ -1,0 +1,569 @@
+// qsa_attn.cu -- block-sparse split-K flash attention over the selected q8_0 / f16 KV rows.
+//
+// Reference: ggml_flash_attn_ext over the gathered cells with the cell mask, precision F32,
+// scale 1/sqrt(head_dim), GQA (src/qwfn_graph.cpp:497-502, 530-541; prefill :362-403).
+//
+// Work item = (query t, chunk of 64-cell tiles), both KV heads in one CTA of 8 warps.  The
+// selected blocks of a query, ascending, expand to a cell list (block b -> cells b*r ..
+// b*r+r-1); a tile is 64 consecutive entries.
+//   - the rows of one block are contiguous in the cache (row = both heads, 544 B in q8_0), so a
+//     tile arrives as one bulk-async copy per block-run of valid rows (cells <= the query
+//     position) for K and for V, into a ring of shared-memory stages completed by mbarrier
+//     transaction counts; rows past the query or past the list are not fetched, they are masked
+//     in registers (their scores -inf, their V scales / f16 values zero);
+//   - warps 0-3 take KV head 0, warps 4-7 KV head 1, 16 cells each; the 8 query heads of a KV
+//     head are the N=8 dimension of mma.m16n8k16: S^T = K Q^T (cells x heads), O^T += V^T P;
+//   - q8_0 is dequantised in registers: int8 bytes become exact f16 integers; the K scale
+//     multiplies the f32 partial dot of each 32-dim group, the V scale multiplies P;
+//   - online softmax in the exp2 domain with warp shuffles; warps merge in shared memory; the
+//     CTAs of a thread-block cluster (consecutive chunks) merge through distributed shared
+//     memory; clusters merge through global memory in the last one to arrive (arrival counter
+//     with acquire/release, no waiting).
+#include <cooperative_groups.h>
+
+#include "qsa_kernels.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace qsa {
+
+constexpr int ATT_THREADS = 256;
+constexpr int ATT_WARPS   = 8;
+constexpr int HROWS       = 16;        // 2 KV heads x 8 query heads: rows of the CTA state
+
+template <int KV_TYPE> struct AttnCfg;
+template <> struct AttnCfg<QSA_TYPE_Q8_0> {
+    static constexpr int HB     = 272;   // one head of a q8_0 row: 8 blocks x 34 B
+    static constexpr int NSTAGE = 3;
+};
+template <> struct AttnCfg<QSA_TYPE_F16> {
+    static constexpr int HB     = 512;
+    static constexpr int NSTAGE = 1;
+};
+
+// shared-memory row = the KV heads of the CTA (all heads of a row: n_head_kv <= 2)
+template <int KV_TYPE> constexpr int attn_row_bytes() { return 2 * AttnCfg<KV_TYPE>::HB; }
+template <int KV_TYPE> constexpr int attn_stage_bytes() { return 2 * CELLS_TILE * attn_row_bytes<KV_TYPE>(); }
+template <int KV_TYPE> constexpr int attn_smem_bytes() {
+    return AttnCfg<KV_TYPE>::NSTAGE * attn_stage_bytes<KV_TYPE>() + MAX_KB * 4 + HROWS * HEAD_DIM * 2 + 64;
+}
+
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&a)[4], const void * p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3]) : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Cell of list entry `idx` of a query (cells of the selected blocks, in order).
+__device__ __forceinline__ int list_cell(const int * sel, int r, int idx) { return sel[idx / r] * r + idx % r; }
+
+template <int KV_TYPE>
+__global__ void __launch_bounds__(ATT_THREADS, 1) attn_kernel(
+        DevDesc d, const qsa_decode_item * __restrict__ items, qsa_layer_cache cache0, int n_past0,
+        const void * __restrict__ q, int q_type,
+        const int * __restrict__ sel_ws, const int * __restrict__ nsel_ws, int tiles_per_cta, int max_chunks,
+        float * __restrict__ part_o, float * __restrict__ part_ml, unsigned * __restrict__ counters,
+        float * __restrict__ out, uint32_t * __restrict__ status) {
+    using Cfg = AttnCfg<KV_TYPE>;
+    constexpr int NS = Cfg::NSTAGE, HB = Cfg::HB, RB = attn_row_bytes<KV_TYPE>();
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ uint64_t full_bar[NS];
+    __shared__ bool is_last;
+
+    const int t = blockIdx.y, chunk = blockIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int r8 = lane >> 2, j4 = lane & 3;
+    const int hs = warp >> 2;                 // KV head of this warp
+    const int cw = warp & 3;                  // 16-cell slice of the tile
+    const bool head_live = hs < d.n_head_kv;
+    int * sel = reinterpret_cast<int *>(smem + NS * attn_stage_bytes<KV_TYPE>());
+    __half * qs = reinterpret_cast<__half *>(smem + NS * attn_stage_bytes<KV_TYPE>() + MAX_KB * 4);
+
+    // ---- prologue: every input load is independent, issued together
+    int qpos;
+    const uint8_t * kbase;
+    const uint8_t * vbase;
+    if (items) {
+        qpos = items[t].n_past;
+        kbase = (const uint8_t *) items[t].cache.k;
+        vbase = (const uint8_t *) items[t].cache.v;
+    } else {
+        qpos = n_past0 + t;
+        kbase = (const uint8_t *) cache0.k;
+        vbase = (const uint8_t *) cache0.v;
+    }
+    const int nsel_raw = nsel_ws[t];
+    for (int i = tid; i < d.kb; i += ATT_THREADS) sel[i] = sel_ws[(size_t) t * d.kb + i];
+    {   // Q of the CTA's query heads -> f16 (the reference converts Q to K's vec_dot type, F16)
+        for (int i = tid; i < HROWS * HEAD_DIM / 8; i += ATT_THREADS) {
+            const int hrow = (i * 8) / HEAD_DIM, h = hrow & 7, g = hrow >> 3;
+            float f[8];
+            if (g < d.n_head_kv && h < d.gqa) {
+                const size_t o = ((size_t) t * d.n_head + g * d.gqa + h) * HEAD_DIM + (i * 8) % HEAD_DIM;
+                if (q_type == QSA_TYPE_BF16) {
+                    const uint4 w = *reinterpret_cast<const uint4 *>(reinterpret_cast<const __nv_bfloat16 *>(q) + o);
+                    const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+                    #pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        f[2 * k]     = __uint_as_float(ww[k] << 16);
+                        f[2 * k + 1] = __uint_as_float(ww[k] & 0xffff0000u);
+                    }
+                } else {
+                    const float4 a = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(q) + o);
+                    const float4 b = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(q) + o + 4);
+                    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+                }
+            } else {
+                #pragma unroll
+                for (int k = 0; k < 8; k++) f[k] = 0.0f;
+            }
+            uint4 o4;
+            o4.x = pack_f16x2(f[0], f[1]); o4.y = pack_f16x2(f[2], f[3]);
+            o4.z = pack_f16x2(f[4], f[5]); o4.w = pack_f16x2(f[6], f[7]);
+            *reinterpret_cast<uint4 *>(qs + i * 8) = o4;
+        }
+    }
+    const bool pos_ok = qpos >= 0 && qpos < d.n_ctx;
+    const int nsel = pos_ok ? max(0, min(nsel_raw, d.kb)) : 0;
+    const int r = d.ratio;
+    const int RBr = (int) d.rb_k;                        // cache row bytes: the run copies' row pitch
+    const int n_cells = nsel * r;
+    const int n_tiles = (n_cells + CELLS_TILE - 1) / CELLS_TILE;
+    const int n_chunks = (n_tiles + tiles_per_cta - 1) / tiles_per_cta;
+    float * outq = out + (size_t) t * d.n_head * HEAD_DIM;
+    if (n_chunks == 0) {                       // nothing selected (or a bad position): zero output
+        if (chunk == 0)
+            for (int i = tid; i < d.n_head * HEAD_DIM; i += ATT_THREADS) outq[i] = 0.0f;
+        return;
+    }
+    {   // whole clusters past the last chunk have nothing to merge (uniform within a cluster)
+        const int CL = (int) cg::this_cluster().num_blocks();
+        if ((chunk / CL) * CL >= n_chunks) return;
+    }
+    if ((smem_u32(smem) & 15u) != 0) {        // bulk copies need 16-byte aligned destinations;
+        if (tid == 0) set_status(status, DEV_BAD_SEL);   // the same in every CTA, so every CTA of
+        return;                                           // a cluster leaves before any cluster barrier
+    }
+    const int tile0 = chunk * tiles_per_cta;
+    // chunks past the last tile (inside a partly used cluster) contribute an empty state
+    const int n_local = chunk < n_chunks ? min(tiles_per_cta, n_tiles - tile0) : 0;
+    if (tid == 0) {
+        for (int s = 0; s < NS; s++) mbar_init(&full_bar[s], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    auto stage_k = [&](int s) { return smem + s * attn_stage_bytes<KV_TYPE>(); };
+    auto stage_v = [&](int s) { return smem + s * attn_stage_bytes<KV_TYPE>() + CELLS_TILE * RB; };  // RB >= row bytes
+    // Warp 0 issues local tile i into stage i % NS: one copy per block-run of valid rows.
+    auto issue = [&](int i) {
+        const int s = i % NS;
+        const int e_lo = (tile0 + i) * CELLS_TILE;
+        const int e_hi = min(e_lo + CELLS_TILE, n_cells);
+        const int j_lo = e_lo / r, j_hi = (e_hi - 1) / r;
+        // per run j: entries [max(e_lo, j r), min(e_hi, (j+1) r)), valid while the cell <= qpos
+        uint32_t bytes = 0;
+        for (int j = j_lo + lane; j <= j_hi; j += 32) {
+            const int a = max(e_lo, j * r), b = min(e_hi, (j + 1) * r);
+            const int cs = sel[j] * r + (a - j * r);
+            const int nv = max(0, min(b - a, qpos - cs + 1));
+            bytes += (uint32_t) nv * RBr * 2;
+        }
+        #pragma unroll
+        for (int off = 16; off > 0; off >>= 1) bytes += __shfl_xor_sync(0xffffffffu, bytes, off);
+        if (lane == 0) mbar_arrive_expect_tx(&full_bar[s], bytes);
+        __syncwarp();
+        for (int j = j_lo + lane; j <= j_hi; j += 32) {
+            const int a = max(e_lo, j * r), b = min(e_hi, (j + 1) * r);
+            const int cs = sel[j] * r + (a - j * r);
+            const int nv = max(0, min(b - a, qpos - cs + 1));
+            if (nv > 0) {
+                bulk_g2s(stage_k(s) + (a - e_lo) * RBr, kbase + (size_t) cs * d.rb_k, (uint32_t) nv * RBr, &full_bar[s]);
+                bulk_g2s(stage_v(s) + (a - e_lo) * RBr, vbase + (size_t) cs * d.rb_v, (uint32_t) nv * RBr, &full_bar[s]);
+            }
+        }
+    };
+    if (warp == 0)
+        for (int i = 0; i < min(NS, n_local); i++) issue(i);
+
+    // Q fragments (B operand) of this warp's KV head; head n = r8 of the 8-head tile
+    const __half * qrow = qs + (hs * 8 + r8) * HEAD_DIM;
+    auto pk2 = [&](int d0, int d1) -> uint32_t {
+        __half2 h = __halves2half2(qrow[d0], qrow[d1]);
+        return *reinterpret_cast<uint32_t *>(&h);
+    };
+    uint32_t qb[16][2];
+    if (KV_TYPE == QSA_TYPE_Q8_0) {
+        // group g8 (32 dims), k-tile kt: virtual k (2j,2j+1) -> dims 8j+4kt+{0,2}; (2j+8,2j+9) -> 8j+4kt+{1,3}
+        #pragma unroll
+        for (int g8 = 0; g8 < 8; g8++)
+            #pragma unroll
+            for (int kt = 0; kt < 2; kt++) {
+                const int base = 32 * g8 + 8 * j4 + 4 * kt;
+                qb[2 * g8 + kt][0] = pk2(base + 0, base + 2);
+                qb[2 * g8 + kt][1] = pk2(base + 1, base + 3);
+            }
+    } else {
+        #pragma unroll
+        for (int kt = 0; kt < 16; kt++) {
+            const int base = 16 * kt + 2 * j4;
+            qb[kt][0] = pk2(base + 0, base + 1);
+            qb[kt][1] = pk2(base + 8, base + 9);
+        }
+    }
+
+    float o[16][4];
+    #pragma unroll
+    for (int i = 0; i < 16; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+    const int rA = 16 * cw + r8, rB = rA + 8;           // this thread's S^T rows (cells of the tile)
+    const int c0 = 16 * cw + 2 * j4;                     // this thread's V^T columns: c0+{0,1,8,9}
+    const int hoff = hs * HB;                            // byte offset of this warp's head in a row
+    const int rb = (int) d.rb_k;                         // row bytes (= smem row stride), K and V alike
+
+    for (int i = 0; i < n_local; i++) {
+        const int s = i % NS;
+        mbar_wait_bounded(&full_bar[s], (uint32_t) ((i / NS) & 1), status);
+        const int e0 = (tile0 + i) * CELLS_TILE;
+        auto valid = [&](int row) { const int e = e0 + row; return e < n_cells && list_cell(sel, r, e) <= qpos; };
+        const bool okA = valid(rA), okB = valid(rB);
+        if (head_live) {
+            const uint8_t * Kt = stage_k(s) + hoff;
+            const uint8_t * Vt = stage_v(s) + hoff;
+            // ---- S^T = K Q^T for the warp's 16 cells x 8 heads
+            float sc[4] = {0.f, 0.f, 0.f, 0.f};
+            if (KV_TYPE == QSA_TYPE_Q8_0) {
+                #pragma unroll
+                for (int g8 = 0; g8 < 8; g8++) {
+                    const uint8_t * ka = Kt + rA * rb + Q8_0_BYTES * g8;
+                    const uint8_t * kb = Kt + rB * rb + Q8_0_BYTES * g8;
+                    const float dA = f16_bits_to_f32(*reinterpret_cast<const uint16_t *>(ka));
+                    const float dB = f16_bits_to_f32(*reinterpret_cast<const uint16_t *>(kb));
+                    const uint32_t w0A = lds_u32_a2(ka + 2 + 8 * j4), w1A = lds_u32_a2(ka + 6 + 8 * j4);
+                    const uint32_t w0B = lds_u32_a2(kb + 2 + 8 * j4), w1B = lds_u32_a2(kb + 6 + 8 * j4);
+                    float c[4] = {0.f, 0.f, 0.f, 0.f};
+                    const uint32_t a0[4] = {i8x2_even_to_f16x2(w0A), i8x2_even_to_f16x2(w0B),
+                                            i8x2_odd_to_f16x2(w0A), i8x2_odd_to_f16x2(w0B)};
+                    const uint32_t a1[4] = {i8x2_even_to_f16x2(w1A), i8x2_even_to_f16x2(w1B),
+                                            i8x2_odd_to_f16x2(w1A), i8x2_odd_to_f16x2(w1B)};
+                    mma_f16_16816(c, a0, qb[2 * g8]);
+                    mma_f16_16816(c, a1, qb[2 * g8 + 1]);
+                    sc[0] = fmaf(dA, c[0], sc[0]); sc[1] = fmaf(dA, c[1], sc[1]);
+                    sc[2] = fmaf(dB, c[2], sc[2]); sc[3] = fmaf(dB, c[3], sc[3]);
+                }
+            } else {
+                #pragma unroll
+                for (int kt = 0; kt < 16; kt++) {
+                    const uint8_t * ka = Kt + rA * rb + 2 * (16 * kt + 2 * j4);
+                    const uint8_t * kb = Kt + rB * rb + 2 * (16 * kt + 2 * j4);
+                    const uint32_t a[4] = {*reinterpret_cast<const uint32_t *>(ka), *reinterpret_cast<const uint32_t *>(kb),
+                                           *reinterpret_cast<const uint32_t *>(ka + 16), *reinterpret_cast<const uint32_t *>(kb + 16)};
+                    mma_f16_16816(sc, a, qb[kt]);
+                }
+            }
+            // ---- mask, scale to the exp2 domain, online softmax (heads 2j, 2j+1 of this thread)
+            sc[0] = okA ? sc[0] * d.scale_log2 : -INFINITY;
+            sc[1] = okA ? sc[1] * d.scale_log2 : -INFINITY;
+            sc[2] = okB ? sc[2] * d.scale_log2 : -INFINITY;
+            sc[3] = okB ? sc[3] * d.scale_log2 : -INFINITY;
+            float mx0 = fmaxf(sc[0], sc[2]), mx1 = fmaxf(sc[1], sc[3]);
+            #pragma unroll
+            for (int off = 4; off < 32; off <<= 1) {
+                mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+                mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+            }
+            const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+            const float mu0 = mn0 == -INFINITY ? 0.0f : mn0, mu1 = mn1 == -INFINITY ? 0.0f : mn1;
+            const float al0 = exp2f(m0 - mu0), al1 = exp2f(m1 - mu1);
+            float p[4];
+            p[0] = exp2f(sc[0] - mu0); p[1] = exp2f(sc[1] - mu1);
+            p[2] = exp2f(sc[2] - mu0); p[3] = exp2f(sc[3] - mu1);
+            l0 = l0 * al0 + p[0] + p[2];
+            l1 = l1 * al1 + p[1] + p[3];
+            m0 = mn0; m1 = mn1;
+            #pragma unroll
+            for (int k = 0; k < 16; k++) { o[k][0] *= al0; o[k][1] *= al1; o[k][2] *= al0; o[k][3] *= al1; }
+
+            // ---- O^T += V^T P   (rows not fetched are masked: zero scale / zero values)
+            if (KV_TYPE == QSA_TYPE_Q8_0) {
+                #pragma unroll
+                for (int g8 = 0; g8 < 8; g8++) {
+                    float dA = f16_bits_to_f32(*reinterpret_cast<const uint16_t *>(Vt + rA * rb + Q8_0_BYTES * g8));
+                    float dB = f16_bits_to_f32(*reinterpret_cast<const uint16_t *>(Vt + rB * rb + Q8_0_BYTES * g8));
+                    dA = okA ? dA : 0.0f;
+                    dB = okB ? dB : 0.0f;
+                    uint32_t b[2];
+                    b[0] = movmatrix_trans(pack_f16x2(p[0] * dA, p[1] * dA));
+                    b[1] = movmatrix_trans(pack_f16x2(p[2] * dB, p[3] * dB));
+                    const int off = Q8_0_BYTES * g8 + 2 + 4 * r8;
+                    const uint32_t W0 = lds_u32_a2(Vt + (c0 + 0) * rb + off);
+                    const uint32_t W1 = lds_u32_a2(Vt + (c0 + 1) * rb + off);
+                    const uint32_t W2 = lds_u32_a2(Vt + (c0 + 8) * rb + off);
+                    const uint32_t W3 = lds_u32_a2(Vt + (c0 + 9) * rb + off);
+                    const uint32_t am0[4] = {i8_pair_to_f16x2<0>(W0, W1), i8_pair_to_f16x2<1>(W0, W1),
+                                             i8_pair_to_f16x2<0>(W2, W3), i8_pair_to_f16x2<1>(W2, W3)};
+                    const uint32_t am1[4] = {i8_pair_to_f16x2<2>(W0, W1), i8_pair_to_f16x2<3>(W0, W1),
+                                             i8_pair_to_f16x2<2>(W2, W3), i8_pair_to_f16x2<3>(W2, W3)};
+                    mma_f16_16816(o[2 * g8], am0, b);
+                    mma_f16_16816(o[2 * g8 + 1], am1, b);
+                }
+            } else {
+                uint32_t b[2];
+                b[0] = movmatrix_trans(pack_f16x2(p[0], p[1]));
+                b[1] = movmatrix_trans(pack_f16x2(p[2], p[3]));
+                const uint32_t m01 = (valid(c0) ? 0x0000ffffu : 0u) | (valid(c0 + 1) ? 0xffff0000u : 0u);
+                const uint32_t m89 = (valid(c0 + 8) ? 0x0000ffffu : 0u) | (valid(c0 + 9) ? 0xffff0000u : 0u);
+                const int cl = 16 * cw + (lane & 7) + ((lane >> 4) << 3);   // ldmatrix row: cell
+                const int dh = ((lane >> 3) & 1) << 3;                        // +8 dims for matrices 1, 3
+                #pragma unroll
+                for (int mt = 0; mt < 16; mt++) {
+                    uint32_t a[4];
+                    ldmatrix_x4_trans(a, Vt + cl * rb + 2 * (16 * mt + dh));
+                    a[0] &= m01; a[1] &= m01; a[2] &= m89; a[3] &= m89;
+                    mma_f16_16816(o[mt], a, b);
+                }
+            }
+        }
+        __syncthreads();                              // every warp is done with stage s
+        if (warp == 0 && i + NS < n_local) {
+            fence_proxy_async_smem();
+            issue(i + NS);
+        }
+    }
+
+    // ---- merge the 4 warps of each KV head (stage memory is free)
+    #pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+        l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+    }
+    float * wm = reinterpret_cast<float *>(smem);               // [8 warps][8 heads] max
+    float * wl = wm + ATT_WARPS * 8;                             // [8][8] sum
+    float * wo = wl + ATT_WARPS * 8;                             // [8][8][256] unnormalised O
+    float * cm = wo + ATT_WARPS * 8 * HEAD_DIM;                  // CTA state: [16] M, [16] L
+    float * co = cm + 2 * HROWS;                                 // CTA state: [16][256] O (scaled to M)
+    if (r8 == 0) {
+        wm[warp * 8 + 2 * j4] = m0; wm[warp * 8 + 2 * j4 + 1] = m1;
+        wl[warp * 8 + 2 * j4] = l0; wl[warp * 8 + 2 * j4 + 1] = l1;
+    }
+    float * myo = wo + warp * 8 * HEAD_DIM;
+    if (KV_TYPE == QSA_TYPE_Q8_0) {
+        #pragma unroll
+        for (int g8 = 0; g8 < 8; g8++) {
+            const int dim = 32 * g8 + 4 * r8;
+            *reinterpret_cast<float4 *>(myo + (2 * j4) * HEAD_DIM + dim) =
+                make_float4(o[2 * g8][0], o[2 * g8][2], o[2 * g8 + 1][0], o[2 * g8 + 1][2]);
+            *reinterpret_cast<float4 *>(myo + (2 * j4 + 1) * HEAD_DIM + dim) =
+                make_float4(o[2 * g8][1], o[2 * g8][3], o[2 * g8 + 1][1], o[2 * g8 + 1][3]);
+        }
+    } else {
+        #pragma unroll
+        for (int mt = 0; mt < 16; mt++) {
+            const int dim = 16 * mt + r8;
+            myo[(2 * j4) * HEAD_DIM + dim]         = o[mt][0];
+            myo[(2 * j4 + 1) * HEAD_DIM + dim]     = o[mt][1];
+            myo[(2 * j4) * HEAD_DIM + dim + 8]     = o[mt][2];
+            myo[(2 * j4 + 1) * HEAD_DIM + dim + 8] = o[mt][3];
+        }
+    }
+    __syncthreads();
+    if (tid < HROWS) {   // row hr = 8*head + h: M = max over the head's 4 warps, L = sum l 2^(m - M)
+        const int w0 = (tid >> 3) * 4, h = tid & 7;
+        float M = -INFINITY;
+        for (int w = w0; w < w0 + 4; w++) M = fmaxf(M, wm[w * 8 + h]);
+        const float Mu = M == -INFINITY ? 0.0f : M;
+        float L = 0.0f;
+        for (int w = w0; w < w0 + 4; w++) L += wl[w * 8 + h] * exp2f(wm[w * 8 + h] - Mu);
+        cm[tid] = M; cm[HROWS + tid] = L;
+    }
+    __syncthreads();
+    for (int e = tid; e < HROWS * HEAD_DIM; e += ATT_THREADS) {
+        const int hr = e / HEAD_DIM, w0 = (hr >> 3) * 4, h = hr & 7, dim = e % HEAD_DIM;
+        const float Mu = cm[hr] == -INFINITY ? 0.0f : cm[hr];
+        float acc = 0.0f;
+        #pragma unroll
+        for (int w = 0; w < 4; w++) acc += wo[((w0 + w) * 8 + h) * HEAD_DIM + dim] * exp2f(wm[(w0 + w) * 8 + h] - Mu);
+        co[e] = acc;
+    }
+    __syncthreads();
+
+    // ---- first combine level: the CTAs of a cluster (consecutive chunks of query t) merge through
+    // distributed shared memory into cluster rank 0
+    cg::cluster_group cluster = cg::this_cluster();
+    const int CL = (int) cluster.num_blocks();
+    const int crank = (int) cluster.block_rank();
+    const int cl_id = chunk / CL;
+    const int n_cl = (n_chunks + CL - 1) / CL;
+    cluster.sync();                                   // every CTA's cm/co are complete
+    float * red = co + HROWS * HEAD_DIM;              // [16] M, [16] L, [8 ranks][16] ranks' m then weights
+    float * rl = red + 2 * HROWS + 8 * HROWS;         // [8 ranks][16] ranks' l
+    float * ro = reinterpret_cast<float *>(smem);     // cluster O [16][256] (wm/wl/wo are free now)
+    if (crank == 0 && CL > 1) {
+        if (tid < CL * HROWS) {                       // all ranks' (m, l) fetched at once
+            const int p = tid / HROWS, hr = tid % HROWS;
+            const float * pc = cluster.map_shared_rank(cm, p);
+            red[2 * HROWS + p * HROWS + hr] = pc[hr];
+            rl[p * HROWS + hr] = pc[HROWS + hr];
+        }
+        __syncthreads();
+        if (tid < HROWS) {
+            float M = -INFINITY;
+            for (int p = 0; p < CL; p++) M = fmaxf(M, red[2 * HROWS + p * HROWS + tid]);
+            const float Mu = M == -INFINITY ? 0.0f : M;
+            float L = 0.0f;
+            for (int p = 0; p < CL; p++) {
+                const float w = exp2f(red[2 * HROWS + p * HROWS + tid] - Mu);
+                red[2 * HROWS + p * HROWS + tid] = w;
+                L += rl[p * HROWS + tid] * w;
+            }
+            red[tid] = M; red[HROWS + tid] = L;
+        }
+        __syncthreads();
+        const float4 * pco[8];
+        #pragma unroll
+        for (int p = 0; p < 8; p++) pco[p] = reinterpret_cast<const float4 *>(cluster.map_shared_rank(co, p < CL ? p : 0));
+        for (int e4 = tid; e4 < HROWS * HEAD_DIM / 4; e4 += ATT_THREADS) {
+            const int hr = (e4 * 4) / HEAD_DIM;
+            float4 v[8];
+            #pragma unroll
+            for (int p = 0; p < 8; p++) v[p] = p < CL ? pco[p][e4] : make_float4(0.f, 0.f, 0.f, 0.f);
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            #pragma unroll
+            for (int p = 0; p < 8; p++) {
+                const float w = p < CL ? red[2 * HROWS + p * HROWS + hr] : 0.0f;
+                acc.x += w * v[p].x; acc.y += w * v[p].y; acc.z += w * v[p].z; acc.w += w * v[p].w;
+            }
+            reinterpret_cast<float4 *>(ro)[e4] = acc;
+        }
+    }
+    cluster.sync();                                   // rank 0 is done reading its peers
+    if (crank != 0) return;
+    const float * rM = CL > 1 ? red : cm;             // cluster state: M[16], L[16], O[16][256]
+    const float * rO = CL > 1 ? ro : co;
+    __syncthreads();
+    const int n_rows = d.n_head_kv * 8;
+    auto write_out = [&](int e4, float4 v, float L) {
+        const int hr = (e4 * 4) / HEAD_DIM, h = hr & 7, g = hr >> 3;
+        if (g < d.n_head_kv && h < d.gqa) {
+            const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+            reinterpret_cast<float4 *>(outq + (size_t) (g * d.gqa + h) * HEAD_DIM)[(e4 * 4 % HEAD_DIM) / 4] =
+                make_float4(v.x * inv, v.y * inv, v.z * inv, v.w * inv);
+        }
+    };
+    if (n_cl == 1) {                                  // the cluster covered every chunk: output
+        for (int e4 = tid; e4 < n_rows * HEAD_DIM / 4; e4 += ATT_THREADS)
+            write_out(e4, reinterpret_cast<const float4 *>(rO)[e4], rM[HROWS + (e4 * 4) / HEAD_DIM]);
+        return;
+    }
+    // ---- second level: cluster partials in global memory, merged by the last cluster to arrive
+    const int max_parts = (max_chunks + CL - 1) / CL;
+    float * po = part_o + ((size_t) t * max_parts + cl_id) * HROWS * HEAD_DIM;
+    for (int e4 = tid; e4 < HROWS * HEAD_DIM / 4; e4 += ATT_THREADS)
+        reinterpret_cast<float4 *>(po)[e4] = reinterpret_cast<const float4 *>(rO)[e4];
+    float * pml = part_ml + ((size_t) t * max_parts + cl_id) * 2 * HROWS;
+    if (tid < 2 * HROWS) pml[tid] = rM[tid];
+    __syncthreads();
+    unsigned * cnt = counters + t;
+    if (tid == 0) {
+        // release this CTA's partial (ordered before by the barrier), acquire the others'
+        unsigned prev;
+        asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], 1;" : "=r"(prev) : "l"(cnt) : "memory");
+        is_last = prev == (unsigned) (n_cl - 1);
+        if (is_last) *cnt = 0;
+    }
+    __syncthreads();
+    if (!is_last) return;
+    const float * pob = part_o + (size_t) t * max_parts * HROWS * HEAD_DIM;
+    const float * pmb = part_ml + (size_t) t * max_parts * 2 * HROWS;
+    float * gm = co;                                  // [n_cl][16] m -> weights (co is free now)
+    float * gl = gm + n_cl * HROWS;                   // [n_cl][16] l
+    float * gML = gl + n_cl * HROWS;                  // [16] M, [16] L
+    for (int i = tid; i < n_cl * 2 * HROWS; i += ATT_THREADS) {     // every (m, l) loaded at once
+        const int c = i / (2 * HROWS), k = i % (2 * HROWS);
+        const float v = __ldcg(pmb + i);
+        if (k < HROWS) gm[c * HROWS + k] = v; else gl[c * HROWS + k - HROWS] = v;
+    }
+    __syncthreads();
+    if (tid < HROWS) {
+        float M = -INFINITY;
+        for (int c = 0; c < n_cl; c++) M = fmaxf(M, gm[c * HROWS + tid]);
+        const float Mu = M == -INFINITY ? 0.0f : M;
+        float L = 0.0f;
+        for (int c = 0; c < n_cl; c++) {
+            const float w = exp2f(gm[c * HROWS + tid] - Mu);
+            gm[c * HROWS + tid] = w;
+            L += gl[c * HROWS + tid] * w;
+        }
+        gML[HROWS + tid] = L;
+    }
+    __syncthreads();
+    const float4 * po4 = reinterpret_cast<const float4 *>(pob);
+    for (int e4 = tid; e4 < n_rows * HEAD_DIM / 4; e4 += ATT_THREADS) {
+        const int hr = (e4 * 4) / HEAD_DIM;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        int c = 0;
+        for (; c + 8 <= n_cl; c += 8) {
+            float4 v[8];
+            #pragma unroll
+            for (int u = 0; u < 8; u++) v[u] = __ldcg(po4 + (size_t) (c + u) * (HROWS * HEAD_DIM / 4) + e4);
+            #pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const float w = gm[(c + u) * HROWS + hr];
+                acc.x += w * v[u].x; acc.y += w * v[u].y; acc.z += w * v[u].z; acc.w += w * v[u].w;
+            }
+        }
+        for (; c < n_cl; c++) {
+            const float4 v = __ldcg(po4 + (size_t) c * (HROWS * HEAD_DIM / 4) + e4);
+            const float w = gm[c * HROWS + hr];
+            acc.x += w * v.x; acc.y += w * v.y; acc.z += w * v.z; acc.w += w * v.w;
+        }
+        write_out(e4, acc, gML[HROWS + hr]);
+    }
+}
+
+cudaError_t attn_set_attrs() {
+    cudaError_t e = cudaFuncSetAttribute(attn_kernel<QSA_TYPE_Q8_0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         attn_smem_bytes<QSA_TYPE_Q8_0>());
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(attn_kernel<QSA_TYPE_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 attn_smem_bytes<QSA_TYPE_F16>());
+    return e;
+}
+
+int attn_cluster_size(int max_chunks) { return max_chunks < 8 ? max_chunks : 8; }
+
+int attn_state_rows() { return HROWS; }
+
+cudaError_t launch_attn(const DevDesc & d, dim3 grid, cudaStream_t st, const qsa_decode_item * items,
+        qsa_layer_cache cache0, int n_past0, const void * q, int q_type, const int * sel_ws, const int * nsel_ws,
+        int tiles_per_cta, int max_chunks, float * part_o, float * part_ml, unsigned * counters, float * out,
+        uint32_t * status) {
+    // CTAs of consecutive chunks of one query form a cluster of up to 8
+    const int CL = attn_cluster_size(max_chunks);
+    grid.x = (unsigned) (((max_chunks + CL - 1) / CL) * CL);
+    grid.y = grid.z;                                  // queries
+    grid.z = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(ATT_THREADS);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned) CL;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (d.type_k == QSA_TYPE_Q8_0) {
+        cfg.dynamicSmemBytes = attn_smem_bytes<QSA_TYPE_Q8_0>();
+        return cudaLaunchKernelEx(&cfg, attn_kernel<QSA_TYPE_Q8_0>, d, items, cache0, n_past0, q, q_type, sel_ws,
+                                  nsel_ws, tiles_per_cta, max_chunks, part_o, part_ml, counters, out, status);
+    }
+    cfg.dynamicSmemBytes = attn_smem_bytes<QSA_TYPE_F16>();
+    return cudaLaunchKernelEx(&cfg, attn_kernel<QSA_TYPE_F16>, d, items, cache0, n_past0, q, q_type, sel_ws,
+                              nsel_ws, tiles_per_cta, max_chunks, part_o, part_ml, counters, out, status);
+}
+
+}  // namespace qsa

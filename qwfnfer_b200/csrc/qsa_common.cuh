@@ -1,0 +1,148 @@
+// qsa_common.cuh -- shared device-side definitions of libqsa (sm_100a).
+#pragma once
+
+#include <cstdint>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "../../include/qsa.h"
+
+namespace qsa {
+
+constexpr int QK8_0        = 32;   // q8_0 block: { f16 d; int8 qs[32] }
+constexpr int Q8_0_BYTES   = 34;
+constexpr int HEAD_DIM     = 256;  // the attention kernels are written for head_dim 256
+constexpr int GQA_TILE     = 8;    // query heads per KV head packed into one MMA N tile
+constexpr int CELLS_TILE   = 64;   // cells per pipeline stage of the attention kernel
+constexpr int MAX_IDX_DIM  = 128;  // indexer key length handled by the pooling/scoring kernels
+
+// Status word codes written by kernels (the host maps them onto qsa_status).
+enum : uint32_t { DEV_OK = 0, DEV_BAD_POS = 1u << 0, DEV_TIMEOUT = 1u << 1, DEV_BAD_SEL = 1u << 2 };
+
+// Descriptor as the kernels see it: the public qsa_desc plus values derived on the host.
+struct DevDesc {
+    int n_head, n_head_kv, head_dim, gqa;
+    int idx_n_head, idx_dim, ratio, top_k, n_force, kb, window;
+    int n_ctx, type_k, type_v, rope_dim;
+    int sections[4];
+    float rms_eps;
+    float theta_scale;      // powf(rope_freq_base, -2/rope_dim), computed by the host libm
+    float inv_ratio;        // 1.0f / ratio
+    float scale_log2;       // log2(e) / sqrt(head_dim)
+    const float * k_norm_w; // may be null
+    int64_t rb_k, rb_v;     // bytes per K/V cache row (all heads)
+    int hb_k, hb_v;         // bytes of one head inside a row
+};
+
+// ------------------------------------------------------------------ small helpers
+__device__ __forceinline__ float f16_bits_to_f32(uint16_t u) { return __half2float(__ushort_as_half(u)); }
+__device__ __forceinline__ uint16_t f32_to_f16_bits(float f) { return __half_as_ushort(__float2half_rn(f)); }
+
+__device__ __forceinline__ float warp_max(float v) {
+    #pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ double warp_sum16_d(double v) {   // butterfly within aligned 16-lane halves
+    #pragma unroll
+    for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ void set_status(uint32_t * status, uint32_t code) {
+    if (status) atomicOr(status, code);
+}
+
+// ------------------------------------------------------------------ mbarrier + bulk copy
+__device__ __forceinline__ uint32_t smem_u32(const void * p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t * bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t * bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;"
+                 :: "r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+// One probe of the phase; returns true when the phase with `parity` has completed.
+__device__ __forceinline__ bool mbar_try_wait(uint64_t * bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(done) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+    return done != 0;
+}
+__device__ __forceinline__ uint64_t global_timer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Wait at most ~2 s of wall time; on running out, flag DEV_TIMEOUT and return false (the
+// caller then skips its work; the host sees QSA_ERR_TIMEOUT from qsa_check).
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t * bar, uint32_t parity, uint32_t * status) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (;;) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (global_timer_ns() - t0 > 2000000000ull) break;
+    }
+    set_status(status, DEV_TIMEOUT);
+    return false;
+}
+// Non-tensor bulk copy global -> this CTA's shared memory, completing on `bar`.
+// Both addresses 16-byte aligned, bytes a multiple of 16.  No multicast.
+__device__ __forceinline__ void bulk_g2s(void * dst, const void * src, uint32_t bytes, uint64_t * bar) {
+    asm volatile("cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 :: "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+
+// ------------------------------------------------------------------ tensor-core fragments
+// mma.sync m16n8k16, f16 x f16 -> f32 (row.col).  Used for the 8-head products of the decode
+// attention, where N = 8 query heads of one KV head.
+__device__ __forceinline__ void mma_f16_16816(float (&c)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+                 "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+// Transpose an 8x8 b16 matrix held in the standard fragment layout.
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+    uint32_t y;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
+}
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&h);
+}
+
+// int8 bytes -> exact f16 values.  For a word w of four int8: f16x2(byte0, byte2) and
+// f16x2(byte1, byte3).  Each byte x becomes the f16 1024 + (x + 128) (bits 0x6400 | (x ^ 0x80))
+// and 1152 is subtracted, exactly.
+__device__ __forceinline__ uint32_t i8x2_even_to_f16x2(uint32_t w) {
+    uint32_t t = (w & 0x00FF00FFu) ^ 0x64806480u;
+    __half2 h = __hsub2(*reinterpret_cast<__half2 *>(&t), __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480)));
+    return *reinterpret_cast<uint32_t *>(&h);
+}
+__device__ __forceinline__ uint32_t i8x2_odd_to_f16x2(uint32_t w) { return i8x2_even_to_f16x2(w >> 8); }
+// f16x2(byte b of w0, byte b of w1)
+template <int B>
+__device__ __forceinline__ uint32_t i8_pair_to_f16x2(uint32_t w0, uint32_t w1) {
+    uint32_t t = __byte_perm(w0, w1, B | ((4 + B) << 8));   // bytes: [w0.B, w0.b0, w1.B, w0.b0]
+    return i8x2_even_to_f16x2(t);
+}
+
+// 32-bit load from shared memory at a 2-byte aligned address (q8_0 rows are 34-byte strided).
+__device__ __forceinline__ uint32_t lds_u32_a2(const uint8_t * p) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    if ((a & 3u) == 0) return *reinterpret_cast<const uint32_t *>(p);
+    const uint32_t * w = reinterpret_cast<const uint32_t *>(a - 2);
+    return __funnelshift_r(w[0], w[1], 16);
+}
+
+}  // namespace qsa

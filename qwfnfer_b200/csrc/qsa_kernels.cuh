@@ -1,0 +1,31 @@
+// qsa_kernels.cuh -- kernel entry points of libqsa and their launch constants.
+#pragma once
+#include "qsa_common.cuh"
+
+namespace qsa {
+
+constexpr int MAX_KB = 1024;          // blocks kept per query that the kernels can hold
+constexpr int SCORE_BLOCKS_PER_CTA = 128;
+
+__global__ void append_rows_kernel(DevDesc d, qsa_layer_cache c, int pos0,
+        const float * k, const float * v, const float * kidx);
+__global__ void pool_blocks_kernel(DevDesc d, const uint16_t * idx, uint16_t * pool, int blk0, int n_blk, float * out_f32);
+__global__ void append_decode_kernel(DevDesc d, const qsa_decode_item * items,
+        const float * k, const float * v, const float * kidx, uint32_t * status);
+
+__global__ void score_select_kernel(DevDesc d, const qsa_decode_item * items, const uint16_t * pool0, int n_past0,
+        const float * q_idx, int blocks_per_cta, float * scores_ws, int scores_stride, unsigned * counters,
+        int * sel_ws, int * nsel_ws, int * sel_out, uint32_t * status);
+
+// Host launcher of the attention kernel (defined beside the kernel template).
+cudaError_t launch_attn(const DevDesc & d, dim3 grid, cudaStream_t st, const qsa_decode_item * items,
+        qsa_layer_cache cache0, int n_past0, const void * q, int q_type, const int * sel_ws, const int * nsel_ws,
+        int tiles_per_cta, int max_chunks, float * part_o, float * part_ml, unsigned * counters, float * out,
+        uint32_t * status);
+cudaError_t attn_set_attrs();
+// CTAs per thread-block cluster of the attention launch (partials are per cluster).
+int attn_cluster_size(int max_chunks);
+// Rows (KV head x query head) of the attention state: a partial is rows x head_dim floats.
+int attn_state_rows();
+
+}  // namespace qsa

@@ -1,0 +1,272 @@
+// qsa_select.cu -- lightning-indexer scores and top-k block selection.
+//
+// Reference: decode scores src/qwfn_graph.cpp:478-492, prefill :277-293 (mul_mat of the F16
+// pooled keys with the indexer query converted to F16, relu per head, sum over heads, + bias);
+// ggml_top_k + block->cell expansion :493-495 / :295-306; the bias rules of
+// src/qwfn_engine.cpp:748-753 (decode) and :936-950 (prefill), applied here as a rule:
+//   visible  = blocks whole at the query, (b+1)*r <= q+1           (bias 0)
+//   forced   = window > 0: blocks b_q-nf+1..b_q; window == 0: b_q while incomplete (bias +1e9)
+//   selected = forced + the (KB - |forced|) best visible non-forced blocks; ties -> lower index.
+//
+// One kernel: CTAs of a query score disjoint block ranges into the workspace; the last CTA of
+// the query to finish (atomic arrival counter, no waiting) selects with a radix select over the
+// scores and writes the ascending block list.
+#include <cub/block/block_scan.cuh>
+
+#include "qsa_kernels.cuh"
+
+namespace qsa {
+
+constexpr int SEL_THREADS = 256;
+
+// Score blocks [b_begin, b_end) of one query: 16 lanes per block row (8 dims = 16 bytes each).
+// Products of two f16 values are exact in f32; they are summed in double (exact for these
+// magnitudes) and rounded once, so the result does not depend on the summation order.
+__device__ __forceinline__ void score_range(const DevDesc & d, const uint16_t * __restrict__ pool,
+        const float (&qf)[4][8], int b_begin, int b_end, float * __restrict__ scores) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int half = lane >> 4, sub = lane & 15;
+    for (int b0 = b_begin + 2 * warp; b0 < b_end; b0 += 2 * nw) {
+        const int b = b0 + half;
+        const bool ok = b < b_end;
+        uint4 w = make_uint4(0, 0, 0, 0);
+        if (ok) w = __ldg(reinterpret_cast<const uint4 *>(pool + (size_t) b * MAX_IDX_DIM + 8 * sub));
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+        float pk[8];
+        #pragma unroll
+        for (int i = 0; i < 4; i++) {
+            pk[2 * i]     = f16_bits_to_f32((uint16_t) (ws[i] & 0xffff));
+            pk[2 * i + 1] = f16_bits_to_f32((uint16_t) (ws[i] >> 16));
+        }
+        double hs = 0.0;
+        #pragma unroll
+        for (int h = 0; h < 4; h++) {
+            if (h >= d.idx_n_head) break;
+            double acc = 0.0;
+            #pragma unroll
+            for (int e = 0; e < 8; e++) acc += (double) __fmul_rn(pk[e], qf[h][e]);
+            acc = warp_sum16_d(acc);
+            const float dot = (float) acc;
+            hs += (double) (dot > 0.0f ? dot : 0.0f);
+        }
+        if (ok && sub == 0) scores[b] = (float) hs;
+    }
+}
+
+// Forced block range of the query at q: [f_lo, f_hi] (empty when f_lo > f_hi).
+__device__ __forceinline__ void forced_range(const DevDesc & d, int q, int & f_lo, int & f_hi) {
+    const int bq = q / d.ratio;
+    if (d.window > 0) { f_lo = max(0, bq - d.n_force + 1); f_hi = bq; }
+    else if ((q + 1) % d.ratio != 0) { f_lo = bq; f_hi = bq; }
+    else { f_lo = 1; f_hi = 0; }
+}
+
+constexpr int HBINS = 4096;      // histogram bins of one selection level (12 key bits)
+constexpr int CAND_MAX = 1024;   // threshold-bin candidates ranked directly
+
+struct SelSmem {
+    typedef cub::BlockScan<int, SEL_THREADS> Scan;
+    typename Scan::TempStorage scan;
+    unsigned hist[HBINS];
+    int cand[CAND_MAX];
+    int ncand;
+    int bcast[4];
+};
+
+// Selection of the query at q by the whole CTA over its scores `sc` (shared memory), writing the
+// ascending block list.  Keys are the bit patterns of the non-negative scores (order-preserving).
+// Threshold search: histograms of 12 key bits ([30:19], then [18:7], then [6:0]) locate the bin
+// holding the cut and how many of its keys to keep; once that bin holds at most CAND_MAX keys
+// they are ranked directly (score, then lower block index).  Keys above the bin are kept.
+__device__ void select_blocks(const DevDesc & d, int q, const float * __restrict__ sc, unsigned char * __restrict__ flag,
+                              int * __restrict__ sel, int * __restrict__ nsel_out, int * __restrict__ sel_out,
+                              SelSmem & sm) {
+    const int tid = threadIdx.x;
+    const int n_vis = (q + 1) / d.ratio;
+    int f_lo, f_hi;
+    forced_range(d, q, f_lo, f_hi);
+    const int n_forced = f_hi >= f_lo ? f_hi - f_lo + 1 : 0;
+    const int want = max(0, d.kb - n_forced);
+    const int n_cand = n_vis - max(0, min(f_hi, n_vis - 1) - f_lo + 1);
+    auto is_cand = [&](int b) { return b < n_vis && !(b >= f_lo && b <= f_hi); };
+    const bool take_all = n_cand <= want;
+    uint32_t prefix = 0, pmask = 0;   // keys with (key & pmask) > prefix are kept
+    int remaining = 0;                // keys with (key & pmask) == prefix to keep
+    bool ranked = false;              // the bin's keys were ranked into flag[]
+    for (int b = tid; b < n_vis; b += blockDim.x) flag[b] = 0;
+    if (!take_all) {
+        remaining = want;
+        const int shifts[3] = {19, 7, 0};
+        const int widths[3] = {12, 12, 7};
+        for (int lv = 0; lv < 3; lv++) {
+            const int shift = shifts[lv], nb = 1 << widths[lv];
+            const uint32_t bmask = (uint32_t) (nb - 1);
+            for (int i = tid; i < nb; i += blockDim.x) sm.hist[i] = 0;
+            __syncthreads();
+            for (int b = tid; b < n_vis; b += blockDim.x) {
+                if (!is_cand(b)) continue;
+                const uint32_t key = __float_as_uint(sc[b]);
+                if ((key & pmask) == prefix) atomicAdd(&sm.hist[(key >> shift) & bmask], 1u);
+            }
+            __syncthreads();
+            // thread i owns bins counted from the top: [nb - per*(i+1), nb - per*i)
+            const int per = (nb + SEL_THREADS - 1) / SEL_THREADS;
+            const int hi_bin = nb - per * tid;
+            int own = 0;
+            for (int k = 0; k < per; k++) {
+                const int bin = hi_bin - 1 - k;
+                if (bin >= 0) own += (int) sm.hist[bin];
+            }
+            int above;
+            SelSmem::Scan(sm.scan).ExclusiveSum(own, above);
+            if (above < remaining && above + own >= remaining) {        // exactly one thread
+                int cum = above, bin = hi_bin - 1;
+                for (int k = 0; k < per; k++, bin--) {
+                    const int h = (int) sm.hist[bin];
+                    if (cum + h >= remaining) break;
+                    cum += h;
+                }
+                sm.bcast[0] = bin;
+                sm.bcast[1] = remaining - cum;
+                sm.bcast[2] = (int) sm.hist[bin];
+            }
+            __syncthreads();
+            prefix |= (uint32_t) sm.bcast[0] << shift;
+            pmask |= bmask << shift;
+            remaining = sm.bcast[1];
+            const int in_bin = sm.bcast[2];
+            __syncthreads();
+            if (in_bin <= CAND_MAX) {
+                // rank the bin's keys directly
+                if (tid == 0) sm.ncand = 0;
+                __syncthreads();
+                for (int b = tid; b < n_vis; b += blockDim.x) {
+                    if (!is_cand(b)) continue;
+                    if ((__float_as_uint(sc[b]) & pmask) == prefix) {
+                        const int slot = atomicAdd(&sm.ncand, 1);
+                        if (slot < CAND_MAX) sm.cand[slot] = b;
+                    }
+                }
+                __syncthreads();
+                const int m = min(sm.ncand, CAND_MAX);
+                for (int i = tid; i < m; i += blockDim.x) {
+                    const int bi = sm.cand[i];
+                    const uint32_t ki = __float_as_uint(sc[bi]);
+                    int rank = 0;
+                    for (int jx = 0; jx < m; jx++) {
+                        const int bj = sm.cand[jx];
+                        const uint32_t kj = __float_as_uint(sc[bj]);
+                        rank += (kj > ki) || (kj == ki && bj < bi);
+                    }
+                    if (rank < remaining) flag[bi] = 1;
+                }
+                ranked = true;
+                break;
+            }
+        }
+        __syncthreads();
+    }
+    // Compaction over [0, max(n_vis, f_hi+1)) in ascending order: each thread owns a contiguous run.
+    // Without ranking (more than CAND_MAX equal keys) the bin's first `remaining` by index are kept.
+    const int n_range = max(n_vis, f_hi + 1);
+    const int per = (n_range + blockDim.x - 1) / blockDim.x;
+    const int lo = tid * per, hi = min(n_range, lo + per);
+    int n_tie = 0;
+    if (!take_all && !ranked)
+        for (int b = lo; b < hi; b++)
+            if (is_cand(b) && (__float_as_uint(sc[b]) & pmask) == prefix) n_tie++;
+    int tie_base;
+    SelSmem::Scan(sm.scan).ExclusiveSum(n_tie, tie_base);
+    __syncthreads();
+    auto take = [&](int b, int & tie_i) -> bool {
+        if (b >= f_lo && b <= f_hi) return true;
+        if (!is_cand(b)) return false;
+        if (take_all) return true;
+        const uint32_t km = __float_as_uint(sc[b]) & pmask;
+        if (km > prefix) return true;
+        if (km != prefix) return false;
+        if (ranked) return flag[b] != 0;
+        return tie_i++ < remaining;
+    };
+    int n_take = 0, tie_i = tie_base;
+    for (int b = lo; b < hi; b++) n_take += take(b, tie_i);
+    int base, total;
+    SelSmem::Scan(sm.scan).ExclusiveSum(n_take, base, total);
+    tie_i = tie_base;
+    int pos = base;
+    for (int b = lo; b < hi; b++) {
+        if (take(b, tie_i)) {
+            if (pos < d.kb) {
+                sel[pos] = b;
+                if (sel_out) sel_out[pos] = b;
+            }
+            pos++;
+        }
+    }
+    const int n = min(total, d.kb);
+    if (sel_out)
+        for (int i = n + tid; i < d.kb; i += blockDim.x) sel_out[i] = -1;
+    if (tid == 0) *nsel_out = n;
+}
+
+// grid = (score CTAs per query, n_queries).  Query t: position q_pos(t), pooled cache `pool`.
+// Decode: items != null (per-query caches and n_past); prefill: one cache, q = n_past0 + t.
+__global__ void __launch_bounds__(SEL_THREADS) score_select_kernel(DevDesc d,
+        const qsa_decode_item * __restrict__ items, const uint16_t * __restrict__ pool0, int n_past0,
+        const float * __restrict__ q_idx, int blocks_per_cta,
+        float * __restrict__ scores_ws, int scores_stride, unsigned * __restrict__ counters,
+        int * __restrict__ sel_ws, int * __restrict__ nsel_ws, int * __restrict__ sel_out,
+        uint32_t * __restrict__ status) {
+    extern __shared__ __align__(16) unsigned char dyn_smem[];
+    __shared__ SelSmem sm;
+    __shared__ bool is_last;
+    const int t = blockIdx.y;
+    const int q = items ? items[t].n_past : n_past0 + t;
+    const uint16_t * pool = items ? items[t].cache.pool : pool0;
+    const bool bad = q < 0 || q >= d.n_ctx || (q + 1) / d.ratio > scores_stride;
+    if (bad && threadIdx.x == 0 && blockIdx.x == 0) set_status(status, DEV_BAD_POS);
+    const int n_vis = bad ? 0 : (q + 1) / d.ratio;
+    float * sc = scores_ws + (size_t) t * scores_stride;
+
+    if (!bad) {
+        float qf[4][8];
+        const int sub = threadIdx.x & 15;
+        #pragma unroll
+        for (int h = 0; h < 4; h++)
+            #pragma unroll
+            for (int e = 0; e < 8; e++)
+                qf[h][e] = h < d.idx_n_head
+                    ? f16_bits_to_f32(f32_to_f16_bits(q_idx[((size_t) t * d.idx_n_head + h) * d.idx_dim + 8 * sub + e]))
+                    : 0.0f;
+        const int b0 = blockIdx.x * blocks_per_cta;
+        const int b1 = min(n_vis, b0 + blocks_per_cta);
+        if (b0 < b1) score_range(d, pool, qf, b0, b1, sc);
+    }
+    // Arrival: the last CTA of this query selects.  The barrier orders the CTA's score stores
+    // before thread 0's release; its acquire orders the other CTAs' stores before our reads.
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned prev;
+        asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], 1;" : "=r"(prev) : "l"(counters + t) : "memory");
+        is_last = prev == gridDim.x - 1;
+        if (is_last) counters[t] = 0;          // leave the counter at zero for the next call
+    }
+    __syncthreads();
+    if (!is_last) return;
+    float * ssc = reinterpret_cast<float *>(dyn_smem);
+    unsigned char * flag = dyn_smem + (size_t) scores_stride * 4;
+    for (int b = threadIdx.x; b < n_vis; b += blockDim.x) ssc[b] = __ldcg(sc + b);
+    __syncthreads();
+    if (bad) {
+        for (int i = threadIdx.x; i < d.kb; i += blockDim.x) {
+            sel_ws[(size_t) t * d.kb + i] = -1;
+            if (sel_out) sel_out[(size_t) t * d.kb + i] = -1;
+        }
+        if (threadIdx.x == 0) nsel_ws[t] = 0;
+        return;
+    }
+    select_blocks(d, q, ssc, flag, sel_ws + (size_t) t * d.kb, nsel_ws + t,
+                  sel_out ? sel_out + (size_t) t * d.kb : nullptr, sm);
+}
+
+}  // namespace qsa
