@@ -55,10 +55,20 @@ size_t align256(size_t x) { return (x + 255) & ~(size_t) 255; }
 
 WsLayout ws_layout(const DevDesc & d, int n_q, int max_n_kv) {
     WsLayout w;
-    w.scores_stride = std::max(1, ceil_div(max_n_kv, d.ratio));
+    w.scores_stride = std::max(4, ceil_div(ceil_div(max_n_kv, d.ratio), 4) * 4);   // 16-byte rows
     const int max_tiles = std::max(1, ceil_div((int64_t) d.kb * d.ratio, CELLS_TILE));
-    const int64_t total_tiles = (int64_t) n_q * max_tiles;
-    int tpc = (int) std::max<int64_t>(1, total_tiles / TARGET_ATTN_CTAS);
+    // Chunks (CTAs) per query: one tile each while every tile of the batch fits one wave of
+    // attention CTAs (latency); otherwise as many chunks as one wave gives each query, rounded
+    // down to whole 8-CTA clusters, so that no CTA of the wave idles.
+    int tpc;
+    if ((int64_t) n_q * max_tiles <= TARGET_ATTN_CTAS) {
+        tpc = 1;
+    } else {
+        int nch = std::max(1, TARGET_ATTN_CTAS / n_q);
+        if (nch > 8) nch -= nch % 8;
+        nch = std::min(nch, max_tiles);
+        tpc = ceil_div(max_tiles, nch);
+    }
     if (tiles_override() > 0) tpc = tiles_override();
     tpc = std::min(tpc, max_tiles);
     w.tiles_per_cta = tpc;
@@ -87,6 +97,8 @@ qsa_status set_attrs() {
     cudaError_t e = attn_set_attrs();
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(score_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(append_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
     if (e != cudaSuccess) return QSA_ERR_CUDA;
     attrs_done = true;
     return QSA_OK;
@@ -99,16 +111,24 @@ qsa_status launch_select(const DevDesc & d, const WsLayout & w, int n_q, const q
     uint32_t * status = reinterpret_cast<uint32_t *>(ws + w.status);
     // blocks per scoring CTA: 16 (one row pair per warp) while the grid is small, more once
     // there are enough CTAs to fill the GPU several times over
-    int bpc = 16;
-    while (bpc < 256 && (int64_t) ceil_div(w.scores_stride, 2 * bpc) * n_q >= 8 * 148) bpc *= 2;
+    int bpc = 2 * (SEL_THREADS_HOST / 32);                 // one row pair per warp
+    while (bpc < 1024 && (int64_t) ceil_div(w.scores_stride, 2 * bpc) * n_q >= 2 * 148) bpc *= 2;
     const int score_ctas = ceil_div(w.scores_stride, bpc);
     const size_t sel_smem = (size_t) w.scores_stride * 5;       // scores + selection flags
     if (sel_smem > 160 * 1024) return QSA_ERR_UNSUPPORTED;
-    score_select_kernel<<<dim3(score_ctas, n_q), 256, sel_smem, st>>>(
-        d, items, cache0.pool, n_past0, q_idx, bpc,
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(score_ctas, n_q);
+    cfg.blockDim = dim3(SEL_THREADS_HOST);
+    cfg.dynamicSmemBytes = sel_smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;      // overlaps the append's tail
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cuda_status(cudaLaunchKernelEx(&cfg, score_select_kernel, d, items, cache0.pool, n_past0, q_idx, bpc,
         reinterpret_cast<float *>(ws + w.scores), w.scores_stride, reinterpret_cast<unsigned *>(ws + w.cnt_sel),
-        reinterpret_cast<int *>(ws + w.sel), reinterpret_cast<int *>(ws + w.nsel), sel_out, status);
-    return cuda_status(cudaGetLastError());
+        reinterpret_cast<int *>(ws + w.sel), reinterpret_cast<int *>(ws + w.nsel), sel_out, status));
 }
 
 // Attention over the selection held in the workspace.
@@ -157,6 +177,7 @@ qsa_status qsa_desc_check(const qsa_desc * d) {
     if (d->idx_dim != MAX_IDX_DIM || d->idx_n_head > 4 || d->rope_dim % 8 != 0) return QSA_ERR_UNSUPPORTED;
     if (d->type_k != d->type_v) return QSA_ERR_UNSUPPORTED;
     if (d->top_k_blocks + n_force_of(d) > MAX_KB) return QSA_ERR_UNSUPPORTED;
+    if (d->ratio > 256) return QSA_ERR_UNSUPPORTED;        // a block of raw keys is staged in shared memory
     return QSA_OK;
 }
 
@@ -247,7 +268,7 @@ qsa_status qsa_decode_append(const qsa_desc * dd, const qsa_decode_item * items,
     qsa_status s = decode_common(dd, items, batch, max_n_kv, ws, ws_bytes, d, w);
     if (s != QSA_OK) return s;
     if (!k_new || !v_new || !kidx_new) return QSA_ERR_INVALID;
-    append_decode_kernel<<<batch, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+    append_decode_kernel<<<batch, APPEND_DECODE_THREADS, append_decode_smem(d), reinterpret_cast<cudaStream_t>(stream)>>>(
         d, items, k_new, v_new, kidx_new, reinterpret_cast<uint32_t *>(static_cast<unsigned char *>(ws) + w.status));
     return cuda_status(cudaGetLastError());
 }
@@ -288,7 +309,7 @@ qsa_status qsa_decode(const qsa_desc * dd, const qsa_decode_item * items, int32_
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     unsigned char * wsb = static_cast<unsigned char *>(ws);
     if (any_new)
-        append_decode_kernel<<<batch, 256, 0, st>>>(d, items, k_new, v_new, kidx_new,
+        append_decode_kernel<<<batch, APPEND_DECODE_THREADS, append_decode_smem(d), st>>>(d, items, k_new, v_new, kidx_new,
                                                     reinterpret_cast<uint32_t *>(wsb + w.status));
     qsa_layer_cache none{};
     if ((s = launch_select(d, w, batch, items, none, 0, q_idx, sel_out, wsb, st)) != QSA_OK) return s;

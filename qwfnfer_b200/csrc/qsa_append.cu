@@ -43,18 +43,27 @@ __device__ __forceinline__ void write_kv_row(const DevDesc & d, int type, const 
 // scale = 1/sqrtf(mean + eps) (IEEE), times k_norm_w; IMRoPE at position b*r with the angle of
 // pair i obtained by i successive f32 multiplies by theta_scale (ggml's cache recurrence), cos and
 // sin of that f32 angle (evaluated in double and rounded), NEOX pairs (i, i + rope_dim/2).
-__device__ void pool_block_warp(const DevDesc & d, const uint16_t * __restrict__ idx, int64_t b,
+// `rows` points at the block's first raw-key row (global memory, or a shared-memory copy).
+__device__ void pool_block_warp(const DevDesc & d, const uint16_t * __restrict__ rows, int64_t b,
                                 uint16_t * __restrict__ pool_row, float * __restrict__ out_f32) {
     const int lane = threadIdx.x & 31;
     const int r = d.ratio;
     float x[4] = {0.f, 0.f, 0.f, 0.f};
-    const uint16_t * base = idx + (size_t) b * r * MAX_IDX_DIM + 4 * lane;
-    for (int i = 0; i < r; i++) {
-        const uint2 w = *reinterpret_cast<const uint2 *>(base + (size_t) i * MAX_IDX_DIM);
-        const float v0 = f16_bits_to_f32((uint16_t) (w.x & 0xffff)), v1 = f16_bits_to_f32((uint16_t) (w.x >> 16));
-        const float v2 = f16_bits_to_f32((uint16_t) (w.y & 0xffff)), v3 = f16_bits_to_f32((uint16_t) (w.y >> 16));
-        if (i == 0) { x[0] = v0; x[1] = v1; x[2] = v2; x[3] = v3; }
-        else { x[0] = __fadd_rn(x[0], v0); x[1] = __fadd_rn(x[1], v1); x[2] = __fadd_rn(x[2], v2); x[3] = __fadd_rn(x[3], v3); }
+    const uint16_t * base = rows + 4 * lane;
+    // rows are fetched 8 at a time (independent loads in flight), then added strictly in order
+    for (int i0 = 0; i0 < r; i0 += 8) {
+        uint2 w[8];
+        #pragma unroll
+        for (int k = 0; k < 8; k++)
+            w[k] = i0 + k < r ? *reinterpret_cast<const uint2 *>(base + (size_t) (i0 + k) * MAX_IDX_DIM) : make_uint2(0, 0);
+        #pragma unroll
+        for (int k = 0; k < 8; k++) {
+            if (i0 + k >= r) break;
+            const float v0 = f16_bits_to_f32((uint16_t) (w[k].x & 0xffff)), v1 = f16_bits_to_f32((uint16_t) (w[k].x >> 16));
+            const float v2 = f16_bits_to_f32((uint16_t) (w[k].y & 0xffff)), v3 = f16_bits_to_f32((uint16_t) (w[k].y >> 16));
+            if (i0 + k == 0) { x[0] = v0; x[1] = v1; x[2] = v2; x[3] = v3; }
+            else { x[0] = __fadd_rn(x[0], v0); x[1] = __fadd_rn(x[1], v1); x[2] = __fadd_rn(x[2], v2); x[3] = __fadd_rn(x[3], v3); }
+        }
     }
     double ss = 0.0;
     #pragma unroll
@@ -90,8 +99,15 @@ __device__ void pool_block_warp(const DevDesc & d, const uint16_t * __restrict__
                                  (sector % 3 == 2 && sector < 3 * d.sections[2]) ||
                                  (sector % 3 == 0 && sector < 3 * d.sections[0]);
             if (!use_pos) th = 0.0f;                            // the 4th section's position is 0
+            // cos/sin of the f32 angle (up to ~1e6 rad): Cody-Waite reduction by 2*pi split into two
+            // doubles (the product k*2pi_hi is exact to the double rounding of one fma), then
+            // sincos of the reduced double argument, rounded once to f32.
+            const double td = (double) th;
+            const double k = rint(td * 0.15915494309189535);               // 1 / (2 pi)
+            double rr = fma(-k, 6.283185307179586, td);                     // 2 pi, high part
+            rr = fma(-k, 2.4492935982947064e-16, rr);                       // 2 pi - high part
             double sd, cd;
-            sincos((double) th, &sd, &cd);
+            sincos(rr, &sd, &cd);
             const float c = (float) cd, s = (float) sd;
             if (first) y[e] = __fsub_rn(__fmul_rn(x[e], c), __fmul_rn(partner, s));     // x0*c - x1*s
             else       y[e] = __fadd_rn(__fmul_rn(partner, s), __fmul_rn(x[e], c));     // x0*s + x1*c
@@ -120,19 +136,25 @@ __global__ void __launch_bounds__(256) append_rows_kernel(DevDesc d, qsa_layer_c
 // Pooled keys of blocks [blk0, blk0+n_blk): one warp per block.
 __global__ void __launch_bounds__(256) pool_blocks_kernel(DevDesc d, const uint16_t * __restrict__ idx,
         uint16_t * __restrict__ pool, int blk0, int n_blk, float * __restrict__ out_f32) {
+    pdl_trigger();
     const int j = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (j >= n_blk) return;
     const int64_t b = blk0 + j;
-    pool_block_warp(d, idx, b, pool + (size_t) b * d.idx_dim, out_f32 ? out_f32 + (size_t) j * d.idx_dim : nullptr);
+    pool_block_warp(d, idx + (size_t) b * d.ratio * MAX_IDX_DIM, b, pool + (size_t) b * d.idx_dim,
+                    out_f32 ? out_f32 + (size_t) j * d.idx_dim : nullptr);
 }
 
-// Decode append for a batch: CTA s writes row n_past of sequence s (K, V, raw key) and, when
-// that row completes its block, the block's pooled key (as the reference recomputes the
+// Decode append for a batch: CTA s (1024 threads) writes row n_past of sequence s (K, V, raw key)
+// and, when that row completes its block, the block's pooled key (as the reference recomputes the
 // current block every token and stores it, src/qwfn_graph.cpp:470-476; only a complete block's
-// pooled key is ever read, an incomplete block being forced by the bias).
-__global__ void __launch_bounds__(256) append_decode_kernel(DevDesc d, const qsa_decode_item * __restrict__ items,
+// pooled key is ever read, an incomplete block being forced by the bias).  The block's raw-key
+// rows are staged into shared memory in one round of loads, then summed in order by one warp.
+constexpr int APPEND_THREADS = 1024;
+__global__ void __launch_bounds__(APPEND_THREADS) append_decode_kernel(DevDesc d, const qsa_decode_item * __restrict__ items,
         const float * __restrict__ k, const float * __restrict__ v, const float * __restrict__ kidx,
         uint32_t * __restrict__ status) {
+    extern __shared__ __align__(16) unsigned char dyn_smem[];
+    pdl_trigger();
     const int s = blockIdx.x;
     const qsa_decode_item it = items[s];
     const int row = it.n_past;
@@ -141,15 +163,31 @@ __global__ void __launch_bounds__(256) append_decode_kernel(DevDesc d, const qsa
         return;
     }
     const int kv_dim = d.n_head_kv * d.head_dim;
-    if (k) write_kv_row(d, d.type_k, k + (size_t) s * kv_dim, (uint8_t *) it.cache.k + (size_t) row * d.rb_k, kv_dim);
-    if (v) write_kv_row(d, d.type_v, v + (size_t) s * kv_dim, (uint8_t *) it.cache.v + (size_t) row * d.rb_v, kv_dim);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nb = kv_dim / QK8_0;
+    if (d.type_k == QSA_TYPE_Q8_0 && 2 * nb <= (int) (blockDim.x >> 5)) {
+        // one q8_0 block per warp: K blocks on warps [0, nb), V blocks on warps [nb, 2 nb)
+        if (warp < nb && k)
+            quantize_q8_0_warp(k + (size_t) s * kv_dim + warp * QK8_0, (uint8_t *) it.cache.k + (size_t) row * d.rb_k + warp * Q8_0_BYTES, lane);
+        else if (warp >= nb && warp < 2 * nb && v)
+            quantize_q8_0_warp(v + (size_t) s * kv_dim + (warp - nb) * QK8_0, (uint8_t *) it.cache.v + (size_t) row * d.rb_v + (warp - nb) * Q8_0_BYTES, lane);
+    } else {
+        if (k) write_kv_row(d, d.type_k, k + (size_t) s * kv_dim, (uint8_t *) it.cache.k + (size_t) row * d.rb_k, kv_dim);
+        if (v) write_kv_row(d, d.type_v, v + (size_t) s * kv_dim, (uint8_t *) it.cache.v + (size_t) row * d.rb_v, kv_dim);
+    }
     if (kidx) {
         for (int i = threadIdx.x; i < d.idx_dim; i += blockDim.x)
             it.cache.idx[(size_t) row * d.idx_dim + i] = f32_to_f16_bits(kidx[(size_t) s * d.idx_dim + i]);
-        __syncthreads();
-        if ((row + 1) % d.ratio == 0 && threadIdx.x < 32) {
+        if ((row + 1) % d.ratio == 0) {
+            __syncthreads();                      // this token's raw key is written
             const int64_t b = row / d.ratio;
-            pool_block_warp(d, it.cache.idx, b, it.cache.pool + (size_t) b * d.idx_dim, nullptr);
+            const uint4 * src = reinterpret_cast<const uint4 *>(it.cache.idx + (size_t) b * d.ratio * MAX_IDX_DIM);
+            uint4 * rows = reinterpret_cast<uint4 *>(dyn_smem);
+            const int n16 = d.ratio * MAX_IDX_DIM / 8;              // 16-byte pieces of the block
+            for (int i = threadIdx.x; i < n16; i += blockDim.x) rows[i] = src[i];
+            __syncthreads();
+            if (threadIdx.x < 32)
+                pool_block_warp(d, reinterpret_cast<const uint16_t *>(dyn_smem), b,
+                                it.cache.pool + (size_t) b * d.idx_dim, nullptr);
         }
     }
 }

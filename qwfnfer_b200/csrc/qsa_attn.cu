@@ -70,6 +70,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_kernel(
     constexpr int NS = Cfg::NSTAGE, HB = Cfg::HB, RB = attn_row_bytes<KV_TYPE>();
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ uint64_t full_bar[NS];
+    __shared__ uint64_t empty_bar[NS];
+    __shared__ unsigned long long vmask[NS];
     __shared__ bool is_last;
 
     const int t = blockIdx.y, chunk = blockIdx.x;
@@ -94,8 +96,6 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_kernel(
         kbase = (const uint8_t *) cache0.k;
         vbase = (const uint8_t *) cache0.v;
     }
-    const int nsel_raw = nsel_ws[t];
-    for (int i = tid; i < d.kb; i += ATT_THREADS) sel[i] = sel_ws[(size_t) t * d.kb + i];
     {   // Q of the CTA's query heads -> f16 (the reference converts Q to K's vec_dot type, F16)
         for (int i = tid; i < HROWS * HEAD_DIM / 8; i += ATT_THREADS) {
             const int hrow = (i * 8) / HEAD_DIM, h = hrow & 7, g = hrow >> 3;
@@ -125,6 +125,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_kernel(
             *reinterpret_cast<uint4 *>(qs + i * 8) = o4;
         }
     }
+    pdl_wait();                                // the selection of this step is complete
+    const int nsel_raw = nsel_ws[t];
+    for (int i = tid; i < d.kb; i += ATT_THREADS) sel[i] = sel_ws[(size_t) t * d.kb + i];
     const bool pos_ok = qpos >= 0 && qpos < d.n_ctx;
     const int nsel = pos_ok ? max(0, min(nsel_raw, d.kb)) : 0;
     const int r = d.ratio;
@@ -150,14 +153,53 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_kernel(
     // chunks past the last tile (inside a partly used cluster) contribute an empty state
     const int n_local = chunk < n_chunks ? min(tiles_per_cta, n_tiles - tile0) : 0;
     if (tid == 0) {
-        for (int s = 0; s < NS; s++) mbar_init(&full_bar[s], 1);
+        for (int s = 0; s < NS; s++) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], ATT_WARPS);
+        }
         fence_mbar_init();
+    }
+    __syncthreads();                                  // staged Q, sel and the barriers are visible
+    // Q fragments (mma B operand) of each KV head, packed in lane order into shared memory (over
+    // the staged Q, which only these two builders read): head n = r8 of the 8-head tile.
+    uint32_t qf[16][2];
+    if (warp == 0 || warp == 4) {
+        const __half * qrow = qs + (hs * 8 + r8) * HEAD_DIM;
+        auto pk2 = [&](int d0, int d1) -> uint32_t {
+            __half2 h = __halves2half2(qrow[d0], qrow[d1]);
+            return *reinterpret_cast<uint32_t *>(&h);
+        };
+        if (KV_TYPE == QSA_TYPE_Q8_0) {
+            // group g8 (32 dims), k-tile kt: virtual k (2j,2j+1) -> dims 8j+4kt+{0,2}; (2j+8,2j+9) -> 8j+4kt+{1,3}
+            #pragma unroll
+            for (int g8 = 0; g8 < 8; g8++)
+                #pragma unroll
+                for (int kt = 0; kt < 2; kt++) {
+                    const int base = 32 * g8 + 8 * j4 + 4 * kt;
+                    qf[2 * g8 + kt][0] = pk2(base + 0, base + 2);
+                    qf[2 * g8 + kt][1] = pk2(base + 1, base + 3);
+                }
+        } else {
+            #pragma unroll
+            for (int kt = 0; kt < 16; kt++) {
+                const int base = 16 * kt + 2 * j4;
+                qf[kt][0] = pk2(base + 0, base + 1);
+                qf[kt][1] = pk2(base + 8, base + 9);
+            }
+        }
+    }
+    __syncthreads();
+    uint2 * qfrag = reinterpret_cast<uint2 *>(qs);       // [2 heads][16 k-steps][32 lanes]
+    if (warp == 0 || warp == 4) {
+        #pragma unroll
+        for (int k = 0; k < 16; k++) qfrag[(hs * 16 + k) * 32 + lane] = make_uint2(qf[k][0], qf[k][1]);
     }
     __syncthreads();
 
     auto stage_k = [&](int s) { return smem + s * attn_stage_bytes<KV_TYPE>(); };
     auto stage_v = [&](int s) { return smem + s * attn_stage_bytes<KV_TYPE>() + CELLS_TILE * RB; };  // RB >= row bytes
-    // Warp 0 issues local tile i into stage i % NS: one copy per block-run of valid rows.
+    // Warp 0 issues local tile i into stage i % NS: one copy per block-run of valid rows, and the
+    // tile's 64-bit row-validity mask (written before the release of the arrive).
     auto issue = [&](int i) {
         const int s = i % NS;
         const int e_lo = (tile0 + i) * CELLS_TILE;
@@ -173,7 +215,13 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_kernel(
         }
         #pragma unroll
         for (int off = 16; off > 0; off >>= 1) bytes += __shfl_xor_sync(0xffffffffu, bytes, off);
-        if (lane == 0) mbar_arrive_expect_tx(&full_bar[s], bytes);
+        const int ea = e_lo + lane, eb = ea + 32;
+        const unsigned lo = __ballot_sync(0xffffffffu, ea < n_cells && list_cell(sel, r, ea) <= qpos);
+        const unsigned hi = __ballot_sync(0xffffffffu, eb < n_cells && list_cell(sel, r, eb) <= qpos);
+        if (lane == 0) {
+            vmask[s] = ((unsigned long long) hi << 32) | lo;
+            mbar_arrive_expect_tx(&full_bar[s], bytes);
+        }
         __syncwarp();
         for (int j = j_lo + lane; j <= j_hi; j += 32) {
             const int a = max(e_lo, j * r), b = min(e_hi, (j + 1) * r);
@@ -188,32 +236,6 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_kernel(
     if (warp == 0)
         for (int i = 0; i < min(NS, n_local); i++) issue(i);
 
-    // Q fragments (B operand) of this warp's KV head; head n = r8 of the 8-head tile
-    const __half * qrow = qs + (hs * 8 + r8) * HEAD_DIM;
-    auto pk2 = [&](int d0, int d1) -> uint32_t {
-        __half2 h = __halves2half2(qrow[d0], qrow[d1]);
-        return *reinterpret_cast<uint32_t *>(&h);
-    };
-    uint32_t qb[16][2];
-    if (KV_TYPE == QSA_TYPE_Q8_0) {
-        // group g8 (32 dims), k-tile kt: virtual k (2j,2j+1) -> dims 8j+4kt+{0,2}; (2j+8,2j+9) -> 8j+4kt+{1,3}
-        #pragma unroll
-        for (int g8 = 0; g8 < 8; g8++)
-            #pragma unroll
-            for (int kt = 0; kt < 2; kt++) {
-                const int base = 32 * g8 + 8 * j4 + 4 * kt;
-                qb[2 * g8 + kt][0] = pk2(base + 0, base + 2);
-                qb[2 * g8 + kt][1] = pk2(base + 1, base + 3);
-            }
-    } else {
-        #pragma unroll
-        for (int kt = 0; kt < 16; kt++) {
-            const int base = 16 * kt + 2 * j4;
-            qb[kt][0] = pk2(base + 0, base + 1);
-            qb[kt][1] = pk2(base + 8, base + 9);
-        }
-    }
-
     float o[16][4];
     #pragma unroll
     for (int i = 0; i < 16; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
@@ -222,34 +244,51 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_kernel(
     const int c0 = 16 * cw + 2 * j4;                     // this thread's V^T columns: c0+{0,1,8,9}
     const int hoff = hs * HB;                            // byte offset of this warp's head in a row
     const int rb = (int) d.rb_k;                         // row bytes (= smem row stride), K and V alike
+    const uint2 * myq = qfrag + hs * 16 * 32 + lane;
 
     for (int i = 0; i < n_local; i++) {
         const int s = i % NS;
-        mbar_wait_bounded(&full_bar[s], (uint32_t) ((i / NS) & 1), status);
-        const int e0 = (tile0 + i) * CELLS_TILE;
-        auto valid = [&](int row) { const int e = e0 + row; return e < n_cells && list_cell(sel, r, e) <= qpos; };
-        const bool okA = valid(rA), okB = valid(rB);
+        const uint32_t ph = (uint32_t) ((i / NS) & 1);
+        mbar_wait_bounded(&full_bar[s], ph, status);
+        const unsigned long long vm = vmask[s];
+        const bool okA = (vm >> rA) & 1ull, okB = (vm >> rB) & 1ull;
         if (head_live) {
             const uint8_t * Kt = stage_k(s) + hoff;
             const uint8_t * Vt = stage_v(s) + hoff;
             // ---- S^T = K Q^T for the warp's 16 cells x 8 heads
             float sc[4] = {0.f, 0.f, 0.f, 0.f};
             if (KV_TYPE == QSA_TYPE_Q8_0) {
+                // row bases are 4-byte aligned; q8_0 block g8 starts at byte 34*g8 (scale) + 2 (quants),
+                // so its quants are word aligned for odd g8 and 2 bytes off for even g8
+                const uint32_t * WA = reinterpret_cast<const uint32_t *>(Kt + rA * rb);
+                const uint32_t * WB = reinterpret_cast<const uint32_t *>(Kt + rB * rb);
+                const uint16_t * HA = reinterpret_cast<const uint16_t *>(WA);
+                const uint16_t * HB_ = reinterpret_cast<const uint16_t *>(WB);
                 #pragma unroll
                 for (int g8 = 0; g8 < 8; g8++) {
-                    const uint8_t * ka = Kt + rA * rb + Q8_0_BYTES * g8;
-                    const uint8_t * kb = Kt + rB * rb + Q8_0_BYTES * g8;
-                    const float dA = f16_bits_to_f32(*reinterpret_cast<const uint16_t *>(ka));
-                    const float dB = f16_bits_to_f32(*reinterpret_cast<const uint16_t *>(kb));
-                    const uint32_t w0A = lds_u32_a2(ka + 2 + 8 * j4), w1A = lds_u32_a2(ka + 6 + 8 * j4);
-                    const uint32_t w0B = lds_u32_a2(kb + 2 + 8 * j4), w1B = lds_u32_a2(kb + 6 + 8 * j4);
+                    uint32_t w0A, w1A, w0B, w1B;
+                    if ((g8 & 1) == 0) {
+                        const int wi = 17 * (g8 / 2) + 2 * j4;
+                        const uint32_t a0 = WA[wi], a1 = WA[wi + 1], a2 = WA[wi + 2];
+                        const uint32_t b0 = WB[wi], b1 = WB[wi + 1], b2 = WB[wi + 2];
+                        w0A = __funnelshift_r(a0, a1, 16); w1A = __funnelshift_r(a1, a2, 16);
+                        w0B = __funnelshift_r(b0, b1, 16); w1B = __funnelshift_r(b1, b2, 16);
+                    } else {
+                        const int wi = 17 * (g8 / 2) + 9 + 2 * j4;
+                        w0A = WA[wi]; w1A = WA[wi + 1];
+                        w0B = WB[wi]; w1B = WB[wi + 1];
+                    }
+                    const float dA = f16_bits_to_f32(HA[17 * g8]);
+                    const float dB = f16_bits_to_f32(HB_[17 * g8]);
+                    const uint2 qa = myq[(2 * g8) * 32], qb2 = myq[(2 * g8 + 1) * 32];
+                    const uint32_t b0[2] = {qa.x, qa.y}, b1[2] = {qb2.x, qb2.y};
                     float c[4] = {0.f, 0.f, 0.f, 0.f};
                     const uint32_t a0[4] = {i8x2_even_to_f16x2(w0A), i8x2_even_to_f16x2(w0B),
                                             i8x2_odd_to_f16x2(w0A), i8x2_odd_to_f16x2(w0B)};
                     const uint32_t a1[4] = {i8x2_even_to_f16x2(w1A), i8x2_even_to_f16x2(w1B),
                                             i8x2_odd_to_f16x2(w1A), i8x2_odd_to_f16x2(w1B)};
-                    mma_f16_16816(c, a0, qb[2 * g8]);
-                    mma_f16_16816(c, a1, qb[2 * g8 + 1]);
+                    mma_f16_16816(c, a0, b0);
+                    mma_f16_16816(c, a1, b1);
                     sc[0] = fmaf(dA, c[0], sc[0]); sc[1] = fmaf(dA, c[1], sc[1]);
                     sc[2] = fmaf(dB, c[2], sc[2]); sc[3] = fmaf(dB, c[3], sc[3]);
                 }
@@ -260,7 +299,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_kernel(
                     const uint8_t * kb = Kt + rB * rb + 2 * (16 * kt + 2 * j4);
                     const uint32_t a[4] = {*reinterpret_cast<const uint32_t *>(ka), *reinterpret_cast<const uint32_t *>(kb),
                                            *reinterpret_cast<const uint32_t *>(ka + 16), *reinterpret_cast<const uint32_t *>(kb + 16)};
-                    mma_f16_16816(sc, a, qb[kt]);
+                    const uint2 qk = myq[kt * 32];
+                    const uint32_t bq[2] = {qk.x, qk.y};
+                    mma_f16_16816(sc, a, bq);
                 }
             }
             // ---- mask, scale to the exp2 domain, online softmax (heads 2j, 2j+1 of this thread)
@@ -283,25 +324,39 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_kernel(
             l0 = l0 * al0 + p[0] + p[2];
             l1 = l1 * al1 + p[1] + p[3];
             m0 = mn0; m1 = mn1;
-            #pragma unroll
-            for (int k = 0; k < 16; k++) { o[k][0] *= al0; o[k][1] *= al1; o[k][2] *= al0; o[k][3] *= al1; }
+            if (__any_sync(0xffffffffu, al0 != 1.0f || al1 != 1.0f)) {   // the running max moved
+                #pragma unroll
+                for (int k = 0; k < 16; k++) { o[k][0] *= al0; o[k][1] *= al1; o[k][2] *= al0; o[k][3] *= al1; }
+            }
 
             // ---- O^T += V^T P   (rows not fetched are masked: zero scale / zero values)
             if (KV_TYPE == QSA_TYPE_Q8_0) {
+                const uint32_t * V0 = reinterpret_cast<const uint32_t *>(Vt + (c0 + 0) * rb);
+                const uint32_t * V1 = reinterpret_cast<const uint32_t *>(Vt + (c0 + 1) * rb);
+                const uint32_t * V8 = reinterpret_cast<const uint32_t *>(Vt + (c0 + 8) * rb);
+                const uint32_t * V9 = reinterpret_cast<const uint32_t *>(Vt + (c0 + 9) * rb);
+                const uint16_t * VA = reinterpret_cast<const uint16_t *>(Vt + rA * rb);
+                const uint16_t * VB = reinterpret_cast<const uint16_t *>(Vt + rB * rb);
                 #pragma unroll
                 for (int g8 = 0; g8 < 8; g8++) {
-                    float dA = f16_bits_to_f32(*reinterpret_cast<const uint16_t *>(Vt + rA * rb + Q8_0_BYTES * g8));
-                    float dB = f16_bits_to_f32(*reinterpret_cast<const uint16_t *>(Vt + rB * rb + Q8_0_BYTES * g8));
+                    float dA = f16_bits_to_f32(VA[17 * g8]);
+                    float dB = f16_bits_to_f32(VB[17 * g8]);
                     dA = okA ? dA : 0.0f;
                     dB = okB ? dB : 0.0f;
                     uint32_t b[2];
                     b[0] = movmatrix_trans(pack_f16x2(p[0] * dA, p[1] * dA));
                     b[1] = movmatrix_trans(pack_f16x2(p[2] * dB, p[3] * dB));
-                    const int off = Q8_0_BYTES * g8 + 2 + 4 * r8;
-                    const uint32_t W0 = lds_u32_a2(Vt + (c0 + 0) * rb + off);
-                    const uint32_t W1 = lds_u32_a2(Vt + (c0 + 1) * rb + off);
-                    const uint32_t W2 = lds_u32_a2(Vt + (c0 + 8) * rb + off);
-                    const uint32_t W3 = lds_u32_a2(Vt + (c0 + 9) * rb + off);
+                    uint32_t W0, W1, W2, W3;
+                    if ((g8 & 1) == 0) {
+                        const int wi = 17 * (g8 / 2) + r8;
+                        W0 = __funnelshift_r(V0[wi], V0[wi + 1], 16);
+                        W1 = __funnelshift_r(V1[wi], V1[wi + 1], 16);
+                        W2 = __funnelshift_r(V8[wi], V8[wi + 1], 16);
+                        W3 = __funnelshift_r(V9[wi], V9[wi + 1], 16);
+                    } else {
+                        const int wi = 17 * (g8 / 2) + 9 + r8;
+                        W0 = V0[wi]; W1 = V1[wi]; W2 = V8[wi]; W3 = V9[wi];
+                    }
                     const uint32_t am0[4] = {i8_pair_to_f16x2<0>(W0, W1), i8_pair_to_f16x2<1>(W0, W1),
                                              i8_pair_to_f16x2<0>(W2, W3), i8_pair_to_f16x2<1>(W2, W3)};
                     const uint32_t am1[4] = {i8_pair_to_f16x2<2>(W0, W1), i8_pair_to_f16x2<3>(W0, W1),
@@ -313,8 +368,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_kernel(
                 uint32_t b[2];
                 b[0] = movmatrix_trans(pack_f16x2(p[0], p[1]));
                 b[1] = movmatrix_trans(pack_f16x2(p[2], p[3]));
-                const uint32_t m01 = (valid(c0) ? 0x0000ffffu : 0u) | (valid(c0 + 1) ? 0xffff0000u : 0u);
-                const uint32_t m89 = (valid(c0 + 8) ? 0x0000ffffu : 0u) | (valid(c0 + 9) ? 0xffff0000u : 0u);
+                const uint32_t m01 = (((vm >> c0) & 1ull) ? 0x0000ffffu : 0u) | (((vm >> (c0 + 1)) & 1ull) ? 0xffff0000u : 0u);
+                const uint32_t m89 = (((vm >> (c0 + 8)) & 1ull) ? 0x0000ffffu : 0u) | (((vm >> (c0 + 9)) & 1ull) ? 0xffff0000u : 0u);
                 const int cl = 16 * cw + (lane & 7) + ((lane >> 4) << 3);   // ldmatrix row: cell
                 const int dh = ((lane >> 3) & 1) << 3;                        // +8 dims for matrices 1, 3
                 #pragma unroll
@@ -326,12 +381,16 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_kernel(
                 }
             }
         }
-        __syncthreads();                              // every warp is done with stage s
+        // this warp is done with stage s; warp 0 refills it once all 8 warps are
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty_bar[s]);
         if (warp == 0 && i + NS < n_local) {
+            mbar_wait_bounded(&empty_bar[s], ph, status);
             fence_proxy_async_smem();
             issue(i + NS);
         }
     }
+    __syncthreads();                                  // all warps past the last tile: stages are free
 
     // ---- merge the 4 warps of each KV head (stage memory is free)
     #pragma unroll
@@ -369,62 +428,85 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_kernel(
         }
     }
     __syncthreads();
+    float * wf = co + HROWS * HEAD_DIM;                          // [8 warps][8 heads] merge factors
     if (tid < HROWS) {   // row hr = 8*head + h: M = max over the head's 4 warps, L = sum l 2^(m - M)
         const int w0 = (tid >> 3) * 4, h = tid & 7;
         float M = -INFINITY;
         for (int w = w0; w < w0 + 4; w++) M = fmaxf(M, wm[w * 8 + h]);
         const float Mu = M == -INFINITY ? 0.0f : M;
         float L = 0.0f;
-        for (int w = w0; w < w0 + 4; w++) L += wl[w * 8 + h] * exp2f(wm[w * 8 + h] - Mu);
+        for (int w = w0; w < w0 + 4; w++) {
+            const float f = exp2f(wm[w * 8 + h] - Mu);
+            wf[w * 8 + h] = f;
+            L += wl[w * 8 + h] * f;
+        }
         cm[tid] = M; cm[HROWS + tid] = L;
     }
     __syncthreads();
-    for (int e = tid; e < HROWS * HEAD_DIM; e += ATT_THREADS) {
-        const int hr = e / HEAD_DIM, w0 = (hr >> 3) * 4, h = hr & 7, dim = e % HEAD_DIM;
-        const float Mu = cm[hr] == -INFINITY ? 0.0f : cm[hr];
-        float acc = 0.0f;
+    for (int e4 = tid; e4 < HROWS * HEAD_DIM / 4; e4 += ATT_THREADS) {
+        const int hr = (e4 * 4) / HEAD_DIM, w0 = (hr >> 3) * 4, h = hr & 7, d4 = e4 % (HEAD_DIM / 4);
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
         #pragma unroll
-        for (int w = 0; w < 4; w++) acc += wo[((w0 + w) * 8 + h) * HEAD_DIM + dim] * exp2f(wm[(w0 + w) * 8 + h] - Mu);
-        co[e] = acc;
+        for (int w = 0; w < 4; w++) {
+            const float f = wf[(w0 + w) * 8 + h];
+            const float4 v = reinterpret_cast<const float4 *>(wo + ((w0 + w) * 8 + h) * HEAD_DIM)[d4];
+            acc.x += f * v.x; acc.y += f * v.y; acc.z += f * v.z; acc.w += f * v.w;
+        }
+        reinterpret_cast<float4 *>(co)[e4] = acc;
     }
     __syncthreads();
 
-    // ---- first combine level: the CTAs of a cluster (consecutive chunks of query t) merge through
-    // distributed shared memory into cluster rank 0
+    // ---- first combine level: the CTAs of a cluster (consecutive chunks of query t) reduce-scatter
+    // through distributed shared memory: every rank derives the per-row weights of all ranks, then
+    // merges its own 1/CL slice of the [16][256] state over the ranks.
     cg::cluster_group cluster = cg::this_cluster();
     const int CL = (int) cluster.num_blocks();
     const int crank = (int) cluster.block_rank();
     const int cl_id = chunk / CL;
     const int n_cl = (n_chunks + CL - 1) / CL;
     cluster.sync();                                   // every CTA's cm/co are complete
-    float * red = co + HROWS * HEAD_DIM;              // [16] M, [16] L, [8 ranks][16] ranks' m then weights
-    float * rl = red + 2 * HROWS + 8 * HROWS;         // [8 ranks][16] ranks' l
-    float * ro = reinterpret_cast<float *>(smem);     // cluster O [16][256] (wm/wl/wo are free now)
-    if (crank == 0 && CL > 1) {
-        if (tid < CL * HROWS) {                       // all ranks' (m, l) fetched at once
-            const int p = tid / HROWS, hr = tid % HROWS;
-            const float * pc = cluster.map_shared_rank(cm, p);
-            red[2 * HROWS + p * HROWS + hr] = pc[hr];
-            rl[p * HROWS + hr] = pc[HROWS + hr];
+    float * rw = co + HROWS * HEAD_DIM + 64;          // [8 ranks][16] ranks' m, then their weights
+    float * rl = rw + 8 * HROWS;                      // [8 ranks][16] ranks' l
+    float * rML = rl + 8 * HROWS;                     // [16] cluster M, [16] cluster L
+    if (tid < CL * HROWS) {
+        const int p = tid / HROWS, hr = tid % HROWS;
+        const float * pc = cluster.map_shared_rank(cm, p);
+        rw[p * HROWS + hr] = pc[hr];
+        rl[p * HROWS + hr] = pc[HROWS + hr];
+    }
+    __syncthreads();
+    if (tid < HROWS) {
+        float M = -INFINITY;
+        for (int p = 0; p < CL; p++) M = fmaxf(M, rw[p * HROWS + tid]);
+        const float Mu = M == -INFINITY ? 0.0f : M;
+        float L = 0.0f;
+        for (int p = 0; p < CL; p++) {
+            const float w = exp2f(rw[p * HROWS + tid] - Mu);
+            rw[p * HROWS + tid] = w;
+            L += rl[p * HROWS + tid] * w;
         }
-        __syncthreads();
-        if (tid < HROWS) {
-            float M = -INFINITY;
-            for (int p = 0; p < CL; p++) M = fmaxf(M, red[2 * HROWS + p * HROWS + tid]);
-            const float Mu = M == -INFINITY ? 0.0f : M;
-            float L = 0.0f;
-            for (int p = 0; p < CL; p++) {
-                const float w = exp2f(red[2 * HROWS + p * HROWS + tid] - Mu);
-                red[2 * HROWS + p * HROWS + tid] = w;
-                L += rl[p * HROWS + tid] * w;
-            }
-            red[tid] = M; red[HROWS + tid] = L;
+        rML[tid] = M; rML[HROWS + tid] = L;
+    }
+    __syncthreads();
+    const int n_rows = d.n_head_kv * 8;
+    const int n_e4 = HROWS * HEAD_DIM / 4;            // float4 elements of the state
+    const int slice = (n_e4 + CL - 1) / CL;
+    const int e_beg = crank * slice, e_end = min(n_e4, e_beg + slice);
+    auto write_out = [&](int e4, float4 v, float L) {
+        const int hr = (e4 * 4) / HEAD_DIM, h = hr & 7, g = hr >> 3;
+        if (hr < n_rows && h < d.gqa) {
+            const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+            reinterpret_cast<float4 *>(outq + (size_t) (g * d.gqa + h) * HEAD_DIM)[(e4 * 4 % HEAD_DIM) / 4] =
+                make_float4(v.x * inv, v.y * inv, v.z * inv, v.w * inv);
         }
-        __syncthreads();
+    };
+    const int max_parts = (max_chunks + CL - 1) / CL;
+    float * po = part_o + ((size_t) t * max_parts + cl_id) * HROWS * HEAD_DIM;
+    {
         const float4 * pco[8];
         #pragma unroll
         for (int p = 0; p < 8; p++) pco[p] = reinterpret_cast<const float4 *>(cluster.map_shared_rank(co, p < CL ? p : 0));
-        for (int e4 = tid; e4 < HROWS * HEAD_DIM / 4; e4 += ATT_THREADS) {
+        for (int e4 = e_beg + tid; e4 < e_end; e4 += ATT_THREADS) {
             const int hr = (e4 * 4) / HEAD_DIM;
             float4 v[8];
             #pragma unroll
@@ -432,54 +514,38 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_kernel(
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
             #pragma unroll
             for (int p = 0; p < 8; p++) {
-                const float w = p < CL ? red[2 * HROWS + p * HROWS + hr] : 0.0f;
+                const float w = p < CL ? rw[p * HROWS + hr] : 0.0f;
                 acc.x += w * v[p].x; acc.y += w * v[p].y; acc.z += w * v[p].z; acc.w += w * v[p].w;
             }
-            reinterpret_cast<float4 *>(ro)[e4] = acc;
+            if (n_cl == 1) write_out(e4, acc, rML[HROWS + hr]);
+            else reinterpret_cast<float4 *>(po)[e4] = acc;
         }
     }
-    cluster.sync();                                   // rank 0 is done reading its peers
-    if (crank != 0) return;
-    const float * rM = CL > 1 ? red : cm;             // cluster state: M[16], L[16], O[16][256]
-    const float * rO = CL > 1 ? ro : co;
-    __syncthreads();
-    const int n_rows = d.n_head_kv * 8;
-    auto write_out = [&](int e4, float4 v, float L) {
-        const int hr = (e4 * 4) / HEAD_DIM, h = hr & 7, g = hr >> 3;
-        if (g < d.n_head_kv && h < d.gqa) {
-            const float inv = L > 0.0f ? 1.0f / L : 0.0f;
-            reinterpret_cast<float4 *>(outq + (size_t) (g * d.gqa + h) * HEAD_DIM)[(e4 * 4 % HEAD_DIM) / 4] =
-                make_float4(v.x * inv, v.y * inv, v.z * inv, v.w * inv);
-        }
-    };
-    if (n_cl == 1) {                                  // the cluster covered every chunk: output
-        for (int e4 = tid; e4 < n_rows * HEAD_DIM / 4; e4 += ATT_THREADS)
-            write_out(e4, reinterpret_cast<const float4 *>(rO)[e4], rM[HROWS + (e4 * 4) / HEAD_DIM]);
-        return;
+    if (n_cl > 1) {
+        if (crank == 0 && tid < 2 * HROWS)
+            part_ml[((size_t) t * max_parts + cl_id) * 2 * HROWS + tid] = rML[tid];
+        __threadfence();                              // this rank's partial slice is visible GPU-wide
     }
-    // ---- second level: cluster partials in global memory, merged by the last cluster to arrive
-    const int max_parts = (max_chunks + CL - 1) / CL;
-    float * po = part_o + ((size_t) t * max_parts + cl_id) * HROWS * HEAD_DIM;
-    for (int e4 = tid; e4 < HROWS * HEAD_DIM / 4; e4 += ATT_THREADS)
-        reinterpret_cast<float4 *>(po)[e4] = reinterpret_cast<const float4 *>(rO)[e4];
-    float * pml = part_ml + ((size_t) t * max_parts + cl_id) * 2 * HROWS;
-    if (tid < 2 * HROWS) pml[tid] = rM[tid];
-    __syncthreads();
-    unsigned * cnt = counters + t;
-    if (tid == 0) {
-        // release this CTA's partial (ordered before by the barrier), acquire the others'
+    cluster.sync();                                   // peers are done reading; all slices written
+    if (n_cl == 1) return;
+    // ---- second level: the last cluster to arrive merges the cluster partials, slice by slice
+    // Rank 0 counts the arrival and writes the verdict into every rank's own shared memory before
+    // the barrier (a rank must never read the shared memory of a CTA that may already have exited).
+    if (crank == 0 && tid == 0) {
         unsigned prev;
-        asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], 1;" : "=r"(prev) : "l"(cnt) : "memory");
-        is_last = prev == (unsigned) (n_cl - 1);
-        if (is_last) *cnt = 0;
+        asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], 1;" : "=r"(prev) : "l"(counters + t) : "memory");
+        const bool last = prev == (unsigned) (n_cl - 1);
+        if (last) counters[t] = 0;
+        for (int p = 0; p < CL; p++) *cluster.map_shared_rank(&is_last, p) = last;
     }
-    __syncthreads();
+    cluster.sync();
     if (!is_last) return;
+    __threadfence();
     const float * pob = part_o + (size_t) t * max_parts * HROWS * HEAD_DIM;
     const float * pmb = part_ml + (size_t) t * max_parts * 2 * HROWS;
     float * gm = co;                                  // [n_cl][16] m -> weights (co is free now)
     float * gl = gm + n_cl * HROWS;                   // [n_cl][16] l
-    float * gML = gl + n_cl * HROWS;                  // [16] M, [16] L
+    float * gL = gl + n_cl * HROWS;                   // [16] L
     for (int i = tid; i < n_cl * 2 * HROWS; i += ATT_THREADS) {     // every (m, l) loaded at once
         const int c = i / (2 * HROWS), k = i % (2 * HROWS);
         const float v = __ldcg(pmb + i);
@@ -496,18 +562,18 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_kernel(
             gm[c * HROWS + tid] = w;
             L += gl[c * HROWS + tid] * w;
         }
-        gML[HROWS + tid] = L;
+        gL[tid] = L;
     }
     __syncthreads();
     const float4 * po4 = reinterpret_cast<const float4 *>(pob);
-    for (int e4 = tid; e4 < n_rows * HEAD_DIM / 4; e4 += ATT_THREADS) {
+    for (int e4 = e_beg + tid; e4 < e_end; e4 += ATT_THREADS) {
         const int hr = (e4 * 4) / HEAD_DIM;
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
         int c = 0;
         for (; c + 8 <= n_cl; c += 8) {
             float4 v[8];
             #pragma unroll
-            for (int u = 0; u < 8; u++) v[u] = __ldcg(po4 + (size_t) (c + u) * (HROWS * HEAD_DIM / 4) + e4);
+            for (int u = 0; u < 8; u++) v[u] = __ldcg(po4 + (size_t) (c + u) * n_e4 + e4);
             #pragma unroll
             for (int u = 0; u < 8; u++) {
                 const float w = gm[(c + u) * HROWS + hr];
@@ -515,11 +581,11 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_kernel(
             }
         }
         for (; c < n_cl; c++) {
-            const float4 v = __ldcg(po4 + (size_t) c * (HROWS * HEAD_DIM / 4) + e4);
+            const float4 v = __ldcg(po4 + (size_t) c * n_e4 + e4);
             const float w = gm[c * HROWS + hr];
             acc.x += w * v.x; acc.y += w * v.y; acc.z += w * v.z; acc.w += w * v.w;
         }
-        write_out(e4, acc, gML[HROWS + hr]);
+        write_out(e4, acc, gL[hr]);
     }
 }
 
@@ -549,13 +615,15 @@ cudaError_t launch_attn(const DevDesc & d, dim3 grid, cudaStream_t st, const qsa
     cfg.gridDim = grid;
     cfg.blockDim = dim3(ATT_THREADS);
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = (unsigned) CL;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;   // prologue overlaps the select
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     if (d.type_k == QSA_TYPE_Q8_0) {
         cfg.dynamicSmemBytes = attn_smem_bytes<QSA_TYPE_Q8_0>();
         return cudaLaunchKernelEx(&cfg, attn_kernel<QSA_TYPE_Q8_0>, d, items, cache0, n_past0, q, q_type, sel_ws,

@@ -50,6 +50,12 @@ __device__ __forceinline__ double warp_sum16_d(double v) {   // butterfly within
     return v;
 }
 
+// Programmatic dependent launch: a kernel launched with programmatic stream serialization may
+// start while its predecessor runs; it must wait before touching what the predecessor writes.
+// Triggering lets the successor launch once every CTA of this grid has started or exited.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ void set_status(uint32_t * status, uint32_t code) {
     if (status) atomicOr(status, code);
 }
@@ -63,6 +69,9 @@ __device__ __forceinline__ void mbar_init(uint64_t * bar, uint32_t count) {
 }
 __device__ __forceinline__ void fence_mbar_init() {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t * bar) {
+    asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" :: "r"(smem_u32(bar)) : "memory");
 }
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t * bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;"

@@ -5,13 +5,16 @@
 namespace qsa {
 
 constexpr int MAX_KB = 1024;          // blocks kept per query that the kernels can hold
-constexpr int SCORE_BLOCKS_PER_CTA = 128;
+constexpr int SEL_THREADS_HOST = 1024;      // threads of a scoring/selection CTA
 
 __global__ void append_rows_kernel(DevDesc d, qsa_layer_cache c, int pos0,
         const float * k, const float * v, const float * kidx);
 __global__ void pool_blocks_kernel(DevDesc d, const uint16_t * idx, uint16_t * pool, int blk0, int n_blk, float * out_f32);
 __global__ void append_decode_kernel(DevDesc d, const qsa_decode_item * items,
         const float * k, const float * v, const float * kidx, uint32_t * status);
+constexpr int APPEND_DECODE_THREADS = 1024;
+// dynamic shared memory of append_decode_kernel: one block of raw indexer keys
+inline size_t append_decode_smem(const DevDesc & d) { return (size_t) d.ratio * MAX_IDX_DIM * 2; }
 
 __global__ void score_select_kernel(DevDesc d, const qsa_decode_item * items, const uint16_t * pool0, int n_past0,
         const float * q_idx, int blocks_per_cta, float * scores_ws, int scores_stride, unsigned * counters,

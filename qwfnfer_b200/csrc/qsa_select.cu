@@ -17,7 +17,7 @@
 
 namespace qsa {
 
-constexpr int SEL_THREADS = 256;
+constexpr int SEL_THREADS = SEL_THREADS_HOST;
 
 // Score blocks [b_begin, b_end) of one query: 16 lanes per block row (8 dims = 16 bytes each).
 // Products of two f16 values are exact in f32; they are summed in double (exact for these
@@ -96,6 +96,29 @@ __device__ void select_blocks(const DevDesc & d, int q, const float * __restrict
     for (int b = tid; b < n_vis; b += blockDim.x) flag[b] = 0;
     if (!take_all) {
         remaining = want;
+        // Zero scores (relu cut every head) can only fill what the positive ones leave: count the
+        // positive candidates; when they are too few the cut is at 0 and zeros go by lowest index.
+        int n_pos = 0;
+        for (int b0 = 0; b0 < n_vis; b0 += blockDim.x) {
+            const int b = b0 + tid;
+            const bool pos = is_cand(b) && __float_as_uint(sc[b]) != 0u;
+            const unsigned bal = __ballot_sync(0xffffffffu, pos);
+            if ((tid & 31) == 0) n_pos += __popc(bal);
+        }
+        if ((tid & 31) == 0) sm.hist[tid >> 5] = (unsigned) n_pos;
+        __syncthreads();
+        if (tid == 0) {
+            int tot = 0;
+            for (int w = 0; w < (int) (blockDim.x >> 5); w++) tot += (int) sm.hist[w];
+            sm.bcast[3] = tot;
+        }
+        __syncthreads();
+        n_pos = sm.bcast[3];
+        __syncthreads();
+        if (n_pos < remaining) {               // cut at zero: every positive key is kept
+            prefix = 0; pmask = 0xffffffffu; remaining -= n_pos;
+            goto compaction;
+        }
         const int shifts[3] = {19, 7, 0};
         const int widths[3] = {12, 12, 7};
         for (int lv = 0; lv < 3; lv++) {
@@ -106,7 +129,7 @@ __device__ void select_blocks(const DevDesc & d, int q, const float * __restrict
             for (int b = tid; b < n_vis; b += blockDim.x) {
                 if (!is_cand(b)) continue;
                 const uint32_t key = __float_as_uint(sc[b]);
-                if ((key & pmask) == prefix) atomicAdd(&sm.hist[(key >> shift) & bmask], 1u);
+                if (key != 0u && (key & pmask) == prefix) atomicAdd(&sm.hist[(key >> shift) & bmask], 1u);
             }
             __syncthreads();
             // thread i owns bins counted from the top: [nb - per*(i+1), nb - per*i)
@@ -166,18 +189,22 @@ __device__ void select_blocks(const DevDesc & d, int q, const float * __restrict
         }
         __syncthreads();
     }
+compaction:
     // Compaction over [0, max(n_vis, f_hi+1)) in ascending order: each thread owns a contiguous run.
-    // Without ranking (more than CAND_MAX equal keys) the bin's first `remaining` by index are kept.
+    // Without ranking (more than CAND_MAX equal keys) the bin's first `remaining` by index are kept,
+    // which needs the number of such ties before each thread's run.
     const int n_range = max(n_vis, f_hi + 1);
     const int per = (n_range + blockDim.x - 1) / blockDim.x;
     const int lo = tid * per, hi = min(n_range, lo + per);
-    int n_tie = 0;
-    if (!take_all && !ranked)
+    const bool tie_quota = !take_all && !ranked;
+    int tie_base = 0;
+    if (tie_quota) {
+        int n_tie = 0;
         for (int b = lo; b < hi; b++)
             if (is_cand(b) && (__float_as_uint(sc[b]) & pmask) == prefix) n_tie++;
-    int tie_base;
-    SelSmem::Scan(sm.scan).ExclusiveSum(n_tie, tie_base);
-    __syncthreads();
+        SelSmem::Scan(sm.scan).ExclusiveSum(n_tie, tie_base);
+        __syncthreads();
+    }
     auto take = [&](int b, int & tie_i) -> bool {
         if (b >= f_lo && b <= f_hi) return true;
         if (!is_cand(b)) return false;
@@ -188,19 +215,36 @@ __device__ void select_blocks(const DevDesc & d, int q, const float * __restrict
         if (ranked) return flag[b] != 0;
         return tie_i++ < remaining;
     };
+    unsigned long long bits = 0;                       // take flags of the run (runs of <= 64)
     int n_take = 0, tie_i = tie_base;
-    for (int b = lo; b < hi; b++) n_take += take(b, tie_i);
+    for (int b = lo; b < hi; b++) {
+        const bool tk = take(b, tie_i);
+        n_take += tk;
+        if (per <= 64 && tk) bits |= 1ull << (b - lo);
+    }
     int base, total;
     SelSmem::Scan(sm.scan).ExclusiveSum(n_take, base, total);
-    tie_i = tie_base;
     int pos = base;
-    for (int b = lo; b < hi; b++) {
-        if (take(b, tie_i)) {
+    if (per <= 64) {
+        while (bits) {
+            const int b = lo + __ffsll((long long) bits) - 1;
+            bits &= bits - 1;
             if (pos < d.kb) {
                 sel[pos] = b;
                 if (sel_out) sel_out[pos] = b;
             }
             pos++;
+        }
+    } else {
+        tie_i = tie_base;
+        for (int b = lo; b < hi; b++) {
+            if (take(b, tie_i)) {
+                if (pos < d.kb) {
+                    sel[pos] = b;
+                    if (sel_out) sel_out[pos] = b;
+                }
+                pos++;
+            }
         }
     }
     const int n = min(total, d.kb);
@@ -220,6 +264,7 @@ __global__ void __launch_bounds__(SEL_THREADS) score_select_kernel(DevDesc d,
     extern __shared__ __align__(16) unsigned char dyn_smem[];
     __shared__ SelSmem sm;
     __shared__ bool is_last;
+    pdl_trigger();
     const int t = blockIdx.y;
     const int q = items ? items[t].n_past : n_past0 + t;
     const uint16_t * pool = items ? items[t].cache.pool : pool0;
@@ -240,8 +285,10 @@ __global__ void __launch_bounds__(SEL_THREADS) score_select_kernel(DevDesc d,
                     : 0.0f;
         const int b0 = blockIdx.x * blocks_per_cta;
         const int b1 = min(n_vis, b0 + blocks_per_cta);
+        pdl_wait();                              // the append of this step (pooled keys) is complete
         if (b0 < b1) score_range(d, pool, qf, b0, b1, sc);
     }
+    if (bad) pdl_wait();
     // Arrival: the last CTA of this query selects.  The barrier orders the CTA's score stores
     // before thread 0's release; its acquire orders the other CTAs' stores before our reads.
     __syncthreads();
@@ -255,7 +302,12 @@ __global__ void __launch_bounds__(SEL_THREADS) score_select_kernel(DevDesc d,
     if (!is_last) return;
     float * ssc = reinterpret_cast<float *>(dyn_smem);
     unsigned char * flag = dyn_smem + (size_t) scores_stride * 4;
-    for (int b = threadIdx.x; b < n_vis; b += blockDim.x) ssc[b] = __ldcg(sc + b);
+    {   // the query's scores, 16 bytes per load (score rows are 16-byte aligned)
+        const int n4 = (n_vis + 3) / 4;
+        #pragma unroll 4
+        for (int i = threadIdx.x; i < n4; i += blockDim.x)
+            reinterpret_cast<float4 *>(ssc)[i] = __ldcg(reinterpret_cast<const float4 *>(sc) + i);
+    }
     __syncthreads();
     if (bad) {
         for (int i = threadIdx.x; i < d.kb; i += blockDim.x) {
