@@ -171,6 +171,22 @@ qsa_status qsa_decode_attend(const qsa_desc * d, const qsa_decode_item * items, 
                              const void * q, int32_t q_type, float * out, void * ws, size_t ws_bytes,
                              qsa_stream_t stream);
 
+/* qsa_decode without a caller workspace.  No counterpart in the reference.
+ * For callers that cannot allocate device memory -- an operator run inside another framework's
+ * planned graph sees only its input and output tensors, and a serving loop under a fixed memory
+ * budget must not call cudaMalloc on the token path -- the scratch lives in a fixed device array
+ * of 4 MiB inside the library (held on every GPU that loads it, until exit).  Arguments and
+ * results are those of qsa_decode; a call whose qsa_decode_workspace_size() exceeds 4 MiB returns
+ * QSA_ERR_WORKSPACE.  The first call on a device looks up the array's device address and zeroes
+ * it (synchronously): make that first call before any stream capture.  Every call zeroes the
+ * array's status word and counters and otherwise reuses the last call's contents, so calls that
+ * overlap on the GPU (other streams or threads) race; device-side range errors cannot be read back
+ * through this entry point (the affected query's output is zero).  Nothing is allocated. */
+qsa_status qsa_decode_noalloc(const qsa_desc * d, const qsa_decode_item * items, int32_t batch, int32_t max_n_kv,
+                              const void * q, int32_t q_type, const float * q_idx,
+                              const float * k_new, const float * v_new, const float * kidx_new,
+                              float * out, int32_t * sel_out, qsa_stream_t stream);
+
 /* ------------------------------------------------------------------ prefill */
 size_t qsa_prefill_workspace_size(const qsa_desc * d, int32_t T, int32_t max_n_kv);
 

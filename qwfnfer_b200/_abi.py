@@ -114,6 +114,7 @@ def lib() -> ctypes.CDLL:
         "qsa_decode_append": (I32, [D, VP, I32, I32, VP, VP, VP, VP, SZ, VP]),
         "qsa_decode_select": (I32, [D, VP, I32, I32, VP, VP, VP, SZ, VP]),
         "qsa_decode_attend": (I32, [D, VP, I32, I32, VP, I32, VP, VP, SZ, VP]),
+        "qsa_decode_noalloc": (I32, [D, VP, I32, I32, VP, I32, VP, VP, VP, VP, VP, VP, VP]),
         "qsa_prefill_workspace_size": (SZ, [D, I32, I32]),
         "qsa_prefill": (I32, [D, C, I32, I32, VP, I32, VP, VP, VP, VP, VP, VP, VP, SZ, VP]),
         "qsa_check": (I32, [VP, SZ, VP]),
@@ -135,5 +136,5 @@ def check(status: int, where: str) -> None:
 HEADER_SYMBOLS = [
     "qsa_status_string", "qsa_desc_check", "qsa_k_blocks", "qsa_row_bytes", "qsa_cache_bytes",
     "qsa_append", "qsa_pool_rebuild", "qsa_decode_workspace_size", "qsa_workspace_init",
-    "qsa_decode", "qsa_decode_append", "qsa_decode_select", "qsa_decode_attend", "qsa_prefill_workspace_size", "qsa_prefill", "qsa_check", "qsa_version",
+    "qsa_decode", "qsa_decode_append", "qsa_decode_select", "qsa_decode_attend", "qsa_decode_noalloc", "qsa_prefill_workspace_size", "qsa_prefill", "qsa_check", "qsa_version",
 ]

@@ -144,6 +144,14 @@ qsa_status launch_attend(const DevDesc & d, const WsLayout & w, int n_q, const q
 }
 
 }  // namespace
+
+// Bytes at the start of a decode workspace that must be zero before a call: the status word and
+// the arrival counters (the kernels leave their counters at zero, but the region's extent depends
+// on the batch size).
+size_t decode_workspace_zero_prefix(const qsa_desc * d, int32_t batch, int32_t max_n_kv) {
+    return ws_layout(make_dev(d), batch, max_n_kv).scores;
+}
+
 }  // namespace qsa
 
 using namespace qsa;

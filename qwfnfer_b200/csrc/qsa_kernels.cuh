@@ -20,6 +20,9 @@ __global__ void score_select_kernel(DevDesc d, const qsa_decode_item * items, co
         const float * q_idx, int blocks_per_cta, float * scores_ws, int scores_stride, unsigned * counters,
         int * sel_ws, int * nsel_ws, int * sel_out, uint32_t * status);
 
+// Leading bytes of a decode workspace that must be zero before a call (status word + counters).
+size_t decode_workspace_zero_prefix(const qsa_desc * d, int32_t batch, int32_t max_n_kv);
+
 // Host launcher of the attention kernel (defined beside the kernel template).
 cudaError_t launch_attn(const DevDesc & d, dim3 grid, cudaStream_t st, const qsa_decode_item * items,
         qsa_layer_cache cache0, int n_past0, const void * q, int q_type, const int * sel_ws, const int * nsel_ws,
