@@ -187,6 +187,42 @@ qsa_status qsa_decode_noalloc(const qsa_desc * d, const qsa_decode_item * items,
                               const float * k_new, const float * v_new, const float * kidx_new,
                               float * out, int32_t * sel_out, qsa_stream_t stream);
 
+/* ------------------------------------------------------------------ KV-sequence-sharded decode
+ * No counterpart in the reference, which decodes a sequence on one device: for contexts whose
+ * caches do not fit (or are not fast enough on) one GPU, the cells of every layer are split into
+ * contiguous block ranges, one per GPU.  Shard g holds blocks [blk_lo, blk_hi) (cells
+ * blk_lo*ratio .. blk_hi*ratio-1) in local arrays: the caches named by `items` on that GPU have
+ * row 0 = cell blk_lo*ratio and pooled row 0 = block blk_lo.  The descriptor (n_ctx included),
+ * n_past and max_n_kv stay global.  One step, on every shard with the same arguments otherwise:
+ *   1. qsa_shard_candidates: append of the new token by the shard holding its cell (the others
+ *      skip it), scores of the shard's visible blocks, and the shard's best KB blocks outside the
+ *      forced window, into cand = int32 [2][batch][KB]: the block ids (-1 padded), then the bits
+ *      of their f32 scores.
+ *   2. the caller all-gathers cand, in shard order: all_cand = int32 [n_shards][2][batch][KB].
+ *   3. qsa_shard_attend: the global selection (identical to qsa_decode's; sel_out optional,
+ *      [batch][KB] ascending), then attention over the shard's part of it into `state`,
+ *      f32 [batch][qsa_shard_state_floats()]: per (KV head x 8) row its running max (log2
+ *      domain), its sum of weights, and its unnormalised output.
+ *   4. the caller all-gathers the states: [n_shards][batch][...].
+ *   5. qsa_merge_states: out f32 [batch][n_head][head_dim], as qsa_decode's.
+ * Workspaces are sized by qsa_decode_workspace_size with the global max_n_kv. */
+size_t qsa_shard_state_floats(const qsa_desc * d);
+/* qsa_append into a shard's local arrays: global rows [pos0, pos0+n_tok), all inside the shard's
+ * cells; pooled keys carry their global block positions. */
+qsa_status qsa_shard_append(const qsa_desc * d, const qsa_layer_cache * cache /* host struct */,
+                            int32_t blk_lo, int32_t blk_hi, int32_t pos0, int32_t n_tok,
+                            const float * k, const float * v, const float * kidx, qsa_stream_t stream);
+qsa_status qsa_shard_candidates(const qsa_desc * d, const qsa_decode_item * items, int32_t batch, int32_t max_n_kv,
+                                int32_t blk_lo, int32_t blk_hi, const float * q_idx,
+                                const float * k_new, const float * v_new, const float * kidx_new,
+                                int32_t * cand, void * ws, size_t ws_bytes, qsa_stream_t stream);
+qsa_status qsa_shard_attend(const qsa_desc * d, const qsa_decode_item * items, int32_t batch, int32_t max_n_kv,
+                            int32_t blk_lo, int32_t blk_hi, int32_t n_shards, const int32_t * all_cand,
+                            const void * q, int32_t q_type, float * state,
+                            int32_t * sel_out, void * ws, size_t ws_bytes, qsa_stream_t stream);
+qsa_status qsa_merge_states(const qsa_desc * d, int32_t n_parts, int32_t batch, const float * states, float * out,
+                            qsa_stream_t stream);
+
 /* ------------------------------------------------------------------ prefill */
 size_t qsa_prefill_workspace_size(const qsa_desc * d, int32_t T, int32_t max_n_kv);
 

@@ -44,6 +44,7 @@ def lib() -> ctypes.CDLL:
             "orc_scores": (None, [D, VP, I64, I64, VP, VP]),
             "orc_select": (ctypes.c_int, [D, VP, I64, VP, VP]),
             "orc_attend": (None, [D, VP, VP, I64, VP, VP, I64, VP, I32, VP, I32]),
+            "orc_attend_state": (None, [D, VP, VP, I64, VP, VP, I64, VP, I32, VP, I32]),
             "orc_k_blocks": (ctypes.c_int, [D]),
             "orc_node": (None, [D, VP, VP, VP, I64, VP, VP, I32, VP, VP, VP, VP, I32]),
         }
@@ -150,6 +151,38 @@ def attend(d: QsaDesc, kc: np.ndarray, vc: np.ndarray, q_pos, sel: np.ndarray, Q
     lib().orc_attend(ctypes.byref(d), _p(np.ascontiguousarray(kc)), _p(np.ascontiguousarray(vc)), n_q,
                      _p(q_pos), _p(sel), sel.shape[1], _p(Q), q_type, _p(out), flags)
     return out
+
+
+def attend_state(d: QsaDesc, kc: np.ndarray, vc: np.ndarray, q_pos, sel: np.ndarray, Q: np.ndarray,
+                 q_type: int = TYPE_F32, flags: int = DEFAULT_FLAGS) -> np.ndarray:
+    """Unnormalised attention state f32 [n_q, 32 + 16*head_dim] ([M 16][L 16][O 16 x hd], rows
+    8*kv_head + head, M in the log2 domain) over the selected blocks; orc_attend_state."""
+    q_pos = np.ascontiguousarray(np.atleast_1d(q_pos), dtype=np.int64)
+    n_q = q_pos.size
+    sel = np.ascontiguousarray(sel, dtype=np.int32).reshape(n_q, -1)
+    Q = np.ascontiguousarray(Q)
+    out = np.empty((n_q, 32 + 16 * d.head_dim), dtype=np.float32)
+    lib().orc_attend_state(ctypes.byref(d), _p(np.ascontiguousarray(kc)), _p(np.ascontiguousarray(vc)), n_q,
+                           _p(q_pos), _p(sel), sel.shape[1], _p(Q), q_type, _p(out), flags)
+    return out
+
+
+def merge_states(d: QsaDesc, states: np.ndarray) -> np.ndarray:
+    """Log-sum-exp merge of states [n_parts, n_q, 32 + 16*hd] -> f32 [n_q, n_head, hd], in double:
+    M = max_p M_p;  out = sum_p 2^(M_p - M) O_p / sum_p 2^(M_p - M) L_p."""
+    P, n_q, _ = states.shape
+    hd, gqa = d.head_dim, d.n_head // d.n_head_kv
+    M = states[:, :, :16].astype(np.float64)
+    L = states[:, :, 16:32].astype(np.float64)
+    O = states[:, :, 32:].astype(np.float64).reshape(P, n_q, 16, hd)
+    Mx = M.max(axis=0)
+    Mu = np.where(np.isneginf(Mx), 0.0, Mx)
+    w = np.exp2(M - Mu[None])                                   # [P, n_q, 16]
+    Ls = (w * L).sum(axis=0)
+    Os = (w[..., None] * O).sum(axis=0)
+    res = np.where(Ls[..., None] > 0, Os / np.where(Ls > 0, Ls, 1.0)[..., None], 0.0)
+    rows = [8 * g + h for g in range(d.n_head_kv) for h in range(gqa)]
+    return res[:, rows, :].astype(np.float32)
 
 
 def node(d: QsaDesc, kc, vc, pool, q_pos, Q, q_idx, q_type: int = TYPE_F32, flags: int = DEFAULT_FLAGS):

@@ -375,6 +375,69 @@ void orc_attend(const qsa_desc * d, const uint8_t * kc, const uint8_t * vc,
     }
 }
 
+// Unnormalised attention state of n_q queries over their selected blocks, the layout the
+// sharded decode exchanges between devices: per query 16 rows (KV head g, query head h of its
+// group -> row 8g+h; unused rows M=-inf, L=0, O=0), as [M 16][L 16][O 16 x head_dim] with
+//   M = max_c s_c * log2(e) / sqrt(head_dim)   (log2 domain),
+//   L = sum_c 2^(s'_c - M),  O = sum_c 2^(s'_c - M) v_c.
+// Computed in double (exact reference arithmetic) and rounded once; an empty selection gives
+// M = -inf.  Merging states of disjoint cell sets reproduces orc_attend's output.
+void orc_attend_state(const qsa_desc * d, const uint8_t * kc, const uint8_t * vc,
+                      int64_t n_q, const int64_t * q_pos, const int32_t * sel, int64_t sel_stride,
+                      const void * Q, int32_t q_type, float * state, int32_t flags) {
+    const int64_t hd = d->head_dim, nh = d->n_head, nkv = d->n_head_kv, gqa = nh / nkv, r = d->ratio;
+    const int64_t kv_dim = nkv * hd, SF = 2 * 16 + 16 * hd;
+    const size_t rbk = row_bytes(d->type_k, kv_dim), rbv = row_bytes(d->type_v, kv_dim);
+    const bool kv_round = flags & ORC_KV_F16_ROUND, q_f16 = flags & ORC_Q_F16;
+    const double scale_log2 = 1.4426950408889634 / std::sqrt((double) hd);
+    #pragma omp parallel for schedule(dynamic) collapse(2)
+    for (int64_t t = 0; t < n_q; t++) {
+        for (int64_t row = 0; row < 16; row++) {
+            float * st = state + t * SF;
+            const int64_t g = row / 8, h = row % 8;
+            float * o = st + 32 + row * hd;
+            if (g >= nkv || h >= gqa) {
+                st[row] = -INFINITY; st[16 + row] = 0.0f;
+                for (int64_t e = 0; e < hd; e++) o[e] = 0.0f;
+                continue;
+            }
+            const int64_t head = g * gqa + h, qp = q_pos[t];
+            std::vector<float> qv(hd);
+            for (int64_t e = 0; e < hd; e++) {
+                const int64_t idx = (t * nh + head) * hd + e;
+                float x = q_type == QSA_TYPE_BF16 ? bf16_to_f32(((const uint16_t *) Q)[idx]) : ((const float *) Q)[idx];
+                qv[e] = q_f16 ? f16_to_f32(f32_to_f16(x)) : x;
+            }
+            std::vector<int64_t> cells;
+            for (int64_t i = 0; i < sel_stride; i++) {
+                const int32_t b = sel[t * sel_stride + i];
+                if (b < 0) continue;
+                for (int64_t c = b * r; c < (b + 1) * r && c <= qp; c++) cells.push_back(c);
+            }
+            std::vector<double> s(cells.size());
+            double m = -INFINITY;
+            for (size_t j = 0; j < cells.size(); j++) {
+                const uint8_t * kr = kc + (size_t) cells[j] * rbk;
+                double acc = 0.0;
+                for (int64_t e = 0; e < hd; e++) acc += (double) kv_value(kr, d->type_k, (int) (g * hd + e), kv_round) * (double) qv[e];
+                s[j] = acc * scale_log2;
+                m = std::max(m, s[j]);
+            }
+            std::vector<double> acc(hd, 0.0);
+            double l = 0.0;
+            for (size_t j = 0; j < cells.size(); j++) {
+                const double p = std::exp2(s[j] - m);
+                l += p;
+                const uint8_t * vr = vc + (size_t) cells[j] * rbv;
+                for (int64_t e = 0; e < hd; e++) acc[e] += p * (double) kv_value(vr, d->type_v, (int) (g * hd + e), kv_round);
+            }
+            st[row] = (float) m;
+            st[16 + row] = (float) l;
+            for (int64_t e = 0; e < hd; e++) o[e] = (float) acc[e];
+        }
+    }
+}
+
 // Blocks kept per query (KB).
 int orc_k_blocks(const qsa_desc * d) { return (int) (d->top_k_blocks + n_force_max(d)); }
 

@@ -13,6 +13,7 @@ PKG_DIR = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(PKG_DIR, "libqsa.so")
 
 QSA_OK = 0
+QSA_ERR_INVALID, QSA_ERR_CUDA, QSA_ERR_TIMEOUT, QSA_ERR_UNSUPPORTED, QSA_ERR_WORKSPACE, QSA_ERR_DEVICE_ARG = 1, 2, 3, 4, 5, 6
 STATUS_NAMES = {
     0: "QSA_OK", 1: "QSA_ERR_INVALID", 2: "QSA_ERR_CUDA", 3: "QSA_ERR_TIMEOUT",
     4: "QSA_ERR_UNSUPPORTED", 5: "QSA_ERR_WORKSPACE", 6: "QSA_ERR_DEVICE_ARG",
@@ -115,6 +116,11 @@ def lib() -> ctypes.CDLL:
         "qsa_decode_select": (I32, [D, VP, I32, I32, VP, VP, VP, SZ, VP]),
         "qsa_decode_attend": (I32, [D, VP, I32, I32, VP, I32, VP, VP, SZ, VP]),
         "qsa_decode_noalloc": (I32, [D, VP, I32, I32, VP, I32, VP, VP, VP, VP, VP, VP, VP]),
+        "qsa_shard_state_floats": (SZ, [D]),
+        "qsa_shard_append": (I32, [D, C, I32, I32, I32, I32, VP, VP, VP, VP]),
+        "qsa_shard_candidates": (I32, [D, VP, I32, I32, I32, I32, VP, VP, VP, VP, VP, VP, SZ, VP]),
+        "qsa_shard_attend": (I32, [D, VP, I32, I32, I32, I32, I32, VP, VP, I32, VP, VP, VP, SZ, VP]),
+        "qsa_merge_states": (I32, [D, I32, I32, VP, VP, VP]),
         "qsa_prefill_workspace_size": (SZ, [D, I32, I32]),
         "qsa_prefill": (I32, [D, C, I32, I32, VP, I32, VP, VP, VP, VP, VP, VP, VP, SZ, VP]),
         "qsa_check": (I32, [VP, SZ, VP]),
@@ -136,5 +142,7 @@ def check(status: int, where: str) -> None:
 HEADER_SYMBOLS = [
     "qsa_status_string", "qsa_desc_check", "qsa_k_blocks", "qsa_row_bytes", "qsa_cache_bytes",
     "qsa_append", "qsa_pool_rebuild", "qsa_decode_workspace_size", "qsa_workspace_init",
-    "qsa_decode", "qsa_decode_append", "qsa_decode_select", "qsa_decode_attend", "qsa_decode_noalloc", "qsa_prefill_workspace_size", "qsa_prefill", "qsa_check", "qsa_version",
+    "qsa_decode", "qsa_decode_append", "qsa_decode_select", "qsa_decode_attend", "qsa_decode_noalloc",
+    "qsa_shard_state_floats", "qsa_shard_append", "qsa_shard_candidates", "qsa_shard_attend", "qsa_merge_states",
+    "qsa_prefill_workspace_size", "qsa_prefill", "qsa_check", "qsa_version",
 ]

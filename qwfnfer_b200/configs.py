@@ -54,10 +54,14 @@ CONFIGS = {
 }
 
 
-def fill_cache(node, state, il: int, n_tok: int, seed: int, chunk: int = 1 << 16, device="cuda") -> None:
+def fill_cache(node, state, il: int, n_tok: int, seed: int, chunk: int = 1 << 16, device="cuda",
+               append=None) -> None:
     """Append n_tok seeded random tokens at rows [0, n_tok) through the library's append path
-    (q8_0 quantisation, raw indexer keys, pooled keys of the completed blocks)."""
+    (q8_0 quantisation, raw indexer keys, pooled keys of the completed blocks).  `append(cache,
+    pos0, K, V, kidx)` replaces node.append (a shard's append keeps the rows in its cells; the
+    random stream is the same, so shards hold exactly the rows of the unsharded cache)."""
     d = node.desc
+    append = append or node.append
     kv_dim = d.n_head_kv * d.head_dim
     g = torch.Generator(device=device).manual_seed(seed)
     for pos in range(0, n_tok, chunk):
@@ -65,7 +69,7 @@ def fill_cache(node, state, il: int, n_tok: int, seed: int, chunk: int = 1 << 16
         K = torch.randn(n, kv_dim, generator=g, device=device) * K_SCALE
         V = torch.randn(n, kv_dim, generator=g, device=device)
         ki = torch.randn(n, d.idx_dim, generator=g, device=device) * IDX_STD
-        node.append(state.layer(il), pos, K, V, ki)
+        append(state.layer(il), pos, K, V, ki)
 
 
 def token_inputs(d: QsaDesc, n: int, seed: int, q_dtype=torch.bfloat16, device="cuda"):

@@ -1,4 +1,5 @@
 // qsa_api.cu -- the C ABI of libqsa (include/qsa.h): validation, workspace layout, launches.
+#include <climits>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -43,6 +44,8 @@ DevDesc make_dev(const qsa_desc * d) {
     x.rb_v = (int64_t) kv_row_bytes(d->type_v, kv_dim);
     x.hb_k = (int) kv_row_bytes(d->type_k, d->head_dim);
     x.hb_v = (int) kv_row_bytes(d->type_v, d->head_dim);
+    x.shard_blk0 = 0;
+    x.shard_blk1 = INT_MAX;
     return x;
 }
 
@@ -104,16 +107,18 @@ qsa_status set_attrs() {
     return QSA_OK;
 }
 
-// Scores + selection into the workspace (and sel_out).
+// Scores + selection into the workspace (and sel_out).  Sharded (cand_scores != null): scores of
+// the shard's blocks only, and its candidates with their scores in sel_out / cand_scores.
 qsa_status launch_select(const DevDesc & d, const WsLayout & w, int n_q, const qsa_decode_item * items,
                          qsa_layer_cache cache0, int n_past0, const float * q_idx, int32_t * sel_out,
-                         unsigned char * ws, cudaStream_t st) {
+                         unsigned char * ws, cudaStream_t st, float * cand_scores = nullptr) {
     uint32_t * status = reinterpret_cast<uint32_t *>(ws + w.status);
     // blocks per scoring CTA: 16 (one row pair per warp) while the grid is small, more once
     // there are enough CTAs to fill the GPU several times over
+    const int n_blk = std::max(1, std::min(w.scores_stride, d.shard_blk1) - d.shard_blk0);   // blocks scored
     int bpc = 2 * (SEL_THREADS_HOST / 32);                 // one row pair per warp
-    while (bpc < 1024 && (int64_t) ceil_div(w.scores_stride, 2 * bpc) * n_q >= 2 * 148) bpc *= 2;
-    const int score_ctas = ceil_div(w.scores_stride, bpc);
+    while (bpc < 1024 && (int64_t) ceil_div(n_blk, 2 * bpc) * n_q >= 2 * 148) bpc *= 2;
+    const int score_ctas = ceil_div(n_blk, bpc);
     const size_t sel_smem = (size_t) w.scores_stride * 5;       // scores + selection flags
     if (sel_smem > 160 * 1024) return QSA_ERR_UNSUPPORTED;
     cudaLaunchConfig_t cfg = {};
@@ -128,19 +133,19 @@ qsa_status launch_select(const DevDesc & d, const WsLayout & w, int n_q, const q
     cfg.numAttrs = 1;
     return cuda_status(cudaLaunchKernelEx(&cfg, score_select_kernel, d, items, cache0.pool, n_past0, q_idx, bpc,
         reinterpret_cast<float *>(ws + w.scores), w.scores_stride, reinterpret_cast<unsigned *>(ws + w.cnt_sel),
-        reinterpret_cast<int *>(ws + w.sel), reinterpret_cast<int *>(ws + w.nsel), sel_out, status));
+        reinterpret_cast<int *>(ws + w.sel), reinterpret_cast<int *>(ws + w.nsel), sel_out, status, cand_scores));
 }
 
 // Attention over the selection held in the workspace.
 qsa_status launch_attend(const DevDesc & d, const WsLayout & w, int n_q, const qsa_decode_item * items,
                          qsa_layer_cache cache0, int n_past0, const void * q, int q_type, float * out,
-                         unsigned char * ws, cudaStream_t st) {
+                         unsigned char * ws, cudaStream_t st, float * state_out = nullptr) {
     const dim3 grid(w.max_chunks, d.n_head_kv, n_q);
     return cuda_status(launch_attn(d, grid, st, items, cache0, n_past0, q, q_type,
                                    reinterpret_cast<const int *>(ws + w.sel), reinterpret_cast<const int *>(ws + w.nsel),
                                    w.tiles_per_cta, w.max_chunks, reinterpret_cast<float *>(ws + w.part_o),
                                    reinterpret_cast<float *>(ws + w.part_ml), reinterpret_cast<unsigned *>(ws + w.cnt_att),
-                                   out, reinterpret_cast<uint32_t *>(ws + w.status)));
+                                   out, reinterpret_cast<uint32_t *>(ws + w.status), state_out));
 }
 
 }  // namespace
@@ -209,15 +214,12 @@ size_t qsa_cache_bytes(const qsa_desc * d, int32_t which) {
     return rows * qsa_row_bytes(d, which);
 }
 
-qsa_status qsa_append(const qsa_desc * dd, const qsa_layer_cache * cache, int32_t pos0, int32_t n_tok,
-                      const float * k, const float * v, const float * kidx, qsa_stream_t stream) {
-    qsa_status s = qsa_desc_check(dd);
-    if (s != QSA_OK) return s;
-    if (!cache || pos0 < 0 || n_tok < 0 || (int64_t) pos0 + n_tok > dd->n_ctx) return QSA_ERR_INVALID;
+namespace {
+qsa_status append_impl(const DevDesc & d, const qsa_layer_cache * cache, int32_t pos0, int32_t n_tok,
+                       const float * k, const float * v, const float * kidx, qsa_stream_t stream) {
     if ((k && !cache->k) || (v && !cache->v) || (kidx && (!cache->idx || !cache->pool))) return QSA_ERR_INVALID;
     if (n_tok == 0) return QSA_OK;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    const DevDesc d = make_dev(dd);
     append_rows_kernel<<<n_tok, 256, 0, st>>>(d, *cache, pos0, k, v, kidx);
     if (kidx) {
         const int b0 = pos0 / d.ratio, b1 = (pos0 + n_tok) / d.ratio;   // blocks complete after the append
@@ -227,6 +229,29 @@ qsa_status qsa_append(const qsa_desc * dd, const qsa_layer_cache * cache, int32_
         }
     }
     return cuda_status(cudaGetLastError());
+}
+}  // namespace
+
+qsa_status qsa_append(const qsa_desc * dd, const qsa_layer_cache * cache, int32_t pos0, int32_t n_tok,
+                      const float * k, const float * v, const float * kidx, qsa_stream_t stream) {
+    qsa_status s = qsa_desc_check(dd);
+    if (s != QSA_OK) return s;
+    if (!cache || pos0 < 0 || n_tok < 0 || (int64_t) pos0 + n_tok > dd->n_ctx) return QSA_ERR_INVALID;
+    return append_impl(make_dev(dd), cache, pos0, n_tok, k, v, kidx, stream);
+}
+
+qsa_status qsa_shard_append(const qsa_desc * dd, const qsa_layer_cache * cache, int32_t blk_lo, int32_t blk_hi,
+                            int32_t pos0, int32_t n_tok, const float * k, const float * v, const float * kidx,
+                            qsa_stream_t stream) {
+    qsa_status s = qsa_desc_check(dd);
+    if (s != QSA_OK) return s;
+    if (!cache || blk_lo < 0 || blk_hi <= blk_lo || (int64_t) blk_hi * dd->ratio > dd->n_ctx) return QSA_ERR_INVALID;
+    if (n_tok < 0 || pos0 < blk_lo * dd->ratio || (int64_t) pos0 + n_tok > (int64_t) blk_hi * dd->ratio)
+        return QSA_ERR_INVALID;
+    DevDesc d = make_dev(dd);
+    d.shard_blk0 = blk_lo;
+    d.shard_blk1 = blk_hi;
+    return append_impl(d, cache, pos0, n_tok, k, v, kidx, stream);
 }
 
 qsa_status qsa_pool_rebuild(const qsa_desc * dd, const qsa_layer_cache * cache, int32_t blk0, int32_t n_blk,
@@ -361,6 +386,72 @@ qsa_status qsa_check(void * ws, size_t ws_bytes, qsa_stream_t stream) {
         return QSA_ERR_DEVICE_ARG;
     }
     return QSA_OK;
+}
+
+// ---- KV-sequence-sharded decode
+size_t qsa_shard_state_floats(const qsa_desc * d) {
+    (void) d;
+    return (size_t) attn_state_rows() * (2 + HEAD_DIM);
+}
+
+namespace {
+qsa_status shard_common(const qsa_desc * dd, const qsa_decode_item * items, int32_t batch, int32_t max_n_kv,
+                        int32_t blk_lo, int32_t blk_hi, void * ws, size_t ws_bytes, DevDesc & d, WsLayout & w) {
+    qsa_status s = decode_common(dd, items, batch, max_n_kv, ws, ws_bytes, d, w);
+    if (s != QSA_OK) return s;
+    if (blk_lo < 0 || blk_hi <= blk_lo || (int64_t) blk_hi * dd->ratio > dd->n_ctx) return QSA_ERR_INVALID;
+    d.shard_blk0 = blk_lo;
+    d.shard_blk1 = blk_hi;
+    return QSA_OK;
+}
+}  // namespace
+
+qsa_status qsa_shard_candidates(const qsa_desc * dd, const qsa_decode_item * items, int32_t batch, int32_t max_n_kv,
+                                int32_t blk_lo, int32_t blk_hi, const float * q_idx,
+                                const float * k_new, const float * v_new, const float * kidx_new,
+                                int32_t * cand, void * ws, size_t ws_bytes, qsa_stream_t stream) {
+    DevDesc d; WsLayout w;
+    qsa_status s = shard_common(dd, items, batch, max_n_kv, blk_lo, blk_hi, ws, ws_bytes, d, w);
+    if (s != QSA_OK) return s;
+    if (!q_idx || !cand) return QSA_ERR_INVALID;
+    const bool any_new = k_new || v_new || kidx_new;
+    if (any_new && !(k_new && v_new && kidx_new)) return QSA_ERR_INVALID;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    unsigned char * wsb = static_cast<unsigned char *>(ws);
+    if (any_new)           // only the shard holding a query's cell writes it (the kernel skips the rest)
+        append_decode_kernel<<<batch, APPEND_DECODE_THREADS, append_decode_smem(d), st>>>(d, items, k_new, v_new, kidx_new,
+                                                    reinterpret_cast<uint32_t *>(wsb + w.status));
+    qsa_layer_cache none{};
+    return launch_select(d, w, batch, items, none, 0, q_idx, cand, wsb, st,
+                         reinterpret_cast<float *>(cand + (size_t) batch * d.kb));
+}
+
+qsa_status qsa_shard_attend(const qsa_desc * dd, const qsa_decode_item * items, int32_t batch, int32_t max_n_kv,
+                            int32_t blk_lo, int32_t blk_hi, int32_t n_shards, const int32_t * all_cand,
+                            const void * q, int32_t q_type, float * state,
+                            int32_t * sel_out, void * ws, size_t ws_bytes, qsa_stream_t stream) {
+    DevDesc d; WsLayout w;
+    qsa_status s = shard_common(dd, items, batch, max_n_kv, blk_lo, blk_hi, ws, ws_bytes, d, w);
+    if (s != QSA_OK) return s;
+    if (n_shards <= 0 || !all_cand || !q || !state) return QSA_ERR_INVALID;
+    if (q_type != QSA_TYPE_BF16 && q_type != QSA_TYPE_F32) return QSA_ERR_INVALID;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    unsigned char * wsb = static_cast<unsigned char *>(ws);
+    cudaError_t e = launch_shard_select(d, st, items, n_shards, batch, all_cand, blk_lo, blk_hi, sel_out, reinterpret_cast<int *>(wsb + w.sel), reinterpret_cast<int *>(wsb + w.nsel),
+                                        reinterpret_cast<uint32_t *>(wsb + w.status));
+    if (e == cudaErrorInvalidValue) return QSA_ERR_UNSUPPORTED;       // too many candidates for one CTA
+    if (e != cudaSuccess) return QSA_ERR_CUDA;
+    qsa_layer_cache none{};
+    return launch_attend(d, w, batch, items, none, 0, q, q_type, nullptr, wsb, st, state);
+}
+
+qsa_status qsa_merge_states(const qsa_desc * dd, int32_t n_parts, int32_t batch, const float * states, float * out,
+                            qsa_stream_t stream) {
+    qsa_status s = qsa_desc_check(dd);
+    if (s != QSA_OK) return s;
+    if (n_parts <= 0 || batch <= 0 || !states || !out) return QSA_ERR_INVALID;
+    return cuda_status(launch_merge_states(make_dev(dd), reinterpret_cast<cudaStream_t>(stream), n_parts, batch,
+                                           states, out));
 }
 
 int32_t qsa_version(void) { return 100; }

@@ -125,6 +125,7 @@ __device__ void pool_block_warp(const DevDesc & d, const uint16_t * __restrict__
 __global__ void __launch_bounds__(256) append_rows_kernel(DevDesc d, qsa_layer_cache c, int pos0,
         const float * __restrict__ k, const float * __restrict__ v, const float * __restrict__ kidx) {
     const int t = blockIdx.x, row = pos0 + t;
+    c = shard_cache(d, c);
     const int kv_dim = d.n_head_kv * d.head_dim;
     if (k) write_kv_row(d, d.type_k, k + (size_t) t * kv_dim, (uint8_t *) c.k + (size_t) row * d.rb_k, kv_dim);
     if (v) write_kv_row(d, d.type_v, v + (size_t) t * kv_dim, (uint8_t *) c.v + (size_t) row * d.rb_v, kv_dim);
@@ -140,6 +141,10 @@ __global__ void __launch_bounds__(256) pool_blocks_kernel(DevDesc d, const uint1
     const int j = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (j >= n_blk) return;
     const int64_t b = blk0 + j;
+    if (d.shard_blk0 != 0) {               // a shard's local arrays, indexed by global row / block
+        idx = shard_row(idx, (int64_t) d.shard_blk0 * d.ratio, 0, (int64_t) MAX_IDX_DIM * 2);
+        pool = shard_row(pool, (int64_t) d.shard_blk0, 0, (int64_t) d.idx_dim * 2);
+    }
     pool_block_warp(d, idx + (size_t) b * d.ratio * MAX_IDX_DIM, b, pool + (size_t) b * d.idx_dim,
                     out_f32 ? out_f32 + (size_t) j * d.idx_dim : nullptr);
 }
@@ -156,12 +161,14 @@ __global__ void __launch_bounds__(APPEND_THREADS) append_decode_kernel(DevDesc d
     extern __shared__ __align__(16) unsigned char dyn_smem[];
     pdl_trigger();
     const int s = blockIdx.x;
-    const qsa_decode_item it = items[s];
+    qsa_decode_item it = items[s];
     const int row = it.n_past;
     if (row < 0 || row >= d.n_ctx) {
         if (threadIdx.x == 0) set_status(status, DEV_BAD_POS);
         return;
     }
+    if (row / d.ratio < d.shard_blk0 || row / d.ratio >= d.shard_blk1) return;   // another shard's cell
+    it.cache = shard_cache(d, it.cache);
     const int kv_dim = d.n_head_kv * d.head_dim;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nb = kv_dim / QK8_0;
     if (d.type_k == QSA_TYPE_Q8_0 && 2 * nb <= (int) (blockDim.x >> 5)) {

@@ -65,7 +65,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_kernel(
         const void * __restrict__ q, int q_type,
         const int * __restrict__ sel_ws, const int * __restrict__ nsel_ws, int tiles_per_cta, int max_chunks,
         float * __restrict__ part_o, float * __restrict__ part_ml, unsigned * __restrict__ counters,
-        float * __restrict__ out, uint32_t * __restrict__ status) {
+        float * __restrict__ out, uint32_t * __restrict__ status, float * __restrict__ state_out) {
     using Cfg = AttnCfg<KV_TYPE>;
     constexpr int NS = Cfg::NSTAGE, HB = Cfg::HB, RB = attn_row_bytes<KV_TYPE>();
     extern __shared__ __align__(128) unsigned char smem[];
@@ -95,6 +95,11 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_kernel(
         qpos = n_past0 + t;
         kbase = (const uint8_t *) cache0.k;
         vbase = (const uint8_t *) cache0.v;
+    }
+    if (d.shard_blk0 != 0) {                   // address of global cell 0 (only shard cells are read)
+        const int64_t row0 = (int64_t) d.shard_blk0 * d.ratio;
+        kbase = shard_row(kbase, row0, 0, d.rb_k);
+        vbase = shard_row(vbase, row0, 0, d.rb_v);
     }
     {   // Q of the CTA's query heads -> f16 (the reference converts Q to K's vec_dot type, F16)
         for (int i = tid; i < HROWS * HEAD_DIM / 8; i += ATT_THREADS) {
@@ -136,9 +141,15 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_kernel(
     const int n_tiles = (n_cells + CELLS_TILE - 1) / CELLS_TILE;
     const int n_chunks = (n_tiles + tiles_per_cta - 1) / tiles_per_cta;
     float * outq = out + (size_t) t * d.n_head * HEAD_DIM;
+    // sharded mode: the unnormalised state [M 16][L 16][O 16x256] of query t instead of the output
+    float * stq = state_out ? state_out + (size_t) t * (2 * HROWS + HROWS * HEAD_DIM) : nullptr;
     if (n_chunks == 0) {                       // nothing selected (or a bad position): zero output
-        if (chunk == 0)
-            for (int i = tid; i < d.n_head * HEAD_DIM; i += ATT_THREADS) outq[i] = 0.0f;
+        if (chunk == 0) {
+            if (stq)
+                for (int i = tid; i < 2 * HROWS + HROWS * HEAD_DIM; i += ATT_THREADS) stq[i] = i < HROWS ? -INFINITY : 0.0f;
+            else
+                for (int i = tid; i < d.n_head * HEAD_DIM; i += ATT_THREADS) outq[i] = 0.0f;
+        }
         return;
     }
     {   // whole clusters past the last chunk have nothing to merge (uniform within a cluster)
@@ -517,10 +528,15 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_kernel(
                 const float w = p < CL ? rw[p * HROWS + hr] : 0.0f;
                 acc.x += w * v[p].x; acc.y += w * v[p].y; acc.z += w * v[p].z; acc.w += w * v[p].w;
             }
-            if (n_cl == 1) write_out(e4, acc, rML[HROWS + hr]);
-            else reinterpret_cast<float4 *>(po)[e4] = acc;
+            if (n_cl == 1) {
+                if (stq) reinterpret_cast<float4 *>(stq + 2 * HROWS)[e4] = acc;
+                else write_out(e4, acc, rML[HROWS + hr]);
+            } else {
+                reinterpret_cast<float4 *>(po)[e4] = acc;
+            }
         }
     }
+    if (n_cl == 1 && stq && crank == 0 && tid < 2 * HROWS) stq[tid] = rML[tid];
     if (n_cl > 1) {
         if (crank == 0 && tid < 2 * HROWS)
             part_ml[((size_t) t * max_parts + cl_id) * 2 * HROWS + tid] = rML[tid];
@@ -545,7 +561,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_kernel(
     const float * pmb = part_ml + (size_t) t * max_parts * 2 * HROWS;
     float * gm = co;                                  // [n_cl][16] m -> weights (co is free now)
     float * gl = gm + n_cl * HROWS;                   // [n_cl][16] l
-    float * gL = gl + n_cl * HROWS;                   // [16] L
+    float * gL = gl + n_cl * HROWS;                   // [16] L, then [16] M
     for (int i = tid; i < n_cl * 2 * HROWS; i += ATT_THREADS) {     // every (m, l) loaded at once
         const int c = i / (2 * HROWS), k = i % (2 * HROWS);
         const float v = __ldcg(pmb + i);
@@ -563,6 +579,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_kernel(
             L += gl[c * HROWS + tid] * w;
         }
         gL[tid] = L;
+        gL[HROWS + tid] = M;
+        if (stq && crank == 0) { stq[tid] = M; stq[HROWS + tid] = L; }
     }
     __syncthreads();
     const float4 * po4 = reinterpret_cast<const float4 *>(pob);
@@ -585,7 +603,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_kernel(
             const float w = gm[c * HROWS + hr];
             acc.x += w * v.x; acc.y += w * v.y; acc.z += w * v.z; acc.w += w * v.w;
         }
-        write_out(e4, acc, gL[hr]);
+        if (stq) reinterpret_cast<float4 *>(stq + 2 * HROWS)[e4] = acc;
+        else write_out(e4, acc, gL[hr]);
     }
 }
 
@@ -605,7 +624,7 @@ int attn_state_rows() { return HROWS; }
 cudaError_t launch_attn(const DevDesc & d, dim3 grid, cudaStream_t st, const qsa_decode_item * items,
         qsa_layer_cache cache0, int n_past0, const void * q, int q_type, const int * sel_ws, const int * nsel_ws,
         int tiles_per_cta, int max_chunks, float * part_o, float * part_ml, unsigned * counters, float * out,
-        uint32_t * status) {
+        uint32_t * status, float * state_out) {
     // CTAs of consecutive chunks of one query form a cluster of up to 8
     const int CL = attn_cluster_size(max_chunks);
     grid.x = (unsigned) (((max_chunks + CL - 1) / CL) * CL);
@@ -627,11 +646,11 @@ cudaError_t launch_attn(const DevDesc & d, dim3 grid, cudaStream_t st, const qsa
     if (d.type_k == QSA_TYPE_Q8_0) {
         cfg.dynamicSmemBytes = attn_smem_bytes<QSA_TYPE_Q8_0>();
         return cudaLaunchKernelEx(&cfg, attn_kernel<QSA_TYPE_Q8_0>, d, items, cache0, n_past0, q, q_type, sel_ws,
-                                  nsel_ws, tiles_per_cta, max_chunks, part_o, part_ml, counters, out, status);
+                                  nsel_ws, tiles_per_cta, max_chunks, part_o, part_ml, counters, out, status, state_out);
     }
     cfg.dynamicSmemBytes = attn_smem_bytes<QSA_TYPE_F16>();
     return cudaLaunchKernelEx(&cfg, attn_kernel<QSA_TYPE_F16>, d, items, cache0, n_past0, q, q_type, sel_ws,
-                              nsel_ws, tiles_per_cta, max_chunks, part_o, part_ml, counters, out, status);
+                              nsel_ws, tiles_per_cta, max_chunks, part_o, part_ml, counters, out, status, state_out);
 }
 
 }  // namespace qsa

@@ -33,7 +33,30 @@ struct DevDesc {
     const float * k_norm_w; // may be null
     int64_t rb_k, rb_v;     // bytes per K/V cache row (all heads)
     int hb_k, hb_v;         // bytes of one head inside a row
+    // KV-sequence sharding: this device holds blocks [shard_blk0, shard_blk1) of every cache, in
+    // local arrays whose row 0 is cell shard_blk0 * ratio (pooled row 0 is block shard_blk0).
+    // Unsharded: [0, INT_MAX).
+    int shard_blk0, shard_blk1;
 };
+
+// Local address of global row `row` of a sharded cache array with `row_bytes` per row; rows
+// before the shard are never dereferenced (the callers stay inside [shard_blk0, shard_blk1)).
+template <typename T>
+__device__ __forceinline__ T * shard_row(T * base, int64_t row0, int64_t row, int64_t row_bytes) {
+    return reinterpret_cast<T *>(reinterpret_cast<uintptr_t>(base) + (uintptr_t) ((row - row0) * row_bytes));
+}
+
+// A shard's cache arrays re-based so that global rows index them (identity when unsharded).
+__device__ __forceinline__ qsa_layer_cache shard_cache(const DevDesc & d, qsa_layer_cache c) {
+    if (d.shard_blk0 != 0) {
+        const int64_t row0 = (int64_t) d.shard_blk0 * d.ratio;
+        c.k = shard_row(c.k, row0, 0, d.rb_k);
+        c.v = shard_row(c.v, row0, 0, d.rb_v);
+        c.idx = shard_row(c.idx, row0, 0, (int64_t) d.idx_dim * 2);
+        c.pool = shard_row(c.pool, (int64_t) d.shard_blk0, 0, (int64_t) d.idx_dim * 2);
+    }
+    return c;
+}
 
 // ------------------------------------------------------------------ small helpers
 __device__ __forceinline__ float f16_bits_to_f32(uint16_t u) { return __half2float(__ushort_as_half(u)); }
@@ -104,7 +127,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t * bar, uint32_t parit
     return false;
 }
 // Non-tensor bulk copy global -> this CTA's shared memory, completing on `bar`.
-// Both addresses 16-byte aligned, bytes a multiple of 16.  No multicast.
+// Both addresses 16-byte aligned, bytes a multiple of 16; the destination is this CTA only.
 __device__ __forceinline__ void bulk_g2s(void * dst, const void * src, uint32_t bytes, uint64_t * bar) {
     asm volatile("cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                  :: "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");

@@ -18,7 +18,7 @@ inline size_t append_decode_smem(const DevDesc & d) { return (size_t) d.ratio * 
 
 __global__ void score_select_kernel(DevDesc d, const qsa_decode_item * items, const uint16_t * pool0, int n_past0,
         const float * q_idx, int blocks_per_cta, float * scores_ws, int scores_stride, unsigned * counters,
-        int * sel_ws, int * nsel_ws, int * sel_out, uint32_t * status);
+        int * sel_ws, int * nsel_ws, int * sel_out, uint32_t * status, float * cand_scores);
 
 // Leading bytes of a decode workspace that must be zero before a call (status word + counters).
 size_t decode_workspace_zero_prefix(const qsa_desc * d, int32_t batch, int32_t max_n_kv);
@@ -27,8 +27,15 @@ size_t decode_workspace_zero_prefix(const qsa_desc * d, int32_t batch, int32_t m
 cudaError_t launch_attn(const DevDesc & d, dim3 grid, cudaStream_t st, const qsa_decode_item * items,
         qsa_layer_cache cache0, int n_past0, const void * q, int q_type, const int * sel_ws, const int * nsel_ws,
         int tiles_per_cta, int max_chunks, float * part_o, float * part_ml, unsigned * counters, float * out,
-        uint32_t * status);
+        uint32_t * status, float * state_out = nullptr);
 cudaError_t attn_set_attrs();
+
+// KV-sequence-sharded decode: global selection from all shards' candidates, and the log-sum-exp
+// merge of the shards' attention states (qsa_shard.cu).
+cudaError_t launch_shard_select(const DevDesc & d, cudaStream_t st, const qsa_decode_item * items, int n_shards,
+        int batch, const int * cand, int blo, int bhi, int * sel_out, int * sel_ws, int * nsel_ws, uint32_t * status);
+cudaError_t launch_merge_states(const DevDesc & d, cudaStream_t st, int n_parts, int batch, const float * states,
+        float * out);
 // CTAs per thread-block cluster of the attention launch (partials are per cluster).
 int attn_cluster_size(int max_chunks);
 // Rows (KV head x query head) of the attention state: a partial is rows x head_dim floats.

@@ -78,17 +78,21 @@ struct SelSmem {
 // Threshold search: histograms of 12 key bits ([30:19], then [18:7], then [6:0]) locate the bin
 // holding the cut and how many of its keys to keep; once that bin holds at most CAND_MAX keys
 // they are ranked directly (score, then lower block index).  Keys above the bin are kept.
+// Sharded mode (cand_scores != null): only blocks in [blo, bhi) compete, forced blocks are left
+// to the global merge, and each kept block's score is written beside it.
 __device__ void select_blocks(const DevDesc & d, int q, const float * __restrict__ sc, unsigned char * __restrict__ flag,
                               int * __restrict__ sel, int * __restrict__ nsel_out, int * __restrict__ sel_out,
-                              SelSmem & sm) {
+                              SelSmem & sm, int blo, int bhi, float * __restrict__ cand_scores) {
+    const bool shard = cand_scores != nullptr;
     const int tid = threadIdx.x;
     const int n_vis = (q + 1) / d.ratio;
     int f_lo, f_hi;
     forced_range(d, q, f_lo, f_hi);
     const int n_forced = f_hi >= f_lo ? f_hi - f_lo + 1 : 0;
     const int want = max(0, d.kb - n_forced);
-    const int n_cand = n_vis - max(0, min(f_hi, n_vis - 1) - f_lo + 1);
-    auto is_cand = [&](int b) { return b < n_vis && !(b >= f_lo && b <= f_hi); };
+    const int lo_c = max(blo, 0), hi_c = min(bhi, n_vis);          // candidate range
+    const int n_cand = max(0, hi_c - lo_c) - max(0, min(f_hi, hi_c - 1) - max(f_lo, lo_c) + 1);
+    auto is_cand = [&](int b) { return b >= lo_c && b < hi_c && !(b >= f_lo && b <= f_hi); };
     const bool take_all = n_cand <= want;
     uint32_t prefix = 0, pmask = 0;   // keys with (key & pmask) > prefix are kept
     int remaining = 0;                // keys with (key & pmask) == prefix to keep
@@ -193,9 +197,9 @@ compaction:
     // Compaction over [0, max(n_vis, f_hi+1)) in ascending order: each thread owns a contiguous run.
     // Without ranking (more than CAND_MAX equal keys) the bin's first `remaining` by index are kept,
     // which needs the number of such ties before each thread's run.
-    const int n_range = max(n_vis, f_hi + 1);
-    const int per = (n_range + blockDim.x - 1) / blockDim.x;
-    const int lo = tid * per, hi = min(n_range, lo + per);
+    const int r_lo = shard ? lo_c : 0, r_hi = shard ? max(lo_c, hi_c) : max(n_vis, f_hi + 1);
+    const int per = (r_hi - r_lo + blockDim.x - 1) / blockDim.x;
+    const int lo = r_lo + tid * per, hi = min(r_hi, lo + per);
     const bool tie_quota = !take_all && !ranked;
     int tie_base = 0;
     if (tie_quota) {
@@ -206,7 +210,7 @@ compaction:
         __syncthreads();
     }
     auto take = [&](int b, int & tie_i) -> bool {
-        if (b >= f_lo && b <= f_hi) return true;
+        if (b >= f_lo && b <= f_hi) return !shard;
         if (!is_cand(b)) return false;
         if (take_all) return true;
         const uint32_t km = __float_as_uint(sc[b]) & pmask;
@@ -232,6 +236,7 @@ compaction:
             if (pos < d.kb) {
                 sel[pos] = b;
                 if (sel_out) sel_out[pos] = b;
+                if (shard) cand_scores[pos] = sc[b];
             }
             pos++;
         }
@@ -242,14 +247,17 @@ compaction:
                 if (pos < d.kb) {
                     sel[pos] = b;
                     if (sel_out) sel_out[pos] = b;
+                    if (shard) cand_scores[pos] = sc[b];
                 }
                 pos++;
             }
         }
     }
     const int n = min(total, d.kb);
-    if (sel_out)
-        for (int i = n + tid; i < d.kb; i += blockDim.x) sel_out[i] = -1;
+    for (int i = n + tid; i < d.kb; i += blockDim.x) {
+        if (sel_out) sel_out[i] = -1;
+        if (shard) { sel[i] = -1; cand_scores[i] = 0.0f; }
+    }
     if (tid == 0) *nsel_out = n;
 }
 
@@ -260,7 +268,7 @@ __global__ void __launch_bounds__(SEL_THREADS) score_select_kernel(DevDesc d,
         const float * __restrict__ q_idx, int blocks_per_cta,
         float * __restrict__ scores_ws, int scores_stride, unsigned * __restrict__ counters,
         int * __restrict__ sel_ws, int * __restrict__ nsel_ws, int * __restrict__ sel_out,
-        uint32_t * __restrict__ status) {
+        uint32_t * __restrict__ status, float * __restrict__ cand_scores) {
     extern __shared__ __align__(16) unsigned char dyn_smem[];
     __shared__ SelSmem sm;
     __shared__ bool is_last;
@@ -268,6 +276,8 @@ __global__ void __launch_bounds__(SEL_THREADS) score_select_kernel(DevDesc d,
     const int t = blockIdx.y;
     const int q = items ? items[t].n_past : n_past0 + t;
     const uint16_t * pool = items ? items[t].cache.pool : pool0;
+    const int blo = d.shard_blk0, bhi = d.shard_blk1;          // [0, INT_MAX) unless sharded
+    if (blo != 0) pool = shard_row(pool, (int64_t) blo, 0, (int64_t) d.idx_dim * 2);   // address of block 0
     const bool bad = q < 0 || q >= d.n_ctx || (q + 1) / d.ratio > scores_stride;
     if (bad && threadIdx.x == 0 && blockIdx.x == 0) set_status(status, DEV_BAD_POS);
     const int n_vis = bad ? 0 : (q + 1) / d.ratio;
@@ -283,8 +293,8 @@ __global__ void __launch_bounds__(SEL_THREADS) score_select_kernel(DevDesc d,
                 qf[h][e] = h < d.idx_n_head
                     ? f16_bits_to_f32(f32_to_f16_bits(q_idx[((size_t) t * d.idx_n_head + h) * d.idx_dim + 8 * sub + e]))
                     : 0.0f;
-        const int b0 = blockIdx.x * blocks_per_cta;
-        const int b1 = min(n_vis, b0 + blocks_per_cta);
+        const int b0 = blo + blockIdx.x * blocks_per_cta;
+        const int b1 = min(min(n_vis, bhi), b0 + blocks_per_cta);
         pdl_wait();                              // the append of this step (pooled keys) is complete
         if (b0 < b1) score_range(d, pool, qf, b0, b1, sc);
     }
@@ -302,10 +312,10 @@ __global__ void __launch_bounds__(SEL_THREADS) score_select_kernel(DevDesc d,
     if (!is_last) return;
     float * ssc = reinterpret_cast<float *>(dyn_smem);
     unsigned char * flag = dyn_smem + (size_t) scores_stride * 4;
-    {   // the query's scores, 16 bytes per load (score rows are 16-byte aligned)
-        const int n4 = (n_vis + 3) / 4;
+    {   // the query's scores in [blo, n_vis), 16 bytes per load (score rows are 16-byte aligned)
+        const int i0 = max(blo, 0) / 4, n4 = (min(n_vis, bhi) + 3) / 4;
         #pragma unroll 4
-        for (int i = threadIdx.x; i < n4; i += blockDim.x)
+        for (int i = i0 + threadIdx.x; i < n4; i += blockDim.x)
             reinterpret_cast<float4 *>(ssc)[i] = __ldcg(reinterpret_cast<const float4 *>(sc) + i);
     }
     __syncthreads();
@@ -313,12 +323,14 @@ __global__ void __launch_bounds__(SEL_THREADS) score_select_kernel(DevDesc d,
         for (int i = threadIdx.x; i < d.kb; i += blockDim.x) {
             sel_ws[(size_t) t * d.kb + i] = -1;
             if (sel_out) sel_out[(size_t) t * d.kb + i] = -1;
+            if (cand_scores) cand_scores[(size_t) t * d.kb + i] = 0.0f;
         }
         if (threadIdx.x == 0) nsel_ws[t] = 0;
         return;
     }
     select_blocks(d, q, ssc, flag, sel_ws + (size_t) t * d.kb, nsel_ws + t,
-                  sel_out ? sel_out + (size_t) t * d.kb : nullptr, sm);
+                  sel_out ? sel_out + (size_t) t * d.kb : nullptr, sm, blo, bhi,
+                  cand_scores ? cand_scores + (size_t) t * d.kb : nullptr);
 }
 
 }  // namespace qsa

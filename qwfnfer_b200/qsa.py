@@ -33,13 +33,17 @@ def _stream(stream: torch.cuda.Stream | None) -> int:
 
 
 class QsaState:
-    """Per-sequence caches of `n_layers` QSA layers, reference layouts (include/qsa.h)."""
+    """Per-sequence caches of `n_layers` QSA layers, reference layouts (include/qsa.h).
 
-    def __init__(self, desc: QsaDesc, n_layers: int = 1, device: str | torch.device = "cuda", zero: bool = False):
+    blocks=(lo, hi): a shard's caches, holding blocks [lo, hi) only (row 0 = cell lo*ratio)."""
+
+    def __init__(self, desc: QsaDesc, n_layers: int = 1, device: str | torch.device = "cuda", zero: bool = False,
+                 blocks: tuple[int, int] | None = None):
         check(lib().qsa_desc_check(ctypes.byref(desc)), "qsa_desc_check")
         self.desc = desc
         self.device = torch.device(device)
-        n = desc.n_ctx
+        self.blocks = blocks if blocks is not None else (0, desc.n_ctx // desc.ratio)
+        n = (self.blocks[1] - self.blocks[0]) * desc.ratio
         alloc = torch.zeros if zero else torch.empty
         self.k = [alloc((n, row_bytes(desc, 0)), dtype=torch.uint8, device=self.device) for _ in range(n_layers)]
         self.v = [alloc((n, row_bytes(desc, 1)), dtype=torch.uint8, device=self.device) for _ in range(n_layers)]

@@ -1,0 +1,160 @@
+"""KV-sequence-sharded QSA decode: one process per GPU over torch.distributed.
+
+The reference decodes a sequence on one device (its engine keeps one KV cache per layer,
+src/qwfn_state.cpp:18-96).  For contexts whose caches do not fit one GPU, or decode faster spread
+over several, the cells of every layer are split into contiguous block ranges, one per rank, and
+one decode step of one layer becomes:
+
+  1. candidates (libqsa): the rank holding the new token's cell appends it (K, V, raw key, and the
+     pooled key of a block it completes); every rank scores its own visible blocks and keeps its
+     best KB blocks outside the forced window, with their scores;
+  2. one all-gather of the candidates ([2, batch, KB] int32 per rank: ids, then score bits);
+  3. attend (libqsa): the exact global selection, identical on every rank and to the unsharded
+     qsa_decode's (a block among the global best is among its owner's best), then attention over
+     the rank's part of it into an unnormalised state [M | L | O] per query;
+  4. one all-gather of the states;
+  5. merge (libqsa): log-sum-exp combination of the states in rank order.
+
+The two exchanges carry O(batch x KB) and O(batch x 16 x head_dim) words, independent of the
+context length; the cache reads stay local.  The backend computes steps 1, 3 and 5; the default is
+the library on this rank's GPU.  PyTorch provides memory, streams and the collectives only.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+import torch.distributed as dist
+
+from ._abi import QsaDesc, QsaLayerCache, TYPE_BF16, TYPE_F32, check, k_blocks, lib
+
+
+def shard_blocks(n_blocks: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous block range [lo, hi) of `rank`: an even split, the first n_blocks % world ranks
+    holding one block more."""
+    if world <= 0 or not 0 <= rank < world or n_blocks < world:
+        raise ValueError(f"cannot split {n_blocks} blocks over {world} ranks (rank {rank})")
+    base, extra = divmod(n_blocks, world)
+    lo = rank * base + min(rank, extra)
+    return lo, lo + base + (1 if rank < extra else 0)
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    if t is None:
+        return None
+    assert t.is_cuda and t.is_contiguous(), "device tensors must be contiguous CUDA tensors"
+    return t.data_ptr()
+
+
+class LibShardBackend:
+    """Steps 1, 3 and 5 on this rank's GPU through libqsa's sharded entry points."""
+
+    def __init__(self, desc: QsaDesc, device: str | torch.device = "cuda"):
+        check(lib().qsa_desc_check(ctypes.byref(desc)), "qsa_desc_check")
+        self.desc = desc
+        self.device = torch.device(device)
+        self.kb = k_blocks(desc)
+        self.state_floats = lib().qsa_shard_state_floats(ctypes.byref(desc))
+        self._ws: dict[int, torch.Tensor] = {}
+
+    def _stream(self) -> int:
+        return torch.cuda.current_stream(self.device).cuda_stream
+
+    def workspace(self, batch: int, max_n_kv: int) -> torch.Tensor:
+        size = lib().qsa_decode_workspace_size(ctypes.byref(self.desc), batch, max_n_kv)
+        if size == 0:
+            raise ValueError("invalid decode shape")
+        ws = self._ws.get(size)
+        if ws is None:
+            ws = torch.empty(size, dtype=torch.uint8, device=self.device)
+            check(lib().qsa_workspace_init(ws.data_ptr(), size, self._stream()), "qsa_workspace_init")
+            self._ws[size] = ws
+        return ws
+
+    def append(self, cache: QsaLayerCache, blocks: tuple[int, int], pos0: int, k, v, kidx) -> None:
+        n = (k if k is not None else kidx).shape[0]
+        check(lib().qsa_shard_append(ctypes.byref(self.desc), ctypes.byref(cache), blocks[0], blocks[1], pos0, n,
+                                     _ptr(k), _ptr(v), _ptr(kidx), self._stream()), "qsa_shard_append")
+
+    def candidates(self, items, batch: int, max_n_kv: int, blocks: tuple[int, int], q_idx,
+                   k_new=None, v_new=None, kidx_new=None, out: torch.Tensor | None = None) -> torch.Tensor:
+        """This rank's candidates, int32 [2, batch, KB]: block ids (-1 padded), then score bits."""
+        if out is None:
+            out = torch.empty((2, batch, self.kb), dtype=torch.int32, device=self.device)
+        ws = self.workspace(batch, max_n_kv)
+        check(lib().qsa_shard_candidates(ctypes.byref(self.desc), _ptr(items), batch, max_n_kv, blocks[0], blocks[1],
+                                         _ptr(q_idx), _ptr(k_new), _ptr(v_new), _ptr(kidx_new), _ptr(out),
+                                         ws.data_ptr(), ws.numel(), self._stream()), "qsa_shard_candidates")
+        return out
+
+    def attend(self, items, batch: int, max_n_kv: int, blocks: tuple[int, int], gathered: torch.Tensor, q,
+               sel_out: torch.Tensor | None = None, state: torch.Tensor | None = None) -> torch.Tensor:
+        """gathered: int32 [n_shards, 2, batch, KB], every rank's candidates in rank order."""
+        if state is None:
+            state = torch.empty((batch, self.state_floats), dtype=torch.float32, device=self.device)
+        q_type = TYPE_BF16 if q.dtype == torch.bfloat16 else TYPE_F32
+        ws = self.workspace(batch, max_n_kv)
+        check(lib().qsa_shard_attend(ctypes.byref(self.desc), _ptr(items), batch, max_n_kv, blocks[0], blocks[1],
+                                     gathered.shape[0], _ptr(gathered), _ptr(q), q_type, state.data_ptr(),
+                                     _ptr(sel_out), ws.data_ptr(), ws.numel(), self._stream()), "qsa_shard_attend")
+        return state
+
+    def merge(self, states: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """states: f32 [n_parts, batch, state_floats] -> f32 [batch, n_head, head_dim]."""
+        P, B = states.shape[0], states.shape[1]
+        d = self.desc
+        if out is None:
+            out = torch.empty((B, d.n_head, d.head_dim), dtype=torch.float32, device=self.device)
+        check(lib().qsa_merge_states(ctypes.byref(d), P, B, _ptr(states.contiguous()), out.data_ptr(), self._stream()),
+              "qsa_merge_states")
+        return out
+
+    def check(self, batch: int, max_n_kv: int) -> int:
+        ws = self.workspace(batch, max_n_kv)
+        return lib().qsa_check(ws.data_ptr(), ws.numel(), self._stream())
+
+
+class ShardedDecoder:
+    """The per-rank driver of the sharded decode step (module docstring).  `group` is a
+    torch.distributed process group (default: the world); world size 1 runs without collectives."""
+
+    def __init__(self, desc: QsaDesc, backend=None, group=None, rank: int | None = None,
+                 world: int | None = None):
+        self.desc = desc
+        self.group = group
+        dist_on = dist.is_available() and dist.is_initialized()
+        self.world = world if world is not None else (dist.get_world_size(group) if dist_on else 1)
+        self.rank = rank if rank is not None else (dist.get_rank(group) if dist_on else 0)
+        self.blocks = shard_blocks(desc.n_ctx // desc.ratio, self.world, self.rank)
+        self.backend = backend if backend is not None else LibShardBackend(desc)
+        self.kb = k_blocks(desc)
+
+    def _all_gather(self, t: torch.Tensor) -> torch.Tensor:
+        """[world, *t.shape], rank order."""
+        if self.world == 1:
+            return t.unsqueeze(0)
+        t = t.contiguous()
+        out = torch.empty((self.world * t.shape[0],) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+        dist.all_gather_into_tensor(out, t, group=self.group)
+        return out.view((self.world,) + tuple(t.shape))
+
+    def append(self, cache: QsaLayerCache, pos0: int, k, v, kidx) -> None:
+        """Append global rows [pos0, pos0+n): the rows inside this rank's cells are written."""
+        n = (k if k is not None else kidx).shape[0]
+        r = self.desc.ratio
+        lo, hi = max(pos0, self.blocks[0] * r), min(pos0 + n, self.blocks[1] * r)
+        if lo >= hi:
+            return
+        sl = slice(lo - pos0, hi - pos0)
+        self.backend.append(cache, self.blocks, lo, None if k is None else k[sl], None if v is None else v[sl],
+                            None if kidx is None else kidx[sl])
+
+    def step(self, items, batch: int, max_n_kv: int, q, q_idx, k_new=None, v_new=None, kidx_new=None,
+             sel_out: torch.Tensor | None = None) -> torch.Tensor:
+        """One decode step of one layer for `batch` queries (items: this rank's device item table,
+        global n_past, local caches).  Returns f32 [batch, n_head, head_dim] on every rank."""
+        cand = self.backend.candidates(items, batch, max_n_kv, self.blocks, q_idx, k_new, v_new, kidx_new)
+        gathered = self._all_gather(cand)
+        state = self.backend.attend(items, batch, max_n_kv, self.blocks, gathered, q, sel_out=sel_out)
+        states = self._all_gather(state)
+        return self.backend.merge(states)

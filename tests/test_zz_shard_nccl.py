@@ -1,0 +1,39 @@
+"""The sharded decode over real ranks: one process per GPU, NCCL all-gathers (2 GPUs or more).
+
+Runs tests/shard_nccl_worker.py under torch.distributed.run on min(4, visible GPUs) ranks and
+requires its SHARD_NCCL line to report ok (selections identical to the unsharded qsa_decode on
+every rank, outputs within the parity tolerance and identical across ranks, clean status).
+"""
+from __future__ import annotations
+
+import json
+import os
+import socket
+import subprocess
+import sys
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+TESTS = os.path.dirname(os.path.abspath(__file__))
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_sharded_decode_over_nccl():
+    n = min(4, torch.cuda.device_count())
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes", "1",
+           "--nproc-per-node", str(n), "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
+           os.path.join(TESTS, "shard_nccl_worker.py")]
+    r = subprocess.run(cmd, capture_output=True, text=True, env=dict(os.environ, NCCL_NVLS_ENABLE="0"))
+    lines = [l for l in r.stdout.splitlines() if l.startswith("SHARD_NCCL ")]
+    assert r.returncode == 0 and lines, r.stdout[-3000:] + r.stderr[-3000:]
+    res = json.loads(lines[-1][len("SHARD_NCCL "):])
+    assert res["ok"] and res["world"] == n, res
