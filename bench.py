@@ -324,6 +324,298 @@ def run_ours_config2(args, ws, rank, local):
     return res
 
 
+def _timed_replays(graph, n, before=None):
+    """Device time (us) of n replays of `graph`, each after `before()` (input load + L2 flush)."""
+    import torch
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+    for i in range(n):
+        if before:
+            before(i)
+        ev[i][0].record()
+        graph.replay()
+        ev[i][1].record()
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) * 1e3 for a, b in ev]
+
+
+def _clock_sampler(local):
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    return ClockSampler(vis.split(",")[local] if vis else str(local))
+
+
+def run_ours_config3(args, ws, rank, local):
+    """Batched decode of 64 sequences (lengths U[4096, 163840], seed 2), one layer; with N ranks
+    each GPU decodes its contiguous share of the sequences (data parallel, no collective)."""
+    import ctypes
+
+    import torch
+
+    from qwfnfer_b200._abi import TYPE_BF16, check, k_blocks, lib
+    from qwfnfer_b200.configs import CONFIGS, config3_lengths, fill_cache, token_inputs
+    from qwfnfer_b200.qsa import QsaNode, QsaState, _stream, decode_items
+
+    cfg = CONFIGS[3]
+    d = cfg.desc()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    lengths = config3_lengths()
+    if len(lengths) % ws:
+        raise SystemExit(f"config 3: {len(lengths)} sequences do not split over {ws} ranks")
+    per = len(lengths) // ws
+    mine = lengths[rank * per:(rank + 1) * per]
+    positions = [n - 1 for n in mine]                 # the decoded token is the sequence's last
+    node = QsaNode(d, dev)
+    states = []
+    for j, n in enumerate(positions):
+        st = QsaState(d, device=dev)
+        fill_cache(node, st, 0, n, cfg.seed * 1000 + rank * per + j)
+        states.append(st)
+    B, KB = len(positions), k_blocks(d)
+    max_n_kv = max(positions) + 1
+    items = decode_items([st.layer() for st in states], positions, device=dev)
+    S = 4
+    ins = [token_inputs(d, B, cfg.seed + 100 * s + rank) for s in range(S)]
+    sq, sqi, sk, sv, ski = (torch.empty_like(x) for x in ins[0])
+    out = torch.empty(B, d.n_head, d.head_dim, device=dev)
+    sel = torch.empty(B, KB, dtype=torch.int32, device=dev)
+    wsb = node.workspace("decode", B, max_n_kv)
+    L, D = lib(), ctypes.byref(d)
+
+    def load(s):
+        for dst, src in zip((sq, sqi, sk, sv, ski), ins[s % S]):
+            dst.copy_(src)
+
+    def step_api(stream_ptr):
+        check(L.qsa_decode(D, items.data_ptr(), B, max_n_kv, sq.data_ptr(), TYPE_BF16, sqi.data_ptr(), sk.data_ptr(),
+                           sv.data_ptr(), ski.data_ptr(), out.data_ptr(), sel.data_ptr(), wsb.data_ptr(), wsb.numel(),
+                           stream_ptr), "qsa_decode")
+
+    def attend_api(stream_ptr):
+        check(L.qsa_decode_attend(D, items.data_ptr(), B, max_n_kv, sq.data_ptr(), TYPE_BF16, out.data_ptr(),
+                                  wsb.data_ptr(), wsb.numel(), stream_ptr), "qsa_decode_attend")
+
+    for s in range(args.warmup):
+        load(s)
+        step_api(_stream(None))
+    torch.cuda.synchronize()
+    g_step, g_attn = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_step):
+        step_api(_stream(None))
+    with torch.cuda.graph(g_attn):
+        attend_api(_stream(None))
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def before(i):
+        load(i)
+        flush.zero_()
+
+    K = args.steps
+    clocks = _clock_sampler(local)
+    clocks.start()
+    _timed_replays(g_step, 20, before)
+    if ws > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    clocks.mark("t0")
+    step_us = _timed_replays(g_step, K, before)
+    if ws > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    clocks.mark("t1")
+    attn_us = _timed_replays(g_attn, K, before)
+    # e2e: the public call with this rank's inputs copied from pinned host memory and the outputs back
+    hins = [tuple(x.cpu().pin_memory() for x in t) for t in ins]
+    hout = torch.empty(B, d.n_head, d.head_dim).pin_memory()
+    stream = torch.cuda.current_stream()
+    e2e = []
+    for i in range(K):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for dst, src in zip((sq, sqi, sk, sv, ski), hins[i % S]):
+            dst.copy_(src, non_blocking=True)
+        step_api(stream.cuda_stream)
+        hout.copy_(out, non_blocking=True)
+        b.record()
+        e2e.append((a, b))
+    torch.cuda.synchronize()
+    e2e_us = [a.elapsed_time(b) * 1e3 for a, b in e2e]
+    clocks.stop()
+    check(node.check(wsb), "qsa_check")
+    h2d = sum(x.numel() * x.element_size() for x in ins[0])
+    d2h = out.numel() * out.element_size()
+    sel_h = sel.cpu().numpy()
+    cells = sum(attended_cells(sel_h[t], positions[t], d.ratio) for t in range(B))
+    attn_bytes = cells * 2 * 544 + sum(x.numel() * x.element_size() for x in (sq, out)) + B * KB * 4
+    attn_mean = statistics.mean(attn_us)
+    hbm, _, src = peaks()
+    achieved = attn_bytes / (attn_mean * 1e-6) / 1e9
+    step_bytes = attn_bytes + sum((p + 1) // d.ratio for p in positions) * 256
+    total_us = max_over_ranks(statistics.mean(step_us), ws)
+    e2e_max = max_over_ranks(statistics.mean(e2e_us), ws)
+    n_tok = B * ws
+    return {
+        "metric": "batched sparse-attn decode us/token, 64 seqs @4K-160K q8_0", "value": round(total_us / n_tok, 4),
+        "unit": "us/token", "n_gpus": ws, "steps": K, "warmup": args.warmup, "ms_per_step": round(total_us / 1e3, 6),
+        "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
+        "dtype": "q8_0 KV, bf16 Q, f16 MMA / f32 softmax", "data": "synthetic",
+        "config": {"workload": f"config3: one decode step of 64 sequences, lengths U[4096,163840] seed 2, q8_0, "
+                               f"top-64 + 128-token window; {per} sequences per GPU",
+                   "global_batch": len(lengths), "seq_len": max(lengths),
+                   "parallelism": f"data parallel x{ws}" if ws > 1 else "1 GPU",
+                   "l2": "flushed (256 MB write) before every timed step", "cuda_graph": True},
+        "roofline": {"bound": "hbm", "kernel": "attn_kernel<q8_0> (qsa_decode_attend), rank 0",
+                     "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
+                     "peak_source": f"{src} hbm_gbs (burst)", "traffic": None,
+                     "algorithmic_bytes_per_launch": attn_bytes, "launch_us": round(attn_mean, 3)},
+        "step_roofline": {"algorithmic_bytes": step_bytes,
+                          "achieved_gbs": round(step_bytes / (statistics.mean(step_us) * 1e-6) / 1e9, 1)},
+        "stages_us": {"step": round(statistics.mean(step_us), 3), "attend": round(attn_mean, 3)},
+        "e2e": {"value": round(e2e_max / n_tok, 4), "unit": "us/token", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": 3 * K,
+        "clocks": clocks.summary(),
+    }
+
+
+def run_ours_config5(args, ws, rank, local):
+    """One token through 12 sparse-attention layers at 1,048,576 tokens of context (top-128), the
+    KV sequence sharded over the ranks: per layer, shard-local candidates, an all-gather, the
+    global selection and local attention, an all-gather of the states, the merge."""
+    import numpy as np
+    import torch
+
+    from qwfnfer_b200._abi import k_blocks
+    from qwfnfer_b200.configs import CONFIGS, fill_cache, token_inputs
+    from qwfnfer_b200.qsa import QsaNode, QsaState, decode_items
+    from qwfnfer_b200.shard import ShardedDecoder
+
+    cfg = CONFIGS[5]
+    d = cfg.desc()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    NL, n_past = cfg.layers, cfg.n_past
+    dec = ShardedDecoder(d, rank=rank, world=ws)
+    node = QsaNode(d, dev)
+    st = QsaState(d, n_layers=NL, device=dev, blocks=dec.blocks)
+    for il in range(NL):                       # every rank draws the same stream, keeps its cells
+        fill_cache(node, st, il, n_past, cfg.seed * 1000 + il, append=dec.append)
+    items = [decode_items([st.layer(il)], [n_past], device=dev) for il in range(NL)]
+    KB = k_blocks(d)
+    S = 4
+    ins = [token_inputs(d, NL, cfg.seed + 100 * s) for s in range(S)]     # identical on every rank
+    slots = [torch.empty_like(x) for x in ins[0]]
+    sel = torch.empty(NL, KB, dtype=torch.int32, device=dev)
+
+    def load(s):
+        for dst, src in zip(slots, ins[s % S]):
+            dst.copy_(src)
+
+    outs = [None] * NL
+
+    def step():
+        q, qi, k, v, ki = slots
+        for il in range(NL):
+            outs[il] = dec.step(items[il], 1, n_past + 1, q[il:il + 1], qi[il:il + 1], k[il:il + 1], v[il:il + 1],
+                                ki[il:il + 1], sel_out=sel[il:il + 1])
+
+    for s in range(args.warmup):
+        load(s)
+        step()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, capture_error_mode="thread_local"):
+        step()
+    # the attention stage of layer 0 alone (the dominant kernel), on this rank's share
+    cand = dec.backend.candidates(items[0], 1, n_past + 1, dec.blocks, slots[1][:1])
+    gathered = dec._all_gather(cand)
+    torch.cuda.synchronize()
+    g_attn = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_attn):
+        dec.backend.attend(items[0], 1, n_past + 1, dec.blocks, gathered, slots[0][:1])
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def before(i):
+        load(i)
+        flush.zero_()
+
+    K = args.steps
+    clocks = _clock_sampler(local)
+    clocks.start()
+    _timed_replays(g, 10, before)
+    if ws > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    clocks.mark("t0")
+    step_us = _timed_replays(g, K, before)
+    if ws > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    clocks.mark("t1")
+    attn_us = _timed_replays(g_attn, K, lambda i: flush.zero_())
+    # e2e: the public ShardedDecoder.step per layer, inputs from pinned host memory, outputs back
+    hins = [tuple(x.cpu().pin_memory() for x in t) for t in ins]
+    hout = torch.empty(NL, d.n_head, d.head_dim).pin_memory()
+    e2e = []
+    for i in range(min(K, 20)):
+        flush.zero_()
+        if ws > 1:
+            torch.distributed.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for dst, src in zip(slots, hins[i % S]):
+            dst.copy_(src, non_blocking=True)
+        step()
+        for il in range(NL):
+            hout[il:il + 1].copy_(outs[il], non_blocking=True)
+        b.record()
+        e2e.append((a, b))
+    torch.cuda.synchronize()
+    e2e_us = [a.elapsed_time(b) * 1e3 for a, b in e2e]
+    clocks.stop()
+    if dec.backend.check(1, n_past + 1) != 0:
+        raise SystemExit("device status error")
+    sel_h = sel.cpu().numpy()
+    lo, hi = dec.blocks
+    local_cells = sum(attended_cells([b for b in sel_h[il] if lo <= b < hi], n_past, d.ratio) for il in range(NL))
+    scored = max(0, min(hi, (n_past + 1) // d.ratio) - lo)
+    sf = 16 * (2 + d.head_dim) * 4
+    step_bytes = local_cells * 2 * 544 + NL * (scored * 256 + 2 * 544 + 256 + (ws + 1) * sf)
+    attn_cells0 = attended_cells([b for b in sel_h[0] if lo <= b < hi], n_past, d.ratio)
+    attn_bytes = attn_cells0 * 2 * 544 + 16 * 256 * 2 + sf
+    attn_mean = statistics.mean(attn_us)
+    hbm, _, src = peaks()
+    achieved = attn_bytes / (attn_mean * 1e-6) / 1e9
+    total_us = max_over_ranks(statistics.mean(step_us), ws)
+    e2e_max = max_over_ranks(statistics.mean(e2e_us), ws)
+    res = {
+        "metric": "sparse-attn decode us/layer @1M q8_0, 12 layers, KV-sequence-sharded",
+        "value": round(total_us / NL, 3), "unit": "us/layer-token", "n_gpus": ws, "steps": K,
+        "warmup": args.warmup, "ms_per_step": round(total_us / 1e3, 6), "higher_is_better": False,
+        "scaling": "strong", "vs_baseline": None, "dtype": "q8_0 KV, bf16 Q, f16 MMA / f32 softmax",
+        "data": "synthetic",
+        "config": {"workload": "config5: decode 1 token through 12 layers, ctx 1048576, q8_0, top-128 of 16384 "
+                               "blocks + 128-token window (131 blocks)",
+                   "global_batch": 1, "seq_len": n_past + 1, "layers": NL,
+                   "parallelism": f"KV-sequence-sharded x{ws} (NCCL all-gathers)" if ws > 1 else "1 GPU",
+                   "blocks_per_gpu": hi - lo,
+                   "l2": "flushed (256 MB write) before every timed step", "cuda_graph": True},
+        "roofline": {"bound": "hbm", "kernel": "attn_kernel<q8_0> (qsa_shard_attend), layer 0, rank 0",
+                     "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
+                     "peak_source": f"{src} hbm_gbs (burst)", "traffic": None,
+                     "algorithmic_bytes_per_launch": attn_bytes, "launch_us": round(attn_mean, 3)},
+        "step_roofline": {"algorithmic_bytes_per_gpu": step_bytes,
+                          "achieved_gbs": round(step_bytes / (statistics.mean(step_us) * 1e-6) / 1e9, 1)},
+        "e2e": {"value": round(e2e_max / NL, 3), "unit": "us/layer-token",
+                "h2d_bytes_per_step": sum(x.numel() * x.element_size() for x in ins[0]),
+                "d2h_bytes_per_step": NL * d.n_head * d.head_dim * 4},
+        "gpu_launches": 5 * NL * K,          # per layer: append, select, global select, attention, merge
+        "clocks": clocks.summary(),
+    }
+    del g, g_attn                               # graphs holding NCCL work go before the process group
+    return res
+
+
 def run_reference_config2(args):
     """The reference's CPU algorithm (oracle port, ggml mode, all host cores) on config 2."""
     import numpy as np
@@ -397,6 +689,9 @@ def main():
         rank = int(os.environ.get("RANK", "0"))
         if rank != 0:
             return
+        if args.config != 2:
+            print(json.dumps({"impl": "reference", "unavailable": f"the CPU reference arm times config 2 only"}))
+            return
         res = run_reference_config2(args)
         print(json.dumps(res), flush=True)
         return
@@ -404,8 +699,10 @@ def main():
     ws, rank, local = dist_setup("nccl")
     if args.config == 2:
         res = run_ours_config2(args, ws, rank, local)
+    elif args.config == 3:
+        res = run_ours_config3(args, ws, rank, local)
     else:
-        raise SystemExit(f"--config {args.config}: not wired into bench.py yet")
+        res = run_ours_config5(args, ws, rank, local)
     if rank == 0:
         print(json.dumps(res), flush=True)
     if ws > 1:

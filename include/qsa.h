@@ -175,8 +175,8 @@ qsa_status qsa_decode_attend(const qsa_desc * d, const qsa_decode_item * items, 
  * For callers that cannot allocate device memory -- an operator run inside another framework's
  * planned graph sees only its input and output tensors, and a serving loop under a fixed memory
  * budget must not call cudaMalloc on the token path -- the scratch lives in a fixed device array
- * of 4 MiB inside the library (held on every GPU that loads it, until exit).  Arguments and
- * results are those of qsa_decode; a call whose qsa_decode_workspace_size() exceeds 4 MiB returns
+ * of 8 MiB inside the library (held on every GPU that loads it, until exit).  Arguments and
+ * results are those of qsa_decode; a call whose qsa_decode_workspace_size() exceeds 8 MiB returns
  * QSA_ERR_WORKSPACE.  The first call on a device looks up the array's device address and zeroes
  * it (synchronously): make that first call before any stream capture.  Every call zeroes the
  * array's status word and counters and otherwise reuses the last call's contents, so calls that

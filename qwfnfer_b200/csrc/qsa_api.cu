@@ -9,9 +9,7 @@
 namespace qsa {
 namespace {
 
-constexpr int TARGET_ATTN_CTAS = 148;   // one resident attention CTA (8 warps, both KV heads) per SM
-
-// Tiles (64 cells) per attention CTA; QSA_TILES_PER_CTA overrides the heuristic (tuning).
+// Tiles per attention CTA; QSA_TILES_PER_CTA overrides the heuristic (tuning).
 int tiles_override() {
     static int v = [] { const char * e = getenv("QSA_TILES_PER_CTA"); return e ? atoi(e) : 0; }();
     return v;
@@ -50,7 +48,7 @@ DevDesc make_dev(const qsa_desc * d) {
 }
 
 struct WsLayout {
-    size_t status, cnt_sel, cnt_att, scores, sel, nsel, part_o, part_ml, total;
+    size_t status, cnt_sel, scores, sel, nsel, part_o, part_ml, total;
     int scores_stride, max_chunks, tiles_per_cta;
 };
 
@@ -59,17 +57,15 @@ size_t align256(size_t x) { return (x + 255) & ~(size_t) 255; }
 WsLayout ws_layout(const DevDesc & d, int n_q, int max_n_kv) {
     WsLayout w;
     w.scores_stride = std::max(4, ceil_div(ceil_div(max_n_kv, d.ratio), 4) * 4);   // 16-byte rows
-    const int max_tiles = std::max(1, ceil_div((int64_t) d.kb * d.ratio, CELLS_TILE));
+    const int max_tiles = std::max(1, ceil_div((int64_t) d.kb * d.ratio, attn_tile_cells()));
     // Chunks (CTAs) per query: one tile each while every tile of the batch fits one wave of
-    // attention CTAs (latency); otherwise as many chunks as one wave gives each query, rounded
-    // down to whole 8-CTA clusters, so that no CTA of the wave idles.
+    // attention CTAs (latency); otherwise as many chunks as one wave gives each query.
+    const int wave = attn_resident_ctas(d.type_k);
     int tpc;
-    if ((int64_t) n_q * max_tiles <= TARGET_ATTN_CTAS) {
+    if ((int64_t) n_q * max_tiles <= wave) {
         tpc = 1;
     } else {
-        int nch = std::max(1, TARGET_ATTN_CTAS / n_q);
-        if (nch > 8) nch -= nch % 8;
-        nch = std::min(nch, max_tiles);
+        const int nch = std::min(std::max(1, wave / n_q), max_tiles);
         tpc = ceil_div(max_tiles, nch);
     }
     if (tiles_override() > 0) tpc = tiles_override();
@@ -79,13 +75,10 @@ WsLayout ws_layout(const DevDesc & d, int n_q, int max_n_kv) {
     size_t o = 0;
     w.status  = o; o = align256(o + 16);
     w.cnt_sel = o; o = align256(o + (size_t) n_q * 4);
-    w.cnt_att = o; o = align256(o + (size_t) n_q * 4);
     w.scores  = o; o = align256(o + (size_t) n_q * w.scores_stride * 4);
     w.sel     = o; o = align256(o + (size_t) n_q * d.kb * 4);
     w.nsel    = o; o = align256(o + (size_t) n_q * 4);
-    const int CL = attn_cluster_size(w.max_chunks);
-    const int max_parts = (w.max_chunks + CL - 1) / CL;          // one partial per cluster
-    const size_t parts = max_parts > 1 ? (size_t) n_q * max_parts : 0;
+    const size_t parts = w.max_chunks > 1 ? (size_t) n_q * w.max_chunks : 0;   // one partial per CTA
     w.part_o  = o; o = align256(o + parts * attn_state_rows() * HEAD_DIM * 4);
     w.part_ml = o; o = align256(o + parts * 2 * attn_state_rows() * 4);
     w.total = o;
@@ -136,16 +129,15 @@ qsa_status launch_select(const DevDesc & d, const WsLayout & w, int n_q, const q
         reinterpret_cast<int *>(ws + w.sel), reinterpret_cast<int *>(ws + w.nsel), sel_out, status, cand_scores));
 }
 
-// Attention over the selection held in the workspace.
+// Attention over the selection held in the workspace (and the merge of split queries).
 qsa_status launch_attend(const DevDesc & d, const WsLayout & w, int n_q, const qsa_decode_item * items,
                          qsa_layer_cache cache0, int n_past0, const void * q, int q_type, float * out,
                          unsigned char * ws, cudaStream_t st, float * state_out = nullptr) {
-    const dim3 grid(w.max_chunks, d.n_head_kv, n_q);
-    return cuda_status(launch_attn(d, grid, st, items, cache0, n_past0, q, q_type,
+    return cuda_status(launch_attn(d, st, n_q, items, cache0, n_past0, q, q_type,
                                    reinterpret_cast<const int *>(ws + w.sel), reinterpret_cast<const int *>(ws + w.nsel),
                                    w.tiles_per_cta, w.max_chunks, reinterpret_cast<float *>(ws + w.part_o),
-                                   reinterpret_cast<float *>(ws + w.part_ml), reinterpret_cast<unsigned *>(ws + w.cnt_att),
-                                   out, reinterpret_cast<uint32_t *>(ws + w.status), state_out));
+                                   reinterpret_cast<float *>(ws + w.part_ml), out,
+                                   reinterpret_cast<uint32_t *>(ws + w.status), state_out));
 }
 
 }  // namespace

@@ -3,50 +3,56 @@
 // Reference: ggml_flash_attn_ext over the gathered cells with the cell mask, precision F32,
 // scale 1/sqrt(head_dim), GQA (src/qwfn_graph.cpp:497-502, 530-541; prefill :362-403).
 //
-// Work item = (query t, chunk of 64-cell tiles), both KV heads in one CTA of 8 warps.  The
-// selected blocks of a query, ascending, expand to a cell list (block b -> cells b*r ..
-// b*r+r-1); a tile is 64 consecutive entries.
+// Work item = (query t, chunk of 32-cell tiles), both KV heads in one CTA: 4 consumer warps and
+// one producer warp, two CTAs per SM.  The selected blocks of a query, ascending, expand to a cell
+// list (block b -> cells b*r .. b*r+r-1); a tile is 32 consecutive entries.
 //   - the rows of one block are contiguous in the cache (row = both heads, 544 B in q8_0), so a
 //     tile arrives as one bulk-async copy per block-run of valid rows (cells <= the query
 //     position) for K and for V, into a ring of shared-memory stages completed by mbarrier
 //     transaction counts; rows past the query or past the list are not fetched, they are masked
 //     in registers (their scores -inf, their V scales / f16 values zero);
-//   - warps 0-3 take KV head 0, warps 4-7 KV head 1, 16 cells each; the 8 query heads of a KV
+//   - the producer warp issues the copies of a stage once the consumers released it; consumer
+//     warps 0-1 take KV head 0, warps 2-3 KV head 1, 16 cells each; the 8 query heads of a KV
 //     head are the N=8 dimension of mma.m16n8k16: S^T = K Q^T (cells x heads), O^T += V^T P;
 //   - q8_0 is dequantised in registers: int8 bytes become exact f16 integers; the K scale
 //     multiplies the f32 partial dot of each 32-dim group, the V scale multiplies P;
-//   - online softmax in the exp2 domain with warp shuffles; warps merge in shared memory; the
-//     CTAs of a thread-block cluster (consecutive chunks) merge through distributed shared
-//     memory; clusters merge through global memory in the last one to arrive (arrival counter
-//     with acquire/release, no waiting).
-#include <cooperative_groups.h>
-
+//   - online softmax in the exp2 domain with warp shuffles; the two warps of a KV head merge in
+//     shared memory; a query split over several CTAs leaves one unnormalised partial per CTA in
+//     the workspace, merged by attn_merge_kernel (launched programmatically behind the
+//     attention grid, it waits for it with griddepcontrol.wait).
 #include "qsa_kernels.cuh"
-
-namespace cg = cooperative_groups;
 
 namespace qsa {
 
-constexpr int ATT_THREADS = 256;
-constexpr int ATT_WARPS   = 8;
+constexpr int ATT_CELLS   = 32;        // cells per tile (one pipeline stage)
+constexpr int ATT_CWARPS  = 4;         // consumer warps: (KV head, 16-cell half of the tile)
+constexpr int ATT_THREADS = 32 * (ATT_CWARPS + 1);   // + the producer warp
 constexpr int HROWS       = 16;        // 2 KV heads x 8 query heads: rows of the CTA state
+constexpr int MERGE_THREADS = 256;     // attn_merge_kernel: threads per CTA
 
 template <int KV_TYPE> struct AttnCfg;
 template <> struct AttnCfg<QSA_TYPE_Q8_0> {
-    static constexpr int HB     = 272;   // one head of a q8_0 row: 8 blocks x 34 B
-    static constexpr int NSTAGE = 3;
+    static constexpr int HB       = 272;   // one head of a q8_0 row: 8 blocks x 34 B
+    static constexpr int NSTAGE   = 2;     // 2 x 34.8 KB stages: two CTAs fit one SM's 228 KB
+    static constexpr int MIN_CTAS = 2;     // CTAs per SM
 };
 template <> struct AttnCfg<QSA_TYPE_F16> {
-    static constexpr int HB     = 512;
-    static constexpr int NSTAGE = 1;
+    static constexpr int HB       = 512;
+    static constexpr int NSTAGE   = 2;
+    static constexpr int MIN_CTAS = 1;
 };
 
 // shared-memory row = the KV heads of the CTA (all heads of a row: n_head_kv <= 2)
 template <int KV_TYPE> constexpr int attn_row_bytes() { return 2 * AttnCfg<KV_TYPE>::HB; }
-template <int KV_TYPE> constexpr int attn_stage_bytes() { return 2 * CELLS_TILE * attn_row_bytes<KV_TYPE>(); }
+template <int KV_TYPE> constexpr int attn_stage_bytes() { return 2 * ATT_CELLS * attn_row_bytes<KV_TYPE>(); }
 template <int KV_TYPE> constexpr int attn_smem_bytes() {
-    return AttnCfg<KV_TYPE>::NSTAGE * attn_stage_bytes<KV_TYPE>() + MAX_KB * 4 + HROWS * HEAD_DIM * 2 + 64;
+    return AttnCfg<KV_TYPE>::NSTAGE * attn_stage_bytes<KV_TYPE>() + MAX_KB * 4 + HROWS * HEAD_DIM * 2;
 }
+static_assert(AttnCfg<QSA_TYPE_Q8_0>::MIN_CTAS * (attn_smem_bytes<QSA_TYPE_Q8_0>() + 2048) <= 228 * 1024,
+              "q8_0 attention CTAs per SM");
+// the post-loop merge scratch (per-warp O, m, l) lives in the stage memory
+static_assert(ATT_CWARPS * 8 * HEAD_DIM * 4 + 2 * ATT_CWARPS * 8 * 4 + 2 * ATT_CWARPS * 8 * 4 <=
+              AttnCfg<QSA_TYPE_Q8_0>::NSTAGE * 2 * ATT_CELLS * 2 * AttnCfg<QSA_TYPE_Q8_0>::HB, "merge scratch");
 
 __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&a)[4], const void * p) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
@@ -59,27 +65,35 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 // Cell of list entry `idx` of a query (cells of the selected blocks, in order).
 __device__ __forceinline__ int list_cell(const int * sel, int r, int idx) { return sel[idx / r] * r + idx % r; }
 
+// Tiles and chunks of a query with `nsel` selected blocks (the same in both kernels).
+__device__ __forceinline__ int attn_n_chunks(const DevDesc & d, int nsel, int tiles_per_cta) {
+    const int n_tiles = (nsel * d.ratio + ATT_CELLS - 1) / ATT_CELLS;
+    return (n_tiles + tiles_per_cta - 1) / tiles_per_cta;
+}
+
 template <int KV_TYPE>
-__global__ void __launch_bounds__(ATT_THREADS, 1) attn_kernel(
+__global__ void __launch_bounds__(ATT_THREADS, AttnCfg<KV_TYPE>::MIN_CTAS) attn_kernel(
         DevDesc d, const qsa_decode_item * __restrict__ items, qsa_layer_cache cache0, int n_past0,
         const void * __restrict__ q, int q_type,
         const int * __restrict__ sel_ws, const int * __restrict__ nsel_ws, int tiles_per_cta, int max_chunks,
-        float * __restrict__ part_o, float * __restrict__ part_ml, unsigned * __restrict__ counters,
+        float * __restrict__ part_o, float * __restrict__ part_ml,
         float * __restrict__ out, uint32_t * __restrict__ status, float * __restrict__ state_out) {
     using Cfg = AttnCfg<KV_TYPE>;
     constexpr int NS = Cfg::NSTAGE, HB = Cfg::HB, RB = attn_row_bytes<KV_TYPE>();
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ uint64_t full_bar[NS];
     __shared__ uint64_t empty_bar[NS];
-    __shared__ unsigned long long vmask[NS];
-    __shared__ bool is_last;
+    __shared__ uint32_t vmask[NS];
+    __shared__ int abort_wait;
 
+    pdl_trigger();                             // the merge kernel may start; it waits for this grid
     const int t = blockIdx.y, chunk = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int r8 = lane >> 2, j4 = lane & 3;
-    const int hs = warp >> 2;                 // KV head of this warp
-    const int cw = warp & 3;                  // 16-cell slice of the tile
-    const bool head_live = hs < d.n_head_kv;
+    const int hs = (warp >> 1) & 1;           // KV head of a consumer warp
+    const int cw = warp & 1;                  // 16-cell half of the tile
+    const bool producer = warp == ATT_CWARPS;
+    const bool head_live = !producer && hs < d.n_head_kv;
     int * sel = reinterpret_cast<int *>(smem + NS * attn_stage_bytes<KV_TYPE>());
     __half * qs = reinterpret_cast<__half *>(smem + NS * attn_stage_bytes<KV_TYPE>() + MAX_KB * 4);
 
@@ -138,9 +152,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_kernel(
     const int r = d.ratio;
     const int RBr = (int) d.rb_k;                        // cache row bytes: the run copies' row pitch
     const int n_cells = nsel * r;
-    const int n_tiles = (n_cells + CELLS_TILE - 1) / CELLS_TILE;
-    const int n_chunks = (n_tiles + tiles_per_cta - 1) / tiles_per_cta;
-    float * outq = out + (size_t) t * d.n_head * HEAD_DIM;
+    const int n_tiles = (n_cells + ATT_CELLS - 1) / ATT_CELLS;
+    const int n_chunks = attn_n_chunks(d, nsel, tiles_per_cta);
+    float * outq = out ? out + (size_t) t * d.n_head * HEAD_DIM : nullptr;
     // sharded mode: the unnormalised state [M 16][L 16][O 16x256] of query t instead of the output
     float * stq = state_out ? state_out + (size_t) t * (2 * HROWS + HROWS * HEAD_DIM) : nullptr;
     if (n_chunks == 0) {                       // nothing selected (or a bad position): zero output
@@ -152,29 +166,27 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_kernel(
         }
         return;
     }
-    {   // whole clusters past the last chunk have nothing to merge (uniform within a cluster)
-        const int CL = (int) cg::this_cluster().num_blocks();
-        if ((chunk / CL) * CL >= n_chunks) return;
-    }
-    if ((smem_u32(smem) & 15u) != 0) {        // bulk copies need 16-byte aligned destinations;
-        if (tid == 0) set_status(status, DEV_BAD_SEL);   // the same in every CTA, so every CTA of
-        return;                                           // a cluster leaves before any cluster barrier
+    if (chunk >= n_chunks) return;             // the grid covers the longest query of the batch
+    if ((smem_u32(smem) & 15u) != 0) {        // bulk copies need 16-byte aligned destinations
+        if (tid == 0) set_status(status, DEV_BAD_SEL);
+        return;
     }
     const int tile0 = chunk * tiles_per_cta;
-    // chunks past the last tile (inside a partly used cluster) contribute an empty state
-    const int n_local = chunk < n_chunks ? min(tiles_per_cta, n_tiles - tile0) : 0;
+    const int n_local = min(tiles_per_cta, n_tiles - tile0);
     if (tid == 0) {
         for (int s = 0; s < NS; s++) {
             mbar_init(&full_bar[s], 1);
-            mbar_init(&empty_bar[s], ATT_WARPS);
+            mbar_init(&empty_bar[s], ATT_CWARPS);
         }
+        abort_wait = 0;
         fence_mbar_init();
     }
     __syncthreads();                                  // staged Q, sel and the barriers are visible
     // Q fragments (mma B operand) of each KV head, packed in lane order into shared memory (over
     // the staged Q, which only these two builders read): head n = r8 of the 8-head tile.
     uint32_t qf[16][2];
-    if (warp == 0 || warp == 4) {
+    const bool qbuilder = warp == 0 || warp == 2;
+    if (qbuilder) {
         const __half * qrow = qs + (hs * 8 + r8) * HEAD_DIM;
         auto pk2 = [&](int d0, int d1) -> uint32_t {
             __half2 h = __halves2half2(qrow[d0], qrow[d1]);
@@ -201,68 +213,79 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_kernel(
     }
     __syncthreads();
     uint2 * qfrag = reinterpret_cast<uint2 *>(qs);       // [2 heads][16 k-steps][32 lanes]
-    if (warp == 0 || warp == 4) {
+    if (qbuilder) {
         #pragma unroll
         for (int k = 0; k < 16; k++) qfrag[(hs * 16 + k) * 32 + lane] = make_uint2(qf[k][0], qf[k][1]);
     }
     __syncthreads();
 
     auto stage_k = [&](int s) { return smem + s * attn_stage_bytes<KV_TYPE>(); };
-    auto stage_v = [&](int s) { return smem + s * attn_stage_bytes<KV_TYPE>() + CELLS_TILE * RB; };  // RB >= row bytes
-    // Warp 0 issues local tile i into stage i % NS: one copy per block-run of valid rows, and the
-    // tile's 64-bit row-validity mask (written before the release of the arrive).
-    auto issue = [&](int i) {
-        const int s = i % NS;
-        const int e_lo = (tile0 + i) * CELLS_TILE;
-        const int e_hi = min(e_lo + CELLS_TILE, n_cells);
-        const int j_lo = e_lo / r, j_hi = (e_hi - 1) / r;
-        // per run j: entries [max(e_lo, j r), min(e_hi, (j+1) r)), valid while the cell <= qpos
-        uint32_t bytes = 0;
-        for (int j = j_lo + lane; j <= j_hi; j += 32) {
-            const int a = max(e_lo, j * r), b = min(e_hi, (j + 1) * r);
-            const int cs = sel[j] * r + (a - j * r);
-            const int nv = max(0, min(b - a, qpos - cs + 1));
-            bytes += (uint32_t) nv * RBr * 2;
-        }
-        #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) bytes += __shfl_xor_sync(0xffffffffu, bytes, off);
-        const int ea = e_lo + lane, eb = ea + 32;
-        const unsigned lo = __ballot_sync(0xffffffffu, ea < n_cells && list_cell(sel, r, ea) <= qpos);
-        const unsigned hi = __ballot_sync(0xffffffffu, eb < n_cells && list_cell(sel, r, eb) <= qpos);
-        if (lane == 0) {
-            vmask[s] = ((unsigned long long) hi << 32) | lo;
-            mbar_arrive_expect_tx(&full_bar[s], bytes);
-        }
-        __syncwarp();
-        for (int j = j_lo + lane; j <= j_hi; j += 32) {
-            const int a = max(e_lo, j * r), b = min(e_hi, (j + 1) * r);
-            const int cs = sel[j] * r + (a - j * r);
-            const int nv = max(0, min(b - a, qpos - cs + 1));
-            if (nv > 0) {
-                bulk_g2s(stage_k(s) + (a - e_lo) * RBr, kbase + (size_t) cs * d.rb_k, (uint32_t) nv * RBr, &full_bar[s]);
-                bulk_g2s(stage_v(s) + (a - e_lo) * RBr, vbase + (size_t) cs * d.rb_v, (uint32_t) nv * RBr, &full_bar[s]);
-            }
-        }
+    auto stage_v = [&](int s) { return smem + s * attn_stage_bytes<KV_TYPE>() + ATT_CELLS * RB; };  // RB >= row bytes
+    // A bounded wait; after one wait of the CTA ran out, the others return at once (the status
+    // word already says QSA_ERR_TIMEOUT; the results of this call are not used).
+    auto wait_bar = [&](uint64_t * bar, uint32_t parity) -> bool {
+        if (*reinterpret_cast<volatile int *>(&abort_wait)) return false;
+        if (mbar_wait_bounded(bar, parity, status)) return true;
+        *reinterpret_cast<volatile int *>(&abort_wait) = 1;
+        return false;
     };
-    if (warp == 0)
-        for (int i = 0; i < min(NS, n_local); i++) issue(i);
 
     float o[16][4];
     #pragma unroll
     for (int i = 0; i < 16; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
-    const int rA = 16 * cw + r8, rB = rA + 8;           // this thread's S^T rows (cells of the tile)
-    const int c0 = 16 * cw + 2 * j4;                     // this thread's V^T columns: c0+{0,1,8,9}
-    const int hoff = hs * HB;                            // byte offset of this warp's head in a row
-    const int rb = (int) d.rb_k;                         // row bytes (= smem row stride), K and V alike
-    const uint2 * myq = qfrag + hs * 16 * 32 + lane;
 
-    for (int i = 0; i < n_local; i++) {
-        const int s = i % NS;
-        const uint32_t ph = (uint32_t) ((i / NS) & 1);
-        mbar_wait_bounded(&full_bar[s], ph, status);
-        const unsigned long long vm = vmask[s];
-        const bool okA = (vm >> rA) & 1ull, okB = (vm >> rB) & 1ull;
+    if (producer) {
+        // Tile i goes to stage i % NS: one copy per block-run of valid rows (cells <= the query
+        // position) for K and V, and the tile's 32-bit row-validity mask (written before the
+        // release of the arrive).  Lane = tile entry.
+        for (int i = 0; i < n_local; i++) {
+            const int s = i % NS;
+            if (i >= NS) {
+                if (!wait_bar(&empty_bar[s], (uint32_t) (((i / NS) - 1) & 1))) break;
+                fence_proxy_async_smem();
+            }
+            const int e_lo = (tile0 + i) * ATT_CELLS;
+            const int e_hi = min(e_lo + ATT_CELLS, n_cells);
+            const int j_lo = e_lo / r, j_hi = (e_hi - 1) / r;
+            uint32_t bytes = 0;
+            for (int j = j_lo + lane; j <= j_hi; j += 32) {
+                const int a = max(e_lo, j * r), b = min(e_hi, (j + 1) * r);
+                const int cs = sel[j] * r + (a - j * r);
+                const int nv = max(0, min(b - a, qpos - cs + 1));
+                bytes += (uint32_t) nv * RBr * 2;
+            }
+            #pragma unroll
+            for (int off = 16; off > 0; off >>= 1) bytes += __shfl_xor_sync(0xffffffffu, bytes, off);
+            const int ea = e_lo + lane;
+            const unsigned vm = __ballot_sync(0xffffffffu, ea < n_cells && list_cell(sel, r, ea) <= qpos);
+            if (lane == 0) {
+                vmask[s] = vm;
+                mbar_arrive_expect_tx(&full_bar[s], bytes);
+            }
+            __syncwarp();
+            for (int j = j_lo + lane; j <= j_hi; j += 32) {
+                const int a = max(e_lo, j * r), b = min(e_hi, (j + 1) * r);
+                const int cs = sel[j] * r + (a - j * r);
+                const int nv = max(0, min(b - a, qpos - cs + 1));
+                if (nv > 0) {
+                    bulk_g2s(stage_k(s) + (a - e_lo) * RBr, kbase + (size_t) cs * d.rb_k, (uint32_t) nv * RBr, &full_bar[s]);
+                    bulk_g2s(stage_v(s) + (a - e_lo) * RBr, vbase + (size_t) cs * d.rb_v, (uint32_t) nv * RBr, &full_bar[s]);
+                }
+            }
+        }
+    } else {
+        const int rA = 16 * cw + r8, rB = rA + 8;           // this thread's S^T rows (cells of the tile)
+        const int c0 = 16 * cw + 2 * j4;                     // this thread's V^T columns: c0+{0,1,8,9}
+        const int hoff = hs * HB;                            // byte offset of this warp's head in a row
+        const int rb = (int) d.rb_k;                         // row bytes (= smem row stride), K and V alike
+        const uint2 * myq = qfrag + hs * 16 * 32 + lane;
+        for (int i = 0; i < n_local; i++) {
+            const int s = i % NS;
+            const uint32_t ph = (uint32_t) ((i / NS) & 1);
+            if (!wait_bar(&full_bar[s], ph)) break;
+            const uint32_t vm = vmask[s];
+            const bool okA = (vm >> rA) & 1u, okB = (vm >> rB) & 1u;
         if (head_live) {
             const uint8_t * Kt = stage_k(s) + hoff;
             const uint8_t * Vt = stage_v(s) + hoff;
@@ -392,219 +415,172 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_kernel(
                 }
             }
         }
-        // this warp is done with stage s; warp 0 refills it once all 8 warps are
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty_bar[s]);
-        if (warp == 0 && i + NS < n_local) {
-            mbar_wait_bounded(&empty_bar[s], ph, status);
-            fence_proxy_async_smem();
-            issue(i + NS);
+            // this warp is done with stage s: the producer may refill it
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty_bar[s]);
         }
     }
-    __syncthreads();                                  // all warps past the last tile: stages are free
+    __syncthreads();                                  // every warp past its last tile: stages are free
 
-    // ---- merge the 4 warps of each KV head (stage memory is free)
+    // ---- merge the 2 warps of each KV head (stage memory is free)
     #pragma unroll
     for (int off = 4; off < 32; off <<= 1) {
         l0 += __shfl_xor_sync(0xffffffffu, l0, off);
         l1 += __shfl_xor_sync(0xffffffffu, l1, off);
     }
-    float * wm = reinterpret_cast<float *>(smem);               // [8 warps][8 heads] max
-    float * wl = wm + ATT_WARPS * 8;                             // [8][8] sum
-    float * wo = wl + ATT_WARPS * 8;                             // [8][8][256] unnormalised O
-    float * cm = wo + ATT_WARPS * 8 * HEAD_DIM;                  // CTA state: [16] M, [16] L
-    float * co = cm + 2 * HROWS;                                 // CTA state: [16][256] O (scaled to M)
-    if (r8 == 0) {
-        wm[warp * 8 + 2 * j4] = m0; wm[warp * 8 + 2 * j4 + 1] = m1;
-        wl[warp * 8 + 2 * j4] = l0; wl[warp * 8 + 2 * j4 + 1] = l1;
-    }
-    float * myo = wo + warp * 8 * HEAD_DIM;
-    if (KV_TYPE == QSA_TYPE_Q8_0) {
-        #pragma unroll
-        for (int g8 = 0; g8 < 8; g8++) {
-            const int dim = 32 * g8 + 4 * r8;
-            *reinterpret_cast<float4 *>(myo + (2 * j4) * HEAD_DIM + dim) =
-                make_float4(o[2 * g8][0], o[2 * g8][2], o[2 * g8 + 1][0], o[2 * g8 + 1][2]);
-            *reinterpret_cast<float4 *>(myo + (2 * j4 + 1) * HEAD_DIM + dim) =
-                make_float4(o[2 * g8][1], o[2 * g8][3], o[2 * g8 + 1][1], o[2 * g8 + 1][3]);
+    float * wm = reinterpret_cast<float *>(smem);               // [4 warps][8 heads] max
+    float * wl = wm + ATT_CWARPS * 8;                            // [4][8] sum
+    float * wf = wl + ATT_CWARPS * 8;                            // [4][8] merge factors
+    float * cml = wf + ATT_CWARPS * 8;                           // [16] M, [16] L of the CTA
+    float * wo = cml + 2 * HROWS;                                // [4][8][256] unnormalised O
+    if (!producer) {
+        if (r8 == 0) {
+            wm[warp * 8 + 2 * j4] = m0; wm[warp * 8 + 2 * j4 + 1] = m1;
+            wl[warp * 8 + 2 * j4] = l0; wl[warp * 8 + 2 * j4 + 1] = l1;
         }
-    } else {
-        #pragma unroll
-        for (int mt = 0; mt < 16; mt++) {
-            const int dim = 16 * mt + r8;
-            myo[(2 * j4) * HEAD_DIM + dim]         = o[mt][0];
-            myo[(2 * j4 + 1) * HEAD_DIM + dim]     = o[mt][1];
-            myo[(2 * j4) * HEAD_DIM + dim + 8]     = o[mt][2];
-            myo[(2 * j4 + 1) * HEAD_DIM + dim + 8] = o[mt][3];
+        float * myo = wo + warp * 8 * HEAD_DIM;
+        if (KV_TYPE == QSA_TYPE_Q8_0) {
+            #pragma unroll
+            for (int g8 = 0; g8 < 8; g8++) {
+                const int dim = 32 * g8 + 4 * r8;
+                *reinterpret_cast<float4 *>(myo + (2 * j4) * HEAD_DIM + dim) =
+                    make_float4(o[2 * g8][0], o[2 * g8][2], o[2 * g8 + 1][0], o[2 * g8 + 1][2]);
+                *reinterpret_cast<float4 *>(myo + (2 * j4 + 1) * HEAD_DIM + dim) =
+                    make_float4(o[2 * g8][1], o[2 * g8][3], o[2 * g8 + 1][1], o[2 * g8 + 1][3]);
+            }
+        } else {
+            #pragma unroll
+            for (int mt = 0; mt < 16; mt++) {
+                const int dim = 16 * mt + r8;
+                myo[(2 * j4) * HEAD_DIM + dim]         = o[mt][0];
+                myo[(2 * j4 + 1) * HEAD_DIM + dim]     = o[mt][1];
+                myo[(2 * j4) * HEAD_DIM + dim + 8]     = o[mt][2];
+                myo[(2 * j4 + 1) * HEAD_DIM + dim + 8] = o[mt][3];
+            }
         }
     }
     __syncthreads();
-    float * wf = co + HROWS * HEAD_DIM;                          // [8 warps][8 heads] merge factors
-    if (tid < HROWS) {   // row hr = 8*head + h: M = max over the head's 4 warps, L = sum l 2^(m - M)
-        const int w0 = (tid >> 3) * 4, h = tid & 7;
+    if (tid < HROWS) {   // row hr = 8*head + h: M = max over the head's 2 warps, L = sum l 2^(m - M)
+        const int w0 = (tid >> 3) * 2, h = tid & 7;
         float M = -INFINITY;
-        for (int w = w0; w < w0 + 4; w++) M = fmaxf(M, wm[w * 8 + h]);
+        for (int w = w0; w < w0 + 2; w++) M = fmaxf(M, wm[w * 8 + h]);
         const float Mu = M == -INFINITY ? 0.0f : M;
         float L = 0.0f;
-        for (int w = w0; w < w0 + 4; w++) {
+        for (int w = w0; w < w0 + 2; w++) {
             const float f = exp2f(wm[w * 8 + h] - Mu);
             wf[w * 8 + h] = f;
             L += wl[w * 8 + h] * f;
         }
-        cm[tid] = M; cm[HROWS + tid] = L;
+        cml[tid] = M; cml[HROWS + tid] = L;
     }
     __syncthreads();
+    // ---- the CTA's state: the final output (one chunk), or a partial for attn_merge_kernel
+    const bool single = n_chunks == 1;
+    float * po = part_o + ((size_t) t * max_chunks + chunk) * HROWS * HEAD_DIM;
+    const int n_rows = d.n_head_kv * 8;
     for (int e4 = tid; e4 < HROWS * HEAD_DIM / 4; e4 += ATT_THREADS) {
-        const int hr = (e4 * 4) / HEAD_DIM, w0 = (hr >> 3) * 4, h = hr & 7, d4 = e4 % (HEAD_DIM / 4);
+        const int hr = (e4 * 4) / HEAD_DIM, w0 = (hr >> 3) * 2, h = hr & 7, d4 = e4 % (HEAD_DIM / 4);
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
         #pragma unroll
-        for (int w = 0; w < 4; w++) {
+        for (int w = 0; w < 2; w++) {
             const float f = wf[(w0 + w) * 8 + h];
             const float4 v = reinterpret_cast<const float4 *>(wo + ((w0 + w) * 8 + h) * HEAD_DIM)[d4];
             acc.x += f * v.x; acc.y += f * v.y; acc.z += f * v.z; acc.w += f * v.w;
         }
-        reinterpret_cast<float4 *>(co)[e4] = acc;
-    }
-    __syncthreads();
-
-    // ---- first combine level: the CTAs of a cluster (consecutive chunks of query t) reduce-scatter
-    // through distributed shared memory: every rank derives the per-row weights of all ranks, then
-    // merges its own 1/CL slice of the [16][256] state over the ranks.
-    cg::cluster_group cluster = cg::this_cluster();
-    const int CL = (int) cluster.num_blocks();
-    const int crank = (int) cluster.block_rank();
-    const int cl_id = chunk / CL;
-    const int n_cl = (n_chunks + CL - 1) / CL;
-    cluster.sync();                                   // every CTA's cm/co are complete
-    float * rw = co + HROWS * HEAD_DIM + 64;          // [8 ranks][16] ranks' m, then their weights
-    float * rl = rw + 8 * HROWS;                      // [8 ranks][16] ranks' l
-    float * rML = rl + 8 * HROWS;                     // [16] cluster M, [16] cluster L
-    if (tid < CL * HROWS) {
-        const int p = tid / HROWS, hr = tid % HROWS;
-        const float * pc = cluster.map_shared_rank(cm, p);
-        rw[p * HROWS + hr] = pc[hr];
-        rl[p * HROWS + hr] = pc[HROWS + hr];
-    }
-    __syncthreads();
-    if (tid < HROWS) {
-        float M = -INFINITY;
-        for (int p = 0; p < CL; p++) M = fmaxf(M, rw[p * HROWS + tid]);
-        const float Mu = M == -INFINITY ? 0.0f : M;
-        float L = 0.0f;
-        for (int p = 0; p < CL; p++) {
-            const float w = exp2f(rw[p * HROWS + tid] - Mu);
-            rw[p * HROWS + tid] = w;
-            L += rl[p * HROWS + tid] * w;
-        }
-        rML[tid] = M; rML[HROWS + tid] = L;
-    }
-    __syncthreads();
-    const int n_rows = d.n_head_kv * 8;
-    const int n_e4 = HROWS * HEAD_DIM / 4;            // float4 elements of the state
-    const int slice = (n_e4 + CL - 1) / CL;
-    const int e_beg = crank * slice, e_end = min(n_e4, e_beg + slice);
-    auto write_out = [&](int e4, float4 v, float L) {
-        const int hr = (e4 * 4) / HEAD_DIM, h = hr & 7, g = hr >> 3;
-        if (hr < n_rows && h < d.gqa) {
+        if (!single) {
+            reinterpret_cast<float4 *>(po)[e4] = acc;
+        } else if (stq) {
+            reinterpret_cast<float4 *>(stq + 2 * HROWS)[e4] = acc;
+        } else if (hr < n_rows && h < d.gqa) {
+            const float L = cml[HROWS + hr];
             const float inv = L > 0.0f ? 1.0f / L : 0.0f;
-            reinterpret_cast<float4 *>(outq + (size_t) (g * d.gqa + h) * HEAD_DIM)[(e4 * 4 % HEAD_DIM) / 4] =
-                make_float4(v.x * inv, v.y * inv, v.z * inv, v.w * inv);
+            reinterpret_cast<float4 *>(outq + (size_t) (hr >> 3) * d.gqa * HEAD_DIM + (size_t) h * HEAD_DIM)[d4] =
+                make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
         }
-    };
-    const int max_parts = (max_chunks + CL - 1) / CL;
-    float * po = part_o + ((size_t) t * max_parts + cl_id) * HROWS * HEAD_DIM;
-    {
-        const float4 * pco[8];
+    }
+    if (tid < 2 * HROWS) {
+        if (!single) part_ml[((size_t) t * max_chunks + chunk) * 2 * HROWS + tid] = cml[tid];
+        else if (stq) stq[tid] = cml[tid];
+    }
+}
+
+// Merge of the per-CTA partials of the queries split over several chunks: CTA (t, row hr, 64-dim
+// slice); out = sum_c 2^(m_c - M) O_c / sum_c 2^(m_c - M) l_c, M = max_c m_c (the state one CTA
+// would have reached).  Thread = (float4 column of the slice, group of chunks), so that every
+// thread has only a few independent partial loads in flight.  Launched programmatically behind
+// attn_kernel.
+constexpr int MERGE_COLS = 16;                        // float4 columns: 64 dims per CTA
+constexpr int MERGE_GROUPS = MERGE_THREADS / MERGE_COLS;
+__global__ void __launch_bounds__(MERGE_THREADS) attn_merge_kernel(DevDesc d, const qsa_decode_item * __restrict__ items,
+        int n_past0, const int * __restrict__ nsel_ws, int tiles_per_cta, int max_chunks,
+        const float * __restrict__ part_o, const float * __restrict__ part_ml,
+        float * __restrict__ out, float * __restrict__ state_out) {
+    extern __shared__ float wsh[];                    // [max_chunks] weights
+    __shared__ float red[2][MERGE_THREADS / 32];
+    __shared__ float4 racc[MERGE_GROUPS][MERGE_COLS];
+    const int t = blockIdx.x, hr = blockIdx.y;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int col = tid % MERGE_COLS, grp = tid / MERGE_COLS;
+    const int d4 = blockIdx.z * MERGE_COLS + col;     // float4 index inside the row
+    const int qpos = items ? items[t].n_past : n_past0 + t;
+    const int g = hr >> 3, h = hr & 7;
+    const bool live = g < d.n_head_kv && h < d.gqa;
+    if (!state_out && !live) return;
+    pdl_wait();                                       // attn_kernel has completed: partials are written
+    const bool pos_ok = qpos >= 0 && qpos < d.n_ctx;
+    const int nsel = pos_ok ? max(0, min(nsel_ws[t], d.kb)) : 0;
+    const int n_chunks = attn_n_chunks(d, nsel, tiles_per_cta);
+    if (n_chunks <= 1) return;                        // written by the attention CTA itself
+    const float * ml = part_ml + (size_t) t * max_chunks * 2 * HROWS;
+    float M = -INFINITY;
+    for (int c = tid; c < n_chunks; c += MERGE_THREADS) M = fmaxf(M, __ldcg(ml + c * 2 * HROWS + hr));
+    M = warp_max(M);
+    if (lane == 0) red[0][warp] = M;
+    __syncthreads();
+    M = red[0][0];
+    #pragma unroll
+    for (int w = 1; w < MERGE_THREADS / 32; w++) M = fmaxf(M, red[0][w]);
+    const float Mu = M == -INFINITY ? 0.0f : M;
+    float L = 0.0f;
+    for (int c = tid; c < n_chunks; c += MERGE_THREADS) {
+        const float w = exp2f(__ldcg(ml + c * 2 * HROWS + hr) - Mu);
+        wsh[c] = w;
+        L += __ldcg(ml + c * 2 * HROWS + HROWS + hr) * w;
+    }
+    #pragma unroll
+    for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+    if (lane == 0) red[1][warp] = L;
+    __syncthreads();                                  // wsh and the partial sums are complete
+    L = 0.0f;
+    #pragma unroll
+    for (int w = 0; w < MERGE_THREADS / 32; w++) L += red[1][w];
+    const float4 * po = reinterpret_cast<const float4 *>(part_o + ((size_t) t * max_chunks * HROWS + hr) * HEAD_DIM) + d4;
+    const size_t cstride = (size_t) HROWS * HEAD_DIM / 4;         // float4s between chunks
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    #pragma unroll 4
+    for (int c = grp; c < n_chunks; c += MERGE_GROUPS) {
+        const float4 v = __ldcg(po + (size_t) c * cstride);
+        const float w = wsh[c];
+        acc.x += w * v.x; acc.y += w * v.y; acc.z += w * v.z; acc.w += w * v.w;
+    }
+    racc[grp][col] = acc;
+    __syncthreads();
+    if (tid < MERGE_COLS) {
+        float4 s = racc[0][tid];
         #pragma unroll
-        for (int p = 0; p < 8; p++) pco[p] = reinterpret_cast<const float4 *>(cluster.map_shared_rank(co, p < CL ? p : 0));
-        for (int e4 = e_beg + tid; e4 < e_end; e4 += ATT_THREADS) {
-            const int hr = (e4 * 4) / HEAD_DIM;
-            float4 v[8];
-            #pragma unroll
-            for (int p = 0; p < 8; p++) v[p] = p < CL ? pco[p][e4] : make_float4(0.f, 0.f, 0.f, 0.f);
-            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            #pragma unroll
-            for (int p = 0; p < 8; p++) {
-                const float w = p < CL ? rw[p * HROWS + hr] : 0.0f;
-                acc.x += w * v[p].x; acc.y += w * v[p].y; acc.z += w * v[p].z; acc.w += w * v[p].w;
-            }
-            if (n_cl == 1) {
-                if (stq) reinterpret_cast<float4 *>(stq + 2 * HROWS)[e4] = acc;
-                else write_out(e4, acc, rML[HROWS + hr]);
-            } else {
-                reinterpret_cast<float4 *>(po)[e4] = acc;
-            }
+        for (int k = 1; k < MERGE_GROUPS; k++) {
+            const float4 v = racc[k][tid];
+            s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
         }
-    }
-    if (n_cl == 1 && stq && crank == 0 && tid < 2 * HROWS) stq[tid] = rML[tid];
-    if (n_cl > 1) {
-        if (crank == 0 && tid < 2 * HROWS)
-            part_ml[((size_t) t * max_parts + cl_id) * 2 * HROWS + tid] = rML[tid];
-        __threadfence();                              // this rank's partial slice is visible GPU-wide
-    }
-    cluster.sync();                                   // peers are done reading; all slices written
-    if (n_cl == 1) return;
-    // ---- second level: the last cluster to arrive merges the cluster partials, slice by slice
-    // Rank 0 counts the arrival and writes the verdict into every rank's own shared memory before
-    // the barrier (a rank must never read the shared memory of a CTA that may already have exited).
-    if (crank == 0 && tid == 0) {
-        unsigned prev;
-        asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], 1;" : "=r"(prev) : "l"(counters + t) : "memory");
-        const bool last = prev == (unsigned) (n_cl - 1);
-        if (last) counters[t] = 0;
-        for (int p = 0; p < CL; p++) *cluster.map_shared_rank(&is_last, p) = last;
-    }
-    cluster.sync();
-    if (!is_last) return;
-    __threadfence();
-    const float * pob = part_o + (size_t) t * max_parts * HROWS * HEAD_DIM;
-    const float * pmb = part_ml + (size_t) t * max_parts * 2 * HROWS;
-    float * gm = co;                                  // [n_cl][16] m -> weights (co is free now)
-    float * gl = gm + n_cl * HROWS;                   // [n_cl][16] l
-    float * gL = gl + n_cl * HROWS;                   // [16] L, then [16] M
-    for (int i = tid; i < n_cl * 2 * HROWS; i += ATT_THREADS) {     // every (m, l) loaded at once
-        const int c = i / (2 * HROWS), k = i % (2 * HROWS);
-        const float v = __ldcg(pmb + i);
-        if (k < HROWS) gm[c * HROWS + k] = v; else gl[c * HROWS + k - HROWS] = v;
-    }
-    __syncthreads();
-    if (tid < HROWS) {
-        float M = -INFINITY;
-        for (int c = 0; c < n_cl; c++) M = fmaxf(M, gm[c * HROWS + tid]);
-        const float Mu = M == -INFINITY ? 0.0f : M;
-        float L = 0.0f;
-        for (int c = 0; c < n_cl; c++) {
-            const float w = exp2f(gm[c * HROWS + tid] - Mu);
-            gm[c * HROWS + tid] = w;
-            L += gl[c * HROWS + tid] * w;
+        if (state_out) {
+            float * stq = state_out + (size_t) t * (2 * HROWS + HROWS * HEAD_DIM);
+            reinterpret_cast<float4 *>(stq + 2 * HROWS + hr * HEAD_DIM)[d4] = s;
+            if (blockIdx.z == 0 && tid == 0) { stq[hr] = M; stq[HROWS + hr] = L; }
+        } else {
+            const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+            reinterpret_cast<float4 *>(out + ((size_t) t * d.n_head + g * d.gqa + h) * HEAD_DIM)[d4] =
+                make_float4(s.x * inv, s.y * inv, s.z * inv, s.w * inv);
         }
-        gL[tid] = L;
-        gL[HROWS + tid] = M;
-        if (stq && crank == 0) { stq[tid] = M; stq[HROWS + tid] = L; }
-    }
-    __syncthreads();
-    const float4 * po4 = reinterpret_cast<const float4 *>(pob);
-    for (int e4 = e_beg + tid; e4 < e_end; e4 += ATT_THREADS) {
-        const int hr = (e4 * 4) / HEAD_DIM;
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        int c = 0;
-        for (; c + 8 <= n_cl; c += 8) {
-            float4 v[8];
-            #pragma unroll
-            for (int u = 0; u < 8; u++) v[u] = __ldcg(po4 + (size_t) (c + u) * n_e4 + e4);
-            #pragma unroll
-            for (int u = 0; u < 8; u++) {
-                const float w = gm[(c + u) * HROWS + hr];
-                acc.x += w * v[u].x; acc.y += w * v[u].y; acc.z += w * v[u].z; acc.w += w * v[u].w;
-            }
-        }
-        for (; c < n_cl; c++) {
-            const float4 v = __ldcg(po4 + (size_t) c * n_e4 + e4);
-            const float w = gm[c * HROWS + hr];
-            acc.x += w * v.x; acc.y += w * v.y; acc.z += w * v.z; acc.w += w * v.w;
-        }
-        if (stq) reinterpret_cast<float4 *>(stq + 2 * HROWS)[e4] = acc;
-        else write_out(e4, acc, gL[hr]);
     }
 }
 
@@ -617,40 +593,44 @@ cudaError_t attn_set_attrs() {
     return e;
 }
 
-int attn_cluster_size(int max_chunks) { return max_chunks < 8 ? max_chunks : 8; }
+int attn_tile_cells() { return ATT_CELLS; }
 
 int attn_state_rows() { return HROWS; }
 
-cudaError_t launch_attn(const DevDesc & d, dim3 grid, cudaStream_t st, const qsa_decode_item * items,
+int attn_resident_ctas(int type_k) {
+    return 148 * (type_k == QSA_TYPE_Q8_0 ? AttnCfg<QSA_TYPE_Q8_0>::MIN_CTAS : AttnCfg<QSA_TYPE_F16>::MIN_CTAS);
+}
+
+cudaError_t launch_attn(const DevDesc & d, cudaStream_t st, int n_q, const qsa_decode_item * items,
         qsa_layer_cache cache0, int n_past0, const void * q, int q_type, const int * sel_ws, const int * nsel_ws,
-        int tiles_per_cta, int max_chunks, float * part_o, float * part_ml, unsigned * counters, float * out,
-        uint32_t * status, float * state_out) {
-    // CTAs of consecutive chunks of one query form a cluster of up to 8
-    const int CL = attn_cluster_size(max_chunks);
-    grid.x = (unsigned) (((max_chunks + CL - 1) / CL) * CL);
-    grid.y = grid.z;                                  // queries
-    grid.z = 1;
+        int tiles_per_cta, int max_chunks, float * part_o, float * part_ml, float * out, uint32_t * status,
+        float * state_out) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
+    cfg.gridDim = dim3((unsigned) max_chunks, (unsigned) n_q);
     cfg.blockDim = dim3(ATT_THREADS);
     cfg.stream = st;
-    cudaLaunchAttribute attr[2];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = (unsigned) CL;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;   // prologue overlaps the select
-    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;   // prologue overlaps the select
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 2;
+    cfg.numAttrs = 1;
+    cudaError_t e;
     if (d.type_k == QSA_TYPE_Q8_0) {
         cfg.dynamicSmemBytes = attn_smem_bytes<QSA_TYPE_Q8_0>();
-        return cudaLaunchKernelEx(&cfg, attn_kernel<QSA_TYPE_Q8_0>, d, items, cache0, n_past0, q, q_type, sel_ws,
-                                  nsel_ws, tiles_per_cta, max_chunks, part_o, part_ml, counters, out, status, state_out);
+        e = cudaLaunchKernelEx(&cfg, attn_kernel<QSA_TYPE_Q8_0>, d, items, cache0, n_past0, q, q_type, sel_ws,
+                               nsel_ws, tiles_per_cta, max_chunks, part_o, part_ml, out, status, state_out);
+    } else {
+        cfg.dynamicSmemBytes = attn_smem_bytes<QSA_TYPE_F16>();
+        e = cudaLaunchKernelEx(&cfg, attn_kernel<QSA_TYPE_F16>, d, items, cache0, n_past0, q, q_type, sel_ws,
+                               nsel_ws, tiles_per_cta, max_chunks, part_o, part_ml, out, status, state_out);
     }
-    cfg.dynamicSmemBytes = attn_smem_bytes<QSA_TYPE_F16>();
-    return cudaLaunchKernelEx(&cfg, attn_kernel<QSA_TYPE_F16>, d, items, cache0, n_past0, q, q_type, sel_ws,
-                              nsel_ws, tiles_per_cta, max_chunks, part_o, part_ml, counters, out, status, state_out);
+    if (e != cudaSuccess || max_chunks <= 1) return e;
+    cudaLaunchConfig_t mc = cfg;
+    mc.gridDim = dim3((unsigned) n_q, HROWS, HEAD_DIM / (4 * MERGE_COLS));
+    mc.blockDim = dim3(MERGE_THREADS);
+    mc.dynamicSmemBytes = (size_t) max_chunks * 4;
+    return cudaLaunchKernelEx(&mc, attn_merge_kernel, d, items, n_past0, nsel_ws, tiles_per_cta, max_chunks,
+                              (const float *) part_o, (const float *) part_ml, out, state_out);
 }
 
 }  // namespace qsa

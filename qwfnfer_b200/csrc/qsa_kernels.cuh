@@ -23,12 +23,19 @@ __global__ void score_select_kernel(DevDesc d, const qsa_decode_item * items, co
 // Leading bytes of a decode workspace that must be zero before a call (status word + counters).
 size_t decode_workspace_zero_prefix(const qsa_desc * d, int32_t batch, int32_t max_n_kv);
 
-// Host launcher of the attention kernel (defined beside the kernel template).
-cudaError_t launch_attn(const DevDesc & d, dim3 grid, cudaStream_t st, const qsa_decode_item * items,
+// Host launcher of the attention kernel and, when a query spans several CTAs (max_chunks > 1),
+// of the merge of their partials (defined beside the kernels).
+cudaError_t launch_attn(const DevDesc & d, cudaStream_t st, int n_q, const qsa_decode_item * items,
         qsa_layer_cache cache0, int n_past0, const void * q, int q_type, const int * sel_ws, const int * nsel_ws,
-        int tiles_per_cta, int max_chunks, float * part_o, float * part_ml, unsigned * counters, float * out,
-        uint32_t * status, float * state_out = nullptr);
+        int tiles_per_cta, int max_chunks, float * part_o, float * part_ml, float * out, uint32_t * status,
+        float * state_out);
 cudaError_t attn_set_attrs();
+// Cells per attention tile.
+int attn_tile_cells();
+// Rows (KV head x query head) of the attention state: a partial is rows x head_dim floats.
+int attn_state_rows();
+// Attention CTAs resident on the GPU at once for a KV type (the CTAs of one wave).
+int attn_resident_ctas(int type_k);
 
 // KV-sequence-sharded decode: global selection from all shards' candidates, and the log-sum-exp
 // merge of the shards' attention states (qsa_shard.cu).

@@ -283,6 +283,10 @@ __global__ void __launch_bounds__(SEL_THREADS) score_select_kernel(DevDesc d,
     const int n_vis = bad ? 0 : (q + 1) / d.ratio;
     float * sc = scores_ws + (size_t) t * scores_stride;
 
+    // Decode with a window: this step's append writes only the query's own block (its pooled
+    // key included), which is forced, so scoring need not wait for it; the wait moves to the exit
+    // (the attention, launched behind this grid, still finds the appended row).
+    const bool defer_wait = items != nullptr && d.window > 0;
     if (!bad) {
         float qf[4][8];
         const int sub = threadIdx.x & 15;
@@ -293,12 +297,16 @@ __global__ void __launch_bounds__(SEL_THREADS) score_select_kernel(DevDesc d,
                 qf[h][e] = h < d.idx_n_head
                     ? f16_bits_to_f32(f32_to_f16_bits(q_idx[((size_t) t * d.idx_n_head + h) * d.idx_dim + 8 * sub + e]))
                     : 0.0f;
+        // candidates only: the forced blocks are the top of the visible range and never compete
+        int f_lo, f_hi;
+        forced_range(d, q, f_lo, f_hi);
+        const int cand_hi = f_lo <= f_hi ? min(n_vis, f_lo) : n_vis;
         const int b0 = blo + blockIdx.x * blocks_per_cta;
-        const int b1 = min(min(n_vis, bhi), b0 + blocks_per_cta);
-        pdl_wait();                              // the append of this step (pooled keys) is complete
+        const int b1 = min(min(cand_hi, bhi), b0 + blocks_per_cta);
+        if (!defer_wait) pdl_wait();             // the append of this step (pooled keys) is complete
         if (b0 < b1) score_range(d, pool, qf, b0, b1, sc);
     }
-    if (bad) pdl_wait();
+    if (bad && !defer_wait) pdl_wait();
     // Arrival: the last CTA of this query selects.  The barrier orders the CTA's score stores
     // before thread 0's release; its acquire orders the other CTAs' stores before our reads.
     __syncthreads();
@@ -309,7 +317,10 @@ __global__ void __launch_bounds__(SEL_THREADS) score_select_kernel(DevDesc d,
         if (is_last) counters[t] = 0;          // leave the counter at zero for the next call
     }
     __syncthreads();
-    if (!is_last) return;
+    if (!is_last) {
+        if (defer_wait) pdl_wait();
+        return;
+    }
     float * ssc = reinterpret_cast<float *>(dyn_smem);
     unsigned char * flag = dyn_smem + (size_t) scores_stride * 4;
     {   // the query's scores in [blo, n_vis), 16 bytes per load (score rows are 16-byte aligned)
@@ -326,11 +337,13 @@ __global__ void __launch_bounds__(SEL_THREADS) score_select_kernel(DevDesc d,
             if (cand_scores) cand_scores[(size_t) t * d.kb + i] = 0.0f;
         }
         if (threadIdx.x == 0) nsel_ws[t] = 0;
+        if (defer_wait) pdl_wait();
         return;
     }
     select_blocks(d, q, ssc, flag, sel_ws + (size_t) t * d.kb, nsel_ws + t,
                   sel_out ? sel_out + (size_t) t * d.kb : nullptr, sm, blo, bhi,
                   cand_scores ? cand_scores + (size_t) t * d.kb : nullptr);
+    if (defer_wait) pdl_wait();                  // the append is complete before this grid is
 }
 
 }  // namespace qsa

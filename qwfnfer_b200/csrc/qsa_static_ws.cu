@@ -13,7 +13,7 @@
 namespace {
 
 // Maximum scratch of one call.  Every GPU that loads the library holds this array until exit.
-constexpr size_t QSA_STATIC_SCRATCH_BYTES = 4u << 20;   // 4 MiB
+constexpr size_t QSA_STATIC_SCRATCH_BYTES = 8u << 20;   // 8 MiB
 
 static __device__ __align__(256) unsigned char g_qsa_static_scratch[QSA_STATIC_SCRATCH_BYTES];
 
