@@ -3,7 +3,7 @@
 // Reference: ggml_flash_attn_ext over the gathered cells with the cell mask, precision F32,
 // scale 1/sqrt(head_dim), GQA (src/qwfn_graph.cpp:497-502, 530-541; prefill :362-403).
 //
-// Work item = (query t, chunk of 32-cell tiles), both KV heads in one CTA: 4 consumer warps and
+// Work item = (query t, chunk of 32-cell tiles), both KV heads in one CTA: 8 consumer warps and
 // one producer warp, two CTAs per SM.  The selected blocks of a query, ascending, expand to a cell
 // list (block b -> cells b*r .. b*r+r-1); a tile is 32 consecutive entries.
 //   - the rows of one block are contiguous in the cache (row = both heads, 544 B in q8_0), so a
@@ -12,12 +12,15 @@
 //     transaction counts; rows past the query or past the list are not fetched, they are masked
 //     in registers (their scores -inf, their V scales / f16 values zero);
 //   - the producer warp issues the copies of a stage once the consumers released it; consumer
-//     warps 0-1 take KV head 0, warps 2-3 KV head 1, 16 cells each; the 8 query heads of a KV
-//     head are the N=8 dimension of mma.m16n8k16: S^T = K Q^T (cells x heads), O^T += V^T P;
+//     warps 0-3 take KV head 0, warps 4-7 KV head 1; a warp pair owns 16 cells and splits the
+//     256 dims in halves: each half-warp pair member computes a partial S over its 128 dims,
+//     the pair exchanges them through shared memory, and each then accumulates O for its own
+//     128 dims; the 8 query heads of a KV head are the N=8 dimension of mma.m16n8k16:
+//     S^T = K Q^T (cells x heads), O^T += V^T P;
 //   - q8_0 is dequantised in registers: int8 bytes become exact f16 integers; the K scale
 //     multiplies the f32 partial dot of each 32-dim group, the V scale multiplies P;
-//   - online softmax in the exp2 domain with warp shuffles; the two warps of a KV head merge in
-//     shared memory; a query split over several CTAs leaves one unnormalised partial per CTA in
+//   - online softmax in the exp2 domain with warp shuffles; the two cell halves of a KV head
+//     merge in shared memory; a query split over several CTAs leaves one unnormalised partial per CTA in
 //     the workspace, merged by attn_merge_kernel (launched programmatically behind the
 //     attention grid, it waits for it with griddepcontrol.wait).
 #include "qsa_kernels.cuh"
@@ -25,7 +28,7 @@
 namespace qsa {
 
 constexpr int ATT_CELLS   = 32;        // cells per tile (one pipeline stage)
-constexpr int ATT_CWARPS  = 4;         // consumer warps: (KV head, 16-cell half of the tile)
+constexpr int ATT_CWARPS  = 8;         // consumer warps: (KV head, 16-cell half, 128-dim half)
 constexpr int ATT_THREADS = 32 * (ATT_CWARPS + 1);   // + the producer warp
 constexpr int HROWS       = 16;        // 2 KV heads x 8 query heads: rows of the CTA state
 constexpr int MERGE_THREADS = 256;     // attn_merge_kernel: threads per CTA
@@ -45,13 +48,15 @@ template <> struct AttnCfg<QSA_TYPE_F16> {
 // shared-memory row = the KV heads of the CTA (all heads of a row: n_head_kv <= 2)
 template <int KV_TYPE> constexpr int attn_row_bytes() { return 2 * AttnCfg<KV_TYPE>::HB; }
 template <int KV_TYPE> constexpr int attn_stage_bytes() { return 2 * ATT_CELLS * attn_row_bytes<KV_TYPE>(); }
+// S exchange between the two dim-half warps of a pair: [2 tiles][consumer warps][32 lanes] float4
+constexpr int ATT_XCH_BYTES = 2 * ATT_CWARPS * 32 * 16;
 template <int KV_TYPE> constexpr int attn_smem_bytes() {
-    return AttnCfg<KV_TYPE>::NSTAGE * attn_stage_bytes<KV_TYPE>() + MAX_KB * 4 + HROWS * HEAD_DIM * 2;
+    return AttnCfg<KV_TYPE>::NSTAGE * attn_stage_bytes<KV_TYPE>() + MAX_KB * 4 + HROWS * HEAD_DIM * 2 + ATT_XCH_BYTES;
 }
 static_assert(AttnCfg<QSA_TYPE_Q8_0>::MIN_CTAS * (attn_smem_bytes<QSA_TYPE_Q8_0>() + 2048) <= 228 * 1024,
               "q8_0 attention CTAs per SM");
 // the post-loop merge scratch (per-warp O, m, l) lives in the stage memory
-static_assert(ATT_CWARPS * 8 * HEAD_DIM * 4 + 2 * ATT_CWARPS * 8 * 4 + 2 * ATT_CWARPS * 8 * 4 <=
+static_assert(ATT_CWARPS * 8 * (HEAD_DIM / 2) * 4 + 3 * ATT_CWARPS * 8 * 4 + 2 * HROWS * 4 <=
               AttnCfg<QSA_TYPE_Q8_0>::NSTAGE * 2 * ATT_CELLS * 2 * AttnCfg<QSA_TYPE_Q8_0>::HB, "merge scratch");
 
 __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&a)[4], const void * p) {
@@ -60,6 +65,10 @@ __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&a)[4], const void *
 }
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// Barrier of the `n` threads (whole warps) that name barrier `id` (1..15; 0 is __syncthreads).
+__device__ __forceinline__ void named_bar_sync(int id, int n) {
+    asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(n) : "memory");
 }
 
 // Cell of list entry `idx` of a query (cells of the selected blocks, in order).
@@ -90,12 +99,14 @@ __global__ void __launch_bounds__(ATT_THREADS, AttnCfg<KV_TYPE>::MIN_CTAS) attn_
     const int t = blockIdx.y, chunk = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int r8 = lane >> 2, j4 = lane & 3;
-    const int hs = (warp >> 1) & 1;           // KV head of a consumer warp
-    const int cw = warp & 1;                  // 16-cell half of the tile
+    const int hs = (warp >> 2) & 1;           // consumer warp: KV head,
+    const int cw = (warp >> 1) & 1;           //   16-cell half of the tile,
+    const int dh = warp & 1;                  //   128-dim half (q8_0 groups 4dh..4dh+3)
     const bool producer = warp == ATT_CWARPS;
     const bool head_live = !producer && hs < d.n_head_kv;
     int * sel = reinterpret_cast<int *>(smem + NS * attn_stage_bytes<KV_TYPE>());
     __half * qs = reinterpret_cast<__half *>(smem + NS * attn_stage_bytes<KV_TYPE>() + MAX_KB * 4);
+    float4 * xch = reinterpret_cast<float4 *>(smem + NS * attn_stage_bytes<KV_TYPE>() + MAX_KB * 4 + HROWS * HEAD_DIM * 2);
 
     // ---- prologue: every input load is independent, issued together
     int qpos;
@@ -185,7 +196,7 @@ __global__ void __launch_bounds__(ATT_THREADS, AttnCfg<KV_TYPE>::MIN_CTAS) attn_
     // Q fragments (mma B operand) of each KV head, packed in lane order into shared memory (over
     // the staged Q, which only these two builders read): head n = r8 of the 8-head tile.
     uint32_t qf[16][2];
-    const bool qbuilder = warp == 0 || warp == 2;
+    const bool qbuilder = warp == 0 || warp == 4;
     if (qbuilder) {
         const __half * qrow = qs + (hs * 8 + r8) * HEAD_DIM;
         auto pk2 = [&](int d0, int d1) -> uint32_t {
@@ -230,9 +241,9 @@ __global__ void __launch_bounds__(ATT_THREADS, AttnCfg<KV_TYPE>::MIN_CTAS) attn_
         return false;
     };
 
-    float o[16][4];
+    float o[8][4];                                       // this warp's 128 dims x 8 heads
     #pragma unroll
-    for (int i = 0; i < 16; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
+    for (int i = 0; i < 8; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
 
     if (producer) {
@@ -279,142 +290,167 @@ __global__ void __launch_bounds__(ATT_THREADS, AttnCfg<KV_TYPE>::MIN_CTAS) attn_
         const int c0 = 16 * cw + 2 * j4;                     // this thread's V^T columns: c0+{0,1,8,9}
         const int hoff = hs * HB;                            // byte offset of this warp's head in a row
         const int rb = (int) d.rb_k;                         // row bytes (= smem row stride), K and V alike
-        const uint2 * myq = qfrag + hs * 16 * 32 + lane;
+        // this warp's Q fragments (its 8 k-steps of 16 dims) stay in registers for the whole loop
+        uint2 qreg[8];
+        #pragma unroll
+        for (int k = 0; k < 8; k++) qreg[k] = qfrag[(hs * 16 + 8 * dh + k) * 32 + lane];
+        const int pair_bar = 1 + (warp >> 1);                // the two dim-half warps of (head, cells)
+        const uint32_t negb[4] = {F16X2_NEG1152, F16X2_NEG1152, F16X2_NEG1152, F16X2_NEG1152};
         for (int i = 0; i < n_local; i++) {
             const int s = i % NS;
             const uint32_t ph = (uint32_t) ((i / NS) & 1);
-            if (!wait_bar(&full_bar[s], ph)) break;
+            // every iteration reaches the pair barrier, also after a timed-out wait
+            const bool ok = wait_bar(&full_bar[s], ph) && head_live;
             const uint32_t vm = vmask[s];
             const bool okA = (vm >> rA) & 1u, okB = (vm >> rB) & 1u;
-        if (head_live) {
             const uint8_t * Kt = stage_k(s) + hoff;
             const uint8_t * Vt = stage_v(s) + hoff;
-            // ---- S^T = K Q^T for the warp's 16 cells x 8 heads
+            // ---- partial S^T = K Q^T over this warp's 128 dims, for its 16 cells x 8 heads
             float sc[4] = {0.f, 0.f, 0.f, 0.f};
-            if (KV_TYPE == QSA_TYPE_Q8_0) {
-                // row bases are 4-byte aligned; q8_0 block g8 starts at byte 34*g8 (scale) + 2 (quants),
-                // so its quants are word aligned for odd g8 and 2 bytes off for even g8
-                const uint32_t * WA = reinterpret_cast<const uint32_t *>(Kt + rA * rb);
-                const uint32_t * WB = reinterpret_cast<const uint32_t *>(Kt + rB * rb);
-                const uint16_t * HA = reinterpret_cast<const uint16_t *>(WA);
-                const uint16_t * HB_ = reinterpret_cast<const uint16_t *>(WB);
-                #pragma unroll
-                for (int g8 = 0; g8 < 8; g8++) {
-                    uint32_t w0A, w1A, w0B, w1B;
-                    if ((g8 & 1) == 0) {
-                        const int wi = 17 * (g8 / 2) + 2 * j4;
-                        const uint32_t a0 = WA[wi], a1 = WA[wi + 1], a2 = WA[wi + 2];
-                        const uint32_t b0 = WB[wi], b1 = WB[wi + 1], b2 = WB[wi + 2];
-                        w0A = __funnelshift_r(a0, a1, 16); w1A = __funnelshift_r(a1, a2, 16);
-                        w0B = __funnelshift_r(b0, b1, 16); w1B = __funnelshift_r(b1, b2, 16);
-                    } else {
-                        const int wi = 17 * (g8 / 2) + 9 + 2 * j4;
-                        w0A = WA[wi]; w1A = WA[wi + 1];
-                        w0B = WB[wi]; w1B = WB[wi + 1];
+            if (ok) {
+                if (KV_TYPE == QSA_TYPE_Q8_0) {
+                    // row bases are 4-byte aligned; q8_0 block g8 starts at byte 34*g8 (scale) + 2 (quants),
+                    // so its quants are word aligned for odd g8 and 2 bytes off for even g8
+                    const uint32_t * WA = reinterpret_cast<const uint32_t *>(Kt + rA * rb) + 34 * dh;
+                    const uint32_t * WB = reinterpret_cast<const uint32_t *>(Kt + rB * rb) + 34 * dh;
+                    const uint16_t * HA = reinterpret_cast<const uint16_t *>(WA);
+                    const uint16_t * HB_ = reinterpret_cast<const uint16_t *>(WB);
+                    #pragma unroll
+                    for (int gg = 0; gg < 4; gg++) {            // group g8 = 4 dh + gg
+                        uint32_t w0A, w1A, w0B, w1B;
+                        if ((gg & 1) == 0) {
+                            const int wi = 17 * (gg / 2) + 2 * j4;
+                            const uint32_t a0 = WA[wi], a1 = WA[wi + 1], a2 = WA[wi + 2];
+                            const uint32_t b0 = WB[wi], b1 = WB[wi + 1], b2 = WB[wi + 2];
+                            w0A = __funnelshift_r(a0, a1, 16); w1A = __funnelshift_r(a1, a2, 16);
+                            w0B = __funnelshift_r(b0, b1, 16); w1B = __funnelshift_r(b1, b2, 16);
+                        } else {
+                            const int wi = 17 * (gg / 2) + 9 + 2 * j4;
+                            w0A = WA[wi]; w1A = WA[wi + 1];
+                            w0B = WB[wi]; w1B = WB[wi + 1];
+                        }
+                        const float dA = f16_bits_to_f32(HA[17 * gg]);
+                        const float dB = f16_bits_to_f32(HB_[17 * gg]);
+                        const uint2 qa = qreg[2 * gg], qb2 = qreg[2 * gg + 1];
+                        const uint32_t b0[2] = {qa.x, qa.y}, b1[2] = {qb2.x, qb2.y};
+                        float c[4] = {0.f, 0.f, 0.f, 0.f};
+                        // K + 1152 (exact f16 integers), then -1152 x the Q column sums
+                        const uint32_t a0[4] = {i8x2_even_biased(w0A), i8x2_even_biased(w0B),
+                                                i8x2_odd_biased(w0A), i8x2_odd_biased(w0B)};
+                        const uint32_t a1[4] = {i8x2_even_biased(w1A), i8x2_even_biased(w1B),
+                                                i8x2_odd_biased(w1A), i8x2_odd_biased(w1B)};
+                        mma_f16_16816(c, negb, b0);
+                        mma_f16_16816(c, negb, b1);
+                        mma_f16_16816(c, a0, b0);
+                        mma_f16_16816(c, a1, b1);
+                        sc[0] = fmaf(dA, c[0], sc[0]); sc[1] = fmaf(dA, c[1], sc[1]);
+                        sc[2] = fmaf(dB, c[2], sc[2]); sc[3] = fmaf(dB, c[3], sc[3]);
                     }
-                    const float dA = f16_bits_to_f32(HA[17 * g8]);
-                    const float dB = f16_bits_to_f32(HB_[17 * g8]);
-                    const uint2 qa = myq[(2 * g8) * 32], qb2 = myq[(2 * g8 + 1) * 32];
-                    const uint32_t b0[2] = {qa.x, qa.y}, b1[2] = {qb2.x, qb2.y};
-                    float c[4] = {0.f, 0.f, 0.f, 0.f};
-                    const uint32_t a0[4] = {i8x2_even_to_f16x2(w0A), i8x2_even_to_f16x2(w0B),
-                                            i8x2_odd_to_f16x2(w0A), i8x2_odd_to_f16x2(w0B)};
-                    const uint32_t a1[4] = {i8x2_even_to_f16x2(w1A), i8x2_even_to_f16x2(w1B),
-                                            i8x2_odd_to_f16x2(w1A), i8x2_odd_to_f16x2(w1B)};
-                    mma_f16_16816(c, a0, b0);
-                    mma_f16_16816(c, a1, b1);
-                    sc[0] = fmaf(dA, c[0], sc[0]); sc[1] = fmaf(dA, c[1], sc[1]);
-                    sc[2] = fmaf(dB, c[2], sc[2]); sc[3] = fmaf(dB, c[3], sc[3]);
-                }
-            } else {
-                #pragma unroll
-                for (int kt = 0; kt < 16; kt++) {
-                    const uint8_t * ka = Kt + rA * rb + 2 * (16 * kt + 2 * j4);
-                    const uint8_t * kb = Kt + rB * rb + 2 * (16 * kt + 2 * j4);
-                    const uint32_t a[4] = {*reinterpret_cast<const uint32_t *>(ka), *reinterpret_cast<const uint32_t *>(kb),
-                                           *reinterpret_cast<const uint32_t *>(ka + 16), *reinterpret_cast<const uint32_t *>(kb + 16)};
-                    const uint2 qk = myq[kt * 32];
-                    const uint32_t bq[2] = {qk.x, qk.y};
-                    mma_f16_16816(sc, a, bq);
+                } else {
+                    #pragma unroll
+                    for (int kk = 0; kk < 8; kk++) {
+                        const int kt = 8 * dh + kk;
+                        const uint8_t * ka = Kt + rA * rb + 2 * (16 * kt + 2 * j4);
+                        const uint8_t * kb = Kt + rB * rb + 2 * (16 * kt + 2 * j4);
+                        const uint32_t a[4] = {*reinterpret_cast<const uint32_t *>(ka), *reinterpret_cast<const uint32_t *>(kb),
+                                               *reinterpret_cast<const uint32_t *>(ka + 16), *reinterpret_cast<const uint32_t *>(kb + 16)};
+                        const uint2 qk = qreg[kk];
+                        const uint32_t bq[2] = {qk.x, qk.y};
+                        mma_f16_16816(sc, a, bq);
+                    }
                 }
             }
-            // ---- mask, scale to the exp2 domain, online softmax (heads 2j, 2j+1 of this thread)
-            sc[0] = okA ? sc[0] * d.scale_log2 : -INFINITY;
-            sc[1] = okA ? sc[1] * d.scale_log2 : -INFINITY;
-            sc[2] = okB ? sc[2] * d.scale_log2 : -INFINITY;
-            sc[3] = okB ? sc[3] * d.scale_log2 : -INFINITY;
-            float mx0 = fmaxf(sc[0], sc[2]), mx1 = fmaxf(sc[1], sc[3]);
-            #pragma unroll
-            for (int off = 4; off < 32; off <<= 1) {
-                mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
-                mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+            // ---- the pair's two halves of S: exchange through shared memory (double-buffered by
+            // tile parity, so one barrier per tile suffices); a + b == b + a, both warps agree
+            if (head_live) {
+                xch[((i & 1) * ATT_CWARPS + warp) * 32 + lane] = make_float4(sc[0], sc[1], sc[2], sc[3]);
+                named_bar_sync(pair_bar, 64);
+                const float4 pv = xch[((i & 1) * ATT_CWARPS + (warp ^ 1)) * 32 + lane];
+                sc[0] += pv.x; sc[1] += pv.y; sc[2] += pv.z; sc[3] += pv.w;
             }
-            const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-            const float mu0 = mn0 == -INFINITY ? 0.0f : mn0, mu1 = mn1 == -INFINITY ? 0.0f : mn1;
-            const float al0 = exp2f(m0 - mu0), al1 = exp2f(m1 - mu1);
-            float p[4];
-            p[0] = exp2f(sc[0] - mu0); p[1] = exp2f(sc[1] - mu1);
-            p[2] = exp2f(sc[2] - mu0); p[3] = exp2f(sc[3] - mu1);
-            l0 = l0 * al0 + p[0] + p[2];
-            l1 = l1 * al1 + p[1] + p[3];
-            m0 = mn0; m1 = mn1;
-            if (__any_sync(0xffffffffu, al0 != 1.0f || al1 != 1.0f)) {   // the running max moved
+            if (ok) {
+                // ---- mask, scale to the exp2 domain, online softmax (heads 2j, 2j+1 of this thread)
+                sc[0] = okA ? sc[0] * d.scale_log2 : -INFINITY;
+                sc[1] = okA ? sc[1] * d.scale_log2 : -INFINITY;
+                sc[2] = okB ? sc[2] * d.scale_log2 : -INFINITY;
+                sc[3] = okB ? sc[3] * d.scale_log2 : -INFINITY;
+                float mx0 = fmaxf(sc[0], sc[2]), mx1 = fmaxf(sc[1], sc[3]);
                 #pragma unroll
-                for (int k = 0; k < 16; k++) { o[k][0] *= al0; o[k][1] *= al1; o[k][2] *= al0; o[k][3] *= al1; }
-            }
+                for (int off = 4; off < 32; off <<= 1) {
+                    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+                    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+                }
+                const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+                const float mu0 = mn0 == -INFINITY ? 0.0f : mn0, mu1 = mn1 == -INFINITY ? 0.0f : mn1;
+                const float al0 = exp2f(m0 - mu0), al1 = exp2f(m1 - mu1);
+                float p[4];
+                p[0] = exp2f(sc[0] - mu0); p[1] = exp2f(sc[1] - mu1);
+                p[2] = exp2f(sc[2] - mu0); p[3] = exp2f(sc[3] - mu1);
+                l0 = l0 * al0 + p[0] + p[2];
+                l1 = l1 * al1 + p[1] + p[3];
+                m0 = mn0; m1 = mn1;
+                if (__any_sync(0xffffffffu, al0 != 1.0f || al1 != 1.0f)) {   // the running max moved
+                    #pragma unroll
+                    for (int k = 0; k < 8; k++) { o[k][0] *= al0; o[k][1] *= al1; o[k][2] *= al0; o[k][3] *= al1; }
+                }
 
-            // ---- O^T += V^T P   (rows not fetched are masked: zero scale / zero values)
-            if (KV_TYPE == QSA_TYPE_Q8_0) {
-                const uint32_t * V0 = reinterpret_cast<const uint32_t *>(Vt + (c0 + 0) * rb);
-                const uint32_t * V1 = reinterpret_cast<const uint32_t *>(Vt + (c0 + 1) * rb);
-                const uint32_t * V8 = reinterpret_cast<const uint32_t *>(Vt + (c0 + 8) * rb);
-                const uint32_t * V9 = reinterpret_cast<const uint32_t *>(Vt + (c0 + 9) * rb);
-                const uint16_t * VA = reinterpret_cast<const uint16_t *>(Vt + rA * rb);
-                const uint16_t * VB = reinterpret_cast<const uint16_t *>(Vt + rB * rb);
-                #pragma unroll
-                for (int g8 = 0; g8 < 8; g8++) {
-                    float dA = f16_bits_to_f32(VA[17 * g8]);
-                    float dB = f16_bits_to_f32(VB[17 * g8]);
-                    dA = okA ? dA : 0.0f;
-                    dB = okB ? dB : 0.0f;
-                    uint32_t b[2];
-                    b[0] = movmatrix_trans(pack_f16x2(p[0] * dA, p[1] * dA));
-                    b[1] = movmatrix_trans(pack_f16x2(p[2] * dB, p[3] * dB));
-                    uint32_t W0, W1, W2, W3;
-                    if ((g8 & 1) == 0) {
-                        const int wi = 17 * (g8 / 2) + r8;
-                        W0 = __funnelshift_r(V0[wi], V0[wi + 1], 16);
-                        W1 = __funnelshift_r(V1[wi], V1[wi + 1], 16);
-                        W2 = __funnelshift_r(V8[wi], V8[wi + 1], 16);
-                        W3 = __funnelshift_r(V9[wi], V9[wi + 1], 16);
-                    } else {
-                        const int wi = 17 * (g8 / 2) + 9 + r8;
-                        W0 = V0[wi]; W1 = V1[wi]; W2 = V8[wi]; W3 = V9[wi];
+                // ---- O^T += V^T P over this warp's 128 dims (rows not fetched: zero scale / values)
+                if (KV_TYPE == QSA_TYPE_Q8_0) {
+                    const uint32_t * V0 = reinterpret_cast<const uint32_t *>(Vt + (c0 + 0) * rb) + 34 * dh;
+                    const uint32_t * V1 = reinterpret_cast<const uint32_t *>(Vt + (c0 + 1) * rb) + 34 * dh;
+                    const uint32_t * V8 = reinterpret_cast<const uint32_t *>(Vt + (c0 + 8) * rb) + 34 * dh;
+                    const uint32_t * V9 = reinterpret_cast<const uint32_t *>(Vt + (c0 + 9) * rb) + 34 * dh;
+                    const uint16_t * VA = reinterpret_cast<const uint16_t *>(Vt + rA * rb) + 68 * dh;
+                    const uint16_t * VB = reinterpret_cast<const uint16_t *>(Vt + rB * rb) + 68 * dh;
+                    #pragma unroll
+                    for (int gg = 0; gg < 4; gg++) {
+                        float dA = f16_bits_to_f32(VA[17 * gg]);
+                        float dB = f16_bits_to_f32(VB[17 * gg]);
+                        dA = okA ? dA : 0.0f;
+                        dB = okB ? dB : 0.0f;
+                        uint32_t b[2];
+                        b[0] = movmatrix_trans(pack_f16x2(p[0] * dA, p[1] * dA));
+                        b[1] = movmatrix_trans(pack_f16x2(p[2] * dB, p[3] * dB));
+                        uint32_t W0, W1, W2, W3;
+                        if ((gg & 1) == 0) {
+                            const int wi = 17 * (gg / 2) + r8;
+                            W0 = __funnelshift_r(V0[wi], V0[wi + 1], 16);
+                            W1 = __funnelshift_r(V1[wi], V1[wi + 1], 16);
+                            W2 = __funnelshift_r(V8[wi], V8[wi + 1], 16);
+                            W3 = __funnelshift_r(V9[wi], V9[wi + 1], 16);
+                        } else {
+                            const int wi = 17 * (gg / 2) + 9 + r8;
+                            W0 = V0[wi]; W1 = V1[wi]; W2 = V8[wi]; W3 = V9[wi];
+                        }
+                        // V + 1152 (exact f16 integers); the bias is removed from both 16-dim
+                        // tiles by -1152 x the column sums of the scaled P
+                        const uint32_t am0[4] = {i8_pair_biased<0>(W0, W1), i8_pair_biased<1>(W0, W1),
+                                                 i8_pair_biased<0>(W2, W3), i8_pair_biased<1>(W2, W3)};
+                        const uint32_t am1[4] = {i8_pair_biased<2>(W0, W1), i8_pair_biased<3>(W0, W1),
+                                                 i8_pair_biased<2>(W2, W3), i8_pair_biased<3>(W2, W3)};
+                        mma_f16_16816(o[2 * gg], negb, b);
+                        mma_f16_16816(o[2 * gg + 1], negb, b);
+                        mma_f16_16816(o[2 * gg], am0, b);
+                        mma_f16_16816(o[2 * gg + 1], am1, b);
                     }
-                    const uint32_t am0[4] = {i8_pair_to_f16x2<0>(W0, W1), i8_pair_to_f16x2<1>(W0, W1),
-                                             i8_pair_to_f16x2<0>(W2, W3), i8_pair_to_f16x2<1>(W2, W3)};
-                    const uint32_t am1[4] = {i8_pair_to_f16x2<2>(W0, W1), i8_pair_to_f16x2<3>(W0, W1),
-                                             i8_pair_to_f16x2<2>(W2, W3), i8_pair_to_f16x2<3>(W2, W3)};
-                    mma_f16_16816(o[2 * g8], am0, b);
-                    mma_f16_16816(o[2 * g8 + 1], am1, b);
-                }
-            } else {
-                uint32_t b[2];
-                b[0] = movmatrix_trans(pack_f16x2(p[0], p[1]));
-                b[1] = movmatrix_trans(pack_f16x2(p[2], p[3]));
-                const uint32_t m01 = (((vm >> c0) & 1ull) ? 0x0000ffffu : 0u) | (((vm >> (c0 + 1)) & 1ull) ? 0xffff0000u : 0u);
-                const uint32_t m89 = (((vm >> (c0 + 8)) & 1ull) ? 0x0000ffffu : 0u) | (((vm >> (c0 + 9)) & 1ull) ? 0xffff0000u : 0u);
-                const int cl = 16 * cw + (lane & 7) + ((lane >> 4) << 3);   // ldmatrix row: cell
-                const int dh = ((lane >> 3) & 1) << 3;                        // +8 dims for matrices 1, 3
-                #pragma unroll
-                for (int mt = 0; mt < 16; mt++) {
-                    uint32_t a[4];
-                    ldmatrix_x4_trans(a, Vt + cl * rb + 2 * (16 * mt + dh));
-                    a[0] &= m01; a[1] &= m01; a[2] &= m89; a[3] &= m89;
-                    mma_f16_16816(o[mt], a, b);
+                } else {
+                    uint32_t b[2];
+                    b[0] = movmatrix_trans(pack_f16x2(p[0], p[1]));
+                    b[1] = movmatrix_trans(pack_f16x2(p[2], p[3]));
+                    const uint32_t m01 = (((vm >> c0) & 1u) ? 0x0000ffffu : 0u) | (((vm >> (c0 + 1)) & 1u) ? 0xffff0000u : 0u);
+                    const uint32_t m89 = (((vm >> (c0 + 8)) & 1u) ? 0x0000ffffu : 0u) | (((vm >> (c0 + 9)) & 1u) ? 0xffff0000u : 0u);
+                    const int cl = 16 * cw + (lane & 7) + ((lane >> 4) << 3);   // ldmatrix row: cell
+                    const int d8 = ((lane >> 3) & 1) << 3;                        // +8 dims for matrices 1, 3
+                    #pragma unroll
+                    for (int mm = 0; mm < 8; mm++) {
+                        const int mt = 8 * dh + mm;
+                        uint32_t a[4];
+                        ldmatrix_x4_trans(a, Vt + cl * rb + 2 * (16 * mt + d8));
+                        a[0] &= m01; a[1] &= m01; a[2] &= m89; a[3] &= m89;
+                        mma_f16_16816(o[mm], a, b);
+                    }
                 }
             }
-        }
             // this warp is done with stage s: the producer may refill it
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty_bar[s]);
@@ -422,56 +458,54 @@ __global__ void __launch_bounds__(ATT_THREADS, AttnCfg<KV_TYPE>::MIN_CTAS) attn_
     }
     __syncthreads();                                  // every warp past its last tile: stages are free
 
-    // ---- merge the 2 warps of each KV head (stage memory is free)
+    // ---- merge the two 16-cell halves of each KV head (stage memory is free); the two dim-half
+    // warps of a pair carry the same (m, l)
     #pragma unroll
     for (int off = 4; off < 32; off <<= 1) {
         l0 += __shfl_xor_sync(0xffffffffu, l0, off);
         l1 += __shfl_xor_sync(0xffffffffu, l1, off);
     }
-    float * wm = reinterpret_cast<float *>(smem);               // [4 warps][8 heads] max
-    float * wl = wm + ATT_CWARPS * 8;                            // [4][8] sum
-    float * wf = wl + ATT_CWARPS * 8;                            // [4][8] merge factors
+    constexpr int HD2 = HEAD_DIM / 2;
+    float * wm = reinterpret_cast<float *>(smem);               // [8 warps][8 heads] max
+    float * wl = wm + ATT_CWARPS * 8;                            // [8][8] sum
+    float * wf = wl + ATT_CWARPS * 8;                            // [8][8] merge factors
     float * cml = wf + ATT_CWARPS * 8;                           // [16] M, [16] L of the CTA
-    float * wo = cml + 2 * HROWS;                                // [4][8][256] unnormalised O
+    float * wo = cml + 2 * HROWS;                                // [8][8][128] unnormalised O
     if (!producer) {
         if (r8 == 0) {
             wm[warp * 8 + 2 * j4] = m0; wm[warp * 8 + 2 * j4 + 1] = m1;
             wl[warp * 8 + 2 * j4] = l0; wl[warp * 8 + 2 * j4 + 1] = l1;
         }
-        float * myo = wo + warp * 8 * HEAD_DIM;
+        float * myo = wo + warp * 8 * HD2;
         if (KV_TYPE == QSA_TYPE_Q8_0) {
             #pragma unroll
-            for (int g8 = 0; g8 < 8; g8++) {
-                const int dim = 32 * g8 + 4 * r8;
-                *reinterpret_cast<float4 *>(myo + (2 * j4) * HEAD_DIM + dim) =
-                    make_float4(o[2 * g8][0], o[2 * g8][2], o[2 * g8 + 1][0], o[2 * g8 + 1][2]);
-                *reinterpret_cast<float4 *>(myo + (2 * j4 + 1) * HEAD_DIM + dim) =
-                    make_float4(o[2 * g8][1], o[2 * g8][3], o[2 * g8 + 1][1], o[2 * g8 + 1][3]);
+            for (int gg = 0; gg < 4; gg++) {
+                const int dim = 32 * gg + 4 * r8;
+                *reinterpret_cast<float4 *>(myo + (2 * j4) * HD2 + dim) =
+                    make_float4(o[2 * gg][0], o[2 * gg][2], o[2 * gg + 1][0], o[2 * gg + 1][2]);
+                *reinterpret_cast<float4 *>(myo + (2 * j4 + 1) * HD2 + dim) =
+                    make_float4(o[2 * gg][1], o[2 * gg][3], o[2 * gg + 1][1], o[2 * gg + 1][3]);
             }
         } else {
             #pragma unroll
-            for (int mt = 0; mt < 16; mt++) {
-                const int dim = 16 * mt + r8;
-                myo[(2 * j4) * HEAD_DIM + dim]         = o[mt][0];
-                myo[(2 * j4 + 1) * HEAD_DIM + dim]     = o[mt][1];
-                myo[(2 * j4) * HEAD_DIM + dim + 8]     = o[mt][2];
-                myo[(2 * j4 + 1) * HEAD_DIM + dim + 8] = o[mt][3];
+            for (int mm = 0; mm < 8; mm++) {
+                const int dim = 16 * mm + r8;
+                myo[(2 * j4) * HD2 + dim]         = o[mm][0];
+                myo[(2 * j4 + 1) * HD2 + dim]     = o[mm][1];
+                myo[(2 * j4) * HD2 + dim + 8]     = o[mm][2];
+                myo[(2 * j4 + 1) * HD2 + dim + 8] = o[mm][3];
             }
         }
     }
     __syncthreads();
-    if (tid < HROWS) {   // row hr = 8*head + h: M = max over the head's 2 warps, L = sum l 2^(m - M)
-        const int w0 = (tid >> 3) * 2, h = tid & 7;
-        float M = -INFINITY;
-        for (int w = w0; w < w0 + 2; w++) M = fmaxf(M, wm[w * 8 + h]);
+    if (tid < HROWS) {   // row hr = 8*head + h: M over the head's two cell halves, L = sum l 2^(m - M)
+        const int hh = tid >> 3, h = tid & 7;
+        const int wa = 4 * hh, wb = 4 * hh + 2;                  // (head, cells 0-15 / 16-31, dims 0-127)
+        const float M = fmaxf(wm[wa * 8 + h], wm[wb * 8 + h]);
         const float Mu = M == -INFINITY ? 0.0f : M;
-        float L = 0.0f;
-        for (int w = w0; w < w0 + 2; w++) {
-            const float f = exp2f(wm[w * 8 + h] - Mu);
-            wf[w * 8 + h] = f;
-            L += wl[w * 8 + h] * f;
-        }
-        cml[tid] = M; cml[HROWS + tid] = L;
+        const float fa = exp2f(wm[wa * 8 + h] - Mu), fb = exp2f(wm[wb * 8 + h] - Mu);
+        wf[wa * 8 + h] = fa; wf[wb * 8 + h] = fb;
+        cml[tid] = M; cml[HROWS + tid] = wl[wa * 8 + h] * fa + wl[wb * 8 + h] * fb;
     }
     __syncthreads();
     // ---- the CTA's state: the final output (one chunk), or a partial for attn_merge_kernel
@@ -479,14 +513,14 @@ __global__ void __launch_bounds__(ATT_THREADS, AttnCfg<KV_TYPE>::MIN_CTAS) attn_
     float * po = part_o + ((size_t) t * max_chunks + chunk) * HROWS * HEAD_DIM;
     const int n_rows = d.n_head_kv * 8;
     for (int e4 = tid; e4 < HROWS * HEAD_DIM / 4; e4 += ATT_THREADS) {
-        const int hr = (e4 * 4) / HEAD_DIM, w0 = (hr >> 3) * 2, h = hr & 7, d4 = e4 % (HEAD_DIM / 4);
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        #pragma unroll
-        for (int w = 0; w < 2; w++) {
-            const float f = wf[(w0 + w) * 8 + h];
-            const float4 v = reinterpret_cast<const float4 *>(wo + ((w0 + w) * 8 + h) * HEAD_DIM)[d4];
-            acc.x += f * v.x; acc.y += f * v.y; acc.z += f * v.z; acc.w += f * v.w;
-        }
+        const int hr = (e4 * 4) / HEAD_DIM, hh = hr >> 3, h = hr & 7, d4 = e4 % (HEAD_DIM / 4);
+        const int half = (d4 * 4) / HD2, dd4 = d4 % (HD2 / 4);
+        const int wa = 4 * hh + half, wb = 4 * hh + 2 + half;    // the two cell halves, this dim half
+        const float fa = wf[(4 * hh) * 8 + h], fb = wf[(4 * hh + 2) * 8 + h];
+        const float4 va = reinterpret_cast<const float4 *>(wo + (wa * 8 + h) * HD2)[dd4];
+        const float4 vb = reinterpret_cast<const float4 *>(wo + (wb * 8 + h) * HD2)[dd4];
+        const float4 acc = make_float4(fa * va.x + fb * vb.x, fa * va.y + fb * vb.y,
+                                       fa * va.z + fb * vb.z, fa * va.w + fb * vb.w);
         if (!single) {
             reinterpret_cast<float4 *>(po)[e4] = acc;
         } else if (stq) {
@@ -494,7 +528,7 @@ __global__ void __launch_bounds__(ATT_THREADS, AttnCfg<KV_TYPE>::MIN_CTAS) attn_
         } else if (hr < n_rows && h < d.gqa) {
             const float L = cml[HROWS + hr];
             const float inv = L > 0.0f ? 1.0f / L : 0.0f;
-            reinterpret_cast<float4 *>(outq + (size_t) (hr >> 3) * d.gqa * HEAD_DIM + (size_t) h * HEAD_DIM)[d4] =
+            reinterpret_cast<float4 *>(outq + (size_t) hh * d.gqa * HEAD_DIM + (size_t) h * HEAD_DIM)[d4] =
                 make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
         }
     }

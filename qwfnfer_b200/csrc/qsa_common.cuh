@@ -169,6 +169,17 @@ __device__ __forceinline__ uint32_t i8_pair_to_f16x2(uint32_t w0, uint32_t w1) {
     return i8x2_even_to_f16x2(t);
 }
 
+// The same conversions without the subtraction: each value comes out as the f16 1152 + x
+// (exact).  The bias is removed by one more MMA whose A operand is the constant -1152
+// (F16X2_NEG1152 in every register): it adds -1152 x (sum of the B column) to every row.
+constexpr uint32_t F16X2_NEG1152 = 0xE480E480u;
+__device__ __forceinline__ uint32_t i8x2_even_biased(uint32_t w) { return (w & 0x00FF00FFu) ^ 0x64806480u; }
+__device__ __forceinline__ uint32_t i8x2_odd_biased(uint32_t w) { return ((w >> 8) & 0x00FF00FFu) ^ 0x64806480u; }
+template <int B>
+__device__ __forceinline__ uint32_t i8_pair_biased(uint32_t w0, uint32_t w1) {
+    return i8x2_even_biased(__byte_perm(w0, w1, B | ((4 + B) << 8)));
+}
+
 // 32-bit load from shared memory at a 2-byte aligned address (q8_0 rows are 34-byte strided).
 __device__ __forceinline__ uint32_t lds_u32_a2(const uint8_t * p) {
     const uintptr_t a = reinterpret_cast<uintptr_t>(p);
