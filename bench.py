@@ -9,6 +9,7 @@ whole node: append of the token's K/V/raw key (+ the pooled key of the block it 
 indexer scores + top-k, and split-K attention.  Metric: microseconds per layer-token (lower is
 better).  Inputs are resident in HBM; L2 is flushed (256 MB write) before every timed step.
   --config 3: 64 sequences, lengths U[4096, 163840] (seed 2), one batched decode step.
+  --config 4: chunked prefill of 8192 tokens at position 155,648 (tok/s).
   --config 5: 12 layers at 1,048,576 tokens, top-128, one token through all 12 layers.
 With N > 1 GPUs (torchrun) each rank runs the workload on its own GPU ("replicas", config 2) or
 its share of the sequences (config 3, data parallel); value = total units / max-over-ranks time.
@@ -51,7 +52,7 @@ def profile_traffic(name: str):
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 20 ms while running."""
+    """nvidia-smi clocks and throttle reasons sampled every 5 ms while running."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
@@ -63,7 +64,7 @@ class ClockSampler:
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                                          "-lms", "20", "-i", self.gpu], stdout=subprocess.PIPE,
+                                          "-lms", "5", "-i", self.gpu], stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
@@ -315,7 +316,7 @@ def run_ours_config2(args, ws, rank, local):
         "gpu_launches": 3 * K,
         "clocks": clocks.summary(),
     }
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         kc = st.k[0][:n_past + 1].cpu().numpy()
         vc = st.v[0][:n_past + 1].cpu().numpy()
         pool = st.pool[0].cpu().numpy().view(np.uint16)
@@ -616,6 +617,110 @@ def run_ours_config5(args, ws, rank, local):
     return res
 
 
+def run_ours_config4(args, ws, rank, local):
+    """Chunked prefill: 8192 new tokens appended at position 155,648 of a
+    q8_0 cache; a step is one qsa_prefill call (append of the chunk's K/V/raw keys and pooled
+    keys, indexer scores of every query, per-query top-k + window, sparse attention)."""
+    import ctypes
+
+    import numpy as np
+    import torch
+
+    from qwfnfer_b200._abi import TYPE_BF16, check, k_blocks, lib
+    from qwfnfer_b200.configs import CONFIGS, fill_cache, token_inputs
+    from qwfnfer_b200.qsa import QsaNode, QsaState, _stream
+
+    cfg = CONFIGS[4]
+    d = cfg.desc()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    T, n_past = cfg.prefill_T, cfg.n_past
+    node, st = QsaNode(d, dev), QsaState(d, device=dev)
+    fill_cache(node, st, 0, n_past, cfg.seed + 17 * rank)
+    q, qi, k, v, ki = token_inputs(d, T, cfg.seed + 1000 + rank)
+    out = torch.empty(T, d.n_head, d.head_dim, device=dev)
+    KB = k_blocks(d)
+    sel = torch.empty(T, KB, dtype=torch.int32, device=dev)
+    wsb = node.workspace("prefill", T, n_past + T)
+    L, D = lib(), ctypes.byref(d)
+    cache = st.layer()
+
+    def step_api(stream_ptr, qq=q, qqi=qi, kk=k, vv=v, kki=ki, oo=out):
+        check(L.qsa_prefill(D, ctypes.byref(cache), n_past, T, qq.data_ptr(), TYPE_BF16, qqi.data_ptr(), kk.data_ptr(),
+                            vv.data_ptr(), kki.data_ptr(), oo.data_ptr(), sel.data_ptr(), wsb.data_ptr(), wsb.numel(),
+                            stream_ptr), "qsa_prefill")
+
+    for _ in range(args.warmup):
+        step_api(_stream(None))
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step_api(_stream(None))
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    K = args.steps
+    clocks = _clock_sampler(local)
+    clocks.start()
+    _timed_replays(g, 2, lambda i: flush.zero_())
+    if ws > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    clocks.mark("t0")
+    step_us = _timed_replays(g, K, lambda i: flush.zero_())
+    if ws > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    clocks.mark("t1")
+    # e2e: qsa_prefill with the chunk's inputs copied from pinned host memory and the output read back
+    hq, hqi, hk, hv, hki = (x.cpu().pin_memory() for x in (q, qi, k, v, ki))
+    hout = torch.empty_like(out, device="cpu").pin_memory()
+    sq, sqi, sk, sv, ski = (torch.empty_like(x) for x in (q, qi, k, v, ki))
+    e2e = []
+    for i in range(min(K, 5)):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for dst, src in zip((sq, sqi, sk, sv, ski), (hq, hqi, hk, hv, hki)):
+            dst.copy_(src, non_blocking=True)
+        step_api(torch.cuda.current_stream().cuda_stream, sq, sqi, sk, sv, ski, out)
+        hout.copy_(out, non_blocking=True)
+        b.record()
+        e2e.append((a, b))
+    torch.cuda.synchronize()
+    e2e_us = [a.elapsed_time(b) * 1e3 for a, b in e2e]
+    clocks.stop()
+    check(node.check(wsb), "qsa_check")
+    sel_h = sel.cpu().numpy()
+    cells = sum(attended_cells(sel_h[t], n_past + t, d.ratio) for t in range(0, T, 64)) * 64
+    nb = (n_past + T) // d.ratio
+    flops_idx = 2.0 * T * nb * d.idx_dim * d.idx_n_head
+    flops_attn = 4.0 * cells * d.n_head * d.head_dim
+    step_mean = statistics.mean(step_us)
+    total_us = max_over_ranks(step_mean, ws)
+    e2e_max = max_over_ranks(statistics.mean(e2e_us), ws)
+    _, tfs, src = peaks()
+    achieved = (flops_idx + flops_attn) / (step_mean * 1e-6) / 1e12
+    toks = T * ws
+    return {
+        "metric": "sparse-attn prefill tok/s @8192 on 155648 q8_0", "value": round(toks / (total_us * 1e-6), 1),
+        "unit": "tok/s", "n_gpus": ws, "steps": K, "warmup": args.warmup, "ms_per_step": round(total_us / 1e3, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "q8_0 KV, bf16 Q, f16 MMA / f32 softmax", "data": "synthetic",
+        "config": {"workload": "config4: one chunk of 8192 tokens at n_past 155648 (append + indexer + top-64 + window "
+                               "+ attention), q8_0", "global_batch": toks, "seq_len": n_past + T,
+                   "parallelism": f"replicas x{ws}" if ws > 1 else "1 GPU",
+                   "l2": "flushed (256 MB write) before every timed step; inputs exceed L2", "cuda_graph": True},
+        "roofline": {"bound": "tensor", "kernel": "whole qsa_prefill step (indexer + attention FLOPs)",
+                     "achieved": round(achieved, 2), "peak": tfs, "unit": "TFLOP/s", "frac": round(achieved / tfs, 4),
+                     "peak_source": f"{src} bf16_tflops (burst)", "traffic": None,
+                     "flops_per_step": flops_idx + flops_attn, "indexer_flops": flops_idx},
+        "e2e": {"value": round(toks / (e2e_max * 1e-6), 1), "unit": "tok/s",
+                "h2d_bytes_per_step": sum(x.numel() * x.element_size() for x in (q, qi, k, v, ki)),
+                "d2h_bytes_per_step": out.numel() * out.element_size()},
+        "gpu_launches": 5 * K,
+        "clocks": clocks.summary(),
+    }
+
+
 def run_reference_config2(args):
     """The reference's CPU algorithm (oracle port, ggml mode, all host cores) on config 2."""
     import numpy as np
@@ -680,7 +785,7 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 5])
+    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -701,6 +806,8 @@ def main():
         res = run_ours_config2(args, ws, rank, local)
     elif args.config == 3:
         res = run_ours_config3(args, ws, rank, local)
+    elif args.config == 4:
+        res = run_ours_config4(args, ws, rank, local)
     else:
         res = run_ours_config5(args, ws, rank, local)
     if rank == 0:

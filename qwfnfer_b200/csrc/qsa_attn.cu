@@ -80,7 +80,7 @@ __device__ __forceinline__ int attn_n_chunks(const DevDesc & d, int nsel, int ti
     return (n_tiles + tiles_per_cta - 1) / tiles_per_cta;
 }
 
-template <int KV_TYPE>
+template <int KV_TYPE, int NKV>
 __global__ void __launch_bounds__(ATT_THREADS, AttnCfg<KV_TYPE>::MIN_CTAS) attn_kernel(
         DevDesc d, const qsa_decode_item * __restrict__ items, qsa_layer_cache cache0, int n_past0,
         const void * __restrict__ q, int q_type,
@@ -103,7 +103,7 @@ __global__ void __launch_bounds__(ATT_THREADS, AttnCfg<KV_TYPE>::MIN_CTAS) attn_
     const int cw = (warp >> 1) & 1;           //   16-cell half of the tile,
     const int dh = warp & 1;                  //   128-dim half (q8_0 groups 4dh..4dh+3)
     const bool producer = warp == ATT_CWARPS;
-    const bool head_live = !producer && hs < d.n_head_kv;
+    const bool head_live = !producer && hs < NKV;
     int * sel = reinterpret_cast<int *>(smem + NS * attn_stage_bytes<KV_TYPE>());
     __half * qs = reinterpret_cast<__half *>(smem + NS * attn_stage_bytes<KV_TYPE>() + MAX_KB * 4);
     float4 * xch = reinterpret_cast<float4 *>(smem + NS * attn_stage_bytes<KV_TYPE>() + MAX_KB * 4 + HROWS * HEAD_DIM * 2);
@@ -161,7 +161,7 @@ __global__ void __launch_bounds__(ATT_THREADS, AttnCfg<KV_TYPE>::MIN_CTAS) attn_
     const bool pos_ok = qpos >= 0 && qpos < d.n_ctx;
     const int nsel = pos_ok ? max(0, min(nsel_raw, d.kb)) : 0;
     const int r = d.ratio;
-    const int RBr = (int) d.rb_k;                        // cache row bytes: the run copies' row pitch
+    constexpr int RBr = NKV * HB;                        // cache row bytes: the run copies' row pitch
     const int n_cells = nsel * r;
     const int n_tiles = (n_cells + ATT_CELLS - 1) / ATT_CELLS;
     const int n_chunks = attn_n_chunks(d, nsel, tiles_per_cta);
@@ -289,7 +289,7 @@ __global__ void __launch_bounds__(ATT_THREADS, AttnCfg<KV_TYPE>::MIN_CTAS) attn_
         const int rA = 16 * cw + r8, rB = rA + 8;           // this thread's S^T rows (cells of the tile)
         const int c0 = 16 * cw + 2 * j4;                     // this thread's V^T columns: c0+{0,1,8,9}
         const int hoff = hs * HB;                            // byte offset of this warp's head in a row
-        const int rb = (int) d.rb_k;                         // row bytes (= smem row stride), K and V alike
+        constexpr int rb = NKV * HB;                         // row bytes (= smem row stride), K and V alike
         // this warp's Q fragments (its 8 k-steps of 16 dims) stay in registers for the whole loop
         uint2 qreg[8];
         #pragma unroll
@@ -618,12 +618,17 @@ __global__ void __launch_bounds__(MERGE_THREADS) attn_merge_kernel(DevDesc d, co
     }
 }
 
+template <int KV_TYPE, int NKV>
+cudaError_t attn_set_attr_one() {
+    return cudaFuncSetAttribute(attn_kernel<KV_TYPE, NKV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                attn_smem_bytes<KV_TYPE>());
+}
+
 cudaError_t attn_set_attrs() {
-    cudaError_t e = cudaFuncSetAttribute(attn_kernel<QSA_TYPE_Q8_0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         attn_smem_bytes<QSA_TYPE_Q8_0>());
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(attn_kernel<QSA_TYPE_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 attn_smem_bytes<QSA_TYPE_F16>());
+    cudaError_t e = attn_set_attr_one<QSA_TYPE_Q8_0, 2>();
+    if (e == cudaSuccess) e = attn_set_attr_one<QSA_TYPE_Q8_0, 1>();
+    if (e == cudaSuccess) e = attn_set_attr_one<QSA_TYPE_F16, 2>();
+    if (e == cudaSuccess) e = attn_set_attr_one<QSA_TYPE_F16, 1>();
     return e;
 }
 
@@ -649,15 +654,12 @@ cudaError_t launch_attn(const DevDesc & d, cudaStream_t st, int n_q, const qsa_d
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     cudaError_t e;
-    if (d.type_k == QSA_TYPE_Q8_0) {
-        cfg.dynamicSmemBytes = attn_smem_bytes<QSA_TYPE_Q8_0>();
-        e = cudaLaunchKernelEx(&cfg, attn_kernel<QSA_TYPE_Q8_0>, d, items, cache0, n_past0, q, q_type, sel_ws,
-                               nsel_ws, tiles_per_cta, max_chunks, part_o, part_ml, out, status, state_out);
-    } else {
-        cfg.dynamicSmemBytes = attn_smem_bytes<QSA_TYPE_F16>();
-        e = cudaLaunchKernelEx(&cfg, attn_kernel<QSA_TYPE_F16>, d, items, cache0, n_past0, q, q_type, sel_ws,
-                               nsel_ws, tiles_per_cta, max_chunks, part_o, part_ml, out, status, state_out);
-    }
+    cfg.dynamicSmemBytes = d.type_k == QSA_TYPE_Q8_0 ? attn_smem_bytes<QSA_TYPE_Q8_0>() : attn_smem_bytes<QSA_TYPE_F16>();
+#define QSA_LAUNCH_ATTN(T, N) cudaLaunchKernelEx(&cfg, attn_kernel<T, N>, d, items, cache0, n_past0, q, q_type, sel_ws, \
+                                                 nsel_ws, tiles_per_cta, max_chunks, part_o, part_ml, out, status, state_out)
+    if (d.type_k == QSA_TYPE_Q8_0) e = d.n_head_kv == 2 ? QSA_LAUNCH_ATTN(QSA_TYPE_Q8_0, 2) : QSA_LAUNCH_ATTN(QSA_TYPE_Q8_0, 1);
+    else                           e = d.n_head_kv == 2 ? QSA_LAUNCH_ATTN(QSA_TYPE_F16, 2) : QSA_LAUNCH_ATTN(QSA_TYPE_F16, 1);
+#undef QSA_LAUNCH_ATTN
     if (e != cudaSuccess || max_chunks <= 1) return e;
     cudaLaunchConfig_t mc = cfg;
     mc.gridDim = dim3((unsigned) n_q, HROWS, HEAD_DIM / (4 * MERGE_COLS));

@@ -100,13 +100,15 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t * bar, uint32_t b
     asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;"
                  :: "r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
-// One probe of the phase; returns true when the phase with `parity` has completed.
+// One probe of the phase; returns true when the phase with `parity` has completed.  A thread
+// whose phase is still open is suspended in hardware until it completes or about 20 us pass (the
+// time hint), so waiting costs few instructions.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t * bar, uint32_t parity) {
     uint32_t done;
     asm volatile("{\n\t.reg .pred p;\n\t"
-                 "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+                 "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
                  "selp.u32 %0, 1, 0, p;\n\t}"
-                 : "=r"(done) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+                 : "=r"(done) : "r"(smem_u32(bar)), "r"(parity), "r"(20000u) : "memory");
     return done != 0;
 }
 __device__ __forceinline__ uint64_t global_timer_ns() {
