@@ -361,7 +361,20 @@ qsa_status qsa_prefill(const qsa_desc * dd, const qsa_layer_cache * cache, int32
         if ((s = qsa_append(dd, cache, n_past, T, k_new, v_new, kidx_new, stream)) != QSA_OK) return s;
     }
     unsigned char * wsb = static_cast<unsigned char *>(ws);
-    if ((s = launch_select(d, w, T, nullptr, *cache, n_past, q_idx, sel_out, wsb, st)) != QSA_OK) return s;
+    if (d.idx_n_head == 1 || d.idx_n_head == 2 || d.idx_n_head == 4) {
+        // scores of every query of the chunk against every block whole at its end on the tensor
+        // cores, then one warp per query selects
+        uint32_t * status = reinterpret_cast<uint32_t *>(wsb + w.status);
+        float * scores = reinterpret_cast<float *>(wsb + w.scores);
+        cudaError_t e = launch_prefill_scores_tc(d, st, q_idx, T, cache->pool, (n_past + T) / d.ratio, scores,
+                                                 w.scores_stride, status);
+        if (e == cudaSuccess)
+            e = launch_select_scores_warp(d, st, n_past, T, scores, w.scores_stride, reinterpret_cast<int *>(wsb + w.sel),
+                                          reinterpret_cast<int *>(wsb + w.nsel), sel_out, status);
+        if (e != cudaSuccess) return QSA_ERR_CUDA;
+    } else if ((s = launch_select(d, w, T, nullptr, *cache, n_past, q_idx, sel_out, wsb, st)) != QSA_OK) {
+        return s;
+    }
     return launch_attend(d, w, T, nullptr, *cache, n_past, q, q_type, out, wsb, st);
 }
 

@@ -37,6 +37,14 @@ int attn_state_rows();
 // Attention CTAs resident on the GPU at once for a KV type (the CTAs of one wave).
 int attn_resident_ctas(int type_k);
 
+// Prefill indexer scores on tcgen05 (idx_n_head 1, 2 or 4) and the warp-per-query selection over
+// precomputed scores (qsa_prefill_tc.cu).
+cudaError_t launch_prefill_scores_tc(const DevDesc & d, cudaStream_t st, const float * q_idx, int T,
+                                     const uint16_t * pool, int n_blocks, float * scores, int scores_stride,
+                                     uint32_t * status);
+cudaError_t launch_select_scores_warp(const DevDesc & d, cudaStream_t st, int n_past0, int T, const float * scores,
+                                      int scores_stride, int * sel_ws, int * nsel_ws, int * sel_out, uint32_t * status);
+
 // KV-sequence-sharded decode: global selection from all shards' candidates, and the log-sum-exp
 // merge of the shards' attention states (qsa_shard.cu).
 cudaError_t launch_shard_select(const DevDesc & d, cudaStream_t st, const qsa_decode_item * items, int n_shards,

@@ -1,0 +1,330 @@
+// qsa_prefill_tc.cu -- prefill indexer scores on the 5th-generation tensor cores, and a
+// warp-per-query top-k over precomputed scores.
+//
+// Reference: the prefill scores of graph_builder::qsa_top_k (src/qwfn_graph.cpp:277-293): one
+// [n_blocks x (idx_n_head*T)] product of the pooled keys with the indexer queries, relu per head,
+// sum over heads; then ggml_top_k per query (:295-306) over score + bias, whose rule
+// (src/qwfn_engine.cpp:936-950) the selection below applies directly.
+//
+// idx_scores_tc_kernel: CTA tile = 128 (query, head) rows x 256 blocks x 128 dims.  The indexer
+// queries (f32, rounded to f16 as the reference's vec_dot conversion does) and the F16 pooled keys
+// are written to shared memory in the 128-byte-swizzled K-major layout, one elected thread issues
+// 8 tcgen05.mma (kind::f16, M=128, N=256, K=16) into a 256-column TMEM accumulator and commits to an
+// mbarrier; 8 warps read the accumulator back (tcgen05.ld 32x32b), apply relu, sum the heads of a
+// query across lanes and store f32 scores.  Products of f16 values are exact; the sums are f32
+// (the reference sums in f32 as well), so scores can differ from an exactly rounded sum by a few
+// ulp and the selection only at near-ties.
+//
+// select_scores_warp_kernel: one warp per query.  Keys are the bit patterns of the non-negative
+// scores of the candidate blocks (visible and not forced); a radix select with 8-bit digits from
+// the top finds the cut, then lanes, each owning a contiguous run of blocks, emit the kept blocks
+// in ascending order (equal keys at the cut kept by lower block index), then the forced blocks.
+#include "qsa_kernels.cuh"
+
+namespace qsa {
+
+constexpr int TC_M = 128;                 // rows (query, head) per CTA
+constexpr int TC_N = 256;                 // blocks per CTA
+constexpr int TC_K = 128;                 // indexer dims (MAX_IDX_DIM)
+constexpr int TC_THREADS = 256;
+constexpr int TC_A_BYTES = TC_M * TC_K * 2;      // 32 KB
+constexpr int TC_B_BYTES = TC_N * TC_K * 2;      // 64 KB
+constexpr int TC_SMEM = TC_A_BYTES + TC_B_BYTES + 1024;   // + alignment slack for the 1024-byte swizzle atoms
+
+// Byte offset of the 16-byte chunk c (k = 8c .. 8c+7) of row r in a K-major, 128-byte-swizzled
+// tile of `rows` rows and 128 f16 columns: two atoms of 64 columns, each rows x 128 B in groups of 8
+// rows (1024 B); inside a group, chunk c of row r sits at chunk position c ^ (r % 8).
+__device__ __forceinline__ uint32_t sw128_offset(int rows, int r, int c) {
+    const int atom = c >> 3, cc = c & 7;
+    return (uint32_t) (atom * rows * 128 + (r >> 3) * 1024 + (r & 7) * 128 + ((cc ^ (r & 7)) << 4));
+}
+
+// Shared-memory matrix descriptor (tcgen05): start address >> 4, leading byte offset 1 (unused for
+// swizzled K-major), stride byte offset 1024 >> 4 between 8-row groups, version 1, layout
+// SWIZZLE_128B (2).
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr) {
+    return (uint64_t) ((smem_addr >> 4) & 0x3FFFu) | ((uint64_t) 1 << 16) | ((uint64_t) 64 << 32) |
+           ((uint64_t) 1 << 46) | ((uint64_t) 2 << 61);
+}
+
+// Instruction descriptor, kind::f16: D f32, A and B f16, both K-major, N = 256, M = 128.
+constexpr uint32_t TC_IDESC = (1u << 4) | ((uint32_t) (TC_N >> 3) << 17) | ((uint32_t) (TC_M >> 4) << 24);
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__global__ void __launch_bounds__(TC_THREADS) idx_scores_tc_kernel(DevDesc d, const float * __restrict__ q_idx,
+        int n_rows, const uint16_t * __restrict__ pool, int n_blocks, float * __restrict__ scores, int scores_stride,
+        uint32_t * __restrict__ status) {
+    extern __shared__ __align__(1024) unsigned char tc_smem_raw[];
+    __shared__ uint64_t mma_bar;
+    __shared__ uint32_t tmem_slot;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int row0 = blockIdx.x * TC_M, blk0 = blockIdx.y * TC_N;
+    // 1024-byte aligned operand tiles
+    const uint32_t raw = smem_u32(tc_smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    unsigned char * sA = tc_smem_raw + (base - raw);
+    unsigned char * sB = sA + TC_A_BYTES;
+
+    if (warp == 0) {                          // TMEM accumulator: 128 lanes x 256 f32 columns
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     :: "r"(smem_u32(&tmem_slot)), "r"(TC_N) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    if (tid == 0) {
+        mbar_init(&mma_bar, 1);
+        fence_mbar_init();
+    }
+    // A: (query, head) rows of the indexer query, f32 -> f16 (RNE), 16-byte chunks
+    for (int i = tid; i < TC_M * (TC_K / 8); i += TC_THREADS) {
+        const int r = i >> 4, c = i & 15;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (row0 + r < n_rows) {
+            const float4 * src = reinterpret_cast<const float4 *>(q_idx + (size_t) (row0 + r) * TC_K + 8 * c);
+            const float4 a = __ldg(src), b = __ldg(src + 1);
+            v.x = pack_f16x2(a.x, a.y); v.y = pack_f16x2(a.z, a.w);
+            v.z = pack_f16x2(b.x, b.y); v.w = pack_f16x2(b.z, b.w);
+        }
+        *reinterpret_cast<uint4 *>(sA + sw128_offset(TC_M, r, c)) = v;
+    }
+    // B: pooled keys of blocks blk0 .. blk0+255 (already F16)
+    for (int i = tid; i < TC_N * (TC_K / 8); i += TC_THREADS) {
+        const int r = i >> 4, c = i & 15;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (blk0 + r < n_blocks) v = __ldg(reinterpret_cast<const uint4 *>(pool + (size_t) (blk0 + r) * TC_K + 8 * c));
+        *reinterpret_cast<uint4 *>(sB + sw128_offset(TC_N, r, c)) = v;
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // operands visible to the tensor core
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+    if (tid == 0) {
+        #pragma unroll
+        for (int k = 0; k < TC_K / 16; k++) {
+            // k-step k: columns 16k .. 16k+15 = atom k/4, byte offset 32 (k%4) inside the swizzled rows
+            const uint64_t da = umma_desc_sw128(base + (uint32_t) ((k >> 2) * TC_M * 128 + (k & 3) * 32));
+            const uint64_t db = umma_desc_sw128(base + TC_A_BYTES + (uint32_t) ((k >> 2) * TC_N * 128 + (k & 3) * 32));
+            const uint32_t acc = k > 0 ? 1u : 0u;
+            asm volatile("{\n\t.reg .pred p;\n\t"
+                         "setp.ne.b32 p, %4, 0;\n\t"
+                         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}"
+                         :: "r"(tmem), "l"(da), "l"(db), "r"(TC_IDESC), "r"(acc), "r"(0u) : "memory");
+        }
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                     :: "r"(smem_u32(&mma_bar)) : "memory");
+    }
+    const bool ok = mbar_wait_bounded(&mma_bar, 0, status);
+    tc_fence_after();
+    // Epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 (its rows), columns 128 (w / 4) .. +127.
+    const int H = d.idx_n_head;
+    const int sub = warp & 3, chalf = warp >> 2;
+    const int r = sub * 32 + lane;                     // tile row = TMEM lane
+    const int grow = row0 + r;                         // global (query, head) row
+    const int t = grow / H, h = grow - t * H;
+    #pragma unroll 1
+    for (int c0 = chalf * 128; c0 < chalf * 128 + 128; c0 += 32) {
+        uint32_t v[32];
+        const uint32_t taddr = tmem + ((uint32_t) (sub * 32) << 16) + (uint32_t) c0;
+        asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+                     "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                     "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                     : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+                       "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+                       "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+                       "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+                     : "r"(taddr));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        float s[32];
+        #pragma unroll
+        for (int j = 0; j < 32; j++) {
+            const float x = __uint_as_float(v[j]);
+            s[j] = x > 0.0f ? x : 0.0f;                // relu per head
+        }
+        // sum over the heads of a query: its H rows are consecutive lanes (H divides 32)
+        for (int off = 1; off < H; off <<= 1)
+            #pragma unroll
+            for (int j = 0; j < 32; j++) s[j] += __shfl_xor_sync(0xffffffffu, s[j], off);
+        if (ok && h == 0 && grow < n_rows) {
+            float * dst = scores + (size_t) t * scores_stride + blk0 + c0;
+            const int nvalid = min(32, n_blocks - (blk0 + c0));
+            if (nvalid == 32) {
+                #pragma unroll
+                for (int j = 0; j < 32; j += 4)
+                    *reinterpret_cast<float4 *>(dst + j) = make_float4(s[j], s[j + 1], s[j + 2], s[j + 3]);
+            } else {
+                for (int j = 0; j < nvalid; j++) dst[j] = s[j];
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(TC_N) : "memory");
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+constexpr int SELW_WARPS = 8;             // queries per CTA
+
+// One warp per query t (prefill: position n_past0 + t); scores row t of `scores` (stride
+// scores_stride) holds the candidates' head-summed relu scores.
+__global__ void __launch_bounds__(32 * SELW_WARPS) select_scores_warp_kernel(DevDesc d, int n_past0, int n_q,
+        const float * __restrict__ scores, int scores_stride, int * __restrict__ sel_ws, int * __restrict__ nsel_ws,
+        int * __restrict__ sel_out, uint32_t * __restrict__ status) {
+    __shared__ unsigned hist[SELW_WARPS][256];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * SELW_WARPS + warp;
+    if (t >= n_q) return;
+    const int q = n_past0 + t;
+    int * sel = sel_ws + (size_t) t * d.kb;
+    int * so = sel_out ? sel_out + (size_t) t * d.kb : nullptr;
+    if (q < 0 || q >= d.n_ctx || (q + 1) / d.ratio > scores_stride) {
+        if (lane == 0) { set_status(status, DEV_BAD_POS); nsel_ws[t] = 0; }
+        for (int i = lane; i < d.kb; i += 32) { sel[i] = -1; if (so) so[i] = -1; }
+        return;
+    }
+    const int n_vis = (q + 1) / d.ratio;
+    const int bq = q / d.ratio;
+    int f_lo, f_hi;
+    if (d.window > 0) { f_lo = max(0, bq - d.n_force + 1); f_hi = bq; }
+    else if ((q + 1) % d.ratio != 0) { f_lo = bq; f_hi = bq; }
+    else { f_lo = 1; f_hi = 0; }
+    const int n_forced = f_hi >= f_lo ? f_hi - f_lo + 1 : 0;
+    const int cand_hi = n_forced ? min(n_vis, f_lo) : n_vis;   // candidates: [0, cand_hi)
+    const int want = max(0, d.kb - n_forced);
+    const float * sc = scores + (size_t) t * scores_stride;
+    // lane-owned contiguous run of candidate blocks
+    const int per = (cand_hi + 31) / 32;
+    const int lo = min(cand_hi, lane * per), hi = min(cand_hi, lo + per);
+    uint32_t prefix = 0, pmask = 0;
+    int remaining = want;
+    const bool take_none = want == 0;
+    const bool take_all = !take_none && cand_hi <= want;
+    unsigned * hw = hist[warp];
+    if (!take_all && !take_none) {
+        for (int shift = 24; shift >= 0; shift -= 8) {
+            for (int i = lane; i < 256; i += 32) hw[i] = 0;
+            __syncwarp();
+            for (int b = lo; b < hi; b++) {
+                const uint32_t key = __float_as_uint(__ldg(sc + b));
+                if ((key & pmask) == prefix) atomicAdd(&hw[(key >> shift) & 255u], 1u);
+            }
+            __syncwarp();
+            // lane owns bins 255-8*lane .. 248-8*lane (from the top); suffix counts across lanes
+            int own = 0;
+            #pragma unroll
+            for (int k = 0; k < 8; k++) own += (int) hw[255 - 8 * lane - k];
+            int incl = own;
+            #pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += y;
+            }
+            const int above = incl - own;
+            const unsigned hit = __ballot_sync(0xffffffffu, above < remaining && incl >= remaining);
+            const int src = __ffs(hit) - 1;
+            int bin = 0, cut_rem = 0;
+            if (lane == src) {
+                int cum = above;
+                int k = 0;
+                for (; k < 8; k++) {
+                    const int hc = (int) hw[255 - 8 * lane - k];
+                    if (cum + hc >= remaining) break;
+                    cum += hc;
+                }
+                bin = 255 - 8 * lane - k;
+                cut_rem = remaining - cum;
+            }
+            bin = __shfl_sync(0xffffffffu, bin, src);
+            cut_rem = __shfl_sync(0xffffffffu, cut_rem, src);
+            prefix |= (uint32_t) bin << shift;
+            pmask |= 255u << shift;
+            remaining = cut_rem;
+            __syncwarp();
+        }
+    }
+    // keys above the cut are kept; keys equal to it (all 32 bits) by lower block index, `remaining` of them
+    auto cmp = [&](int b) -> int {                       // 1 above, 0 equal, -1 below
+        const uint32_t key = __float_as_uint(__ldg(sc + b));
+        return key > prefix ? 1 : (key == prefix ? 0 : -1);
+    };
+    int n_take = 0, n_eq = 0;
+    if (take_all) {
+        n_take = hi - lo;
+    } else if (!take_none) {
+        for (int b = lo; b < hi; b++) {
+            const int c = cmp(b);
+            n_take += c > 0;
+            n_eq += c == 0;
+        }
+    }
+    // ties before this lane's run
+    int eq_incl = n_eq;
+    #pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, eq_incl, o);
+        if (lane >= o) eq_incl += y;
+    }
+    const int eq_before = eq_incl - n_eq;
+    const int eq_mine = (take_all || take_none) ? 0 : max(0, min(n_eq, remaining - eq_before));
+    const int mine = n_take + eq_mine;
+    int pos_incl = mine;
+    #pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, pos_incl, o);
+        if (lane >= o) pos_incl += y;
+    }
+    int pos = pos_incl - mine;
+    const int n_cand_taken = __shfl_sync(0xffffffffu, pos_incl, 31);
+    int eq_left = eq_mine;
+    for (int b = take_none ? hi : lo; b < hi; b++) {
+        bool tk;
+        if (take_all) tk = true;
+        else {
+            const int c = cmp(b);
+            tk = c > 0 || (c == 0 && eq_left > 0);
+            if (c == 0 && eq_left > 0) eq_left--;
+        }
+        if (tk) {
+            if (pos < d.kb) { sel[pos] = b; if (so) so[pos] = b; }
+            pos++;
+        }
+    }
+    // forced blocks follow (they are above every candidate)
+    for (int i = lane; i < n_forced; i += 32) {
+        const int p = n_cand_taken + i;
+        if (p < d.kb) { sel[p] = f_lo + i; if (so) so[p] = f_lo + i; }
+    }
+    const int n = min(d.kb, n_cand_taken + n_forced);
+    for (int i = n + lane; i < d.kb; i += 32) { sel[i] = -1; if (so) so[i] = -1; }
+    if (lane == 0) nsel_ws[t] = n;
+}
+
+cudaError_t launch_prefill_scores_tc(const DevDesc & d, cudaStream_t st, const float * q_idx, int T,
+                                     const uint16_t * pool, int n_blocks, float * scores, int scores_stride,
+                                     uint32_t * status) {
+    static bool attr = false;
+    if (!attr) {
+        cudaError_t e = cudaFuncSetAttribute(idx_scores_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM);
+        if (e != cudaSuccess) return e;
+        attr = true;
+    }
+    const int n_rows = T * d.idx_n_head;
+    const dim3 grid((unsigned) ((n_rows + TC_M - 1) / TC_M), (unsigned) ((n_blocks + TC_N - 1) / TC_N));
+    if (n_blocks <= 0) return cudaSuccess;
+    idx_scores_tc_kernel<<<grid, TC_THREADS, TC_SMEM, st>>>(d, q_idx, n_rows, pool, n_blocks, scores, scores_stride,
+                                                            status);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_select_scores_warp(const DevDesc & d, cudaStream_t st, int n_past0, int T, const float * scores,
+                                      int scores_stride, int * sel_ws, int * nsel_ws, int * sel_out, uint32_t * status) {
+    select_scores_warp_kernel<<<(T + SELW_WARPS - 1) / SELW_WARPS, 32 * SELW_WARPS, 0, st>>>(
+        d, n_past0, T, scores, scores_stride, sel_ws, nsel_ws, sel_out, status);
+    return cudaGetLastError();
+}
+
+}  // namespace qsa

@@ -210,8 +210,16 @@ def test_decode_equals_prefill_at_same_position():
     sel = torch.empty(1, k_blocks(d), dtype=torch.int32, device="cuda")
     out = node.sparse_attn_decode(decode_items([st.layer()], [n_past + t]), 1, n_past + T, q[t:t + 1],
                                   q_idx[t:t + 1], k[t:t + 1], v[t:t + 1], ki[t:t + 1], sel_out=sel)
-    assert np.array_equal(sel.cpu().numpy()[0], sel_p[t])
-    assert rel_err(out.cpu().numpy()[0], out_p[t]) <= ATTN_TOL
+    sel_d = sel.cpu().numpy()[0]
+    # decode scores are exactly rounded, prefill scores are tensor-core f32 sums: both selections
+    # equal the oracle's outside near-ties, and the outputs agree whenever the selections do
+    _, _, _, pool = host_caches(st, 0, n_past + T)
+    qp = n_past + t
+    sc = oracle.scores(d, pool, (qp + 1) // 64, q_idx[t].cpu().numpy())[0]
+    check_selection(d, sel_d, sc, qp)
+    check_selection(d, sel_p[t], sc, qp)
+    if np.array_equal(sel_d, sel_p[t]):
+        assert rel_err(out.cpu().numpy()[0], out_p[t]) <= ATTN_TOL
 
 
 def test_out_of_range_position_is_reported_not_faulted():
