@@ -71,6 +71,14 @@ __device__ __forceinline__ void named_bar_sync(int id, int n) {
     asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(n) : "memory");
 }
 
+// 2^x with the hardware approximation (relative error below 2^-22; -inf gives 0): the softmax
+// weights of the streaming loop.
+__device__ __forceinline__ float ex2_fast(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 // Cell of list entry `idx` of a query (cells of the selected blocks, in order).
 __device__ __forceinline__ int list_cell(const int * sel, int r, int idx) { return sel[idx / r] * r + idx % r; }
 
@@ -244,7 +252,9 @@ __global__ void __launch_bounds__(ATT_THREADS, AttnCfg<KV_TYPE>::MIN_CTAS) attn_
     float o[8][4];                                       // this warp's 128 dims x 8 heads
     #pragma unroll
     for (int i = 0; i < 8; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
-    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+    // running reference maxima of the thread's two heads (log2 domain; finite start, so that a
+    // weight 2^(s - m) never needs a guard), and the sums of weights
+    float m0 = -1e30f, m1 = -1e30f, l0 = 0.0f, l1 = 0.0f;
 
     if (producer) {
         // Tile i goes to stage i % NS: one copy per block-run of valid rows (cells <= the query
@@ -269,7 +279,9 @@ __global__ void __launch_bounds__(ATT_THREADS, AttnCfg<KV_TYPE>::MIN_CTAS) attn_
             #pragma unroll
             for (int off = 16; off > 0; off >>= 1) bytes += __shfl_xor_sync(0xffffffffu, bytes, off);
             const int ea = e_lo + lane;
-            const unsigned vm = __ballot_sync(0xffffffffu, ea < n_cells && list_cell(sel, r, ea) <= qpos);
+            // r a multiple of the tile: the whole tile lies in block j_lo (no per-lane division)
+            const int cell = (r % ATT_CELLS == 0) ? sel[j_lo] * r + (e_lo - j_lo * r) + lane : list_cell(sel, r, ea);
+            const unsigned vm = __ballot_sync(0xffffffffu, ea < n_cells && cell <= qpos);
             if (lane == 0) {
                 vmask[s] = vm;
                 mbar_arrive_expect_tx(&full_bar[s], bytes);
@@ -380,19 +392,23 @@ __global__ void __launch_bounds__(ATT_THREADS, AttnCfg<KV_TYPE>::MIN_CTAS) attn_
                     mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
                     mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
                 }
-                const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-                const float mu0 = mn0 == -INFINITY ? 0.0f : mn0, mu1 = mn1 == -INFINITY ? 0.0f : mn1;
-                const float al0 = exp2f(m0 - mu0), al1 = exp2f(m1 - mu1);
-                float p[4];
-                p[0] = exp2f(sc[0] - mu0); p[1] = exp2f(sc[1] - mu1);
-                p[2] = exp2f(sc[2] - mu0); p[3] = exp2f(sc[3] - mu1);
-                l0 = l0 * al0 + p[0] + p[2];
-                l1 = l1 * al1 + p[1] + p[3];
-                m0 = mn0; m1 = mn1;
-                if (__any_sync(0xffffffffu, al0 != 1.0f || al1 != 1.0f)) {   // the running max moved
+                // lazy rescale: the reference max moves only when a score exceeds it by more than 8
+                // (weights stay below 2^8, well inside f16 and f32), so O and l are rescaled a few
+                // times per query instead of at every new maximum
+                const bool up0 = mx0 > m0 + 8.0f, up1 = mx1 > m1 + 8.0f;
+                if (__any_sync(0xffffffffu, up0 || up1)) {
+                    const float mn0 = up0 ? mx0 : m0, mn1 = up1 ? mx1 : m1;
+                    const float al0 = ex2_fast(m0 - mn0), al1 = ex2_fast(m1 - mn1);
                     #pragma unroll
                     for (int k = 0; k < 8; k++) { o[k][0] *= al0; o[k][1] *= al1; o[k][2] *= al0; o[k][3] *= al1; }
+                    l0 *= al0; l1 *= al1;
+                    m0 = mn0; m1 = mn1;
                 }
+                float p[4];
+                p[0] = ex2_fast(sc[0] - m0); p[1] = ex2_fast(sc[1] - m1);
+                p[2] = ex2_fast(sc[2] - m0); p[3] = ex2_fast(sc[3] - m1);
+                l0 += p[0] + p[2];
+                l1 += p[1] + p[3];
 
                 // ---- O^T += V^T P over this warp's 128 dims (rows not fetched: zero scale / values)
                 if (KV_TYPE == QSA_TYPE_Q8_0) {
