@@ -36,7 +36,7 @@ constexpr int MERGE_THREADS = 256;     // attn_merge_kernel: threads per CTA
 template <int KV_TYPE> struct AttnCfg;
 template <> struct AttnCfg<QSA_TYPE_Q8_0> {
     static constexpr int HB       = 272;   // one head of a q8_0 row: 8 blocks x 34 B
-    static constexpr int NSTAGE   = 2;     // 2 x 34.8 KB stages: two CTAs fit one SM's 228 KB
+    static constexpr int NSTAGE   = 3;     // 3 x 34.8 KB stages: two CTAs fit one SM's 228 KB
     static constexpr int MIN_CTAS = 2;     // CTAs per SM
 };
 template <> struct AttnCfg<QSA_TYPE_F16> {
@@ -50,11 +50,15 @@ template <int KV_TYPE> constexpr int attn_row_bytes() { return 2 * AttnCfg<KV_TY
 template <int KV_TYPE> constexpr int attn_stage_bytes() { return 2 * ATT_CELLS * attn_row_bytes<KV_TYPE>(); }
 // S exchange between the two dim-half warps of a pair: [2 tiles][consumer warps][32 lanes] float4
 constexpr int ATT_XCH_BYTES = 2 * ATT_CWARPS * 32 * 16;
-template <int KV_TYPE> constexpr int attn_smem_bytes() {
-    return AttnCfg<KV_TYPE>::NSTAGE * attn_stage_bytes<KV_TYPE>() + MAX_KB * 4 + HROWS * HEAD_DIM * 2 + ATT_XCH_BYTES;
+// Dynamic shared memory: the stage ring (the staged Q lives in stage 0 before the first tile),
+// the S exchange, then the selected block list (kb entries).
+template <int KV_TYPE> constexpr int attn_smem_bytes(int kb) {
+    return AttnCfg<KV_TYPE>::NSTAGE * attn_stage_bytes<KV_TYPE>() + ATT_XCH_BYTES + ((kb * 4 + 15) & ~15);
 }
-static_assert(AttnCfg<QSA_TYPE_Q8_0>::MIN_CTAS * (attn_smem_bytes<QSA_TYPE_Q8_0>() + 2048) <= 228 * 1024,
+// two q8_0 CTAs per SM (228 KB, 1 KB reserved per CTA) for up to 256 kept blocks
+static_assert(AttnCfg<QSA_TYPE_Q8_0>::MIN_CTAS * (attn_smem_bytes<QSA_TYPE_Q8_0>(256) + 1024 + 128) <= 228 * 1024,
               "q8_0 attention CTAs per SM");
+static_assert(HROWS * HEAD_DIM * 2 <= 2 * ATT_CELLS * 2 * AttnCfg<QSA_TYPE_Q8_0>::HB, "staged Q fits stage 0");
 // the post-loop merge scratch (per-warp O, m, l) lives in the stage memory
 static_assert(ATT_CWARPS * 8 * (HEAD_DIM / 2) * 4 + 3 * ATT_CWARPS * 8 * 4 + 2 * HROWS * 4 <=
               AttnCfg<QSA_TYPE_Q8_0>::NSTAGE * 2 * ATT_CELLS * 2 * AttnCfg<QSA_TYPE_Q8_0>::HB, "merge scratch");
@@ -112,9 +116,9 @@ __global__ void __launch_bounds__(ATT_THREADS, AttnCfg<KV_TYPE>::MIN_CTAS) attn_
     const int dh = warp & 1;                  //   128-dim half (q8_0 groups 4dh..4dh+3)
     const bool producer = warp == ATT_CWARPS;
     const bool head_live = !producer && hs < NKV;
-    int * sel = reinterpret_cast<int *>(smem + NS * attn_stage_bytes<KV_TYPE>());
-    __half * qs = reinterpret_cast<__half *>(smem + NS * attn_stage_bytes<KV_TYPE>() + MAX_KB * 4);
-    float4 * xch = reinterpret_cast<float4 *>(smem + NS * attn_stage_bytes<KV_TYPE>() + MAX_KB * 4 + HROWS * HEAD_DIM * 2);
+    __half * qs = reinterpret_cast<__half *>(smem);      // staged Q, then Q fragments (stage 0, before tile 0)
+    float4 * xch = reinterpret_cast<float4 *>(smem + NS * attn_stage_bytes<KV_TYPE>());
+    int * sel = reinterpret_cast<int *>(smem + NS * attn_stage_bytes<KV_TYPE>() + ATT_XCH_BYTES);
 
     // ---- prologue: every input load is independent, issued together
     int qpos;
@@ -237,6 +241,14 @@ __global__ void __launch_bounds__(ATT_THREADS, AttnCfg<KV_TYPE>::MIN_CTAS) attn_
         for (int k = 0; k < 16; k++) qfrag[(hs * 16 + k) * 32 + lane] = make_uint2(qf[k][0], qf[k][1]);
     }
     __syncthreads();
+    // each consumer warp's Q fragments (its 8 k-steps of 16 dims) stay in registers for the whole
+    // loop; afterwards stage 0 (where Q was staged) is free for tile 0
+    uint2 qreg[8];
+    if (!producer) {
+        #pragma unroll
+        for (int k = 0; k < 8; k++) qreg[k] = qfrag[(hs * 16 + 8 * dh + k) * 32 + lane];
+    }
+    __syncthreads();
 
     auto stage_k = [&](int s) { return smem + s * attn_stage_bytes<KV_TYPE>(); };
     auto stage_v = [&](int s) { return smem + s * attn_stage_bytes<KV_TYPE>() + ATT_CELLS * RB; };  // RB >= row bytes
@@ -302,10 +314,6 @@ __global__ void __launch_bounds__(ATT_THREADS, AttnCfg<KV_TYPE>::MIN_CTAS) attn_
         const int c0 = 16 * cw + 2 * j4;                     // this thread's V^T columns: c0+{0,1,8,9}
         const int hoff = hs * HB;                            // byte offset of this warp's head in a row
         constexpr int rb = NKV * HB;                         // row bytes (= smem row stride), K and V alike
-        // this warp's Q fragments (its 8 k-steps of 16 dims) stay in registers for the whole loop
-        uint2 qreg[8];
-        #pragma unroll
-        for (int k = 0; k < 8; k++) qreg[k] = qfrag[(hs * 16 + 8 * dh + k) * 32 + lane];
         const int pair_bar = 1 + (warp >> 1);                // the two dim-half warps of (head, cells)
         const uint32_t negb[4] = {F16X2_NEG1152, F16X2_NEG1152, F16X2_NEG1152, F16X2_NEG1152};
         for (int i = 0; i < n_local; i++) {
@@ -637,7 +645,7 @@ __global__ void __launch_bounds__(MERGE_THREADS) attn_merge_kernel(DevDesc d, co
 template <int KV_TYPE, int NKV>
 cudaError_t attn_set_attr_one() {
     return cudaFuncSetAttribute(attn_kernel<KV_TYPE, NKV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                attn_smem_bytes<KV_TYPE>());
+                                attn_smem_bytes<KV_TYPE>(MAX_KB));
 }
 
 cudaError_t attn_set_attrs() {
@@ -670,7 +678,7 @@ cudaError_t launch_attn(const DevDesc & d, cudaStream_t st, int n_q, const qsa_d
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     cudaError_t e;
-    cfg.dynamicSmemBytes = d.type_k == QSA_TYPE_Q8_0 ? attn_smem_bytes<QSA_TYPE_Q8_0>() : attn_smem_bytes<QSA_TYPE_F16>();
+    cfg.dynamicSmemBytes = d.type_k == QSA_TYPE_Q8_0 ? attn_smem_bytes<QSA_TYPE_Q8_0>(d.kb) : attn_smem_bytes<QSA_TYPE_F16>(d.kb);
 #define QSA_LAUNCH_ATTN(T, N) cudaLaunchKernelEx(&cfg, attn_kernel<T, N>, d, items, cache0, n_past0, q, q_type, sel_ws, \
                                                  nsel_ws, tiles_per_cta, max_chunks, part_o, part_ml, out, status, state_out)
     if (d.type_k == QSA_TYPE_Q8_0) e = d.n_head_kv == 2 ? QSA_LAUNCH_ATTN(QSA_TYPE_Q8_0, 2) : QSA_LAUNCH_ATTN(QSA_TYPE_Q8_0, 1);
