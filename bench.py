@@ -496,7 +496,7 @@ def run_ours_config5(args, ws, rank, local):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     NL, n_past = cfg.layers, cfg.n_past
-    dec = ShardedDecoder(d, rank=rank, world=ws)
+    dec = ShardedDecoder(d, rank=rank, world=ws, exchange=args.exchange, batch=1)
     node = QsaNode(d, dev)
     st = QsaState(d, n_layers=NL, device=dev, blocks=dec.blocks)
     for il in range(NL):                       # every rank draws the same stream, keeps its cells
@@ -529,11 +529,12 @@ def run_ours_config5(args, ws, rank, local):
         step()
     # the attention stage of layer 0 alone (the dominant kernel), on this rank's share
     cand = dec.backend.candidates(items[0], 1, n_past + 1, dec.blocks, slots[1][:1])
-    gathered = dec._all_gather(cand)
+    gathered, cstride = dec._all_gather(cand, 0)
     torch.cuda.synchronize()
     g_attn = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g_attn):
-        dec.backend.attend(items[0], 1, n_past + 1, dec.blocks, gathered, slots[0][:1])
+        dec.backend.attend(items[0], 1, n_past + 1, dec.blocks, gathered, slots[0][:1], n_shards=dec.world,
+                           cand_stride=cstride)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
 
     def before(i):
@@ -598,7 +599,9 @@ def run_ours_config5(args, ws, rank, local):
         "config": {"workload": "config5: decode 1 token through 12 layers, ctx 1048576, q8_0, top-128 of 16384 "
                                "blocks + 128-token window (131 blocks)",
                    "global_batch": 1, "seq_len": n_past + 1, "layers": NL,
-                   "parallelism": f"KV-sequence-sharded x{ws} (NCCL all-gathers)" if ws > 1 else "1 GPU",
+                   "parallelism": (f"KV-sequence-sharded x{ws} ("
+                                   + ("NVLink peer-memory all-gathers" if args.exchange == "peer" else "NCCL all-gathers")
+                                   + ")") if ws > 1 else "1 GPU",
                    "blocks_per_gpu": hi - lo,
                    "l2": "flushed (256 MB write) before every timed step", "cuda_graph": True},
         "roofline": {"bound": "hbm", "kernel": "attn_kernel<q8_0> (qsa_shard_attend), layer 0, rank 0",
@@ -614,6 +617,10 @@ def run_ours_config5(args, ws, rank, local):
         "clocks": clocks.summary(),
     }
     del g, g_attn                               # graphs holding NCCL work go before the process group
+    if dec.peer is not None:
+        torch.cuda.synchronize()
+        torch.distributed.barrier()
+        dec.peer.close()
     return res
 
 
@@ -787,6 +794,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+                    help="config 5 with N > 1: the shards' exchanges over NVLink peer memory or NCCL")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 

@@ -218,10 +218,32 @@ qsa_status qsa_shard_candidates(const qsa_desc * d, const qsa_decode_item * item
                                 int32_t * cand, void * ws, size_t ws_bytes, qsa_stream_t stream);
 qsa_status qsa_shard_attend(const qsa_desc * d, const qsa_decode_item * items, int32_t batch, int32_t max_n_kv,
                             int32_t blk_lo, int32_t blk_hi, int32_t n_shards, const int32_t * all_cand,
+                            int32_t cand_stride /* int32 between shards' slices; 0 = 2*batch*KB */,
                             const void * q, int32_t q_type, float * state,
                             int32_t * sel_out, void * ws, size_t ws_bytes, qsa_stream_t stream);
 qsa_status qsa_merge_states(const qsa_desc * d, int32_t n_parts, int32_t batch, const float * states, float * out,
                             qsa_stream_t stream);
+
+/* ------------------------------------------------------------------ all-gather over peer memory
+ * The two exchanges of the sharded decode without a collective library: every rank owns a gather
+ * buffer of qsa_peer_buffer_bytes(n_ranks, slot_bytes) bytes ([n_ranks][slot_bytes] + flags,
+ * zeroed once) and maps the buffers of all ranks through CUDA IPC.  qsa_peer_push stores this
+ * rank's slice (`slot_bytes`, a multiple of 16, from `src`) into slot `rank` of every buffer (`bufs`:
+ * a device array of the n_ranks buffer addresses, this rank's own among them) over NVLink, then
+ * publishes it with a release flag carrying the round's epoch (`epoch`, `counter`: two zeroed device
+ * uint32 per buffer, owned by this rank).  qsa_peer_wait returns once all n_ranks slices of the
+ * round are in this rank's buffer (bounded wait: QSA_ERR_TIMEOUT through the status word of `ws`,
+ * read by qsa_check).  slot_bytes is a multiple of 4; slots start at a stride rounded up to 16
+ * bytes.  All ranks must push and wait on a buffer in the same order.  No
+ * counterpart in the reference. */
+qsa_status qsa_ipc_handle(const void * ptr, void * handle /* host, 64 bytes */, size_t * offset /* host */);
+qsa_status qsa_ipc_open(const void * handle /* host, 64 bytes */, void ** base /* host */);
+qsa_status qsa_ipc_close(void * base);
+size_t qsa_peer_buffer_bytes(int32_t n_ranks, size_t slot_bytes);
+qsa_status qsa_peer_push(void * const * bufs, int32_t n_ranks, int32_t rank, const void * src, size_t slot_bytes,
+                         uint32_t * epoch, uint32_t * counter, qsa_stream_t stream);
+qsa_status qsa_peer_wait(const void * local_buf, int32_t n_ranks, size_t slot_bytes, const uint32_t * epoch,
+                         void * ws, size_t ws_bytes, qsa_stream_t stream);
 
 /* ------------------------------------------------------------------ prefill */
 size_t qsa_prefill_workspace_size(const qsa_desc * d, int32_t T, int32_t max_n_kv);

@@ -119,8 +119,14 @@ def lib() -> ctypes.CDLL:
         "qsa_shard_state_floats": (SZ, [D]),
         "qsa_shard_append": (I32, [D, C, I32, I32, I32, I32, VP, VP, VP, VP]),
         "qsa_shard_candidates": (I32, [D, VP, I32, I32, I32, I32, VP, VP, VP, VP, VP, VP, SZ, VP]),
-        "qsa_shard_attend": (I32, [D, VP, I32, I32, I32, I32, I32, VP, VP, I32, VP, VP, VP, SZ, VP]),
+        "qsa_shard_attend": (I32, [D, VP, I32, I32, I32, I32, I32, VP, I32, VP, I32, VP, VP, VP, SZ, VP]),
         "qsa_merge_states": (I32, [D, I32, I32, VP, VP, VP]),
+        "qsa_ipc_handle": (I32, [VP, VP, P(SZ)]),
+        "qsa_ipc_open": (I32, [VP, P(VP)]),
+        "qsa_ipc_close": (I32, [VP]),
+        "qsa_peer_buffer_bytes": (SZ, [I32, SZ]),
+        "qsa_peer_push": (I32, [VP, I32, I32, VP, SZ, VP, VP, VP]),
+        "qsa_peer_wait": (I32, [VP, I32, SZ, VP, VP, SZ, VP]),
         "qsa_prefill_workspace_size": (SZ, [D, I32, I32]),
         "qsa_prefill": (I32, [D, C, I32, I32, VP, I32, VP, VP, VP, VP, VP, VP, VP, SZ, VP]),
         "qsa_check": (I32, [VP, SZ, VP]),
@@ -144,5 +150,6 @@ HEADER_SYMBOLS = [
     "qsa_append", "qsa_pool_rebuild", "qsa_decode_workspace_size", "qsa_workspace_init",
     "qsa_decode", "qsa_decode_append", "qsa_decode_select", "qsa_decode_attend", "qsa_decode_noalloc",
     "qsa_shard_state_floats", "qsa_shard_append", "qsa_shard_candidates", "qsa_shard_attend", "qsa_merge_states",
+    "qsa_ipc_handle", "qsa_ipc_open", "qsa_ipc_close", "qsa_peer_buffer_bytes", "qsa_peer_push", "qsa_peer_wait",
     "qsa_prefill_workspace_size", "qsa_prefill", "qsa_check", "qsa_version",
 ]

@@ -433,7 +433,7 @@ qsa_status qsa_shard_candidates(const qsa_desc * dd, const qsa_decode_item * ite
 
 qsa_status qsa_shard_attend(const qsa_desc * dd, const qsa_decode_item * items, int32_t batch, int32_t max_n_kv,
                             int32_t blk_lo, int32_t blk_hi, int32_t n_shards, const int32_t * all_cand,
-                            const void * q, int32_t q_type, float * state,
+                            int32_t cand_stride, const void * q, int32_t q_type, float * state,
                             int32_t * sel_out, void * ws, size_t ws_bytes, qsa_stream_t stream) {
     DevDesc d; WsLayout w;
     qsa_status s = shard_common(dd, items, batch, max_n_kv, blk_lo, blk_hi, ws, ws_bytes, d, w);
@@ -442,7 +442,9 @@ qsa_status qsa_shard_attend(const qsa_desc * dd, const qsa_decode_item * items, 
     if (q_type != QSA_TYPE_BF16 && q_type != QSA_TYPE_F32) return QSA_ERR_INVALID;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     unsigned char * wsb = static_cast<unsigned char *>(ws);
-    cudaError_t e = launch_shard_select(d, st, items, n_shards, batch, all_cand, blk_lo, blk_hi, sel_out, reinterpret_cast<int *>(wsb + w.sel), reinterpret_cast<int *>(wsb + w.nsel),
+    const size_t stride = cand_stride > 0 ? (size_t) cand_stride : (size_t) 2 * batch * d.kb;
+    if (stride < (size_t) 2 * batch * d.kb) return QSA_ERR_INVALID;
+    cudaError_t e = launch_shard_select(d, st, items, n_shards, batch, all_cand, stride, blk_lo, blk_hi, sel_out, reinterpret_cast<int *>(wsb + w.sel), reinterpret_cast<int *>(wsb + w.nsel),
                                         reinterpret_cast<uint32_t *>(wsb + w.status));
     if (e == cudaErrorInvalidValue) return QSA_ERR_UNSUPPORTED;       // too many candidates for one CTA
     if (e != cudaSuccess) return QSA_ERR_CUDA;

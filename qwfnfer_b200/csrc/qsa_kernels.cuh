@@ -48,7 +48,8 @@ cudaError_t launch_select_scores_warp(const DevDesc & d, cudaStream_t st, int n_
 // KV-sequence-sharded decode: global selection from all shards' candidates, and the log-sum-exp
 // merge of the shards' attention states (qsa_shard.cu).
 cudaError_t launch_shard_select(const DevDesc & d, cudaStream_t st, const qsa_decode_item * items, int n_shards,
-        int batch, const int * cand, int blo, int bhi, int * sel_out, int * sel_ws, int * nsel_ws, uint32_t * status);
+        int batch, const int * cand, size_t cand_stride, int blo, int bhi, int * sel_out, int * sel_ws, int * nsel_ws,
+        uint32_t * status);
 cudaError_t launch_merge_states(const DevDesc & d, cudaStream_t st, int n_parts, int batch, const float * states,
         float * out);
 // CTAs per thread-block cluster of the attention launch (partials are per cluster).

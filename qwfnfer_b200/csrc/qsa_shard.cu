@@ -4,14 +4,15 @@
 // this library's addition for very long contexts.  Rank g owns blocks [blo, bhi) of every layer.
 // One step: every rank scores its blocks and keeps its local best (score_select_kernel in sharded
 // mode); the candidates of all ranks are all-gathered by the caller; shard_select_kernel forms
-// the exact global selection on every rank (every global winner is in its owner's local best);
+// the exact global selection on every rank (every global winner is in its owner's local best;
+// a radix select over the gathered scores, one warp per query);
 // each rank attends its own selected blocks into an unnormalised state (attn_kernel, state mode);
 // the states are all-gathered and merge_states_kernel combines them by log-sum-exp in rank order.
 #include "qsa_kernels.cuh"
 
 namespace qsa {
 
-constexpr int SHARD_SEL_THREADS = 1024;
+constexpr int SHARD_SEL_WARPS = 8;        // queries per CTA (one warp each)
 
 // Forced blocks of the query at q (the same rule as the selection kernel).
 __device__ __forceinline__ void shard_forced_range(const DevDesc & d, int q, int & f_lo, int & f_hi) {
@@ -21,103 +22,164 @@ __device__ __forceinline__ void shard_forced_range(const DevDesc & d, int q, int
     else { f_lo = 1; f_hi = 0; }
 }
 
-// Bitonic sort of n (a power of two) 64-bit keys in shared memory, descending.
-__device__ void bitonic_desc(unsigned long long * key, int n) {
-    for (int k = 2; k <= n; k <<= 1) {
-        for (int j = k >> 1; j > 0; j >>= 1) {
-            for (int i = threadIdx.x; i < n; i += blockDim.x) {
-                const int ixj = i ^ j;
-                if (ixj > i) {
-                    const unsigned long long a = key[i], b = key[ixj];
-                    const bool desc = (i & k) == 0;
-                    if (desc ? (a < b) : (a > b)) { key[i] = b; key[ixj] = a; }
-                }
-            }
-            __syncthreads();
-        }
+__device__ __forceinline__ int warp_incl_scan(int x, int lane) {
+    #pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
     }
+    return x;
 }
 
-// One CTA per query.  Candidates: int32 [n_shards][2][batch][kb], per shard the block ids
-// (-1 = none), then the f32 scores' bits.  Writes the global selection (ascending, -1 padded) to
-// sel_out (optional) and this rank's blocks [blo, bhi) of it to the workspace list the attention
-// kernel reads.
-__global__ void __launch_bounds__(SHARD_SEL_THREADS) shard_select_kernel(DevDesc d,
+// One warp per query.  Candidates: per shard (cand_stride int32 apart) int32 [2][batch][kb], the
+// block ids (-1 = none), then the f32 scores' bits.  Every shard sends its kept blocks in
+// ascending order and the shards hold ascending block ranges, so the concatenation of the lists
+// (slot order) is ascending by block: a radix select over the scores (8-bit digits from the top)
+// with the lower slot first on equal scores is the global rule (score, then lower block).  Writes
+// the global selection (ascending, -1 padded) to sel_out (optional) and this rank's blocks
+// [blo, bhi) of it to the workspace list the attention kernel reads.  A candidate that no shard
+// could have sent (not visible, forced, or not a non-negative score) is dropped and flagged.
+__global__ void __launch_bounds__(32 * SHARD_SEL_WARPS) shard_select_kernel(DevDesc d,
         const qsa_decode_item * __restrict__ items, int n_shards, int batch,
-        const int * __restrict__ cand, int blo, int bhi,
+        const int * __restrict__ cand, size_t cand_stride, int blo, int bhi,
         int * __restrict__ sel_out, int * __restrict__ sel_ws, int * __restrict__ nsel_ws,
         uint32_t * __restrict__ status) {
-    extern __shared__ __align__(16) unsigned long long keys[];     // [npow2]
-    __shared__ int chosen[MAX_KB];
-    __shared__ int n_chosen;
-    const int t = blockIdx.x;
+    __shared__ unsigned hist[SHARD_SEL_WARPS][256];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * SHARD_SEL_WARPS + warp;
+    if (t >= batch) return;
     const int q = items[t].n_past;
     const int kb = d.kb;
+    int * sw = sel_ws + (size_t) t * kb;
+    int * so = sel_out ? sel_out + (size_t) t * kb : nullptr;
     if (q < 0 || q >= d.n_ctx) {
-        if (threadIdx.x == 0) { set_status(status, DEV_BAD_POS); nsel_ws[t] = 0; }
-        for (int i = threadIdx.x; i < kb; i += blockDim.x) {
-            sel_ws[(size_t) t * kb + i] = -1;
-            if (sel_out) sel_out[(size_t) t * kb + i] = -1;
-        }
+        if (lane == 0) { set_status(status, DEV_BAD_POS); nsel_ws[t] = 0; }
+        for (int i = lane; i < kb; i += 32) { sw[i] = -1; if (so) so[i] = -1; }
         return;
     }
     int f_lo, f_hi;
     shard_forced_range(d, q, f_lo, f_hi);
     const int n_forced = f_hi >= f_lo ? f_hi - f_lo + 1 : 0;
     const int want = max(0, kb - n_forced);
-    const int n = n_shards * kb;
-    int np2 = 1;
-    while (np2 < n) np2 <<= 1;
     const int n_vis = (q + 1) / d.ratio;
-    // key = score bits (non-negative scores order as unsigned) : complement of the block id, so a
-    // descending sort orders by score, then lower block first; empty slots are 0 (last).  A
-    // candidate that no shard could have sent (not visible, forced, or a negative score) is
-    // dropped and flagged.
-    for (int i = threadIdx.x; i < np2; i += blockDim.x) {
-        unsigned long long k = 0;
-        if (i < n) {
-            const int sh = i / kb, j = i % kb;
-            const size_t o = ((size_t) sh * 2 * batch + t) * kb + j;
-            const int b = cand[o];
-            if (b >= 0) {
-                const uint32_t sbits = (uint32_t) cand[o + (size_t) batch * kb];
-                if (b >= n_vis || (b >= f_lo && b <= f_hi) || (sbits >> 31) != 0u || sbits > 0x7f800000u)
-                    set_status(status, DEV_BAD_SEL);
-                else
-                    k = ((unsigned long long) sbits << 32) | (0xffffffffu - (unsigned) b);
+    const int n = n_shards * kb;                     // candidate slots, slot i = shard i / kb, entry i % kb
+    auto slot_block = [&](int i) -> int {
+        return cand[(size_t) (i / kb) * cand_stride + (size_t) t * kb + (i % kb)];
+    };
+    auto slot_key = [&](int i) -> uint32_t {
+        return (uint32_t) cand[(size_t) (i / kb) * cand_stride + (size_t) (batch + t) * kb + (i % kb)];
+    };
+    auto valid = [&](int b, uint32_t key) {
+        return b >= 0 && b < n_vis && !(b >= f_lo && b <= f_hi) && (key >> 31) == 0u && key <= 0x7f800000u;
+    };
+    const int per = (n + 31) / 32;
+    const int lo = min(n, lane * per), hi = min(n, lo + per);
+    int n_valid = 0;
+    for (int i = lo; i < hi; i++) {
+        const int b = slot_block(i);
+        if (b < 0) continue;
+        if (valid(b, slot_key(i))) n_valid++;
+        else set_status(status, DEV_BAD_SEL);
+    }
+    int tot_valid = warp_incl_scan(n_valid, lane);
+    tot_valid = __shfl_sync(0xffffffffu, tot_valid, 31);
+    const bool take_all = tot_valid <= want;
+    uint32_t prefix = 0, pmask = 0;
+    int remaining = want;
+    unsigned * hw = hist[warp];
+    if (!take_all && want > 0) {
+        for (int shift = 24; shift >= 0; shift -= 8) {
+            for (int i = lane; i < 256; i += 32) hw[i] = 0;
+            __syncwarp();
+            for (int i = lo; i < hi; i++) {
+                const int b = slot_block(i);
+                const uint32_t key = slot_key(i);
+                if (valid(b, key) && (key & pmask) == prefix) atomicAdd(&hw[(key >> shift) & 255u], 1u);
             }
+            __syncwarp();
+            int own = 0;
+            #pragma unroll
+            for (int k = 0; k < 8; k++) own += (int) hw[255 - 8 * lane - k];
+            const int incl = warp_incl_scan(own, lane);
+            const int above = incl - own;
+            const unsigned hit = __ballot_sync(0xffffffffu, above < remaining && incl >= remaining);
+            const int src = __ffs(hit) - 1;
+            int bin = 0, cut_rem = 0;
+            if (lane == src) {
+                int cum = above, k = 0;
+                for (; k < 8; k++) {
+                    const int hc = (int) hw[255 - 8 * lane - k];
+                    if (cum + hc >= remaining) break;
+                    cum += hc;
+                }
+                bin = 255 - 8 * lane - k;
+                cut_rem = remaining - cum;
+            }
+            bin = __shfl_sync(0xffffffffu, bin, src);
+            cut_rem = __shfl_sync(0xffffffffu, cut_rem, src);
+            prefix |= (uint32_t) bin << shift;
+            pmask |= 255u << shift;
+            remaining = cut_rem;
+            __syncwarp();
         }
-        keys[i] = k;
     }
-    if (threadIdx.x == 0) n_chosen = 0;
-    __syncthreads();
-    bitonic_desc(keys, np2);
-    // the best `want` candidates plus the forced blocks
-    for (int i = threadIdx.x; i < want; i += blockDim.x) {
-        const unsigned long long k = keys[i];
-        if (k != 0ull) chosen[atomicAdd(&n_chosen, 1)] = (int) (0xffffffffu - (unsigned) (k & 0xffffffffull));
+    const bool none = !take_all && want == 0;
+    // per slot: 2 kept, 1 equal to the cut, 0 not kept
+    auto cls = [&](int i) -> int {
+        const int b = slot_block(i);
+        const uint32_t key = slot_key(i);
+        if (!valid(b, key) || none) return 0;
+        if (take_all) return 2;
+        return key > prefix ? 2 : (key == prefix ? 1 : 0);
+    };
+    int n_take = 0, n_tie = 0;
+    for (int i = lo; i < hi; i++) {
+        const int c = cls(i);
+        n_take += c == 2;
+        n_tie += c == 1;
     }
-    for (int b = f_lo + (int) threadIdx.x; b <= f_hi; b += blockDim.x) chosen[atomicAdd(&n_chosen, 1)] = b;
-    __syncthreads();
-    // ascending order: rank each by counting the smaller ones (equal ids, which only a caller
-    // that sent one block from two shards produces, by their slot)
-    const int m = n_chosen;
-    __shared__ int asc[MAX_KB];
-    for (int i = threadIdx.x; i < m; i += blockDim.x) {
-        const int b = chosen[i];
-        int rank = 0;
-        for (int j = 0; j < m; j++) rank += chosen[j] < b || (chosen[j] == b && j < i);
-        asc[rank] = b;
+    const int tie_incl = warp_incl_scan(n_tie, lane);
+    const int tie_mine = max(0, min(n_tie, remaining - (tie_incl - n_tie)));
+    // positions in the global list and in this rank's list
+    int n_mine_rank = 0;
+    {
+        int tl = tie_mine;
+        for (int i = lo; i < hi; i++) {
+            const int c = cls(i);
+            bool tk = c == 2;
+            if (c == 1 && tl > 0) { tk = true; tl--; }
+            if (tk) { const int b = slot_block(i); n_mine_rank += b >= blo && b < bhi; }
+        }
     }
-    __syncthreads();
-    if (sel_out)
-        for (int i = threadIdx.x; i < kb; i += blockDim.x) sel_out[(size_t) t * kb + i] = i < m ? asc[i] : -1;
-    if (threadIdx.x == 0) {                       // this rank's blocks, ascending, for the attention
-        int c = 0;
-        for (int i = 0; i < m; i++)
-            if (asc[i] >= blo && asc[i] < bhi) sel_ws[(size_t) t * kb + c++] = asc[i];
-        nsel_ws[t] = c;
+    const int mine = n_take + tie_mine;
+    const int pos_incl = warp_incl_scan(mine, lane), rk_incl = warp_incl_scan(n_mine_rank, lane);
+    int pos = pos_incl - mine, rpos = rk_incl - n_mine_rank;
+    const int n_cand_kept = __shfl_sync(0xffffffffu, pos_incl, 31);
+    const int n_rank_kept = __shfl_sync(0xffffffffu, rk_incl, 31);
+    int tl = tie_mine;
+    for (int i = lo; i < hi; i++) {
+        const int c = cls(i);
+        bool tk = c == 2;
+        if (c == 1 && tl > 0) { tk = true; tl--; }
+        if (!tk) continue;
+        const int b = slot_block(i);
+        if (so && pos < kb) so[pos] = b;
+        pos++;
+        if (b >= blo && b < bhi) { if (rpos < kb) sw[rpos] = b; rpos++; }
     }
+    // the forced blocks follow (they are above every candidate)
+    const int f_rank_lo = max(f_lo, blo), f_rank_hi = min(f_hi, bhi - 1);
+    const int n_f_rank = n_forced ? max(0, f_rank_hi - f_rank_lo + 1) : 0;
+    for (int i = lane; i < n_forced; i += 32) {
+        if (so && n_cand_kept + i < kb) so[n_cand_kept + i] = f_lo + i;
+    }
+    for (int i = lane; i < n_f_rank; i += 32) {
+        if (n_rank_kept + i < kb) sw[n_rank_kept + i] = f_rank_lo + i;
+    }
+    const int m_all = min(kb, n_cand_kept + n_forced), m_rank = min(kb, n_rank_kept + n_f_rank);
+    if (so) for (int i = m_all + lane; i < kb; i += 32) so[i] = -1;
+    for (int i = m_rank + lane; i < kb; i += 32) sw[i] = -1;
+    if (lane == 0) nsel_ws[t] = m_rank;
 }
 
 // out[t][h][d] from the gathered states [n_parts][batch][M 16 | L 16 | O 16x256], merged in rank
@@ -142,15 +204,10 @@ __global__ void __launch_bounds__(256) merge_states_kernel(DevDesc d, int n_part
 }
 
 cudaError_t launch_shard_select(const DevDesc & d, cudaStream_t st, const qsa_decode_item * items, int n_shards,
-        int batch, const int * cand, int blo, int bhi, int * sel_out, int * sel_ws, int * nsel_ws, uint32_t * status) {
-    int np2 = 1;
-    while (np2 < n_shards * d.kb) np2 <<= 1;
-    const size_t smem = (size_t) np2 * 8;
-    if (smem > 200 * 1024) return cudaErrorInvalidValue;
-    cudaError_t e = cudaFuncSetAttribute(shard_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    if (e != cudaSuccess) return e;
-    shard_select_kernel<<<batch, SHARD_SEL_THREADS, smem, st>>>(d, items, n_shards, batch, cand, blo, bhi, sel_out,
-                                                                sel_ws, nsel_ws, status);
+        int batch, const int * cand, size_t cand_stride, int blo, int bhi, int * sel_out, int * sel_ws, int * nsel_ws,
+        uint32_t * status) {
+    shard_select_kernel<<<(batch + SHARD_SEL_WARPS - 1) / SHARD_SEL_WARPS, 32 * SHARD_SEL_WARPS, 0, st>>>(
+        d, items, n_shards, batch, cand, cand_stride, blo, bhi, sel_out, sel_ws, nsel_ws, status);
     return cudaGetLastError();
 }
 

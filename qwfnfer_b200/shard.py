@@ -8,7 +8,8 @@ one decode step of one layer becomes:
   1. candidates (libqsa): the rank holding the new token's cell appends it (K, V, raw key, and the
      pooled key of a block it completes); every rank scores its own visible blocks and keeps its
      best KB blocks outside the forced window, with their scores;
-  2. one all-gather of the candidates ([2, batch, KB] int32 per rank: ids, then score bits);
+  2. one all-gather of the candidates ([2, batch, KB] int32 per rank: ids, then score bits), by NCCL
+     or by libqsa's push/wait over NVLink peer memory (exchange="peer");
   3. attend (libqsa): the exact global selection, identical on every rank and to the unsharded
      qsa_decode's (a block among the global best is among its owner's best), then attention over
      the rank's part of it into an unnormalised state [M | L | O] per query;
@@ -88,14 +89,17 @@ class LibShardBackend:
         return out
 
     def attend(self, items, batch: int, max_n_kv: int, blocks: tuple[int, int], gathered: torch.Tensor, q,
-               sel_out: torch.Tensor | None = None, state: torch.Tensor | None = None) -> torch.Tensor:
-        """gathered: int32 [n_shards, 2, batch, KB], every rank's candidates in rank order."""
+               sel_out: torch.Tensor | None = None, state: torch.Tensor | None = None,
+               n_shards: int | None = None, cand_stride: int = 0) -> torch.Tensor:
+        """gathered: every rank's candidates in rank order, int32 [n_shards, 2, batch, KB], or a flat
+        tensor whose shard slices are cand_stride elements apart."""
+        n_shards = n_shards if n_shards is not None else gathered.shape[0]
         if state is None:
             state = torch.empty((batch, self.state_floats), dtype=torch.float32, device=self.device)
         q_type = TYPE_BF16 if q.dtype == torch.bfloat16 else TYPE_F32
         ws = self.workspace(batch, max_n_kv)
         check(lib().qsa_shard_attend(ctypes.byref(self.desc), _ptr(items), batch, max_n_kv, blocks[0], blocks[1],
-                                     gathered.shape[0], _ptr(gathered), _ptr(q), q_type, state.data_ptr(),
+                                     n_shards, _ptr(gathered), cand_stride, _ptr(q), q_type, state.data_ptr(),
                                      _ptr(sel_out), ws.data_ptr(), ws.numel(), self._stream()), "qsa_shard_attend")
         return state
 
@@ -114,12 +118,90 @@ class LibShardBackend:
         return lib().qsa_check(ws.data_ptr(), ws.numel(), self._stream())
 
 
+class PeerExchange:
+    """All-gathers of fixed-size slices over NVLink peer memory (libqsa's qsa_peer_push/_wait):
+    one buffer per rank holding a gather region per channel, mapped by every rank through CUDA
+    IPC.  `all_gather(channel, src)` returns a view [world, *src.shape] of this rank's region; the
+    view stays valid until the same channel's next all_gather (every rank must call the channels
+    in the same order)."""
+
+    def __init__(self, slot_bytes: list[int], group=None, device: str | torch.device = "cuda"):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.device = torch.device(device)
+        L = lib()
+        self.slot = [int(b) for b in slot_bytes]
+        assert all(b % 4 == 0 for b in self.slot), "slots are 4-byte multiples"
+        self.stride = [(b + 15) // 16 * 16 for b in self.slot]
+        region = [L.qsa_peer_buffer_bytes(self.world, b) for b in self.slot]
+        self.offsets = [0]
+        for r in region[:-1]:
+            self.offsets.append(self.offsets[-1] + ((r + 255) // 256) * 256)
+        total = self.offsets[-1] + ((region[-1] + 255) // 256) * 256
+        self.buf = torch.zeros(total, dtype=torch.uint8, device=self.device)
+        self.sync = torch.zeros(len(self.slot), 2, dtype=torch.int32, device=self.device)   # epoch, counter
+        handle = (ctypes.c_char * 64)()
+        off = ctypes.c_size_t()
+        check(L.qsa_ipc_handle(self.buf.data_ptr(), handle, ctypes.byref(off)), "qsa_ipc_handle")
+        everyone = [None] * self.world
+        dist.all_gather_object(everyone, (bytes(handle), off.value), group=group)
+        self._opened = []
+        bases = []
+        for r, (h, o) in enumerate(everyone):
+            if r == self.rank:
+                bases.append(self.buf.data_ptr())
+                continue
+            hb = (ctypes.c_char * 64).from_buffer_copy(h)
+            base = ctypes.c_void_p()
+            check(L.qsa_ipc_open(hb, ctypes.byref(base)), "qsa_ipc_open")
+            self._opened.append(base.value)
+            bases.append(base.value + o)
+        # per channel, the device array of every rank's region address
+        self.ptrs = [torch.tensor([b + off_c for b in bases], dtype=torch.int64, device=self.device)
+                     for off_c in self.offsets]
+        self.status = torch.zeros(64, dtype=torch.uint8, device=self.device)   # status word of the waits
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=group)
+
+    def all_gather(self, channel: int, src: torch.Tensor):
+        """(gathered, stride): gathered = this rank's region as a flat tensor of src's dtype, the
+        slices `stride` elements apart (a [world, *src.shape] view when there is no padding)."""
+        L = lib()
+        nb = src.numel() * src.element_size()
+        assert src.is_contiguous() and nb == self.slot[channel]
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        region = self.buf.data_ptr() + self.offsets[channel]
+        epoch = self.sync[channel].data_ptr()
+        check(L.qsa_peer_push(self.ptrs[channel].data_ptr(), self.world, self.rank, src.data_ptr(), nb, epoch,
+                              epoch + 4, stream), "qsa_peer_push")
+        check(L.qsa_peer_wait(region, self.world, nb, epoch, self.status.data_ptr(), self.status.numel(), stream),
+              "qsa_peer_wait")
+        st = self.stride[channel]
+        flat = self.buf[self.offsets[channel]:self.offsets[channel] + self.world * st].view(src.dtype)
+        stride = st // src.element_size()
+        if st == nb:
+            return flat.view((self.world,) + tuple(src.shape)), stride
+        return flat, stride
+
+    def check(self) -> int:
+        return lib().qsa_check(self.status.data_ptr(), self.status.numel(),
+                               torch.cuda.current_stream(self.device).cuda_stream)
+
+    def close(self) -> None:
+        for b in self._opened:
+            lib().qsa_ipc_close(b)
+        self._opened = []
+
+
 class ShardedDecoder:
     """The per-rank driver of the sharded decode step (module docstring).  `group` is a
     torch.distributed process group (default: the world); world size 1 runs without collectives."""
 
     def __init__(self, desc: QsaDesc, backend=None, group=None, rank: int | None = None,
-                 world: int | None = None):
+                 world: int | None = None, exchange: str = "nccl", batch: int = 1):
+        """exchange: "nccl" (all-gathers of the process group) or "peer" (libqsa's all-gather over
+        NVLink peer memory, GPUs of one node; sized for `batch` queries per step)."""
         self.desc = desc
         self.group = group
         dist_on = dist.is_available() and dist.is_initialized()
@@ -128,15 +210,23 @@ class ShardedDecoder:
         self.blocks = shard_blocks(desc.n_ctx // desc.ratio, self.world, self.rank)
         self.backend = backend if backend is not None else LibShardBackend(desc)
         self.kb = k_blocks(desc)
+        self.peer = None
+        if exchange == "peer" and self.world > 1:
+            state_floats = lib().qsa_shard_state_floats(ctypes.byref(desc))
+            self.peer = PeerExchange([2 * batch * self.kb * 4, batch * state_floats * 4], group=group,
+                                     device=self.backend.device)
 
-    def _all_gather(self, t: torch.Tensor) -> torch.Tensor:
-        """[world, *t.shape], rank order."""
+    def _all_gather(self, t: torch.Tensor, channel: int = 0):
+        """(gathered, stride): every rank's t in rank order, slices `stride` elements apart
+        ([world, *t.shape] when dense)."""
         if self.world == 1:
-            return t.unsqueeze(0)
+            return t.unsqueeze(0), t.numel()
         t = t.contiguous()
+        if self.peer is not None:
+            return self.peer.all_gather(channel, t)
         out = torch.empty((self.world * t.shape[0],) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
         dist.all_gather_into_tensor(out, t, group=self.group)
-        return out.view((self.world,) + tuple(t.shape))
+        return out.view((self.world,) + tuple(t.shape)), t.numel()
 
     def append(self, cache: QsaLayerCache, pos0: int, k, v, kidx) -> None:
         """Append global rows [pos0, pos0+n): the rows inside this rank's cells are written."""
@@ -154,7 +244,8 @@ class ShardedDecoder:
         """One decode step of one layer for `batch` queries (items: this rank's device item table,
         global n_past, local caches).  Returns f32 [batch, n_head, head_dim] on every rank."""
         cand = self.backend.candidates(items, batch, max_n_kv, self.blocks, q_idx, k_new, v_new, kidx_new)
-        gathered = self._all_gather(cand)
-        state = self.backend.attend(items, batch, max_n_kv, self.blocks, gathered, q, sel_out=sel_out)
-        states = self._all_gather(state)
-        return self.backend.merge(states)
+        gathered, cstride = self._all_gather(cand, 0)
+        state = self.backend.attend(items, batch, max_n_kv, self.blocks, gathered, q, sel_out=sel_out,
+                                    n_shards=self.world, cand_stride=cstride)
+        states, _ = self._all_gather(state, 1)
+        return self.backend.merge(states.view(self.world, batch, -1))

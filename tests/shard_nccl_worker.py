@@ -1,7 +1,9 @@
 """One rank of the sharded decode over NCCL (launched by tests/test_zz_shard_nccl.py):
 
     python -m torch.distributed.run --nnodes 1 --nproc-per-node N --master-addr 127.0.0.1 \
-        --master-port P tests/shard_nccl_worker.py
+        --master-port P tests/shard_nccl_worker.py [nccl|peer]
+
+The exchange is NCCL's all-gather or libqsa's all-gather over NVLink peer memory.
 
 Every rank fills its shard of two sequences' caches, runs one ShardedDecoder step (append of the
 new token, the two all-gathers, the merge), and checks its status.  Rank 0 also builds the
@@ -39,7 +41,8 @@ def main() -> int:
     d = make_desc(n_ctx=65536, top_k_blocks=64, window=128)
     positions = [60031, 20000]                   # 60032 = 938 * 64: the token completes block 937
     seeds = [41, 42]
-    dec = ShardedDecoder(d)
+    exchange = sys.argv[1] if len(sys.argv) > 1 else "nccl"
+    dec = ShardedDecoder(d, exchange=exchange, batch=2)
     node = QsaNode(d)
     sts = [QsaState(d, blocks=dec.blocks) for _ in positions]
     for st, n, s in zip(sts, positions, seeds):
@@ -49,7 +52,10 @@ def main() -> int:
     B, KB, max_n_kv = len(positions), k_blocks(d), max(positions) + 1
     sel = torch.empty((B, KB), dtype=torch.int32, device=dev)
     out = dec.step(items, B, max_n_kv, q, q_idx, k, v, ki, sel_out=sel)
-    status = torch.tensor([dec.backend.check(B, max_n_kv)], dtype=torch.int32, device=dev)
+    st_code = dec.backend.check(B, max_n_kv)
+    if dec.peer is not None and st_code == QSA_OK:
+        st_code = dec.peer.check()
+    status = torch.tensor([st_code], dtype=torch.int32, device=dev)
     outs = [torch.empty_like(out) for _ in range(world)]
     sels = [torch.empty_like(sel) for _ in range(world)]
     stats = [torch.empty_like(status) for _ in range(world)]
@@ -71,10 +77,14 @@ def main() -> int:
         same = all(torch.equal(o, outs[0]) for o in outs)
         statuses = [int(s.item()) for s in stats]
         ok = all(sel_ok) and max(errs) <= ATTN_TOL and same and all(s == QSA_OK for s in statuses)
-        print("SHARD_NCCL " + json.dumps({"world": world, "blocks": dec.blocks, "rel_err": errs, "sel_equal": sel_ok,
+        print("SHARD_NCCL " + json.dumps({"world": world, "exchange": exchange, "blocks": dec.blocks, "rel_err": errs, "sel_equal": sel_ok,
                                           "ranks_identical": same, "status": statuses, "ok": ok}), flush=True)
     flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=dev)
     dist.broadcast(flag, 0)
+    if dec.peer is not None:
+        torch.cuda.synchronize()
+        dist.barrier()
+        dec.peer.close()
     dist.destroy_process_group()
     return 0 if flag.item() == 1 else 1
 

@@ -71,7 +71,7 @@ class OracleShardBackend:
         chosen = [b for _, b in pairs[:want]] + list(range(f_lo, f_hi + 1))
         return sorted(chosen)
 
-    def attend(self, items, batch, max_n_kv, blocks, gathered, q, sel_out=None):
+    def attend(self, items, batch, max_n_kv, blocks, gathered, q, sel_out=None, n_shards=None, cand_stride=0):
         d, lo, hi = self.d, self.blocks[0], self.blocks[1]
         r = d.ratio
         gathered = gathered.numpy()
