@@ -264,8 +264,17 @@ size_t qsa_decode_workspace_size(const qsa_desc * dd, int32_t batch, int32_t max
     return ws_layout(make_dev(dd), batch, max_n_kv).total;
 }
 
+namespace {
+// The prefill's KV-stationary attention applies (and how many blocks its buckets cover).
+bool prefill_kv_path(const DevDesc & d, int T) { return T >= 64 && prefill_kv_supported(d); }
+int prefill_n_blocks(const DevDesc & d, int max_n_kv) { return std::max(1, ceil_div(max_n_kv, d.ratio)); }
+}  // namespace
+
 size_t qsa_prefill_workspace_size(const qsa_desc * dd, int32_t T, int32_t max_n_kv) {
-    return qsa_decode_workspace_size(dd, T, max_n_kv);
+    const size_t base = qsa_decode_workspace_size(dd, T, max_n_kv);
+    if (base == 0) return 0;
+    const DevDesc d = make_dev(dd);
+    return prefill_kv_path(d, T) ? base + prefill_kv_workspace(d, T, prefill_n_blocks(d, max_n_kv)) : base;
 }
 
 qsa_status qsa_workspace_init(void * ws, size_t ws_bytes, qsa_stream_t stream) {
@@ -354,7 +363,9 @@ qsa_status qsa_prefill(const qsa_desc * dd, const qsa_layer_cache * cache, int32
     if (any_new && !(k_new && v_new && kidx_new)) return QSA_ERR_INVALID;
     const DevDesc d = make_dev(dd);
     const WsLayout w = ws_layout(d, T, n_past + T);
-    if (!ws || ws_bytes < w.total) return QSA_ERR_WORKSPACE;
+    const bool kv_path = prefill_kv_path(d, T);
+    const size_t need = kv_path ? w.total + prefill_kv_workspace(d, T, prefill_n_blocks(d, n_past + T)) : w.total;
+    if (!ws || ws_bytes < need) return QSA_ERR_WORKSPACE;
     if ((s = set_attrs()) != QSA_OK) return s;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     if (any_new) {
@@ -375,6 +386,10 @@ qsa_status qsa_prefill(const qsa_desc * dd, const qsa_layer_cache * cache, int32
     } else if ((s = launch_select(d, w, T, nullptr, *cache, n_past, q_idx, sel_out, wsb, st)) != QSA_OK) {
         return s;
     }
+    if (kv_path)
+        return cuda_status(launch_prefill_attn_kv(d, st, *cache, n_past, T, q, q_type, reinterpret_cast<const int *>(wsb + w.sel),
+                                                  reinterpret_cast<const int *>(wsb + w.nsel), prefill_n_blocks(d, n_past + T),
+                                                  wsb + w.total, out, reinterpret_cast<uint32_t *>(wsb + w.status)));
     return launch_attend(d, w, T, nullptr, *cache, n_past, q, q_type, out, wsb, st);
 }
 

@@ -45,6 +45,14 @@ cudaError_t launch_prefill_scores_tc(const DevDesc & d, cudaStream_t st, const f
 cudaError_t launch_select_scores_warp(const DevDesc & d, cudaStream_t st, int n_past0, int T, const float * scores,
                                       int scores_stride, int * sel_ws, int * nsel_ws, int * sel_out, uint32_t * status);
 
+// KV-stationary prefill attention on tcgen05 (qsa_prefill_attn.cu): q8_0, ratio 64, 8 query heads
+// per KV head.  Workspace: prefill_kv_workspace bytes at `ws`.
+bool prefill_kv_supported(const DevDesc & d);
+size_t prefill_kv_workspace(const DevDesc & d, int T, int n_blocks);
+cudaError_t launch_prefill_attn_kv(const DevDesc & d, cudaStream_t st, qsa_layer_cache cache, int n_past0, int T,
+                                   const void * q, int q_type, const int * sel, const int * nsel, int n_blocks,
+                                   unsigned char * ws, float * out, uint32_t * status);
+
 // KV-sequence-sharded decode: global selection from all shards' candidates, and the log-sum-exp
 // merge of the shards' attention states (qsa_shard.cu).
 cudaError_t launch_shard_select(const DevDesc & d, cudaStream_t st, const qsa_decode_item * items, int n_shards,

@@ -200,6 +200,30 @@ def test_prefill_parity_and_chunk_invariance():
         assert rel_err(out1[t], ref) <= ATTN_TOL
 
 
+@pytest.mark.parametrize("kv_type", [TYPE_Q8_0, TYPE_F16])
+def test_prefill_ignores_unwritten_cells(kv_type):
+    """Cells at or past n_past + T of the last block are never written; with their bytes all 0xFF
+    (NaN scales and values) the output must still be finite and equal the oracle's."""
+    d = desc_for(kv_type, 8192)
+    node, st = QsaNode(d), QsaState(d)
+    for t in st.k + st.v + st.idx:
+        t.fill_(-1)
+    n_past, T = 3010, 100                         # ends inside block 48 (cells 3072..3135)
+    fill_cache(node, st, 0, n_past, 61)
+    q, q_idx, k, v, ki = token_inputs(d, T, 62)
+    sel = torch.empty(T, k_blocks(d), dtype=torch.int32, device="cuda")
+    out = node.sparse_attn(st.layer(), n_past, q, q_idx, k, v, ki, sel_out=sel)
+    torch.cuda.synchronize()
+    assert node.check(node.workspace("prefill", T, n_past + T)) == QSA_OK
+    out, sel = out.cpu().numpy(), sel.cpu().numpy()
+    assert np.isfinite(out).all()
+    kc, vc, _, _ = host_caches(st, 0, n_past + T)
+    qh, qt = q_host(q)
+    for t in [0, 37, 61, T - 1]:
+        ref = oracle.attend(d, kc, vc, [n_past + t], sel[t][None], qh[t][None], q_type=qt)[0]
+        assert rel_err(out[t], ref) <= ATTN_TOL
+
+
 def test_decode_equals_prefill_at_same_position():
     d = desc_for(TYPE_Q8_0, 8192)
     n_past, T = 4000, 70
