@@ -266,7 +266,7 @@ size_t qsa_decode_workspace_size(const qsa_desc * dd, int32_t batch, int32_t max
 
 namespace {
 // The prefill's KV-stationary attention applies (and how many blocks its buckets cover).
-bool prefill_kv_path(const DevDesc & d, int T) { return T >= 64 && prefill_kv_supported(d); }
+bool prefill_kv_path(const DevDesc & d, int T) { return T >= 64 && prefill_kv_supported(d, T); }
 int prefill_n_blocks(const DevDesc & d, int max_n_kv) { return std::max(1, ceil_div(max_n_kv, d.ratio)); }
 }  // namespace
 
@@ -363,7 +363,9 @@ qsa_status qsa_prefill(const qsa_desc * dd, const qsa_layer_cache * cache, int32
     if (any_new && !(k_new && v_new && kidx_new)) return QSA_ERR_INVALID;
     const DevDesc d = make_dev(dd);
     const WsLayout w = ws_layout(d, T, n_past + T);
-    const bool kv_path = prefill_kv_path(d, T);
+    // the block-grouped path reads the caches with TMA, which wants 16-byte aligned rows
+    const bool kv_path = prefill_kv_path(d, T) && reinterpret_cast<uintptr_t>(cache->k) % 16 == 0 &&
+                         reinterpret_cast<uintptr_t>(cache->v) % 16 == 0;
     const size_t need = kv_path ? w.total + prefill_kv_workspace(d, T, prefill_n_blocks(d, n_past + T)) : w.total;
     if (!ws || ws_bytes < need) return QSA_ERR_WORKSPACE;
     if ((s = set_attrs()) != QSA_OK) return s;

@@ -47,7 +47,7 @@ cudaError_t launch_select_scores_warp(const DevDesc & d, cudaStream_t st, int n_
 
 // KV-stationary prefill attention on tcgen05 (qsa_prefill_attn.cu): q8_0, ratio 64, 8 query heads
 // per KV head.  Workspace: prefill_kv_workspace bytes at `ws`.
-bool prefill_kv_supported(const DevDesc & d);
+bool prefill_kv_supported(const DevDesc & d, int T);
 size_t prefill_kv_workspace(const DevDesc & d, int T, int n_blocks);
 cudaError_t launch_prefill_attn_kv(const DevDesc & d, cudaStream_t st, qsa_layer_cache cache, int n_past0, int T,
                                    const void * q, int q_type, const int * sel, const int * nsel, int n_blocks,

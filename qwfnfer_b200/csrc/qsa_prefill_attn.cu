@@ -9,23 +9,29 @@
 // every query that selected it (about 200 times per block in an 8192-token chunk).  Here the work
 // is grouped by block instead:
 //   1. prefill_bucket_*: the (query, slot) pairs of the chunk's selections are bucketed by block
-//      (counting sort: counts, one scan, a fill); prefill_q16_kernel converts Q to f16 rows;
+//      (counting sort: counts, one scan, a fill that also records each pair's bucket position,
+//      its "entry"); prefill_q16_kernel converts Q to f16 rows;
 //   2. prefill_attn_kv_kernel, CTA = (block, KV head): the block's K and V rows of that head are
 //      dequantised once into shared memory (f16 of d x q, the rounding of the reference's decode
 //      gather); then the CTA walks its queries 16 at a time (16 x 8 query heads = 128 rows) in a
 //      warp-specialised pipeline:
-//        warp 8      TMA loads of the 16 queries' Q rows (128-byte swizzle) -> sQ
+//        warp 8      TMA loads of the block's raw q8_0 rows, then of the 16 queries' Q rows
+//                    (128-byte swizzle) into one of two Q stages
 //        warp 9      one thread issues S = Q K^T (16 tcgen05.mma, M=128, N=64 cells, K=16) into one
 //                    of two TMEM S buffers, and O = P V (4 tcgen05.mma, M=128, N=256, K=16) into
-//                    TMEM; S of chunk i+1 is issued before O of chunk i
+//                    TMEM, each as soon as its inputs are ready (non-blocking barrier tests)
 //        warps 0-3   thread = row = TMEM lane: S from TMEM, mask of the cells past the query,
 //                    P = 2^(s - m) (f16) -> sP, row maximum and sum -> shared memory
-//        warps 4-7   thread = row: O from TMEM, O / l (f16) -> swizzled staging in shared memory,
-//                    then TMA tensor stores of the rows (query t, slot j, head) to the partials,
-//                    and (m, l) of the row
-//   3. prefill_merge_kernel: per query, a warp per head merges its slots' partials (log-sum-exp).
-// Operands are K-major with the 128-byte swizzle: Q [128 rows][256 dims], K [64 cells][256 dims],
-// V^T [256 dims][64 cells], P [128 rows][64 cells]; the O staging has Q's layout.
+//        warps 4-7   thread = row: O from TMEM, O / l (f16) -> the chunk's Q stage (free once its
+//                    S MMAs are done), then TMA tensor stores of the chunk's 128 rows, and (m, l)
+//                    of each row; the stage is loaded again after the stores have read it
+//      The partials are entry-major, [KV head][entry][8 query heads][256], so a chunk's rows are
+//      contiguous (four 16 KB boxes);
+//   3. prefill_merge_kernel: per query, a warp per head merges its slots' partials (log-sum-exp),
+//      finding each slot's row through the entry recorded for it.
+// Operands are K-major with the 128-byte swizzle: Q [16 queries][4 atoms of 64 dims][8 rows],
+// K [64 cells][256 dims], V^T [256 dims][64 cells], P [128 rows][64 cells]; the O rows staged for
+// the stores have Q's layout, so that one TMA box moves a query's rows (4 KB) or a chunk's (64 KB).
 #include <cuda.h>          // CUtensorMap and its enums; the encoder is reached through the runtime
 
 #include "qsa_kernels.cuh"
@@ -41,15 +47,26 @@ constexpr int PA_SQ = PA_ROWS * HEAD_DIM * 2;      // 64 KB
 constexpr int PA_SK = PA_CELLS * HEAD_DIM * 2;     // 32 KB
 constexpr int PA_SV = HEAD_DIM * PA_CELLS * 2;     // 32 KB
 constexpr int PA_SP = PA_ROWS * PA_CELLS * 2;      // 16 KB
-constexpr int PA_SO = PA_ROWS * HEAD_DIM * 2;      // 64 KB of O staging
-constexpr int PA_SMEM = PA_SQ + PA_SK + PA_SV + PA_SP + PA_SO + 1024;
-constexpr int PA_ATOM_Q = PA_ROWS * 128;           // bytes of one 64-column atom of sQ / sO
+constexpr int PA_SMEM = 2 * PA_SQ + PA_SK + PA_SV + PA_SP + 1024;
+constexpr int PA_HEAD_Q8 = HEAD_DIM / QK8_0 * Q8_0_BYTES;   // 272 bytes of one head's q8_0 row
+constexpr int PA_QROWS = 8 * HEAD_DIM * 2;         // 4 KB: one query's 8 head rows in a Q stage
 constexpr uint32_t PA_TMEM_COLS = 512;             // S buffers: columns 0..63, 64..127; O: 256..511
 constexpr uint32_t PA_TMEM_O = 256;
 constexpr uint32_t PA_IDESC_S = umma_idesc_f16(PA_ROWS, PA_CELLS);
 constexpr uint32_t PA_IDESC_O = umma_idesc_f16(PA_ROWS, HEAD_DIM);
 constexpr int PA_SLOT_SHIFT = 10;                  // entry = query << 10 | slot (slot < MAX_KB)
-constexpr int PA_BOX_BYTES = 8 * 128;              // a TMA box: 8 rows x 64 f16
+// A Q stage (and the O rows staged in it) is [query][64-column atom][8 rows][128 bytes] with the
+// 128-byte swizzle inside each 1 KB (8 rows x 128 bytes): the MMA reads it as a K-major operand
+// whose 8-row groups are 4 KB apart, and one 4-D TMA box moves a query's 4 KB.
+__device__ __forceinline__ uint32_t q_stage_off(int r, int k) {
+    return (uint32_t) ((r >> 3) * PA_QROWS + (k >> 6) * 1024 + (r & 7) * 128 + ((((k >> 3) & 7) ^ (r & 7)) << 4) +
+                       ((k & 7) << 1));
+}
+// shared-memory descriptor of a 128-byte-swizzled K-major operand whose 8-row groups are sbo bytes apart
+__device__ __forceinline__ uint64_t umma_desc_sw128_sbo(uint32_t smem_addr, uint32_t sbo) {
+    return (uint64_t) ((smem_addr >> 4) & 0x3FFFu) | ((uint64_t) 1 << 16) | ((uint64_t) ((sbo >> 4) & 0x3FFFu) << 32) |
+           ((uint64_t) 1 << 46) | ((uint64_t) 2 << 61);
+}
 
 // ------------------------------------------------------------------ bucketing by block
 __global__ void prefill_bucket_count_kernel(const DevDesc d, int T, const int * __restrict__ sel,
@@ -100,16 +117,21 @@ __global__ void __launch_bounds__(1024) prefill_bucket_scan_kernel(const int * _
     if (tid == 0) offsets[n_blocks] = carry;
 }
 
+// entries[pos] = query << 10 | slot, and entry_of[query * kb + slot] = pos (-1 for no block)
 __global__ void prefill_bucket_fill_kernel(const DevDesc d, int T, const int * __restrict__ sel,
                                            const int * __restrict__ nsel, int n_blocks, int * __restrict__ cursor,
-                                           uint32_t * __restrict__ entries) {
+                                           uint32_t * __restrict__ entries, int * __restrict__ entry_of) {
     const int64_t i = (int64_t) blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (int64_t) T * d.kb) return;
     const int t = (int) (i / d.kb), j = (int) (i % d.kb);
-    if (j >= nsel[t]) return;
-    const int b = sel[i];
-    if (b < 0 || b >= n_blocks) return;
-    entries[atomicAdd(&cursor[b], 1)] = ((uint32_t) t << PA_SLOT_SHIFT) | (uint32_t) j;
+    const int b = j < nsel[t] ? sel[i] : -1;
+    if (b < 0 || b >= n_blocks) {
+        entry_of[i] = -1;
+        return;
+    }
+    const int pos = atomicAdd(&cursor[b], 1);
+    entries[pos] = ((uint32_t) t << PA_SLOT_SHIFT) | (uint32_t) j;
+    entry_of[i] = pos;
 }
 
 // Q (bf16 or f32, [T][n_head][256]) -> f16 rows [T * n_head][256], 8 values per thread
@@ -134,9 +156,34 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap * ma
     asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
                  :: "r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)) : "memory");
 }
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap * map, int x, int y, uint32_t src) {
-    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];"
-                 :: "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(src) : "memory");
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap * map, int w, uint64_t * bar) {
+    asm volatile("cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %2, %2, %3}], [%4];"
+                 :: "r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(w), "r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap * map, int w, uint32_t src) {
+    asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%1, %1, %1, %2}], [%3];"
+                 :: "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(w), "r"(src) : "memory");
+}
+// non-blocking probe of a phase (the MMA thread polls two streams of work with it)
+__device__ __forceinline__ bool mbar_test(uint64_t * bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(done) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+    return done != 0;
+}
+// Bounded wait by polling (no suspension): a thread suspended on a phase that other threads'
+// arrivals complete was seen to resume microseconds late, so the loader polls.
+__device__ __forceinline__ bool mbar_poll_bounded(uint64_t * bar, uint32_t parity, uint32_t * status) {
+    if (mbar_test(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (int k = 1;; k++) {
+        if (mbar_test(bar, parity)) return true;
+        if ((k & 63) == 0 && global_timer_ns() - t0 > 2000000000ull) break;
+    }
+    set_status(status, DEV_TIMEOUT);
+    return false;
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
@@ -159,7 +206,9 @@ __device__ __forceinline__ uint32_t f16x2_scaled(int8_t a, int8_t b, float d) {
 }
 
 struct PaBarriers {
-    uint64_t q_full, q_empty;         // sQ loaded (TMA bytes) / read by the S MMAs (commit)
+    uint64_t kv_full;                 // raw q8_0 rows of the block copied in (bulk-copy bytes)
+    uint64_t q_full[2], q_empty[2];   // Q stage loaded (TMA bytes) / free again: its S MMAs and the
+                                      // TMA stores of the O rows staged in it are done (128 arrivals)
     uint64_t s_full[2], s_empty[2];   // S buffer written (commit) / read by the 128 softmax threads
     uint64_t p_full, p_empty;         // sP written by the softmax threads / read by the O MMAs (commit)
     uint64_t o_full, o_empty;         // O in TMEM (commit) / read by the 128 epilogue threads
@@ -168,9 +217,11 @@ struct PaBarriers {
 };
 
 __global__ void __launch_bounds__(PA_THREADS, 1) prefill_attn_kv_kernel(
-        const __grid_constant__ CUtensorMap q_map, const __grid_constant__ CUtensorMap o_map, DevDesc d,
-        qsa_layer_cache cache, int n_past0, int n_kv, const uint32_t * __restrict__ entries,
-        const int * __restrict__ offsets, float * __restrict__ part_ml, uint32_t * __restrict__ status) {
+        const __grid_constant__ CUtensorMap q_map, const __grid_constant__ CUtensorMap o_map,
+        const __grid_constant__ CUtensorMap o1_map, const __grid_constant__ CUtensorMap k_map,
+        const __grid_constant__ CUtensorMap v_map, DevDesc d, int n_past0, int n_kv, int slots,
+        const uint32_t * __restrict__ entries, const int * __restrict__ offsets, float * __restrict__ part_ml,
+        uint32_t * __restrict__ status) {
     extern __shared__ __align__(1024) unsigned char pa_smem_raw[];
     __shared__ PaBarriers bars;
     __shared__ uint32_t tmem_slot;
@@ -182,17 +233,22 @@ __global__ void __launch_bounds__(PA_THREADS, 1) prefill_attn_kv_kernel(
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t raw = smem_u32(pa_smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
-    unsigned char * sK = pa_smem_raw + (base - raw) + PA_SQ;
+    unsigned char * sQ0 = pa_smem_raw + (base - raw);       // two Q stages; a stage also holds the
+    unsigned char * sK = sQ0 + 2 * PA_SQ;                   // O rows of its chunk for the TMA stores
     unsigned char * sV = sK + PA_SK;                        // V^T [256 dims][64 cells]
     unsigned char * sP = sV + PA_SV;
-    unsigned char * sO = sP + PA_SP;
-    const uint32_t aQ = base, aK = base + PA_SQ, aV = aK + PA_SK, aP = aV + PA_SV, aO = aP + PA_SP;
+    const uint32_t aQ0 = base, aK = base + 2 * PA_SQ, aV = aK + PA_SK, aP = aV + PA_SV;
+    // the raw q8_0 rows (head g: 272 bytes of a 544-byte row) land in Q stage 1 before chunk 1 does
+    unsigned char * rawK = sQ0 + PA_SQ;
+    unsigned char * rawV = rawK + PA_CELLS * PA_HEAD_Q8;
+    const int n_valid = min(PA_CELLS, n_kv - b * PA_CELLS);
 
     if (warp == 0) tmem_alloc_warp(&tmem_slot, PA_TMEM_COLS);
     if (tid == 32) {
-        mbar_init(&bars.q_full, 1);
-        mbar_init(&bars.q_empty, 1);
+        mbar_init(&bars.kv_full, 1);
         for (int k = 0; k < 2; k++) {
+            mbar_init(&bars.q_full[k], 1);
+            mbar_init(&bars.q_empty[k], PA_ROWS);
             mbar_init(&bars.s_full[k], 1);
             mbar_init(&bars.s_empty[k], PA_ROWS);
             mbar_init(&bars.meta_full[k], PA_ROWS);
@@ -205,31 +261,38 @@ __global__ void __launch_bounds__(PA_THREADS, 1) prefill_attn_kv_kernel(
         fence_mbar_init();
     }
     __syncthreads();
-    // the loader issues the first chunk's Q rows before the dequantisation below
-    auto load_q = [&](int i) {
-        const int c0 = e0 + i * PA_QC, nq = min(PA_QC, e1 - c0);
-        if (lane == 0) mbar_arrive_expect_tx(&bars.q_full, (uint32_t) (nq * 4 * PA_BOX_BYTES));
-        __syncwarp();
-        if (lane < nq) {
-            const int t = (int) (entries[c0 + lane] >> PA_SLOT_SHIFT);
-            const int y = t * d.n_head + g * d.gqa;
-            #pragma unroll
-            for (int a = 0; a < 4; a++) tma_load_2d(aQ + a * PA_ATOM_Q + lane * PA_BOX_BYTES, &q_map, a * 64, y, &bars.q_full);
-        }
+    auto chunk_entry = [&](int i, int k) -> uint32_t {     // entry k of chunk i, or ~0u past its end
+        const int c = e0 + i * PA_QC + k;
+        return k < PA_QC && c < e1 ? entries[c] : ~0u;
     };
-    if (warp == 8) load_q(0);
+    // Q rows of chunk i into stage i % 2 (the whole loader warp; lane k holds entry k of the chunk)
+    auto load_q = [&](int i, uint32_t e) {
+        const int s = i & 1, nq = min(PA_QC, e1 - (e0 + i * PA_QC));
+        if (lane == 0) mbar_arrive_expect_tx(&bars.q_full[s], (uint32_t) (nq * PA_QROWS));
+        __syncwarp();
+        if (lane < nq)          // query t's rows of KV head g: 8-row group t * n_head_kv + g of Q
+            tma_load_4d(aQ0 + s * PA_SQ + lane * PA_QROWS, &q_map, (int) (e >> PA_SLOT_SHIFT) * d.n_head_kv + g,
+                        &bars.q_full[s]);
+    };
+    if (warp == 8) {
+        // the block's raw K and V rows of head g: one box of 64 rows x 272 bytes each (the bytes of
+        // cells past n_kv are fetched too, and ignored)
+        if (lane == 0) {
+            mbar_arrive_expect_tx(&bars.kv_full, (uint32_t) (2 * PA_CELLS * PA_HEAD_Q8));
+            tma_load_2d(smem_u32(rawK), &k_map, g * (PA_HEAD_Q8 / 2), b * PA_CELLS, &bars.kv_full);
+            tma_load_2d(smem_u32(rawV), &v_map, g * (PA_HEAD_Q8 / 2), b * PA_CELLS, &bars.kv_full);
+        }
+        load_q(0, chunk_entry(0, lane));
+    }
+    mbar_wait_bounded(&bars.kv_full, 0u, status);
 
-    // ---- K and V of head g of block b -> f16 (d x q), K as [cell][dim], V as [dim][cell]; cells at
-    // or past n_kv were never written (their bytes may decode to Inf or NaN, and a masked P of 0
-    // times a NaN of V is NaN in the MMA), so they are zero
-    const int n_valid = min(PA_CELLS, n_kv - b * PA_CELLS);
-    const uint8_t * krow0 = (const uint8_t *) cache.k + (size_t) b * PA_CELLS * d.rb_k + (size_t) g * d.hb_k;
-    const uint8_t * vrow0 = (const uint8_t *) cache.v + (size_t) b * PA_CELLS * d.rb_v + (size_t) g * d.hb_v;
+    // ---- K and V -> f16 (d x q), K as [cell][dim], V as [dim][cell]; cells at or past n_kv are
+    // zero (their bytes may decode to Inf or NaN, and a masked P of 0 times a NaN is NaN in the MMA)
     for (int i = tid; i < PA_CELLS * (HEAD_DIM / 8); i += PA_THREADS) {      // (cell, 8-dim group)
         const int cell = i >> 5, d8 = i & 31;
         uint4 w = make_uint4(0, 0, 0, 0);
         if (cell < n_valid) {
-            const uint8_t * blk = krow0 + (size_t) cell * d.rb_k + (d8 >> 2) * Q8_0_BYTES;
+            const unsigned char * blk = rawK + cell * PA_HEAD_Q8 + (d8 >> 2) * Q8_0_BYTES;
             const float sc = f16_bits_to_f32(*reinterpret_cast<const uint16_t *>(blk));
             const int8_t * qs = reinterpret_cast<const int8_t *>(blk + 2) + (d8 & 3) * 8;
             w.x = f16x2_scaled(qs[0], qs[1], sc); w.y = f16x2_scaled(qs[2], qs[3], sc);
@@ -243,7 +306,7 @@ __global__ void __launch_bounds__(PA_THREADS, 1) prefill_attn_kv_kernel(
         #pragma unroll
         for (int c = 0; c < 8; c++) {
             if (c8 * 8 + c < n_valid) {
-                const uint8_t * blk = vrow0 + (size_t) (c8 * 8 + c) * d.rb_v + (d8 >> 2) * Q8_0_BYTES;
+                const unsigned char * blk = rawV + (c8 * 8 + c) * PA_HEAD_Q8 + (d8 >> 2) * Q8_0_BYTES;
                 const float sc = f16_bits_to_f32(*reinterpret_cast<const uint16_t *>(blk));
                 const int8_t * qs = reinterpret_cast<const int8_t *>(blk + 2) + (d8 & 3) * 8;
                 #pragma unroll
@@ -261,8 +324,8 @@ __global__ void __launch_bounds__(PA_THREADS, 1) prefill_attn_kv_kernel(
             *reinterpret_cast<uint4 *>(sV + sw128_off(HEAD_DIM, d8 * 8 + k, c8 * 8)) = w;
         }
     }
-    fence_async_smem();                                     // K and V tiles visible to the tensor core
-    tc_fence_before();
+    fence_async_smem();                                     // K and V tiles visible to the tensor core,
+    tc_fence_before();                                      // and stage 1 free for the TMA
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tmem_slot;
@@ -271,41 +334,58 @@ __global__ void __launch_bounds__(PA_THREADS, 1) prefill_attn_kv_kernel(
         // ---------------------------------------------------------------- Q loads
         int i = 1;
         for (; i < n_chunks; i++) {
-            if (!mbar_wait_bounded(&bars.q_empty, (uint32_t) ((i - 1) & 1), status)) break;   // S MMAs of i-1 done
-            load_q(i);
+            const uint32_t e = chunk_entry(i, lane);
+            // stage i % 2 is free once the O rows of chunk i-2 have been read out of it
+            int ok = 1;
+            if (i >= 2 && lane == 0) ok = mbar_poll_bounded(&bars.q_empty[i & 1], (uint32_t) (((i - 2) >> 1) & 1), status);
+            if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+            load_q(i, e);
         }
         // every issued load has landed before the CTA can leave
-        mbar_wait_bounded(&bars.q_full, (uint32_t) ((i - 1) & 1), status);
+        mbar_wait_bounded(&bars.q_full[(i - 1) & 1], (uint32_t) (((i - 1) >> 1) & 1), status);
     } else if (warp == 9) {
         // ---------------------------------------------------------------- MMA issue (one thread)
+        // S of chunk ns (Q loaded, its S buffer read out) and O of chunk no (P written, the previous
+        // O read out) are issued as soon as they are ready, in whichever order that happens
         if (lane == 0) {
-            bool ok = true;
-            auto issue_s = [&](int i) {
-                const int buf = i & 1;
-                ok = ok && mbar_wait_bounded(&bars.q_full, (uint32_t) (i & 1), status);
-                if (i >= 2) ok = ok && mbar_wait_bounded(&bars.s_empty[buf], (uint32_t) (((i - 2) >> 1) & 1), status);
-                if (!ok) return;
-                tc_fence_after();
-                #pragma unroll
-                for (int kk = 0; kk < HEAD_DIM / 16; kk++)
-                    umma_f16(tmem + (uint32_t) (buf * PA_CELLS),
-                             umma_desc_sw128(aQ + (kk >> 2) * PA_ATOM_Q + (kk & 3) * 32),
-                             umma_desc_sw128(aK + (kk >> 2) * (PA_CELLS * 128) + (kk & 3) * 32), PA_IDESC_S, kk > 0);
-                umma_commit(&bars.s_full[buf]);
-                umma_commit(&bars.q_empty);
-            };
-            issue_s(0);
-            for (int i = 0; i < n_chunks && ok; i++) {
-                if (i + 1 < n_chunks) issue_s(i + 1);
-                ok = ok && mbar_wait_bounded(&bars.p_full, (uint32_t) (i & 1), status);
-                if (i >= 1) ok = ok && mbar_wait_bounded(&bars.o_empty, (uint32_t) ((i - 1) & 1), status);
-                if (!ok) break;
-                tc_fence_after();
-                #pragma unroll
-                for (int kk = 0; kk < PA_CELLS / 16; kk++)
-                    umma_f16(tmem + PA_TMEM_O, umma_desc_sw128(aP + kk * 32), umma_desc_sw128(aV + kk * 32), PA_IDESC_O, kk > 0);
-                umma_commit(&bars.o_full);
-                umma_commit(&bars.p_empty);
+            int ns = 0, no = 0;
+            uint64_t t_last = global_timer_ns();
+            while (no < n_chunks) {
+                bool progress = false;
+                if (ns < n_chunks && ns <= no + 2) {
+                    const int s = ns & 1;
+                    if (mbar_test(&bars.q_full[s], (uint32_t) ((ns >> 1) & 1)) &&
+                        (ns < 2 || mbar_test(&bars.s_empty[s], (uint32_t) (((ns - 2) >> 1) & 1)))) {
+                        tc_fence_after();
+                        const uint32_t aQ = aQ0 + s * PA_SQ;
+                        #pragma unroll
+                        for (int kk = 0; kk < HEAD_DIM / 16; kk++)
+                            umma_f16(tmem + (uint32_t) (s * PA_CELLS),
+                                     umma_desc_sw128_sbo(aQ + (kk >> 2) * 1024 + (kk & 3) * 32, PA_QROWS),
+                                     umma_desc_sw128(aK + (kk >> 2) * (PA_CELLS * 128) + (kk & 3) * 32), PA_IDESC_S, kk > 0);
+                        umma_commit(&bars.s_full[s]);
+                        ns++;
+                        progress = true;
+                    }
+                }
+                if (no < ns && mbar_test(&bars.p_full, (uint32_t) (no & 1)) &&
+                    (no < 1 || mbar_test(&bars.o_empty, (uint32_t) ((no - 1) & 1)))) {
+                    tc_fence_after();
+                    #pragma unroll
+                    for (int kk = 0; kk < PA_CELLS / 16; kk++)
+                        umma_f16(tmem + PA_TMEM_O, umma_desc_sw128(aP + kk * 32), umma_desc_sw128(aV + kk * 32), PA_IDESC_O, kk > 0);
+                    umma_commit(&bars.o_full);
+                    umma_commit(&bars.p_empty);
+                    no++;
+                    progress = true;
+                }
+                const uint64_t now = global_timer_ns();
+                if (progress) {
+                    t_last = now;
+                } else if (now - t_last > 2000000000ull) {
+                    set_status(status, DEV_TIMEOUT);
+                    break;
+                }
             }
             umma_commit(&bars.mma_done);                     // every MMA issued above has completed
             mbar_wait_bounded(&bars.mma_done, 0u, status);
@@ -316,7 +396,10 @@ __global__ void __launch_bounds__(PA_THREADS, 1) prefill_attn_kv_kernel(
         const int r = tid, qi = r >> 3;
         const uint32_t lane_base = (uint32_t) (warp * 32) << 16;
         for (int i = 0; i < n_chunks; i++) {
-            const int buf = i & 1, c0 = e0 + i * PA_QC, nq = min(PA_QC, e1 - c0);
+            const int buf = i & 1;
+            const uint32_t e = chunk_entry(i, qi);
+            int lim = -1;                                     // cells 0..lim of the block are visible
+            if (e != ~0u) lim = n_past0 + (int) (e >> PA_SLOT_SHIFT) - b * PA_CELLS;
             if (!mbar_wait_bounded(&bars.s_full[buf], (uint32_t) ((i >> 1) & 1), status)) break;
             tc_fence_after();
             uint32_t v[32], u[32];
@@ -325,8 +408,6 @@ __global__ void __launch_bounds__(PA_THREADS, 1) prefill_attn_kv_kernel(
             tmem_ld_wait();
             tc_fence_before();
             mbar_arrive(&bars.s_empty[buf]);
-            int lim = -1;                                     // cells 0..lim of the block are visible
-            if (qi < nq) lim = n_past0 + (int) (entries[c0 + qi] >> PA_SLOT_SHIFT) - b * PA_CELLS;
             float s[64];
             float m = -INFINITY;
             #pragma unroll
@@ -360,50 +441,55 @@ __global__ void __launch_bounds__(PA_THREADS, 1) prefill_attn_kv_kernel(
         }
     } else {
         // ---------------------------------------------------------------- epilogue, thread = row
-        const int r = tid - 128, qi = r >> 3, h = r & 7;
+        const int r = tid - 128, qi = r >> 3;
         const uint32_t lane_base = (uint32_t) ((warp - 4) * 32) << 16;
         for (int i = 0; i < n_chunks; i++) {
-            const int buf = i & 1, c0 = e0 + i * PA_QC, nq = min(PA_QC, e1 - c0);
+            const int buf = i & 1;
+            const int c0 = e0 + i * PA_QC, nq = min(PA_QC, e1 - c0);
             bool ok = mbar_wait_bounded(&bars.meta_full[buf], (uint32_t) ((i >> 1) & 1), status);
             const float m = row_m[buf][r], l = row_l[buf][r];
             ok = ok && mbar_wait_bounded(&bars.o_full, (uint32_t) (i & 1), status);
-            if (r < PA_QC) bulk_wait_read_all();              // this thread's stores of chunk i-1 have read sO
             if (!epilogue_all(ok)) break;
             tc_fence_after();
+            // O / l as f16 into the chunk's Q stage (its S MMAs finished before this O was made)
+            unsigned char * stage = sQ0 + buf * PA_SQ;
             const float inv = l > 0.0f ? 1.0f / l : 0.0f;
             #pragma unroll 1
-            for (int c0v = 0; c0v < HEAD_DIM; c0v += 32) {
-                uint32_t v[32];
-                tmem_ld32(tmem + lane_base + PA_TMEM_O + (uint32_t) c0v, v);
+            for (int c0v = 0; c0v < HEAD_DIM; c0v += 64) {
+                uint32_t v[2][32];
+                tmem_ld32(tmem + lane_base + PA_TMEM_O + (uint32_t) c0v, v[0]);
+                tmem_ld32(tmem + lane_base + PA_TMEM_O + (uint32_t) (c0v + 32), v[1]);
                 tmem_ld_wait();
                 #pragma unroll
-                for (int k = 0; k < 4; k++)
-                    *reinterpret_cast<uint4 *>(sO + sw128_off(PA_ROWS, r, c0v + 8 * k)) =
-                        make_uint4(pack_f16x2(__uint_as_float(v[8 * k]) * inv, __uint_as_float(v[8 * k + 1]) * inv),
-                                   pack_f16x2(__uint_as_float(v[8 * k + 2]) * inv, __uint_as_float(v[8 * k + 3]) * inv),
-                                   pack_f16x2(__uint_as_float(v[8 * k + 4]) * inv, __uint_as_float(v[8 * k + 5]) * inv),
-                                   pack_f16x2(__uint_as_float(v[8 * k + 6]) * inv, __uint_as_float(v[8 * k + 7]) * inv));
+                for (int hh = 0; hh < 2; hh++)
+                    #pragma unroll
+                    for (int k = 0; k < 4; k++)
+                        *reinterpret_cast<uint4 *>(stage + q_stage_off(r, c0v + 32 * hh + 8 * k)) =
+                            make_uint4(pack_f16x2(__uint_as_float(v[hh][8 * k]) * inv, __uint_as_float(v[hh][8 * k + 1]) * inv),
+                                       pack_f16x2(__uint_as_float(v[hh][8 * k + 2]) * inv, __uint_as_float(v[hh][8 * k + 3]) * inv),
+                                       pack_f16x2(__uint_as_float(v[hh][8 * k + 4]) * inv, __uint_as_float(v[hh][8 * k + 5]) * inv),
+                                       pack_f16x2(__uint_as_float(v[hh][8 * k + 6]) * inv, __uint_as_float(v[hh][8 * k + 7]) * inv));
             }
             tc_fence_before();
             mbar_arrive(&bars.o_empty);
-            if (qi < nq) {
-                const uint32_t e = entries[c0 + qi];
-                const size_t slot = ((size_t) (e >> PA_SLOT_SHIFT) * d.kb + (e & ((1u << PA_SLOT_SHIFT) - 1))) * d.n_head +
-                                    g * d.gqa + h;
-                *reinterpret_cast<float2 *>(part_ml + slot * 2) = make_float2(m, l);
-            }
+            // row (KV head g, entry c, query head h) of the partials; the chunk's rows are contiguous
+            const int y0 = (g * slots + c0) * GQA_TILE;
+            if (qi < nq) *reinterpret_cast<float2 *>(part_ml + ((size_t) y0 + r) * 2) = make_float2(m, l);
             fence_async_smem();                               // staging visible to the TMA unit
             epilogue_sync();
-            if (r < nq) {                                     // thread q stores query q's 8 rows
-                const uint32_t e = entries[c0 + r];
-                const int y = (int) (((e >> PA_SLOT_SHIFT) * (uint32_t) d.kb + (e & ((1u << PA_SLOT_SHIFT) - 1))) *
-                                     (uint32_t) d.n_head) + g * d.gqa;
-                #pragma unroll
-                for (int a = 0; a < 4; a++) tma_store_2d(&o_map, a * 64, y, aO + a * PA_ATOM_Q + r * PA_BOX_BYTES);
+            if (r == 0) {               // 8-row group w of the partials = (KV head g, entry w - g * slots)
+                const uint32_t st0 = aQ0 + buf * PA_SQ;
+                if (nq == PA_QC) {
+                    tma_store_4d(&o_map, g * slots + c0, st0);
+                } else {
+                    for (int q = 0; q < nq; q++) tma_store_4d(&o1_map, g * slots + c0 + q, st0 + q * PA_QROWS);
+                }
                 bulk_commit();
+                bulk_wait_read_all();                         // the stage may be loaded again
             }
+            mbar_arrive(&bars.q_empty[buf]);
         }
-        if (r < PA_QC) bulk_wait_all();                       // the partials are written before the CTA ends
+        if (r == 0) bulk_wait_all();                          // the partials are written before the CTA ends
     }
     tc_fence_before();
     __syncthreads();
@@ -412,22 +498,35 @@ __global__ void __launch_bounds__(PA_THREADS, 1) prefill_attn_kv_kernel(
 }
 
 // ------------------------------------------------------------------ merge per query
-// CTA = query t, warp = head h, lane = 8 dimensions: the weights 2^(m_j - M) l_j of the slots go
-// to shared memory, then every slot's 512-byte partial row is read once, coalesced.
-__global__ void prefill_merge_kernel(DevDesc d, int T, const int * __restrict__ nsel,
-        const __half * __restrict__ part_o, const float * __restrict__ part_ml, float * __restrict__ out) {
-    extern __shared__ float pm_w[];                          // [n_head][kb]
+// CTA = query t, warp = head h, lane = 8 dimensions: each slot's partial row (through its entry)
+// and weight 2^(m_j - M) l_j go to shared memory, then every row's 512 bytes are read once,
+// coalesced.
+__global__ void prefill_merge_kernel(DevDesc d, int T, int slots, const int * __restrict__ nsel,
+        const int * __restrict__ entry_of, const __half * __restrict__ part_o, const float * __restrict__ part_ml,
+        float * __restrict__ out) {
+    extern __shared__ float pm_smem[];                       // [n_head][kb] weights, [n_head][kb] rows
     const int t = blockIdx.x, h = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n = max(0, min(nsel[t], d.kb));
-    float * w = pm_w + h * d.kb;
+    float * w = pm_smem + h * d.kb;
+    int * rows = reinterpret_cast<int *>(pm_smem + d.n_head * d.kb) + h * d.kb;
+    const int g = h / d.gqa, hh = h % d.gqa;
     float M = -INFINITY;
-    for (int j = lane; j < n; j += 32) M = fmaxf(M, part_ml[(((size_t) t * d.kb + j) * d.n_head + h) * 2]);
+    for (int j = lane; j < n; j += 32) {
+        const int e = entry_of[(size_t) t * d.kb + j];
+        const int row = e < 0 ? -1 : (g * slots + e) * d.gqa + hh;
+        rows[j] = row;
+        if (row >= 0) M = fmaxf(M, part_ml[(size_t) row * 2]);
+    }
     M = warp_max(M);
     const float Mu = M == -INFINITY ? 0.0f : M;
     float Wl = 0.0f;
     for (int j = lane; j < n; j += 32) {
-        const float2 ml = *reinterpret_cast<const float2 *>(part_ml + (((size_t) t * d.kb + j) * d.n_head + h) * 2);
-        const float wj = ml.y * exp2f(ml.x - Mu);
+        const int row = rows[j];
+        float wj = 0.0f;
+        if (row >= 0) {
+            const float2 ml = *reinterpret_cast<const float2 *>(part_ml + (size_t) row * 2);
+            wj = ml.y * exp2f(ml.x - Mu);
+        }
         w[j] = wj;
         Wl += wj;
     }
@@ -435,8 +534,11 @@ __global__ void prefill_merge_kernel(DevDesc d, int T, const int * __restrict__ 
     for (int o = 16; o > 0; o >>= 1) Wl += __shfl_xor_sync(0xffffffffu, Wl, o);
     __syncwarp();
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    const uint4 * src = reinterpret_cast<const uint4 *>(part_o + ((size_t) t * d.kb * d.n_head + h) * HEAD_DIM) + lane;
-    const size_t jstride = (size_t) d.n_head * HEAD_DIM / 8;   // uint4 per slot
+    const uint4 * src = reinterpret_cast<const uint4 *>(part_o) + lane;
+    auto load = [&](int j) -> uint4 {
+        const int row = rows[j];
+        return row >= 0 ? __ldcs(src + (size_t) row * (HEAD_DIM / 8)) : make_uint4(0, 0, 0, 0);
+    };
     auto add = [&](const uint4 & x, float wj) {
         const uint32_t xx[4] = {x.x, x.y, x.z, x.w};
         #pragma unroll
@@ -450,27 +552,29 @@ __global__ void prefill_merge_kernel(DevDesc d, int T, const int * __restrict__ 
     for (; j + 4 <= n; j += 4) {
         uint4 x[4];
         #pragma unroll
-        for (int k = 0; k < 4; k++) x[k] = __ldcs(src + (size_t) (j + k) * jstride);
+        for (int k = 0; k < 4; k++) x[k] = load(j + k);
         #pragma unroll
         for (int k = 0; k < 4; k++) add(x[k], w[j + k]);
     }
-    for (; j < n; j++) add(__ldcs(src + (size_t) j * jstride), w[j]);
+    for (; j < n; j++) add(load(j), w[j]);
     const float inv = Wl > 0.0f ? 1.0f / Wl : 0.0f;
     float4 * dst = reinterpret_cast<float4 *>(out + ((size_t) t * d.n_head + h) * HEAD_DIM) + lane * 2;
     dst[0] = make_float4(acc[0] * inv, acc[1] * inv, acc[2] * inv, acc[3] * inv);
     dst[1] = make_float4(acc[4] * inv, acc[5] * inv, acc[6] * inv, acc[7] * inv);
 }
 
-bool prefill_kv_supported(const DevDesc & d) {
+bool prefill_kv_supported(const DevDesc & d, int T) {
+    // partial rows are indexed in int32 (TMA coordinates): T * kb * n_head < 2^31
     return d.type_k == QSA_TYPE_Q8_0 && d.type_v == QSA_TYPE_Q8_0 && d.ratio == PA_CELLS && d.gqa == GQA_TILE &&
-           d.kb <= (1 << PA_SLOT_SHIFT) && d.n_head <= 32;
+           d.head_dim == HEAD_DIM && d.kb <= (1 << PA_SLOT_SHIFT) && d.n_head <= 32 &&
+           (int64_t) T * d.kb * d.n_head < ((int64_t) 1 << 31);
 }
 
 namespace {
 size_t a256(size_t x) { return (x + 255) & ~(size_t) 255; }
 
 struct PrefillKvLayout {
-    size_t cnt, cursor, offsets, entries, q16, part_o, part_ml, total;
+    size_t cnt, cursor, offsets, entries, entry_of, q16, part_o, part_ml, total;
 };
 PrefillKvLayout prefill_kv_layout(const DevDesc & d, int T, int n_blocks) {
     PrefillKvLayout L;
@@ -479,7 +583,8 @@ PrefillKvLayout prefill_kv_layout(const DevDesc & d, int T, int n_blocks) {
     L.cursor = L.cnt + a256((size_t) n_blocks * 4);
     L.offsets = L.cursor + a256((size_t) n_blocks * 4);
     L.entries = L.offsets + a256((size_t) (n_blocks + 1) * 4);
-    L.q16 = L.entries + a256(slots * 4);
+    L.entry_of = L.entries + a256(slots * 4);
+    L.q16 = L.entry_of + a256(slots * 4);
     L.part_o = L.q16 + a256((size_t) T * d.n_head * HEAD_DIM * 2);
     L.part_ml = L.part_o + a256(slots * d.n_head * HEAD_DIM * 2);
     L.total = L.part_ml + a256(slots * d.n_head * 2 * 4);
@@ -502,16 +607,32 @@ encode_tiled_fn tensor_map_encoder() {
     return fn;
 }
 
-// rows x 256 f16 at `ptr` (rows of 512 bytes), boxes of 8 rows x 64 columns, 128-byte swizzle
-bool encode_rows_map(CUtensorMap * map, void * ptr, uint64_t rows) {
+// groups x 8 rows x 256 f16 at `ptr` (rows of 512 bytes) seen as [group][atom][row][64 columns]:
+// dims {64 columns, 8 rows (512 B apart), 4 atoms (128 B apart), groups (4 KB apart)}; a box of
+// box_groups groups lands as [group][atom][8 rows][128 bytes], 128-byte swizzle
+bool encode_groups_map(CUtensorMap * map, void * ptr, uint64_t groups, uint32_t box_groups) {
     encode_tiled_fn enc = tensor_map_encoder();
     if (!enc) return false;
-    const cuuint64_t dims[2] = {(cuuint64_t) HEAD_DIM, (cuuint64_t) rows};
-    const cuuint64_t strides[1] = {(cuuint64_t) HEAD_DIM * 2};
-    const cuuint32_t box[2] = {64, 8};
-    const cuuint32_t estr[2] = {1, 1};
-    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ptr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+    const cuuint64_t dims[4] = {64, 8, 4, (cuuint64_t) groups};
+    const cuuint64_t strides[3] = {(cuuint64_t) HEAD_DIM * 2, 128, (cuuint64_t) PA_QROWS};
+    const cuuint32_t box[4] = {64, 8, 4, box_groups};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, ptr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// the raw bytes of a q8_0 cache (n_ctx rows of row_bytes) as u16 elements; boxes of one head's
+// 272 bytes x 64 rows, no swizzle (rows past n_ctx read as zero)
+bool encode_cache_map(CUtensorMap * map, const void * ptr, int64_t row_bytes, int n_ctx) {
+    encode_tiled_fn enc = tensor_map_encoder();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t) (row_bytes / 2), (cuuint64_t) n_ctx};
+    const cuuint64_t strides[1] = {(cuuint64_t) row_bytes};
+    const cuuint32_t box[2] = {(cuuint32_t) (PA_HEAD_Q8 / 2), (cuuint32_t) PA_CELLS};
+    const cuuint32_t estr[2] = {1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void *>(ptr), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 }  // namespace
 
@@ -532,11 +653,15 @@ cudaError_t launch_prefill_attn_kv(const DevDesc & d, cudaStream_t st, qsa_layer
     int * cursor = reinterpret_cast<int *>(ws + L.cursor);
     int * offsets = reinterpret_cast<int *>(ws + L.offsets);
     uint32_t * entries = reinterpret_cast<uint32_t *>(ws + L.entries);
+    int * entry_of = reinterpret_cast<int *>(ws + L.entry_of);
     __half * q16 = reinterpret_cast<__half *>(ws + L.q16);
     __half * part_o = reinterpret_cast<__half *>(ws + L.part_o);
     float * part_ml = reinterpret_cast<float *>(ws + L.part_ml);
-    CUtensorMap q_map, o_map;
-    if (!encode_rows_map(&q_map, q16, (uint64_t) T * d.n_head) || !encode_rows_map(&o_map, part_o, (uint64_t) slots * d.n_head))
+    CUtensorMap q_map, o_map, o1_map, k_map, v_map;
+    if (!encode_groups_map(&q_map, q16, (uint64_t) T * d.n_head_kv, 1) ||
+        !encode_groups_map(&o_map, part_o, (uint64_t) slots * d.n_head_kv, PA_QC) ||
+        !encode_groups_map(&o1_map, part_o, (uint64_t) slots * d.n_head_kv, 1) ||
+        !encode_cache_map(&k_map, cache.k, d.rb_k, d.n_ctx) || !encode_cache_map(&v_map, cache.v, d.rb_v, d.n_ctx))
         return cudaErrorNotSupported;
     cudaError_t e = cudaMemsetAsync(cnt, 0, (size_t) n_blocks * 4, st);
     if (e != cudaSuccess) return e;
@@ -546,15 +671,16 @@ cudaError_t launch_prefill_attn_kv(const DevDesc & d, cudaStream_t st, qsa_layer
     prefill_q16_kernel<<<(unsigned) ((n8 + nthr - 1) / nthr), nthr, 0, st>>>(q, q_type, n8, reinterpret_cast<uint4 *>(q16));
     prefill_bucket_count_kernel<<<nb_slots, nthr, 0, st>>>(d, T, sel, nsel, n_blocks, cnt);
     prefill_bucket_scan_kernel<<<1, 1024, 0, st>>>(cnt, n_blocks, offsets, cursor);
-    prefill_bucket_fill_kernel<<<nb_slots, nthr, 0, st>>>(d, T, sel, nsel, n_blocks, cursor, entries);
+    prefill_bucket_fill_kernel<<<nb_slots, nthr, 0, st>>>(d, T, sel, nsel, n_blocks, cursor, entries, entry_of);
     prefill_attn_kv_kernel<<<dim3((unsigned) n_blocks, (unsigned) d.n_head_kv), PA_THREADS, PA_SMEM, st>>>(
-        q_map, o_map, d, cache, n_past0, n_past0 + T, entries, offsets, part_ml, status);
-    const size_t merge_smem = (size_t) d.n_head * d.kb * 4;
+        q_map, o_map, o1_map, k_map, v_map, d, n_past0, n_past0 + T, (int) slots, entries, offsets, part_ml, status);
+    const size_t merge_smem = (size_t) d.n_head * d.kb * 8;
     if (merge_smem > 48 * 1024) {
         e = cudaFuncSetAttribute(prefill_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) merge_smem);
         if (e != cudaSuccess) return e;
     }
-    prefill_merge_kernel<<<(unsigned) T, 32 * d.n_head, merge_smem, st>>>(d, T, nsel, part_o, part_ml, out);
+    prefill_merge_kernel<<<(unsigned) T, 32 * d.n_head, merge_smem, st>>>(d, T, (int) slots, nsel, entry_of, part_o,
+                                                                          part_ml, out);
     return cudaGetLastError();
 }
 
