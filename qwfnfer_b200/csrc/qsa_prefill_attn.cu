@@ -47,7 +47,8 @@ constexpr int PA_SQ = PA_ROWS * HEAD_DIM * 2;      // 64 KB
 constexpr int PA_SK = PA_CELLS * HEAD_DIM * 2;     // 32 KB
 constexpr int PA_SV = HEAD_DIM * PA_CELLS * 2;     // 32 KB
 constexpr int PA_SP = PA_ROWS * PA_CELLS * 2;      // 16 KB
-constexpr int PA_SMEM = 2 * PA_SQ + PA_SK + PA_SV + PA_SP + 1024;
+constexpr int PA_SW = 32 * 64;                      // 2 KB per epilogue warp: 32 rows x 64 bytes
+constexpr int PA_SMEM = 2 * PA_SQ + PA_SK + PA_SV + PA_SP + 4 * PA_SW + 1024;
 constexpr int PA_HEAD_Q8 = HEAD_DIM / QK8_0 * Q8_0_BYTES;   // 272 bytes of one head's q8_0 row
 constexpr int PA_QROWS = 8 * HEAD_DIM * 2;         // 4 KB: one query's 8 head rows in a Q stage
 constexpr uint32_t PA_TMEM_COLS = 512;             // S buffers: columns 0..63, 64..127; O: 256..511
@@ -160,10 +161,6 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap * ma
     asm volatile("cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %2, %2, %3}], [%4];"
                  :: "r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(w), "r"(smem_u32(bar)) : "memory");
 }
-__device__ __forceinline__ void tma_store_4d(const CUtensorMap * map, int w, uint32_t src) {
-    asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%1, %1, %1, %2}], [%3];"
-                 :: "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(w), "r"(src) : "memory");
-}
 // non-blocking probe of a phase (the MMA thread polls two streams of work with it)
 __device__ __forceinline__ bool mbar_test(uint64_t * bar, uint32_t parity) {
     uint32_t done;
@@ -185,21 +182,6 @@ __device__ __forceinline__ bool mbar_poll_bounded(uint64_t * bar, uint32_t parit
     set_status(status, DEV_TIMEOUT);
     return false;
 }
-__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
-__device__ __forceinline__ void epilogue_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
-// barrier of the 128 epilogue threads that also ANDs `ok` over them, so that all leave together
-__device__ __forceinline__ bool epilogue_all(bool ok) {
-    uint32_t r;
-    asm volatile("{\n\t.reg .pred p, q;\n\t"
-                 "setp.ne.u32 p, %1, 0;\n\t"
-                 "bar.red.and.pred q, 1, 128, p;\n\t"
-                 "selp.u32 %0, 1, 0, q;\n\t}"
-                 : "=r"(r) : "r"(ok ? 1u : 0u) : "memory");
-    return r != 0;
-}
-
 // ------------------------------------------------------------------ attention per (block, KV head)
 __device__ __forceinline__ uint32_t f16x2_scaled(int8_t a, int8_t b, float d) {
     return pack_f16x2((float) a * d, (float) b * d);        // f16(d x q), exact product rounded once
@@ -207,8 +189,7 @@ __device__ __forceinline__ uint32_t f16x2_scaled(int8_t a, int8_t b, float d) {
 
 struct PaBarriers {
     uint64_t kv_full;                 // raw q8_0 rows of the block copied in (bulk-copy bytes)
-    uint64_t q_full[2], q_empty[2];   // Q stage loaded (TMA bytes) / free again: its S MMAs and the
-                                      // TMA stores of the O rows staged in it are done (128 arrivals)
+    uint64_t q_full[2], q_empty[2];   // Q stage loaded (TMA bytes) / read by its S MMAs (commit)
     uint64_t s_full[2], s_empty[2];   // S buffer written (commit) / read by the 128 softmax threads
     uint64_t p_full, p_empty;         // sP written by the softmax threads / read by the O MMAs (commit)
     uint64_t o_full, o_empty;         // O in TMEM (commit) / read by the 128 epilogue threads
@@ -217,11 +198,10 @@ struct PaBarriers {
 };
 
 __global__ void __launch_bounds__(PA_THREADS, 1) prefill_attn_kv_kernel(
-        const __grid_constant__ CUtensorMap q_map, const __grid_constant__ CUtensorMap o_map,
-        const __grid_constant__ CUtensorMap o1_map, const __grid_constant__ CUtensorMap k_map,
+        const __grid_constant__ CUtensorMap q_map, const __grid_constant__ CUtensorMap k_map,
         const __grid_constant__ CUtensorMap v_map, DevDesc d, int n_past0, int n_kv, int slots,
-        const uint32_t * __restrict__ entries, const int * __restrict__ offsets, float * __restrict__ part_ml,
-        uint32_t * __restrict__ status) {
+        const uint32_t * __restrict__ entries, const int * __restrict__ offsets, __half * __restrict__ part_o,
+        float * __restrict__ part_ml, uint32_t * __restrict__ status) {
     extern __shared__ __align__(1024) unsigned char pa_smem_raw[];
     __shared__ PaBarriers bars;
     __shared__ uint32_t tmem_slot;
@@ -237,6 +217,7 @@ __global__ void __launch_bounds__(PA_THREADS, 1) prefill_attn_kv_kernel(
     unsigned char * sK = sQ0 + 2 * PA_SQ;                   // O rows of its chunk for the TMA stores
     unsigned char * sV = sK + PA_SK;                        // V^T [256 dims][64 cells]
     unsigned char * sP = sV + PA_SV;
+    unsigned char * sW = sP + PA_SP;                        // the epilogue warps' row pieces
     const uint32_t aQ0 = base, aK = base + 2 * PA_SQ, aV = aK + PA_SK, aP = aV + PA_SV;
     // the raw q8_0 rows (head g: 272 bytes of a 544-byte row) land in Q stage 1 before chunk 1 does
     unsigned char * rawK = sQ0 + PA_SQ;
@@ -248,7 +229,7 @@ __global__ void __launch_bounds__(PA_THREADS, 1) prefill_attn_kv_kernel(
         mbar_init(&bars.kv_full, 1);
         for (int k = 0; k < 2; k++) {
             mbar_init(&bars.q_full[k], 1);
-            mbar_init(&bars.q_empty[k], PA_ROWS);
+            mbar_init(&bars.q_empty[k], 1);
             mbar_init(&bars.s_full[k], 1);
             mbar_init(&bars.s_empty[k], PA_ROWS);
             mbar_init(&bars.meta_full[k], PA_ROWS);
@@ -335,7 +316,7 @@ __global__ void __launch_bounds__(PA_THREADS, 1) prefill_attn_kv_kernel(
         int i = 1;
         for (; i < n_chunks; i++) {
             const uint32_t e = chunk_entry(i, lane);
-            // stage i % 2 is free once the O rows of chunk i-2 have been read out of it
+            // stage i % 2 is free once the S MMAs of chunk i-2 are done
             int ok = 1;
             if (i >= 2 && lane == 0) ok = mbar_poll_bounded(&bars.q_empty[i & 1], (uint32_t) (((i - 2) >> 1) & 1), status);
             if (!__shfl_sync(0xffffffffu, ok, 0)) break;
@@ -364,6 +345,7 @@ __global__ void __launch_bounds__(PA_THREADS, 1) prefill_attn_kv_kernel(
                                      umma_desc_sw128_sbo(aQ + (kk >> 2) * 1024 + (kk & 3) * 32, PA_QROWS),
                                      umma_desc_sw128(aK + (kk >> 2) * (PA_CELLS * 128) + (kk & 3) * 32), PA_IDESC_S, kk > 0);
                         umma_commit(&bars.s_full[s]);
+                        umma_commit(&bars.q_empty[s]);
                         ns++;
                         progress = true;
                     }
@@ -441,55 +423,57 @@ __global__ void __launch_bounds__(PA_THREADS, 1) prefill_attn_kv_kernel(
         }
     } else {
         // ---------------------------------------------------------------- epilogue, thread = row
-        const int r = tid - 128, qi = r >> 3;
-        const uint32_t lane_base = (uint32_t) ((warp - 4) * 32) << 16;
+        // O / l of the row as f16 into registers, release O, then the warp's 32 rows go out 64 bytes
+        // of a row at a time through a 2 KB slice (8 rows x 64 bytes per store instruction)
+        const int r = tid - 128, qi = r >> 3, ew = warp - 4;
+        const uint32_t lane_base = (uint32_t) (ew * 32) << 16;
+        unsigned char * wbuf = sW + ew * PA_SW;
         for (int i = 0; i < n_chunks; i++) {
             const int buf = i & 1;
             const int c0 = e0 + i * PA_QC, nq = min(PA_QC, e1 - c0);
             bool ok = mbar_wait_bounded(&bars.meta_full[buf], (uint32_t) ((i >> 1) & 1), status);
             const float m = row_m[buf][r], l = row_l[buf][r];
             ok = ok && mbar_wait_bounded(&bars.o_full, (uint32_t) (i & 1), status);
-            if (!epilogue_all(ok)) break;
+            if (!__all_sync(0xffffffffu, ok)) break;
             tc_fence_after();
-            // O / l as f16 into the chunk's Q stage (its S MMAs finished before this O was made)
-            unsigned char * stage = sQ0 + buf * PA_SQ;
             const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-            #pragma unroll 1
+            uint32_t pk[HEAD_DIM / 2];
+            #pragma unroll
             for (int c0v = 0; c0v < HEAD_DIM; c0v += 64) {
                 uint32_t v[2][32];
                 tmem_ld32(tmem + lane_base + PA_TMEM_O + (uint32_t) c0v, v[0]);
                 tmem_ld32(tmem + lane_base + PA_TMEM_O + (uint32_t) (c0v + 32), v[1]);
                 tmem_ld_wait();
                 #pragma unroll
-                for (int hh = 0; hh < 2; hh++)
-                    #pragma unroll
-                    for (int k = 0; k < 4; k++)
-                        *reinterpret_cast<uint4 *>(stage + q_stage_off(r, c0v + 32 * hh + 8 * k)) =
-                            make_uint4(pack_f16x2(__uint_as_float(v[hh][8 * k]) * inv, __uint_as_float(v[hh][8 * k + 1]) * inv),
-                                       pack_f16x2(__uint_as_float(v[hh][8 * k + 2]) * inv, __uint_as_float(v[hh][8 * k + 3]) * inv),
-                                       pack_f16x2(__uint_as_float(v[hh][8 * k + 4]) * inv, __uint_as_float(v[hh][8 * k + 5]) * inv),
-                                       pack_f16x2(__uint_as_float(v[hh][8 * k + 6]) * inv, __uint_as_float(v[hh][8 * k + 7]) * inv));
+                for (int k = 0; k < 32; k++)
+                    pk[c0v / 2 + k] = pack_f16x2(__uint_as_float(v[k >> 4][2 * (k & 15)]) * inv,
+                                                 __uint_as_float(v[k >> 4][2 * (k & 15) + 1]) * inv);
             }
             tc_fence_before();
             mbar_arrive(&bars.o_empty);
             // row (KV head g, entry c, query head h) of the partials; the chunk's rows are contiguous
-            const int y0 = (g * slots + c0) * GQA_TILE;
-            if (qi < nq) *reinterpret_cast<float2 *>(part_ml + ((size_t) y0 + r) * 2) = make_float2(m, l);
-            fence_async_smem();                               // staging visible to the TMA unit
-            epilogue_sync();
-            if (r == 0) {               // 8-row group w of the partials = (KV head g, entry w - g * slots)
-                const uint32_t st0 = aQ0 + buf * PA_SQ;
-                if (nq == PA_QC) {
-                    tma_store_4d(&o_map, g * slots + c0, st0);
-                } else {
-                    for (int q = 0; q < nq; q++) tma_store_4d(&o1_map, g * slots + c0 + q, st0 + q * PA_QROWS);
+            const size_t y0 = ((size_t) g * slots + c0) * GQA_TILE;
+            if (qi < nq) *reinterpret_cast<float2 *>(part_ml + (y0 + r) * 2) = make_float2(m, l);
+            // slice: row x (lane) holds its 4 16-byte pieces at positions k ^ ((x >> 1) & 3)
+            const int swz_w = (lane >> 1) & 3;
+            #pragma unroll
+            for (int p = 0; p < HEAD_DIM / 32; p++) {       // 32 columns (64 bytes) of every row
+                #pragma unroll
+                for (int k = 0; k < 4; k++)
+                    *reinterpret_cast<uint4 *>(wbuf + lane * 64 + ((k ^ swz_w) << 4)) =
+                        make_uint4(pk[16 * p + 4 * k], pk[16 * p + 4 * k + 1], pk[16 * p + 4 * k + 2], pk[16 * p + 4 * k + 3]);
+                __syncwarp();
+                #pragma unroll
+                for (int j = 0; j < 4; j++) {                // rows 8j + lane / 4, piece lane % 4
+                    const int x = 8 * j + (lane >> 2), k = lane & 3;
+                    const int rr = ew * 32 + x;
+                    if ((rr >> 3) < nq)
+                        __stcs(reinterpret_cast<uint4 *>(part_o + (y0 + rr) * HEAD_DIM + p * 32) + k,
+                               *reinterpret_cast<const uint4 *>(wbuf + x * 64 + ((k ^ ((x >> 1) & 3)) << 4)));
                 }
-                bulk_commit();
-                bulk_wait_read_all();                         // the stage may be loaded again
+                __syncwarp();
             }
-            mbar_arrive(&bars.q_empty[buf]);
         }
-        if (r == 0) bulk_wait_all();                          // the partials are written before the CTA ends
     }
     tc_fence_before();
     __syncthreads();
@@ -657,10 +641,8 @@ cudaError_t launch_prefill_attn_kv(const DevDesc & d, cudaStream_t st, qsa_layer
     __half * q16 = reinterpret_cast<__half *>(ws + L.q16);
     __half * part_o = reinterpret_cast<__half *>(ws + L.part_o);
     float * part_ml = reinterpret_cast<float *>(ws + L.part_ml);
-    CUtensorMap q_map, o_map, o1_map, k_map, v_map;
+    CUtensorMap q_map, k_map, v_map;
     if (!encode_groups_map(&q_map, q16, (uint64_t) T * d.n_head_kv, 1) ||
-        !encode_groups_map(&o_map, part_o, (uint64_t) slots * d.n_head_kv, PA_QC) ||
-        !encode_groups_map(&o1_map, part_o, (uint64_t) slots * d.n_head_kv, 1) ||
         !encode_cache_map(&k_map, cache.k, d.rb_k, d.n_ctx) || !encode_cache_map(&v_map, cache.v, d.rb_v, d.n_ctx))
         return cudaErrorNotSupported;
     cudaError_t e = cudaMemsetAsync(cnt, 0, (size_t) n_blocks * 4, st);
@@ -673,7 +655,7 @@ cudaError_t launch_prefill_attn_kv(const DevDesc & d, cudaStream_t st, qsa_layer
     prefill_bucket_scan_kernel<<<1, 1024, 0, st>>>(cnt, n_blocks, offsets, cursor);
     prefill_bucket_fill_kernel<<<nb_slots, nthr, 0, st>>>(d, T, sel, nsel, n_blocks, cursor, entries, entry_of);
     prefill_attn_kv_kernel<<<dim3((unsigned) n_blocks, (unsigned) d.n_head_kv), PA_THREADS, PA_SMEM, st>>>(
-        q_map, o_map, o1_map, k_map, v_map, d, n_past0, n_past0 + T, (int) slots, entries, offsets, part_ml, status);
+        q_map, k_map, v_map, d, n_past0, n_past0 + T, (int) slots, entries, offsets, part_o, part_ml, status);
     const size_t merge_smem = (size_t) d.n_head * d.kb * 8;
     if (merge_smem > 48 * 1024) {
         e = cudaFuncSetAttribute(prefill_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) merge_smem);
