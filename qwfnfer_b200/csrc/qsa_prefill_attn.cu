@@ -11,27 +11,28 @@
 //   1. prefill_bucket_*: the (query, slot) pairs of the chunk's selections are bucketed by block
 //      (counting sort: counts, one scan, a fill that also records each pair's bucket position,
 //      its "entry"); prefill_q16_kernel converts Q to f16 rows;
-//   2. prefill_attn_kv_kernel, CTA = (block, KV head): the block's K and V rows of that head are
-//      dequantised once into shared memory (f16 of d x q, the rounding of the reference's decode
-//      gather); then the CTA walks its queries 16 at a time (16 x 8 query heads = 128 rows) in a
-//      warp-specialised pipeline:
-//        warp 8      TMA loads of the block's raw q8_0 rows, then of the 16 queries' Q rows
-//                    (128-byte swizzle) into one of two Q stages
+//   2. prefill_attn_kv_kernel, CTA = (block, KV head): the block's raw K and V rows of that head
+//      come in by TMA and are dequantised once into shared memory (f16 of d x q, the rounding of
+//      the reference's decode gather); then the CTA walks its entries 16 at a time (16 queries x 8
+//      query heads = 128 rows) in a warp-specialised pipeline:
+//        warp 8      TMA loads of the queries' Q rows (one 4 KB box per query) into one of two
+//                    Q stages
 //        warp 9      one thread issues S = Q K^T (16 tcgen05.mma, M=128, N=64 cells, K=16) into one
 //                    of two TMEM S buffers, and O = P V (4 tcgen05.mma, M=128, N=256, K=16) into
-//                    TMEM, each as soon as its inputs are ready (non-blocking barrier tests)
+//                    TMEM, each as soon as its inputs are ready (non-blocking barrier tests); the
+//                    S commit also releases the Q stage
 //        warps 0-3   thread = row = TMEM lane: S from TMEM, mask of the cells past the query,
-//                    P = 2^(s - m) (f16) -> sP, row maximum and sum -> shared memory
-//        warps 4-7   thread = row: O from TMEM, O / l (f16) -> the chunk's Q stage (free once its
-//                    S MMAs are done), then TMA tensor stores of the chunk's 128 rows, and (m, l)
-//                    of each row; the stage is loaded again after the stores have read it
-//      The partials are entry-major, [KV head][entry][8 query heads][256], so a chunk's rows are
-//      contiguous (four 16 KB boxes);
+//                    P = 2^(s - m) (f16) -> shared memory, row maximum and sum
+//        warps 4-7   thread = row: O / l from TMEM into registers (f16), release O, then each
+//                    warp writes its 32 rows through a 2 KB slice (8 rows x 64 bytes per store
+//                    instruction), and (m, l) of each row
+//      The partials are entry-major, [KV head][entry][8 query heads][256 dims] f16, so a chunk's
+//      rows are contiguous;
 //   3. prefill_merge_kernel: per query, a warp per head merges its slots' partials (log-sum-exp),
 //      finding each slot's row through the entry recorded for it.
-// Operands are K-major with the 128-byte swizzle: Q [16 queries][4 atoms of 64 dims][8 rows],
-// K [64 cells][256 dims], V^T [256 dims][64 cells], P [128 rows][64 cells]; the O rows staged for
-// the stores have Q's layout, so that one TMA box moves a query's rows (4 KB) or a chunk's (64 KB).
+// Tensor-core operands use the 128-byte swizzle: Q [16 queries][4 atoms of 64 dims][8 rows] (K-major,
+// 8-row groups 4 KB apart), K and V [64 cells][256 dims] (K-major for S; V as the MN-major B of
+// O = P V), P [128 rows][64 cells] (K-major).
 #include <cuda.h>          // CUtensorMap and its enums; the encoder is reached through the runtime
 
 #include "qsa_kernels.cuh"
@@ -54,7 +55,7 @@ constexpr int PA_QROWS = 8 * HEAD_DIM * 2;         // 4 KB: one query's 8 head r
 constexpr uint32_t PA_TMEM_COLS = 512;             // S buffers: columns 0..63, 64..127; O: 256..511
 constexpr uint32_t PA_TMEM_O = 256;
 constexpr uint32_t PA_IDESC_S = umma_idesc_f16(PA_ROWS, PA_CELLS);
-constexpr uint32_t PA_IDESC_O = umma_idesc_f16(PA_ROWS, HEAD_DIM);
+constexpr uint32_t PA_IDESC_O = umma_idesc_f16(PA_ROWS, HEAD_DIM) | (1u << 16);   // B (V) MN-major
 constexpr int PA_SLOT_SHIFT = 10;                  // entry = query << 10 | slot (slot < MAX_KB)
 // A Q stage (and the O rows staged in it) is [query][64-column atom][8 rows][128 bytes] with the
 // 128-byte swizzle inside each 1 KB (8 rows x 128 bytes): the MMA reads it as a K-major operand
@@ -62,6 +63,12 @@ constexpr int PA_SLOT_SHIFT = 10;                  // entry = query << 10 | slot
 __device__ __forceinline__ uint32_t q_stage_off(int r, int k) {
     return (uint32_t) ((r >> 3) * PA_QROWS + (k >> 6) * 1024 + (r & 7) * 128 + ((((k >> 3) & 7) ^ (r & 7)) << 4) +
                        ((k & 7) << 1));
+}
+// shared-memory descriptor of a 128-byte-swizzled MN-major operand: 64-element MN blocks lbo bytes
+// apart, groups of 8 K rows (1 KB atoms) sbo bytes apart
+__device__ __forceinline__ uint64_t umma_desc_sw128_mn(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t) ((smem_addr >> 4) & 0x3FFFu) | ((uint64_t) ((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t) ((sbo >> 4) & 0x3FFFu) << 32) | ((uint64_t) 1 << 46) | ((uint64_t) 2 << 61);
 }
 // shared-memory descriptor of a 128-byte-swizzled K-major operand whose 8-row groups are sbo bytes apart
 __device__ __forceinline__ uint64_t umma_desc_sw128_sbo(uint32_t smem_addr, uint32_t sbo) {
@@ -215,7 +222,7 @@ __global__ void __launch_bounds__(PA_THREADS, 1) prefill_attn_kv_kernel(
     const uint32_t base = (raw + 1023u) & ~1023u;
     unsigned char * sQ0 = pa_smem_raw + (base - raw);       // two Q stages; a stage also holds the
     unsigned char * sK = sQ0 + 2 * PA_SQ;                   // O rows of its chunk for the TMA stores
-    unsigned char * sV = sK + PA_SK;                        // V^T [256 dims][64 cells]
+    unsigned char * sV = sK + PA_SK;                        // V [64 cells][256 dims], like K
     unsigned char * sP = sV + PA_SV;
     unsigned char * sW = sP + PA_SP;                        // the epilogue warps' row pieces
     const uint32_t aQ0 = base, aK = base + 2 * PA_SQ, aV = aK + PA_SK, aP = aV + PA_SV;
@@ -267,43 +274,22 @@ __global__ void __launch_bounds__(PA_THREADS, 1) prefill_attn_kv_kernel(
     }
     mbar_wait_bounded(&bars.kv_full, 0u, status);
 
-    // ---- K and V -> f16 (d x q), K as [cell][dim], V as [dim][cell]; cells at or past n_kv are
-    // zero (their bytes may decode to Inf or NaN, and a masked P of 0 times a NaN is NaN in the MMA)
-    for (int i = tid; i < PA_CELLS * (HEAD_DIM / 8); i += PA_THREADS) {      // (cell, 8-dim group)
-        const int cell = i >> 5, d8 = i & 31;
+    // ---- K and V -> f16 (d x q), both as [cell][dim] (K-major for S = Q K^T, MN-major for O = P V);
+    // cells at or past n_kv are zero (their bytes may decode to Inf or NaN, and a masked P of 0
+    // times a NaN is NaN in the MMA)
+    for (int i = tid; i < 2 * PA_CELLS * (HEAD_DIM / 8); i += PA_THREADS) {   // (K or V, cell, 8-dim group)
+        const int kv = i >> 11, cell = (i >> 5) & (PA_CELLS - 1), d8 = i & 31;
         uint4 w = make_uint4(0, 0, 0, 0);
         if (cell < n_valid) {
-            const unsigned char * blk = rawK + cell * PA_HEAD_Q8 + (d8 >> 2) * Q8_0_BYTES;
+            const uint8_t * blk = (kv ? rawV : rawK) + cell * PA_HEAD_Q8 + (d8 >> 2) * Q8_0_BYTES;
             const float sc = f16_bits_to_f32(*reinterpret_cast<const uint16_t *>(blk));
-            const int8_t * qs = reinterpret_cast<const int8_t *>(blk + 2) + (d8 & 3) * 8;
-            w.x = f16x2_scaled(qs[0], qs[1], sc); w.y = f16x2_scaled(qs[2], qs[3], sc);
-            w.z = f16x2_scaled(qs[4], qs[5], sc); w.w = f16x2_scaled(qs[6], qs[7], sc);
+            const uint32_t lo = lds_u32_a2(blk + 2 + (d8 & 3) * 8), hi = lds_u32_a2(blk + 6 + (d8 & 3) * 8);
+            w.x = f16x2_scaled((int8_t) lo, (int8_t) (lo >> 8), sc);
+            w.y = f16x2_scaled((int8_t) (lo >> 16), (int8_t) (lo >> 24), sc);
+            w.z = f16x2_scaled((int8_t) hi, (int8_t) (hi >> 8), sc);
+            w.w = f16x2_scaled((int8_t) (hi >> 16), (int8_t) (hi >> 24), sc);
         }
-        *reinterpret_cast<uint4 *>(sK + sw128_off(PA_CELLS, cell, d8 * 8)) = w;
-    }
-    for (int i = tid; i < (HEAD_DIM / 8) * (PA_CELLS / 8); i += PA_THREADS) {   // (8-dim group, 8-cell group)
-        const int d8 = i >> 3, c8 = i & 7;
-        uint16_t val[8][8];                                   // [dim][cell]
-        #pragma unroll
-        for (int c = 0; c < 8; c++) {
-            if (c8 * 8 + c < n_valid) {
-                const unsigned char * blk = rawV + (c8 * 8 + c) * PA_HEAD_Q8 + (d8 >> 2) * Q8_0_BYTES;
-                const float sc = f16_bits_to_f32(*reinterpret_cast<const uint16_t *>(blk));
-                const int8_t * qs = reinterpret_cast<const int8_t *>(blk + 2) + (d8 & 3) * 8;
-                #pragma unroll
-                for (int k = 0; k < 8; k++) val[k][c] = f32_to_f16_bits((float) qs[k] * sc);
-            } else {
-                #pragma unroll
-                for (int k = 0; k < 8; k++) val[k][c] = 0;
-            }
-        }
-        #pragma unroll
-        for (int k = 0; k < 8; k++) {
-            uint4 w;
-            w.x = val[k][0] | ((uint32_t) val[k][1] << 16); w.y = val[k][2] | ((uint32_t) val[k][3] << 16);
-            w.z = val[k][4] | ((uint32_t) val[k][5] << 16); w.w = val[k][6] | ((uint32_t) val[k][7] << 16);
-            *reinterpret_cast<uint4 *>(sV + sw128_off(HEAD_DIM, d8 * 8 + k, c8 * 8)) = w;
-        }
+        *reinterpret_cast<uint4 *>((kv ? sV : sK) + sw128_off(PA_CELLS, cell, d8 * 8)) = w;
     }
     fence_async_smem();                                     // K and V tiles visible to the tensor core,
     tc_fence_before();                                      // and stage 1 free for the TMA
@@ -355,7 +341,8 @@ __global__ void __launch_bounds__(PA_THREADS, 1) prefill_attn_kv_kernel(
                     tc_fence_after();
                     #pragma unroll
                     for (int kk = 0; kk < PA_CELLS / 16; kk++)
-                        umma_f16(tmem + PA_TMEM_O, umma_desc_sw128(aP + kk * 32), umma_desc_sw128(aV + kk * 32), PA_IDESC_O, kk > 0);
+                        umma_f16(tmem + PA_TMEM_O, umma_desc_sw128(aP + kk * 32),
+                                 umma_desc_sw128_mn(aV + kk * 2048, PA_CELLS * 128, 1024), PA_IDESC_O, kk > 0);
                     umma_commit(&bars.o_full);
                     umma_commit(&bars.p_empty);
                     no++;
