@@ -17,8 +17,9 @@
 //
 // select_scores_warp_kernel: one warp per query.  Keys are the bit patterns of the non-negative
 // scores of the candidate blocks (visible and not forced); a radix select with 8-bit digits from
-// the top finds the cut, then lanes, each owning a contiguous run of blocks, emit the kept blocks
-// in ascending order (equal keys at the cut kept by lower block index), then the forced blocks.
+// the top finds the cut (coalesced passes over the row), then the warp emits the kept blocks 32 at
+// a time in ascending order with ballots (equal keys at the cut kept by lower block index), then
+// the forced blocks.
 #include "qsa_kernels.cuh"
 
 namespace qsa {
@@ -196,9 +197,8 @@ __global__ void __launch_bounds__(32 * SELW_WARPS) select_scores_warp_kernel(Dev
     const int cand_hi = n_forced ? min(n_vis, f_lo) : n_vis;   // candidates: [0, cand_hi)
     const int want = max(0, d.kb - n_forced);
     const float * sc = scores + (size_t) t * scores_stride;
-    // lane-owned contiguous run of candidate blocks
-    const int per = (cand_hi + 31) / 32;
-    const int lo = min(cand_hi, lane * per), hi = min(cand_hi, lo + per);
+    // lane l visits candidates l, l + 32, ...: every warp load reads 128 contiguous bytes, and the
+    // row (a few KB) stays in L1 across the passes
     uint32_t prefix = 0, pmask = 0;
     int remaining = want;
     const bool take_none = want == 0;
@@ -208,7 +208,16 @@ __global__ void __launch_bounds__(32 * SELW_WARPS) select_scores_warp_kernel(Dev
         for (int shift = 24; shift >= 0; shift -= 8) {
             for (int i = lane; i < 256; i += 32) hw[i] = 0;
             __syncwarp();
-            for (int b = lo; b < hi; b++) {
+            int b = lane;
+            for (; b + 96 < cand_hi; b += 128) {
+                uint32_t k4[4];
+                #pragma unroll
+                for (int u = 0; u < 4; u++) k4[u] = __float_as_uint(__ldg(sc + b + 32 * u));
+                #pragma unroll
+                for (int u = 0; u < 4; u++)
+                    if ((k4[u] & pmask) == prefix) atomicAdd(&hw[(k4[u] >> shift) & 255u], 1u);
+            }
+            for (; b < cand_hi; b += 32) {
                 const uint32_t key = __float_as_uint(__ldg(sc + b));
                 if ((key & pmask) == prefix) atomicAdd(&hw[(key >> shift) & 255u], 1u);
             }
@@ -246,51 +255,30 @@ __global__ void __launch_bounds__(32 * SELW_WARPS) select_scores_warp_kernel(Dev
             __syncwarp();
         }
     }
-    // keys above the cut are kept; keys equal to it (all 32 bits) by lower block index, `remaining` of them
-    auto cmp = [&](int b) -> int {                       // 1 above, 0 equal, -1 below
-        const uint32_t key = __float_as_uint(__ldg(sc + b));
-        return key > prefix ? 1 : (key == prefix ? 0 : -1);
-    };
-    int n_take = 0, n_eq = 0;
-    if (take_all) {
-        n_take = hi - lo;
-    } else if (!take_none) {
-        for (int b = lo; b < hi; b++) {
-            const int c = cmp(b);
-            n_take += c > 0;
-            n_eq += c == 0;
-        }
-    }
-    // ties before this lane's run
-    int eq_incl = n_eq;
-    #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, eq_incl, o);
-        if (lane >= o) eq_incl += y;
-    }
-    const int eq_before = eq_incl - n_eq;
-    const int eq_mine = (take_all || take_none) ? 0 : max(0, min(n_eq, remaining - eq_before));
-    const int mine = n_take + eq_mine;
-    int pos_incl = mine;
-    #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, pos_incl, o);
-        if (lane >= o) pos_incl += y;
-    }
-    int pos = pos_incl - mine;
-    const int n_cand_taken = __shfl_sync(0xffffffffu, pos_incl, 31);
-    int eq_left = eq_mine;
-    for (int b = take_none ? hi : lo; b < hi; b++) {
-        bool tk;
-        if (take_all) tk = true;
-        else {
-            const int c = cmp(b);
-            tk = c > 0 || (c == 0 && eq_left > 0);
-            if (c == 0 && eq_left > 0) eq_left--;
-        }
-        if (tk) {
-            if (pos < d.kb) { sel[pos] = b; if (so) so[pos] = b; }
-            pos++;
+    // emission in ascending block order, 32 blocks at a time: keys above the cut are kept, keys
+    // equal to it (all 32 bits) by lower block index, `remaining` of them
+    const unsigned lt = (1u << lane) - 1u;
+    int n_cand_taken = 0, eq_seen = 0;
+    if (!take_none) {
+        for (int b0 = 0; b0 < cand_hi; b0 += 32) {
+            const int b = b0 + lane;
+            bool above = false, eq = false;
+            if (b < cand_hi) {
+                if (take_all) {
+                    above = true;
+                } else {
+                    const uint32_t key = __float_as_uint(__ldg(sc + b));
+                    above = key > prefix;
+                    eq = key == prefix;
+                }
+            }
+            const unsigned eqb = __ballot_sync(0xffffffffu, eq);
+            const bool tk = above || (eq && eq_seen + __popc(eqb & lt) < remaining);
+            const unsigned tb = __ballot_sync(0xffffffffu, tk);
+            const int pos = n_cand_taken + __popc(tb & lt);
+            if (tk && pos < d.kb) { sel[pos] = b; if (so) so[pos] = b; }
+            n_cand_taken += __popc(tb);
+            eq_seen += __popc(eqb);
         }
     }
     // forced blocks follow (they are above every candidate)

@@ -200,6 +200,28 @@ def test_prefill_parity_and_chunk_invariance():
         assert rel_err(out1[t], ref) <= ATTN_TOL
 
 
+@pytest.mark.parametrize("top_k", [16, 40])
+def test_prefill_radix_selection_and_attention(top_k):
+    """More visible blocks than top_k: the radix cut of the warp-per-query selection (not the
+    take-everything branch), then the block-grouped attention, against the oracle; chunking the
+    same tokens gives the same selections."""
+    d = desc_for(TYPE_Q8_0, 16384, top_k=top_k)
+    n_past, T = 9000, 200                          # 140..143 whole blocks visible
+    node, st, (q, q_idx, k, v, ki), out1, sel1 = run_prefill(d, n_past, T, [T], 71)
+    _, _, _, out2, sel2 = run_prefill(d, n_past, T, [64, 136], 71)
+    assert np.array_equal(sel1, sel2)
+    assert rel_err(out2, out1) <= ATTN_TOL
+    kc, vc, _, pool = host_caches(st, 0, n_past + T)
+    qh, qt = q_host(q)
+    qi = q_idx.cpu().numpy()
+    for t in list(range(0, T, 17)) + [T - 1]:
+        qp = n_past + t
+        sc = oracle.scores(d, pool, (qp + 1) // 64, qi[t])[0]
+        check_selection(d, sel1[t], sc, qp)
+        ref = oracle.attend(d, kc, vc, [qp], sel1[t][None], qh[t][None], q_type=qt)[0]
+        assert rel_err(out1[t], ref) <= ATTN_TOL
+
+
 @pytest.mark.parametrize("kv_type", [TYPE_Q8_0, TYPE_F16])
 def test_prefill_ignores_unwritten_cells(kv_type):
     """Cells at or past n_past + T of the last block are never written; with their bytes all 0xFF
