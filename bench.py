@@ -24,6 +24,7 @@ import re
 import statistics
 import subprocess
 import sys
+import tempfile
 import threading
 import time
 
@@ -51,15 +52,36 @@ def profile_traffic(name: str):
     return float(m.group(1)) if m else None
 
 
+NVML_SAMPLER = r"""
+import sys, time
+import pynvml
+pynvml.nvmlInit()
+h = pynvml.nvmlDeviceGetHandleByIndex(int(sys.argv[1]))
+mx = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+out = sys.stdout
+while True:
+    sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+    bits = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+    out.write("%.6f,%d,%d,%d\n" % (time.time(), sm, mx, bits))
+    time.sleep(0.0005)
+"""
+
+
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 5 ms while running."""
+    """SM clocks and throttle reasons while running (read-only queries): a child process samples
+    NVML every ~0.5 ms and stamps each sample with its wall time, so that even millisecond timed
+    regions get samples inside them whatever the main process is doing; nvidia-smi at 5 ms runs
+    beside it (its lines arrive buffered, so they only count towards the reasons seen in the run)."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
+    NVML_BITS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+                 ("sw_power_cap", 0x4))
 
     def __init__(self, gpu_index: str):
         self.samples, self.proc, self.gpu = [], None, gpu_index
         self.t0 = self.t1 = None
+        self.nvml_proc, self.nvml_samples = None, []
 
     def start(self):
         try:
@@ -70,6 +92,15 @@ class ClockSampler:
             self.thread.start()
         except OSError:
             self.proc = None
+        try:                                   # unbuffered child writing to a file: nothing is lost at stop
+            self.nvml_file = tempfile.TemporaryFile(mode="w+")
+            self.nvml_proc = subprocess.Popen([sys.executable, "-u", "-c", NVML_SAMPLER, str(int(self.gpu))],
+                                              stdout=self.nvml_file, stderr=subprocess.DEVNULL, text=True)
+            t_end = time.time() + 5.0          # the timed region starts once the child is sampling
+            while time.time() < t_end and self.nvml_proc.poll() is None and os.fstat(self.nvml_file.fileno()).st_size == 0:
+                time.sleep(0.01)
+        except (OSError, ValueError):
+            self.nvml_proc = None
 
     def _read(self):
         for line in self.proc.stdout:
@@ -79,6 +110,22 @@ class ClockSampler:
         setattr(self, which, time.time())
 
     def stop(self):
+        if self.nvml_proc:
+            self.nvml_proc.terminate()
+            try:
+                self.nvml_proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.nvml_proc.kill()
+                self.nvml_proc.wait()
+            self.nvml_file.seek(0)
+            out = self.nvml_file.read()
+            self.nvml_file.close()
+            for line in out.splitlines():
+                try:
+                    t, sm, mx, bits = line.split(",")
+                    self.nvml_samples.append((float(t), int(sm), int(mx), int(bits)))
+                except ValueError:
+                    continue
         if self.proc:
             self.proc.terminate()
             try:
@@ -88,24 +135,32 @@ class ClockSampler:
             self.thread.join(timeout=2)
 
     def summary(self):
-        if not self.samples:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
-        inside = [s for t, s in self.samples if self.t0 and self.t1 and self.t0 <= t <= self.t1]
-        use = inside or [s for _, s in self.samples[-10:]]
+        marked = self.t0 is not None and self.t1 is not None
+        nv_inside = [x for x in self.nvml_samples if marked and self.t0 <= x[0] <= self.t1]
+        sm, mx, reasons = [], [], set()
+        nv_use = nv_inside or self.nvml_samples[-20:]
+        for _, f, m, bits in nv_use:
+            sm.append(float(f))
+            mx.append(float(m))
+            for n, bit in self.NVML_BITS:
+                if bits & bit:
+                    reasons.add(n)
         names = ["active", "hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = set()
-        sm, mx = [], []
-        for s in use:
+        for _, s in self.samples:
             try:
-                sm.append(float(s[1]))
-                mx.append(float(s[2]))
+                if not nv_use:
+                    sm.append(float(s[1]))
+                    mx.append(float(s[2]))
             except (ValueError, IndexError):
                 continue
             for i, n in enumerate(names[1:], start=5):
-                if i < len(s) and s[i].lower().startswith("active"):
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(use), "samples_in_timed_region": len(inside)}
+                if i < len(s) and s[i].lower().startswith("active") and n != "sw_power_cap":
+                    reasons.add(n)            # a slowdown seen anywhere in the run is reported
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no clock samples"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(nv_use) if nv_use else len(self.samples), "samples_in_timed_region": len(nv_inside),
+                "sources": "NVML every 0.5 ms (child process) + nvidia-smi -lms 5"}
 
 
 # ------------------------------------------------------------------------------------------------
@@ -496,12 +551,14 @@ def run_ours_config5(args, ws, rank, local):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     NL, n_past = cfg.layers, cfg.n_past
-    dec = ShardedDecoder(d, rank=rank, world=ws, exchange=args.exchange, batch=1)
+    lb = args.layer_batch                      # the 12 independent layers as one batch of 12 items
+    dec = ShardedDecoder(d, rank=rank, world=ws, exchange=args.exchange, batch=NL if lb else 1)
     node = QsaNode(d, dev)
     st = QsaState(d, n_layers=NL, device=dev, blocks=dec.blocks)
     for il in range(NL):                       # every rank draws the same stream, keeps its cells
         fill_cache(node, st, il, n_past, cfg.seed * 1000 + il, append=dec.append)
     items = [decode_items([st.layer(il)], [n_past], device=dev) for il in range(NL)]
+    items_all = decode_items([st.layer(il) for il in range(NL)], [n_past] * NL, device=dev)
     KB = k_blocks(d)
     S = 4
     ins = [token_inputs(d, NL, cfg.seed + 100 * s) for s in range(S)]     # identical on every rank
@@ -516,6 +573,11 @@ def run_ours_config5(args, ws, rank, local):
 
     def step():
         q, qi, k, v, ki = slots
+        if lb:                                 # one exchange of candidates and one of states for all layers
+            o = dec.step(items_all, NL, n_past + 1, q, qi, k, v, ki, sel_out=sel)
+            for il in range(NL):
+                outs[il] = o[il:il + 1]
+            return
         for il in range(NL):
             outs[il] = dec.step(items[il], 1, n_past + 1, q[il:il + 1], qi[il:il + 1], k[il:il + 1], v[il:il + 1],
                                 ki[il:il + 1], sel_out=sel[il:il + 1])
@@ -575,7 +637,7 @@ def run_ours_config5(args, ws, rank, local):
     torch.cuda.synchronize()
     e2e_us = [a.elapsed_time(b) * 1e3 for a, b in e2e]
     clocks.stop()
-    if dec.backend.check(1, n_past + 1) != 0:
+    if dec.backend.check(NL if lb else 1, n_past + 1) != 0:
         raise SystemExit("device status error")
     sel_h = sel.cpu().numpy()
     lo, hi = dec.blocks
@@ -597,7 +659,9 @@ def run_ours_config5(args, ws, rank, local):
         "scaling": "strong", "vs_baseline": None, "dtype": "q8_0 KV, bf16 Q, f16 MMA / f32 softmax",
         "data": "synthetic",
         "config": {"workload": "config5: decode 1 token through 12 layers, ctx 1048576, q8_0, top-128 of 16384 "
-                               "blocks + 128-token window (131 blocks)",
+                               "blocks + 128-token window (131 blocks)"
+                               + (", the 12 independent layers issued as one batch (one candidate and one state "
+                                  "exchange per token for all layers)" if lb else ", layer after layer"),
                    "global_batch": 1, "seq_len": n_past + 1, "layers": NL,
                    "parallelism": (f"KV-sequence-sharded x{ws} ("
                                    + ("NVLink peer-memory all-gathers" if args.exchange == "peer" else "NCCL all-gathers")
@@ -613,7 +677,7 @@ def run_ours_config5(args, ws, rank, local):
         "e2e": {"value": round(e2e_max / NL, 3), "unit": "us/layer-token",
                 "h2d_bytes_per_step": sum(x.numel() * x.element_size() for x in ins[0]),
                 "d2h_bytes_per_step": NL * d.n_head * d.head_dim * 4},
-        "gpu_launches": 5 * NL * K,          # per layer: append, select, global select, attention, merge
+        "gpu_launches": 5 * (1 if lb else NL) * K,   # per call: append, select, global select, attention, merge
         "clocks": clocks.summary(),
     }
     del g, g_attn                               # graphs holding NCCL work go before the process group
@@ -794,6 +858,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layer-batch", action="store_true",
+                    help="config 5: issue the 12 independent layers as one batch of 12 items (2 exchanges per token)")
     ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
                     help="config 5 with N > 1: the shards' exchanges over NVLink peer memory or NCCL")
     args = ap.parse_args()
