@@ -589,13 +589,15 @@ def run_ours_config5(args, ws, rank, local):
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g, capture_error_mode="thread_local"):
         step()
-    # the attention stage of layer 0 alone (the dominant kernel), on this rank's share
-    cand = dec.backend.candidates(items[0], 1, n_past + 1, dec.blocks, slots[1][:1])
+    # the attention stage alone (the dominant kernel), on this rank's share: layer 0, or all 12
+    # layers in one launch with --layer-batch
+    a_items, a_b = (items_all, NL) if lb else (items[0], 1)
+    cand = dec.backend.candidates(a_items, a_b, n_past + 1, dec.blocks, slots[1][:a_b])
     gathered, cstride = dec._all_gather(cand, 0)
     torch.cuda.synchronize()
     g_attn = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g_attn):
-        dec.backend.attend(items[0], 1, n_past + 1, dec.blocks, gathered, slots[0][:1], n_shards=dec.world,
+        dec.backend.attend(a_items, a_b, n_past + 1, dec.blocks, gathered, slots[0][:a_b], n_shards=dec.world,
                            cand_stride=cstride)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
 
@@ -645,8 +647,9 @@ def run_ours_config5(args, ws, rank, local):
     scored = max(0, min(hi, (n_past + 1) // d.ratio) - lo)
     sf = 16 * (2 + d.head_dim) * 4
     step_bytes = local_cells * 2 * 544 + NL * (scored * 256 + 2 * 544 + 256 + (ws + 1) * sf)
-    attn_cells0 = attended_cells([b for b in sel_h[0] if lo <= b < hi], n_past, d.ratio)
-    attn_bytes = attn_cells0 * 2 * 544 + 16 * 256 * 2 + sf
+    attn_layers = range(NL) if lb else range(1)
+    attn_cells0 = sum(attended_cells([b for b in sel_h[il] if lo <= b < hi], n_past, d.ratio) for il in attn_layers)
+    attn_bytes = attn_cells0 * 2 * 544 + len(attn_layers) * (16 * 256 * 2 + sf)
     attn_mean = statistics.mean(attn_us)
     hbm, _, src = peaks()
     achieved = attn_bytes / (attn_mean * 1e-6) / 1e9
@@ -668,7 +671,8 @@ def run_ours_config5(args, ws, rank, local):
                                    + ")") if ws > 1 else "1 GPU",
                    "blocks_per_gpu": hi - lo,
                    "l2": "flushed (256 MB write) before every timed step", "cuda_graph": True},
-        "roofline": {"bound": "hbm", "kernel": "attn_kernel<q8_0> (qsa_shard_attend), layer 0, rank 0",
+        "roofline": {"bound": "hbm", "kernel": "attn_kernel<q8_0> (qsa_shard_attend), "
+                               + ("all 12 layers in one launch" if lb else "layer 0") + ", rank 0",
                      "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
                      "peak_source": f"{src} hbm_gbs (burst)", "traffic": None,
                      "algorithmic_bytes_per_launch": attn_bytes, "launch_us": round(attn_mean, 3)},

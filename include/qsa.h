@@ -205,8 +205,10 @@ qsa_status qsa_decode_noalloc(const qsa_desc * d, const qsa_decode_item * items,
  *      domain), its sum of weights, and its unnormalised output.
  *   4. the caller all-gathers the states: [n_shards][batch][...].
  *   5. qsa_merge_states: out f32 [batch][n_head][head_dim], as qsa_decode's.
- * Workspaces are sized by qsa_decode_workspace_size with the global max_n_kv. */
+ * Workspaces are sized by qsa_shard_workspace_size with the global max_n_kv and the shard's
+ * block range (the attention's split over CTAs follows the shard's expected share of blocks). */
 size_t qsa_shard_state_floats(const qsa_desc * d);
+size_t qsa_shard_workspace_size(const qsa_desc * d, int32_t batch, int32_t max_n_kv, int32_t blk_lo, int32_t blk_hi);
 /* qsa_append into a shard's local arrays: global rows [pos0, pos0+n_tok), all inside the shard's
  * cells; pooled keys carry their global block positions. */
 qsa_status qsa_shard_append(const qsa_desc * d, const qsa_layer_cache * cache /* host struct */,

@@ -110,6 +110,7 @@ def lib() -> ctypes.CDLL:
         "qsa_append": (I32, [D, C, I32, I32, VP, VP, VP, VP]),
         "qsa_pool_rebuild": (I32, [D, C, I32, I32, VP, VP]),
         "qsa_decode_workspace_size": (SZ, [D, I32, I32]),
+        "qsa_shard_workspace_size": (SZ, [D, I32, I32, I32, I32]),
         "qsa_workspace_init": (I32, [VP, SZ, VP]),
         "qsa_decode": (I32, [D, VP, I32, I32, VP, I32, VP, VP, VP, VP, VP, VP, VP, SZ, VP]),
         "qsa_decode_append": (I32, [D, VP, I32, I32, VP, VP, VP, VP, SZ, VP]),
@@ -149,7 +150,8 @@ HEADER_SYMBOLS = [
     "qsa_status_string", "qsa_desc_check", "qsa_k_blocks", "qsa_row_bytes", "qsa_cache_bytes",
     "qsa_append", "qsa_pool_rebuild", "qsa_decode_workspace_size", "qsa_workspace_init",
     "qsa_decode", "qsa_decode_append", "qsa_decode_select", "qsa_decode_attend", "qsa_decode_noalloc",
-    "qsa_shard_state_floats", "qsa_shard_append", "qsa_shard_candidates", "qsa_shard_attend", "qsa_merge_states",
+    "qsa_shard_state_floats", "qsa_shard_workspace_size", "qsa_shard_append", "qsa_shard_candidates", "qsa_shard_attend",
+    "qsa_merge_states",
     "qsa_ipc_handle", "qsa_ipc_open", "qsa_ipc_close", "qsa_peer_buffer_bytes", "qsa_peer_push", "qsa_peer_wait",
     "qsa_prefill_workspace_size", "qsa_prefill", "qsa_check", "qsa_version",
 ]

@@ -58,15 +58,26 @@ WsLayout ws_layout(const DevDesc & d, int n_q, int max_n_kv) {
     WsLayout w;
     w.scores_stride = std::max(4, ceil_div(ceil_div(max_n_kv, d.ratio), 4) * 4);   // 16-byte rows
     const int max_tiles = std::max(1, ceil_div((int64_t) d.kb * d.ratio, attn_tile_cells()));
+    // Tiles a query is expected to have here: all of them, or on a KV shard its share of the
+    // visible blocks (selections are spread over the sequence) plus the window, which its tail
+    // shard holds.  The grid still covers max_tiles; chunks past a query's tiles exit at once.
+    int exp_tiles = max_tiles;
+    if (d.shard_blk0 > 0 || d.shard_blk1 != INT_MAX) {
+        const int64_t n_blk = std::max(1, ceil_div(max_n_kv, d.ratio));
+        const int64_t mine = std::max<int64_t>(0, std::min<int64_t>(d.shard_blk1, n_blk) - d.shard_blk0);
+        exp_tiles = std::min<int64_t>(max_tiles, ceil_div((int64_t) max_tiles * mine, n_blk) +
+                                                     ceil_div((int64_t) d.n_force * d.ratio, attn_tile_cells()));
+        exp_tiles = std::max(1, exp_tiles);
+    }
     // Chunks (CTAs) per query: one tile each while every tile of the batch fits one wave of
     // attention CTAs (latency); otherwise as many chunks as one wave gives each query.
     const int wave = attn_resident_ctas(d.type_k);
     int tpc;
-    if ((int64_t) n_q * max_tiles <= wave) {
+    if ((int64_t) n_q * exp_tiles <= wave) {
         tpc = 1;
     } else {
-        const int nch = std::min(std::max(1, wave / n_q), max_tiles);
-        tpc = ceil_div(max_tiles, nch);
+        const int nch = std::min(std::max(1, wave / n_q), exp_tiles);
+        tpc = ceil_div(exp_tiles, nch);
     }
     if (tiles_override() > 0) tpc = tiles_override();
     tpc = std::min(tpc, max_tiles);
@@ -264,6 +275,14 @@ size_t qsa_decode_workspace_size(const qsa_desc * dd, int32_t batch, int32_t max
     return ws_layout(make_dev(dd), batch, max_n_kv).total;
 }
 
+size_t qsa_shard_workspace_size(const qsa_desc * dd, int32_t batch, int32_t max_n_kv, int32_t blk_lo, int32_t blk_hi) {
+    if (qsa_desc_check(dd) != QSA_OK || batch <= 0 || max_n_kv <= 0 || blk_lo < 0 || blk_hi <= blk_lo) return 0;
+    DevDesc d = make_dev(dd);
+    d.shard_blk0 = blk_lo;
+    d.shard_blk1 = blk_hi;
+    return ws_layout(d, batch, max_n_kv).total;
+}
+
 namespace {
 // The prefill's KV-stationary attention applies (and how many blocks its buckets cover).
 bool prefill_kv_path(const DevDesc & d, int T) { return T >= 64 && prefill_kv_supported(d, T); }
@@ -419,12 +438,16 @@ size_t qsa_shard_state_floats(const qsa_desc * d) {
 namespace {
 qsa_status shard_common(const qsa_desc * dd, const qsa_decode_item * items, int32_t batch, int32_t max_n_kv,
                         int32_t blk_lo, int32_t blk_hi, void * ws, size_t ws_bytes, DevDesc & d, WsLayout & w) {
-    qsa_status s = decode_common(dd, items, batch, max_n_kv, ws, ws_bytes, d, w);
+    qsa_status s = qsa_desc_check(dd);
     if (s != QSA_OK) return s;
+    if (!items || batch <= 0 || max_n_kv <= 0 || max_n_kv > dd->n_ctx) return QSA_ERR_INVALID;
     if (blk_lo < 0 || blk_hi <= blk_lo || (int64_t) blk_hi * dd->ratio > dd->n_ctx) return QSA_ERR_INVALID;
+    d = make_dev(dd);
     d.shard_blk0 = blk_lo;
     d.shard_blk1 = blk_hi;
-    return QSA_OK;
+    w = ws_layout(d, batch, max_n_kv);
+    if (!ws || ws_bytes < w.total) return QSA_ERR_WORKSPACE;
+    return set_attrs();
 }
 }  // namespace
 

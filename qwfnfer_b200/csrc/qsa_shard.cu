@@ -35,18 +35,20 @@ __device__ __forceinline__ int warp_incl_scan(int x, int lane) {
 // block ids (-1 = none), then the f32 scores' bits.  Every shard sends its kept blocks in
 // ascending order and the shards hold ascending block ranges, so the concatenation of the lists
 // (slot order) is ascending by block: a radix select over the scores (8-bit digits from the top)
-// with the lower slot first on equal scores is the global rule (score, then lower block).  Writes
-// the global selection (ascending, -1 padded) to sel_out (optional) and this rank's blocks
-// [blo, bhi) of it to the workspace list the attention kernel reads.  A candidate that no shard
-// could have sent (not visible, forced, or not a non-negative score) is dropped and flagged.
-__global__ void __launch_bounds__(32 * SHARD_SEL_WARPS) shard_select_kernel(DevDesc d,
-        const qsa_decode_item * __restrict__ items, int n_shards, int batch,
+// with the lower slot first on equal scores is the global rule (score, then lower block).  The
+// warp stages its query's slots in shared memory (coalesced), runs the radix passes over them and
+// emits the kept slots 32 at a time in slot order with ballots.  Writes the global selection
+// (ascending, -1 padded) to sel_out (optional) and this rank's blocks [blo, bhi) of it to the
+// workspace list the attention kernel reads.  A candidate that no shard could have sent (not
+// visible, forced, or not a non-negative score) is dropped and flagged.
+__global__ void shard_select_kernel(DevDesc d, const qsa_decode_item * __restrict__ items, int n_shards, int batch,
         const int * __restrict__ cand, size_t cand_stride, int blo, int bhi,
         int * __restrict__ sel_out, int * __restrict__ sel_ws, int * __restrict__ nsel_ws,
         uint32_t * __restrict__ status) {
+    extern __shared__ int ss_smem[];                 // per warp: [n] block ids, then [n] keys
     __shared__ unsigned hist[SHARD_SEL_WARPS][256];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int t = blockIdx.x * SHARD_SEL_WARPS + warp;
+    const int t = blockIdx.x * (blockDim.x >> 5) + warp;
     if (t >= batch) return;
     const int q = items[t].n_past;
     const int kb = d.kb;
@@ -63,24 +65,24 @@ __global__ void __launch_bounds__(32 * SHARD_SEL_WARPS) shard_select_kernel(DevD
     const int want = max(0, kb - n_forced);
     const int n_vis = (q + 1) / d.ratio;
     const int n = n_shards * kb;                     // candidate slots, slot i = shard i / kb, entry i % kb
-    auto slot_block = [&](int i) -> int {
-        return cand[(size_t) (i / kb) * cand_stride + (size_t) t * kb + (i % kb)];
-    };
-    auto slot_key = [&](int i) -> uint32_t {
-        return (uint32_t) cand[(size_t) (i / kb) * cand_stride + (size_t) (batch + t) * kb + (i % kb)];
-    };
-    auto valid = [&](int b, uint32_t key) {
-        return b >= 0 && b < n_vis && !(b >= f_lo && b <= f_hi) && (key >> 31) == 0u && key <= 0x7f800000u;
-    };
-    const int per = (n + 31) / 32;
-    const int lo = min(n, lane * per), hi = min(n, lo + per);
+    int * sb = ss_smem + (size_t) warp * 2 * n;
+    uint32_t * sk = reinterpret_cast<uint32_t *>(sb + n);
     int n_valid = 0;
-    for (int i = lo; i < hi; i++) {
-        const int b = slot_block(i);
-        if (b < 0) continue;
-        if (valid(b, slot_key(i))) n_valid++;
-        else set_status(status, DEV_BAD_SEL);
+    for (int s = 0; s < n_shards; s++) {
+        const int * ids = cand + (size_t) s * cand_stride + (size_t) t * kb;
+        const int * keys = cand + (size_t) s * cand_stride + (size_t) (batch + t) * kb;
+        for (int j = lane; j < kb; j += 32) {
+            int b = ids[j];
+            const uint32_t key = (uint32_t) keys[j];
+            if (b >= 0) {
+                if (b < n_vis && !(b >= f_lo && b <= f_hi) && (key >> 31) == 0u && key <= 0x7f800000u) n_valid++;
+                else { set_status(status, DEV_BAD_SEL); b = -1; }
+            }
+            sb[s * kb + j] = b;
+            sk[s * kb + j] = key;
+        }
     }
+    __syncwarp();
     int tot_valid = warp_incl_scan(n_valid, lane);
     tot_valid = __shfl_sync(0xffffffffu, tot_valid, 31);
     const bool take_all = tot_valid <= want;
@@ -88,14 +90,27 @@ __global__ void __launch_bounds__(32 * SHARD_SEL_WARPS) shard_select_kernel(DevD
     int remaining = want;
     unsigned * hw = hist[warp];
     if (!take_all && want > 0) {
-        for (int shift = 24; shift >= 0; shift -= 8) {
+        // the bits every valid key shares need no pass: digits start at the highest differing bit
+        uint32_t kmin = 0xffffffffu, kmax = 0u;
+        for (int i = lane; i < n; i += 32)
+            if (sb[i] >= 0) { kmin = min(kmin, sk[i]); kmax = max(kmax, sk[i]); }
+        #pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            kmin = min(kmin, __shfl_xor_sync(0xffffffffu, kmin, o));
+            kmax = max(kmax, __shfl_xor_sync(0xffffffffu, kmax, o));
+        }
+        int hi_bit = kmin == kmax ? -1 : 31 - __clz(kmin ^ kmax);
+        // bits 0..hi_bit (none when every valid key is equal: the cut is that key)
+        const uint32_t low = hi_bit < 0 ? 0u : (hi_bit >= 31 ? 0xffffffffu : (2u << hi_bit) - 1u);
+        pmask = ~low;
+        prefix = kmax & pmask;
+        while (hi_bit >= 0) {
+            const int width = min(8, hi_bit + 1), shift = hi_bit + 1 - width;
+            const uint32_t dmask = (1u << width) - 1u;
             for (int i = lane; i < 256; i += 32) hw[i] = 0;
             __syncwarp();
-            for (int i = lo; i < hi; i++) {
-                const int b = slot_block(i);
-                const uint32_t key = slot_key(i);
-                if (valid(b, key) && (key & pmask) == prefix) atomicAdd(&hw[(key >> shift) & 255u], 1u);
-            }
+            for (int i = lane; i < n; i += 32)
+                if (sb[i] >= 0 && (sk[i] & pmask) == prefix) atomicAdd(&hw[(sk[i] >> shift) & dmask], 1u);
             __syncwarp();
             int own = 0;
             #pragma unroll
@@ -118,54 +133,35 @@ __global__ void __launch_bounds__(32 * SHARD_SEL_WARPS) shard_select_kernel(DevD
             bin = __shfl_sync(0xffffffffu, bin, src);
             cut_rem = __shfl_sync(0xffffffffu, cut_rem, src);
             prefix |= (uint32_t) bin << shift;
-            pmask |= 255u << shift;
+            pmask |= dmask << shift;
             remaining = cut_rem;
+            hi_bit = shift - 1;
             __syncwarp();
         }
     }
     const bool none = !take_all && want == 0;
-    // per slot: 2 kept, 1 equal to the cut, 0 not kept
-    auto cls = [&](int i) -> int {
-        const int b = slot_block(i);
-        const uint32_t key = slot_key(i);
-        if (!valid(b, key) || none) return 0;
-        if (take_all) return 2;
-        return key > prefix ? 2 : (key == prefix ? 1 : 0);
-    };
-    int n_take = 0, n_tie = 0;
-    for (int i = lo; i < hi; i++) {
-        const int c = cls(i);
-        n_take += c == 2;
-        n_tie += c == 1;
-    }
-    const int tie_incl = warp_incl_scan(n_tie, lane);
-    const int tie_mine = max(0, min(n_tie, remaining - (tie_incl - n_tie)));
-    // positions in the global list and in this rank's list
-    int n_mine_rank = 0;
-    {
-        int tl = tie_mine;
-        for (int i = lo; i < hi; i++) {
-            const int c = cls(i);
-            bool tk = c == 2;
-            if (c == 1 && tl > 0) { tk = true; tl--; }
-            if (tk) { const int b = slot_block(i); n_mine_rank += b >= blo && b < bhi; }
+    // emission in slot order: keys above the cut kept, keys equal to it by lower slot, `remaining`
+    // of them; positions in the global list and in this rank's list by ballots
+    const unsigned lt = (1u << lane) - 1u;
+    int n_cand_kept = 0, n_rank_kept = 0, ties_seen = 0;
+    for (int i0 = 0; i0 < n; i0 += 32) {
+        const int i = i0 + lane;
+        int c = 0, b = -1;
+        if (i < n && !none) {
+            b = sb[i];
+            if (b >= 0) c = take_all ? 2 : (sk[i] > prefix ? 2 : (sk[i] == prefix ? 1 : 0));
         }
-    }
-    const int mine = n_take + tie_mine;
-    const int pos_incl = warp_incl_scan(mine, lane), rk_incl = warp_incl_scan(n_mine_rank, lane);
-    int pos = pos_incl - mine, rpos = rk_incl - n_mine_rank;
-    const int n_cand_kept = __shfl_sync(0xffffffffu, pos_incl, 31);
-    const int n_rank_kept = __shfl_sync(0xffffffffu, rk_incl, 31);
-    int tl = tie_mine;
-    for (int i = lo; i < hi; i++) {
-        const int c = cls(i);
-        bool tk = c == 2;
-        if (c == 1 && tl > 0) { tk = true; tl--; }
-        if (!tk) continue;
-        const int b = slot_block(i);
-        if (so && pos < kb) so[pos] = b;
-        pos++;
-        if (b >= blo && b < bhi) { if (rpos < kb) sw[rpos] = b; rpos++; }
+        const unsigned tieb = __ballot_sync(0xffffffffu, c == 1);
+        const bool tk = c == 2 || (c == 1 && ties_seen + __popc(tieb & lt) < remaining);
+        const unsigned tb = __ballot_sync(0xffffffffu, tk);
+        const bool rk = tk && b >= blo && b < bhi;
+        const unsigned rb = __ballot_sync(0xffffffffu, rk);
+        const int pos = n_cand_kept + __popc(tb & lt), rpos = n_rank_kept + __popc(rb & lt);
+        if (tk && so && pos < kb) so[pos] = b;
+        if (rk && rpos < kb) sw[rpos] = b;
+        n_cand_kept += __popc(tb);
+        n_rank_kept += __popc(rb);
+        ties_seen += __popc(tieb);
     }
     // the forced blocks follow (they are above every candidate)
     const int f_rank_lo = max(f_lo, blo), f_rank_hi = min(f_hi, bhi - 1);
@@ -180,6 +176,116 @@ __global__ void __launch_bounds__(32 * SHARD_SEL_WARPS) shard_select_kernel(DevD
     if (so) for (int i = m_all + lane; i < kb; i += 32) so[i] = -1;
     for (int i = m_rank + lane; i < kb; i += 32) sw[i] = -1;
     if (lane == 0) nsel_ws[t] = m_rank;
+}
+
+// The same selection for lists of up to SORT_MAX slots, one CTA per query: each slot's 64-bit key
+// (score bits, then the complement of its slot index; 0 for an empty or dropped slot) is sorted
+// descending by a bitonic network in shared memory, so the first `want` keys are the kept ones
+// (higher score, then lower block); kept flags are then scanned in slot order (ascending blocks).
+constexpr int SORT_MAX = 2048;
+
+__global__ void __launch_bounds__(1024) shard_select_sort_kernel(DevDesc d, const qsa_decode_item * __restrict__ items,
+        int n_shards, int batch, const int * __restrict__ cand, size_t cand_stride, int blo, int bhi,
+        int * __restrict__ sel_out, int * __restrict__ sel_ws, int * __restrict__ nsel_ws, uint32_t * __restrict__ status) {
+    __shared__ unsigned long long key[SORT_MAX];
+    __shared__ int blk[SORT_MAX];
+    __shared__ unsigned char kept[SORT_MAX];
+    __shared__ int wsum[2][32];
+    __shared__ int n_valid_s;
+    const int t = blockIdx.x, tid = threadIdx.x, nthr = blockDim.x, lane = tid & 31, warp = tid >> 5;
+    const int q = items[t].n_past;
+    const int kb = d.kb;
+    int * sw = sel_ws + (size_t) t * kb;
+    int * so = sel_out ? sel_out + (size_t) t * kb : nullptr;
+    if (q < 0 || q >= d.n_ctx) {
+        if (tid == 0) { set_status(status, DEV_BAD_POS); nsel_ws[t] = 0; }
+        for (int i = tid; i < kb; i += nthr) { sw[i] = -1; if (so) so[i] = -1; }
+        return;
+    }
+    int f_lo, f_hi;
+    shard_forced_range(d, q, f_lo, f_hi);
+    const int n_forced = f_hi >= f_lo ? f_hi - f_lo + 1 : 0;
+    const int want = max(0, kb - n_forced);
+    const int n_vis = (q + 1) / d.ratio;
+    const int n = n_shards * kb;
+    int n2 = 1;
+    while (n2 < n) n2 <<= 1;
+    if (tid == 0) n_valid_s = 0;
+    __syncthreads();
+    int my_valid = 0;
+    for (int i = tid; i < n2; i += nthr) {
+        unsigned long long k = 0ull;
+        int b = -1;
+        if (i < n) {
+            const int s = i / kb, j = i - s * kb;
+            b = cand[(size_t) s * cand_stride + (size_t) t * kb + j];
+            const uint32_t kbits = (uint32_t) cand[(size_t) s * cand_stride + (size_t) (batch + t) * kb + j];
+            if (b >= 0) {
+                if (b < n_vis && !(b >= f_lo && b <= f_hi) && (kbits >> 31) == 0u && kbits <= 0x7f800000u) {
+                    k = ((unsigned long long) kbits << 32) | (0xffffffffu - (uint32_t) i);
+                    my_valid++;
+                } else {
+                    set_status(status, DEV_BAD_SEL);
+                    b = -1;
+                }
+            }
+        }
+        key[i] = k;
+        if (i < n) { blk[i] = b; kept[i] = 0; }
+    }
+    if (my_valid) atomicAdd(&n_valid_s, my_valid);
+    __syncthreads();
+    // bitonic sort, descending
+    for (int size = 2; size <= n2; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int i = tid; i < n2 / 2; i += nthr) {
+                const int lo = 2 * i - (i & (stride - 1));     // index with the stride bit clear
+                const int hi = lo + stride;
+                const bool desc = (lo & size) == 0;
+                const unsigned long long a = key[lo], c = key[hi];
+                if ((a < c) == desc) { key[lo] = c; key[hi] = a; }
+            }
+            __syncthreads();
+        }
+    }
+    const int n_keep = min(want, n_valid_s);
+    for (int i = tid; i < n_keep; i += nthr) kept[0xffffffffu - (uint32_t) (key[i] & 0xffffffffull)] = 1;
+    __syncthreads();
+    // positions in slot order: a CTA scan of the kept flags (all kept, and this rank's)
+    int n_cand_kept = 0, n_rank_kept = 0;
+    for (int base = 0; base < n; base += nthr) {
+        const int i = base + tid;
+        const bool tk = i < n && kept[i];
+        const int b = tk ? blk[i] : -1;
+        const bool rk = tk && b >= blo && b < bhi;
+        const unsigned tb = __ballot_sync(0xffffffffu, tk), rb = __ballot_sync(0xffffffffu, rk);
+        if (lane == 0) { wsum[0][warp] = __popc(tb); wsum[1][warp] = __popc(rb); }
+        __syncthreads();
+        int pre_t = 0, pre_r = 0, tot_t = 0, tot_r = 0;
+        for (int w = 0; w < nthr / 32; w++) {
+            if (w < warp) { pre_t += wsum[0][w]; pre_r += wsum[1][w]; }
+            tot_t += wsum[0][w];
+            tot_r += wsum[1][w];
+        }
+        const unsigned lt = (1u << lane) - 1u;
+        const int pos = n_cand_kept + pre_t + __popc(tb & lt), rpos = n_rank_kept + pre_r + __popc(rb & lt);
+        if (tk && so && pos < kb) so[pos] = b;
+        if (rk && rpos < kb) sw[rpos] = b;
+        n_cand_kept += tot_t;
+        n_rank_kept += tot_r;
+        __syncthreads();
+    }
+    // the forced blocks follow (they are above every candidate)
+    const int f_rank_lo = max(f_lo, blo), f_rank_hi = min(f_hi, bhi - 1);
+    const int n_f_rank = n_forced ? max(0, f_rank_hi - f_rank_lo + 1) : 0;
+    for (int i = tid; i < n_forced; i += nthr)
+        if (so && n_cand_kept + i < kb) so[n_cand_kept + i] = f_lo + i;
+    for (int i = tid; i < n_f_rank; i += nthr)
+        if (n_rank_kept + i < kb) sw[n_rank_kept + i] = f_rank_lo + i;
+    const int m_all = min(kb, n_cand_kept + n_forced), m_rank = min(kb, n_rank_kept + n_f_rank);
+    if (so) for (int i = m_all + tid; i < kb; i += nthr) so[i] = -1;
+    for (int i = m_rank + tid; i < kb; i += nthr) sw[i] = -1;
+    if (tid == 0) nsel_ws[t] = m_rank;
 }
 
 // out[t][h][d] from the gathered states [n_parts][batch][M 16 | L 16 | O 16x256], merged in rank
@@ -206,7 +312,28 @@ __global__ void __launch_bounds__(256) merge_states_kernel(DevDesc d, int n_part
 cudaError_t launch_shard_select(const DevDesc & d, cudaStream_t st, const qsa_decode_item * items, int n_shards,
         int batch, const int * cand, size_t cand_stride, int blo, int bhi, int * sel_out, int * sel_ws, int * nsel_ws,
         uint32_t * status) {
-    shard_select_kernel<<<(batch + SHARD_SEL_WARPS - 1) / SHARD_SEL_WARPS, 32 * SHARD_SEL_WARPS, 0, st>>>(
+    const int n = n_shards * d.kb;
+    if (n <= SORT_MAX) {                    // a CTA per query: bitonic sort of the slot keys
+        int n2 = 1;
+        while (n2 < n) n2 <<= 1;
+        const int thr = std::max(32, std::min(1024, n2 / 2));
+        shard_select_sort_kernel<<<batch, thr, 0, st>>>(d, items, n_shards, batch, cand, cand_stride, blo, bhi, sel_out,
+                                                      sel_ws, nsel_ws, status);
+        return cudaGetLastError();
+    }
+    // longer lists: a warp per query stages its slots (8 bytes each) in shared memory
+    const size_t per_warp = (size_t) n * 8;
+    constexpr size_t SMEM_MAX = 200 * 1024;
+    if (per_warp > SMEM_MAX) return cudaErrorInvalidValue;
+    const int warps = (int) std::min<size_t>(std::min<size_t>(SHARD_SEL_WARPS, SMEM_MAX / per_warp), (size_t) batch);
+    const size_t smem = per_warp * warps;
+    static size_t attr = 48 * 1024;
+    if (smem > attr) {
+        cudaError_t e = cudaFuncSetAttribute(shard_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) SMEM_MAX);
+        if (e != cudaSuccess) return e;
+        attr = SMEM_MAX;
+    }
+    shard_select_kernel<<<(batch + warps - 1) / warps, 32 * warps, smem, st>>>(
         d, items, n_shards, batch, cand, cand_stride, blo, bhi, sel_out, sel_ws, nsel_ws, status);
     return cudaGetLastError();
 }

@@ -57,12 +57,17 @@ class LibShardBackend:
         self.kb = k_blocks(desc)
         self.state_floats = lib().qsa_shard_state_floats(ctypes.byref(desc))
         self._ws: dict[int, torch.Tensor] = {}
+        self._blocks: tuple[int, int] | None = None       # the shard range of the last call
 
     def _stream(self) -> int:
         return torch.cuda.current_stream(self.device).cuda_stream
 
-    def workspace(self, batch: int, max_n_kv: int) -> torch.Tensor:
-        size = lib().qsa_decode_workspace_size(ctypes.byref(self.desc), batch, max_n_kv)
+    def workspace(self, batch: int, max_n_kv: int, blocks: tuple[int, int] | None = None) -> torch.Tensor:
+        blocks = blocks if blocks is not None else self._blocks
+        if blocks is None:
+            raise ValueError("no shard block range yet")
+        self._blocks = tuple(blocks)
+        size = lib().qsa_shard_workspace_size(ctypes.byref(self.desc), batch, max_n_kv, blocks[0], blocks[1])
         if size == 0:
             raise ValueError("invalid decode shape")
         ws = self._ws.get(size)
@@ -82,7 +87,7 @@ class LibShardBackend:
         """This rank's candidates, int32 [2, batch, KB]: block ids (-1 padded), then score bits."""
         if out is None:
             out = torch.empty((2, batch, self.kb), dtype=torch.int32, device=self.device)
-        ws = self.workspace(batch, max_n_kv)
+        ws = self.workspace(batch, max_n_kv, blocks)
         check(lib().qsa_shard_candidates(ctypes.byref(self.desc), _ptr(items), batch, max_n_kv, blocks[0], blocks[1],
                                          _ptr(q_idx), _ptr(k_new), _ptr(v_new), _ptr(kidx_new), _ptr(out),
                                          ws.data_ptr(), ws.numel(), self._stream()), "qsa_shard_candidates")
@@ -97,7 +102,7 @@ class LibShardBackend:
         if state is None:
             state = torch.empty((batch, self.state_floats), dtype=torch.float32, device=self.device)
         q_type = TYPE_BF16 if q.dtype == torch.bfloat16 else TYPE_F32
-        ws = self.workspace(batch, max_n_kv)
+        ws = self.workspace(batch, max_n_kv, blocks)
         check(lib().qsa_shard_attend(ctypes.byref(self.desc), _ptr(items), batch, max_n_kv, blocks[0], blocks[1],
                                      n_shards, _ptr(gathered), cand_stride, _ptr(q), q_type, state.data_ptr(),
                                      _ptr(sel_out), ws.data_ptr(), ws.numel(), self._stream()), "qsa_shard_attend")
@@ -113,8 +118,8 @@ class LibShardBackend:
               "qsa_merge_states")
         return out
 
-    def check(self, batch: int, max_n_kv: int) -> int:
-        ws = self.workspace(batch, max_n_kv)
+    def check(self, batch: int, max_n_kv: int, blocks: tuple[int, int] | None = None) -> int:
+        ws = self.workspace(batch, max_n_kv, blocks)
         return lib().qsa_check(ws.data_ptr(), ws.numel(), self._stream())
 
 

@@ -106,3 +106,35 @@ def test_shard_select_drops_impossible_candidates():
     state = dec.backend.attend(it, 1, 5001, dec.blocks, gathered, q)
     assert dec.backend.check(1, 5001) == QSA_ERR_DEVICE_ARG
     assert not torch.isnan(state).any()
+
+
+@pytest.mark.parametrize("case", ["all_equal", "tie_at_cut"])
+def test_shard_select_equal_keys_by_lower_block(case):
+    """Global selection from hand-made candidate lists of 2 shards whose scores tie: equal keys
+    are kept by lower block (slot order), also when every key is equal."""
+    d = make_desc(n_ctx=8192, top_k_blocks=16, window=128)
+    pos = 5000                                        # 78 whole blocks visible; forced 76..78
+    node, full, ranks = build(d, 2, [pos], seeds=[33])
+    q, _, _, _, _ = token_inputs(d, 1, seed=34)
+    KB = k_blocks(d)
+    want = KB - 3
+    lists = [list(range(0, 19)), list(range(64, 76))]  # what the two shards could send (ascending)
+    f32 = lambda x: int(np.float32(x).view(np.int32))
+    if case == "all_equal":
+        keys = [[f32(0.5)] * 19, [f32(0.5)] * 12]
+        expect = list(range(0, want))
+    else:
+        keys = [[f32(0.25)] * 19, [f32(1.0)] * 6 + [f32(0.25)] * 6]
+        expect = list(range(0, want - 6)) + list(range(64, 70))
+    expect = sorted(expect) + [76, 77, 78]
+    gathered = torch.full((2, 2, 1, KB), -1, dtype=torch.int32)
+    for s in range(2):
+        gathered[s, 0, 0, :len(lists[s])] = torch.tensor(lists[s], dtype=torch.int32)
+        gathered[s, 1, 0, :len(keys[s])] = torch.tensor(keys[s], dtype=torch.int32)
+    gathered = gathered.cuda()
+    for dec, sts in ranks:
+        it = decode_items([s.layer() for s in sts], [pos])
+        sel = torch.empty(1, KB, dtype=torch.int32, device="cuda")
+        dec.backend.attend(it, 1, pos + 1, dec.blocks, gathered, q, sel_out=sel)
+        assert dec.backend.check(1, pos + 1) == QSA_OK
+        assert sel.cpu().numpy()[0].tolist() == expect
