@@ -569,6 +569,9 @@ __global__ void __launch_bounds__(ATT_THREADS, AttnCfg<KV_TYPE>::MIN_CTAS) attn_
 // attn_kernel.
 constexpr int MERGE_COLS = 16;                        // float4 columns: 64 dims per CTA
 constexpr int MERGE_GROUPS = MERGE_THREADS / MERGE_COLS;
+// PRE: partial loads per thread issued up front (16 for long splits such as a batch-1 query over
+// 134 chunks; 2 for batched decode, whose few chunks per query need few registers)
+template <int PRE>
 __global__ void __launch_bounds__(MERGE_THREADS) attn_merge_kernel(DevDesc d, const qsa_decode_item * __restrict__ items,
         int n_past0, const int * __restrict__ nsel_ws, int tiles_per_cta, int max_chunks,
         const float * __restrict__ part_o, const float * __restrict__ part_ml,
@@ -589,6 +592,16 @@ __global__ void __launch_bounds__(MERGE_THREADS) attn_merge_kernel(DevDesc d, co
     const int nsel = pos_ok ? max(0, min(nsel_ws[t], d.kb)) : 0;
     const int n_chunks = attn_n_chunks(d, nsel, tiles_per_cta);
     if (n_chunks <= 1) return;                        // written by the attention CTA itself
+    // the partial rows do not depend on the weights: this thread's (up to PRE) loads go out
+    // first, and the max / weight / sum rounds run while they are in flight
+    const float4 * po = reinterpret_cast<const float4 *>(part_o + ((size_t) t * max_chunks * HROWS + hr) * HEAD_DIM) + d4;
+    const size_t cstride = (size_t) HROWS * HEAD_DIM / 4;         // float4s between chunks
+    float4 pre[PRE];
+    #pragma unroll
+    for (int k = 0; k < PRE; k++) {
+        const int c = grp + k * MERGE_GROUPS;
+        pre[k] = c < n_chunks ? __ldcg(po + (size_t) c * cstride) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     const float * ml = part_ml + (size_t) t * max_chunks * 2 * HROWS;
     float M = -INFINITY;
     for (int c = tid; c < n_chunks; c += MERGE_THREADS) M = fmaxf(M, __ldcg(ml + c * 2 * HROWS + hr));
@@ -612,11 +625,15 @@ __global__ void __launch_bounds__(MERGE_THREADS) attn_merge_kernel(DevDesc d, co
     L = 0.0f;
     #pragma unroll
     for (int w = 0; w < MERGE_THREADS / 32; w++) L += red[1][w];
-    const float4 * po = reinterpret_cast<const float4 *>(part_o + ((size_t) t * max_chunks * HROWS + hr) * HEAD_DIM) + d4;
-    const size_t cstride = (size_t) HROWS * HEAD_DIM / 4;         // float4s between chunks
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    #pragma unroll
+    for (int k = 0; k < PRE; k++) {
+        const int c = grp + k * MERGE_GROUPS;
+        const float w = c < n_chunks ? wsh[c] : 0.0f;
+        acc.x += w * pre[k].x; acc.y += w * pre[k].y; acc.z += w * pre[k].z; acc.w += w * pre[k].w;
+    }
     #pragma unroll 4
-    for (int c = grp; c < n_chunks; c += MERGE_GROUPS) {
+    for (int c = grp + PRE * MERGE_GROUPS; c < n_chunks; c += MERGE_GROUPS) {   // longer splits
         const float4 v = __ldcg(po + (size_t) c * cstride);
         const float w = wsh[c];
         acc.x += w * v.x; acc.y += w * v.y; acc.z += w * v.z; acc.w += w * v.w;
@@ -689,7 +706,10 @@ cudaError_t launch_attn(const DevDesc & d, cudaStream_t st, int n_q, const qsa_d
     mc.gridDim = dim3((unsigned) n_q, HROWS, HEAD_DIM / (4 * MERGE_COLS));
     mc.blockDim = dim3(MERGE_THREADS);
     mc.dynamicSmemBytes = (size_t) max_chunks * 4;
-    return cudaLaunchKernelEx(&mc, attn_merge_kernel, d, items, n_past0, nsel_ws, tiles_per_cta, max_chunks,
+    if (max_chunks > 2 * MERGE_GROUPS)
+        return cudaLaunchKernelEx(&mc, attn_merge_kernel<16>, d, items, n_past0, nsel_ws, tiles_per_cta, max_chunks,
+                                  (const float *) part_o, (const float *) part_ml, out, state_out);
+    return cudaLaunchKernelEx(&mc, attn_merge_kernel<2>, d, items, n_past0, nsel_ws, tiles_per_cta, max_chunks,
                               (const float *) part_o, (const float *) part_ml, out, state_out);
 }
 
