@@ -298,6 +298,7 @@ def run_ours_config2(args, ws, rank, local):
         torch.cuda.synchronize()
         return [a.elapsed_time(b) * 1e3 for a, b in ev]   # us
 
+    launches = _launches_per_replay(g_step)
     clocks = ClockSampler(os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local]
                           if "CUDA_VISIBLE_DEVICES" in os.environ else str(local))
     clocks.start()
@@ -368,7 +369,7 @@ def run_ours_config2(args, ws, rank, local):
                       "attend": round(attn_mean, 3)},
         "e2e": {"value": round(e2e_total / units, 3), "unit": "us/layer-token", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
-        "gpu_launches": 3 * K,
+        "gpu_launches": launches * K,       # libqsa kernels per replay (CUPTI count) x timed steps
         "clocks": clocks.summary(),
     }
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
@@ -392,6 +393,18 @@ def _timed_replays(graph, n, before=None):
         ev[i][1].record()
     torch.cuda.synchronize()
     return [a.elapsed_time(b) * 1e3 for a, b in ev]
+
+
+def _launches_per_replay(graph):
+    """libqsa kernels in one replay of `graph`, counted from CUPTI kernel records (torch.profiler)
+    of a replay outside the timed region."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        graph.replay()
+        torch.cuda.synchronize()
+    return sum(1 for e in prof.events() if e.device_type.name == "CUDA" and "qsa" in e.name)
 
 
 def _clock_sampler(local):
@@ -466,6 +479,7 @@ def run_ours_config3(args, ws, rank, local):
         flush.zero_()
 
     K = args.steps
+    launches = _launches_per_replay(g_step)
     clocks = _clock_sampler(local)
     clocks.start()
     _timed_replays(g_step, 20, before)
@@ -529,7 +543,7 @@ def run_ours_config3(args, ws, rank, local):
         "stages_us": {"step": round(statistics.mean(step_us), 3), "attend": round(attn_mean, 3)},
         "e2e": {"value": round(e2e_max / n_tok, 4), "unit": "us/token", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
-        "gpu_launches": 3 * K,
+        "gpu_launches": launches * K,       # libqsa kernels per replay (CUPTI count) x timed steps
         "clocks": clocks.summary(),
     }
 
@@ -606,6 +620,7 @@ def run_ours_config5(args, ws, rank, local):
         flush.zero_()
 
     K = args.steps
+    launches = _launches_per_replay(g)
     clocks = _clock_sampler(local)
     clocks.start()
     _timed_replays(g, 10, before)
@@ -681,7 +696,7 @@ def run_ours_config5(args, ws, rank, local):
         "e2e": {"value": round(e2e_max / NL, 3), "unit": "us/layer-token",
                 "h2d_bytes_per_step": sum(x.numel() * x.element_size() for x in ins[0]),
                 "d2h_bytes_per_step": NL * d.n_head * d.head_dim * 4},
-        "gpu_launches": 5 * (1 if lb else NL) * K,   # per call: append, select, global select, attention, merge
+        "gpu_launches": launches * K,       # libqsa kernels per replay (CUPTI count) x timed steps
         "clocks": clocks.summary(),
     }
     del g, g_attn                               # graphs holding NCCL work go before the process group
@@ -733,6 +748,7 @@ def run_ours_config4(args, ws, rank, local):
         step_api(_stream(None))
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     K = args.steps
+    launches = _launches_per_replay(g)
     clocks = _clock_sampler(local)
     clocks.start()
     _timed_replays(g, 2, lambda i: flush.zero_())
@@ -791,7 +807,7 @@ def run_ours_config4(args, ws, rank, local):
         "e2e": {"value": round(toks / (e2e_max * 1e-6), 1), "unit": "tok/s",
                 "h2d_bytes_per_step": sum(x.numel() * x.element_size() for x in (q, qi, k, v, ki)),
                 "d2h_bytes_per_step": out.numel() * out.element_size()},
-        "gpu_launches": 5 * K,
+        "gpu_launches": launches * K,       # libqsa kernels per replay (CUPTI count) x timed steps
         "clocks": clocks.summary(),
     }
 
