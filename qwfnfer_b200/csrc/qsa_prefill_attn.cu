@@ -190,8 +190,13 @@ __device__ __forceinline__ bool mbar_poll_bounded(uint64_t * bar, uint32_t parit
     return false;
 }
 // ------------------------------------------------------------------ attention per (block, KV head)
-__device__ __forceinline__ uint32_t f16x2_scaled(int8_t a, int8_t b, float d) {
-    return pack_f16x2((float) a * d, (float) b * d);        // f16(d x q), exact product rounded once
+// Bytes 0 and 2 of t (int8) times the f16 scale, as f16x2: the bytes become exact f16 integers and
+// the f16 multiply rounds d x q once, as the reference's f16(f32(d) * q) does (that f32 product is
+// exact).
+__device__ __forceinline__ uint32_t i8x2_scaled(uint32_t t, __half2 d) {
+    const uint32_t x = i8x2_even_to_f16x2(t);
+    const __half2 r = __hmul2(*reinterpret_cast<const __half2 *>(&x), d);
+    return *reinterpret_cast<const uint32_t *>(&r);
 }
 
 struct PaBarriers {
@@ -282,12 +287,12 @@ __global__ void __launch_bounds__(PA_THREADS, 1) prefill_attn_kv_kernel(
         uint4 w = make_uint4(0, 0, 0, 0);
         if (cell < n_valid) {
             const uint8_t * blk = (kv ? rawV : rawK) + cell * PA_HEAD_Q8 + (d8 >> 2) * Q8_0_BYTES;
-            const float sc = f16_bits_to_f32(*reinterpret_cast<const uint16_t *>(blk));
+            const __half2 sc = __half2half2(__ushort_as_half(*reinterpret_cast<const uint16_t *>(blk)));
             const uint32_t lo = lds_u32_a2(blk + 2 + (d8 & 3) * 8), hi = lds_u32_a2(blk + 6 + (d8 & 3) * 8);
-            w.x = f16x2_scaled((int8_t) lo, (int8_t) (lo >> 8), sc);
-            w.y = f16x2_scaled((int8_t) (lo >> 16), (int8_t) (lo >> 24), sc);
-            w.z = f16x2_scaled((int8_t) hi, (int8_t) (hi >> 8), sc);
-            w.w = f16x2_scaled((int8_t) (hi >> 16), (int8_t) (hi >> 24), sc);
+            w.x = i8x2_scaled(__byte_perm(lo, 0u, 0x0100), sc);
+            w.y = i8x2_scaled(__byte_perm(lo, 0u, 0x0302), sc);
+            w.z = i8x2_scaled(__byte_perm(hi, 0u, 0x0100), sc);
+            w.w = i8x2_scaled(__byte_perm(hi, 0u, 0x0302), sc);
         }
         *reinterpret_cast<uint4 *>((kv ? sV : sK) + sw128_off(PA_CELLS, cell, d8 * 8)) = w;
     }
