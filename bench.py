@@ -250,8 +250,15 @@ def run_ours_config2(args, ws, rank, local):
     items = decode_items([st.layer()], [n_past], device=dev)
     KB = k_blocks(d)
     wsb = node.workspace("decode", 1, n_past + 1)
-    # static buffers for graph replay; slot inputs are copied in before each timed step
-    sq, sqi, sk, sv, ski = (torch.empty_like(x[:1]) for x in (q, qi, k, v, ki))
+    # static buffers for graph replay; slot inputs are copied in before each timed step.  They are
+    # slices of one device staging buffer, so that the e2e step brings a token's inputs over in one
+    # copy from one pinned host buffer (how an engine holding its activations together would).
+    parts = [x[:1] for x in (q, qi, k, v, ki)]
+    nbytes = [x.numel() * x.element_size() for x in parts]
+    offs = [sum(nbytes[:i]) for i in range(len(nbytes))]
+    assert all(o % 16 == 0 for o in offs)
+    dstage = torch.empty(sum(nbytes), dtype=torch.uint8, device=dev)
+    sq, sqi, sk, sv, ski = (dstage[o:o + n].view(x.dtype).view(x.shape) for x, o, n in zip(parts, offs, nbytes))
     out = torch.empty(1, d.n_head, d.head_dim, device=dev)
     sel = torch.empty(1, KB, dtype=torch.int32, device=dev)
     L = lib()
@@ -316,7 +323,10 @@ def run_ours_config2(args, ws, rank, local):
     attn_us = timed(g_attn, K)
     sel_us = timed(g_sel, K)
     # e2e through the public C ABI with pinned host buffers, copies inside the timed region
-    hq, hqi, hk, hv, hki = (x.cpu().pin_memory() for x in (q, qi, k, v, ki))
+    hstage = torch.empty(S, dstage.numel(), dtype=torch.uint8).pin_memory()   # one packed row per token
+    for s_, row in enumerate(hstage):
+        for x, o, n in zip((q, qi, k, v, ki), offs, nbytes):
+            row[o:o + n].copy_(x[s_:s_ + 1].contiguous().view(torch.uint8).reshape(-1).cpu())
     hout = torch.empty(S, d.n_head, d.head_dim).pin_memory()
     stream = torch.cuda.current_stream()
     e2e = []
@@ -325,9 +335,7 @@ def run_ours_config2(args, ws, rank, local):
         flush.zero_()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
-        sq.copy_(hq[s:s + 1], non_blocking=True); sqi.copy_(hqi[s:s + 1], non_blocking=True)
-        sk.copy_(hk[s:s + 1], non_blocking=True); sv.copy_(hv[s:s + 1], non_blocking=True)
-        ski.copy_(hki[s:s + 1], non_blocking=True)
+        dstage.copy_(hstage[s], non_blocking=True)
         step_api(stream.cuda_stream)
         hout[s:s + 1].copy_(out, non_blocking=True)
         b.record()
@@ -335,7 +343,7 @@ def run_ours_config2(args, ws, rank, local):
     torch.cuda.synchronize()
     e2e_us = [a.elapsed_time(b) * 1e3 for a, b in e2e]
     clocks.stop()
-    h2d = sum(x[:1].numel() * x.element_size() for x in (q, qi, k, v, ki))
+    h2d = dstage.numel()
     d2h = out.numel() * out.element_size()
     check(node.check(wsb), "qsa_check")
 
@@ -858,7 +866,8 @@ def run_reference_config2(args):
         times.append(time.perf_counter() - t0)
     us = statistics.mean(times) * 1e6
     return {
-        "impl": "reference", "metric": METRIC, "value": round(us, 1), "unit": "us/layer-token", "n_gpus": 0,
+        "impl": "reference", "metric": METRIC, "value": round(us, 1), "unit": "us/layer-token",
+        "n_gpus": args.gpus,                   # the N of the launch (rank 0 runs the CPU arm alone)
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(us / 1e3, 4), "higher_is_better": False,
         "scaling": "weak", "vs_baseline": None, "dtype": "q8_0 KV, f16-rounded K/V and Q, f32 softmax", "data": "synthetic",
         "config": {"workload": "config2: decode 1 token, 1 layer, ctx 163840, q8_0 KV, top-64 + 128-token window",
