@@ -164,6 +164,10 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap * ma
     asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
                  :: "r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)) : "memory");
 }
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap * map, int x, int y, int z, uint64_t * bar) {
+    asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+                 :: "r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar)) : "memory");
+}
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap * map, int w, uint64_t * bar) {
     asm volatile("cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %2, %2, %3}], [%4];"
                  :: "r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(w), "r"(smem_u32(bar)) : "memory");
@@ -235,6 +239,7 @@ __global__ void __launch_bounds__(PA_THREADS, 1) prefill_attn_kv_kernel(
     unsigned char * rawK = sQ0 + PA_SQ;
     unsigned char * rawV = rawK + PA_CELLS * PA_HEAD_Q8;
     const int n_valid = min(PA_CELLS, n_kv - b * PA_CELLS);
+    const bool kv_f16 = d.type_k == QSA_TYPE_F16;
 
     if (warp == 0) tmem_alloc_warp(&tmem_slot, PA_TMEM_COLS);
     if (tid == 32) {
@@ -268,12 +273,20 @@ __global__ void __launch_bounds__(PA_THREADS, 1) prefill_attn_kv_kernel(
                         &bars.q_full[s]);
     };
     if (warp == 8) {
-        // the block's raw K and V rows of head g: one box of 64 rows x 272 bytes each (the bytes of
-        // cells past n_kv are fetched too, and ignored)
         if (lane == 0) {
-            mbar_arrive_expect_tx(&bars.kv_full, (uint32_t) (2 * PA_CELLS * PA_HEAD_Q8));
-            tma_load_2d(smem_u32(rawK), &k_map, g * (PA_HEAD_Q8 / 2), b * PA_CELLS, &bars.kv_full);
-            tma_load_2d(smem_u32(rawV), &v_map, g * (PA_HEAD_Q8 / 2), b * PA_CELLS, &bars.kv_full);
+            if (kv_f16) {
+                // f16 caches: head g's K and V tiles straight into the swizzled [cell][dim] layout
+                // (atoms 4g..4g+3 of the rows; cells past n_kv are zeroed below)
+                mbar_arrive_expect_tx(&bars.kv_full, (uint32_t) (PA_SK + PA_SV));
+                tma_load_3d(aK, &k_map, 0, b * PA_CELLS, 4 * g, &bars.kv_full);
+                tma_load_3d(aV, &v_map, 0, b * PA_CELLS, 4 * g, &bars.kv_full);
+            } else {
+                // q8_0: the block's raw rows of head g, one box of 64 rows x 272 bytes each (the bytes
+                // of cells past n_kv are fetched too, and ignored)
+                mbar_arrive_expect_tx(&bars.kv_full, (uint32_t) (2 * PA_CELLS * PA_HEAD_Q8));
+                tma_load_2d(smem_u32(rawK), &k_map, g * (PA_HEAD_Q8 / 2), b * PA_CELLS, &bars.kv_full);
+                tma_load_2d(smem_u32(rawV), &v_map, g * (PA_HEAD_Q8 / 2), b * PA_CELLS, &bars.kv_full);
+            }
         }
         load_q(0, chunk_entry(0, lane));
     }
@@ -282,6 +295,13 @@ __global__ void __launch_bounds__(PA_THREADS, 1) prefill_attn_kv_kernel(
     // ---- K and V -> f16 (d x q), both as [cell][dim] (K-major for S = Q K^T, MN-major for O = P V);
     // cells at or past n_kv are zero (their bytes may decode to Inf or NaN, and a masked P of 0
     // times a NaN is NaN in the MMA)
+    if (kv_f16) {
+        for (int i = tid; i < 2 * (PA_CELLS - n_valid) * (HEAD_DIM / 8); i += PA_THREADS) {
+            const int per = (PA_CELLS - n_valid) * (HEAD_DIM / 8);
+            const int kv = i >= per, j = i - kv * per, cell = n_valid + (j >> 5), d8 = j & 31;
+            *reinterpret_cast<uint4 *>((kv ? sV : sK) + sw128_off(PA_CELLS, cell, d8 * 8)) = make_uint4(0, 0, 0, 0);
+        }
+    } else
     for (int i = tid; i < 2 * PA_CELLS * (HEAD_DIM / 8); i += PA_THREADS) {   // (K or V, cell, 8-dim group)
         const int kv = i >> 11, cell = (i >> 5) & (PA_CELLS - 1), d8 = i & 31;
         uint4 w = make_uint4(0, 0, 0, 0);
@@ -541,7 +561,9 @@ __global__ void prefill_merge_kernel(DevDesc d, int T, int slots, const int * __
 
 bool prefill_kv_supported(const DevDesc & d, int T) {
     // partial rows are indexed in int32 (TMA coordinates): T * kb * n_head < 2^31
-    return d.type_k == QSA_TYPE_Q8_0 && d.type_v == QSA_TYPE_Q8_0 && d.ratio == PA_CELLS && d.gqa == GQA_TILE &&
+    const bool types = (d.type_k == QSA_TYPE_Q8_0 && d.type_v == QSA_TYPE_Q8_0) ||
+                       (d.type_k == QSA_TYPE_F16 && d.type_v == QSA_TYPE_F16);
+    return types && d.ratio == PA_CELLS && d.gqa == GQA_TILE &&
            d.head_dim == HEAD_DIM && d.kb <= (1 << PA_SLOT_SHIFT) && d.n_head <= 32 &&
            (int64_t) T * d.kb * d.n_head < ((int64_t) 1 << 31);
 }
@@ -597,6 +619,20 @@ bool encode_groups_map(CUtensorMap * map, void * ptr, uint64_t groups, uint32_t 
                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// an f16 cache (n_ctx rows of row_bytes) as {64 dims, rows, atoms of 64 dims (128 bytes apart)}: a box
+// of 64 rows x 4 atoms is one head's [cell][dim] tile in the 128-byte swizzled layout
+bool encode_cache_map_f16(CUtensorMap * map, const void * ptr, int64_t row_bytes, int n_ctx, int n_head_kv) {
+    encode_tiled_fn enc = tensor_map_encoder();
+    if (!enc) return false;
+    const cuuint64_t dims[3] = {64, (cuuint64_t) n_ctx, (cuuint64_t) (4 * n_head_kv)};
+    const cuuint64_t strides[2] = {(cuuint64_t) row_bytes, 128};
+    const cuuint32_t box[3] = {64, (cuuint32_t) PA_CELLS, 4};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(ptr), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // the raw bytes of a q8_0 cache (n_ctx rows of row_bytes) as u16 elements; boxes of one head's
 // 272 bytes x 64 rows, no swizzle (rows past n_ctx read as zero)
 bool encode_cache_map(CUtensorMap * map, const void * ptr, int64_t row_bytes, int n_ctx) {
@@ -635,7 +671,10 @@ cudaError_t launch_prefill_attn_kv(const DevDesc & d, cudaStream_t st, qsa_layer
     float * part_ml = reinterpret_cast<float *>(ws + L.part_ml);
     CUtensorMap q_map, k_map, v_map;
     if (!encode_groups_map(&q_map, q16, (uint64_t) T * d.n_head_kv, 1) ||
-        !encode_cache_map(&k_map, cache.k, d.rb_k, d.n_ctx) || !encode_cache_map(&v_map, cache.v, d.rb_v, d.n_ctx))
+        (d.type_k == QSA_TYPE_F16
+             ? !encode_cache_map_f16(&k_map, cache.k, d.rb_k, d.n_ctx, d.n_head_kv) ||
+               !encode_cache_map_f16(&v_map, cache.v, d.rb_v, d.n_ctx, d.n_head_kv)
+             : !encode_cache_map(&k_map, cache.k, d.rb_k, d.n_ctx) || !encode_cache_map(&v_map, cache.v, d.rb_v, d.n_ctx)))
         return cudaErrorNotSupported;
     cudaError_t e = cudaMemsetAsync(cnt, 0, (size_t) n_blocks * 4, st);
     if (e != cudaSuccess) return e;

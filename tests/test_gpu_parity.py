@@ -200,12 +200,12 @@ def test_prefill_parity_and_chunk_invariance():
         assert rel_err(out1[t], ref) <= ATTN_TOL
 
 
-@pytest.mark.parametrize("top_k", [16, 40])
-def test_prefill_radix_selection_and_attention(top_k):
+@pytest.mark.parametrize("kv_type,top_k", [(TYPE_Q8_0, 16), (TYPE_Q8_0, 40), (TYPE_F16, 16)])
+def test_prefill_radix_selection_and_attention(kv_type, top_k):
     """More visible blocks than top_k: the radix cut of the warp-per-query selection (not the
     take-everything branch), then the block-grouped attention, against the oracle; chunking the
     same tokens gives the same selections."""
-    d = desc_for(TYPE_Q8_0, 16384, top_k=top_k)
+    d = desc_for(kv_type, 16384, top_k=top_k)
     n_past, T = 9000, 200                          # 140..143 whole blocks visible
     node, st, (q, q_idx, k, v, ki), out1, sel1 = run_prefill(d, n_past, T, [T], 71)
     _, _, _, out2, sel2 = run_prefill(d, n_past, T, [64, 136], 71)
