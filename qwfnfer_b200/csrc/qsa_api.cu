@@ -9,11 +9,6 @@
 namespace qsa {
 namespace {
 
-// Tiles per attention CTA; QSA_TILES_PER_CTA overrides the heuristic (tuning).
-int tiles_override() {
-    static int v = [] { const char * e = getenv("QSA_TILES_PER_CTA"); return e ? atoi(e) : 0; }();
-    return v;
-}
 
 inline int ceil_div(int64_t a, int64_t b) { return (int) ((a + b - 1) / b); }
 
@@ -79,7 +74,6 @@ WsLayout ws_layout(const DevDesc & d, int n_q, int max_n_kv) {
         const int nch = std::min(std::max(1, wave / n_q), exp_tiles);
         tpc = ceil_div(exp_tiles, nch);
     }
-    if (tiles_override() > 0) tpc = tiles_override();
     tpc = std::min(tpc, max_tiles);
     w.tiles_per_cta = tpc;
     w.max_chunks = ceil_div(max_tiles, tpc);

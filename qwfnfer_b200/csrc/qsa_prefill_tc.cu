@@ -21,6 +21,7 @@
 // a time in ascending order with ballots (equal keys at the cut kept by lower block index), then
 // the forced blocks.
 #include "qsa_kernels.cuh"
+#include "qsa_tc.cuh"
 
 namespace qsa {
 
@@ -32,27 +33,8 @@ constexpr int TC_A_BYTES = TC_M * TC_K * 2;      // 32 KB
 constexpr int TC_B_BYTES = TC_N * TC_K * 2;      // 64 KB
 constexpr int TC_SMEM = TC_A_BYTES + TC_B_BYTES + 1024;   // + alignment slack for the 1024-byte swizzle atoms
 
-// Byte offset of the 16-byte chunk c (k = 8c .. 8c+7) of row r in a K-major, 128-byte-swizzled
-// tile of `rows` rows and 128 f16 columns: two atoms of 64 columns, each rows x 128 B in groups of 8
-// rows (1024 B); inside a group, chunk c of row r sits at chunk position c ^ (r % 8).
-__device__ __forceinline__ uint32_t sw128_offset(int rows, int r, int c) {
-    const int atom = c >> 3, cc = c & 7;
-    return (uint32_t) (atom * rows * 128 + (r >> 3) * 1024 + (r & 7) * 128 + ((cc ^ (r & 7)) << 4));
-}
-
-// Shared-memory matrix descriptor (tcgen05): start address >> 4, leading byte offset 1 (unused for
-// swizzled K-major), stride byte offset 1024 >> 4 between 8-row groups, version 1, layout
-// SWIZZLE_128B (2).
-__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr) {
-    return (uint64_t) ((smem_addr >> 4) & 0x3FFFu) | ((uint64_t) 1 << 16) | ((uint64_t) 64 << 32) |
-           ((uint64_t) 1 << 46) | ((uint64_t) 2 << 61);
-}
-
 // Instruction descriptor, kind::f16: D f32, A and B f16, both K-major, N = 256, M = 128.
-constexpr uint32_t TC_IDESC = (1u << 4) | ((uint32_t) (TC_N >> 3) << 17) | ((uint32_t) (TC_M >> 4) << 24);
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+constexpr uint32_t TC_IDESC = umma_idesc_f16(TC_M, TC_N);
 
 __global__ void __launch_bounds__(TC_THREADS) idx_scores_tc_kernel(DevDesc d, const float * __restrict__ q_idx,
         int n_rows, const uint16_t * __restrict__ pool, int n_blocks, float * __restrict__ scores, int scores_stride,
@@ -68,11 +50,7 @@ __global__ void __launch_bounds__(TC_THREADS) idx_scores_tc_kernel(DevDesc d, co
     unsigned char * sA = tc_smem_raw + (base - raw);
     unsigned char * sB = sA + TC_A_BYTES;
 
-    if (warp == 0) {                          // TMEM accumulator: 128 lanes x 256 f32 columns
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
-                     :: "r"(smem_u32(&tmem_slot)), "r"(TC_N) : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-    }
+    if (warp == 0) tmem_alloc_warp(&tmem_slot, TC_N);   // TMEM accumulator: 128 lanes x 256 f32 columns
     if (tid == 0) {
         mbar_init(&mma_bar, 1);
         fence_mbar_init();
@@ -87,16 +65,16 @@ __global__ void __launch_bounds__(TC_THREADS) idx_scores_tc_kernel(DevDesc d, co
             v.x = pack_f16x2(a.x, a.y); v.y = pack_f16x2(a.z, a.w);
             v.z = pack_f16x2(b.x, b.y); v.w = pack_f16x2(b.z, b.w);
         }
-        *reinterpret_cast<uint4 *>(sA + sw128_offset(TC_M, r, c)) = v;
+        *reinterpret_cast<uint4 *>(sA + sw128_off(TC_M, r, 8 * c)) = v;
     }
     // B: pooled keys of blocks blk0 .. blk0+255 (already F16)
     for (int i = tid; i < TC_N * (TC_K / 8); i += TC_THREADS) {
         const int r = i >> 4, c = i & 15;
         uint4 v = make_uint4(0, 0, 0, 0);
         if (blk0 + r < n_blocks) v = __ldg(reinterpret_cast<const uint4 *>(pool + (size_t) (blk0 + r) * TC_K + 8 * c));
-        *reinterpret_cast<uint4 *>(sB + sw128_offset(TC_N, r, c)) = v;
+        *reinterpret_cast<uint4 *>(sB + sw128_off(TC_N, r, 8 * c)) = v;
     }
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // operands visible to the tensor core
+    fence_async_smem();                       // operands visible to the tensor core
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -107,14 +85,9 @@ __global__ void __launch_bounds__(TC_THREADS) idx_scores_tc_kernel(DevDesc d, co
             // k-step k: columns 16k .. 16k+15 = atom k/4, byte offset 32 (k%4) inside the swizzled rows
             const uint64_t da = umma_desc_sw128(base + (uint32_t) ((k >> 2) * TC_M * 128 + (k & 3) * 32));
             const uint64_t db = umma_desc_sw128(base + TC_A_BYTES + (uint32_t) ((k >> 2) * TC_N * 128 + (k & 3) * 32));
-            const uint32_t acc = k > 0 ? 1u : 0u;
-            asm volatile("{\n\t.reg .pred p;\n\t"
-                         "setp.ne.b32 p, %4, 0;\n\t"
-                         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}"
-                         :: "r"(tmem), "l"(da), "l"(db), "r"(TC_IDESC), "r"(acc), "r"(0u) : "memory");
+            umma_f16(tmem, da, db, TC_IDESC, k > 0);
         }
-        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
-                     :: "r"(smem_u32(&mma_bar)) : "memory");
+        umma_commit(&mma_bar);
     }
     const bool ok = mbar_wait_bounded(&mma_bar, 0, status);
     tc_fence_after();
@@ -127,16 +100,8 @@ __global__ void __launch_bounds__(TC_THREADS) idx_scores_tc_kernel(DevDesc d, co
     #pragma unroll 1
     for (int c0 = chalf * 128; c0 < chalf * 128 + 128; c0 += 32) {
         uint32_t v[32];
-        const uint32_t taddr = tmem + ((uint32_t) (sub * 32) << 16) + (uint32_t) c0;
-        asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-                     "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-                     "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-                     : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-                       "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
-                       "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
-                       "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
-                     : "r"(taddr));
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        tmem_ld32(tmem + ((uint32_t) (sub * 32) << 16) + (uint32_t) c0, v);
+        tmem_ld_wait();
         float s[32];
         #pragma unroll
         for (int j = 0; j < 32; j++) {
@@ -163,7 +128,7 @@ __global__ void __launch_bounds__(TC_THREADS) idx_scores_tc_kernel(DevDesc d, co
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(TC_N) : "memory");
+        tmem_dealloc_warp(tmem, TC_N);
     }
 }
 
