@@ -574,9 +574,9 @@ def run_ours_config5(args, ws, rank, local):
     torch.cuda.set_device(dev)
     NL, n_past = cfg.layers, cfg.n_past
     lb = args.layer_batch                      # the 12 independent layers as one batch of 12 items
-    dec = ShardedDecoder(d, rank=rank, world=ws, exchange=args.exchange, batch=NL if lb else 1)
+    dec = ShardedDecoder(d, rank=rank, world=ws, exchange=args.exchange, batch=NL if lb else 1, index=args.index)
     node = QsaNode(d, dev)
-    st = QsaState(d, n_layers=NL, device=dev, blocks=dec.blocks)
+    st = QsaState(d, n_layers=NL, device=dev, blocks=dec.blocks, index_full=dec.index_replicated)
     for il in range(NL):                       # every rank draws the same stream, keeps its cells
         fill_cache(node, st, il, n_past, cfg.seed * 1000 + il, append=dec.append)
     items = [decode_items([st.layer(il)], [n_past], device=dev) for il in range(NL)]
@@ -612,15 +612,21 @@ def run_ours_config5(args, ws, rank, local):
     with torch.cuda.graph(g, capture_error_mode="thread_local"):
         step()
     # the attention stage alone (the dominant kernel), on this rank's share: layer 0, or all 12
-    # layers in one launch with --layer-batch
+    # layers in one launch with --layer-batch (with replicated indexer caches: selection + attention)
     a_items, a_b = (items_all, NL) if lb else (items[0], 1)
-    cand = dec.backend.candidates(a_items, a_b, n_past + 1, dec.blocks, slots[1][:a_b])
-    gathered, cstride = dec._all_gather(cand, 0)
-    torch.cuda.synchronize()
-    g_attn = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g_attn):
-        dec.backend.attend(a_items, a_b, n_past + 1, dec.blocks, gathered, slots[0][:a_b], n_shards=dec.world,
-                           cand_stride=cstride)
+    if dec.index_replicated:
+        torch.cuda.synchronize()
+        g_attn = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_attn):
+            dec.backend.decode_ri(a_items, a_b, n_past + 1, dec.blocks, slots[0][:a_b], slots[1][:a_b])
+    else:
+        cand = dec.backend.candidates(a_items, a_b, n_past + 1, dec.blocks, slots[1][:a_b])
+        gathered, cstride = dec._all_gather(cand, 0)
+        torch.cuda.synchronize()
+        g_attn = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_attn):
+            dec.backend.attend(a_items, a_b, n_past + 1, dec.blocks, gathered, slots[0][:a_b], n_shards=dec.world,
+                               cand_stride=cstride)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
 
     def before(i):
@@ -667,7 +673,7 @@ def run_ours_config5(args, ws, rank, local):
     sel_h = sel.cpu().numpy()
     lo, hi = dec.blocks
     local_cells = sum(attended_cells([b for b in sel_h[il] if lo <= b < hi], n_past, d.ratio) for il in range(NL))
-    scored = max(0, min(hi, (n_past + 1) // d.ratio) - lo)
+    scored = (n_past + 1) // d.ratio if dec.index_replicated else max(0, min(hi, (n_past + 1) // d.ratio) - lo)
     sf = 16 * (2 + d.head_dim) * 4
     step_bytes = local_cells * 2 * 544 + NL * (scored * 256 + 2 * 544 + 256 + (ws + 1) * sf)
     attn_layers = range(NL) if lb else range(1)
@@ -691,6 +697,7 @@ def run_ours_config5(args, ws, rank, local):
                    "global_batch": 1, "seq_len": n_past + 1, "layers": NL,
                    "parallelism": (f"KV-sequence-sharded x{ws} ("
                                    + ("NVLink peer-memory all-gathers" if args.exchange == "peer" else "NCCL all-gathers")
+                                   + (", indexer caches replicated" if dec.index_replicated else "")
                                    + ")") if ws > 1 else "1 GPU",
                    "blocks_per_gpu": hi - lo,
                    "l2": "flushed (256 MB write) before every timed step", "cuda_graph": True},
@@ -889,6 +896,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layer-batch", action="store_true",
                     help="config 5: issue the 12 independent layers as one batch of 12 items (2 exchanges per token)")
+    ap.add_argument("--index", default="replicated", choices=["sharded", "replicated"],
+                    help="config 5: the indexer caches replicated on every rank (one state exchange per layer) or "
+                         "sharded with the K/V (candidates exchanged too)")
     ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
                     help="config 5 with N > 1: the shards' exchanges over NVLink peer memory or NCCL")
     args = ap.parse_args()

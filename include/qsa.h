@@ -208,6 +208,20 @@ qsa_status qsa_decode_noalloc(const qsa_desc * d, const qsa_decode_item * items,
  * Workspaces are sized by qsa_shard_workspace_size with the global max_n_kv and the shard's
  * block range (the attention's split over CTAs follows the shard's expected share of blocks). */
 size_t qsa_shard_state_floats(const qsa_desc * d);
+/* The same decode with the indexer caches replicated: every rank holds the raw keys and pooled keys
+ * of all blocks (global rows) and only the K/V rows of blocks [blk_lo, blk_hi) (row 0 = cell
+ * blk_lo * ratio).  Every rank then computes the identical global selection itself, so a step is
+ * qsa_shard_decode_ri (append, selection, attention over the shard's selected blocks into
+ * `state`), one all-gather of the states and qsa_merge_states: one exchange instead of two.
+ * Workspaces: qsa_shard_workspace_size.  qsa_shard_append_ri writes rows [pos0, pos0+n_tok): every
+ * raw key (and the pooled keys of the blocks they complete), the K/V rows inside the shard. */
+qsa_status qsa_shard_append_ri(const qsa_desc * d, const qsa_layer_cache * cache /* host struct */,
+                               int32_t blk_lo, int32_t blk_hi, int32_t pos0, int32_t n_tok,
+                               const float * k, const float * v, const float * kidx, qsa_stream_t stream);
+qsa_status qsa_shard_decode_ri(const qsa_desc * d, const qsa_decode_item * items, int32_t batch, int32_t max_n_kv,
+                               int32_t blk_lo, int32_t blk_hi, const void * q, int32_t q_type, const float * q_idx,
+                               const float * k_new, const float * v_new, const float * kidx_new, float * state,
+                               int32_t * sel_out, void * ws, size_t ws_bytes, qsa_stream_t stream);
 size_t qsa_shard_workspace_size(const qsa_desc * d, int32_t batch, int32_t max_n_kv, int32_t blk_lo, int32_t blk_hi);
 /* qsa_append into a shard's local arrays: global rows [pos0, pos0+n_tok), all inside the shard's
  * cells; pooled keys carry their global block positions. */

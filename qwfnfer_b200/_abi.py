@@ -119,6 +119,8 @@ def lib() -> ctypes.CDLL:
         "qsa_decode_noalloc": (I32, [D, VP, I32, I32, VP, I32, VP, VP, VP, VP, VP, VP, VP]),
         "qsa_shard_state_floats": (SZ, [D]),
         "qsa_shard_append": (I32, [D, C, I32, I32, I32, I32, VP, VP, VP, VP]),
+        "qsa_shard_append_ri": (I32, [D, C, I32, I32, I32, I32, VP, VP, VP, VP]),
+        "qsa_shard_decode_ri": (I32, [D, VP, I32, I32, I32, I32, VP, I32, VP, VP, VP, VP, VP, VP, VP, SZ, VP]),
         "qsa_shard_candidates": (I32, [D, VP, I32, I32, I32, I32, VP, VP, VP, VP, VP, VP, SZ, VP]),
         "qsa_shard_attend": (I32, [D, VP, I32, I32, I32, I32, I32, VP, I32, VP, I32, VP, VP, VP, SZ, VP]),
         "qsa_merge_states": (I32, [D, I32, I32, VP, VP, VP]),
@@ -151,6 +153,7 @@ HEADER_SYMBOLS = [
     "qsa_append", "qsa_pool_rebuild", "qsa_decode_workspace_size", "qsa_workspace_init",
     "qsa_decode", "qsa_decode_append", "qsa_decode_select", "qsa_decode_attend", "qsa_decode_noalloc",
     "qsa_shard_state_floats", "qsa_shard_workspace_size", "qsa_shard_append", "qsa_shard_candidates", "qsa_shard_attend",
+    "qsa_shard_append_ri", "qsa_shard_decode_ri",
     "qsa_merge_states",
     "qsa_ipc_handle", "qsa_ipc_open", "qsa_ipc_close", "qsa_peer_buffer_bytes", "qsa_peer_push", "qsa_peer_wait",
     "qsa_prefill_workspace_size", "qsa_prefill", "qsa_check", "qsa_version",

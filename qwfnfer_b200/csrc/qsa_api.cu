@@ -113,7 +113,8 @@ qsa_status launch_select(const DevDesc & d, const WsLayout & w, int n_q, const q
     uint32_t * status = reinterpret_cast<uint32_t *>(ws + w.status);
     // blocks per scoring CTA: 16 (one row pair per warp) while the grid is small, more once
     // there are enough CTAs to fill the GPU several times over
-    const int n_blk = std::max(1, std::min(w.scores_stride, d.shard_blk1) - d.shard_blk0);   // blocks scored
+    const int lo = d.shard_ri ? 0 : d.shard_blk0, hi = d.shard_ri ? INT_MAX : d.shard_blk1;
+    const int n_blk = std::max(1, std::min(w.scores_stride, hi) - lo);   // blocks scored
     int bpc = 2 * (SEL_THREADS_HOST / 32);                 // one row pair per warp
     while (bpc < 1024 && (int64_t) ceil_div(n_blk, 2 * bpc) * n_q >= 2 * 148) bpc *= 2;
     const int score_ctas = ceil_div(n_blk, bpc);
@@ -483,6 +484,42 @@ qsa_status qsa_shard_attend(const qsa_desc * dd, const qsa_decode_item * items, 
     if (e == cudaErrorInvalidValue) return QSA_ERR_UNSUPPORTED;       // too many candidates for one CTA
     if (e != cudaSuccess) return QSA_ERR_CUDA;
     qsa_layer_cache none{};
+    return launch_attend(d, w, batch, items, none, 0, q, q_type, nullptr, wsb, st, state);
+}
+
+// ---- KV-sharded decode with the indexer caches replicated on every rank
+qsa_status qsa_shard_append_ri(const qsa_desc * dd, const qsa_layer_cache * cache, int32_t blk_lo, int32_t blk_hi,
+                               int32_t pos0, int32_t n_tok, const float * k, const float * v, const float * kidx,
+                               qsa_stream_t stream) {
+    qsa_status s = qsa_desc_check(dd);
+    if (s != QSA_OK) return s;
+    if (!cache || blk_lo < 0 || blk_hi <= blk_lo || (int64_t) blk_hi * dd->ratio > dd->n_ctx) return QSA_ERR_INVALID;
+    if (pos0 < 0 || n_tok < 0 || (int64_t) pos0 + n_tok > dd->n_ctx) return QSA_ERR_INVALID;
+    DevDesc d = make_dev(dd);
+    d.shard_blk0 = blk_lo;
+    d.shard_blk1 = blk_hi;
+    d.shard_ri = 1;
+    return append_impl(d, cache, pos0, n_tok, k, v, kidx, stream);
+}
+
+qsa_status qsa_shard_decode_ri(const qsa_desc * dd, const qsa_decode_item * items, int32_t batch, int32_t max_n_kv,
+                               int32_t blk_lo, int32_t blk_hi, const void * q, int32_t q_type, const float * q_idx,
+                               const float * k_new, const float * v_new, const float * kidx_new, float * state,
+                               int32_t * sel_out, void * ws, size_t ws_bytes, qsa_stream_t stream) {
+    DevDesc d; WsLayout w;
+    qsa_status s = shard_common(dd, items, batch, max_n_kv, blk_lo, blk_hi, ws, ws_bytes, d, w);
+    if (s != QSA_OK) return s;
+    d.shard_ri = 1;
+    if (!q || !q_idx || !state || (q_type != QSA_TYPE_BF16 && q_type != QSA_TYPE_F32)) return QSA_ERR_INVALID;
+    const bool any_new = k_new || v_new || kidx_new;
+    if (any_new && !(k_new && v_new && kidx_new)) return QSA_ERR_INVALID;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    unsigned char * wsb = static_cast<unsigned char *>(ws);
+    if (any_new)           // every rank writes the raw and pooled keys, the owning shard the K/V row
+        append_decode_kernel<<<batch, APPEND_DECODE_THREADS, append_decode_smem(d), st>>>(d, items, k_new, v_new, kidx_new,
+                                                    reinterpret_cast<uint32_t *>(wsb + w.status));
+    qsa_layer_cache none{};
+    if ((s = launch_select(d, w, batch, items, none, 0, q_idx, sel_out, wsb, st)) != QSA_OK) return s;
     return launch_attend(d, w, batch, items, none, 0, q, q_type, nullptr, wsb, st, state);
 }
 

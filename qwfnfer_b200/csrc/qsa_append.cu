@@ -127,8 +127,10 @@ __global__ void __launch_bounds__(256) append_rows_kernel(DevDesc d, qsa_layer_c
     const int t = blockIdx.x, row = pos0 + t;
     c = shard_cache(d, c);
     const int kv_dim = d.n_head_kv * d.head_dim;
-    if (k) write_kv_row(d, d.type_k, k + (size_t) t * kv_dim, (uint8_t *) c.k + (size_t) row * d.rb_k, kv_dim);
-    if (v) write_kv_row(d, d.type_v, v + (size_t) t * kv_dim, (uint8_t *) c.v + (size_t) row * d.rb_v, kv_dim);
+    // replicated indexer caches: every row's raw key, only the shard's K/V rows
+    const bool kv_here = !d.shard_ri || (row / d.ratio >= d.shard_blk0 && row / d.ratio < d.shard_blk1);
+    if (k && kv_here) write_kv_row(d, d.type_k, k + (size_t) t * kv_dim, (uint8_t *) c.k + (size_t) row * d.rb_k, kv_dim);
+    if (v && kv_here) write_kv_row(d, d.type_v, v + (size_t) t * kv_dim, (uint8_t *) c.v + (size_t) row * d.rb_v, kv_dim);
     if (kidx)
         for (int i = threadIdx.x; i < d.idx_dim; i += blockDim.x)
             c.idx[(size_t) row * d.idx_dim + i] = f32_to_f16_bits(kidx[(size_t) t * d.idx_dim + i]);
@@ -141,7 +143,7 @@ __global__ void __launch_bounds__(256) pool_blocks_kernel(DevDesc d, const uint1
     const int j = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (j >= n_blk) return;
     const int64_t b = blk0 + j;
-    if (d.shard_blk0 != 0) {               // a shard's local arrays, indexed by global row / block
+    if (d.shard_blk0 != 0 && !d.shard_ri) {   // a shard's local arrays, indexed by global row / block
         idx = shard_row(idx, (int64_t) d.shard_blk0 * d.ratio, 0, (int64_t) MAX_IDX_DIM * 2);
         pool = shard_row(pool, (int64_t) d.shard_blk0, 0, (int64_t) d.idx_dim * 2);
     }
@@ -167,11 +169,14 @@ __global__ void __launch_bounds__(APPEND_THREADS) append_decode_kernel(DevDesc d
         if (threadIdx.x == 0) set_status(status, DEV_BAD_POS);
         return;
     }
-    if (row / d.ratio < d.shard_blk0 || row / d.ratio >= d.shard_blk1) return;   // another shard's cell
+    const bool kv_here = row / d.ratio >= d.shard_blk0 && row / d.ratio < d.shard_blk1;
+    if (!kv_here && !d.shard_ri) return;       // another shard's cell
     it.cache = shard_cache(d, it.cache);
     const int kv_dim = d.n_head_kv * d.head_dim;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nb = kv_dim / QK8_0;
-    if (d.type_k == QSA_TYPE_Q8_0 && 2 * nb <= (int) (blockDim.x >> 5)) {
+    if (!kv_here) {
+        // replicated indexer caches: the raw key and pooled key below, K/V on the owning shard
+    } else if (d.type_k == QSA_TYPE_Q8_0 && 2 * nb <= (int) (blockDim.x >> 5)) {
         // one q8_0 block per warp: K blocks on warps [0, nb), V blocks on warps [nb, 2 nb)
         if (warp < nb && k)
             quantize_q8_0_warp(k + (size_t) s * kv_dim + warp * QK8_0, (uint8_t *) it.cache.k + (size_t) row * d.rb_k + warp * Q8_0_BYTES, lane);

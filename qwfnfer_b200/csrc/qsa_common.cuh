@@ -37,6 +37,9 @@ struct DevDesc {
     // local arrays whose row 0 is cell shard_blk0 * ratio (pooled row 0 is block shard_blk0).
     // Unsharded: [0, INT_MAX).
     int shard_blk0, shard_blk1;
+    // Replicated indexer caches: with shard_ri set only K and V are local to the shard; the raw
+    // keys and pooled keys of every block are held (global rows) and every rank selects globally.
+    int shard_ri;
 };
 
 // Local address of global row `row` of a sharded cache array with `row_bytes` per row; rows
@@ -52,8 +55,10 @@ __device__ __forceinline__ qsa_layer_cache shard_cache(const DevDesc & d, qsa_la
         const int64_t row0 = (int64_t) d.shard_blk0 * d.ratio;
         c.k = shard_row(c.k, row0, 0, d.rb_k);
         c.v = shard_row(c.v, row0, 0, d.rb_v);
-        c.idx = shard_row(c.idx, row0, 0, (int64_t) d.idx_dim * 2);
-        c.pool = shard_row(c.pool, (int64_t) d.shard_blk0, 0, (int64_t) d.idx_dim * 2);
+        if (!d.shard_ri) {
+            c.idx = shard_row(c.idx, row0, 0, (int64_t) d.idx_dim * 2);
+            c.pool = shard_row(c.pool, (int64_t) d.shard_blk0, 0, (int64_t) d.idx_dim * 2);
+        }
     }
     return c;
 }

@@ -18,6 +18,7 @@
 namespace qsa {
 
 constexpr int SEL_THREADS = SEL_THREADS_HOST;
+static_assert(MAX_KB <= SEL_THREADS, "one kept block per selection thread");
 
 // Score blocks [b_begin, b_end) of one query: 16 lanes per block row (8 dims = 16 bytes each).
 // Products of two f16 values are exact in f32; they are summed in double (exact for these
@@ -263,6 +264,25 @@ compaction:
 
 // grid = (score CTAs per query, n_queries).  Query t: position q_pos(t), pooled cache `pool`.
 // Decode: items != null (per-query caches and n_past); prefill: one cache, q = n_past0 + t.
+// Replicated indexer caches: the global selection stays in sel_out; the attention's list keeps the
+// blocks of this shard's K/V rows, in order.
+__device__ void keep_shard_blocks(const DevDesc & d, int * __restrict__ list, int * __restrict__ nsel, SelSmem & sm) {
+    __syncthreads();                                 // the selection's stores are visible to the CTA
+    const int n = *nsel;
+    const int i = threadIdx.x;
+    const int b = i < n && i < d.kb ? list[i] : -1;
+    const bool keep = b >= d.shard_blk0 && b < d.shard_blk1;
+    int rank;
+    SelSmem::Scan(sm.scan).ExclusiveSum(keep ? 1 : 0, rank);
+    __syncthreads();                                 // every thread has read its entry
+    if (keep) list[rank] = b;
+    if (i == SEL_THREADS - 1) sm.bcast[0] = rank + (keep ? 1 : 0);
+    __syncthreads();
+    const int m = sm.bcast[0];
+    for (int j = m + i; j < d.kb; j += SEL_THREADS) list[j] = -1;
+    if (i == 0) *nsel = m;
+}
+
 __global__ void __launch_bounds__(SEL_THREADS) score_select_kernel(DevDesc d,
         const qsa_decode_item * __restrict__ items, const uint16_t * __restrict__ pool0, int n_past0,
         const float * __restrict__ q_idx, int blocks_per_cta,
@@ -276,7 +296,8 @@ __global__ void __launch_bounds__(SEL_THREADS) score_select_kernel(DevDesc d,
     const int t = blockIdx.y;
     const int q = items ? items[t].n_past : n_past0 + t;
     const uint16_t * pool = items ? items[t].cache.pool : pool0;
-    const int blo = d.shard_blk0, bhi = d.shard_blk1;          // [0, INT_MAX) unless sharded
+    // the blocks that compete: all ([0, INT_MAX)) unless the indexer caches are sharded too
+    const int blo = d.shard_ri ? 0 : d.shard_blk0, bhi = d.shard_ri ? INT_MAX : d.shard_blk1;
     if (blo != 0) pool = shard_row(pool, (int64_t) blo, 0, (int64_t) d.idx_dim * 2);   // address of block 0
     const bool bad = q < 0 || q >= d.n_ctx || (q + 1) / d.ratio > scores_stride;
     if (bad && threadIdx.x == 0 && blockIdx.x == 0) set_status(status, DEV_BAD_POS);
@@ -343,6 +364,7 @@ __global__ void __launch_bounds__(SEL_THREADS) score_select_kernel(DevDesc d,
     select_blocks(d, q, ssc, flag, sel_ws + (size_t) t * d.kb, nsel_ws + t,
                   sel_out ? sel_out + (size_t) t * d.kb : nullptr, sm, blo, bhi,
                   cand_scores ? cand_scores + (size_t) t * d.kb : nullptr);
+    if (d.shard_ri) keep_shard_blocks(d, sel_ws + (size_t) t * d.kb, nsel_ws + t, sm);
     if (defer_wait) pdl_wait();                  // the append is complete before this grid is
 }
 

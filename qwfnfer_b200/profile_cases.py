@@ -3,14 +3,15 @@
     python -m qwfnfer_b200.profile_cases batch B STEPS    # B decode queries over one config-2 cache
     python -m qwfnfer_b200.profile_cases decode STEPS     # the config-2 decode step (append + select + attend)
     python -m qwfnfer_b200.profile_cases prefill T N_PAST STEPS   # one qsa_prefill chunk (config-4 shape)
-    python -m torch.distributed.run --nproc-per-node N ... -m qwfnfer_b200.profile_cases shard5 peer|nccl [lb]
+    python -m torch.distributed.run --nproc-per-node N ... -m qwfnfer_b200.profile_cases shard5 peer|nccl [lb] [ri]
                                                           # config-5 sharded step: per-kernel timeline per rank
 
 `batch` places the B queries at positions 163839 - 64 i of one 160K q8_0 cache (no append), so the attention runs in its
 multi-tile streaming regime with 220 MB of caches on the device; `decode` is one token of config 2.  `prefill` appends
 T tokens at N_PAST of a q8_0 cache and runs the whole chunk (T=4096 at 77824 keeps config 4's ~210 queries per block
 with about 2.5 GB on the device).  Each step is preceded by a 256 MB L2 flush; the device time of every step is printed.
-`shard5` replays the config-5 sharded decode step (one layer after another, or with `lb` the 12 layers as one batch)
+`shard5` replays the config-5 sharded decode step (one layer after another, or with `lb` the 12 layers as one batch;
+`ri`: indexer caches replicated)
 from a CUDA graph under torch.profiler and prints, per rank, each kernel's median start offset and duration within
 the step (CUPTI activity records; a breakdown, not a bench value).
 """
@@ -107,9 +108,10 @@ def shard5(argv: list[str]) -> None:
     cfg = CONFIGS[5]
     d = cfg.desc()
     NL, n_past = cfg.layers, cfg.n_past
-    dec = ShardedDecoder(d, rank=rank, world=ws, exchange=exchange, batch=NL if lb else 1)
+    index = "replicated" if "ri" in argv else "sharded"
+    dec = ShardedDecoder(d, rank=rank, world=ws, exchange=exchange, batch=NL if lb else 1, index=index)
     node = QsaNode(d, dev)
-    st = QsaState(d, n_layers=NL, device=dev, blocks=dec.blocks)
+    st = QsaState(d, n_layers=NL, device=dev, blocks=dec.blocks, index_full=dec.index_replicated)
     for il in range(NL):
         fill_cache(node, st, il, n_past, cfg.seed * 1000 + il, append=dec.append)
     items = [decode_items([st.layer(il)], [n_past], device=dev) for il in range(NL)]

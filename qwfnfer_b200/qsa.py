@@ -35,20 +35,23 @@ def _stream(stream: torch.cuda.Stream | None) -> int:
 class QsaState:
     """Per-sequence caches of `n_layers` QSA layers, reference layouts (include/qsa.h).
 
-    blocks=(lo, hi): a shard's caches, holding blocks [lo, hi) only (row 0 = cell lo*ratio)."""
+    blocks=(lo, hi): a shard's caches, holding blocks [lo, hi) only (row 0 = cell lo*ratio);
+    with index_full the raw-key and pooled-key caches still cover every block (the sharded decode
+    with replicated indexer caches)."""
 
     def __init__(self, desc: QsaDesc, n_layers: int = 1, device: str | torch.device = "cuda", zero: bool = False,
-                 blocks: tuple[int, int] | None = None):
+                 blocks: tuple[int, int] | None = None, index_full: bool = False):
         check(lib().qsa_desc_check(ctypes.byref(desc)), "qsa_desc_check")
         self.desc = desc
         self.device = torch.device(device)
         self.blocks = blocks if blocks is not None else (0, desc.n_ctx // desc.ratio)
         n = (self.blocks[1] - self.blocks[0]) * desc.ratio
+        ni = desc.n_ctx if index_full else n
         alloc = torch.zeros if zero else torch.empty
         self.k = [alloc((n, row_bytes(desc, 0)), dtype=torch.uint8, device=self.device) for _ in range(n_layers)]
         self.v = [alloc((n, row_bytes(desc, 1)), dtype=torch.uint8, device=self.device) for _ in range(n_layers)]
-        self.idx = [alloc((n, desc.idx_dim), dtype=torch.int16, device=self.device) for _ in range(n_layers)]
-        self.pool = [torch.zeros((n // desc.ratio, desc.idx_dim), dtype=torch.int16, device=self.device)
+        self.idx = [alloc((ni, desc.idx_dim), dtype=torch.int16, device=self.device) for _ in range(n_layers)]
+        self.pool = [torch.zeros((ni // desc.ratio, desc.idx_dim), dtype=torch.int16, device=self.device)
                      for _ in range(n_layers)]
 
     def layer(self, il: int = 0) -> QsaLayerCache:

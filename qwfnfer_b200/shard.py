@@ -82,6 +82,26 @@ class LibShardBackend:
         check(lib().qsa_shard_append(ctypes.byref(self.desc), ctypes.byref(cache), blocks[0], blocks[1], pos0, n,
                                      _ptr(k), _ptr(v), _ptr(kidx), self._stream()), "qsa_shard_append")
 
+    def append_ri(self, cache: QsaLayerCache, blocks: tuple[int, int], pos0: int, k, v, kidx) -> None:
+        """Replicated indexer caches: every row's raw key (and pooled keys), the shard's K/V rows."""
+        n = (k if k is not None else kidx).shape[0]
+        check(lib().qsa_shard_append_ri(ctypes.byref(self.desc), ctypes.byref(cache), blocks[0], blocks[1], pos0, n,
+                                        _ptr(k), _ptr(v), _ptr(kidx), self._stream()), "qsa_shard_append_ri")
+
+    def decode_ri(self, items, batch: int, max_n_kv: int, blocks: tuple[int, int], q, q_idx, k_new=None, v_new=None,
+                  kidx_new=None, sel_out: torch.Tensor | None = None, state: torch.Tensor | None = None) -> torch.Tensor:
+        """Replicated indexer caches: append, the global selection and the attention over this
+        shard's selected blocks, into an unnormalised state f32 [batch, state_floats]."""
+        if state is None:
+            state = torch.empty((batch, self.state_floats), dtype=torch.float32, device=self.device)
+        q_type = TYPE_BF16 if q.dtype == torch.bfloat16 else TYPE_F32
+        ws = self.workspace(batch, max_n_kv, blocks)
+        check(lib().qsa_shard_decode_ri(ctypes.byref(self.desc), _ptr(items), batch, max_n_kv, blocks[0], blocks[1],
+                                        _ptr(q), q_type, _ptr(q_idx), _ptr(k_new), _ptr(v_new), _ptr(kidx_new),
+                                        state.data_ptr(), _ptr(sel_out), ws.data_ptr(), ws.numel(), self._stream()),
+              "qsa_shard_decode_ri")
+        return state
+
     def candidates(self, items, batch: int, max_n_kv: int, blocks: tuple[int, int], q_idx,
                    k_new=None, v_new=None, kidx_new=None, out: torch.Tensor | None = None) -> torch.Tensor:
         """This rank's candidates, int32 [2, batch, KB]: block ids (-1 padded), then score bits."""
@@ -204,9 +224,15 @@ class ShardedDecoder:
     torch.distributed process group (default: the world); world size 1 runs without collectives."""
 
     def __init__(self, desc: QsaDesc, backend=None, group=None, rank: int | None = None,
-                 world: int | None = None, exchange: str = "nccl", batch: int = 1):
+                 world: int | None = None, exchange: str = "nccl", batch: int = 1, index: str = "sharded"):
         """exchange: "nccl" (all-gathers of the process group) or "peer" (libqsa's all-gather over
-        NVLink peer memory, GPUs of one node; sized for `batch` queries per step)."""
+        NVLink peer memory, GPUs of one node; sized for `batch` queries per step).  index: "sharded"
+        (each rank holds its blocks' raw and pooled keys; candidates are exchanged) or "replicated"
+        (every rank holds all of them, QsaState(index_full=True), and selects globally itself: one
+        exchange per step)."""
+        if index not in ("sharded", "replicated"):
+            raise ValueError("index is 'sharded' or 'replicated'")
+        self.index_replicated = index == "replicated"
         self.desc = desc
         self.group = group
         dist_on = dist.is_available() and dist.is_initialized()
@@ -234,7 +260,11 @@ class ShardedDecoder:
         return out.view((self.world,) + tuple(t.shape)), t.numel()
 
     def append(self, cache: QsaLayerCache, pos0: int, k, v, kidx) -> None:
-        """Append global rows [pos0, pos0+n): the rows inside this rank's cells are written."""
+        """Append global rows [pos0, pos0+n): the rows inside this rank's cells are written (with
+        replicated indexer caches: every row's raw key, the K/V rows inside this rank's cells)."""
+        if self.index_replicated:
+            self.backend.append_ri(cache, self.blocks, pos0, k, v, kidx)
+            return
         n = (k if k is not None else kidx).shape[0]
         r = self.desc.ratio
         lo, hi = max(pos0, self.blocks[0] * r), min(pos0 + n, self.blocks[1] * r)
@@ -248,6 +278,11 @@ class ShardedDecoder:
              sel_out: torch.Tensor | None = None) -> torch.Tensor:
         """One decode step of one layer for `batch` queries (items: this rank's device item table,
         global n_past, local caches).  Returns f32 [batch, n_head, head_dim] on every rank."""
+        if self.index_replicated:
+            state = self.backend.decode_ri(items, batch, max_n_kv, self.blocks, q, q_idx, k_new, v_new, kidx_new,
+                                           sel_out=sel_out)
+            states, _ = self._all_gather(state, 1)
+            return self.backend.merge(states.view(self.world, batch, -1))
         cand = self.backend.candidates(items, batch, max_n_kv, self.blocks, q_idx, k_new, v_new, kidx_new)
         gathered, cstride = self._all_gather(cand, 0)
         state = self.backend.attend(items, batch, max_n_kv, self.blocks, gathered, q, sel_out=sel_out,

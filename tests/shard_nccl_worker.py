@@ -1,9 +1,10 @@
 """One rank of the sharded decode over NCCL (launched by tests/test_zz_shard_nccl.py):
 
     python -m torch.distributed.run --nnodes 1 --nproc-per-node N --master-addr 127.0.0.1 \
-        --master-port P tests/shard_nccl_worker.py [nccl|peer]
+        --master-port P tests/shard_nccl_worker.py [nccl|peer] [sharded|replicated]
 
-The exchange is NCCL's all-gather or libqsa's all-gather over NVLink peer memory.
+The exchange is NCCL's all-gather or libqsa's all-gather over NVLink peer memory; the indexer
+caches are sharded with the K/V (candidates exchanged) or replicated on every rank.
 
 Every rank fills its shard of two sequences' caches, runs one ShardedDecoder step (append of the
 new token, the two all-gathers, the merge), and checks its status.  Rank 0 also builds the
@@ -42,9 +43,10 @@ def main() -> int:
     positions = [60031, 20000]                   # 60032 = 938 * 64: the token completes block 937
     seeds = [41, 42]
     exchange = sys.argv[1] if len(sys.argv) > 1 else "nccl"
-    dec = ShardedDecoder(d, exchange=exchange, batch=2)
+    index = sys.argv[2] if len(sys.argv) > 2 else "sharded"
+    dec = ShardedDecoder(d, exchange=exchange, batch=2, index=index)
     node = QsaNode(d)
-    sts = [QsaState(d, blocks=dec.blocks) for _ in positions]
+    sts = [QsaState(d, blocks=dec.blocks, index_full=dec.index_replicated) for _ in positions]
     for st, n, s in zip(sts, positions, seeds):
         fill_cache(node, st, 0, n, s, append=dec.append)
     q, q_idx, k, v, ki = token_inputs(d, 2, seed=43)
@@ -77,7 +79,8 @@ def main() -> int:
         same = all(torch.equal(o, outs[0]) for o in outs)
         statuses = [int(s.item()) for s in stats]
         ok = all(sel_ok) and max(errs) <= ATTN_TOL and same and all(s == QSA_OK for s in statuses)
-        print("SHARD_NCCL " + json.dumps({"world": world, "exchange": exchange, "blocks": dec.blocks, "rel_err": errs, "sel_equal": sel_ok,
+        print("SHARD_NCCL " + json.dumps({"world": world, "exchange": exchange, "index": index, "blocks": dec.blocks,
+                                          "rel_err": errs, "sel_equal": sel_ok,
                                           "ranks_identical": same, "status": statuses, "ok": ok}), flush=True)
     flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=dev)
     dist.broadcast(flag, 0)

@@ -138,3 +138,51 @@ def test_shard_select_equal_keys_by_lower_block(case):
         dec.backend.attend(it, 1, pos + 1, dec.blocks, gathered, q, sel_out=sel)
         assert dec.backend.check(1, pos + 1) == QSA_OK
         assert sel.cpu().numpy()[0].tolist() == expect
+
+
+@pytest.mark.parametrize("world,type_", [(2, TYPE_Q8_0), (3, TYPE_F16)])
+def test_sharded_decode_replicated_index_equals_unsharded(world, type_):
+    """Replicated indexer caches: every emulated rank holds all raw and pooled keys (byte-equal to
+    the unsharded caches) and its shard's K/V rows; each selects globally (the unsharded
+    selection, exactly), attends its own blocks, and the merged states equal qsa_decode's output."""
+    d = make_desc(n_ctx=32768, top_k_blocks=64, window=128, type_k=type_, type_v=type_)
+    positions = [30015, 9000]
+    node = QsaNode(d)
+    full = [QsaState(d) for _ in positions]
+    for st, n, s in zip(full, positions, [21, 22]):
+        fill_cache(node, st, 0, n, s)
+    ranks = []
+    for r in range(world):
+        dec = ShardedDecoder(d, backend=LibShardBackend(d), rank=r, world=world, index="replicated")
+        sts = [QsaState(d, blocks=dec.blocks, index_full=True) for _ in positions]
+        for st, n, s in zip(sts, positions, [21, 22]):
+            fill_cache(node, st, 0, n, s, append=dec.append)
+        ranks.append((dec, sts))
+    q, q_idx, k, v, ki = token_inputs(d, 2, seed=23, q_dtype=torch.float32 if type_ == TYPE_F16 else torch.bfloat16)
+    max_n_kv = max(positions) + 1
+    sel_ref = torch.empty((2, k_blocks(d)), dtype=torch.int32, device="cuda")
+    out_ref = node.sparse_attn_decode(decode_items([s.layer() for s in full], positions), 2, max_n_kv, q, q_idx,
+                                      k, v, ki, sel_out=sel_ref)
+    states, sels = [], []
+    for dec, sts in ranks:
+        sel = torch.empty((2, k_blocks(d)), dtype=torch.int32, device="cuda")
+        states.append(dec.backend.decode_ri(decode_items([s.layer() for s in sts], positions), 2, max_n_kv,
+                                            dec.blocks, q, q_idx, k, v, ki, sel_out=sel))
+        sels.append(sel)
+    out = ranks[0][0].backend.merge(torch.stack(states))
+    torch.cuda.synchronize()
+    for dec, _ in ranks:
+        assert dec.backend.check(2, max_n_kv) == QSA_OK
+    for s in sels:
+        assert torch.equal(s, sel_ref)
+    assert rel_err(out.cpu().numpy(), out_ref.cpu().numpy()) <= ATTN_TOL
+    r = d.ratio
+    for dec, sts in ranks:                             # caches after the step's append
+        lo, hi = dec.blocks
+        for f, s, n in zip(full, sts, [p + 1 for p in positions]):
+            assert torch.equal(f.idx[0][:n], s.idx[0][:n])
+            assert torch.equal(f.pool[0][:n // r], s.pool[0][:n // r])
+            c0, c1 = lo * r, min(hi * r, n)
+            if c1 > c0:
+                assert torch.equal(f.k[0][c0:c1], s.k[0][:c1 - c0])
+                assert torch.equal(f.v[0][c0:c1], s.v[0][:c1 - c0])

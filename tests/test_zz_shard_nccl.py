@@ -1,5 +1,6 @@
 """The sharded decode over real ranks: one process per GPU, exchanges by NCCL all-gathers or by
-libqsa's all-gather over NVLink peer memory (2 GPUs or more).
+libqsa's all-gather over NVLink peer memory, the indexer caches sharded or replicated (2 GPUs or
+more).
 
 Runs tests/shard_nccl_worker.py under torch.distributed.run on min(4, visible GPUs) ranks and
 requires its SHARD_NCCL line to report ok (selections identical to the unsharded qsa_decode on
@@ -28,12 +29,12 @@ def _free_port():
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("exchange", ["nccl", "peer"])
-def test_sharded_decode_over_ranks(exchange):
+@pytest.mark.parametrize("exchange,index", [("nccl", "sharded"), ("peer", "sharded"), ("peer", "replicated")])
+def test_sharded_decode_over_ranks(exchange, index):
     n = min(4, torch.cuda.device_count())
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes", "1",
            "--nproc-per-node", str(n), "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
-           os.path.join(TESTS, "shard_nccl_worker.py"), exchange]
+           os.path.join(TESTS, "shard_nccl_worker.py"), exchange, index]
     r = subprocess.run(cmd, capture_output=True, text=True, env=dict(os.environ, NCCL_NVLS_ENABLE="0"))
     lines = [l for l in r.stdout.splitlines() if l.startswith("SHARD_NCCL ")]
     assert r.returncode == 0 and lines, r.stdout[-3000:] + r.stderr[-3000:]
