@@ -111,12 +111,12 @@ qsa_status launch_select(const DevDesc & d, const WsLayout & w, int n_q, const q
                          qsa_layer_cache cache0, int n_past0, const float * q_idx, int32_t * sel_out,
                          unsigned char * ws, cudaStream_t st, float * cand_scores = nullptr) {
     uint32_t * status = reinterpret_cast<uint32_t *>(ws + w.status);
-    // blocks per scoring CTA: 16 (one row pair per warp) while the grid is small, more once
-    // there are enough CTAs to fill the GPU several times over
+    // blocks per scoring CTA: one row pair per warp while the grid fits one wave, more once it
+    // would not (a 1024-thread CTA holds a whole SM's registers: one wave is 148 CTAs)
     const int lo = d.shard_ri ? 0 : d.shard_blk0, hi = d.shard_ri ? INT_MAX : d.shard_blk1;
     const int n_blk = std::max(1, std::min(w.scores_stride, hi) - lo);   // blocks scored
     int bpc = 2 * (SEL_THREADS_HOST / 32);                 // one row pair per warp
-    while (bpc < 1024 && (int64_t) ceil_div(n_blk, 2 * bpc) * n_q >= 2 * 148) bpc *= 2;
+    while (bpc < 1024 && (int64_t) ceil_div(n_blk, bpc) * n_q > 148) bpc *= 2;
     const int score_ctas = ceil_div(n_blk, bpc);
     const size_t sel_smem = (size_t) w.scores_stride * 5;       // scores + selection flags
     if (sel_smem > 160 * 1024) return QSA_ERR_UNSUPPORTED;

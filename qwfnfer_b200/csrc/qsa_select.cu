@@ -103,31 +103,61 @@ __device__ void select_blocks(const DevDesc & d, int q, const float * __restrict
         remaining = want;
         // Zero scores (relu cut every head) can only fill what the positive ones leave: count the
         // positive candidates; when they are too few the cut is at 0 and zeros go by lowest index.
+        // The same pass finds the smallest and largest positive key: the bits they share are shared
+        // by every positive key, so the histogram levels start at the highest differing bit.
         int n_pos = 0;
+        uint32_t kmin = 0xffffffffu, kmax = 0u;
         for (int b0 = 0; b0 < n_vis; b0 += blockDim.x) {
             const int b = b0 + tid;
-            const bool pos = is_cand(b) && __float_as_uint(sc[b]) != 0u;
+            const uint32_t key = b < n_vis ? __float_as_uint(sc[b]) : 0u;
+            const bool pos = is_cand(b) && key != 0u;
+            if (pos) { kmin = min(kmin, key); kmax = max(kmax, key); }
             const unsigned bal = __ballot_sync(0xffffffffu, pos);
             if ((tid & 31) == 0) n_pos += __popc(bal);
         }
-        if ((tid & 31) == 0) sm.hist[tid >> 5] = (unsigned) n_pos;
+        #pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            kmin = min(kmin, __shfl_xor_sync(0xffffffffu, kmin, o));
+            kmax = max(kmax, __shfl_xor_sync(0xffffffffu, kmax, o));
+        }
+        const int nwarps = (int) (blockDim.x >> 5);
+        if ((tid & 31) == 0) {
+            sm.hist[tid >> 5] = (unsigned) n_pos;
+            sm.hist[nwarps + (tid >> 5)] = kmin;
+            sm.hist[2 * nwarps + (tid >> 5)] = kmax;
+        }
         __syncthreads();
         if (tid == 0) {
             int tot = 0;
-            for (int w = 0; w < (int) (blockDim.x >> 5); w++) tot += (int) sm.hist[w];
+            uint32_t mn = 0xffffffffu, mx = 0u;
+            for (int w = 0; w < nwarps; w++) {
+                tot += (int) sm.hist[w];
+                mn = min(mn, sm.hist[nwarps + w]);
+                mx = max(mx, sm.hist[2 * nwarps + w]);
+            }
             sm.bcast[3] = tot;
+            sm.bcast[0] = (int) mn;
+            sm.bcast[1] = (int) mx;
         }
         __syncthreads();
         n_pos = sm.bcast[3];
+        kmin = (uint32_t) sm.bcast[0];
+        kmax = (uint32_t) sm.bcast[1];
         __syncthreads();
         if (n_pos < remaining) {               // cut at zero: every positive key is kept
             prefix = 0; pmask = 0xffffffffu; remaining -= n_pos;
             goto compaction;
         }
-        const int shifts[3] = {19, 7, 0};
-        const int widths[3] = {12, 12, 7};
-        for (int lv = 0; lv < 3; lv++) {
-            const int shift = shifts[lv], nb = 1 << widths[lv];
+        if (kmin == kmax) {                    // every positive key equal: the first `remaining` by index
+            prefix = kmax; pmask = 0xffffffffu;
+            goto compaction;
+        }
+        int hb = 31 - __clz(kmin ^ kmax);      // bits above hb are common to every positive key
+        pmask = ~((2u << hb) - 1u);
+        prefix = kmax & pmask;
+        while (hb >= 0) {
+            const int width = min(12, hb + 1), shift = hb + 1 - width, nb = 1 << width;
+            hb = shift - 1;
             const uint32_t bmask = (uint32_t) (nb - 1);
             for (int i = tid; i < nb; i += blockDim.x) sm.hist[i] = 0;
             __syncthreads();
