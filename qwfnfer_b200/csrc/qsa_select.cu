@@ -81,9 +81,12 @@ struct SelSmem {
 // they are ranked directly (score, then lower block index).  Keys above the bin are kept.
 // Sharded mode (cand_scores != null): only blocks in [blo, bhi) compete, forced blocks are left
 // to the global merge, and each kept block's score is written beside it.
+// pre != null: the caller's load of the scores already cleared the candidates' flags and left in
+// pre[0..2] this thread's count, smallest and largest positive candidate key.
 __device__ void select_blocks(const DevDesc & d, int q, const float * __restrict__ sc, unsigned char * __restrict__ flag,
                               int * __restrict__ sel, int * __restrict__ nsel_out, int * __restrict__ sel_out,
-                              SelSmem & sm, int blo, int bhi, float * __restrict__ cand_scores) {
+                              SelSmem & sm, int blo, int bhi, float * __restrict__ cand_scores,
+                              const uint32_t * pre = nullptr) {
     const bool shard = cand_scores != nullptr;
     const int tid = threadIdx.x;
     const int n_vis = (q + 1) / d.ratio;
@@ -98,7 +101,8 @@ __device__ void select_blocks(const DevDesc & d, int q, const float * __restrict
     uint32_t prefix = 0, pmask = 0;   // keys with (key & pmask) > prefix are kept
     int remaining = 0;                // keys with (key & pmask) == prefix to keep
     bool ranked = false;              // the bin's keys were ranked into flag[]
-    for (int b = tid; b < n_vis; b += blockDim.x) flag[b] = 0;
+    if (!pre)
+        for (int b = tid; b < n_vis; b += blockDim.x) flag[b] = 0;
     if (!take_all) {
         remaining = want;
         // Zero scores (relu cut every head) can only fill what the positive ones leave: count the
@@ -107,16 +111,17 @@ __device__ void select_blocks(const DevDesc & d, int q, const float * __restrict
         // by every positive key, so the histogram levels start at the highest differing bit.
         int n_pos = 0;
         uint32_t kmin = 0xffffffffu, kmax = 0u;
-        for (int b0 = 0; b0 < n_vis; b0 += blockDim.x) {
-            const int b = b0 + tid;
-            const uint32_t key = b < n_vis ? __float_as_uint(sc[b]) : 0u;
-            const bool pos = is_cand(b) && key != 0u;
-            if (pos) { kmin = min(kmin, key); kmax = max(kmax, key); }
-            const unsigned bal = __ballot_sync(0xffffffffu, pos);
-            if ((tid & 31) == 0) n_pos += __popc(bal);
+        if (pre) {
+            n_pos = (int) pre[0]; kmin = pre[1]; kmax = pre[2];
+        } else {
+            for (int b = tid; b < n_vis; b += blockDim.x) {
+                const uint32_t key = __float_as_uint(sc[b]);
+                if (is_cand(b) && key != 0u) { n_pos++; kmin = min(kmin, key); kmax = max(kmax, key); }
+            }
         }
         #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
+            n_pos += __shfl_xor_sync(0xffffffffu, n_pos, o);
             kmin = min(kmin, __shfl_xor_sync(0xffffffffu, kmin, o));
             kmax = max(kmax, __shfl_xor_sync(0xffffffffu, kmax, o));
         }
@@ -374,11 +379,31 @@ __global__ void __launch_bounds__(SEL_THREADS) score_select_kernel(DevDesc d,
     }
     float * ssc = reinterpret_cast<float *>(dyn_smem);
     unsigned char * flag = dyn_smem + (size_t) scores_stride * 4;
-    {   // the query's scores in [blo, n_vis), 16 bytes per load (score rows are 16-byte aligned)
+    uint32_t pre[3] = {0u, 0xffffffffu, 0u};       // this thread's count, min and max positive candidate key
+    {   // the query's scores in [blo, n_vis), 16 bytes per load (score rows are 16-byte aligned); the
+        // same loop clears the candidates' selection flags and gathers what the selection's first
+        // pass needs
+        int f_lo, f_hi;
+        forced_range(d, q, f_lo, f_hi);
+        const int lo_c = max(blo, 0), hi_c = min(bhi, n_vis);
         const int i0 = max(blo, 0) / 4, n4 = (min(n_vis, bhi) + 3) / 4;
         #pragma unroll 4
-        for (int i = i0 + threadIdx.x; i < n4; i += blockDim.x)
-            reinterpret_cast<float4 *>(ssc)[i] = __ldcg(reinterpret_cast<const float4 *>(sc) + i);
+        for (int i = i0 + threadIdx.x; i < n4; i += blockDim.x) {
+            const float4 v = __ldcg(reinterpret_cast<const float4 *>(sc) + i);
+            reinterpret_cast<float4 *>(ssc)[i] = v;
+            reinterpret_cast<uint32_t *>(flag)[i] = 0u;
+            const float e[4] = {v.x, v.y, v.z, v.w};
+            #pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const int b = 4 * i + k;
+                const uint32_t key = __float_as_uint(e[k]);
+                if (b >= lo_c && b < hi_c && !(b >= f_lo && b <= f_hi) && key != 0u) {
+                    pre[0]++;
+                    pre[1] = min(pre[1], key);
+                    pre[2] = max(pre[2], key);
+                }
+            }
+        }
     }
     __syncthreads();
     if (bad) {
@@ -393,7 +418,7 @@ __global__ void __launch_bounds__(SEL_THREADS) score_select_kernel(DevDesc d,
     }
     select_blocks(d, q, ssc, flag, sel_ws + (size_t) t * d.kb, nsel_ws + t,
                   sel_out ? sel_out + (size_t) t * d.kb : nullptr, sm, blo, bhi,
-                  cand_scores ? cand_scores + (size_t) t * d.kb : nullptr);
+                  cand_scores ? cand_scores + (size_t) t * d.kb : nullptr, pre);
     if (d.shard_ri) keep_shard_blocks(d, sel_ws + (size_t) t * d.kb, nsel_ws + t, sm);
     if (defer_wait) pdl_wait();                  // the append is complete before this grid is
 }
