@@ -71,6 +71,7 @@ struct SelSmem {
     unsigned hist[HBINS];
     int cand[CAND_MAX];
     int ncand;
+    int nkept;
     int bcast[4];
 };
 
@@ -81,6 +82,42 @@ struct SelSmem {
 // they are ranked directly (score, then lower block index).  Keys above the bin are kept.
 // Sharded mode (cand_scores != null): only blocks in [blo, bhi) compete, forced blocks are left
 // to the global merge, and each kept block's score is written beside it.
+// The kept candidates kept[0..nk) (any order) written in ascending block order, then (unless
+// sharded) the forced blocks f_lo.. (above every candidate); the list is padded as the
+// compaction pads it.
+__device__ void emit_kept(const DevDesc & d, const int * kept, int nk, int f_lo, int n_forced,
+                          const float * __restrict__ sc, int * __restrict__ sel, int * __restrict__ nsel_out,
+                          int * __restrict__ sel_out, bool shard, float * __restrict__ cand_scores) {
+    const int tid = threadIdx.x;
+    for (int i = tid; i < nk; i += blockDim.x) {
+        const int bi = kept[i];
+        int pos = 0;
+        for (int j = 0; j < nk; j++) pos += kept[j] < bi;
+        if (pos < d.kb) {
+            sel[pos] = bi;
+            if (sel_out) sel_out[pos] = bi;
+            if (shard) cand_scores[pos] = sc[bi];
+        }
+    }
+    int total = nk;
+    if (!shard) {
+        for (int i = tid; i < n_forced; i += blockDim.x) {
+            const int pos = nk + i;
+            if (pos < d.kb) {
+                sel[pos] = f_lo + i;
+                if (sel_out) sel_out[pos] = f_lo + i;
+            }
+        }
+        total += n_forced;
+    }
+    const int n = min(total, d.kb);
+    for (int i = n + tid; i < d.kb; i += blockDim.x) {
+        if (sel_out) sel_out[i] = -1;
+        if (shard) { sel[i] = -1; cand_scores[i] = 0.0f; }
+    }
+    if (tid == 0) *nsel_out = n;
+}
+
 // pre != null: the caller's load of the scores already cleared the candidates' flags and left in
 // pre[0..2] this thread's count, smallest and largest positive candidate key.
 __device__ void select_blocks(const DevDesc & d, int q, const float * __restrict__ sc, unsigned char * __restrict__ flag,
@@ -200,12 +237,21 @@ __device__ void select_blocks(const DevDesc & d, int q, const float * __restrict
             const int in_bin = sm.bcast[2];
             __syncthreads();
             if (in_bin <= CAND_MAX) {
-                // rank the bin's keys directly
-                if (tid == 0) sm.ncand = 0;
+                // One pass collects the keys above the cut bin (kept) and the bin's keys, which are
+                // ranked directly (score, then lower block); the kept list (at most kb) is then put
+                // in block order without another pass over the scores.
+                int * kept = reinterpret_cast<int *>(sm.hist);
+                if (tid == 0) { sm.ncand = 0; sm.nkept = 0; }
                 __syncthreads();
                 for (int b = tid; b < n_vis; b += blockDim.x) {
                     if (!is_cand(b)) continue;
-                    if ((__float_as_uint(sc[b]) & pmask) == prefix) {
+                    const uint32_t key = __float_as_uint(sc[b]);
+                    if (key == 0u) continue;
+                    const uint32_t km = key & pmask;
+                    if (km > prefix) {
+                        const int slot = atomicAdd(&sm.nkept, 1);
+                        if (slot < MAX_KB) kept[slot] = b;
+                    } else if (km == prefix) {
                         const int slot = atomicAdd(&sm.ncand, 1);
                         if (slot < CAND_MAX) sm.cand[slot] = b;
                     }
@@ -221,10 +267,14 @@ __device__ void select_blocks(const DevDesc & d, int q, const float * __restrict
                         const uint32_t kj = __float_as_uint(sc[bj]);
                         rank += (kj > ki) || (kj == ki && bj < bi);
                     }
-                    if (rank < remaining) flag[bi] = 1;
+                    if (rank < remaining) {
+                        const int slot = atomicAdd(&sm.nkept, 1);
+                        if (slot < MAX_KB) kept[slot] = bi;
+                    }
                 }
-                ranked = true;
-                break;
+                __syncthreads();
+                emit_kept(d, kept, min(sm.nkept, MAX_KB), f_lo, n_forced, sc, sel, nsel_out, sel_out, shard, cand_scores);
+                return;
             }
         }
         __syncthreads();
