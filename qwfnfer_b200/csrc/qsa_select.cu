@@ -134,6 +134,8 @@ __device__ void select_blocks(const DevDesc & d, int q, const float * __restrict
     const int lo_c = max(blo, 0), hi_c = min(bhi, n_vis);          // candidate range
     const int n_cand = max(0, hi_c - lo_c) - max(0, min(f_hi, hi_c - 1) - max(f_lo, lo_c) + 1);
     auto is_cand = [&](int b) { return b >= lo_c && b < hi_c && !(b >= f_lo && b <= f_hi); };
+    // The forced blocks are the top of the visible range, so the candidates are one run [lo_c, c_end)
+    const int c_end = max(lo_c, n_forced ? min(hi_c, f_lo) : hi_c);
     const bool take_all = n_cand <= want;
     uint32_t prefix = 0, pmask = 0;   // keys with (key & pmask) > prefix are kept
     int remaining = 0;                // keys with (key & pmask) == prefix to keep
@@ -151,9 +153,9 @@ __device__ void select_blocks(const DevDesc & d, int q, const float * __restrict
         if (pre) {
             n_pos = (int) pre[0]; kmin = pre[1]; kmax = pre[2];
         } else {
-            for (int b = tid; b < n_vis; b += blockDim.x) {
+            for (int b = lo_c + tid; b < c_end; b += blockDim.x) {
                 const uint32_t key = __float_as_uint(sc[b]);
-                if (is_cand(b) && key != 0u) { n_pos++; kmin = min(kmin, key); kmax = max(kmax, key); }
+                if (key != 0u) { n_pos++; kmin = min(kmin, key); kmax = max(kmax, key); }
             }
         }
         #pragma unroll
@@ -203,8 +205,7 @@ __device__ void select_blocks(const DevDesc & d, int q, const float * __restrict
             const uint32_t bmask = (uint32_t) (nb - 1);
             for (int i = tid; i < nb; i += blockDim.x) sm.hist[i] = 0;
             __syncthreads();
-            for (int b = tid; b < n_vis; b += blockDim.x) {
-                if (!is_cand(b)) continue;
+            for (int b = lo_c + tid; b < c_end; b += blockDim.x) {
                 const uint32_t key = __float_as_uint(sc[b]);
                 if (key != 0u && (key & pmask) == prefix) atomicAdd(&sm.hist[(key >> shift) & bmask], 1u);
             }
@@ -243,8 +244,7 @@ __device__ void select_blocks(const DevDesc & d, int q, const float * __restrict
                 int * kept = reinterpret_cast<int *>(sm.hist);
                 if (tid == 0) { sm.ncand = 0; sm.nkept = 0; }
                 __syncthreads();
-                for (int b = tid; b < n_vis; b += blockDim.x) {
-                    if (!is_cand(b)) continue;
+                for (int b = lo_c + tid; b < c_end; b += blockDim.x) {
                     const uint32_t key = __float_as_uint(sc[b]);
                     if (key == 0u) continue;
                     const uint32_t km = key & pmask;
@@ -436,6 +436,7 @@ __global__ void __launch_bounds__(SEL_THREADS) score_select_kernel(DevDesc d,
         int f_lo, f_hi;
         forced_range(d, q, f_lo, f_hi);
         const int lo_c = max(blo, 0), hi_c = min(bhi, n_vis);
+        const int c_end = max(lo_c, f_lo <= f_hi ? min(hi_c, f_lo) : hi_c);   // candidates [lo_c, c_end)
         const int i0 = max(blo, 0) / 4, n4 = (min(n_vis, bhi) + 3) / 4;
         #pragma unroll 4
         for (int i = i0 + threadIdx.x; i < n4; i += blockDim.x) {
@@ -447,7 +448,7 @@ __global__ void __launch_bounds__(SEL_THREADS) score_select_kernel(DevDesc d,
             for (int k = 0; k < 4; k++) {
                 const int b = 4 * i + k;
                 const uint32_t key = __float_as_uint(e[k]);
-                if (b >= lo_c && b < hi_c && !(b >= f_lo && b <= f_hi) && key != 0u) {
+                if (b >= lo_c && b < c_end && key != 0u) {
                     pre[0]++;
                     pre[1] = min(pre[1], key);
                     pre[2] = max(pre[2], key);
