@@ -160,20 +160,12 @@ __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
     return *reinterpret_cast<uint32_t *>(&h);
 }
 
-// int8 bytes -> exact f16 values.  For a word w of four int8: f16x2(byte0, byte2) and
-// f16x2(byte1, byte3).  Each byte x becomes the f16 1024 + (x + 128) (bits 0x6400 | (x ^ 0x80))
-// and 1152 is subtracted, exactly.
+// int8 bytes -> exact f16 values: f16x2(byte0, byte2) of a word w of four int8.  Each byte x
+// becomes the f16 1024 + (x + 128) (bits 0x6400 | (x ^ 0x80)) and 1152 is subtracted, exactly.
 __device__ __forceinline__ uint32_t i8x2_even_to_f16x2(uint32_t w) {
     uint32_t t = (w & 0x00FF00FFu) ^ 0x64806480u;
     __half2 h = __hsub2(*reinterpret_cast<__half2 *>(&t), __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480)));
     return *reinterpret_cast<uint32_t *>(&h);
-}
-__device__ __forceinline__ uint32_t i8x2_odd_to_f16x2(uint32_t w) { return i8x2_even_to_f16x2(w >> 8); }
-// f16x2(byte b of w0, byte b of w1)
-template <int B>
-__device__ __forceinline__ uint32_t i8_pair_to_f16x2(uint32_t w0, uint32_t w1) {
-    uint32_t t = __byte_perm(w0, w1, B | ((4 + B) << 8));   // bytes: [w0.B, w0.b0, w1.B, w0.b0]
-    return i8x2_even_to_f16x2(t);
 }
 
 // The same conversions without the subtraction: each value comes out as the f16 1152 + x

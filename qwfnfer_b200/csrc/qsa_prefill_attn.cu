@@ -57,13 +57,9 @@ constexpr uint32_t PA_TMEM_O = 256;
 constexpr uint32_t PA_IDESC_S = umma_idesc_f16(PA_ROWS, PA_CELLS);
 constexpr uint32_t PA_IDESC_O = umma_idesc_f16(PA_ROWS, HEAD_DIM) | (1u << 16);   // B (V) MN-major
 constexpr int PA_SLOT_SHIFT = 10;                  // entry = query << 10 | slot (slot < MAX_KB)
-// A Q stage (and the O rows staged in it) is [query][64-column atom][8 rows][128 bytes] with the
-// 128-byte swizzle inside each 1 KB (8 rows x 128 bytes): the MMA reads it as a K-major operand
-// whose 8-row groups are 4 KB apart, and one 4-D TMA box moves a query's 4 KB.
-__device__ __forceinline__ uint32_t q_stage_off(int r, int k) {
-    return (uint32_t) ((r >> 3) * PA_QROWS + (k >> 6) * 1024 + (r & 7) * 128 + ((((k >> 3) & 7) ^ (r & 7)) << 4) +
-                       ((k & 7) << 1));
-}
+// A Q stage is [query][64-column atom][8 rows][128 bytes] with the 128-byte swizzle inside each
+// 1 KB (8 rows x 128 bytes): the MMA reads it as a K-major operand whose 8-row groups are 4 KB
+// apart, and one 4-D TMA box moves a query's 4 KB.
 // shared-memory descriptor of a 128-byte-swizzled MN-major operand: 64-element MN blocks lbo bytes
 // apart, groups of 8 K rows (1 KB atoms) sbo bytes apart
 __device__ __forceinline__ uint64_t umma_desc_sw128_mn(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
