@@ -211,7 +211,7 @@ def cpu_baseline_config2(d, kc, vc, pool, q_host, qi_host, n_past, budget_s=12.0
 
     import oracle
     from qwfnfer_b200._abi import TYPE_BF16
-    threads = oracle.max_threads()
+    threads = len(os.sched_getaffinity(0))   # every host core this process may use (torchrun sets OMP_NUM_THREADS=1)
     oracle.set_threads(threads)
     flags = oracle.DEFAULT_FLAGS | oracle.GGML_FA | oracle.GGML_V_F16
     times = []
@@ -837,7 +837,7 @@ def run_reference_config2(args):
     cfg = CONFIGS[2]
     d = cfg.desc()
     n_past = cfg.n_past
-    threads = oracle.max_threads()
+    threads = len(os.sched_getaffinity(0))   # every host core this process may use (torchrun sets OMP_NUM_THREADS=1)
     oracle.set_threads(threads)
     rng = np.random.default_rng(cfg.seed)
     kc, vc, ic, pool = oracle.cache_arrays(d)

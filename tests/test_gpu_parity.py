@@ -11,7 +11,7 @@ import pytest
 import torch
 
 import oracle
-from helpers import ATTN_TOL, POOL_TOL, check_selection, host_caches, rel_err, sel_matrix
+from helpers import ATTN_TOL, POOL_TOL, check_selection, forced_blocks, host_caches, rel_err, sel_matrix
 from qwfnfer_b200._abi import QSA_OK, TYPE_BF16, TYPE_F16, TYPE_F32, TYPE_Q8_0, k_blocks, lib, make_desc
 from qwfnfer_b200.configs import IDX_STD, K_SCALE, fill_cache, token_inputs
 from qwfnfer_b200.qsa import QsaNode, QsaState, decode_items
@@ -220,6 +220,28 @@ def test_prefill_radix_selection_and_attention(kv_type, top_k):
         check_selection(d, sel1[t], sc, qp)
         ref = oracle.attend(d, kc, vc, [qp], sel1[t][None], qh[t][None], q_type=qt)[0]
         assert rel_err(out1[t], ref) <= ATTN_TOL
+
+
+@pytest.mark.parametrize("n_past,T", [(0, 300), (0, 64), (130, 65), (4000, 63)])
+def test_prefill_first_chunks_and_path_boundary(n_past, T):
+    """Prefill from an empty cache (early queries see no whole block: only the window) and chunk
+    sizes on both sides of the block-grouped path's threshold (64 tokens), against the oracle."""
+    d = desc_for(TYPE_Q8_0, 8192, top_k=16)
+    node, st, (q, q_idx, k, v, ki), out, sel = run_prefill(d, n_past, T, [T], 81)
+    assert np.isfinite(out).all()
+    kc, vc, _, pool = host_caches(st, 0, n_past + T)
+    qh, qt = q_host(q)
+    qi = q_idx.cpu().numpy()
+    for t in sorted(set([0, 1, T // 2, T - 1] + list(range(0, T, 29)))):
+        qp = n_past + t
+        nb = (qp + 1) // 64
+        if nb > 0:
+            sc = oracle.scores(d, pool, nb, qi[t])[0]
+            check_selection(d, sel[t], sc, qp)
+        else:                                         # no whole block yet: the window alone
+            assert {int(x) for x in sel[t] if x >= 0} == forced_blocks(d, qp)
+        ref = oracle.attend(d, kc, vc, [qp], sel[t][None], qh[t][None], q_type=qt)[0]
+        assert rel_err(out[t], ref) <= ATTN_TOL
 
 
 @pytest.mark.parametrize("kv_type", [TYPE_Q8_0, TYPE_F16])
