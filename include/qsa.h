@@ -278,6 +278,15 @@ qsa_status qsa_prefill(const qsa_desc * d, const qsa_layer_cache * cache /* host
                        float * out, int32_t * sel_out,
                        void * ws, size_t ws_bytes, qsa_stream_t stream);
 
+/* ------------------------------------------------------------------ staging */
+/* Copy `bytes` (a multiple of 16, both addresses 16-byte aligned) from src to dst with a kernel on
+ * `stream`, chained to the kernels around it by programmatic dependent launch.  Each side is device
+ * memory of the current device, managed memory, or pinned host memory mapped at its host address
+ * (QSA_ERR_INVALID otherwise).  Moves a decode step's activations in and its output out without a
+ * copy-engine hand-over; replaces the per-token ggml_backend_tensor_set of the decode inputs
+ * (src/qwfn_engine.cpp:738-753) and the read of the result after the graph computes. */
+qsa_status qsa_stage_copy(void * dst, const void * src, size_t bytes, qsa_stream_t stream);
+
 /* ------------------------------------------------------------------ status */
 /* Synchronise `stream`, read and clear the workspace status word. */
 qsa_status qsa_check(void * ws, size_t ws_bytes, qsa_stream_t stream);

@@ -133,6 +133,7 @@ def lib() -> ctypes.CDLL:
         "qsa_prefill_workspace_size": (SZ, [D, I32, I32]),
         "qsa_prefill": (I32, [D, C, I32, I32, VP, I32, VP, VP, VP, VP, VP, VP, VP, SZ, VP]),
         "qsa_check": (I32, [VP, SZ, VP]),
+        "qsa_stage_copy": (I32, [VP, VP, SZ, VP]),
         "qsa_version": (I32, []),
     }
     for name, (res, args) in sigs.items():
@@ -156,5 +157,5 @@ HEADER_SYMBOLS = [
     "qsa_shard_append_ri", "qsa_shard_decode_ri",
     "qsa_merge_states",
     "qsa_ipc_handle", "qsa_ipc_open", "qsa_ipc_close", "qsa_peer_buffer_bytes", "qsa_peer_push", "qsa_peer_wait",
-    "qsa_prefill_workspace_size", "qsa_prefill", "qsa_check", "qsa_version",
+    "qsa_prefill_workspace_size", "qsa_prefill", "qsa_stage_copy", "qsa_check", "qsa_version",
 ]

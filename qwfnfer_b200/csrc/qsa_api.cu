@@ -297,6 +297,17 @@ qsa_status qsa_workspace_init(void * ws, size_t ws_bytes, qsa_stream_t stream) {
 }
 
 namespace {
+// The append of a decode step: a plain launch, never a programmatic dependent.  Everything
+// before it in the stream (whatever wrote the items, q_idx and the new rows) is then complete
+// when the chain starts, which the selection relies on: launched behind the append, it reads
+// the items and q_idx before its own griddepcontrol.wait.
+qsa_status launch_append_decode(const DevDesc & d, cudaStream_t st, int batch, const qsa_decode_item * items,
+                                const float * k_new, const float * v_new, const float * kidx_new, uint32_t * status) {
+    append_decode_kernel<<<batch, APPEND_DECODE_THREADS, append_decode_smem(d), st>>>(d, items, k_new, v_new, kidx_new,
+                                                                                     status);
+    return cuda_status(cudaGetLastError());
+}
+
 qsa_status decode_common(const qsa_desc * dd, const qsa_decode_item * items, int32_t batch, int32_t max_n_kv,
                          void * ws, size_t ws_bytes, DevDesc & d, WsLayout & w) {
     qsa_status s = qsa_desc_check(dd);
@@ -316,9 +327,8 @@ qsa_status qsa_decode_append(const qsa_desc * dd, const qsa_decode_item * items,
     qsa_status s = decode_common(dd, items, batch, max_n_kv, ws, ws_bytes, d, w);
     if (s != QSA_OK) return s;
     if (!k_new || !v_new || !kidx_new) return QSA_ERR_INVALID;
-    append_decode_kernel<<<batch, APPEND_DECODE_THREADS, append_decode_smem(d), reinterpret_cast<cudaStream_t>(stream)>>>(
-        d, items, k_new, v_new, kidx_new, reinterpret_cast<uint32_t *>(static_cast<unsigned char *>(ws) + w.status));
-    return cuda_status(cudaGetLastError());
+    return launch_append_decode(d, reinterpret_cast<cudaStream_t>(stream), batch, items, k_new, v_new, kidx_new,
+                                reinterpret_cast<uint32_t *>(static_cast<unsigned char *>(ws) + w.status));
 }
 
 qsa_status qsa_decode_select(const qsa_desc * dd, const qsa_decode_item * items, int32_t batch, int32_t max_n_kv,
@@ -357,8 +367,8 @@ qsa_status qsa_decode(const qsa_desc * dd, const qsa_decode_item * items, int32_
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     unsigned char * wsb = static_cast<unsigned char *>(ws);
     if (any_new)
-        append_decode_kernel<<<batch, APPEND_DECODE_THREADS, append_decode_smem(d), st>>>(d, items, k_new, v_new, kidx_new,
-                                                    reinterpret_cast<uint32_t *>(wsb + w.status));
+        if ((s = launch_append_decode(d, st, batch, items, k_new, v_new, kidx_new,
+                                      reinterpret_cast<uint32_t *>(wsb + w.status))) != QSA_OK) return s;
     qsa_layer_cache none{};
     if ((s = launch_select(d, w, batch, items, none, 0, q_idx, sel_out, wsb, st)) != QSA_OK) return s;
     return launch_attend(d, w, batch, items, none, 0, q, q_type, out, wsb, st);
@@ -459,8 +469,8 @@ qsa_status qsa_shard_candidates(const qsa_desc * dd, const qsa_decode_item * ite
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     unsigned char * wsb = static_cast<unsigned char *>(ws);
     if (any_new)           // only the shard holding a query's cell writes it (the kernel skips the rest)
-        append_decode_kernel<<<batch, APPEND_DECODE_THREADS, append_decode_smem(d), st>>>(d, items, k_new, v_new, kidx_new,
-                                                    reinterpret_cast<uint32_t *>(wsb + w.status));
+        if ((s = launch_append_decode(d, st, batch, items, k_new, v_new, kidx_new,
+                                      reinterpret_cast<uint32_t *>(wsb + w.status))) != QSA_OK) return s;
     qsa_layer_cache none{};
     return launch_select(d, w, batch, items, none, 0, q_idx, cand, wsb, st,
                          reinterpret_cast<float *>(cand + (size_t) batch * d.kb));
@@ -516,8 +526,8 @@ qsa_status qsa_shard_decode_ri(const qsa_desc * dd, const qsa_decode_item * item
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     unsigned char * wsb = static_cast<unsigned char *>(ws);
     if (any_new)           // every rank writes the raw and pooled keys, the owning shard the K/V row
-        append_decode_kernel<<<batch, APPEND_DECODE_THREADS, append_decode_smem(d), st>>>(d, items, k_new, v_new, kidx_new,
-                                                    reinterpret_cast<uint32_t *>(wsb + w.status));
+        if ((s = launch_append_decode(d, st, batch, items, k_new, v_new, kidx_new,
+                                      reinterpret_cast<uint32_t *>(wsb + w.status))) != QSA_OK) return s;
     qsa_layer_cache none{};
     if ((s = launch_select(d, w, batch, items, none, 0, q_idx, sel_out, wsb, st)) != QSA_OK) return s;
     return launch_attend(d, w, batch, items, none, 0, q, q_type, nullptr, wsb, st, state);

@@ -6,6 +6,8 @@ Names follow the reference so that callers and tests read like it:
   QsaNode.sparse_attn_decode   graph_builder::sparse_attn_decode (src/qwfn_graph.cpp:450-546)
   QsaNode.sparse_attn          graph_builder::sparse_attn / qsa_top_k (src/qwfn_graph.cpp:235-408)
   QsaNode.qsa_pool_rebuild     graph_builder::qsa_pool_rebuild (src/qwfn_graph.cpp:431-448)
+  QsaDecodeStep      one captured decode step per token, as the engine computes one graph per step
+                     (src/qwfn_engine.cpp:814)
 Errors raise QsaError carrying the qsa_status (the reference aborts; the library never does).
 PyTorch provides device memory and streams only; every computation runs in libqsa.so.
 """
@@ -153,3 +155,96 @@ class QsaNode:
     def check(self, ws: torch.Tensor, stream=None) -> int:
         """qsa_check: synchronise and return (and clear) the device status as a qsa_status."""
         return lib().qsa_check(ws.data_ptr(), ws.numel(), _stream(stream))
+
+    def decode_step(self, caches: list[QsaLayerCache], max_n_kv: int, q_dtype=torch.bfloat16,
+                    sel_out: bool = False) -> "QsaDecodeStep":
+        """A captured decode step of these caches (one token per cache, at most max_n_kv cells)."""
+        return QsaDecodeStep(self, caches, max_n_kv, q_dtype, sel_out)
+
+
+class QsaDecodeStep:
+    """One decode step of fixed shape, captured once as a CUDA graph and replayed per token, the way
+    the engine submits one compute graph per step to its backend (src/qwfn_engine.cpp:814).
+
+    A replay is qsa_stage_copy of the step's packed pinned host buffer to the device (the item
+    table with this token's positions, then q, q_idx, k_new, v_new, kidx_new), qsa_decode, and
+    qsa_stage_copy of the output to pinned host memory: kernels on the compute engine at both ends,
+    no copy-engine hand-over.  Between replays: wait(), write the inputs (the views in `host`,
+    or a packed row through load()) and the positions (set_positions()), run(), then read
+    `host_out` once the stream has synchronised (run(sync=True) does that)."""
+
+    def __init__(self, node: QsaNode, caches: list[QsaLayerCache], max_n_kv: int, q_dtype=torch.bfloat16,
+                 sel_out: bool = False):
+        d = node.desc
+        if q_dtype not in (torch.bfloat16, torch.float32):
+            raise QsaError(_abi.QSA_ERR_INVALID, "q dtype must be bfloat16 or float32")
+        self.node, self.batch, self.max_n_kv, self.q_dtype = node, len(caches), int(max_n_kv), q_dtype
+        B, kv_dim = self.batch, d.n_head_kv * d.head_dim
+        item_bytes = ctypes.sizeof(QsaDecodeItem)
+        parts = [("items", (B * item_bytes,), torch.uint8), ("q", (B, d.n_head, d.head_dim), q_dtype),
+                 ("q_idx", (B, d.idx_n_head, d.idx_dim), torch.float32), ("k_new", (B, kv_dim), torch.float32),
+                 ("v_new", (B, kv_dim), torch.float32), ("kidx_new", (B, d.idx_dim), torch.float32)]
+        layout, o = [], 0
+        for name, shape, dt in parts:
+            n = torch.Size(shape).numel() * torch.empty(0, dtype=dt).element_size()
+            layout.append((name, shape, dt, o, n))
+            o += (n + 15) // 16 * 16                 # every part starts on 16 bytes
+        self.row_bytes = o
+        self.input_offset = layout[1][3]            # q..kidx_new: the per-token activations
+        self.host_in = torch.zeros(o, dtype=torch.uint8).pin_memory()
+        self.dev_in = torch.empty(o, dtype=torch.uint8, device=node.device)
+
+        def views(buf):
+            return {name: buf[off:off + n].view(dt).view(shape) for name, shape, dt, off, n in layout}
+
+        self.host, self.dev = views(self.host_in), views(self.dev_in)
+        table = (QsaDecodeItem * B)()
+        for i, c in enumerate(caches):
+            table[i].cache = c
+        self.host["items"].copy_(torch.frombuffer(bytearray(bytes(table)), dtype=torch.uint8))
+        self._n_past = self.host["items"].view(torch.int32).view(B, item_bytes // 4)[:, QsaDecodeItem.n_past.offset // 4]
+        self.out = torch.empty((B, d.n_head, d.head_dim), dtype=torch.float32, device=node.device)
+        self.host_out = torch.empty((B, d.n_head, d.head_dim), dtype=torch.float32).pin_memory()
+        self.sel = torch.empty((B, node.kb), dtype=torch.int32, device=node.device) if sel_out else None
+        self.ws = node.workspace("decode", B, self.max_n_kv)
+        self.done = torch.cuda.Event()
+        self.graph: torch.cuda.CUDAGraph | None = None
+
+    def set_positions(self, n_past: list[int]) -> None:
+        """Cells already cached per sequence: this token is appended at n_past and attends n_past + 1."""
+        if len(n_past) != self.batch or any(n < 0 or n + 1 > self.max_n_kv for n in n_past):
+            raise QsaError(_abi.QSA_ERR_INVALID, "positions outside the captured step's shape")
+        self._n_past.copy_(torch.tensor(n_past, dtype=torch.int32))
+
+    def load(self, row: torch.Tensor) -> None:
+        """Copy one packed host row of the activations (q..kidx_new, the layout of host_in past the
+        item table) into the pinned input buffer."""
+        self.host_in[self.input_offset:].copy_(row)
+
+    def wait(self) -> None:
+        """Block until the last replay has finished with the host buffers."""
+        self.done.synchronize()
+
+    def _call(self) -> None:
+        d, dv, st = self.node.desc, self.dev, _stream(None)
+        check(lib().qsa_stage_copy(self.dev_in.data_ptr(), self.host_in.data_ptr(), self.row_bytes, st),
+              "qsa_stage_copy (inputs)")
+        q_type = TYPE_BF16 if self.q_dtype == torch.bfloat16 else TYPE_F32
+        check(lib().qsa_decode(ctypes.byref(d), self.dev_in.data_ptr(), self.batch, self.max_n_kv,
+                               dv["q"].data_ptr(), q_type, dv["q_idx"].data_ptr(), dv["k_new"].data_ptr(),
+                               dv["v_new"].data_ptr(), dv["kidx_new"].data_ptr(), self.out.data_ptr(),
+                               _ptr(self.sel), self.ws.data_ptr(), self.ws.numel(), st), "qsa_decode")
+        check(lib().qsa_stage_copy(self.host_out.data_ptr(), self.out.data_ptr(),
+                                   self.out.numel() * self.out.element_size(), st), "qsa_stage_copy (output)")
+
+    def run(self, sync: bool = False) -> torch.Tensor:
+        """Replay the step on the current stream (captured on first use); returns host_out."""
+        if self.graph is None:
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph, capture_error_mode="relaxed"):
+                self._call()
+        self.graph.replay()
+        self.done.record()
+        if sync:
+            self.done.synchronize()
+        return self.host_out
