@@ -92,17 +92,16 @@ WsLayout ws_layout(const DevDesc & d, int n_q, int max_n_kv) {
 
 qsa_status cuda_status(cudaError_t e) { return e == cudaSuccess ? QSA_OK : QSA_ERR_CUDA; }
 
-bool attrs_done = false;
+std::atomic<uint64_t> attrs_done{0};
 qsa_status set_attrs() {
-    if (attrs_done) return QSA_OK;
-    cudaError_t e = attn_set_attrs();
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(score_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(append_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
-    if (e != cudaSuccess) return QSA_ERR_CUDA;
-    attrs_done = true;
-    return QSA_OK;
+    return cuda_status(once_per_device(attrs_done, [] {
+        cudaError_t e = attn_set_attrs();
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(score_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(append_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+        return e;
+    }));
 }
 
 // Scores + selection into the workspace (and sel_out).  Sharded (cand_scores != null): scores of

@@ -1,8 +1,27 @@
 // qsa_kernels.cuh -- kernel entry points of libqsa and their launch constants.
 #pragma once
+#include <atomic>
+
 #include "qsa_common.cuh"
 
 namespace qsa {
+
+// Runs `set` (cudaFuncSetAttribute calls) once on each device: function attributes are a
+// per-device setting, so a process driving several GPUs sets them on every device it launches
+// on.  `done` holds one bit per device id; the calls are idempotent, so two threads racing on a
+// device's first launch both just set them.
+template <typename F>
+cudaError_t once_per_device(std::atomic<uint64_t> & done, F && set) {
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    const uint64_t bit = 1ull << dev;
+    if (done.load(std::memory_order_acquire) & bit) return cudaSuccess;
+    e = set();
+    if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_acq_rel);
+    return e;
+}
 
 constexpr int MAX_KB = 1024;          // blocks kept per query that the kernels can hold
 constexpr int SEL_THREADS_HOST = 1024;      // threads of a scoring/selection CTA

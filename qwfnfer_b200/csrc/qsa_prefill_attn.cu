@@ -649,12 +649,11 @@ size_t prefill_kv_workspace(const DevDesc & d, int T, int n_blocks) { return pre
 cudaError_t launch_prefill_attn_kv(const DevDesc & d, cudaStream_t st, qsa_layer_cache cache, int n_past0, int T,
                                    const void * q, int q_type, const int * sel, const int * nsel, int n_blocks,
                                    unsigned char * ws, float * out, uint32_t * status) {
-    static bool attr = false;
-    if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(prefill_attn_kv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PA_SMEM);
-        if (e != cudaSuccess) return e;
-        attr = true;
-    }
+    static std::atomic<uint64_t> attr{0};
+    cudaError_t e = once_per_device(attr, [] {
+        return cudaFuncSetAttribute(prefill_attn_kv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PA_SMEM);
+    });
+    if (e != cudaSuccess) return e;
     const PrefillKvLayout L = prefill_kv_layout(d, T, n_blocks);
     const size_t slots = (size_t) T * d.kb;
     int * cnt = reinterpret_cast<int *>(ws + L.cnt);
@@ -672,7 +671,7 @@ cudaError_t launch_prefill_attn_kv(const DevDesc & d, cudaStream_t st, qsa_layer
                !encode_cache_map_f16(&v_map, cache.v, d.rb_v, d.n_ctx, d.n_head_kv)
              : !encode_cache_map(&k_map, cache.k, d.rb_k, d.n_ctx) || !encode_cache_map(&v_map, cache.v, d.rb_v, d.n_ctx)))
         return cudaErrorNotSupported;
-    cudaError_t e = cudaMemsetAsync(cnt, 0, (size_t) n_blocks * 4, st);
+    e = cudaMemsetAsync(cnt, 0, (size_t) n_blocks * 4, st);
     if (e != cudaSuccess) return e;
     const int nthr = 256;
     const unsigned nb_slots = (unsigned) ((slots + nthr - 1) / nthr);

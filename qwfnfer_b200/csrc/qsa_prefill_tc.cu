@@ -259,12 +259,11 @@ __global__ void __launch_bounds__(32 * SELW_WARPS) select_scores_warp_kernel(Dev
 cudaError_t launch_prefill_scores_tc(const DevDesc & d, cudaStream_t st, const float * q_idx, int T,
                                      const uint16_t * pool, int n_blocks, float * scores, int scores_stride,
                                      uint32_t * status) {
-    static bool attr = false;
-    if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(idx_scores_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM);
-        if (e != cudaSuccess) return e;
-        attr = true;
-    }
+    static std::atomic<uint64_t> attr{0};
+    const cudaError_t e = once_per_device(attr, [] {
+        return cudaFuncSetAttribute(idx_scores_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM);
+    });
+    if (e != cudaSuccess) return e;
     const int n_rows = T * d.idx_n_head;
     const dim3 grid((unsigned) ((n_rows + TC_M - 1) / TC_M), (unsigned) ((n_blocks + TC_N - 1) / TC_N));
     if (n_blocks <= 0) return cudaSuccess;

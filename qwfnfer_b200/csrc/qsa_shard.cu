@@ -327,11 +327,12 @@ cudaError_t launch_shard_select(const DevDesc & d, cudaStream_t st, const qsa_de
     if (per_warp > SMEM_MAX) return cudaErrorInvalidValue;
     const int warps = (int) std::min<size_t>(std::min<size_t>(SHARD_SEL_WARPS, SMEM_MAX / per_warp), (size_t) batch);
     const size_t smem = per_warp * warps;
-    static size_t attr = 48 * 1024;
-    if (smem > attr) {
-        cudaError_t e = cudaFuncSetAttribute(shard_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) SMEM_MAX);
+    static std::atomic<uint64_t> attr{0};
+    if (smem > 48 * 1024) {
+        const cudaError_t e = once_per_device(attr, [] {
+            return cudaFuncSetAttribute(shard_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) SMEM_MAX);
+        });
         if (e != cudaSuccess) return e;
-        attr = SMEM_MAX;
     }
     shard_select_kernel<<<(batch + warps - 1) / warps, 32 * warps, smem, st>>>(
         d, items, n_shards, batch, cand, cand_stride, blo, bhi, sel_out, sel_ws, nsel_ws, status);
