@@ -387,6 +387,7 @@ def run_ours_config2(args, ws, rank, local):
         "gpu_launches": launches * K,       # libqsa kernels per replay (CUPTI count) x timed steps
         "clocks": clocks.summary(),
     }
+    res["front"] = front_stage(d, dev, n_past, flush, K, cfg.seed)
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         kc = st.k[0][:n_past + 1].cpu().numpy()
         vc = st.v[0][:n_past + 1].cpu().numpy()
@@ -394,6 +395,45 @@ def run_ours_config2(args, ws, rank, local):
         qh = q.view(torch.int16).cpu().numpy().view(np.uint16)
         res["cpu_baseline"] = cpu_baseline_config2(d, kc, vc, pool, qh, qi.cpu().numpy(), n_past)
     return res
+
+
+def front_stage(d, dev, n_past, flush, K, seed):
+    """The projection front feeding the node (qsa_front: attn_q/k/v and the indexer projections
+    over n_embd 2560, their norms and IMRoPE) for this token: graph replay, L2 flushed, its own
+    HBM roofline (the bf16 weights dominate its bytes)."""
+    import torch
+
+    from qwfnfer_b200.configs import front_weights
+    from qwfnfer_b200.qsa import QsaFront
+
+    w = front_weights(d, seed=seed + 50, device=dev)
+    front = QsaFront(d, **w)
+    x = torch.randn(1, front.n_embd, generator=torch.Generator(device=dev).manual_seed(seed + 51), device=dev)
+    pos = torch.tensor([n_past], dtype=torch.int32, device=dev)
+    for _ in range(3):
+        outs = front.project(x, pos)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        outs = front.project(x, pos)
+    us = []
+    for _ in range(max(K, 20)):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        g.replay()
+        b.record()
+        us.append((a, b))
+    torch.cuda.synchronize()
+    us = [a.elapsed_time(b) * 1e3 for a, b in us]
+    w_bytes = sum(t.numel() * t.element_size() for t in w.values())
+    nbytes = w_bytes + x.numel() * 4 + sum(o.numel() * 4 for o in outs)
+    mean = statistics.mean(us)
+    hbm, _, src = peaks()
+    ach = nbytes / (mean * 1e-6) / 1e9
+    return {"kernel": "front_kernel (qsa_front), 1 token, n_embd 2560, bf16 weights", "us": round(mean, 3),
+            "algorithmic_bytes": nbytes, "achieved_gbs": round(ach, 1), "peak": hbm,
+            "frac": round(ach / hbm, 4), "peak_source": f"{src} hbm_gbs (burst)", "launches": 1}
 
 
 def _timed_replays(graph, n, before=None):

@@ -278,6 +278,41 @@ qsa_status qsa_prefill(const qsa_desc * d, const qsa_layer_cache * cache /* host
                        float * out, int32_t * sel_out,
                        void * ws, size_t ws_bytes, qsa_stream_t stream);
 
+/* ------------------------------------------------------------------ projection front */
+/* The projections feeding the node, as graph_builder::sparse_attn_decode builds them
+ * (src/qwfn_graph.cpp:465, 479-484, 505-518; prefill :324-347).  Weights are row-major
+ * [out][n_embd] (ggml's mul_mat layout), bf16, 16-byte aligned; the norm weights are f32. */
+typedef struct qsa_front_weights {
+    const void  * wq;          /* attn_q.weight [2*head_dim*n_head][n_embd]: head h's query rows
+                                  [2*h*hd, 2*h*hd + hd), its gate rows the next hd */
+    const void  * wk;          /* attn_k.weight [head_dim*n_head_kv][n_embd] */
+    const void  * wv;          /* attn_v.weight [head_dim*n_head_kv][n_embd] */
+    const void  * wq_idx;      /* indexer.q_proj.weight [idx_dim*idx_n_head][n_embd] */
+    const void  * wk_idx;      /* indexer.k_proj.weight [idx_dim][n_embd] */
+    const float * q_norm;      /* attn_q_norm.weight [head_dim] (NULL = 1) */
+    const float * k_norm;      /* attn_k_norm.weight [head_dim] (NULL = 1) */
+    const float * q_idx_norm;  /* indexer.q_norm.weight [idx_dim] (NULL = 1) */
+    int32_t       n_embd;      /* model width: a multiple of 8, at most 12288 */
+    int32_t       w_type;      /* QSA_TYPE_BF16 */
+} qsa_front_weights;
+
+size_t qsa_front_workspace_size(const qsa_desc * d, const qsa_front_weights * w, int32_t T);
+/* For T tokens at positions pos[T] (device int32) with activations x [T][n_embd] (device f32):
+ *   y = W x, x rounded to bf16 as the CPU mul_mat converts it, f32 accumulation;
+ *   q_out     f32 [T][n_head][head_dim]      rms_norm * q_norm, IMRoPE at pos
+ *   gate_out  f32 [T][n_head*head_dim]       the gate half of attn_q, raw
+ *   q_idx_out f32 [T][idx_n_head][idx_dim]   rms_norm * q_idx_norm, IMRoPE at pos
+ *   k_out     f32 [T][n_head_kv*head_dim]    rms_norm * k_norm, IMRoPE at pos
+ *   v_out     f32 [T][n_head_kv*head_dim]    raw
+ *   kidx_out  f32 [T][idx_dim]               raw (normed and roped when pooled)
+ * which are qsa_decode's q (QSA_TYPE_F32), q_idx, k_new, v_new and kidx_new.  The workspace is
+ * zeroed once (qsa_workspace_init).  Replaces the projection, norm and rope nodes of
+ * src/qwfn_graph.cpp:465, 479-484, 505-518. */
+qsa_status qsa_front(const qsa_desc * d, const qsa_front_weights * w, int32_t T, const int32_t * pos,
+                     const float * x, float * q_out, float * gate_out, float * q_idx_out,
+                     float * k_out, float * v_out, float * kidx_out,
+                     void * ws, size_t ws_bytes, qsa_stream_t stream);
+
 /* ------------------------------------------------------------------ staging */
 /* Copy `bytes` (a multiple of 16, both addresses 16-byte aligned) from src to dst with a kernel on
  * `stream`, chained to the kernels around it by programmatic dependent launch.  Each side is device

@@ -47,6 +47,7 @@ def lib() -> ctypes.CDLL:
             "orc_attend_state": (None, [D, VP, VP, I64, VP, VP, I64, VP, I32, VP, I32]),
             "orc_k_blocks": (ctypes.c_int, [D]),
             "orc_node": (None, [D, VP, VP, VP, I64, VP, VP, I32, VP, VP, VP, VP, I32]),
+            "orc_front": (None, [D, VP, VP, VP, VP, VP, VP, VP, VP, I64, I64, VP, VP, VP, VP, VP, VP, VP, VP]),
         }
         for name, (res, args) in sigs.items():
             fn = getattr(L, name)
@@ -207,3 +208,22 @@ def cache_arrays(d: QsaDesc):
     n = d.n_ctx
     return (np.zeros((n, row_bytes(d, 0)), np.uint8), np.zeros((n, row_bytes(d, 1)), np.uint8),
             np.zeros((n, d.idx_dim), np.uint16), np.zeros((n // d.ratio, d.idx_dim), np.uint16))
+
+
+def front(d: QsaDesc, w: dict, pos: np.ndarray, x: np.ndarray) -> dict:
+    """orc_front: the projections, norms and IMRoPE feeding the node for T tokens.
+    w: wq, wk, wv, wq_idx, wk_idx as uint16 bf16 bits [out][n_embd]; q_norm, k_norm, q_idx_norm f32
+    (or None).  pos int32 [T], x f32 [T][n_embd].  Returns q, gate, q_idx, k, v, kidx (f32)."""
+    T, n_embd = x.shape
+    hd, nh, nkv, H, D = d.head_dim, d.n_head, d.n_head_kv, d.idx_n_head, d.idx_dim
+    out = {"q": np.zeros((T, nh, hd), np.float32), "gate": np.zeros((T, nh * hd), np.float32),
+           "q_idx": np.zeros((T, H, D), np.float32), "k": np.zeros((T, nkv * hd), np.float32),
+           "v": np.zeros((T, nkv * hd), np.float32), "kidx": np.zeros((T, D), np.float32)}
+    ws = [np.ascontiguousarray(w[k], dtype=np.uint16) for k in ("wq", "wk", "wv", "wq_idx", "wk_idx")]
+    ns = [None if w.get(k) is None else np.ascontiguousarray(w[k], dtype=np.float32)
+          for k in ("q_norm", "k_norm", "q_idx_norm")]
+    pos = np.ascontiguousarray(pos, dtype=np.int32)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    lib().orc_front(ctypes.byref(d), *[_p(a) for a in ws], *[_p(a) for a in ns], n_embd, T, _p(pos), _p(x),
+                    *[_p(out[k]) for k in ("q", "gate", "q_idx", "k", "v", "kidx")])
+    return out

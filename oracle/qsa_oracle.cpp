@@ -48,6 +48,14 @@ inline float bf16_to_f32(uint16_t u) {
     return f;
 }
 
+// f32 -> bf16 rounded to nearest even (ggml's fp32 -> bf16 conversion; a NaN stays a quiet NaN).
+inline uint16_t f32_to_bf16(float f) {
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t) ((u >> 16) | 64u);
+    return (uint16_t) ((u + (0x7fffu + ((u >> 16) & 1u))) >> 16);
+}
+
 constexpr int QK8_0 = 32;
 constexpr size_t Q8_0_BYTES = 34;
 
@@ -458,6 +466,86 @@ void orc_node(const qsa_desc * d, const uint8_t * kc, const uint8_t * vc, const 
         if (scores_out) std::memcpy(scores_out + t * nb, sc.data() + t * nb, (size_t) nb * 4);
     }
     orc_attend(d, kc, vc, n_q, q_pos, sel, KB, Q, q_type, out, flags);
+}
+
+
+// rms_norm * w then IMRoPE at position `pos` over one head of D values, in place: the arithmetic
+// of orc_pool_blocks's norm and rope (rms(): ggml_rms_norm then ggml_mul, src/qwfn_graph.cpp:114-115;
+// ggml_rope_multi IMROPE with positions (p, p, p, 0)).
+static void orc_norm_rope(const qsa_desc * d, float * v, int64_t D, const float * w, float pos) {
+    const int64_t nd = d->rope_dim;
+    const float theta_scale = powf(d->rope_freq_base, -2.0f / (float) nd);
+    const int * s = d->sections;
+    const int sect_dims = s[0] + s[1] + s[2] + s[3];
+    double ss = 0.0;
+    for (int64_t e = 0; e < D; e++) ss += (double) (v[e] * v[e]);
+    const float mean  = (float) (ss / (double) D);
+    const float scale = 1.0f / sqrtf(mean + d->rms_eps);
+    std::vector<float> y(D);
+    for (int64_t e = 0; e < D; e++) {
+        y[e] = v[e] * scale;
+        if (w) y[e] = y[e] * w[e];
+    }
+    float th_t = pos, th_h = pos, th_w = pos, th_e = 0.0f;
+    for (int64_t e = 0; e < D; e++) v[e] = y[e];
+    for (int64_t i0 = 0; i0 < nd; i0 += 2) {
+        const int sector = (int) ((i0 / 2) % sect_dims);
+        float theta;
+        if (sector % 3 == 1 && sector < 3 * s[1])      theta = th_h;
+        else if (sector % 3 == 2 && sector < 3 * s[2]) theta = th_w;
+        else if (sector % 3 == 0 && sector < 3 * s[0]) theta = th_t;
+        else                                           theta = th_e;
+        const float c = cosf(theta), sn = sinf(theta);
+        const int64_t ic0 = i0 / 2;
+        const float x0 = y[ic0], x1 = y[ic0 + nd / 2];
+        v[ic0]          = x0 * c - x1 * sn;
+        v[ic0 + nd / 2] = x0 * sn + x1 * c;
+        th_t *= theta_scale; th_h *= theta_scale; th_w *= theta_scale; th_e *= theta_scale;
+    }
+}
+
+// The projections feeding the node for T tokens (src/qwfn_graph.cpp:465, 479-484, 505-518):
+//   y = mul_mat(W bf16, x): x rounded to bf16 (the CPU mul_mat converts the f32 operand to the
+//   weight's dot type), products of two bf16 exact in f32, accumulated in double and rounded
+//   once to f32 (ggml's f32 SIMD lanes agree to a few ulp);
+//   attn_q rows per head h: [2h*hd, 2h*hd+hd) the query, the next hd the gate (:505-510);
+//   Q = rms(Q_h)*q_norm, K = rms(K_h)*k_norm, q_idx = rms(q_h)*q_idx_norm, each then IMRoPE at the
+//   token's position; V, the gate and the raw indexer key as projected.
+void orc_front(const qsa_desc * d, const uint16_t * wq, const uint16_t * wk, const uint16_t * wv,
+               const uint16_t * wq_idx, const uint16_t * wk_idx, const float * q_norm, const float * k_norm,
+               const float * q_idx_norm, int64_t n_embd, int64_t T, const int32_t * pos, const float * x,
+               float * q_out, float * gate_out, float * q_idx_out, float * k_out, float * v_out, float * kidx_out) {
+    const int64_t hd = d->head_dim, nh = d->n_head, nkv = d->n_head_kv, H = d->idx_n_head, D = d->idx_dim;
+    auto dot = [&](const uint16_t * w, const float * xb) {
+        double acc = 0.0;
+        for (int64_t e = 0; e < n_embd; e++) acc += (double) (bf16_to_f32(w[e]) * xb[e]);
+        return (float) acc;
+    };
+    #pragma omp parallel for schedule(static) if (T > 1)
+    for (int64_t t = 0; t < T; t++) {
+        std::vector<float> xb(n_embd), v(hd);
+        for (int64_t e = 0; e < n_embd; e++) xb[e] = bf16_to_f32(f32_to_bf16(x[t * n_embd + e]));
+        const float p = (float) pos[t];
+        for (int64_t h = 0; h < nh; h++) {
+            for (int64_t e = 0; e < hd; e++) v[e] = dot(wq + (2 * h * hd + e) * n_embd, xb.data());
+            orc_norm_rope(d, v.data(), hd, q_norm, p);
+            std::memcpy(q_out + (t * nh + h) * hd, v.data(), (size_t) hd * 4);
+            for (int64_t e = 0; e < hd; e++) gate_out[(t * nh + h) * hd + e] = dot(wq + ((2 * h + 1) * hd + e) * n_embd, xb.data());
+        }
+        for (int64_t j = 0; j < nkv; j++) {
+            for (int64_t e = 0; e < hd; e++) v[e] = dot(wk + (j * hd + e) * n_embd, xb.data());
+            orc_norm_rope(d, v.data(), hd, k_norm, p);
+            std::memcpy(k_out + (t * nkv + j) * hd, v.data(), (size_t) hd * 4);
+            for (int64_t e = 0; e < hd; e++) v_out[(t * nkv + j) * hd + e] = dot(wv + (j * hd + e) * n_embd, xb.data());
+        }
+        std::vector<float> qi(D);
+        for (int64_t h = 0; h < H; h++) {
+            for (int64_t e = 0; e < D; e++) qi[e] = dot(wq_idx + (h * D + e) * n_embd, xb.data());
+            orc_norm_rope(d, qi.data(), D, q_idx_norm, p);
+            std::memcpy(q_idx_out + (t * H + h) * D, qi.data(), (size_t) D * 4);
+        }
+        for (int64_t e = 0; e < D; e++) kidx_out[t * D + e] = dot(wk_idx + e * n_embd, xb.data());
+    }
 }
 
 }  // extern "C"

@@ -51,6 +51,14 @@ class QsaDecodeItem(ctypes.Structure):
                 ("reserved", ctypes.c_int32 * 3)]
 
 
+class QsaFrontWeights(ctypes.Structure):
+    """struct qsa_front_weights (include/qsa.h)."""
+    _fields_ = [("wq", ctypes.c_void_p), ("wk", ctypes.c_void_p), ("wv", ctypes.c_void_p),
+                ("wq_idx", ctypes.c_void_p), ("wk_idx", ctypes.c_void_p),
+                ("q_norm", ctypes.c_void_p), ("k_norm", ctypes.c_void_p), ("q_idx_norm", ctypes.c_void_p),
+                ("n_embd", ctypes.c_int32), ("w_type", ctypes.c_int32)]
+
+
 def make_desc(n_head=16, n_head_kv=2, head_dim=256, idx_n_head=1, idx_dim=128, ratio=64,
               top_k_blocks=64, window=128, n_ctx=4096, type_k=TYPE_Q8_0, type_v=TYPE_Q8_0,
               rope_dim=64, sections=(11, 11, 10, 0), rms_eps=1e-6, rope_freq_base=1e7,
@@ -134,6 +142,8 @@ def lib() -> ctypes.CDLL:
         "qsa_prefill": (I32, [D, C, I32, I32, VP, I32, VP, VP, VP, VP, VP, VP, VP, SZ, VP]),
         "qsa_check": (I32, [VP, SZ, VP]),
         "qsa_stage_copy": (I32, [VP, VP, SZ, VP]),
+        "qsa_front_workspace_size": (SZ, [D, P(QsaFrontWeights), I32]),
+        "qsa_front": (I32, [D, P(QsaFrontWeights), I32, VP, VP, VP, VP, VP, VP, VP, VP, VP, SZ, VP]),
         "qsa_version": (I32, []),
     }
     for name, (res, args) in sigs.items():
@@ -157,5 +167,6 @@ HEADER_SYMBOLS = [
     "qsa_shard_append_ri", "qsa_shard_decode_ri",
     "qsa_merge_states",
     "qsa_ipc_handle", "qsa_ipc_open", "qsa_ipc_close", "qsa_peer_buffer_bytes", "qsa_peer_push", "qsa_peer_wait",
-    "qsa_prefill_workspace_size", "qsa_prefill", "qsa_stage_copy", "qsa_check", "qsa_version",
+    "qsa_prefill_workspace_size", "qsa_prefill", "qsa_front_workspace_size", "qsa_front", "qsa_stage_copy",
+    "qsa_check", "qsa_version",
 ]

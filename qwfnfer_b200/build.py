@@ -17,7 +17,7 @@ import sys
 PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
-SOURCES = ["qsa_api.cu", "qsa_append.cu", "qsa_select.cu", "qsa_attn.cu", "qsa_shard.cu", "qsa_prefill_tc.cu", "qsa_prefill_attn.cu", "qsa_peer.cu", "qsa_static_ws.cu", "qsa_stage.cu"]
+SOURCES = ["qsa_api.cu", "qsa_append.cu", "qsa_select.cu", "qsa_attn.cu", "qsa_shard.cu", "qsa_prefill_tc.cu", "qsa_prefill_attn.cu", "qsa_peer.cu", "qsa_static_ws.cu", "qsa_stage.cu", "qsa_front.cu"]
 OUT = os.path.join(PKG, "libqsa.so")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -82,3 +82,27 @@ def token_inputs(d: QsaDesc, n: int, seed: int, q_dtype=torch.bfloat16, device="
     v = torch.randn(n, kv_dim, generator=g, device=device)
     ki = torch.randn(n, d.idx_dim, generator=g, device=device) * IDX_STD
     return q, q_idx, k, v, ki
+
+
+N_EMBD = 2560     # model width of the synthetic projection weights
+
+
+def front_weights(d: QsaDesc, n_embd: int = N_EMBD, seed: int = 0, gammas: bool = False, device="cuda") -> dict:
+    """Synthetic weights of the projection front (qsa_front): bf16 ~ N(0, 0.02) row-major
+    [out][n_embd] for attn_q (query and gate interleaved per head), attn_k, attn_v,
+    indexer.q_proj, indexer.k_proj; f32 norm weights, 1 (the stand-in) or with gammas=True
+    ~ 1 + N(0, 0.1) to exercise the multiply."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    hd = d.head_dim
+
+    def w(rows):
+        return (torch.randn(rows, n_embd, generator=g, device=device) * 0.02).to(torch.bfloat16)
+
+    def gamma(n):
+        if not gammas:
+            return torch.ones(n, device=device)
+        return 1.0 + 0.1 * torch.randn(n, generator=g, device=device)
+
+    return {"wq": w(2 * hd * d.n_head), "wk": w(hd * d.n_head_kv), "wv": w(hd * d.n_head_kv),
+            "wq_idx": w(d.idx_dim * d.idx_n_head), "wk_idx": w(d.idx_dim),
+            "q_norm": gamma(hd), "k_norm": gamma(hd), "q_idx_norm": gamma(d.idx_dim)}

@@ -154,6 +154,8 @@ size_t decode_workspace_zero_prefix(const qsa_desc * d, int32_t batch, int32_t m
     return ws_layout(make_dev(d), batch, max_n_kv).scores;
 }
 
+DevDesc dev_desc(const qsa_desc * d) { return make_dev(d); }
+
 }  // namespace qsa
 
 using namespace qsa;

@@ -1,0 +1,364 @@
+// qsa_front.cu -- the projections feeding the sparse-attention node, their norms and IMRoPE.
+//
+// Reference (graph_builder::sparse_attn_decode, src/qwfn_graph.cpp): indexer.k_proj (:465),
+// indexer.q_proj + indexer.q_norm + rope (:479-484), attn_q with query and gate interleaved per
+// head + attn_q_norm (:505-510), attn_k + attn_k_norm and attn_v (:512-514), rope of Q and K
+// (:515-518); the prefill graph builds the same nodes (:324-347).  ggml_mul_mat over bf16 weights
+// converts the f32 activations to bf16 and accumulates the products in f32; rms() is
+// ggml_rms_norm over each head followed by the weight multiply (:114-115).
+//
+// At decode batch sizes this is a matrix-vector product over the layer's projection weights
+// (about 48 MB at n_embd 2560): HBM-bound, one pass over the weights per group of 4 tokens.
+//   - every CTA owns 32 consecutive rows of one head group (a query+gate head: 512 rows, a K or V
+//     head: 256, an indexer query head or the raw indexer key: 128), two CTAs per SM; its 8 warps
+//     take 4 rows each and stream the bf16 weights with 16-byte evict-first loads, the next row's
+//     loads issued before the current row's products (two rows in flight per warp, ~160 KB per
+//     SM); the tokens' activations sit in shared memory as f32 of their bf16 values;
+//   - each row's per-token sums (warp-shuffle reduced, a fixed order) go to the workspace; the
+//     last CTA of a head group to arrive (an acq_rel counter) normalises the head, applies IMRoPE
+//     with the pooled key's angle recurrence, and writes the outputs.
+#include "qsa_kernels.cuh"
+
+namespace qsa {
+namespace {
+
+constexpr int FR_THREADS = 256;
+constexpr int FR_ROWS    = 32;             // rows per CTA (4 per warp)
+constexpr int FR_TOK     = 4;              // tokens per launch
+constexpr int FR_UNROLL  = 10;             // 16-byte weight pieces per lane and pass (2560 columns a pass)
+constexpr int FR_MAX_EMBD = 12288;          // FR_TOK tokens of activations: 192 KB of shared memory
+constexpr int FR_KINDS   = 5;              // query+gate, K, V, indexer query, raw indexer key
+
+struct FrontArgs {
+    const uint16_t * w[FR_KINDS];          // bf16 weights of each kind, row-major [rows][n_embd]
+    const float * norm[3];                 // q_norm, k_norm, q_idx_norm (may be null)
+    const int * pos;                       // [T]
+    const float * x;                       // [T][n_embd]
+    float * q_out; float * gate_out; float * q_idx_out; float * k_out; float * v_out; float * kidx_out;
+    float * y;                             // workspace: [FR_TOK][rows_total]
+    unsigned * counters;                   // one per head group
+    int n_embd, T, rows_total;
+};
+
+struct FrontShape {                        // rows per group, groups and CTAs per group of each kind
+    int group_rows[FR_KINDS], groups[FR_KINDS], row0[FR_KINDS], gid0[FR_KINDS];
+    int ctas, n_groups;
+};
+
+__host__ __device__ inline FrontShape front_shape(const DevDesc & d) {
+    FrontShape s;
+    const int rows[FR_KINDS] = {2 * HEAD_DIM, HEAD_DIM, HEAD_DIM, MAX_IDX_DIM, MAX_IDX_DIM};
+    const int groups[FR_KINDS] = {d.n_head, d.n_head_kv, d.n_head_kv, d.idx_n_head, 1};
+    int r = 0, g = 0, c = 0;
+    for (int k = 0; k < FR_KINDS; k++) {
+        s.group_rows[k] = rows[k];
+        s.groups[k] = groups[k];
+        s.row0[k] = r;
+        s.gid0[k] = g;
+        r += rows[k] * groups[k];
+        g += groups[k];
+        c += groups[k] * (rows[k] / FR_ROWS);
+    }
+    s.ctas = c;
+    s.n_groups = g;
+    return s;
+}
+
+// cos/sin of the IMRoPE angle of pair i at position `pos`: the pooled key's arithmetic (the angle
+// advanced from pos by f32 multiplies by theta_scale, the 4th section at position 0; cos/sin of
+// that f32 angle by a reduction by 2*pi split into two doubles and sincos of the reduced double,
+// rounded once to f32).
+__device__ __forceinline__ float2 rope_cs(const DevDesc & d, float pos, int i) {
+    const int sect_dims = d.sections[0] + d.sections[1] + d.sections[2] + d.sections[3];
+    float th = pos;
+    for (int k = 0; k < i; k++) th = __fmul_rn(th, d.theta_scale);
+    const int sector = i % sect_dims;
+    const bool use_pos = (sector % 3 == 1 && sector < 3 * d.sections[1]) ||
+                         (sector % 3 == 2 && sector < 3 * d.sections[2]) ||
+                         (sector % 3 == 0 && sector < 3 * d.sections[0]);
+    if (!use_pos) th = 0.0f;
+    const double td = (double) th;
+    const double k = rint(td * 0.15915494309189535);
+    double rr = fma(-k, 6.283185307179586, td);
+    rr = fma(-k, 2.4492935982947064e-16, rr);
+    double sd, cd;
+    sincos(rr, &sd, &cd);
+    return make_float2((float) cd, (float) sd);
+}
+
+// rms_norm over the warp's D = 32*EPL values (element e of lane l is dim EPL*l + e), times the
+// norm weight (the f32 squares summed in double, 1/sqrtf in f32), then IMRoPE with the pair
+// table cs[i] = (cos, sin): pair i rotates dims (i, i + rope_dim/2); rope_dim/2 is a multiple of EPL.
+template <int EPL>
+__device__ __forceinline__ void norm_rope_warp(const DevDesc & d, float (&x)[EPL], const float * __restrict__ w,
+                                               const float2 * __restrict__ cs, int lane) {
+    constexpr int D = 32 * EPL;
+    double ss = 0.0;
+    #pragma unroll
+    for (int e = 0; e < EPL; e++) ss += (double) __fmul_rn(x[e], x[e]);
+    #pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float mean  = (float) (ss / (double) D);
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, d.rms_eps)));
+    #pragma unroll
+    for (int e = 0; e < EPL; e++) {
+        x[e] = __fmul_rn(x[e], scale);
+        if (w) x[e] = __fmul_rn(x[e], w[EPL * lane + e]);
+    }
+    const int half = d.rope_dim / 2, lane_off = half / EPL;
+    float y[EPL];
+    #pragma unroll
+    for (int e = 0; e < EPL; e++) {
+        const int dim = EPL * lane + e;
+        const bool first = dim < half, second = dim >= half && dim < d.rope_dim;
+        const float partner = __shfl_sync(0xffffffffu, x[e], first ? lane + lane_off : (lane - lane_off) & 31);
+        y[e] = x[e];
+        if (first || second) {
+            const float2 c = cs[first ? dim : dim - half];
+            if (first) y[e] = __fsub_rn(__fmul_rn(x[e], c.x), __fmul_rn(partner, c.y));    // x0*c - x1*s
+            else       y[e] = __fadd_rn(__fmul_rn(partner, c.y), __fmul_rn(x[e], c.x));    // x0*s + x1*c
+        }
+    }
+    #pragma unroll
+    for (int e = 0; e < EPL; e++) x[e] = y[e];
+}
+
+__device__ __forceinline__ uint4 ld_stream(const uint4 * p) {
+    uint4 v;
+    asm volatile("ld.global.cs.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+
+template <int EPL>
+__device__ __forceinline__ void load_head(const float * __restrict__ src, float (&x)[EPL], int lane) {
+    #pragma unroll
+    for (int e = 0; e < EPL; e += 4) {
+        const float4 v = __ldcg(reinterpret_cast<const float4 *>(src + EPL * lane + e));
+        x[e] = v.x; x[e + 1] = v.y; x[e + 2] = v.z; x[e + 3] = v.w;
+    }
+}
+
+template <int EPL>
+__device__ __forceinline__ void store_head(float * __restrict__ dst, const float (&x)[EPL], int lane) {
+    #pragma unroll
+    for (int e = 0; e < EPL; e += 4)
+        *reinterpret_cast<float4 *>(dst + EPL * lane + e) = make_float4(x[e], x[e + 1], x[e + 2], x[e + 3]);
+}
+
+__global__ void __launch_bounds__(FR_THREADS, 2) front_kernel(DevDesc d, FrontArgs a) {
+    extern __shared__ __align__(16) float xs[];                 // [T][n_embd]
+    __shared__ bool is_last;
+    const FrontShape sh = front_shape(d);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    // this CTA's kind, head group and 64-row chunk
+    int kind = 0, c = blockIdx.x;
+    while (kind < FR_KINDS - 1 && c >= sh.groups[kind] * (sh.group_rows[kind] / FR_ROWS)) {
+        c -= sh.groups[kind] * (sh.group_rows[kind] / FR_ROWS);
+        kind++;
+    }
+    const int chunks = sh.group_rows[kind] / FR_ROWS;
+    const int g = c / chunks, chunk = c % chunks;
+    const int row_in_kind = g * sh.group_rows[kind] + chunk * FR_ROWS;
+    const int T = a.T, n = a.n_embd, n16 = n / 8;
+
+
+    // the warp's rows x passes over the columns, one after another; the next item's weight loads
+    // are issued before the current item's products
+    constexpr int WROWS = FR_ROWS / 8;
+    const int passes = (n16 + 32 * FR_UNROLL - 1) / (32 * FR_UNROLL);
+    const int items = WROWS * passes;
+    const uint16_t * wwarp = a.w[kind] + (size_t) (row_in_kind + warp * WROWS) * n;
+    auto load = [&](int it, uint4 (&v)[FR_UNROLL]) {
+        const uint4 * wr = reinterpret_cast<const uint4 *>(wwarp + (size_t) (it / passes) * n);
+        const int base = (it % passes) * 32 * FR_UNROLL + lane;
+        #pragma unroll
+        for (int u = 0; u < FR_UNROLL; u++) {
+            const int i = base + u * 32;
+            v[u] = i < n16 ? ld_stream(wr + i) : make_uint4(0u, 0u, 0u, 0u);
+        }
+    };
+    uint4 cur[FR_UNROLL], nxt[FR_UNROLL];
+    float acc[FR_TOK];
+    #pragma unroll
+    for (int t = 0; t < FR_TOK; t++) acc[t] = 0.0f;
+    // the activations go to shared memory by cp.async ahead of the first weight loads; each thread
+    // then rounds the pieces it copied to bf16 values in place
+    for (int i = tid; i < T * n / 4; i += FR_THREADS)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(smem_u32(xs + 4 * i)), "l"(a.x + 4 * i) : "memory");
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    load(0, cur);
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    for (int i = tid; i < T * n / 4; i += FR_THREADS) {
+        float4 v = reinterpret_cast<float4 *>(xs)[i];
+        v.x = __bfloat162float(__float2bfloat16_rn(v.x)); v.y = __bfloat162float(__float2bfloat16_rn(v.y));
+        v.z = __bfloat162float(__float2bfloat16_rn(v.z)); v.w = __bfloat162float(__float2bfloat16_rn(v.w));
+        reinterpret_cast<float4 *>(xs)[i] = v;
+    }
+    __syncthreads();
+    for (int it = 0; it < items; it++) {
+        if (it + 1 < items) load(it + 1, nxt);
+        const int base = (it % passes) * 32 * FR_UNROLL + lane;
+        #pragma unroll
+        for (int u = 0; u < FR_UNROLL; u++) {
+            const int i = base + u * 32;
+            if (i >= n16) break;
+            const uint32_t p[4] = {cur[u].x, cur[u].y, cur[u].z, cur[u].w};
+            float wf[8];
+            #pragma unroll
+            for (int k = 0; k < 4; k++) {
+                wf[2 * k]     = __uint_as_float(p[k] << 16);
+                wf[2 * k + 1] = __uint_as_float(p[k] & 0xffff0000u);
+            }
+            #pragma unroll
+            for (int t = 0; t < FR_TOK; t++) {
+                if (t >= T) break;
+                const float4 x0 = *reinterpret_cast<const float4 *>(xs + (size_t) t * n + 8 * i);
+                const float4 x1 = *reinterpret_cast<const float4 *>(xs + (size_t) t * n + 8 * i + 4);
+                float s = acc[t];
+                s = fmaf(wf[0], x0.x, s); s = fmaf(wf[1], x0.y, s); s = fmaf(wf[2], x0.z, s); s = fmaf(wf[3], x0.w, s);
+                s = fmaf(wf[4], x1.x, s); s = fmaf(wf[5], x1.y, s); s = fmaf(wf[6], x1.z, s); s = fmaf(wf[7], x1.w, s);
+                acc[t] = s;
+            }
+        }
+        if (it % passes == passes - 1) {                        // the row is complete
+            const int row = warp * WROWS + it / passes;
+            #pragma unroll
+            for (int t = 0; t < FR_TOK; t++) {
+                float s = acc[t];
+                #pragma unroll
+                for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+                if (lane == 0 && t < T) a.y[(size_t) t * a.rows_total + sh.row0[kind] + row_in_kind + row] = s;
+                acc[t] = 0.0f;
+            }
+        }
+        #pragma unroll
+        for (int u = 0; u < FR_UNROLL; u++) cur[u] = nxt[u];
+    }
+
+    // Arrival: the last CTA of the head group finishes it.  The barrier orders the CTA's row
+    // stores before thread 0's release; its acquire orders the other CTAs' stores before our reads.
+    __syncthreads();
+    const int gid = sh.gid0[kind] + g;
+    if (tid == 0) {
+        unsigned prev;
+        asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], 1;" : "=r"(prev) : "l"(a.counters + gid) : "memory");
+        is_last = prev == (unsigned) chunks - 1;
+        if (is_last) a.counters[gid] = 0;                      // leave the counter at zero for the next call
+    }
+    __syncthreads();
+    if (!is_last) return;
+    // the (cos, sin) of every rotated pair of every token, computed by the whole CTA
+    __shared__ float2 cs_tab[FR_TOK][128];
+    const int half = d.rope_dim / 2;
+    for (int e = tid; e < T * half; e += FR_THREADS)
+        cs_tab[e / half][e % half] = rope_cs(d, (float) a.pos[e / half], e % half);
+    __syncthreads();
+    const int t = warp & 3;                                     // warps 0-3: token t; warps 4-7: token t's gate
+    if (t >= T) return;
+    const float * yh = a.y + (size_t) t * a.rows_total + sh.row0[kind] + g * sh.group_rows[kind];
+    if (kind == 0) {                                            // query (normed, roped) + gate (raw)
+        float x[8];
+        if (warp < 4) {
+            load_head<8>(yh, x, lane);
+            norm_rope_warp<8>(d, x, a.norm[0], cs_tab[t], lane);
+            store_head<8>(a.q_out + ((size_t) t * d.n_head + g) * HEAD_DIM, x, lane);
+        } else {
+            load_head<8>(yh + HEAD_DIM, x, lane);
+            store_head<8>(a.gate_out + ((size_t) t * d.n_head + g) * HEAD_DIM, x, lane);
+        }
+    } else if (warp >= 4) {
+        return;
+    } else if (kind == 1 || kind == 2) {                        // K (normed, roped) or V (raw)
+        float x[8];
+        load_head<8>(yh, x, lane);
+        if (kind == 1) norm_rope_warp<8>(d, x, a.norm[1], cs_tab[t], lane);
+        store_head<8>((kind == 1 ? a.k_out : a.v_out) + ((size_t) t * d.n_head_kv + g) * HEAD_DIM, x, lane);
+    } else if (kind == 3) {                                     // indexer query (normed, roped)
+        float x[4];
+        load_head<4>(yh, x, lane);
+        norm_rope_warp<4>(d, x, a.norm[2], cs_tab[t], lane);
+        store_head<4>(a.q_idx_out + ((size_t) t * d.idx_n_head + g) * MAX_IDX_DIM, x, lane);
+    } else {                                                    // raw indexer key
+        float x[4];
+        load_head<4>(yh, x, lane);
+        store_head<4>(a.kidx_out + (size_t) t * MAX_IDX_DIM, x, lane);
+    }
+}
+
+struct FrontWs { size_t counters, y, total; };
+
+FrontWs front_ws(const DevDesc & d) {
+    const FrontShape sh = front_shape(d);
+    const int rows = sh.row0[FR_KINDS - 1] + MAX_IDX_DIM;
+    FrontWs w;
+    w.counters = 0;
+    w.y = ((size_t) sh.n_groups * 4 + 255) & ~(size_t) 255;
+    w.total = w.y + (size_t) FR_TOK * rows * 4;
+    return w;
+}
+
+bool aligned16(const void * p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+}  // namespace qsa
+
+using namespace qsa;
+
+extern "C" size_t qsa_front_workspace_size(const qsa_desc * dd, const qsa_front_weights * w, int32_t T) {
+    if (qsa_desc_check(dd) != QSA_OK || !w || T <= 0) return 0;
+    return front_ws(dev_desc(dd)).total;
+}
+
+extern "C" qsa_status qsa_front(const qsa_desc * dd, const qsa_front_weights * w, int32_t T, const int32_t * pos,
+                                const float * x, float * q_out, float * gate_out, float * q_idx_out,
+                                float * k_out, float * v_out, float * kidx_out,
+                                void * ws, size_t ws_bytes, qsa_stream_t stream) {
+    qsa_status s = qsa_desc_check(dd);
+    if (s != QSA_OK) return s;
+    if (!w || T <= 0 || !pos || !x || !q_out || !gate_out || !q_idx_out || !k_out || !v_out || !kidx_out)
+        return QSA_ERR_INVALID;
+    if (!w->wq || !w->wk || !w->wv || !w->wq_idx || !w->wk_idx) return QSA_ERR_INVALID;
+    if (w->w_type != QSA_TYPE_BF16) return QSA_ERR_UNSUPPORTED;
+    if (w->n_embd <= 0 || w->n_embd % 8 != 0 || w->n_embd > FR_MAX_EMBD) return QSA_ERR_UNSUPPORTED;
+    if (dd->rope_dim % 16 != 0) return QSA_ERR_UNSUPPORTED;          // pairs at a lane distance for 8 values a lane
+    const void * ptrs[] = {w->wq, w->wk, w->wv, w->wq_idx, w->wk_idx, x, q_out, gate_out, q_idx_out, k_out, v_out, kidx_out};
+    for (const void * p : ptrs)
+        if (!aligned16(p)) return QSA_ERR_INVALID;
+    const DevDesc d = dev_desc(dd);
+    const FrontWs L = front_ws(d);
+    if (!ws || ws_bytes < L.total) return QSA_ERR_WORKSPACE;
+    static std::atomic<uint64_t> attr{0};
+    cudaError_t e = once_per_device(attr, [] {
+        return cudaFuncSetAttribute(front_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FR_TOK * FR_MAX_EMBD * 4);
+    });
+    if (e != cudaSuccess) return QSA_ERR_CUDA;
+    const FrontShape sh = front_shape(d);
+    unsigned char * wsb = static_cast<unsigned char *>(ws);
+    FrontArgs a{};
+    a.w[0] = static_cast<const uint16_t *>(w->wq);
+    a.w[1] = static_cast<const uint16_t *>(w->wk);
+    a.w[2] = static_cast<const uint16_t *>(w->wv);
+    a.w[3] = static_cast<const uint16_t *>(w->wq_idx);
+    a.w[4] = static_cast<const uint16_t *>(w->wk_idx);
+    a.norm[0] = w->q_norm; a.norm[1] = w->k_norm; a.norm[2] = w->q_idx_norm;
+    a.counters = reinterpret_cast<unsigned *>(wsb + L.counters);
+    a.y = reinterpret_cast<float *>(wsb + L.y);
+    a.n_embd = w->n_embd;
+    a.rows_total = sh.row0[FR_KINDS - 1] + MAX_IDX_DIM;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const size_t kv = (size_t) d.n_head_kv * HEAD_DIM;
+    for (int t0 = 0; t0 < T; t0 += FR_TOK) {                   // token groups run one after another on the stream
+        a.T = std::min(FR_TOK, T - t0);
+        a.pos = pos + t0;
+        a.x = x + (size_t) t0 * w->n_embd;
+        a.q_out = q_out + (size_t) t0 * d.n_head * HEAD_DIM;
+        a.gate_out = gate_out + (size_t) t0 * d.n_head * HEAD_DIM;
+        a.q_idx_out = q_idx_out + (size_t) t0 * d.idx_n_head * MAX_IDX_DIM;
+        a.k_out = k_out + t0 * kv;
+        a.v_out = v_out + t0 * kv;
+        a.kidx_out = kidx_out + (size_t) t0 * MAX_IDX_DIM;
+        front_kernel<<<sh.ctas, FR_THREADS, (size_t) a.T * w->n_embd * 4, st>>>(d, a);
+        if ((e = cudaGetLastError()) != cudaSuccess) return QSA_ERR_CUDA;
+    }
+    return QSA_OK;
+}

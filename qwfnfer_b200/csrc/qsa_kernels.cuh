@@ -41,6 +41,8 @@ __global__ void score_select_kernel(DevDesc d, const qsa_decode_item * items, co
 
 // Leading bytes of a decode workspace that must be zero before a call (status word + counters).
 size_t decode_workspace_zero_prefix(const qsa_desc * d, int32_t batch, int32_t max_n_kv);
+// The kernels' view of a descriptor that passed qsa_desc_check (derived values filled in).
+DevDesc dev_desc(const qsa_desc * d);
 
 // Host launcher of the attention kernel and, when a query spans several CTAs (max_chunks > 1),
 // of the merge of their partials (defined beside the kernels).

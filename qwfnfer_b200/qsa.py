@@ -8,6 +8,8 @@ Names follow the reference so that callers and tests read like it:
   QsaNode.qsa_pool_rebuild     graph_builder::qsa_pool_rebuild (src/qwfn_graph.cpp:431-448)
   QsaDecodeStep      one captured decode step per token, as the engine computes one graph per step
                      (src/qwfn_engine.cpp:814)
+  QsaFront           the projections, norms and IMRoPE feeding the node (src/qwfn_graph.cpp:465,
+                     479-484, 505-518)
 Errors raise QsaError carrying the qsa_status (the reference aborts; the library never does).
 PyTorch provides device memory and streams only; every computation runs in libqsa.so.
 """
@@ -18,8 +20,8 @@ import ctypes
 import torch
 
 from . import _abi
-from ._abi import (QsaDecodeItem, QsaDesc, QsaError, QsaLayerCache, TYPE_BF16, TYPE_F32, check, k_blocks,
-                   lib, row_bytes)
+from ._abi import (QsaDecodeItem, QsaDesc, QsaError, QsaFrontWeights, QsaLayerCache, TYPE_BF16, TYPE_F32, check,
+                   k_blocks, lib, row_bytes)
 
 
 def _ptr(t: torch.Tensor | None) -> int | None:
@@ -248,3 +250,56 @@ class QsaDecodeStep:
         if sync:
             self.done.synchronize()
         return self.host_out
+
+
+class QsaFront:
+    """The projections feeding the node of one layer (qsa_front): bf16 weights, row-major
+    [out][n_embd] as ggml holds them (attn_q with query and gate interleaved per head, attn_k,
+    attn_v, indexer.q_proj, indexer.k_proj) and the f32 norm weights.  project() returns
+    qsa_decode's inputs: q (f32, QSA_TYPE_F32), q_idx, k_new, v_new, kidx_new, and the gate."""
+
+    def __init__(self, desc: QsaDesc, wq: torch.Tensor, wk: torch.Tensor, wv: torch.Tensor, wq_idx: torch.Tensor,
+                 wk_idx: torch.Tensor, q_norm: torch.Tensor | None = None, k_norm: torch.Tensor | None = None,
+                 q_idx_norm: torch.Tensor | None = None):
+        for t in (wq, wk, wv, wq_idx, wk_idx):
+            if t.dtype != torch.bfloat16 or t.dim() != 2 or t.shape[1] != wq.shape[1]:
+                raise QsaError(_abi.QSA_ERR_INVALID, "front weights: bf16 [out][n_embd]")
+        for t in (q_norm, k_norm, q_idx_norm):
+            if t is not None and t.dtype != torch.float32:
+                raise QsaError(_abi.QSA_ERR_INVALID, "front norm weights: f32")
+        self.desc, self.device, self.n_embd = desc, wq.device, int(wq.shape[1])
+        self._keep = (wq, wk, wv, wq_idx, wk_idx, q_norm, k_norm, q_idx_norm)
+        w = QsaFrontWeights()
+        w.wq, w.wk, w.wv, w.wq_idx, w.wk_idx = (_ptr(t) for t in (wq, wk, wv, wq_idx, wk_idx))
+        w.q_norm, w.k_norm, w.q_idx_norm = (_ptr(t) for t in (q_norm, k_norm, q_idx_norm))
+        w.n_embd, w.w_type = self.n_embd, TYPE_BF16
+        self.w = w
+        self._ws: torch.Tensor | None = None
+
+    def workspace(self, T: int, stream=None) -> torch.Tensor:
+        size = lib().qsa_front_workspace_size(ctypes.byref(self.desc), ctypes.byref(self.w), T)
+        if size == 0:
+            raise QsaError(_abi.QSA_ERR_INVALID, "qsa_front_workspace_size")
+        if self._ws is None or self._ws.numel() < size:
+            self._ws = torch.empty(size, dtype=torch.uint8, device=self.device)
+            check(lib().qsa_workspace_init(self._ws.data_ptr(), size, _stream(stream)), "qsa_workspace_init")
+        return self._ws
+
+    def project(self, x: torch.Tensor, pos: torch.Tensor, stream=None):
+        """x f32 [T][n_embd], pos int32 [T] (device) -> (q, gate, q_idx, k, v, kidx) f32."""
+        d = self.desc
+        T = x.shape[0]
+        if x.dtype != torch.float32 or x.shape[1] != self.n_embd or pos.dtype != torch.int32 or pos.numel() != T:
+            raise QsaError(_abi.QSA_ERR_INVALID, "front inputs: x f32 [T][n_embd], pos int32 [T]")
+        f = dict(dtype=torch.float32, device=self.device)
+        kv = d.n_head_kv * d.head_dim
+        q = torch.empty((T, d.n_head, d.head_dim), **f)
+        gate = torch.empty((T, d.n_head * d.head_dim), **f)
+        q_idx = torch.empty((T, d.idx_n_head, d.idx_dim), **f)
+        k, v = torch.empty((T, kv), **f), torch.empty((T, kv), **f)
+        kidx = torch.empty((T, d.idx_dim), **f)
+        ws = self.workspace(T, stream)
+        check(lib().qsa_front(ctypes.byref(d), ctypes.byref(self.w), T, _ptr(pos), _ptr(x), _ptr(q), _ptr(gate),
+                              _ptr(q_idx), _ptr(k), _ptr(v), _ptr(kidx), ws.data_ptr(), ws.numel(), _stream(stream)),
+              "qsa_front")
+        return q, gate, q_idx, k, v, kidx

@@ -1,0 +1,112 @@
+"""The oracle's projection front (orc_front) on the CPU: against an independent numpy restatement,
+and pinned to the pooled-key path (orc_pool_blocks), whose norm and IMRoPE the front shares.
+
+The numpy restatement keeps ggml's f32 angle recurrence (theta advanced by f32 multiplies, which
+at positions near 160K moves the angle far from the exact value) and does the rest in float64."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from qwfnfer_b200._abi import make_desc
+
+
+def bf16_bits(a: np.ndarray) -> np.ndarray:
+    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+
+
+def bits_to_f64(b: np.ndarray) -> np.ndarray:
+    return (b.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+
+
+def weights(d, n_embd, seed):
+    rng = np.random.default_rng(seed)
+    hd = d.head_dim
+
+    def w(rows):
+        return bf16_bits(rng.standard_normal((rows, n_embd), dtype=np.float32) * 0.02)
+
+    return {"wq": w(2 * hd * d.n_head), "wk": w(hd * d.n_head_kv), "wv": w(hd * d.n_head_kv),
+            "wq_idx": w(d.idx_dim * d.idx_n_head), "wk_idx": w(d.idx_dim),
+            "q_norm": (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32),
+            "k_norm": (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32),
+            "q_idx_norm": (1 + 0.1 * rng.standard_normal(d.idx_dim)).astype(np.float32)}
+
+
+def np_norm_rope(d, v, w, pos):
+    """rms_norm * w, then IMRoPE with ggml's f32 angle chain (cos/sin in float64 of that angle)."""
+    y = v / np.sqrt(np.mean(v * v) + np.float64(np.float32(d.rms_eps))) * w.astype(np.float64)
+    nd, half = d.rope_dim, d.rope_dim // 2
+    ts = np.float32(np.power(np.float32(d.rope_freq_base), np.float32(-2.0 / nd)))
+    s = list(d.sections)
+    sect = sum(s)
+    out = y.copy()
+    th = np.float32(pos)
+    for i in range(half):
+        sec = i % sect
+        use = (sec % 3 == 1 and sec < 3 * s[1]) or (sec % 3 == 2 and sec < 3 * s[2]) or (sec % 3 == 0 and sec < 3 * s[0])
+        a = float(th) if use else 0.0
+        c, sn = np.cos(a), np.sin(a)
+        out[i] = y[i] * c - y[i + half] * sn
+        out[i + half] = y[i] * sn + y[i + half] * c
+        th = np.float32(th * ts)
+    return out
+
+
+def np_front(d, w, pos, x):
+    hd, nh, nkv, H, D = d.head_dim, d.n_head, d.n_head_kv, d.idx_n_head, d.idx_dim
+    xb = bits_to_f64(bf16_bits(x))
+    y = {k: xb @ bits_to_f64(w[k]).T for k in ("wq", "wk", "wv", "wq_idx", "wk_idx")}
+    T = x.shape[0]
+    out = {"q": np.zeros((T, nh, hd)), "gate": np.zeros((T, nh * hd)), "q_idx": np.zeros((T, H, D)),
+           "k": np.zeros((T, nkv * hd)), "v": y["wv"], "kidx": y["wk_idx"]}
+    for t in range(T):
+        for h in range(nh):
+            out["q"][t, h] = np_norm_rope(d, y["wq"][t, 2 * h * hd:2 * h * hd + hd], w["q_norm"], pos[t])
+            out["gate"][t, h * hd:(h + 1) * hd] = y["wq"][t, (2 * h + 1) * hd:(2 * h + 2) * hd]
+        for j in range(nkv):
+            out["k"][t, j * hd:(j + 1) * hd] = np_norm_rope(d, y["wk"][t, j * hd:(j + 1) * hd], w["k_norm"], pos[t])
+        for h in range(H):
+            out["q_idx"][t, h] = np_norm_rope(d, y["wq_idx"][t, h * D:(h + 1) * D], w["q_idx_norm"], pos[t])
+    return out
+
+
+@pytest.mark.parametrize("idx_n_head,n_embd,positions", [(1, 512, [0, 5, 163839]), (4, 256, [77777, 1048575])])
+def test_oracle_front_matches_numpy(idx_n_head, n_embd, positions):
+    d = make_desc(idx_n_head=idx_n_head, n_ctx=1 << 20)
+    w = weights(d, n_embd, seed=idx_n_head)
+    x = np.random.default_rng(9).standard_normal((len(positions), n_embd), dtype=np.float32)
+    pos = np.array(positions, np.int32)
+    got = oracle.front(d, w, pos, x)
+    ref = np_front(d, w, pos, x)
+    for k in ("gate", "v", "kidx"):                          # projections: one f32 rounding of a double sum
+        assert np.allclose(got[k], ref[k], rtol=1e-6, atol=1e-7 * np.abs(ref[k]).max()), k
+    for k in ("q", "k", "q_idx"):                            # normed and roped
+        err = np.abs(got[k] - ref[k]).max() / np.abs(ref[k]).max()
+        assert err < 2e-6, (k, err)
+
+
+@pytest.mark.parametrize("b", [0, 5, 2000])
+def test_front_norm_rope_is_the_pooled_keys(b):
+    """One-hot activations and indexer-query weights holding a vector u (exact in bf16 and f16)
+    give q_idx = norm-rope(u) at position p; a block whose r raw keys all equal u pools to
+    norm-rope(u) at position b*r.  With p = b*r and q_norm = k_norm the two are bit-equal."""
+    r = 64
+    d = make_desc(n_ctx=(b + 1) * r, idx_n_head=1)
+    rng = np.random.default_rng(b)
+    u = (rng.integers(-32, 33, d.idx_dim) / 8.0).astype(np.float32)
+    gamma = (1 + 0.1 * rng.standard_normal(d.idx_dim)).astype(np.float32)
+    n_embd, j = 64, 13
+    w = weights(d, n_embd, seed=1)
+    wq_idx = np.zeros((d.idx_dim, n_embd), np.float32)
+    wq_idx[:, j] = u
+    w["wq_idx"], w["q_idx_norm"] = bf16_bits(wq_idx), gamma
+    x = np.zeros((1, n_embd), np.float32)
+    x[0, j] = 1.0
+    got = oracle.front(d, w, np.array([b * r], np.int32), x)["q_idx"][0, 0]
+    ic = np.zeros(((b + 1) * r, d.idx_dim), np.uint16)
+    ic[b * r:] = oracle.f32_to_f16(u)[None, :]
+    p32, _ = oracle.pool_blocks(d, ic, b, 1, k_norm_w=gamma)
+    assert np.array_equal(got, p32[0])

@@ -1,0 +1,129 @@
+"""qsa_front (the projections, norms and IMRoPE feeding the node) on a B200 against the CPU oracle,
+pinned to the GPU's own pooled keys, and chained into qsa_decode.
+
+Tolerances: a projection's f32 sum may differ from the oracle's (double sum, one rounding) by the
+f32 accumulation error, bounded here by 1e-5 of the row's sum of |w * x|; the normed and roped
+outputs within 1e-4 of their largest magnitude."""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from qwfnfer_b200._abi import (QSA_ERR_INVALID, QSA_ERR_UNSUPPORTED, QSA_ERR_WORKSPACE, QsaFrontWeights, TYPE_F16,
+                               TYPE_Q8_0, lib, make_desc)
+from qwfnfer_b200.configs import fill_cache, front_weights
+from qwfnfer_b200.qsa import QsaFront, QsaNode, QsaState
+from test_gpu_parity import desc_for, run_decode_case
+
+pytestmark = pytest.mark.gpu
+
+PROJ_TOL = 1e-5      # of the row's sum of |w * x|
+NORMED_TOL = 1e-4    # of the output's largest magnitude
+
+
+def host_weights(w: dict) -> dict:
+    out = {}
+    for k, t in w.items():
+        out[k] = t.view(torch.int16).cpu().numpy().view(np.uint16) if t.dtype == torch.bfloat16 else t.cpu().numpy()
+    return out
+
+
+def abs_row_sums(wt: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+    """[T][rows] sums of |w * bf16(x)| (the scale of a row's rounding error)."""
+    return x.to(torch.bfloat16).float().abs() @ wt.float().abs().T
+
+
+@pytest.mark.parametrize("idx_n_head,T", [(1, 1), (1, 6), (4, 3)])
+def test_front_matches_oracle(idx_n_head, T):
+    d = make_desc(idx_n_head=idx_n_head, n_ctx=1 << 20)
+    w = front_weights(d, seed=11 + T, gammas=True)
+    front = QsaFront(d, **w)
+    g = torch.Generator(device="cuda").manual_seed(12)
+    x = torch.randn(T, front.n_embd, generator=g, device="cuda")
+    pos_list = [163839, 0, 70000, 1048575, 5, 129][:T]
+    pos = torch.tensor(pos_list, dtype=torch.int32, device="cuda")
+    q, gate, q_idx, k, v, kidx = front.project(x, pos)
+    torch.cuda.synchronize()
+    ref = oracle.front(d, host_weights(w), np.array(pos_list, np.int32), x.cpu().numpy())
+    hd = d.head_dim
+    wq_gate = w["wq"].view(d.n_head, 2, hd, -1)[:, 1].reshape(d.n_head * hd, -1)
+    for name, got, wt in (("gate", gate, wq_gate), ("v", v, w["wv"]), ("kidx", kidx, w["wk_idx"])):
+        bound = PROJ_TOL * abs_row_sums(wt, x).cpu().numpy()
+        err = np.abs(got.cpu().numpy() - ref[name])
+        assert np.all(err <= bound + 1e-30), (name, float(err.max()), float(bound.max()))
+    for name, got in (("q", q), ("k", k), ("q_idx", q_idx)):
+        e = np.abs(got.cpu().numpy() - ref[name]).max() / np.abs(ref[name]).max()
+        assert e <= NORMED_TOL, (name, e)
+
+
+@pytest.mark.parametrize("b", [3, 2000])
+def test_front_q_idx_equals_gpu_pooled_key(b):
+    """The front's indexer query of one-hot activations over weights holding u, at position b*r,
+    equals (as f16 bits) the pooled key the append path computes for a block of r raw keys equal to
+    u, with the same norm weight: the two kernels share the norm and IMRoPE arithmetic."""
+    r = 64
+    gamma = (1 + 0.1 * torch.randn(128, generator=torch.Generator().manual_seed(b))).cuda()
+    d = make_desc(n_ctx=(b + 1) * r, idx_n_head=1, k_norm_w=gamma.data_ptr())
+    rng = np.random.default_rng(b)
+    u = torch.from_numpy((rng.integers(-32, 33, d.idx_dim) / 8.0).astype(np.float32)).cuda()
+    node, st = QsaNode(d), QsaState(d)
+    kv = d.n_head_kv * d.head_dim
+    node.append(st.layer(), b * r, torch.zeros(r, kv, device="cuda"), torch.zeros(r, kv, device="cuda"),
+                u[None, :].repeat(r, 1).contiguous())
+    w = front_weights(d, n_embd=64, seed=3)
+    j = 13
+    wq_idx = torch.zeros(d.idx_dim, 64, device="cuda")
+    wq_idx[:, j] = u
+    w["wq_idx"], w["q_idx_norm"] = wq_idx.to(torch.bfloat16), gamma
+    x = torch.zeros(1, 64, device="cuda")
+    x[0, j] = 1.0
+    _, _, q_idx, _, _, _ = QsaFront(d, **w).project(x, torch.tensor([b * r], dtype=torch.int32, device="cuda"))
+    torch.cuda.synchronize()
+    got16 = q_idx[0, 0].cpu().numpy().astype(np.float16).view(np.uint16)
+    pool16 = st.pool[0][b].cpu().numpy().view(np.uint16)
+    assert np.array_equal(got16, pool16)
+
+
+@pytest.mark.parametrize("kv_type,n_past", [(TYPE_Q8_0, 30015), (TYPE_F16, 4095)])
+def test_front_then_decode(kv_type, n_past):
+    """qsa_front's outputs are qsa_decode's inputs as they are: q as QSA_TYPE_F32, the indexer query,
+    the new K/V rows (appended bit-exact) and the raw indexer key; the decode then meets every
+    parity bar against the oracle over the caches it wrote."""
+    d = desc_for(kv_type, 32768)
+    w = front_weights(d, seed=21, gammas=True)
+    x = torch.randn(1, w["wq"].shape[1], generator=torch.Generator(device="cuda").manual_seed(22), device="cuda")
+    q, _, q_idx, k, v, kidx = QsaFront(d, **w).project(x, torch.tensor([n_past], dtype=torch.int32, device="cuda"))
+    run_decode_case(d, n_past, seed=23, inputs=(q, q_idx, k, v, kidx))
+
+
+def test_front_argument_errors():
+    """Refused on the host before anything is launched."""
+    d = make_desc(n_ctx=4096)
+    w = front_weights(d, n_embd=64, seed=1)
+    front = QsaFront(d, **w)
+    x = torch.zeros(1, 64, device="cuda")
+    pos = torch.zeros(1, dtype=torch.int32, device="cuda")
+    outs = [torch.empty(4096, device="cuda") for _ in range(6)]
+    ws = front.workspace(1)
+    L = lib()
+
+    def call(wts, xp=x.data_ptr(), ws_bytes=ws.numel()):
+        return L.qsa_front(ctypes.byref(d), ctypes.byref(wts), 1, pos.data_ptr(), xp, *[o.data_ptr() for o in outs],
+                           ws.data_ptr(), ws_bytes, torch.cuda.current_stream().cuda_stream)
+
+    bad = QsaFrontWeights.from_buffer_copy(front.w)
+    bad.w_type = TYPE_F16
+    assert call(bad) == QSA_ERR_UNSUPPORTED
+    bad = QsaFrontWeights.from_buffer_copy(front.w)
+    bad.n_embd = 60
+    assert call(bad) == QSA_ERR_UNSUPPORTED
+    assert call(front.w, xp=x.data_ptr() + 4) == QSA_ERR_INVALID
+    assert call(front.w, ws_bytes=16) == QSA_ERR_WORKSPACE
+    bad = QsaFrontWeights.from_buffer_copy(front.w)
+    bad.wk = None
+    assert call(bad) == QSA_ERR_INVALID
+    torch.cuda.synchronize()

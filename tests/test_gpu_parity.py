@@ -72,15 +72,16 @@ def test_pool_rebuild_matches_oracle(blk0, n_blk, n_ctx):
     assert np.all(np.abs(got16[diff].astype(np.int32) - ref16[diff].astype(np.int32)) <= 1)
 
 
-def run_decode_case(d, n_past, seed, q_dtype=torch.bfloat16, batch_lengths=None):
-    """Fill caches, decode one token per sequence (append included), compare everything."""
+def run_decode_case(d, n_past, seed, q_dtype=torch.bfloat16, batch_lengths=None, inputs=None):
+    """Fill caches, decode one token per sequence (append included), compare everything.
+    inputs: the tokens' (q, q_idx, k, v, kidx) when given (e.g. from qsa_front), else seeded."""
     lengths = batch_lengths or [n_past]
     node = QsaNode(d)
     states = [QsaState(d) for _ in lengths]
     for i, (st, L) in enumerate(zip(states, lengths)):
         fill_cache(node, st, 0, L, seed + 100 * i)
     B = len(lengths)
-    q, q_idx, k, v, ki = token_inputs(d, B, seed + 7, q_dtype)
+    q, q_idx, k, v, ki = inputs if inputs is not None else token_inputs(d, B, seed + 7, q_dtype)
     items = decode_items([st.layer() for st in states], lengths)
     KB = k_blocks(d)
     sel = torch.full((B, KB), -7, dtype=torch.int32, device="cuda")
