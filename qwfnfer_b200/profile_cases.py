@@ -3,6 +3,7 @@
     python -m qwfnfer_b200.profile_cases batch B STEPS    # B decode queries over one config-2 cache
     python -m qwfnfer_b200.profile_cases decode STEPS     # the config-2 decode step (append + select + attend)
     python -m qwfnfer_b200.profile_cases prefill T N_PAST STEPS   # one qsa_prefill chunk (config-4 shape)
+    python -m qwfnfer_b200.profile_cases front T STEPS    # qsa_front for T tokens (n_embd 2560, bf16 weights)
     python -m torch.distributed.run --nproc-per-node N ... -m qwfnfer_b200.profile_cases shard5 peer|nccl [lb] [ri]
                                                           # config-5 sharded step: per-kernel timeline per rank
 
@@ -10,6 +11,8 @@
 multi-tile streaming regime with 220 MB of caches on the device; `decode` is one token of config 2.  `prefill` appends
 T tokens at N_PAST of a q8_0 cache and runs the whole chunk (T=4096 at 77824 keeps config 4's ~210 queries per block
 with about 2.5 GB on the device).  Each step is preceded by a 256 MB L2 flush; the device time of every step is printed.
+`front` projects T tokens through the layer's 48.5 MB of bf16 projection weights (the config-2 descriptor), each
+step after the 256 MB L2 flush, so the weights come from DRAM.
 `shard5` replays the config-5 sharded decode step (one layer after another, or with `lb` the 12 layers as one batch;
 `ri`: indexer caches replicated)
 from a CUDA graph under torch.profiler and prints, per rank, each kernel's median start offset and duration within
@@ -31,6 +34,8 @@ def main(argv: list[str]) -> None:
         return prefill(argv[1:])
     if kind == "shard5":
         return shard5(argv[1:])
+    if kind == "front":
+        return front(argv[1:])
     cfg = CONFIGS[2]
     d = cfg.desc()
     node, st = QsaNode(d), QsaState(d)
@@ -80,6 +85,30 @@ def prefill(argv: list[str]) -> None:
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         node.sparse_attn(st.layer(), n_past, q, qi, k, v, ki, ws=ws)
+        b.record()
+        ev.append((a, b))
+    torch.cuda.synchronize()
+    print("us per step:", [round(a.elapsed_time(b) * 1e3, 1) for a, b in ev])
+
+
+def front(argv: list[str]) -> None:
+    from .configs import front_weights
+    from .qsa import QsaFront
+
+    T = int(argv[0]) if argv else 1
+    steps = int(argv[1]) if len(argv) > 1 else 3
+    d = CONFIGS[2].desc()
+    fr = QsaFront(d, **front_weights(d, seed=5))
+    x = torch.randn(T, fr.n_embd, generator=torch.Generator(device="cuda").manual_seed(6), device="cuda")
+    pos = torch.arange(CONFIGS[2].n_past - T + 1, CONFIGS[2].n_past + 1, dtype=torch.int32, device="cuda")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()
+    ev = []
+    for _ in range(steps):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fr.project(x, pos)
         b.record()
         ev.append((a, b))
     torch.cuda.synchronize()
