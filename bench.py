@@ -388,6 +388,7 @@ def run_ours_config2(args, ws, rank, local):
         "clocks": clocks.summary(),
     }
     res["front"] = front_stage(d, dev, n_past, flush, K, cfg.seed)
+    res["output"] = output_stage(d, dev, flush, K, cfg.seed)
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         kc = st.k[0][:n_past + 1].cpu().numpy()
         vc = st.v[0][:n_past + 1].cpu().numpy()
@@ -432,6 +433,45 @@ def front_stage(d, dev, n_past, flush, K, seed):
     hbm, _, src = peaks()
     ach = nbytes / (mean * 1e-6) / 1e9
     return {"kernel": "front_kernel (qsa_front), 1 token, n_embd 2560, bf16 weights", "us": round(mean, 3),
+            "algorithmic_bytes": nbytes, "achieved_gbs": round(ach, 1), "peak": hbm,
+            "frac": round(ach / hbm, 4), "peak_source": f"{src} hbm_gbs (burst)", "launches": 1}
+
+
+def output_stage(d, dev, flush, K, seed):
+    """The output side after the node (qsa_output: attention output times sigmoid(gate), then the
+    bf16 attn_output projection to n_embd 2560) for one token: graph replay, L2 flushed, HBM roofline."""
+    import torch
+
+    from qwfnfer_b200.configs import N_EMBD
+    from qwfnfer_b200.qsa import QsaOutput
+
+    g = torch.Generator(device=dev).manual_seed(seed + 60)
+    n_in = d.n_head * d.head_dim
+    wo = (torch.randn(N_EMBD, n_in, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    attn = torch.randn(1, d.n_head, d.head_dim, generator=g, device=dev)
+    gate = torch.randn(1, n_in, generator=g, device=dev)
+    out = torch.empty(1, N_EMBD, device=dev)
+    op = QsaOutput(d, wo)
+    for _ in range(3):
+        op.project(attn, gate, out=out)
+    torch.cuda.synchronize()
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        op.project(attn, gate, out=out)
+    ev = []
+    for _ in range(max(K, 20)):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        gr.replay()
+        b.record()
+        ev.append((a, b))
+    torch.cuda.synchronize()
+    mean = statistics.mean(a.elapsed_time(b) * 1e3 for a, b in ev)
+    nbytes = wo.numel() * 2 + attn.numel() * 4 + gate.numel() * 4 + out.numel() * 4
+    hbm, _, src = peaks()
+    ach = nbytes / (mean * 1e-6) / 1e9
+    return {"kernel": "output_kernel (qsa_output), 1 token, 4096 -> n_embd 2560, bf16 weights", "us": round(mean, 3),
             "algorithmic_bytes": nbytes, "achieved_gbs": round(ach, 1), "peak": hbm,
             "frac": round(ach / hbm, 4), "peak_source": f"{src} hbm_gbs (burst)", "launches": 1}
 

@@ -313,6 +313,15 @@ qsa_status qsa_front(const qsa_desc * d, const qsa_front_weights * w, int32_t T,
                      float * k_out, float * v_out, float * kidx_out,
                      void * ws, size_t ws_bytes, qsa_stream_t stream);
 
+/* The output side of the node (src/qwfn_graph.cpp:543-545; prefill :406-407): for T tokens
+ *   y = attn_output.weight * (attn * sigmoid(gate)),
+ * sigmoid 1/(1+exp(-g)) in f32, the gated product rounded to bf16 as the CPU mul_mat converts it,
+ * f32 accumulation.  wo: bf16 [n_embd][n_head*head_dim] (16-byte aligned); attn: f32
+ * [T][n_head][head_dim] (qsa_decode's out); gate: f32 [T][n_head*head_dim] (qsa_front's gate);
+ * y: f32 [T][n_embd]. */
+qsa_status qsa_output(const qsa_desc * d, const void * wo, int32_t n_embd, int32_t w_type, int32_t T,
+                      const float * attn, const float * gate, float * y, qsa_stream_t stream);
+
 /* ------------------------------------------------------------------ staging */
 /* Copy `bytes` (a multiple of 16, both addresses 16-byte aligned) from src to dst with a kernel on
  * `stream`, chained to the kernels around it by programmatic dependent launch.  Each side is device

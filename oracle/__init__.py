@@ -48,6 +48,7 @@ def lib() -> ctypes.CDLL:
             "orc_k_blocks": (ctypes.c_int, [D]),
             "orc_node": (None, [D, VP, VP, VP, I64, VP, VP, I32, VP, VP, VP, VP, I32]),
             "orc_front": (None, [D, VP, VP, VP, VP, VP, VP, VP, VP, I64, I64, VP, VP, VP, VP, VP, VP, VP, VP]),
+            "orc_output": (None, [D, VP, I64, I64, VP, VP, VP]),
         }
         for name, (res, args) in sigs.items():
             fn = getattr(L, name)
@@ -227,3 +228,15 @@ def front(d: QsaDesc, w: dict, pos: np.ndarray, x: np.ndarray) -> dict:
     lib().orc_front(ctypes.byref(d), *[_p(a) for a in ws], *[_p(a) for a in ns], n_embd, T, _p(pos), _p(x),
                     *[_p(out[k]) for k in ("q", "gate", "q_idx", "k", "v", "kidx")])
     return out
+
+
+def output(d: QsaDesc, wo: np.ndarray, attn: np.ndarray, gate: np.ndarray) -> np.ndarray:
+    """orc_output: y = attn_output (attn * sigmoid(gate)); wo uint16 bf16 bits [n_embd][n_head*head_dim],
+    attn f32 [T][n_head][head_dim], gate f32 [T][n_head*head_dim] -> y f32 [T][n_embd]."""
+    wo = np.ascontiguousarray(wo, dtype=np.uint16)
+    attn = np.ascontiguousarray(attn, dtype=np.float32)
+    gate = np.ascontiguousarray(gate, dtype=np.float32)
+    T, n_embd = attn.shape[0], wo.shape[0]
+    y = np.zeros((T, n_embd), np.float32)
+    lib().orc_output(ctypes.byref(d), _p(wo), n_embd, T, _p(attn), _p(gate), _p(y))
+    return y

@@ -548,4 +548,26 @@ void orc_front(const qsa_desc * d, const uint16_t * wq, const uint16_t * wk, con
     }
 }
 
+
+// The output side (src/qwfn_graph.cpp:543-545): z = attn * sigmoid(gate) in f32 (ggml_sigmoid:
+// 1/(1+expf(-g))), then mul_mat(attn_output bf16, z): z rounded to bf16, products exact in f32,
+// accumulated in double and rounded once.
+void orc_output(const qsa_desc * d, const uint16_t * wo, int64_t n_embd, int64_t T, const float * attn,
+                const float * gate, float * y) {
+    const int64_t n_in = (int64_t) d->n_head * d->head_dim;
+    #pragma omp parallel for schedule(static) if (T > 1)
+    for (int64_t t = 0; t < T; t++) {
+        std::vector<float> z(n_in);
+        for (int64_t e = 0; e < n_in; e++) {
+            const float sg = 1.0f / (1.0f + expf(-gate[t * n_in + e]));
+            z[e] = bf16_to_f32(f32_to_bf16(attn[t * n_in + e] * sg));
+        }
+        for (int64_t r = 0; r < n_embd; r++) {
+            double acc = 0.0;
+            for (int64_t e = 0; e < n_in; e++) acc += (double) (bf16_to_f32(wo[r * n_in + e]) * z[e]);
+            y[t * n_embd + r] = (float) acc;
+        }
+    }
+}
+
 }  // extern "C"

@@ -17,6 +17,10 @@
 //   - each row's per-token sums (warp-shuffle reduced, a fixed order) go to the workspace; the
 //     last CTA of a head group to arrive (an acq_rel counter) normalises the head, applies IMRoPE
 //     with the pooled key's angle recurrence, and writes the outputs.
+//
+// The output side (src/qwfn_graph.cpp:543-545; prefill :406-407): ggml_mul(attn, ggml_sigmoid(gate))
+// then ggml_mul_mat(attn_output.weight, .) -- output_kernel: the gated attention output, rounded to
+// bf16, in shared memory, and the same weight streaming over attn_output's n_embd rows (16 per CTA).
 #include "qsa_kernels.cuh"
 
 namespace qsa {
@@ -145,61 +149,40 @@ __device__ __forceinline__ void store_head(float * __restrict__ dst, const float
         *reinterpret_cast<float4 *>(dst + EPL * lane + e) = make_float4(x[e], x[e + 1], x[e + 2], x[e + 3]);
 }
 
-__global__ void __launch_bounds__(FR_THREADS, 2) front_kernel(DevDesc d, FrontArgs a) {
-    extern __shared__ __align__(16) float xs[];                 // [T][n_embd]
-    __shared__ bool is_last;
-    const FrontShape sh = front_shape(d);
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    // this CTA's kind, head group and 64-row chunk
-    int kind = 0, c = blockIdx.x;
-    while (kind < FR_KINDS - 1 && c >= sh.groups[kind] * (sh.group_rows[kind] / FR_ROWS)) {
-        c -= sh.groups[kind] * (sh.group_rows[kind] / FR_ROWS);
-        kind++;
-    }
-    const int chunks = sh.group_rows[kind] / FR_ROWS;
-    const int g = c / chunks, chunk = c % chunks;
-    const int row_in_kind = g * sh.group_rows[kind] + chunk * FR_ROWS;
-    const int T = a.T, n = a.n_embd, n16 = n / 8;
-
-
-    // the warp's rows x passes over the columns, one after another; the next item's weight loads
-    // are issued before the current item's products
-    constexpr int WROWS = FR_ROWS / 8;
-    const int passes = (n16 + 32 * FR_UNROLL - 1) / (32 * FR_UNROLL);
-    const int items = WROWS * passes;
-    const uint16_t * wwarp = a.w[kind] + (size_t) (row_in_kind + warp * WROWS) * n;
-    auto load = [&](int it, uint4 (&v)[FR_UNROLL]) {
-        const uint4 * wr = reinterpret_cast<const uint4 *>(wwarp + (size_t) (it / passes) * n);
-        const int base = (it % passes) * 32 * FR_UNROLL + lane;
+// One warp's matrix-vector products: rows [0, wrows) of the bf16 matrix at `wrow0` (row stride n
+// columns) times the T token vectors in shared memory `xs` ([T][n] f32 of bf16 values).  Work items
+// are (row, pass over 32*UNROLL 16-byte pieces of the row); the next item's loads are issued before
+// the current item's products, and the first item's loads before `stage_issue` / `stage_wait`
+// bring the activations in (every thread of the CTA calls this, and stage_wait ends with the CTA
+// barrier).  emit(r, t, sum) is called by lane 0 per finished row r and token t; sums are f32 FMAs
+// along each lane's pieces, then a fixed shuffle tree.
+template <int UNROLL, typename Issue, typename Wait, typename Emit>
+__device__ __forceinline__ void gemv_stream(const uint16_t * __restrict__ wrow0, int wrows, int n, const float * xs, int T,
+                                            int lane, Issue && stage_issue, Wait && stage_wait, Emit && emit) {
+    const int n16 = n / 8;
+    const int passes = (n16 + 32 * UNROLL - 1) / (32 * UNROLL);
+    const int items = wrows * passes;
+    auto load = [&](int it, uint4 (&v)[UNROLL]) {
+        const uint4 * wr = reinterpret_cast<const uint4 *>(wrow0 + (size_t) (it / passes) * n);
+        const int base = (it % passes) * 32 * UNROLL + lane;
         #pragma unroll
-        for (int u = 0; u < FR_UNROLL; u++) {
+        for (int u = 0; u < UNROLL; u++) {
             const int i = base + u * 32;
             v[u] = i < n16 ? ld_stream(wr + i) : make_uint4(0u, 0u, 0u, 0u);
         }
     };
-    uint4 cur[FR_UNROLL], nxt[FR_UNROLL];
+    uint4 cur[UNROLL], nxt[UNROLL];
     float acc[FR_TOK];
     #pragma unroll
     for (int t = 0; t < FR_TOK; t++) acc[t] = 0.0f;
-    // the activations go to shared memory by cp.async ahead of the first weight loads; each thread
-    // then rounds the pieces it copied to bf16 values in place
-    for (int i = tid; i < T * n / 4; i += FR_THREADS)
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(smem_u32(xs + 4 * i)), "l"(a.x + 4 * i) : "memory");
-    asm volatile("cp.async.commit_group;" ::: "memory");
-    load(0, cur);
-    asm volatile("cp.async.wait_all;" ::: "memory");
-    for (int i = tid; i < T * n / 4; i += FR_THREADS) {
-        float4 v = reinterpret_cast<float4 *>(xs)[i];
-        v.x = __bfloat162float(__float2bfloat16_rn(v.x)); v.y = __bfloat162float(__float2bfloat16_rn(v.y));
-        v.z = __bfloat162float(__float2bfloat16_rn(v.z)); v.w = __bfloat162float(__float2bfloat16_rn(v.w));
-        reinterpret_cast<float4 *>(xs)[i] = v;
-    }
-    __syncthreads();
+    stage_issue();
+    if (items > 0) load(0, cur);
+    stage_wait();
     for (int it = 0; it < items; it++) {
         if (it + 1 < items) load(it + 1, nxt);
-        const int base = (it % passes) * 32 * FR_UNROLL + lane;
+        const int base = (it % passes) * 32 * UNROLL + lane;
         #pragma unroll
-        for (int u = 0; u < FR_UNROLL; u++) {
+        for (int u = 0; u < UNROLL; u++) {
             const int i = base + u * 32;
             if (i >= n16) break;
             const uint32_t p[4] = {cur[u].x, cur[u].y, cur[u].z, cur[u].w};
@@ -221,19 +204,57 @@ __global__ void __launch_bounds__(FR_THREADS, 2) front_kernel(DevDesc d, FrontAr
             }
         }
         if (it % passes == passes - 1) {                        // the row is complete
-            const int row = warp * WROWS + it / passes;
             #pragma unroll
             for (int t = 0; t < FR_TOK; t++) {
                 float s = acc[t];
                 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-                if (lane == 0 && t < T) a.y[(size_t) t * a.rows_total + sh.row0[kind] + row_in_kind + row] = s;
+                if (lane == 0 && t < T) emit(it / passes, t, s);
                 acc[t] = 0.0f;
             }
         }
         #pragma unroll
-        for (int u = 0; u < FR_UNROLL; u++) cur[u] = nxt[u];
+        for (int u = 0; u < UNROLL; u++) cur[u] = nxt[u];
     }
+}
+
+__global__ void __launch_bounds__(FR_THREADS, 2) front_kernel(DevDesc d, FrontArgs a) {
+    extern __shared__ __align__(16) float xs[];                 // [T][n_embd]
+    __shared__ bool is_last;
+    const FrontShape sh = front_shape(d);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    // this CTA's kind, head group and 64-row chunk
+    int kind = 0, c = blockIdx.x;
+    while (kind < FR_KINDS - 1 && c >= sh.groups[kind] * (sh.group_rows[kind] / FR_ROWS)) {
+        c -= sh.groups[kind] * (sh.group_rows[kind] / FR_ROWS);
+        kind++;
+    }
+    const int chunks = sh.group_rows[kind] / FR_ROWS;
+    const int g = c / chunks, chunk = c % chunks;
+    const int row_in_kind = g * sh.group_rows[kind] + chunk * FR_ROWS;
+    const int T = a.T, n = a.n_embd;
+
+
+    gemv_stream<FR_UNROLL>(a.w[kind] + (size_t) (row_in_kind + warp * (FR_ROWS / 8)) * n, FR_ROWS / 8, n, xs, T, lane,
+        [&] {   // the activations go to shared memory by cp.async ahead of the first weight loads' data;
+                // each thread then rounds the pieces it copied to bf16 values in place
+            for (int i = tid; i < T * n / 4; i += FR_THREADS)
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(smem_u32(xs + 4 * i)), "l"(a.x + 4 * i) : "memory");
+            asm volatile("cp.async.commit_group;" ::: "memory");
+        },
+        [&] {
+            asm volatile("cp.async.wait_all;" ::: "memory");
+            for (int i = tid; i < T * n / 4; i += FR_THREADS) {
+                float4 v = reinterpret_cast<float4 *>(xs)[i];
+                v.x = __bfloat162float(__float2bfloat16_rn(v.x)); v.y = __bfloat162float(__float2bfloat16_rn(v.y));
+                v.z = __bfloat162float(__float2bfloat16_rn(v.z)); v.w = __bfloat162float(__float2bfloat16_rn(v.w));
+                reinterpret_cast<float4 *>(xs)[i] = v;
+            }
+            __syncthreads();
+        },
+        [&](int r, int t, float v) {
+            a.y[(size_t) t * a.rows_total + sh.row0[kind] + row_in_kind + warp * (FR_ROWS / 8) + r] = v;
+        });
 
     // Arrival: the last CTA of the head group finishes it.  The barrier orders the CTA's row
     // stores before thread 0's release; its acquire orders the other CTAs' stores before our reads.
@@ -283,6 +304,33 @@ __global__ void __launch_bounds__(FR_THREADS, 2) front_kernel(DevDesc d, FrontAr
         load_head<4>(yh, x, lane);
         store_head<4>(a.kidx_out + (size_t) t * MAX_IDX_DIM, x, lane);
     }
+}
+
+constexpr int OUT_ROWS = 16;               // attn_output rows per CTA (2 per warp)
+constexpr int OUT_MAX_IN = 4096;           // n_head * head_dim
+
+// y[t][row] = sum_e wo[row][e] * bf16(attn[t][e] * sigmoid(gate[t][e])) for the launch's T tokens.
+__global__ void __launch_bounds__(FR_THREADS, 2) output_kernel(const uint16_t * __restrict__ wo, int n_embd, int n_in,
+        int T, const float * __restrict__ attn, const float * __restrict__ gate, float * __restrict__ y) {
+    extern __shared__ __align__(16) float zs[];                 // [T][n_in]
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int row0 = blockIdx.x * OUT_ROWS + warp * (OUT_ROWS / 8);
+    const int wrows = max(0, min(OUT_ROWS / 8, n_embd - row0));
+    gemv_stream<FR_UNROLL>(wo + (size_t) row0 * n_in, wrows, n_in, zs, T, lane,
+        [] {},
+        [&] {   // ggml_sigmoid: 1 / (1 + exp(-g)) in f32; the product rounded to bf16 as mul_mat converts it
+            for (int i = tid; i < T * n_in / 4; i += FR_THREADS) {
+                const float4 o = reinterpret_cast<const float4 *>(attn)[i];
+                const float4 g = reinterpret_cast<const float4 *>(gate)[i];
+                auto z = [](float a, float b) {
+                    const float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-b)));
+                    return __bfloat162float(__float2bfloat16_rn(__fmul_rn(a, sg)));
+                };
+                reinterpret_cast<float4 *>(zs)[i] = make_float4(z(o.x, g.x), z(o.y, g.y), z(o.z, g.z), z(o.w, g.w));
+            }
+            __syncthreads();
+        },
+        [&](int r, int t, float v) { y[(size_t) t * n_embd + row0 + r] = v; });
 }
 
 struct FrontWs { size_t counters, y, total; };
@@ -358,6 +406,33 @@ extern "C" qsa_status qsa_front(const qsa_desc * dd, const qsa_front_weights * w
         a.v_out = v_out + t0 * kv;
         a.kidx_out = kidx_out + (size_t) t0 * MAX_IDX_DIM;
         front_kernel<<<sh.ctas, FR_THREADS, (size_t) a.T * w->n_embd * 4, st>>>(d, a);
+        if ((e = cudaGetLastError()) != cudaSuccess) return QSA_ERR_CUDA;
+    }
+    return QSA_OK;
+}
+
+extern "C" qsa_status qsa_output(const qsa_desc * dd, const void * wo, int32_t n_embd, int32_t w_type, int32_t T,
+                                 const float * attn, const float * gate, float * y, qsa_stream_t stream) {
+    qsa_status s = qsa_desc_check(dd);
+    if (s != QSA_OK) return s;
+    if (!wo || !attn || !gate || !y || T <= 0 || n_embd <= 0) return QSA_ERR_INVALID;
+    if (w_type != QSA_TYPE_BF16) return QSA_ERR_UNSUPPORTED;
+    if (!aligned16(wo) || !aligned16(attn) || !aligned16(gate) || (reinterpret_cast<uintptr_t>(y) & 3u))
+        return QSA_ERR_INVALID;
+    const int n_in = dd->n_head * dd->head_dim;
+    if (n_in > OUT_MAX_IN || n_in % 8 != 0) return QSA_ERR_UNSUPPORTED;
+    static std::atomic<uint64_t> attr{0};
+    cudaError_t e = once_per_device(attr, [] {
+        return cudaFuncSetAttribute(output_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FR_TOK * OUT_MAX_IN * 4);
+    });
+    if (e != cudaSuccess) return QSA_ERR_CUDA;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const unsigned grid = (unsigned) ((n_embd + OUT_ROWS - 1) / OUT_ROWS);
+    for (int t0 = 0; t0 < T; t0 += FR_TOK) {
+        const int Tg = std::min(FR_TOK, T - t0);
+        output_kernel<<<grid, FR_THREADS, (size_t) Tg * n_in * 4, st>>>(
+            static_cast<const uint16_t *>(wo), n_embd, n_in, Tg, attn + (size_t) t0 * n_in, gate + (size_t) t0 * n_in,
+            y + (size_t) t0 * n_embd);
         if ((e = cudaGetLastError()) != cudaSuccess) return QSA_ERR_CUDA;
     }
     return QSA_OK;

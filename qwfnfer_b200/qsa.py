@@ -10,6 +10,7 @@ Names follow the reference so that callers and tests read like it:
                      (src/qwfn_engine.cpp:814)
   QsaFront           the projections, norms and IMRoPE feeding the node (src/qwfn_graph.cpp:465,
                      479-484, 505-518)
+  QsaOutput          the gated output projection after it (src/qwfn_graph.cpp:543-545)
 Errors raise QsaError carrying the qsa_status (the reference aborts; the library never does).
 PyTorch provides device memory and streams only; every computation runs in libqsa.so.
 """
@@ -303,3 +304,22 @@ class QsaFront:
                               _ptr(q_idx), _ptr(k), _ptr(v), _ptr(kidx), ws.data_ptr(), ws.numel(), _stream(stream)),
               "qsa_front")
         return q, gate, q_idx, k, v, kidx
+
+
+class QsaOutput:
+    """The output side of the node (qsa_output): y = attn_output.weight (attn * sigmoid(gate)), the
+    bf16 weight row-major [n_embd][n_head*head_dim]."""
+
+    def __init__(self, desc: QsaDesc, wo: torch.Tensor):
+        if wo.dtype != torch.bfloat16 or wo.dim() != 2 or wo.shape[1] != desc.n_head * desc.head_dim:
+            raise QsaError(_abi.QSA_ERR_INVALID, "attn_output weight: bf16 [n_embd][n_head*head_dim]")
+        self.desc, self.wo, self.n_embd = desc, wo, int(wo.shape[0])
+
+    def project(self, attn: torch.Tensor, gate: torch.Tensor, out: torch.Tensor | None = None, stream=None):
+        """attn f32 [T][n_head][head_dim], gate f32 [T][n_head*head_dim] -> y f32 [T][n_embd]."""
+        T = attn.shape[0]
+        if out is None:
+            out = torch.empty((T, self.n_embd), dtype=torch.float32, device=self.wo.device)
+        check(lib().qsa_output(ctypes.byref(self.desc), _ptr(self.wo), self.n_embd, TYPE_BF16, T, _ptr(attn), _ptr(gate),
+                               _ptr(out), _stream(stream)), "qsa_output")
+        return out

@@ -110,3 +110,20 @@ def test_front_norm_rope_is_the_pooled_keys(b):
     ic[b * r:] = oracle.f32_to_f16(u)[None, :]
     p32, _ = oracle.pool_blocks(d, ic, b, 1, k_norm_w=gamma)
     assert np.array_equal(got, p32[0])
+
+
+def test_oracle_output_matches_numpy():
+    """orc_output: attn * sigmoid(gate) rounded to bf16, then the attn_output projection."""
+    d = make_desc()
+    rng = np.random.default_rng(4)
+    n_in, n_embd, T = d.n_head * d.head_dim, 384, 3
+    wo = bf16_bits(rng.standard_normal((n_embd, n_in), dtype=np.float32) * 0.02)
+    attn = rng.standard_normal((T, d.n_head, d.head_dim), dtype=np.float32)
+    gate = 2 * rng.standard_normal((T, n_in), dtype=np.float32)
+    got = oracle.output(d, wo, attn, gate)
+    sg = (np.float32(1) / (np.float32(1) + np.exp(-gate))).astype(np.float32)
+    z = bits_to_f64(bf16_bits((attn.reshape(T, n_in) * sg).astype(np.float32)))
+    W = bits_to_f64(wo)
+    ref = z @ W.T
+    bound = 1e-6 * (np.abs(z) @ np.abs(W).T) + 2 ** -7 * np.max(np.abs(z)[:, None, :] * np.abs(W)[None], axis=2)
+    assert np.all(np.abs(got - ref) <= bound)

@@ -1,5 +1,6 @@
-"""qsa_front (the projections, norms and IMRoPE feeding the node) on a B200 against the CPU oracle,
-pinned to the GPU's own pooled keys, and chained into qsa_decode.
+"""qsa_front (the projections, norms and IMRoPE feeding the node) and qsa_output (the gated output
+projection after it) on a B200 against the CPU oracle; the front pinned to the GPU's own pooled keys
+and chained into qsa_decode and qsa_output.
 
 Tolerances: a projection's f32 sum may differ from the oracle's (double sum, one rounding) by the
 f32 accumulation error, bounded here by 1e-5 of the row's sum of |w * x|; the normed and roped
@@ -13,10 +14,10 @@ import pytest
 import torch
 
 import oracle
-from qwfnfer_b200._abi import (QSA_ERR_INVALID, QSA_ERR_UNSUPPORTED, QSA_ERR_WORKSPACE, QsaFrontWeights, TYPE_F16,
-                               TYPE_Q8_0, lib, make_desc)
+from qwfnfer_b200._abi import (QSA_ERR_INVALID, QSA_ERR_UNSUPPORTED, QSA_ERR_WORKSPACE, QsaFrontWeights, TYPE_BF16,
+                               TYPE_F16, TYPE_Q8_0, lib, make_desc)
 from qwfnfer_b200.configs import fill_cache, front_weights
-from qwfnfer_b200.qsa import QsaFront, QsaNode, QsaState
+from qwfnfer_b200.qsa import QsaFront, QsaNode, QsaOutput, QsaState, decode_items
 from test_gpu_parity import desc_for, run_decode_case
 
 pytestmark = pytest.mark.gpu
@@ -126,4 +127,69 @@ def test_front_argument_errors():
     bad = QsaFrontWeights.from_buffer_copy(front.w)
     bad.wk = None
     assert call(bad) == QSA_ERR_INVALID
+    torch.cuda.synchronize()
+
+
+def output_bound(wo: torch.Tensor, attn: torch.Tensor, gate: torch.Tensor) -> np.ndarray:
+    """Per (token, row): 1e-5 of the sum of |w * z| plus one bf16 rounding step of the largest term
+    (the device and host expf may round one gated value to a neighbouring bf16)."""
+    T = attn.shape[0]
+    z = (attn.reshape(T, -1) * torch.sigmoid(gate)).abs()
+    W = wo.float().abs()
+    s = z @ W.T
+    m = torch.stack([(z[t][None, :] * W).max(dim=1).values for t in range(T)])
+    return (PROJ_TOL * s + 2 ** -7 * m).cpu().numpy()
+
+
+@pytest.mark.parametrize("T,n_embd", [(1, 2560), (5, 2560), (2, 1000)])
+def test_output_matches_oracle(T, n_embd):
+    d = make_desc()
+    g = torch.Generator(device="cuda").manual_seed(31 + T)
+    n_in = d.n_head * d.head_dim
+    wo = (torch.randn(n_embd, n_in, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    attn = torch.randn(T, d.n_head, d.head_dim, generator=g, device="cuda")
+    gate = 2 * torch.randn(T, n_in, generator=g, device="cuda")
+    y = QsaOutput(d, wo).project(attn, gate)
+    torch.cuda.synchronize()
+    ref = oracle.output(d, wo.view(torch.int16).cpu().numpy().view(np.uint16), attn.cpu().numpy(), gate.cpu().numpy())
+    err = np.abs(y.cpu().numpy() - ref)
+    bound = output_bound(wo, attn, gate)
+    assert np.all(err <= bound), float((err / bound).max())
+
+
+def test_front_decode_output_chain():
+    """The node end to end for one token: qsa_front -> qsa_decode -> qsa_output, each stage's
+    output feeding the next as it is; the output stage checked against the oracle on the GPU's own
+    intermediates (the earlier stages have their own parity tests)."""
+    d = desc_for(TYPE_Q8_0, 16384)
+    n_past = 12000
+    node, st = QsaNode(d), QsaState(d)
+    fill_cache(node, st, 0, n_past, 41)
+    w = front_weights(d, seed=42, gammas=True)
+    g = torch.Generator(device="cuda").manual_seed(43)
+    x = torch.randn(1, w["wq"].shape[1], generator=g, device="cuda")
+    q, gate, q_idx, k, v, kidx = QsaFront(d, **w).project(x, torch.tensor([n_past], dtype=torch.int32, device="cuda"))
+    attn = node.sparse_attn_decode(decode_items([st.layer()], [n_past]), 1, n_past + 1, q, q_idx, k, v, kidx)
+    wo = (torch.randn(2560, d.n_head * d.head_dim, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    y = QsaOutput(d, wo).project(attn, gate)
+    torch.cuda.synchronize()
+    ref = oracle.output(d, wo.view(torch.int16).cpu().numpy().view(np.uint16), attn.cpu().numpy(), gate.cpu().numpy())
+    assert np.all(np.abs(y.cpu().numpy() - ref) <= output_bound(wo, attn, gate))
+    assert np.isfinite(ref).all()
+
+
+def test_output_argument_errors():
+    d = make_desc()
+    n_in = d.n_head * d.head_dim
+    wo = torch.zeros(64, n_in, dtype=torch.bfloat16, device="cuda")
+    attn = torch.zeros(1, n_in + 4, device="cuda")
+    gate = torch.zeros(1, n_in, device="cuda")
+    y = torch.zeros(1, 64, device="cuda")
+    L, st = lib(), torch.cuda.current_stream().cuda_stream
+    assert L.qsa_output(ctypes.byref(d), wo.data_ptr(), 64, TYPE_F16, 1, attn.data_ptr(), gate.data_ptr(),
+                        y.data_ptr(), st) == QSA_ERR_UNSUPPORTED
+    assert L.qsa_output(ctypes.byref(d), wo.data_ptr(), 64, TYPE_BF16, 1, attn.data_ptr() + 4, gate.data_ptr(),
+                        y.data_ptr(), st) == QSA_ERR_INVALID
+    assert L.qsa_output(ctypes.byref(d), wo.data_ptr(), 0, TYPE_BF16, 1, attn.data_ptr(), gate.data_ptr(),
+                        y.data_ptr(), st) == QSA_ERR_INVALID
     torch.cuda.synchronize()
