@@ -4,6 +4,7 @@
     python -m qwfnfer_b200.profile_cases decode STEPS     # the config-2 decode step (append + select + attend)
     python -m qwfnfer_b200.profile_cases prefill T N_PAST STEPS   # one qsa_prefill chunk (config-4 shape)
     python -m qwfnfer_b200.profile_cases front T STEPS    # qsa_front for T tokens (n_embd 2560, bf16 weights)
+    python -m qwfnfer_b200.profile_cases output T STEPS   # qsa_output for T tokens (4096 -> 2560, bf16 weights)
     python -m torch.distributed.run --nproc-per-node N ... -m qwfnfer_b200.profile_cases shard5 peer|nccl [lb] [ri]
                                                           # config-5 sharded step: per-kernel timeline per rank
 
@@ -36,6 +37,8 @@ def main(argv: list[str]) -> None:
         return shard5(argv[1:])
     if kind == "front":
         return front(argv[1:])
+    if kind == "output":
+        return output(argv[1:])
     cfg = CONFIGS[2]
     d = cfg.desc()
     node, st = QsaNode(d), QsaState(d)
@@ -109,6 +112,32 @@ def front(argv: list[str]) -> None:
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         fr.project(x, pos)
+        b.record()
+        ev.append((a, b))
+    torch.cuda.synchronize()
+    print("us per step:", [round(a.elapsed_time(b) * 1e3, 1) for a, b in ev])
+
+
+def output(argv: list[str]) -> None:
+    from .configs import N_EMBD
+    from .qsa import QsaOutput
+
+    T = int(argv[0]) if argv else 1
+    steps = int(argv[1]) if len(argv) > 1 else 3
+    d = CONFIGS[2].desc()
+    g = torch.Generator(device="cuda").manual_seed(7)
+    n_in = d.n_head * d.head_dim
+    op = QsaOutput(d, (torch.randn(N_EMBD, n_in, generator=g, device="cuda") * 0.02).to(torch.bfloat16))
+    attn = torch.randn(T, d.n_head, d.head_dim, generator=g, device="cuda")
+    gate = torch.randn(T, n_in, generator=g, device="cuda")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()
+    ev = []
+    for _ in range(steps):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        op.project(attn, gate)
         b.record()
         ev.append((a, b))
     torch.cuda.synchronize()
