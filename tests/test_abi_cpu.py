@@ -68,3 +68,55 @@ def test_struct_layouts_match_header():
     assert ctypes.sizeof(_abi.QsaDecodeItem) == 48
     assert _abi.QsaDecodeItem.n_past.offset == 32
     assert ctypes.sizeof(_abi.QsaDesc) == 4 * 12 + 16 + 8 + 8
+
+
+def test_front_weights_layout():
+    assert ctypes.sizeof(_abi.QsaFrontWeights) == 8 * 8 + 2 * 4
+    assert _abi.QsaFrontWeights.n_embd.offset == 64
+
+
+# Fake device addresses: 16-byte aligned, never dereferenced (every case below is refused on the
+# host before any CUDA call is made).
+A = 1 << 20
+
+
+def front_call(w=None, T=1, x=A, ws_bytes=1 << 30):
+    d = make_desc(n_ctx=4096)
+    if w is None:
+        w = _abi.QsaFrontWeights(A, A, A, A, A, None, None, None, 2560, _abi.TYPE_BF16)
+    outs = [A] * 6
+    return lib().qsa_front(ctypes.byref(d), ctypes.byref(w), T, A, x, *outs, A, ws_bytes, None)
+
+
+def test_front_host_refusals():
+    d = make_desc(n_ctx=4096)
+    w = _abi.QsaFrontWeights(A, A, A, A, A, None, None, None, 2560, _abi.TYPE_BF16)
+    assert lib().qsa_front_workspace_size(ctypes.byref(d), ctypes.byref(w), 1) > 0
+    assert front_call(T=0) == _abi.QSA_ERR_INVALID
+    assert front_call(x=A + 4) == _abi.QSA_ERR_INVALID                    # misaligned activations
+    assert front_call(ws_bytes=16) == _abi.QSA_ERR_WORKSPACE
+    for field, value, status in (("w_type", _abi.TYPE_F16, _abi.QSA_ERR_UNSUPPORTED),
+                                 ("n_embd", 2564, _abi.QSA_ERR_UNSUPPORTED), ("n_embd", 1 << 15, _abi.QSA_ERR_UNSUPPORTED),
+                                 ("wv", None, _abi.QSA_ERR_INVALID), ("wk_idx", A + 8, _abi.QSA_ERR_INVALID)):
+        bad = _abi.QsaFrontWeights.from_buffer_copy(w)
+        setattr(bad, field, value)
+        assert front_call(w=bad) == status, field
+
+
+def test_output_host_refusals():
+    d = make_desc(n_ctx=4096)
+    L = lib()
+    call = lambda wt=_abi.TYPE_BF16, n_embd=2560, attn=A, T=1: L.qsa_output(ctypes.byref(d), A, n_embd, wt, T, attn, A, A,
+                                                                          None)
+    assert call(wt=TYPE_F16) == _abi.QSA_ERR_UNSUPPORTED
+    assert call(attn=A + 4) == _abi.QSA_ERR_INVALID
+    assert call(n_embd=0) == _abi.QSA_ERR_INVALID
+    assert call(T=0) == _abi.QSA_ERR_INVALID
+
+
+def test_stage_copy_host_refusals():
+    L = lib()
+    assert L.qsa_stage_copy(None, A, 16, None) == _abi.QSA_ERR_INVALID
+    assert L.qsa_stage_copy(A, A, 20, None) == _abi.QSA_ERR_INVALID          # not a multiple of 16 bytes
+    assert L.qsa_stage_copy(A + 8, A, 16, None) == _abi.QSA_ERR_INVALID      # misaligned
+    assert L.qsa_stage_copy(A, A, 0, None) == _abi.QSA_ERR_INVALID
