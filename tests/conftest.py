@@ -14,5 +14,10 @@ def pytest_configure(config):
 
 
 def pytest_collection_modifyitems(config, items):
-    # tests/test_zz_* files run last (a failure there leaves every other test already run).
-    items.sort(key=lambda it: os.path.basename(str(it.fspath)).startswith("test_zz_"))
+    # tests/test_zz_* files run last (a failure there leaves every other test already run), and the
+    # no-allocation entry point's test after all of them.
+    def rank(it):
+        name = os.path.basename(str(it.fspath))
+        return (name.startswith("test_zz_"), name == "test_zz_no_alloc.py")
+
+    items.sort(key=rank)
