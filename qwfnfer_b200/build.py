@@ -56,7 +56,11 @@ def build_lib(verbose: bool = False) -> str:
             sys.stderr.write(r.stdout + r.stderr)
         if r.returncode != 0:
             raise RuntimeError(f"nvcc failed on {src}")
-    cmd = [nvcc(), "-shared", "-o", OUT] + objs + ARCH + ["-ccbin", host_cxx(), "-cudart", "static"]
+    # cuBLAS (the prefill projection GEMMs) is linked dynamically; a process that imported torch
+    # already has a libcublas.so.12 loaded, and the runpath finds the toolkit's otherwise
+    cuda_lib = os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "lib64")
+    cmd = [nvcc(), "-shared", "-o", OUT] + objs + ARCH + ["-ccbin", host_cxx(), "-cudart", "static", "-L", cuda_lib,
+                                                        "-lcublas", "-Xlinker", "-rpath=" + cuda_lib]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         sys.stderr.write(r.stdout + r.stderr)

@@ -21,6 +21,10 @@
 // The output side (src/qwfn_graph.cpp:543-545; prefill :406-407): ggml_mul(attn, ggml_sigmoid(gate))
 // then ggml_mul_mat(attn_output.weight, .) -- output_kernel: the gated attention output, rounded to
 // bf16, in shared memory, and the same weight streaming over attn_output's n_embd rows (16 per CTA).
+#include <mutex>
+
+#include <cublas_v2.h>
+
 #include "qsa_kernels.cuh"
 
 namespace qsa {
@@ -218,6 +222,51 @@ __device__ __forceinline__ void gemv_stream(const uint16_t * __restrict__ wrow0,
     }
 }
 
+// The finish of head group g of `kind` for the a.T (<= FR_TOK) tokens of `a`, their projections in
+// a.y (row stride a.rows_total): the whole CTA builds the (cos, sin) table of every rotated pair of
+// every token; warps 0-3 take token t = warp (norm + IMRoPE, or a copy), warps 4-7 the query
+// group's gate half.
+__device__ __forceinline__ void front_epilogue(const DevDesc & d, const FrontArgs & a, const FrontShape & sh, int kind,
+                                               int g) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, T = a.T;
+    // the (cos, sin) of every rotated pair of every token, computed by the whole CTA
+    __shared__ float2 cs_tab[FR_TOK][128];
+    const int half = d.rope_dim / 2;
+    for (int e = tid; e < T * half; e += FR_THREADS)
+        cs_tab[e / half][e % half] = rope_cs(d, (float) a.pos[e / half], e % half);
+    __syncthreads();
+    const int t = warp & 3;                                     // warps 0-3: token t; warps 4-7: token t's gate
+    if (t >= T) return;
+    const float * yh = a.y + (size_t) t * a.rows_total + sh.row0[kind] + g * sh.group_rows[kind];
+    if (kind == 0) {                                            // query (normed, roped) + gate (raw)
+        float x[8];
+        if (warp < 4) {
+            load_head<8>(yh, x, lane);
+            norm_rope_warp<8>(d, x, a.norm[0], cs_tab[t], lane);
+            store_head<8>(a.q_out + ((size_t) t * d.n_head + g) * HEAD_DIM, x, lane);
+        } else {
+            load_head<8>(yh + HEAD_DIM, x, lane);
+            store_head<8>(a.gate_out + ((size_t) t * d.n_head + g) * HEAD_DIM, x, lane);
+        }
+    } else if (warp >= 4) {
+        return;
+    } else if (kind == 1 || kind == 2) {                        // K (normed, roped) or V (raw)
+        float x[8];
+        load_head<8>(yh, x, lane);
+        if (kind == 1) norm_rope_warp<8>(d, x, a.norm[1], cs_tab[t], lane);
+        store_head<8>((kind == 1 ? a.k_out : a.v_out) + ((size_t) t * d.n_head_kv + g) * HEAD_DIM, x, lane);
+    } else if (kind == 3) {                                     // indexer query (normed, roped)
+        float x[4];
+        load_head<4>(yh, x, lane);
+        norm_rope_warp<4>(d, x, a.norm[2], cs_tab[t], lane);
+        store_head<4>(a.q_idx_out + ((size_t) t * d.idx_n_head + g) * MAX_IDX_DIM, x, lane);
+    } else {                                                    // raw indexer key
+        float x[4];
+        load_head<4>(yh, x, lane);
+        store_head<4>(a.kidx_out + (size_t) t * MAX_IDX_DIM, x, lane);
+    }
+}
+
 __global__ void __launch_bounds__(FR_THREADS, 2) front_kernel(DevDesc d, FrontArgs a) {
     extern __shared__ __align__(16) float xs[];                 // [T][n_embd]
     __shared__ bool is_last;
@@ -268,42 +317,7 @@ __global__ void __launch_bounds__(FR_THREADS, 2) front_kernel(DevDesc d, FrontAr
     }
     __syncthreads();
     if (!is_last) return;
-    // the (cos, sin) of every rotated pair of every token, computed by the whole CTA
-    __shared__ float2 cs_tab[FR_TOK][128];
-    const int half = d.rope_dim / 2;
-    for (int e = tid; e < T * half; e += FR_THREADS)
-        cs_tab[e / half][e % half] = rope_cs(d, (float) a.pos[e / half], e % half);
-    __syncthreads();
-    const int t = warp & 3;                                     // warps 0-3: token t; warps 4-7: token t's gate
-    if (t >= T) return;
-    const float * yh = a.y + (size_t) t * a.rows_total + sh.row0[kind] + g * sh.group_rows[kind];
-    if (kind == 0) {                                            // query (normed, roped) + gate (raw)
-        float x[8];
-        if (warp < 4) {
-            load_head<8>(yh, x, lane);
-            norm_rope_warp<8>(d, x, a.norm[0], cs_tab[t], lane);
-            store_head<8>(a.q_out + ((size_t) t * d.n_head + g) * HEAD_DIM, x, lane);
-        } else {
-            load_head<8>(yh + HEAD_DIM, x, lane);
-            store_head<8>(a.gate_out + ((size_t) t * d.n_head + g) * HEAD_DIM, x, lane);
-        }
-    } else if (warp >= 4) {
-        return;
-    } else if (kind == 1 || kind == 2) {                        // K (normed, roped) or V (raw)
-        float x[8];
-        load_head<8>(yh, x, lane);
-        if (kind == 1) norm_rope_warp<8>(d, x, a.norm[1], cs_tab[t], lane);
-        store_head<8>((kind == 1 ? a.k_out : a.v_out) + ((size_t) t * d.n_head_kv + g) * HEAD_DIM, x, lane);
-    } else if (kind == 3) {                                     // indexer query (normed, roped)
-        float x[4];
-        load_head<4>(yh, x, lane);
-        norm_rope_warp<4>(d, x, a.norm[2], cs_tab[t], lane);
-        store_head<4>(a.q_idx_out + ((size_t) t * d.idx_n_head + g) * MAX_IDX_DIM, x, lane);
-    } else {                                                    // raw indexer key
-        float x[4];
-        load_head<4>(yh, x, lane);
-        store_head<4>(a.kidx_out + (size_t) t * MAX_IDX_DIM, x, lane);
-    }
+    front_epilogue(d, a, sh, kind, g);
 }
 
 constexpr int OUT_ROWS = 16;               // attn_output rows per CTA (2 per warp)
@@ -333,16 +347,108 @@ __global__ void __launch_bounds__(FR_THREADS, 2) output_kernel(const uint16_t * 
         [&](int r, int t, float v) { y[(size_t) t * n_embd + row0 + r] = v; });
 }
 
-struct FrontWs { size_t counters, y, total; };
+constexpr int FR_GEMV_MAX_T = 16;           // above: the projections run as GEMMs (cuBLAS), then the epilogue
+constexpr size_t FR_BLAS_WS = 32u << 20;    // cuBLAS's workspace, a slice of the caller's
 
-FrontWs front_ws(const DevDesc & d) {
+// The GEMM path's finish: grid (head groups, token groups of FR_TOK); y holds every token's rows.
+__global__ void __launch_bounds__(FR_THREADS) front_epilogue_kernel(DevDesc d, FrontArgs a, int T_total) {
+    const FrontShape sh = front_shape(d);
+    int kind = 0, g = blockIdx.x;
+    while (kind < FR_KINDS - 1 && g >= sh.groups[kind]) {
+        g -= sh.groups[kind];
+        kind++;
+    }
+    const int t0 = blockIdx.y * FR_TOK;
+    const size_t kv = (size_t) d.n_head_kv * HEAD_DIM;
+    FrontArgs b = a;
+    b.T = min(FR_TOK, T_total - t0);
+    b.pos = a.pos + t0;
+    b.y = a.y + (size_t) t0 * a.rows_total;
+    b.q_out = a.q_out + (size_t) t0 * d.n_head * HEAD_DIM;
+    b.gate_out = a.gate_out + (size_t) t0 * d.n_head * HEAD_DIM;
+    b.q_idx_out = a.q_idx_out + (size_t) t0 * d.idx_n_head * MAX_IDX_DIM;
+    b.k_out = a.k_out + t0 * kv;
+    b.v_out = a.v_out + t0 * kv;
+    b.kidx_out = a.kidx_out + (size_t) t0 * MAX_IDX_DIM;
+    front_epilogue(d, b, sh, kind, g);
+}
+
+// x (f32) to bf16 (round to nearest even, as the CPU mul_mat converts it), 4 values a thread.
+__global__ void to_bf16_kernel(const float4 * __restrict__ x, uint2 * __restrict__ xb, size_t n4) {
+    for (size_t i = (size_t) blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (size_t) gridDim.x * blockDim.x) {
+        const float4 v = x[i];
+        const uint32_t a0 = __bfloat16_as_ushort(__float2bfloat16_rn(v.x)), a1 = __bfloat16_as_ushort(__float2bfloat16_rn(v.y));
+        const uint32_t a2 = __bfloat16_as_ushort(__float2bfloat16_rn(v.z)), a3 = __bfloat16_as_ushort(__float2bfloat16_rn(v.w));
+        xb[i] = make_uint2(a0 | (a1 << 16), a2 | (a3 << 16));
+    }
+}
+
+struct FrontWs { size_t counters, y, xb, blas, total; };
+
+size_t align256(size_t x) { return (x + 255) & ~(size_t) 255; }
+
+// Up to FR_GEMV_MAX_T tokens: the head-group counters and FR_TOK tokens' projections.  Above: every
+// token's projections, the tokens' activations in bf16, and cuBLAS's workspace.
+FrontWs front_ws(const DevDesc & d, int T, int n_embd) {
     const FrontShape sh = front_shape(d);
     const int rows = sh.row0[FR_KINDS - 1] + MAX_IDX_DIM;
-    FrontWs w;
+    FrontWs w{};
     w.counters = 0;
-    w.y = ((size_t) sh.n_groups * 4 + 255) & ~(size_t) 255;
-    w.total = w.y + (size_t) FR_TOK * rows * 4;
+    w.y = align256((size_t) sh.n_groups * 4);
+    if (T <= FR_GEMV_MAX_T) {
+        w.total = w.y + (size_t) FR_TOK * rows * 4;
+    } else {
+        w.xb = align256(w.y + (size_t) T * rows * 4);
+        w.blas = align256(w.xb + (size_t) T * n_embd * 2);
+        w.total = w.blas + FR_BLAS_WS;
+    }
     return w;
+}
+
+// cuBLAS handles, one per device, created on the device's first GEMM-path call; the mutex also
+// keeps one call's stream, workspace and GEMMs together when threads share a device.
+std::mutex g_blas_mu;
+cublasHandle_t g_blas[64];
+
+cublasHandle_t blas_handle_locked() {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    if (!g_blas[dev] && cublasCreate(&g_blas[dev]) != CUBLAS_STATUS_SUCCESS) g_blas[dev] = nullptr;
+    return g_blas[dev];
+}
+
+// The GEMM path for T > FR_GEMV_MAX_T tokens: x to bf16, then per weight matrix
+// y[t][row0 + r] = sum_e W[r][e] xb[t][e] (bf16 products, f32 accumulation), then the epilogue.
+qsa_status front_gemm(const DevDesc & d, const FrontArgs & a0, int T, const FrontWs & L, unsigned char * wsb,
+                      cudaStream_t st) {
+    const FrontShape sh = front_shape(d);
+    const int n = a0.n_embd;
+    FrontArgs a = a0;
+    a.y = reinterpret_cast<float *>(wsb + L.y);
+    uint16_t * xb = reinterpret_cast<uint16_t *>(wsb + L.xb);
+    const size_t n4 = (size_t) T * n / 4;
+    to_bf16_kernel<<<(unsigned) std::min<size_t>((n4 + 255) / 256, 148 * 8), 256, 0, st>>>(
+        reinterpret_cast<const float4 *>(a.x), reinterpret_cast<uint2 *>(xb), n4);
+    if (cudaGetLastError() != cudaSuccess) return QSA_ERR_CUDA;
+    {
+        std::lock_guard<std::mutex> lock(g_blas_mu);
+        cublasHandle_t h = blas_handle_locked();
+        if (!h) return QSA_ERR_CUDA;
+        if (cublasSetStream(h, st) != CUBLAS_STATUS_SUCCESS ||
+            cublasSetWorkspace(h, wsb + L.blas, FR_BLAS_WS) != CUBLAS_STATUS_SUCCESS)
+            return QSA_ERR_CUDA;
+        const float one = 1.0f, zero = 0.0f;
+        for (int k = 0; k < FR_KINDS; k++) {
+            const int rows_k = sh.groups[k] * sh.group_rows[k];
+            if (cublasGemmEx(h, CUBLAS_OP_T, CUBLAS_OP_N, rows_k, T, n, &one, a.w[k], CUDA_R_16BF, n, xb, CUDA_R_16BF, n,
+                             &zero, a.y + sh.row0[k], CUDA_R_32F, a.rows_total, CUBLAS_COMPUTE_32F,
+                             CUBLAS_GEMM_DEFAULT) != CUBLAS_STATUS_SUCCESS)
+                return QSA_ERR_CUDA;
+        }
+    }
+    front_epilogue_kernel<<<dim3((unsigned) sh.n_groups, (unsigned) ((T + FR_TOK - 1) / FR_TOK)), FR_THREADS, 0, st>>>(
+        d, a, T);
+    return cudaGetLastError() == cudaSuccess ? QSA_OK : QSA_ERR_CUDA;
 }
 
 bool aligned16(const void * p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -353,8 +459,8 @@ bool aligned16(const void * p) { return (reinterpret_cast<uintptr_t>(p) & 15u) =
 using namespace qsa;
 
 extern "C" size_t qsa_front_workspace_size(const qsa_desc * dd, const qsa_front_weights * w, int32_t T) {
-    if (qsa_desc_check(dd) != QSA_OK || !w || T <= 0) return 0;
-    return front_ws(dev_desc(dd)).total;
+    if (qsa_desc_check(dd) != QSA_OK || !w || T <= 0 || w->n_embd <= 0) return 0;
+    return front_ws(dev_desc(dd), T, w->n_embd).total;
 }
 
 extern "C" qsa_status qsa_front(const qsa_desc * dd, const qsa_front_weights * w, int32_t T, const int32_t * pos,
@@ -373,7 +479,7 @@ extern "C" qsa_status qsa_front(const qsa_desc * dd, const qsa_front_weights * w
     for (const void * p : ptrs)
         if (!aligned16(p)) return QSA_ERR_INVALID;
     const DevDesc d = dev_desc(dd);
-    const FrontWs L = front_ws(d);
+    const FrontWs L = front_ws(d, T, w->n_embd);
     if (!ws || ws_bytes < L.total) return QSA_ERR_WORKSPACE;
     static std::atomic<uint64_t> attr{0};
     cudaError_t e = once_per_device(attr, [] {
@@ -394,6 +500,11 @@ extern "C" qsa_status qsa_front(const qsa_desc * dd, const qsa_front_weights * w
     a.n_embd = w->n_embd;
     a.rows_total = sh.row0[FR_KINDS - 1] + MAX_IDX_DIM;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (T > FR_GEMV_MAX_T) {
+        a.pos = pos; a.x = x; a.q_out = q_out; a.gate_out = gate_out; a.q_idx_out = q_idx_out;
+        a.k_out = k_out; a.v_out = v_out; a.kidx_out = kidx_out;
+        return front_gemm(d, a, T, L, wsb, st);
+    }
     const size_t kv = (size_t) d.n_head_kv * HEAD_DIM;
     for (int t0 = 0; t0 < T; t0 += FR_TOK) {                   // token groups run one after another on the stream
         a.T = std::min(FR_TOK, T - t0);

@@ -61,6 +61,35 @@ def test_front_matches_oracle(idx_n_head, T):
         assert e <= NORMED_TOL, (name, e)
 
 
+GEMM_PROJ_TOL = 1e-4    # the GEMM path: cuBLAS's own f32 accumulation order, of the row's sum of |w * x|
+
+
+@pytest.mark.parametrize("idx_n_head,T", [(1, 17), (2, 40)])
+def test_front_gemm_path_matches_oracle(idx_n_head, T):
+    """Above 16 tokens (a prefill chunk) the projections run as GEMMs (bf16 products, f32
+    accumulation) and the norms and IMRoPE as their own kernel over token groups of 4 (17: a
+    last group of one); the outputs agree with the oracle as the GEMV path's do."""
+    d = make_desc(idx_n_head=idx_n_head, n_ctx=1 << 20)
+    w = front_weights(d, seed=50 + T, gammas=True)
+    front = QsaFront(d, **w)
+    g = torch.Generator(device="cuda").manual_seed(51)
+    x = torch.randn(T, front.n_embd, generator=g, device="cuda")
+    pos_list = [int(p) for p in torch.randint(0, 163840, (T,), generator=torch.Generator().manual_seed(T))]
+    pos = torch.tensor(pos_list, dtype=torch.int32, device="cuda")
+    q, gate, q_idx, k, v, kidx = front.project(x, pos)
+    torch.cuda.synchronize()
+    ref = oracle.front(d, host_weights(w), np.array(pos_list, np.int32), x.cpu().numpy())
+    hd = d.head_dim
+    wq_gate = w["wq"].view(d.n_head, 2, hd, -1)[:, 1].reshape(d.n_head * hd, -1)
+    for name, got, wt in (("gate", gate, wq_gate), ("v", v, w["wv"]), ("kidx", kidx, w["wk_idx"])):
+        bound = GEMM_PROJ_TOL * abs_row_sums(wt, x).cpu().numpy()
+        err = np.abs(got.cpu().numpy() - ref[name])
+        assert np.all(err <= bound + 1e-30), (name, float(err.max()), float(bound.max()))
+    for name, got in (("q", q), ("k", k), ("q_idx", q_idx)):
+        e = np.abs(got.cpu().numpy() - ref[name]).max() / np.abs(ref[name]).max()
+        assert e <= NORMED_TOL, (name, e)
+
+
 @pytest.mark.parametrize("b", [3, 2000])
 def test_front_q_idx_equals_gpu_pooled_key(b):
     """The front's indexer query of one-hot activations over weights holding u, at position b*r,
