@@ -318,9 +318,13 @@ qsa_status qsa_front(const qsa_desc * d, const qsa_front_weights * w, int32_t T,
  * sigmoid 1/(1+exp(-g)) in f32, the gated product rounded to bf16 as the CPU mul_mat converts it,
  * f32 accumulation.  wo: bf16 [n_embd][n_head*head_dim] (16-byte aligned); attn: f32
  * [T][n_head][head_dim] (qsa_decode's out); gate: f32 [T][n_head*head_dim] (qsa_front's gate);
- * y: f32 [T][n_embd]. */
+ * y: f32 [T][n_embd].  Up to 16 tokens no workspace is used (ws may be NULL); above, the tokens
+ * run as one cuBLAS GEMM and ws holds qsa_output_workspace_size(d, n_embd, T) bytes (16-byte
+ * aligned).  A device's first call above 16 tokens creates its cuBLAS handle. */
+size_t qsa_output_workspace_size(const qsa_desc * d, int32_t n_embd, int32_t T);
 qsa_status qsa_output(const qsa_desc * d, const void * wo, int32_t n_embd, int32_t w_type, int32_t T,
-                      const float * attn, const float * gate, float * y, qsa_stream_t stream);
+                      const float * attn, const float * gate, float * y, void * ws, size_t ws_bytes,
+                      qsa_stream_t stream);
 
 /* ------------------------------------------------------------------ staging */
 /* Copy `bytes` (a multiple of 16, both addresses 16-byte aligned) from src to dst with a kernel on

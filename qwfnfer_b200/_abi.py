@@ -144,7 +144,8 @@ def lib() -> ctypes.CDLL:
         "qsa_stage_copy": (I32, [VP, VP, SZ, VP]),
         "qsa_front_workspace_size": (SZ, [D, P(QsaFrontWeights), I32]),
         "qsa_front": (I32, [D, P(QsaFrontWeights), I32, VP, VP, VP, VP, VP, VP, VP, VP, VP, SZ, VP]),
-        "qsa_output": (I32, [D, VP, I32, I32, I32, VP, VP, VP, VP]),
+        "qsa_output_workspace_size": (SZ, [D, I32, I32]),
+        "qsa_output": (I32, [D, VP, I32, I32, I32, VP, VP, VP, VP, SZ, VP]),
         "qsa_version": (I32, []),
     }
     for name, (res, args) in sigs.items():
@@ -168,6 +169,7 @@ HEADER_SYMBOLS = [
     "qsa_shard_append_ri", "qsa_shard_decode_ri",
     "qsa_merge_states",
     "qsa_ipc_handle", "qsa_ipc_open", "qsa_ipc_close", "qsa_peer_buffer_bytes", "qsa_peer_push", "qsa_peer_wait",
-    "qsa_prefill_workspace_size", "qsa_prefill", "qsa_front_workspace_size", "qsa_front", "qsa_output", "qsa_stage_copy",
+    "qsa_prefill_workspace_size", "qsa_prefill", "qsa_front_workspace_size", "qsa_front", "qsa_output_workspace_size", "qsa_output",
+    "qsa_stage_copy",
     "qsa_check", "qsa_version",
 ]

@@ -383,6 +383,20 @@ __global__ void to_bf16_kernel(const float4 * __restrict__ x, uint2 * __restrict
     }
 }
 
+// z = bf16(attn * sigmoid(gate)) for the output side's GEMM path, 4 values a thread: the arithmetic
+// of output_kernel's shared-memory staging.
+__global__ void gate_bf16_kernel(const float4 * __restrict__ attn, const float4 * __restrict__ gate,
+                                 uint2 * __restrict__ zb, size_t n4) {
+    auto z = [](float a, float b) {
+        const float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-b)));
+        return (uint32_t) __bfloat16_as_ushort(__float2bfloat16_rn(__fmul_rn(a, sg)));
+    };
+    for (size_t i = (size_t) blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (size_t) gridDim.x * blockDim.x) {
+        const float4 o = attn[i], g = gate[i];
+        zb[i] = make_uint2(z(o.x, g.x) | (z(o.y, g.y) << 16), z(o.z, g.z) | (z(o.w, g.w) << 16));
+    }
+}
+
 struct FrontWs { size_t counters, y, xb, blas, total; };
 
 size_t align256(size_t x) { return (x + 255) & ~(size_t) 255; }
@@ -522,8 +536,24 @@ extern "C" qsa_status qsa_front(const qsa_desc * dd, const qsa_front_weights * w
     return QSA_OK;
 }
 
+// The output side's workspace: none up to FR_GEMV_MAX_T tokens; above, the gated activations in
+// bf16 and cuBLAS's workspace.
+size_t out_ws_bytes(const qsa_desc * d, int T, size_t * blas_off) {
+    if (T <= FR_GEMV_MAX_T) return 0;
+    const size_t zb = (size_t) T * d->n_head * d->head_dim * 2;
+    *blas_off = align256(zb);
+    return *blas_off + FR_BLAS_WS;
+}
+
+extern "C" size_t qsa_output_workspace_size(const qsa_desc * dd, int32_t n_embd, int32_t T) {
+    if (qsa_desc_check(dd) != QSA_OK || n_embd <= 0 || T <= 0) return 0;
+    size_t off = 0;
+    return out_ws_bytes(dd, T, &off);
+}
+
 extern "C" qsa_status qsa_output(const qsa_desc * dd, const void * wo, int32_t n_embd, int32_t w_type, int32_t T,
-                                 const float * attn, const float * gate, float * y, qsa_stream_t stream) {
+                                 const float * attn, const float * gate, float * y, void * ws, size_t ws_bytes,
+                                 qsa_stream_t stream) {
     qsa_status s = qsa_desc_check(dd);
     if (s != QSA_OK) return s;
     if (!wo || !attn || !gate || !y || T <= 0 || n_embd <= 0) return QSA_ERR_INVALID;
@@ -532,6 +562,28 @@ extern "C" qsa_status qsa_output(const qsa_desc * dd, const void * wo, int32_t n
         return QSA_ERR_INVALID;
     const int n_in = dd->n_head * dd->head_dim;
     if (n_in > OUT_MAX_IN || n_in % 8 != 0) return QSA_ERR_UNSUPPORTED;
+    size_t blas_off = 0;
+    const size_t need = out_ws_bytes(dd, T, &blas_off);
+    if (need && (!ws || ws_bytes < need || !aligned16(ws))) return QSA_ERR_WORKSPACE;
+    if (T > FR_GEMV_MAX_T) {       // a prefill-sized batch: y = zb wo^T as one GEMM
+        cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+        unsigned char * wsb = static_cast<unsigned char *>(ws);
+        uint16_t * zb = reinterpret_cast<uint16_t *>(wsb);
+        const size_t n4 = (size_t) T * n_in / 4;
+        gate_bf16_kernel<<<(unsigned) std::min<size_t>((n4 + 255) / 256, 148 * 8), 256, 0, st>>>(
+            reinterpret_cast<const float4 *>(attn), reinterpret_cast<const float4 *>(gate), reinterpret_cast<uint2 *>(zb), n4);
+        if (cudaGetLastError() != cudaSuccess) return QSA_ERR_CUDA;
+        std::lock_guard<std::mutex> lock(g_blas_mu);
+        cublasHandle_t h = blas_handle_locked();
+        if (!h) return QSA_ERR_CUDA;
+        const float one = 1.0f, zero = 0.0f;
+        if (cublasSetStream(h, st) != CUBLAS_STATUS_SUCCESS ||
+            cublasSetWorkspace(h, wsb + blas_off, FR_BLAS_WS) != CUBLAS_STATUS_SUCCESS ||
+            cublasGemmEx(h, CUBLAS_OP_T, CUBLAS_OP_N, n_embd, T, n_in, &one, wo, CUDA_R_16BF, n_in, zb, CUDA_R_16BF, n_in,
+                         &zero, y, CUDA_R_32F, n_embd, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT) != CUBLAS_STATUS_SUCCESS)
+            return QSA_ERR_CUDA;
+        return QSA_OK;
+    }
     static std::atomic<uint64_t> attr{0};
     cudaError_t e = once_per_device(attr, [] {
         return cudaFuncSetAttribute(output_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FR_TOK * OUT_MAX_IN * 4);

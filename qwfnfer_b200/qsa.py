@@ -314,12 +314,24 @@ class QsaOutput:
         if wo.dtype != torch.bfloat16 or wo.dim() != 2 or wo.shape[1] != desc.n_head * desc.head_dim:
             raise QsaError(_abi.QSA_ERR_INVALID, "attn_output weight: bf16 [n_embd][n_head*head_dim]")
         self.desc, self.wo, self.n_embd = desc, wo, int(wo.shape[0])
+        self._ws: torch.Tensor | None = None
+
+    def workspace(self, T: int) -> torch.Tensor | None:
+        """The workspace of a T-token call (none up to 16 tokens; above, the GEMM path's)."""
+        size = lib().qsa_output_workspace_size(ctypes.byref(self.desc), self.n_embd, T)
+        if size == 0:
+            return None
+        if self._ws is None or self._ws.numel() < size:
+            self._ws = torch.empty(size, dtype=torch.uint8, device=self.wo.device)
+        return self._ws
 
     def project(self, attn: torch.Tensor, gate: torch.Tensor, out: torch.Tensor | None = None, stream=None):
         """attn f32 [T][n_head][head_dim], gate f32 [T][n_head*head_dim] -> y f32 [T][n_embd]."""
         T = attn.shape[0]
         if out is None:
             out = torch.empty((T, self.n_embd), dtype=torch.float32, device=self.wo.device)
+        ws = self.workspace(T)
         check(lib().qsa_output(ctypes.byref(self.desc), _ptr(self.wo), self.n_embd, TYPE_BF16, T, _ptr(attn), _ptr(gate),
-                               _ptr(out), _stream(stream)), "qsa_output")
+                               _ptr(out), None if ws is None else ws.data_ptr(), 0 if ws is None else ws.numel(),
+                               _stream(stream)), "qsa_output")
         return out

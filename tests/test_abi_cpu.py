@@ -106,12 +106,17 @@ def test_front_host_refusals():
 def test_output_host_refusals():
     d = make_desc(n_ctx=4096)
     L = lib()
-    call = lambda wt=_abi.TYPE_BF16, n_embd=2560, attn=A, T=1: L.qsa_output(ctypes.byref(d), A, n_embd, wt, T, attn, A, A,
-                                                                          None)
+    call = lambda wt=_abi.TYPE_BF16, n_embd=2560, attn=A, T=1, ws_bytes=0: L.qsa_output(
+        ctypes.byref(d), A, n_embd, wt, T, attn, A, A, A if ws_bytes else None, ws_bytes, None)
     assert call(wt=TYPE_F16) == _abi.QSA_ERR_UNSUPPORTED
     assert call(attn=A + 4) == _abi.QSA_ERR_INVALID
     assert call(n_embd=0) == _abi.QSA_ERR_INVALID
     assert call(T=0) == _abi.QSA_ERR_INVALID
+    assert L.qsa_output_workspace_size(ctypes.byref(d), 2560, 16) == 0           # the GEMV path needs none
+    need = L.qsa_output_workspace_size(ctypes.byref(d), 2560, 64)
+    assert need >= 64 * 4096 * 2
+    assert call(T=64) == _abi.QSA_ERR_WORKSPACE                                   # the GEMM path without one
+    assert call(T=64, ws_bytes=need - 16) == _abi.QSA_ERR_WORKSPACE
 
 
 def test_stage_copy_host_refusals():

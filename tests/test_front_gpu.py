@@ -159,7 +159,7 @@ def test_front_argument_errors():
     torch.cuda.synchronize()
 
 
-def output_bound(wo: torch.Tensor, attn: torch.Tensor, gate: torch.Tensor) -> np.ndarray:
+def output_bound(wo: torch.Tensor, attn: torch.Tensor, gate: torch.Tensor, tol: float = PROJ_TOL) -> np.ndarray:
     """Per (token, row): 1e-5 of the sum of |w * z| plus one bf16 rounding step of the largest term
     (the device and host expf may round one gated value to a neighbouring bf16)."""
     T = attn.shape[0]
@@ -167,7 +167,7 @@ def output_bound(wo: torch.Tensor, attn: torch.Tensor, gate: torch.Tensor) -> np
     W = wo.float().abs()
     s = z @ W.T
     m = torch.stack([(z[t][None, :] * W).max(dim=1).values for t in range(T)])
-    return (PROJ_TOL * s + 2 ** -7 * m).cpu().numpy()
+    return (tol * s + 2 ** -7 * m).cpu().numpy()
 
 
 @pytest.mark.parametrize("T,n_embd", [(1, 2560), (5, 2560), (2, 1000)])
@@ -183,6 +183,24 @@ def test_output_matches_oracle(T, n_embd):
     ref = oracle.output(d, wo.view(torch.int16).cpu().numpy().view(np.uint16), attn.cpu().numpy(), gate.cpu().numpy())
     err = np.abs(y.cpu().numpy() - ref)
     bound = output_bound(wo, attn, gate)
+    assert np.all(err <= bound), float((err / bound).max())
+
+
+@pytest.mark.parametrize("T,n_embd", [(17, 2560), (48, 1000)])
+def test_output_gemm_path_matches_oracle(T, n_embd):
+    """Above 16 tokens the output side is one GEMM (cuBLAS, bf16 products, f32 accumulation) over
+    the gated activations rounded to bf16; the bound takes cuBLAS's accumulation order (GEMM_PROJ_TOL)."""
+    d = make_desc()
+    g = torch.Generator(device="cuda").manual_seed(61 + T)
+    n_in = d.n_head * d.head_dim
+    wo = (torch.randn(n_embd, n_in, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    attn = torch.randn(T, d.n_head, d.head_dim, generator=g, device="cuda")
+    gate = 2 * torch.randn(T, n_in, generator=g, device="cuda")
+    y = QsaOutput(d, wo).project(attn, gate)
+    torch.cuda.synchronize()
+    ref = oracle.output(d, wo.view(torch.int16).cpu().numpy().view(np.uint16), attn.cpu().numpy(), gate.cpu().numpy())
+    err = np.abs(y.cpu().numpy() - ref)
+    bound = output_bound(wo, attn, gate, GEMM_PROJ_TOL)
     assert np.all(err <= bound), float((err / bound).max())
 
 
@@ -215,10 +233,13 @@ def test_output_argument_errors():
     gate = torch.zeros(1, n_in, device="cuda")
     y = torch.zeros(1, 64, device="cuda")
     L, st = lib(), torch.cuda.current_stream().cuda_stream
-    assert L.qsa_output(ctypes.byref(d), wo.data_ptr(), 64, TYPE_F16, 1, attn.data_ptr(), gate.data_ptr(),
-                        y.data_ptr(), st) == QSA_ERR_UNSUPPORTED
-    assert L.qsa_output(ctypes.byref(d), wo.data_ptr(), 64, TYPE_BF16, 1, attn.data_ptr() + 4, gate.data_ptr(),
-                        y.data_ptr(), st) == QSA_ERR_INVALID
-    assert L.qsa_output(ctypes.byref(d), wo.data_ptr(), 0, TYPE_BF16, 1, attn.data_ptr(), gate.data_ptr(),
-                        y.data_ptr(), st) == QSA_ERR_INVALID
+
+    def call(w_type=TYPE_BF16, n_embd=64, ap=attn.data_ptr(), T=1):
+        return L.qsa_output(ctypes.byref(d), wo.data_ptr(), n_embd, w_type, T, ap, gate.data_ptr(), y.data_ptr(),
+                            None, 0, st)
+
+    assert call(w_type=TYPE_F16) == QSA_ERR_UNSUPPORTED
+    assert call(ap=attn.data_ptr() + 4) == QSA_ERR_INVALID
+    assert call(n_embd=0) == QSA_ERR_INVALID
+    assert call(T=32) == QSA_ERR_WORKSPACE            # above 16 tokens the GEMM path needs a workspace
     torch.cuda.synchronize()
