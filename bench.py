@@ -398,10 +398,48 @@ def run_ours_config2(args, ws, rank, local):
     return res
 
 
-def front_stage(d, dev, n_past, flush, K, seed):
-    """The projection front feeding the node (qsa_front: attn_q/k/v and the indexer projections
-    over n_embd 2560, their norms and IMRoPE) for this token: graph replay, L2 flushed, its own
-    HBM roofline (the bf16 weights dominate its bytes)."""
+def _stage_time(fn, flush, n, graph):
+    """Mean device time (us) of n calls of fn, each after the L2 flush: replayed from a CUDA graph
+    (decode-sized calls, where launches matter) or called directly (prefill-sized ones)."""
+    import torch
+
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    run = fn
+    if graph:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        run = g.replay
+    ev = []
+    for _ in range(n):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        run()
+        b.record()
+        ev.append((a, b))
+    torch.cuda.synchronize()
+    return statistics.mean(a.elapsed_time(b) * 1e3 for a, b in ev)
+
+
+def _stage_roofline(T, us, nbytes, flops):
+    """HBM roofline for decode-sized calls (the weights dominate), tensor roofline above 16 tokens."""
+    hbm, tfs, src = peaks()
+    if T <= 16:
+        ach = nbytes / (us * 1e-6) / 1e9
+        return {"bound": "hbm", "algorithmic_bytes": nbytes, "achieved_gbs": round(ach, 1), "peak": hbm,
+                "frac": round(ach / hbm, 4), "peak_source": f"{src} hbm_gbs (burst)"}
+    ach = flops / (us * 1e-6) / 1e12
+    return {"bound": "tensor", "flops": flops, "achieved_tflops": round(ach, 1), "peak": tfs,
+            "frac": round(ach / tfs, 4), "peak_source": f"{src} bf16_tflops (burst)"}
+
+
+def front_stage(d, dev, n_past, flush, K, seed, T=1):
+    """The projection front feeding the node (qsa_front: attn_q/k/v and the indexer projections over
+    n_embd 2560, their norms and IMRoPE) for T tokens ending at n_past, L2 flushed before each call:
+    the bf16 GEMV up to 16 tokens, cuBLAS GEMMs and the epilogue kernel above."""
     import torch
 
     from qwfnfer_b200.configs import front_weights
@@ -409,37 +447,21 @@ def front_stage(d, dev, n_past, flush, K, seed):
 
     w = front_weights(d, seed=seed + 50, device=dev)
     front = QsaFront(d, **w)
-    x = torch.randn(1, front.n_embd, generator=torch.Generator(device=dev).manual_seed(seed + 51), device=dev)
-    pos = torch.tensor([n_past], dtype=torch.int32, device=dev)
-    for _ in range(3):
-        outs = front.project(x, pos)
-    torch.cuda.synchronize()
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
-        outs = front.project(x, pos)
-    us = []
-    for _ in range(max(K, 20)):
-        flush.zero_()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        g.replay()
-        b.record()
-        us.append((a, b))
-    torch.cuda.synchronize()
-    us = [a.elapsed_time(b) * 1e3 for a, b in us]
+    x = torch.randn(T, front.n_embd, generator=torch.Generator(device=dev).manual_seed(seed + 51), device=dev)
+    pos = torch.arange(n_past - T + 1, n_past + 1, dtype=torch.int32, device=dev)
+    outs = front.project(x, pos)
+    us = _stage_time(lambda: front.project(x, pos), flush, max(K, 20) if T <= 16 else max(K, 5), graph=T <= 16)
     w_bytes = sum(t.numel() * t.element_size() for t in w.values())
+    rows = sum(t.shape[0] for k, t in w.items() if k.startswith("w"))
     nbytes = w_bytes + x.numel() * 4 + sum(o.numel() * 4 for o in outs)
-    mean = statistics.mean(us)
-    hbm, _, src = peaks()
-    ach = nbytes / (mean * 1e-6) / 1e9
-    return {"kernel": "front_kernel (qsa_front), 1 token, n_embd 2560, bf16 weights", "us": round(mean, 3),
-            "algorithmic_bytes": nbytes, "achieved_gbs": round(ach, 1), "peak": hbm,
-            "frac": round(ach / hbm, 4), "peak_source": f"{src} hbm_gbs (burst)", "launches": 1}
+    path = "front_kernel (bf16 GEMV)" if T <= 16 else "cuBLAS bf16 GEMMs + front_epilogue_kernel"
+    return {"kernel": f"qsa_front, {T} token(s), n_embd 2560: {path}", "us": round(us, 3),
+            **_stage_roofline(T, us, nbytes, 2 * T * rows * front.n_embd), "launches": 1 if T <= 16 else 7}
 
 
-def output_stage(d, dev, flush, K, seed):
+def output_stage(d, dev, flush, K, seed, T=1):
     """The output side after the node (qsa_output: attention output times sigmoid(gate), then the
-    bf16 attn_output projection to n_embd 2560) for one token: graph replay, L2 flushed, HBM roofline."""
+    bf16 attn_output projection to n_embd 2560) for T tokens, L2 flushed before each call."""
     import torch
 
     from qwfnfer_b200.configs import N_EMBD
@@ -448,32 +470,16 @@ def output_stage(d, dev, flush, K, seed):
     g = torch.Generator(device=dev).manual_seed(seed + 60)
     n_in = d.n_head * d.head_dim
     wo = (torch.randn(N_EMBD, n_in, generator=g, device=dev) * 0.02).to(torch.bfloat16)
-    attn = torch.randn(1, d.n_head, d.head_dim, generator=g, device=dev)
-    gate = torch.randn(1, n_in, generator=g, device=dev)
-    out = torch.empty(1, N_EMBD, device=dev)
+    attn = torch.randn(T, d.n_head, d.head_dim, generator=g, device=dev)
+    gate = torch.randn(T, n_in, generator=g, device=dev)
+    out = torch.empty(T, N_EMBD, device=dev)
     op = QsaOutput(d, wo)
-    for _ in range(3):
-        op.project(attn, gate, out=out)
-    torch.cuda.synchronize()
-    gr = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(gr):
-        op.project(attn, gate, out=out)
-    ev = []
-    for _ in range(max(K, 20)):
-        flush.zero_()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        gr.replay()
-        b.record()
-        ev.append((a, b))
-    torch.cuda.synchronize()
-    mean = statistics.mean(a.elapsed_time(b) * 1e3 for a, b in ev)
+    us = _stage_time(lambda: op.project(attn, gate, out=out), flush, max(K, 20) if T <= 16 else max(K, 5),
+                     graph=T <= 16)
     nbytes = wo.numel() * 2 + attn.numel() * 4 + gate.numel() * 4 + out.numel() * 4
-    hbm, _, src = peaks()
-    ach = nbytes / (mean * 1e-6) / 1e9
-    return {"kernel": "output_kernel (qsa_output), 1 token, 4096 -> n_embd 2560, bf16 weights", "us": round(mean, 3),
-            "algorithmic_bytes": nbytes, "achieved_gbs": round(ach, 1), "peak": hbm,
-            "frac": round(ach / hbm, 4), "peak_source": f"{src} hbm_gbs (burst)", "launches": 1}
+    path = "output_kernel (bf16 GEMV)" if T <= 16 else "gate_bf16_kernel + cuBLAS bf16 GEMM"
+    return {"kernel": f"qsa_output, {T} token(s), 4096 -> n_embd 2560: {path}", "us": round(us, 3),
+            **_stage_roofline(T, us, nbytes, 2 * T * N_EMBD * n_in), "launches": 1 if T <= 16 else 2}
 
 
 def _timed_replays(graph, n, before=None):
@@ -893,7 +899,7 @@ def run_ours_config4(args, ws, rank, local):
     _, tfs, src = peaks()
     achieved = (flops_idx + flops_attn) / (step_mean * 1e-6) / 1e12
     toks = T * ws
-    return {
+    res = {
         "metric": "sparse-attn prefill tok/s @8192 on 155648 q8_0", "value": round(toks / (total_us * 1e-6), 1),
         "unit": "tok/s", "n_gpus": ws, "steps": K, "warmup": args.warmup, "ms_per_step": round(total_us / 1e3, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -912,6 +918,10 @@ def run_ours_config4(args, ws, rank, local):
         "gpu_launches": launches * K,       # libqsa kernels per replay (CUPTI count) x timed steps
         "clocks": clocks.summary(),
     }
+    # the projections around the node for this chunk, reported beside the node's metric
+    res["front"] = front_stage(d, dev, n_past + T - 1, flush, K, cfg.seed, T=T)
+    res["output"] = output_stage(d, dev, flush, K, cfg.seed, T=T)
+    return res
 
 
 def run_reference_config2(args):
