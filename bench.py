@@ -2,17 +2,22 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|3|5]
 
-Default workload: decode of one token on one sparse-attention layer at
+Default workload (benchmark config 2): decode of one token on one sparse-attention layer at
 163,840-token context, q8_0 KV, 16 query / 2 KV heads, head_dim 256, one 128-dim indexer head,
 top-64 of 2560 blocks of 64 cells + a 128-token window (67 blocks, 4288 cells).  A step is the
 whole node: append of the token's K/V/raw key (+ the pooled key of the block it completes),
 indexer scores + top-k, and split-K attention.  Metric: microseconds per layer-token (lower is
 better).  Inputs are resident in HBM; L2 is flushed (256 MB write) before every timed step.
-  --config 3: 64 sequences, lengths U[4096, 163840] (seed 2), one batched decode step.
-  --config 4: chunked prefill of 8192 tokens at position 155,648 (tok/s).
-  --config 5: 12 layers at 1,048,576 tokens, top-128, one token through all 12 layers.
-With N > 1 GPUs (torchrun) each rank runs the workload on its own GPU ("replicas", config 2) or
-its share of the sequences (config 3, data parallel); value = total units / max-over-ranks time.
+The default line also carries the other configurations as sub-objects, each with its own timing,
+clocks and roofline (--headline-only skips them):
+  "batched"  config 3: 64 sequences, lengths U[4096, 163840] (seed 2), one batched decode step;
+             with N ranks each GPU decodes its 64/N sequences (data parallel, no collective);
+  "prefill"  config 4: chunked prefill of 8192 tokens at position 155,648 (tok/s, tensor roofline);
+  "sharded"  config 5: one token through 12 layers at 1,048,576 tokens, top-128, the KV sequence
+             sharded over the N ranks (layer after layer, and the 12 independent layers as one batch).
+  --config 3|4|5 runs one of them alone as the line.
+With N > 1 GPUs (torchrun) each rank runs config 2 on its own GPU ("replicas");
+value = total units / max-over-ranks time.
 --impl reference times the reference's CPU algorithm (the oracle/ port, all host cores).
 """
 from __future__ import annotations
@@ -20,7 +25,6 @@ from __future__ import annotations
 import argparse
 import json
 import os
-import re
 import statistics
 import subprocess
 import sys
@@ -43,13 +47,10 @@ def peaks():
     return HBM_FALLBACK_GBS, BF16_FALLBACK_TFS, "fallback"
 
 
-def profile_traffic(name: str):
-    """dram bytes per launch of the dominant kernel, from the committed ncu summary (or None)."""
-    p = os.path.join(ROOT, "profiles", name)
-    if not os.path.exists(p):
-        return None
-    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", open(p).read())
-    return float(m.group(1)) if m else None
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the config-2 decode
+# attention, from one ncu capture of this kernel (not measured by this run; the capture's command
+# and figures are in profiles/attn_decode_config2.md).
+ATTN_CONFIG2_NCU_TRAFFIC = 4706560
 
 
 NVML_SAMPLER = r"""
@@ -376,7 +377,9 @@ def run_ours_config2(args, ws, rank, local):
         "roofline": {"bound": "hbm", "kernel": "attn_kernel<q8_0> (qsa_decode_attend)",
                      "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4), "peak_source": f"{src} hbm_gbs (burst)",
-                     "traffic": profile_traffic("attn_decode_config2.md"),
+                     "traffic": ATTN_CONFIG2_NCU_TRAFFIC,
+                     "traffic_source": "ncu capture of this kernel at this workload (profiles/attn_decode_config2.md), "
+                                       "not measured in this run",
                      "algorithmic_bytes_per_launch": attn_bytes, "launch_us": round(attn_mean, 3)},
         "step_roofline": {"algorithmic_bytes": step_bytes,
                           "achieved_gbs": round(step_bytes / (statistics.mean(step_us) * 1e-6) / 1e9, 1)},
@@ -816,7 +819,7 @@ def run_ours_config5(args, ws, rank, local):
 
 
 def run_ours_config4(args, ws, rank, local):
-    """Chunked prefill: 8192 new tokens appended at position 155,648 of a
+    """Chunked prefill (benchmark config 4): 8192 new tokens appended at position 155,648 of a
     q8_0 cache; a step is one qsa_prefill call (append of the chunk's K/V/raw keys and pooled
     keys, indexer scores of every query, per-query top-k + window, sparse attention)."""
     import ctypes
@@ -983,6 +986,34 @@ def run_reference_config2(args):
     }
 
 
+def _sub(res):
+    """A configuration's line as a sub-object of the headline line (its own timing, roofline, e2e
+    and clocks; the keys the headline already states are dropped)."""
+    return {k: v for k, v in res.items() if k not in ("n_gpus", "steps", "warmup", "vs_baseline", "data", "dtype")}
+
+
+def run_sub_benches(args, ws, rank, local):
+    """Configs 3, 4 and 5 beside the headline (every rank runs the same sequence of them)."""
+    import torch
+    sub = argparse.Namespace(**vars(args))
+    sub.steps = max(5, min(args.steps, 20))
+    out = {}
+    runs = (("batched", run_ours_config3, {}), ("prefill", run_ours_config4, {}),
+            ("sharded.layer_after_layer", run_ours_config5, {"layer_batch": False}),
+            ("sharded.layer_batched", run_ours_config5, {"layer_batch": True}))
+    for key, fn, over in runs:
+        a = argparse.Namespace(**{**vars(sub), **over})
+        r = _sub(fn(a, ws, rank, local))
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        if "." in key:
+            k0, k1 = key.split(".")
+            out.setdefault(k0, {})[k1] = r
+        else:
+            out[key] = r
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -991,6 +1022,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--headline-only", action="store_true",
+                    help="config 2 only, without the batched / prefill / sharded sub-objects")
     ap.add_argument("--layer-batch", action="store_true",
                     help="config 5: issue the 12 independent layers as one batch of 12 items (2 exchanges per token)")
     ap.add_argument("--index", default="replicated", choices=["sharded", "replicated"],
@@ -1015,6 +1048,8 @@ def main():
     ws, rank, local = dist_setup("nccl")
     if args.config == 2:
         res = run_ours_config2(args, ws, rank, local)
+        if not args.headline_only:
+            res.update(run_sub_benches(args, ws, rank, local))
     elif args.config == 3:
         res = run_ours_config3(args, ws, rank, local)
     elif args.config == 4:

@@ -177,11 +177,12 @@ qsa_status qsa_decode_attend(const qsa_desc * d, const qsa_decode_item * items, 
  * budget must not call cudaMalloc on the token path -- the scratch lives in a fixed device array
  * of 8 MiB inside the library (held on every GPU that loads it, until exit).  Arguments and
  * results are those of qsa_decode; a call whose qsa_decode_workspace_size() exceeds 8 MiB returns
- * QSA_ERR_WORKSPACE.  The first call on a device looks up the array's device address and zeroes
- * it (synchronously): make that first call before any stream capture.  Every call zeroes the
- * array's status word and counters and otherwise reuses the last call's contents, so calls that
- * overlap on the GPU (other streams or threads) race; device-side range errors cannot be read back
- * through this entry point (the affected query's output is zero).  Nothing is allocated. */
+ * QSA_ERR_WORKSPACE.  The first call on a device looks up the array's device address (a host-side
+ * query, cudaGetSymbolAddress): make that first call before any stream capture.  Every call zeroes
+ * the array's status word and counters on `stream` and otherwise reuses the last call's contents,
+ * so calls that overlap on the GPU (other streams or threads) race; device-side range errors cannot
+ * be read back through this entry point (the affected query's output is zero).  Nothing is
+ * allocated. */
 qsa_status qsa_decode_noalloc(const qsa_desc * d, const qsa_decode_item * items, int32_t batch, int32_t max_n_kv,
                               const void * q, int32_t q_type, const float * q_idx,
                               const float * k_new, const float * v_new, const float * kidx_new,
@@ -250,8 +251,11 @@ qsa_status qsa_merge_states(const qsa_desc * d, int32_t n_parts, int32_t batch, 
  * uint32 per buffer, owned by this rank).  qsa_peer_wait returns once all n_ranks slices of the
  * round are in this rank's buffer (bounded wait: QSA_ERR_TIMEOUT through the status word of `ws`,
  * read by qsa_check).  slot_bytes is a multiple of 4; slots start at a stride rounded up to 16
- * bytes.  All ranks must push and wait on a buffer in the same order.  No
- * counterpart in the reference. */
+ * bytes; n_ranks is at most 32.  All ranks must push and wait on a buffer in the same order.
+ * A push overwrites the peers' slots without waiting for them to finish reading the previous
+ * round, so a caller alternates at least two buffers (channels): a rank pushes into a channel
+ * again only after a wait on another channel, which the peers' own pushes (made after they
+ * consumed this channel) complete.  No counterpart in the reference. */
 qsa_status qsa_ipc_handle(const void * ptr, void * handle /* host, 64 bytes */, size_t * offset /* host */);
 qsa_status qsa_ipc_open(const void * handle /* host, 64 bytes */, void ** base /* host */);
 qsa_status qsa_ipc_close(void * base);
@@ -306,7 +310,7 @@ size_t qsa_front_workspace_size(const qsa_desc * d, const qsa_front_weights * w,
  *   v_out     f32 [T][n_head_kv*head_dim]    raw
  *   kidx_out  f32 [T][idx_dim]               raw (normed and roped when pooled)
  * which are qsa_decode's q (QSA_TYPE_F32), q_idx, k_new, v_new and kidx_new.  The workspace is
- * zeroed once (qsa_workspace_init).  Replaces the projection, norm and rope nodes of
+ * zeroed once (qsa_workspace_init); above 16 tokens it must be 256-byte aligned (QSA_ERR_WORKSPACE).  Replaces the projection, norm and rope nodes of
  * src/qwfn_graph.cpp:465, 479-484, 505-518. */
 qsa_status qsa_front(const qsa_desc * d, const qsa_front_weights * w, int32_t T, const int32_t * pos,
                      const float * x, float * q_out, float * gate_out, float * q_idx_out,
@@ -319,8 +323,8 @@ qsa_status qsa_front(const qsa_desc * d, const qsa_front_weights * w, int32_t T,
  * f32 accumulation.  wo: bf16 [n_embd][n_head*head_dim] (16-byte aligned); attn: f32
  * [T][n_head][head_dim] (qsa_decode's out); gate: f32 [T][n_head*head_dim] (qsa_front's gate);
  * y: f32 [T][n_embd].  Up to 16 tokens no workspace is used (ws may be NULL); above, the tokens
- * run as one cuBLAS GEMM and ws holds qsa_output_workspace_size(d, n_embd, T) bytes (16-byte
- * aligned).  A device's first call above 16 tokens creates its cuBLAS handle. */
+ * run as one cuBLAS GEMM and ws holds qsa_output_workspace_size(d, n_embd, T) bytes (256-byte
+ * aligned, else QSA_ERR_WORKSPACE).  A device's first call above 16 tokens creates its cuBLAS handle. */
 size_t qsa_output_workspace_size(const qsa_desc * d, int32_t n_embd, int32_t T);
 qsa_status qsa_output(const qsa_desc * d, const void * wo, int32_t n_embd, int32_t w_type, int32_t T,
                       const float * attn, const float * gate, float * y, void * ws, size_t ws_bytes,

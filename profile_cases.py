@@ -1,11 +1,11 @@
 """Small, fixed workloads of the QSA kernels for profilers (ncu captures one launch of them).
 
-    python -m qwfnfer_b200.profile_cases batch B STEPS    # B decode queries over one config-2 cache
-    python -m qwfnfer_b200.profile_cases decode STEPS     # the config-2 decode step (append + select + attend)
-    python -m qwfnfer_b200.profile_cases prefill T N_PAST STEPS   # one qsa_prefill chunk (config-4 shape)
-    python -m qwfnfer_b200.profile_cases front T STEPS    # qsa_front for T tokens (n_embd 2560, bf16 weights)
-    python -m qwfnfer_b200.profile_cases output T STEPS   # qsa_output for T tokens (4096 -> 2560, bf16 weights)
-    python -m torch.distributed.run --nproc-per-node N ... -m qwfnfer_b200.profile_cases shard5 peer|nccl [lb] [ri]
+    python profile_cases.py batch B STEPS    # B decode queries over one config-2 cache
+    python profile_cases.py decode STEPS     # the config-2 decode step (append + select + attend)
+    python profile_cases.py prefill T N_PAST STEPS   # one qsa_prefill chunk (config-4 shape)
+    python profile_cases.py front T STEPS    # qsa_front for T tokens (n_embd 2560, bf16 weights)
+    python profile_cases.py output T STEPS   # qsa_output for T tokens (4096 -> 2560, bf16 weights)
+    python -m torch.distributed.run --nproc-per-node N ... profile_cases.py shard5 peer|nccl [lb] [ri]
                                                           # config-5 sharded step: per-kernel timeline per rank
 
 `batch` places the B queries at positions 163839 - 64 i of one 160K q8_0 cache (no append), so the attention runs in its
@@ -21,12 +21,15 @@ the step (CUPTI activity records; a breakdown, not a bench value).
 """
 from __future__ import annotations
 
+import os
 import sys
 
 import torch
 
-from .configs import CONFIGS, fill_cache, token_inputs
-from .qsa import QsaNode, QsaState, decode_items
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+
+from qwfnfer_b200.configs import CONFIGS, fill_cache, token_inputs  # noqa: E402
+from qwfnfer_b200.qsa import QsaNode, QsaState, decode_items  # noqa: E402
 
 
 def main(argv: list[str]) -> None:
@@ -95,8 +98,8 @@ def prefill(argv: list[str]) -> None:
 
 
 def front(argv: list[str]) -> None:
-    from .configs import front_weights
-    from .qsa import QsaFront
+    from qwfnfer_b200.configs import front_weights
+    from qwfnfer_b200.qsa import QsaFront
 
     T = int(argv[0]) if argv else 1
     steps = int(argv[1]) if len(argv) > 1 else 3
@@ -119,8 +122,8 @@ def front(argv: list[str]) -> None:
 
 
 def output(argv: list[str]) -> None:
-    from .configs import N_EMBD
-    from .qsa import QsaOutput
+    from qwfnfer_b200.configs import N_EMBD
+    from qwfnfer_b200.qsa import QsaOutput
 
     T = int(argv[0]) if argv else 1
     steps = int(argv[1]) if len(argv) > 1 else 3
@@ -152,8 +155,8 @@ def shard5(argv: list[str]) -> None:
     import torch.distributed as dist
     from torch.profiler import ProfilerActivity, profile
 
-    from ._abi import k_blocks
-    from .shard import ShardedDecoder
+    from qwfnfer_b200._abi import k_blocks
+    from qwfnfer_b200.shard import ShardedDecoder
 
     local, ws = int(os.environ.get("LOCAL_RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
     torch.cuda.set_device(local)

@@ -495,6 +495,8 @@ extern "C" qsa_status qsa_front(const qsa_desc * dd, const qsa_front_weights * w
     const DevDesc d = dev_desc(dd);
     const FrontWs L = front_ws(d, T, w->n_embd);
     if (!ws || ws_bytes < L.total) return QSA_ERR_WORKSPACE;
+    // the GEMM path hands slices of ws to cuBLAS, which wants its workspace 256-byte aligned
+    if (T > FR_GEMV_MAX_T && (reinterpret_cast<uintptr_t>(ws) & 255u)) return QSA_ERR_WORKSPACE;
     static std::atomic<uint64_t> attr{0};
     cudaError_t e = once_per_device(attr, [] {
         return cudaFuncSetAttribute(front_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FR_TOK * FR_MAX_EMBD * 4);
@@ -564,7 +566,7 @@ extern "C" qsa_status qsa_output(const qsa_desc * dd, const void * wo, int32_t n
     if (n_in > OUT_MAX_IN || n_in % 8 != 0) return QSA_ERR_UNSUPPORTED;
     size_t blas_off = 0;
     const size_t need = out_ws_bytes(dd, T, &blas_off);
-    if (need && (!ws || ws_bytes < need || !aligned16(ws))) return QSA_ERR_WORKSPACE;
+    if (need && (!ws || ws_bytes < need || (reinterpret_cast<uintptr_t>(ws) & 255u))) return QSA_ERR_WORKSPACE;
     if (T > FR_GEMV_MAX_T) {       // a prefill-sized batch: y = zb wo^T as one GEMM
         cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
         unsigned char * wsb = static_cast<unsigned char *>(ws);

@@ -77,10 +77,12 @@ __global__ void peer_wait_kernel(const void * __restrict__ local_buf, int n_rank
     if (r >= n_ranks) return;
     const uint32_t * flags = reinterpret_cast<const uint32_t *>(static_cast<const unsigned char *>(local_buf) +
                                                                 (size_t) n_ranks * peer_stride(slot_bytes));
+    // A flag at or past this round's epoch means the peer's slice of this round has landed (the
+    // difference as a signed value, so the test survives the counter wrapping).
     const uint32_t e = *epoch;
-    if (ld_acquire_sys(flags + r) != e) {
+    if ((int32_t) (ld_acquire_sys(flags + r) - e) < 0) {
         const uint64_t t0 = global_timer_ns();
-        while (ld_acquire_sys(flags + r) != e) {
+        while ((int32_t) (ld_acquire_sys(flags + r) - e) < 0) {
             if (global_timer_ns() - t0 > 2000000000ull) {
                 set_status(status, DEV_TIMEOUT);
                 break;
@@ -155,13 +157,14 @@ qsa_status qsa_ipc_close(void * base) {
 }
 
 size_t qsa_peer_buffer_bytes(int32_t n_ranks, size_t slot_bytes) {
-    if (n_ranks <= 0 || slot_bytes == 0 || slot_bytes % 4 != 0) return 0;
+    if (n_ranks <= 0 || n_ranks > 32 || slot_bytes == 0 || slot_bytes % 4 != 0) return 0;
     return (size_t) n_ranks * peer_stride(slot_bytes) + (size_t) ((n_ranks * 4 + 255) & ~255);
 }
 
 qsa_status qsa_peer_push(void * const * bufs, int32_t n_ranks, int32_t rank, const void * src, size_t slot_bytes,
                          uint32_t * epoch, uint32_t * counter, qsa_stream_t stream) {
-    if (!bufs || !src || !epoch || !counter || n_ranks <= 0 || rank < 0 || rank >= n_ranks || slot_bytes == 0 ||
+    if (!bufs || !src || !epoch || !counter || n_ranks <= 0 || n_ranks > 32 || rank < 0 || rank >= n_ranks ||
+        slot_bytes == 0 ||
         slot_bytes % 4 != 0 || reinterpret_cast<uintptr_t>(src) % 16 != 0)
         return QSA_ERR_INVALID;
     return launch_peer_push(reinterpret_cast<cudaStream_t>(stream), bufs, n_ranks, rank, src, slot_bytes, epoch,

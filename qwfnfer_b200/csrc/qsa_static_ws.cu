@@ -23,7 +23,9 @@ void * g_scratch_addr[MAX_DEVICES];   // the array's device address, per device 
 
 // Device address of the array on the current device.  In host code the array's name is only a
 // host-side stand-in; the address kernels may use comes from cudaGetSymbolAddress, taken once
-// per device with that device current.  The first call also zeroes the whole array.
+// per device with that device current.  Nothing is written here: each call zeroes the part of
+// the array that must start at zero on the caller's stream (a memset on another stream would be
+// unordered against a non-blocking caller stream).
 qsa_status scratch_for_current_device(void ** out) {
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEVICES) return QSA_ERR_CUDA;
@@ -31,7 +33,6 @@ qsa_status scratch_for_current_device(void ** out) {
     if (!g_scratch_addr[dev]) {
         void * p = nullptr;
         if (cudaGetSymbolAddress(&p, g_qsa_static_scratch) != cudaSuccess || !p) return QSA_ERR_CUDA;
-        if (cudaMemset(p, 0, QSA_STATIC_SCRATCH_BYTES) != cudaSuccess) return QSA_ERR_CUDA;
         g_scratch_addr[dev] = p;
     }
     *out = g_scratch_addr[dev];
@@ -52,7 +53,8 @@ extern "C" qsa_status qsa_decode_noalloc(const qsa_desc * d, const qsa_decode_it
     void * ws = nullptr;
     if ((s = scratch_for_current_device(&ws)) != QSA_OK) return s;
     // The array keeps the previous call's contents, and the workspace layout moves with the batch
-    // size: zero the status word and arrival counters (the layout's leading region) every call.
+    // size: zero the status word and arrival counters (the layout's leading region, the only part
+    // the kernels read before writing) every call, on the caller's stream.
     const size_t zero_bytes = qsa::decode_workspace_zero_prefix(d, batch, max_n_kv);
     if (cudaMemsetAsync(ws, 0, zero_bytes, reinterpret_cast<cudaStream_t>(stream)) != cudaSuccess) return QSA_ERR_CUDA;
     return qsa_decode(d, items, batch, max_n_kv, q, q_type, q_idx, k_new, v_new, kidx_new, out, sel_out,

@@ -242,10 +242,17 @@ class ShardedDecoder:
         self.backend = backend if backend is not None else LibShardBackend(desc)
         self.kb = k_blocks(desc)
         self.peer = None
+        self._steps = 0
         if exchange == "peer" and self.world > 1:
+            # Channels: 0 candidates, 1 and 2 states.  A push overwrites the peers' slots without
+            # waiting for them to finish reading the last round, so consecutive pushes into one
+            # channel are always separated by a wait on another: the sharded-index step alternates
+            # candidates and states; the replicated-index step (states only) alternates 1 and 2.
+            # A rank's push of round e+2 into a channel then follows its wait of round e+1, which
+            # needs every peer's push of e+1, which each peer issues after its merge read round e.
             state_floats = lib().qsa_shard_state_floats(ctypes.byref(desc))
-            self.peer = PeerExchange([2 * batch * self.kb * 4, batch * state_floats * 4], group=group,
-                                     device=self.backend.device)
+            sb = batch * state_floats * 4
+            self.peer = PeerExchange([2 * batch * self.kb * 4, sb, sb], group=group, device=self.backend.device)
 
     def _all_gather(self, t: torch.Tensor, channel: int = 0):
         """(gathered, stride): every rank's t in rank order, slices `stride` elements apart
@@ -281,7 +288,9 @@ class ShardedDecoder:
         if self.index_replicated:
             state = self.backend.decode_ri(items, batch, max_n_kv, self.blocks, q, q_idx, k_new, v_new, kidx_new,
                                            sel_out=sel_out)
-            states, _ = self._all_gather(state, 1)
+            channel = 1 + (self._steps & 1)
+            self._steps += 1
+            states, _ = self._all_gather(state, channel)
             return self.backend.merge(states.view(self.world, batch, -1))
         cand = self.backend.candidates(items, batch, max_n_kv, self.blocks, q_idx, k_new, v_new, kidx_new)
         gathered, cstride = self._all_gather(cand, 0)

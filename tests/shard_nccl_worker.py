@@ -1,7 +1,7 @@
 """One rank of the sharded decode over NCCL (launched by tests/test_zz_shard_nccl.py):
 
     python -m torch.distributed.run --nnodes 1 --nproc-per-node N --master-addr 127.0.0.1 \
-        --master-port P tests/shard_nccl_worker.py [nccl|peer] [sharded|replicated]
+        --master-port P tests/shard_nccl_worker.py [nccl|peer] [sharded|replicated] [delay]
 
 The exchange is NCCL's all-gather or libqsa's all-gather over NVLink peer memory; the indexer
 caches are sharded with the K/V (candidates exchanged) or replicated on every rank.
@@ -11,12 +11,18 @@ new token, the two all-gathers, the merge), and checks its status.  Rank 0 also 
 unsharded caches on its GPU and runs qsa_decode on them; every rank's output and selection are
 gathered to rank 0 and compared with it.  Rank 0 prints one line `SHARD_NCCL {...}`; the exit
 code is 0 only if every check passed.
+
+With `delay`, the step runs three times back to back and the last rank's host sleeps between
+launching each peer push and the wait behind it, so the other ranks publish later rounds while
+its wait has not been launched yet: the exchange must neither time out nor let a later round's
+push overwrite slots still being read (every step's output is checked).
 """
 from __future__ import annotations
 
 import json
 import os
 import sys
+import time
 from datetime import timedelta
 
 import torch
@@ -33,6 +39,26 @@ from qwfnfer_b200.shard import ShardedDecoder  # noqa: E402
 ATTN_TOL = 2e-3
 
 
+def _delay_waits(peer, seconds):
+    """Make this rank's host sleep between launching each push and its wait."""
+    import qwfnfer_b200.shard as shard_mod
+    real = shard_mod.lib
+
+    class Slow:
+        def __getattr__(self, name):
+            fn = getattr(real(), name)
+            if name != "qsa_peer_wait":
+                return fn
+
+            def wait(*a):
+                torch.cuda.synchronize()        # the push has run; the peers may move on meanwhile
+                time.sleep(seconds)
+                return fn(*a)
+            return wait
+
+    shard_mod.lib = lambda: Slow()
+
+
 def main() -> int:
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
@@ -44,7 +70,10 @@ def main() -> int:
     seeds = [41, 42]
     exchange = sys.argv[1] if len(sys.argv) > 1 else "nccl"
     index = sys.argv[2] if len(sys.argv) > 2 else "sharded"
+    delay = len(sys.argv) > 3 and sys.argv[3] == "delay"
     dec = ShardedDecoder(d, exchange=exchange, batch=2, index=index)
+    if delay and dec.peer is not None and rank == world - 1:
+        _delay_waits(dec.peer, 0.05)
     node = QsaNode(d)
     sts = [QsaState(d, blocks=dec.blocks, index_full=dec.index_replicated) for _ in positions]
     for st, n, s in zip(sts, positions, seeds):
@@ -53,7 +82,10 @@ def main() -> int:
     items = decode_items([s.layer() for s in sts], positions)
     B, KB, max_n_kv = len(positions), k_blocks(d), max(positions) + 1
     sel = torch.empty((B, KB), dtype=torch.int32, device=dev)
-    out = dec.step(items, B, max_n_kv, q, q_idx, k, v, ki, sel_out=sel)
+    # with `delay`, the same step (it rewrites the token's row with the same bytes) three times
+    step_outs = [dec.step(items, B, max_n_kv, q, q_idx, k, v, ki, sel_out=sel).clone() for _ in range(3 if delay else 1)]
+    out = step_outs[-1]
+    steps_equal = all(torch.equal(o, out) for o in step_outs)
     st_code = dec.backend.check(B, max_n_kv)
     if dec.peer is not None and st_code == QSA_OK:
         st_code = dec.peer.check()
@@ -78,8 +110,10 @@ def main() -> int:
         sel_ok = [bool(torch.equal(s, sel_ref)) for s in sels]
         same = all(torch.equal(o, outs[0]) for o in outs)
         statuses = [int(s.item()) for s in stats]
-        ok = all(sel_ok) and max(errs) <= ATTN_TOL and same and all(s == QSA_OK for s in statuses)
+        ok = (all(sel_ok) and max(errs) <= ATTN_TOL and same and all(s == QSA_OK for s in statuses)
+              and steps_equal)
         print("SHARD_NCCL " + json.dumps({"world": world, "exchange": exchange, "index": index, "blocks": dec.blocks,
+                                          "delay": delay, "steps_equal": steps_equal,
                                           "rel_err": errs, "sel_equal": sel_ok,
                                           "ranks_identical": same, "status": statuses, "ok": ok}), flush=True)
     flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=dev)

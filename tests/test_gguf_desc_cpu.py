@@ -36,7 +36,7 @@ STANDIN = {"block_count": 8, "embedding_length": 2560, "context_length": 262144,
 
 
 def test_standin_layer_descriptor(tmp_path):
-    """A file with the BASELINE stand-in's shapes: layers 3 and 7 are the sparse-attention layers;
+    """A file with the benchmark stand-in's shapes: layers 3 and 7 are the sparse-attention layers;
     top_k 4033 at r = 64 keeps ceil((4033 + 63) / 64) = 64 blocks, the tail block among them."""
     p = tmp_path / "standin.gguf"
     write_gguf(p, STANDIN)

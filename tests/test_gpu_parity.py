@@ -1,6 +1,6 @@
 """Parity of the CUDA path (libqsa.so through its C ABI) with the CPU oracle, on a B200.
 
-Bars (BASELINE north star): q8_0/f16 cache bytes bit-exact; pooled keys within 1e-5 (f32 before
+Bars: q8_0/f16 cache bytes bit-exact; pooled keys within 1e-5 (f32 before
 the f16 store); selected block sets bit-exact excluding near-ties; attention within 2e-3 max
 relative error (fp32 softmax).  The oracle always reads the bytes the GPU wrote.
 """
@@ -120,12 +120,12 @@ def _desc_kwargs(d):
 
 
 def test_decode_config1_shape_f16():
-    """BASELINE config 1 shape: 4K context, f16 KV, top-16 + window, f32 query."""
+    """Benchmark config 1 shape: 4K context, f16 KV, top-16 + window, f32 query."""
     run_decode_case(desc_for(TYPE_F16, 4096, top_k=16), 4095, seed=0, q_dtype=torch.float32)
 
 
 def test_decode_config2_full_size_q8_0():
-    """163,840-token q8_0 cache, top-64 of 2560 + window, bf16 query."""
+    """Benchmark config 2: 163,840-token q8_0 cache, top-64 of 2560 + window, bf16 query."""
     run_decode_case(desc_for(TYPE_Q8_0, 163840), 163839, seed=1)
 
 
@@ -137,7 +137,7 @@ def test_decode_edge_cases(n_past, window, top_k):
 
 
 def test_batched_decode_ragged_lengths():
-    """BASELINE config 3 pattern: independent sequences of different lengths in one call."""
+    """Benchmark config 3 pattern: independent sequences of different lengths in one call."""
     lengths = [4096, 163839, 70000, 4095, 1000, 130000 + 63, 64 * 67, 99999]
     run_decode_case(desc_for(TYPE_Q8_0, 163840), None, seed=2, batch_lengths=lengths)
 

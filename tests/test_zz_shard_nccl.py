@@ -29,12 +29,16 @@ def _free_port():
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("exchange,index", [("nccl", "sharded"), ("peer", "sharded"), ("peer", "replicated")])
-def test_sharded_decode_over_ranks(exchange, index):
+@pytest.mark.parametrize("exchange,index,delay", [("nccl", "sharded", ""), ("peer", "sharded", ""),
+                                                 ("peer", "replicated", ""), ("peer", "replicated", "delay"),
+                                                 ("peer", "sharded", "delay")])
+def test_sharded_decode_over_ranks(exchange, index, delay):
+    """`delay`: three steps back to back, the last rank's host sleeping between each peer push and
+    its wait (later rounds published before its wait launches)."""
     n = min(4, torch.cuda.device_count())
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes", "1",
            "--nproc-per-node", str(n), "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
-           os.path.join(TESTS, "shard_nccl_worker.py"), exchange, index]
+           os.path.join(TESTS, "shard_nccl_worker.py"), exchange, index] + ([delay] if delay else [])
     r = subprocess.run(cmd, capture_output=True, text=True, env=dict(os.environ, NCCL_NVLS_ENABLE="0"))
     lines = [l for l in r.stdout.splitlines() if l.startswith("SHARD_NCCL ")]
     assert r.returncode == 0 and lines, r.stdout[-3000:] + r.stderr[-3000:]
