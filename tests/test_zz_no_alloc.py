@@ -82,9 +82,11 @@ def test_noalloc_decode_with_append_matches_workspace_decode():
         torch.cuda.synchronize()
         assert np.array_equal(sel.cpu().numpy(), sel_ref.cpu().numpy())
         assert rel_err(out.cpu().numpy(), out_ref.cpu().numpy()) <= ATTN_TOL
-        for a, b in zip(mine, twin):
-            for x, y in ((a.k, b.k), (a.v, b.v), (a.idx, b.idx), (a.pool, b.pool)):
-                assert torch.equal(x[0], y[0])
+        for a, b, p in zip(mine, twin, positions):      # the written rows (the rest is uninitialised)
+            for x, y in ((a.k, b.k), (a.v, b.v), (a.idx, b.idx)):
+                assert torch.equal(x[0][:p + 1], y[0][:p + 1])
+            nb = (p + 1) // d.ratio
+            assert torch.equal(a.pool[0][:nb], b.pool[0][:nb])
 
 
 def test_noalloc_decode_at_its_scratch_limit():
