@@ -442,7 +442,7 @@ def _stage_roofline(T, us, nbytes, flops):
 def front_stage(d, dev, n_past, flush, K, seed, T=1):
     """The projection front feeding the node (qsa_front: attn_q/k/v and the indexer projections over
     n_embd 2560, their norms and IMRoPE) for T tokens ending at n_past, L2 flushed before each call:
-    the bf16 GEMV up to 16 tokens, cuBLAS GEMMs and the epilogue kernel above."""
+    the bf16 GEMV up to 16 tokens, the tcgen05 projection GEMM (norms and IMRoPE in its epilogue) above."""
     import torch
 
     from qwfnfer_b200.configs import front_weights
@@ -457,9 +457,9 @@ def front_stage(d, dev, n_past, flush, K, seed, T=1):
     w_bytes = sum(t.numel() * t.element_size() for t in w.values())
     rows = sum(t.shape[0] for k, t in w.items() if k.startswith("w"))
     nbytes = w_bytes + x.numel() * 4 + sum(o.numel() * 4 for o in outs)
-    path = "front_kernel (bf16 GEMV)" if T <= 16 else "cuBLAS bf16 GEMMs + front_epilogue_kernel"
+    path = "front_kernel (bf16 GEMV)" if T <= 16 else "to_bf16 + rope table + proj_gemm_kernel (tcgen05, fused norm/IMRoPE epilogue)"
     return {"kernel": f"qsa_front, {T} token(s), n_embd 2560: {path}", "us": round(us, 3),
-            **_stage_roofline(T, us, nbytes, 2 * T * rows * front.n_embd), "launches": 1 if T <= 16 else 7}
+            **_stage_roofline(T, us, nbytes, 2 * T * rows * front.n_embd), "launches": 1 if T <= 16 else 3}
 
 
 def output_stage(d, dev, flush, K, seed, T=1):
@@ -480,7 +480,7 @@ def output_stage(d, dev, flush, K, seed, T=1):
     us = _stage_time(lambda: op.project(attn, gate, out=out), flush, max(K, 20) if T <= 16 else max(K, 5),
                      graph=T <= 16)
     nbytes = wo.numel() * 2 + attn.numel() * 4 + gate.numel() * 4 + out.numel() * 4
-    path = "output_kernel (bf16 GEMV)" if T <= 16 else "gate_bf16_kernel + cuBLAS bf16 GEMM"
+    path = "output_kernel (bf16 GEMV)" if T <= 16 else "gate_bf16_kernel + proj_gemm_kernel (tcgen05)"
     return {"kernel": f"qsa_output, {T} token(s), 4096 -> n_embd 2560: {path}", "us": round(us, 3),
             **_stage_roofline(T, us, nbytes, 2 * T * N_EMBD * n_in), "launches": 1 if T <= 16 else 2}
 

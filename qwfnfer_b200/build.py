@@ -17,7 +17,7 @@ import sys
 PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
-SOURCES = ["qsa_api.cu", "qsa_append.cu", "qsa_select.cu", "qsa_attn.cu", "qsa_shard.cu", "qsa_prefill_tc.cu", "qsa_prefill_attn.cu", "qsa_peer.cu", "qsa_static_ws.cu", "qsa_stage.cu", "qsa_front.cu"]
+SOURCES = ["qsa_api.cu", "qsa_append.cu", "qsa_select.cu", "qsa_attn.cu", "qsa_shard.cu", "qsa_prefill_tc.cu", "qsa_prefill_attn.cu", "qsa_peer.cu", "qsa_static_ws.cu", "qsa_stage.cu", "qsa_front.cu", "qsa_proj_gemm.cu"]
 OUT = os.path.join(PKG, "libqsa.so")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -56,11 +56,7 @@ def build_lib(verbose: bool = False) -> str:
             sys.stderr.write(r.stdout + r.stderr)
         if r.returncode != 0:
             raise RuntimeError(f"nvcc failed on {src}")
-    # cuBLAS (the prefill projection GEMMs) is linked dynamically; a process that imported torch
-    # already has a libcublas.so.12 loaded, and the runpath finds the toolkit's otherwise
-    cuda_lib = os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "lib64")
-    cmd = [nvcc(), "-shared", "-o", OUT] + objs + ARCH + ["-ccbin", host_cxx(), "-cudart", "static", "-L", cuda_lib,
-                                                        "-lcublas", "-Xlinker", "-rpath=" + cuda_lib]
+    cmd = [nvcc(), "-shared", "-o", OUT] + objs + ARCH + ["-ccbin", host_cxx(), "-cudart", "static"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         sys.stderr.write(r.stdout + r.stderr)

@@ -21,10 +21,6 @@
 // The output side (src/qwfn_graph.cpp:543-545; prefill :406-407): ggml_mul(attn, ggml_sigmoid(gate))
 // then ggml_mul_mat(attn_output.weight, .) -- output_kernel: the gated attention output, rounded to
 // bf16, in shared memory, and the same weight streaming over attn_output's n_embd rows (16 per CTA).
-#include <mutex>
-
-#include <cublas_v2.h>
-
 #include "qsa_kernels.cuh"
 
 namespace qsa {
@@ -347,31 +343,7 @@ __global__ void __launch_bounds__(FR_THREADS, 2) output_kernel(const uint16_t * 
         [&](int r, int t, float v) { y[(size_t) t * n_embd + row0 + r] = v; });
 }
 
-constexpr int FR_GEMV_MAX_T = 16;           // above: the projections run as GEMMs (cuBLAS), then the epilogue
-constexpr size_t FR_BLAS_WS = 32u << 20;    // cuBLAS's workspace, a slice of the caller's
-
-// The GEMM path's finish: grid (head groups, token groups of FR_TOK); y holds every token's rows.
-__global__ void __launch_bounds__(FR_THREADS) front_epilogue_kernel(DevDesc d, FrontArgs a, int T_total) {
-    const FrontShape sh = front_shape(d);
-    int kind = 0, g = blockIdx.x;
-    while (kind < FR_KINDS - 1 && g >= sh.groups[kind]) {
-        g -= sh.groups[kind];
-        kind++;
-    }
-    const int t0 = blockIdx.y * FR_TOK;
-    const size_t kv = (size_t) d.n_head_kv * HEAD_DIM;
-    FrontArgs b = a;
-    b.T = min(FR_TOK, T_total - t0);
-    b.pos = a.pos + t0;
-    b.y = a.y + (size_t) t0 * a.rows_total;
-    b.q_out = a.q_out + (size_t) t0 * d.n_head * HEAD_DIM;
-    b.gate_out = a.gate_out + (size_t) t0 * d.n_head * HEAD_DIM;
-    b.q_idx_out = a.q_idx_out + (size_t) t0 * d.idx_n_head * MAX_IDX_DIM;
-    b.k_out = a.k_out + t0 * kv;
-    b.v_out = a.v_out + t0 * kv;
-    b.kidx_out = a.kidx_out + (size_t) t0 * MAX_IDX_DIM;
-    front_epilogue(d, b, sh, kind, g);
-}
+constexpr int FR_GEMV_MAX_T = 16;           // above: the projections run as tcgen05 GEMMs (qsa_proj_gemm.cu)
 
 // x (f32) to bf16 (round to nearest even, as the CPU mul_mat converts it), 4 values a thread.
 __global__ void to_bf16_kernel(const float4 * __restrict__ x, uint2 * __restrict__ xb, size_t n4) {
@@ -397,72 +369,63 @@ __global__ void gate_bf16_kernel(const float4 * __restrict__ attn, const float4 
     }
 }
 
-struct FrontWs { size_t counters, y, xb, blas, total; };
+// (cos, sin) of every rotated pair of every token: cs[t][i] = rope_cs(pos[t], i), i < rope_dim/2.
+__global__ void rope_table_kernel(DevDesc d, const int * __restrict__ pos, int T, float2 * __restrict__ cs) {
+    const int half = d.rope_dim / 2;
+    for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < T * half; e += gridDim.x * blockDim.x)
+        cs[e] = rope_cs(d, (float) pos[e / half], e % half);
+}
+
+// The front's workspace.  Up to FR_GEMV_MAX_T tokens: the status word, the head-group counters and
+// FR_TOK tokens' projections.  Above: the status word, the tokens' activations in bf16 and their
+// rope table.
+struct FrontWs { size_t status, counters, y, xb, cs, total; bool gemm; };
 
 size_t align256(size_t x) { return (x + 255) & ~(size_t) 255; }
 
-// Up to FR_GEMV_MAX_T tokens: the head-group counters and FR_TOK tokens' projections.  Above: every
-// token's projections, the tokens' activations in bf16, and cuBLAS's workspace.
+// The GEMM path's epilogue rotates 32-column chunks against their partners: rope_dim a multiple of
+// 64 (other rope widths run through the GEMV path in token groups).
+bool front_gemm_path(const DevDesc & d, int T) { return T > FR_GEMV_MAX_T && d.rope_dim % 64 == 0; }
+
 FrontWs front_ws(const DevDesc & d, int T, int n_embd) {
     const FrontShape sh = front_shape(d);
     const int rows = sh.row0[FR_KINDS - 1] + MAX_IDX_DIM;
     FrontWs w{};
-    w.counters = 0;
-    w.y = align256((size_t) sh.n_groups * 4);
-    if (T <= FR_GEMV_MAX_T) {
+    w.status = 0;
+    w.counters = 16;
+    w.gemm = front_gemm_path(d, T);
+    if (!w.gemm) {
+        w.y = align256(w.counters + (size_t) sh.n_groups * 4);
         w.total = w.y + (size_t) FR_TOK * rows * 4;
     } else {
-        w.xb = align256(w.y + (size_t) T * rows * 4);
-        w.blas = align256(w.xb + (size_t) T * n_embd * 2);
-        w.total = w.blas + FR_BLAS_WS;
+        w.xb = 256;
+        w.cs = align256(w.xb + (size_t) T * n_embd * 2);
+        w.total = align256(w.cs + (size_t) T * (d.rope_dim / 2) * 8);
     }
     return w;
 }
 
-// cuBLAS handles, one per device, created on the device's first GEMM-path call; the mutex also
-// keeps one call's stream, workspace and GEMMs together when threads share a device.
-std::mutex g_blas_mu;
-cublasHandle_t g_blas[64];
-
-cublasHandle_t blas_handle_locked() {
-    int dev = -1;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-    if (!g_blas[dev] && cublasCreate(&g_blas[dev]) != CUBLAS_STATUS_SUCCESS) g_blas[dev] = nullptr;
-    return g_blas[dev];
+unsigned grid_for(size_t n, int per_thread_block = 256) {
+    return (unsigned) std::min<size_t>((n + per_thread_block - 1) / per_thread_block, 148 * 8);
 }
 
-// The GEMM path for T > FR_GEMV_MAX_T tokens: x to bf16, then per weight matrix
-// y[t][row0 + r] = sum_e W[r][e] xb[t][e] (bf16 products, f32 accumulation), then the epilogue.
-qsa_status front_gemm(const DevDesc & d, const FrontArgs & a0, int T, const FrontWs & L, unsigned char * wsb,
+// The GEMM path for T > FR_GEMV_MAX_T tokens: x to bf16, the rope table, then one tcgen05 GEMM over
+// the five weight matrices whose epilogue applies the norms and IMRoPE and stores the outputs.
+qsa_status front_gemm(const DevDesc & d, const FrontArgs & a, int T, const FrontWs & L, unsigned char * wsb,
                       cudaStream_t st) {
-    const FrontShape sh = front_shape(d);
-    const int n = a0.n_embd;
-    FrontArgs a = a0;
-    a.y = reinterpret_cast<float *>(wsb + L.y);
+    const int n = a.n_embd;
     uint16_t * xb = reinterpret_cast<uint16_t *>(wsb + L.xb);
+    float2 * cs = reinterpret_cast<float2 *>(wsb + L.cs);
     const size_t n4 = (size_t) T * n / 4;
-    to_bf16_kernel<<<(unsigned) std::min<size_t>((n4 + 255) / 256, 148 * 8), 256, 0, st>>>(
-        reinterpret_cast<const float4 *>(a.x), reinterpret_cast<uint2 *>(xb), n4);
+    to_bf16_kernel<<<grid_for(n4), 256, 0, st>>>(reinterpret_cast<const float4 *>(a.x), reinterpret_cast<uint2 *>(xb), n4);
+    rope_table_kernel<<<grid_for((size_t) T * (d.rope_dim / 2)), 256, 0, st>>>(d, a.pos, T, cs);
     if (cudaGetLastError() != cudaSuccess) return QSA_ERR_CUDA;
-    {
-        std::lock_guard<std::mutex> lock(g_blas_mu);
-        cublasHandle_t h = blas_handle_locked();
-        if (!h) return QSA_ERR_CUDA;
-        if (cublasSetStream(h, st) != CUBLAS_STATUS_SUCCESS ||
-            cublasSetWorkspace(h, wsb + L.blas, FR_BLAS_WS) != CUBLAS_STATUS_SUCCESS)
-            return QSA_ERR_CUDA;
-        const float one = 1.0f, zero = 0.0f;
-        for (int k = 0; k < FR_KINDS; k++) {
-            const int rows_k = sh.groups[k] * sh.group_rows[k];
-            if (cublasGemmEx(h, CUBLAS_OP_T, CUBLAS_OP_N, rows_k, T, n, &one, a.w[k], CUDA_R_16BF, n, xb, CUDA_R_16BF, n,
-                             &zero, a.y + sh.row0[k], CUDA_R_32F, a.rows_total, CUBLAS_COMPUTE_32F,
-                             CUBLAS_GEMM_DEFAULT) != CUBLAS_STATUS_SUCCESS)
-                return QSA_ERR_CUDA;
-        }
-    }
-    front_epilogue_kernel<<<dim3((unsigned) sh.n_groups, (unsigned) ((T + FR_TOK - 1) / FR_TOK)), FR_THREADS, 0, st>>>(
-        d, a, T);
-    return cudaGetLastError() == cudaSuccess ? QSA_OK : QSA_ERR_CUDA;
+    const void * w[5] = {a.w[0], a.w[1], a.w[2], a.w[3], a.w[4]};
+    const float * norm[3] = {a.norm[0], a.norm[1], a.norm[2]};
+    float * out[6] = {a.q_out, a.gate_out, a.q_idx_out, a.k_out, a.v_out, a.kidx_out};
+    const cudaError_t e = launch_proj_gemm_front(d, st, T, n, xb, w, false, cs, norm, out,
+                                                 reinterpret_cast<uint32_t *>(wsb + L.status));
+    return e == cudaSuccess ? QSA_OK : (e == cudaErrorNotSupported ? QSA_ERR_UNSUPPORTED : QSA_ERR_CUDA);
 }
 
 bool aligned16(const void * p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -495,8 +458,8 @@ extern "C" qsa_status qsa_front(const qsa_desc * dd, const qsa_front_weights * w
     const DevDesc d = dev_desc(dd);
     const FrontWs L = front_ws(d, T, w->n_embd);
     if (!ws || ws_bytes < L.total) return QSA_ERR_WORKSPACE;
-    // the GEMM path hands slices of ws to cuBLAS, which wants its workspace 256-byte aligned
-    if (T > FR_GEMV_MAX_T && (reinterpret_cast<uintptr_t>(ws) & 255u)) return QSA_ERR_WORKSPACE;
+    // the GEMM path's tensor maps want their base addresses 16-byte aligned (slices of ws at 256)
+    if (L.gemm && (reinterpret_cast<uintptr_t>(ws) & 15u)) return QSA_ERR_WORKSPACE;
     static std::atomic<uint64_t> attr{0};
     cudaError_t e = once_per_device(attr, [] {
         return cudaFuncSetAttribute(front_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FR_TOK * FR_MAX_EMBD * 4);
@@ -516,7 +479,7 @@ extern "C" qsa_status qsa_front(const qsa_desc * dd, const qsa_front_weights * w
     a.n_embd = w->n_embd;
     a.rows_total = sh.row0[FR_KINDS - 1] + MAX_IDX_DIM;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    if (T > FR_GEMV_MAX_T) {
+    if (L.gemm) {
         a.pos = pos; a.x = x; a.q_out = q_out; a.gate_out = gate_out; a.q_idx_out = q_idx_out;
         a.k_out = k_out; a.v_out = v_out; a.kidx_out = kidx_out;
         return front_gemm(d, a, T, L, wsb, st);
@@ -538,13 +501,12 @@ extern "C" qsa_status qsa_front(const qsa_desc * dd, const qsa_front_weights * w
     return QSA_OK;
 }
 
-// The output side's workspace: none up to FR_GEMV_MAX_T tokens; above, the gated activations in
-// bf16 and cuBLAS's workspace.
-size_t out_ws_bytes(const qsa_desc * d, int T, size_t * blas_off) {
+// The output side's workspace: none up to FR_GEMV_MAX_T tokens; above, the status word and the gated
+// activations in bf16 (the GEMM's A operand).
+size_t out_ws_bytes(const qsa_desc * d, int T, size_t * z_off) {
     if (T <= FR_GEMV_MAX_T) return 0;
-    const size_t zb = (size_t) T * d->n_head * d->head_dim * 2;
-    *blas_off = align256(zb);
-    return *blas_off + FR_BLAS_WS;
+    *z_off = 256;
+    return align256(*z_off + (size_t) T * d->n_head * d->head_dim * 2);
 }
 
 extern "C" size_t qsa_output_workspace_size(const qsa_desc * dd, int32_t n_embd, int32_t T) {
@@ -564,27 +526,21 @@ extern "C" qsa_status qsa_output(const qsa_desc * dd, const void * wo, int32_t n
         return QSA_ERR_INVALID;
     const int n_in = dd->n_head * dd->head_dim;
     if (n_in > OUT_MAX_IN || n_in % 8 != 0) return QSA_ERR_UNSUPPORTED;
-    size_t blas_off = 0;
-    const size_t need = out_ws_bytes(dd, T, &blas_off);
-    if (need && (!ws || ws_bytes < need || (reinterpret_cast<uintptr_t>(ws) & 255u))) return QSA_ERR_WORKSPACE;
+    size_t z_off = 0;
+    const size_t need = out_ws_bytes(dd, T, &z_off);
+    if (need && (!ws || ws_bytes < need || !aligned16(ws))) return QSA_ERR_WORKSPACE;
     if (T > FR_GEMV_MAX_T) {       // a prefill-sized batch: y = zb wo^T as one GEMM
+        if (n_embd % 4 != 0) return QSA_ERR_UNSUPPORTED;      // float4 rows of the epilogue's stores
+        if (!aligned16(y)) return QSA_ERR_INVALID;
         cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
         unsigned char * wsb = static_cast<unsigned char *>(ws);
-        uint16_t * zb = reinterpret_cast<uint16_t *>(wsb);
+        uint16_t * zb = reinterpret_cast<uint16_t *>(wsb + z_off);
         const size_t n4 = (size_t) T * n_in / 4;
-        gate_bf16_kernel<<<(unsigned) std::min<size_t>((n4 + 255) / 256, 148 * 8), 256, 0, st>>>(
-            reinterpret_cast<const float4 *>(attn), reinterpret_cast<const float4 *>(gate), reinterpret_cast<uint2 *>(zb), n4);
+        gate_bf16_kernel<<<grid_for(n4), 256, 0, st>>>(reinterpret_cast<const float4 *>(attn),
+                                                      reinterpret_cast<const float4 *>(gate), reinterpret_cast<uint2 *>(zb), n4);
         if (cudaGetLastError() != cudaSuccess) return QSA_ERR_CUDA;
-        std::lock_guard<std::mutex> lock(g_blas_mu);
-        cublasHandle_t h = blas_handle_locked();
-        if (!h) return QSA_ERR_CUDA;
-        const float one = 1.0f, zero = 0.0f;
-        if (cublasSetStream(h, st) != CUBLAS_STATUS_SUCCESS ||
-            cublasSetWorkspace(h, wsb + blas_off, FR_BLAS_WS) != CUBLAS_STATUS_SUCCESS ||
-            cublasGemmEx(h, CUBLAS_OP_T, CUBLAS_OP_N, n_embd, T, n_in, &one, wo, CUDA_R_16BF, n_in, zb, CUDA_R_16BF, n_in,
-                         &zero, y, CUDA_R_32F, n_embd, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT) != CUBLAS_STATUS_SUCCESS)
-            return QSA_ERR_CUDA;
-        return QSA_OK;
+        const cudaError_t e = launch_proj_gemm_plain(st, T, n_in, n_embd, zb, wo, false, y, reinterpret_cast<uint32_t *>(wsb));
+        return e == cudaSuccess ? QSA_OK : (e == cudaErrorNotSupported ? QSA_ERR_UNSUPPORTED : QSA_ERR_CUDA);
     }
     static std::atomic<uint64_t> attr{0};
     cudaError_t e = once_per_device(attr, [] {

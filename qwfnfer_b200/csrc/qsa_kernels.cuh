@@ -74,6 +74,17 @@ cudaError_t launch_prefill_attn_kv(const DevDesc & d, cudaStream_t st, qsa_layer
                                    const void * q, int q_type, const int * sel, const int * nsel, int n_blocks,
                                    unsigned char * ws, float * out, uint32_t * status);
 
+// The prefill-sized projections on tcgen05 (qsa_proj_gemm.cu).  Front: xb [T][n_embd] 16-bit
+// activations, w[5] the 16-bit weights (attn_q, attn_k, attn_v, indexer.q_proj, indexer.k_proj),
+// cs [T][rope_dim/2] the tokens' rope table, norm[3] (q, k, q_idx; null = 1), out[6] = q, gate,
+// q_idx, k, v, kidx.  Plain: y[T][N] = a16[T][K] w[N][K]^T.  f16 selects f16 operands (else bf16).
+int proj_front_tiles(const DevDesc & d);
+cudaError_t launch_proj_gemm_front(const DevDesc & d, cudaStream_t st, int T, int n_embd, const void * xb,
+                                   const void * const w[5], bool f16, const float2 * cs, const float * const norm[3],
+                                   float * const out[6], uint32_t * status);
+cudaError_t launch_proj_gemm_plain(cudaStream_t st, int T, int K, int N, const void * a16, const void * w, bool f16,
+                                   float * y, uint32_t * status);
+
 // KV-sequence-sharded decode: global selection from all shards' candidates, and the log-sum-exp
 // merge of the shards' attention states (qsa_shard.cu).
 cudaError_t launch_shard_select(const DevDesc & d, cudaStream_t st, const qsa_decode_item * items, int n_shards,

@@ -33,10 +33,9 @@
 // Tensor-core operands use the 128-byte swizzle: Q [16 queries][4 atoms of 64 dims][8 rows] (K-major,
 // 8-row groups 4 KB apart), K and V [64 cells][256 dims] (K-major for S; V as the MN-major B of
 // O = P V), P [128 rows][64 cells] (K-major).
-#include <cuda.h>          // CUtensorMap and its enums; the encoder is reached through the runtime
-
 #include "qsa_kernels.cuh"
 #include "qsa_tc.cuh"
+#include "qsa_tma.cuh"
 
 namespace qsa {
 
@@ -155,40 +154,6 @@ __global__ void prefill_q16_kernel(const void * __restrict__ q, int q_type, int6
     q16[i] = make_uint4(pack_f16x2(f[0], f[1]), pack_f16x2(f[2], f[3]), pack_f16x2(f[4], f[5]), pack_f16x2(f[6], f[7]));
 }
 
-// ------------------------------------------------------------------ TMA (tensor maps) and bulk groups
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap * map, int x, int y, uint64_t * bar) {
-    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-                 :: "r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap * map, int x, int y, int z, uint64_t * bar) {
-    asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
-                 :: "r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap * map, int w, uint64_t * bar) {
-    asm volatile("cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %2, %2, %3}], [%4];"
-                 :: "r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(w), "r"(smem_u32(bar)) : "memory");
-}
-// non-blocking probe of a phase (the MMA thread polls two streams of work with it)
-__device__ __forceinline__ bool mbar_test(uint64_t * bar, uint32_t parity) {
-    uint32_t done;
-    asm volatile("{\n\t.reg .pred p;\n\t"
-                 "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
-                 "selp.u32 %0, 1, 0, p;\n\t}"
-                 : "=r"(done) : "r"(smem_u32(bar)), "r"(parity) : "memory");
-    return done != 0;
-}
-// Bounded wait by polling (no suspension): a thread suspended on a phase that other threads'
-// arrivals complete was seen to resume microseconds late, so the loader polls.
-__device__ __forceinline__ bool mbar_poll_bounded(uint64_t * bar, uint32_t parity, uint32_t * status) {
-    if (mbar_test(bar, parity)) return true;
-    const uint64_t t0 = global_timer_ns();
-    for (int k = 1;; k++) {
-        if (mbar_test(bar, parity)) return true;
-        if ((k & 63) == 0 && global_timer_ns() - t0 > 2000000000ull) break;
-    }
-    set_status(status, DEV_TIMEOUT);
-    return false;
-}
 // ------------------------------------------------------------------ attention per (block, KV head)
 // Bytes 0 and 2 of t (int8) times the f16 scale, as f16x2: the bytes become exact f16 integers and
 // the f16 multiply rounds d x q once, as the reference's f16(f32(d) * q) does (that f32 product is
@@ -583,22 +548,6 @@ PrefillKvLayout prefill_kv_layout(const DevDesc & d, int T, int n_blocks) {
     L.part_ml = L.part_o + a256(slots * d.n_head * HEAD_DIM * 2);
     L.total = L.part_ml + a256(slots * d.n_head * 2 * 4);
     return L;
-}
-
-// cuTensorMapEncodeTiled, reached through the runtime's driver entry-point query
-typedef CUresult (*encode_tiled_fn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
-                                    const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
-                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-encode_tiled_fn tensor_map_encoder() {
-    static encode_tiled_fn fn = nullptr;
-    if (!fn) {
-        void * f = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<encode_tiled_fn>(f);
-    }
-    return fn;
 }
 
 // groups x 8 rows x 256 f16 at `ptr` (rows of 512 bytes) seen as [group][atom][row][64 columns]:

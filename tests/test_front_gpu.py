@@ -61,14 +61,14 @@ def test_front_matches_oracle(idx_n_head, T):
         assert e <= NORMED_TOL, (name, e)
 
 
-GEMM_PROJ_TOL = 1e-4    # the GEMM path: cuBLAS's own f32 accumulation order, of the row's sum of |w * x|
+GEMM_PROJ_TOL = 1e-4    # the GEMM path: the tensor cores' f32 accumulation order, of the row's sum of |w * x|
 
 
 @pytest.mark.parametrize("idx_n_head,T", [(1, 17), (2, 40)])
 def test_front_gemm_path_matches_oracle(idx_n_head, T):
-    """Above 16 tokens (a prefill chunk) the projections run as GEMMs (bf16 products, f32
-    accumulation) and the norms and IMRoPE as their own kernel over token groups of 4 (17: a
-    last group of one); the outputs agree with the oracle as the GEMV path's do."""
+    """Above 16 tokens (a prefill chunk) the projections run as one tcgen05 GEMM (bf16 products,
+    f32 accumulation) whose epilogue applies the norms and IMRoPE (17 and 40 tokens: a partly
+    filled 128-row tile); the outputs agree with the oracle as the GEMV path's do."""
     d = make_desc(idx_n_head=idx_n_head, n_ctx=1 << 20)
     w = front_weights(d, seed=50 + T, gammas=True)
     front = QsaFront(d, **w)
@@ -188,8 +188,8 @@ def test_output_matches_oracle(T, n_embd):
 
 @pytest.mark.parametrize("T,n_embd", [(17, 2560), (48, 1000)])
 def test_output_gemm_path_matches_oracle(T, n_embd):
-    """Above 16 tokens the output side is one GEMM (cuBLAS, bf16 products, f32 accumulation) over
-    the gated activations rounded to bf16; the bound takes cuBLAS's accumulation order (GEMM_PROJ_TOL)."""
+    """Above 16 tokens the output side is one tcgen05 GEMM (bf16 products, f32 accumulation) over
+    the gated activations rounded to bf16; the bound takes its accumulation order (GEMM_PROJ_TOL)."""
     d = make_desc()
     g = torch.Generator(device="cuda").manual_seed(61 + T)
     n_in = d.n_head * d.head_dim
@@ -243,3 +243,44 @@ def test_output_argument_errors():
     assert call(n_embd=0) == QSA_ERR_INVALID
     assert call(T=32) == QSA_ERR_WORKSPACE            # above 16 tokens the GEMM path needs a workspace
     torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("which", ["front", "output"])
+def test_projection_gemm_full_chunk_sampled(which):
+    """A whole 8192-token prefill chunk through the GEMM path (64 row tiles; every weight tile of the
+    front, or of attn_output at n_embd 2560), checked against the oracle on 40 sampled tokens (the
+    projections of a token depend on that token only)."""
+    d = make_desc(n_ctx=1 << 20)
+    T = 8192
+    g = torch.Generator(device="cuda").manual_seed(71)
+    samples = sorted(set([0, 1, 127, 128, 4095, 8190, 8191] + list(range(5, T, 251))))[:40]
+    if which == "front":
+        w = front_weights(d, seed=72, gammas=True)
+        front = QsaFront(d, **w)
+        x = torch.randn(T, front.n_embd, generator=g, device="cuda")
+        pos = torch.randint(0, 1 << 20, (T,), generator=g, device="cuda", dtype=torch.int32)
+        outs = front.project(x, pos)
+        torch.cuda.synchronize()
+        xs = x[samples]
+        ref = oracle.front(d, host_weights(w), pos[samples].cpu().numpy(), xs.cpu().numpy())
+        q, gate, q_idx, k, v, kidx = (t[samples] for t in outs)
+        hd = d.head_dim
+        wq_gate = w["wq"].view(d.n_head, 2, hd, -1)[:, 1].reshape(d.n_head * hd, -1)
+        for name, got, wt in (("gate", gate, wq_gate), ("v", v, w["wv"]), ("kidx", kidx, w["wk_idx"])):
+            bound = GEMM_PROJ_TOL * abs_row_sums(wt, xs).cpu().numpy()
+            err = np.abs(got.cpu().numpy() - ref[name])
+            assert np.all(err <= bound + 1e-30), (name, float(err.max()), float(bound.max()))
+        for name, got in (("q", q), ("k", k), ("q_idx", q_idx)):
+            e = np.abs(got.cpu().numpy() - ref[name]).max() / np.abs(ref[name]).max()
+            assert e <= NORMED_TOL, (name, e)
+    else:
+        n_in = d.n_head * d.head_dim
+        wo = (torch.randn(2560, n_in, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+        attn = torch.randn(T, d.n_head, d.head_dim, generator=g, device="cuda")
+        gate = 2 * torch.randn(T, n_in, generator=g, device="cuda")
+        y = QsaOutput(d, wo).project(attn, gate)
+        torch.cuda.synchronize()
+        a_s, g_s = attn[samples], gate[samples]
+        ref = oracle.output(d, wo.view(torch.int16).cpu().numpy().view(np.uint16), a_s.cpu().numpy(), g_s.cpu().numpy())
+        err = np.abs(y[samples].cpu().numpy() - ref)
+        assert np.all(err <= output_bound(wo, a_s, g_s, GEMM_PROJ_TOL)), float(err.max())
