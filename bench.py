@@ -392,6 +392,8 @@ def run_ours_config2(args, ws, rank, local):
     }
     res["front"] = front_stage(d, dev, n_past, flush, K, cfg.seed)
     res["output"] = output_stage(d, dev, flush, K, cfg.seed)
+    res["front_q8_0"] = front_stage(d, dev, n_past, flush, K, cfg.seed, q8_0=True)
+    res["output_q8_0"] = output_stage(d, dev, flush, K, cfg.seed, q8_0=True)
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         kc = st.k[0][:n_past + 1].cpu().numpy()
         vc = st.v[0][:n_past + 1].cpu().numpy()
@@ -439,7 +441,7 @@ def _stage_roofline(T, us, nbytes, flops):
             "frac": round(ach / tfs, 4), "peak_source": f"{src} bf16_tflops (burst)"}
 
 
-def front_stage(d, dev, n_past, flush, K, seed, T=1):
+def front_stage(d, dev, n_past, flush, K, seed, T=1, q8_0=False):
     """The projection front feeding the node (qsa_front: attn_q/k/v and the indexer projections over
     n_embd 2560, their norms and IMRoPE) for T tokens ending at n_past, L2 flushed before each call:
     the bf16 GEMV up to 16 tokens, the tcgen05 projection GEMM (norms and IMRoPE in its epilogue) above."""
@@ -448,7 +450,7 @@ def front_stage(d, dev, n_past, flush, K, seed, T=1):
     from qwfnfer_b200.configs import front_weights
     from qwfnfer_b200.qsa import QsaFront
 
-    w = front_weights(d, seed=seed + 50, device=dev)
+    w = front_weights(d, seed=seed + 50, device=dev, q8_0=q8_0)
     front = QsaFront(d, **w)
     x = torch.randn(T, front.n_embd, generator=torch.Generator(device=dev).manual_seed(seed + 51), device=dev)
     pos = torch.arange(n_past - T + 1, n_past + 1, dtype=torch.int32, device=dev)
@@ -457,32 +459,43 @@ def front_stage(d, dev, n_past, flush, K, seed, T=1):
     w_bytes = sum(t.numel() * t.element_size() for t in w.values())
     rows = sum(t.shape[0] for k, t in w.items() if k.startswith("w"))
     nbytes = w_bytes + x.numel() * 4 + sum(o.numel() * 4 for o in outs)
-    path = "front_kernel (bf16 GEMV)" if T <= 16 else "to_bf16 + rope table + proj_gemm_kernel (tcgen05, fused norm/IMRoPE epilogue)"
-    return {"kernel": f"qsa_front, {T} token(s), n_embd 2560: {path}", "us": round(us, 3),
-            **_stage_roofline(T, us, nbytes, 2 * T * rows * front.n_embd), "launches": 1 if T <= 16 else 3}
+    fmt = "q8_0" if q8_0 else "bf16"
+    if T <= 16:
+        path = f"front_kernel{'_q8' if q8_0 else ''} ({fmt} GEMV)"
+    else:
+        path = ("act_q8_f16 + q8_to_f16 (weights) + " if q8_0 else "to_bf16 + ") + \
+               "rope table + proj_gemm_kernel (tcgen05, fused norm/IMRoPE epilogue)"
+    return {"kernel": f"qsa_front, {T} token(s), n_embd 2560, {fmt} weights: {path}", "us": round(us, 3),
+            **_stage_roofline(T, us, nbytes, 2 * T * rows * front.n_embd), "launches": 1 if T <= 16 else (8 if q8_0 else 3)}
 
 
-def output_stage(d, dev, flush, K, seed, T=1):
+def output_stage(d, dev, flush, K, seed, T=1, q8_0=False):
     """The output side after the node (qsa_output: attention output times sigmoid(gate), then the
     bf16 attn_output projection to n_embd 2560) for T tokens, L2 flushed before each call."""
     import torch
 
-    from qwfnfer_b200.configs import N_EMBD
+    from qwfnfer_b200.configs import N_EMBD, q8_0_rows
     from qwfnfer_b200.qsa import QsaOutput
 
     g = torch.Generator(device=dev).manual_seed(seed + 60)
     n_in = d.n_head * d.head_dim
-    wo = (torch.randn(N_EMBD, n_in, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    wf = torch.randn(N_EMBD, n_in, generator=g, device=dev) * 0.02
+    wo = q8_0_rows(wf) if q8_0 else wf.to(torch.bfloat16)
+    del wf
     attn = torch.randn(T, d.n_head, d.head_dim, generator=g, device=dev)
     gate = torch.randn(T, n_in, generator=g, device=dev)
     out = torch.empty(T, N_EMBD, device=dev)
     op = QsaOutput(d, wo)
     us = _stage_time(lambda: op.project(attn, gate, out=out), flush, max(K, 20) if T <= 16 else max(K, 5),
                      graph=T <= 16)
-    nbytes = wo.numel() * 2 + attn.numel() * 4 + gate.numel() * 4 + out.numel() * 4
-    path = "output_kernel (bf16 GEMV)" if T <= 16 else "gate_bf16_kernel + proj_gemm_kernel (tcgen05)"
-    return {"kernel": f"qsa_output, {T} token(s), 4096 -> n_embd 2560: {path}", "us": round(us, 3),
-            **_stage_roofline(T, us, nbytes, 2 * T * N_EMBD * n_in), "launches": 1 if T <= 16 else 2}
+    nbytes = wo.numel() * wo.element_size() + attn.numel() * 4 + gate.numel() * 4 + out.numel() * 4
+    fmt = "q8_0" if q8_0 else "bf16"
+    if T <= 16:
+        path = f"output_kernel{'_q8' if q8_0 else ''} ({fmt} GEMV)"
+    else:
+        path = ("act_q8_f16 + q8_to_f16 (weights)" if q8_0 else "gate_bf16_kernel") + " + proj_gemm_kernel (tcgen05)"
+    return {"kernel": f"qsa_output, {T} token(s), 4096 -> n_embd 2560, {fmt} weights: {path}", "us": round(us, 3),
+            **_stage_roofline(T, us, nbytes, 2 * T * N_EMBD * n_in), "launches": 1 if T <= 16 else (3 if q8_0 else 2)}
 
 
 def _timed_replays(graph, n, before=None):
@@ -924,6 +937,8 @@ def run_ours_config4(args, ws, rank, local):
     # the projections around the node for this chunk, reported beside the node's metric
     res["front"] = front_stage(d, dev, n_past + T - 1, flush, K, cfg.seed, T=T)
     res["output"] = output_stage(d, dev, flush, K, cfg.seed, T=T)
+    res["front_q8_0"] = front_stage(d, dev, n_past + T - 1, flush, K, cfg.seed, T=T, q8_0=True)
+    res["output_q8_0"] = output_stage(d, dev, flush, K, cfg.seed, T=T, q8_0=True)
     return res
 
 

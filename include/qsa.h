@@ -285,7 +285,12 @@ qsa_status qsa_prefill(const qsa_desc * d, const qsa_layer_cache * cache /* host
 /* ------------------------------------------------------------------ projection front */
 /* The projections feeding the node, as graph_builder::sparse_attn_decode builds them
  * (src/qwfn_graph.cpp:465, 479-484, 505-518; prefill :324-347).  Weights are row-major
- * [out][n_embd] (ggml's mul_mat layout), bf16, 16-byte aligned; the norm weights are f32. */
+ * [out][n_embd] (ggml's mul_mat layout), 16-byte aligned, in one of two formats (w_type):
+ *   QSA_TYPE_BF16  bf16 values; the activations are rounded to bf16 (ggml's vec_dot_bf16);
+ *   QSA_TYPE_Q8_0  q8_0 rows of n_embd/32 blocks {f16 d; int8 qs[32]} (34 bytes); the activations
+ *                  are quantised to q8_0 with ggml's reference rounding and each block contributes
+ *                  its integer dot times f32(d_w) * f32(d_x) (ggml_vec_dot_q8_0_q8_0).
+ * The norm weights are f32. */
 typedef struct qsa_front_weights {
     const void  * wq;          /* attn_q.weight [2*head_dim*n_head][n_embd]: head h's query rows
                                   [2*h*hd, 2*h*hd + hd), its gate rows the next hd */
@@ -296,21 +301,25 @@ typedef struct qsa_front_weights {
     const float * q_norm;      /* attn_q_norm.weight [head_dim] (NULL = 1) */
     const float * k_norm;      /* attn_k_norm.weight [head_dim] (NULL = 1) */
     const float * q_idx_norm;  /* indexer.q_norm.weight [idx_dim] (NULL = 1) */
-    int32_t       n_embd;      /* model width: a multiple of 8, at most 12288 */
-    int32_t       w_type;      /* QSA_TYPE_BF16 */
+    int32_t       n_embd;      /* model width: at most 12288; a multiple of 8 (bf16) or of 256 (q8_0) */
+    int32_t       w_type;      /* QSA_TYPE_BF16 or QSA_TYPE_Q8_0 (all five matrices) */
 } qsa_front_weights;
 
 size_t qsa_front_workspace_size(const qsa_desc * d, const qsa_front_weights * w, int32_t T);
 /* For T tokens at positions pos[T] (device int32) with activations x [T][n_embd] (device f32):
- *   y = W x, x rounded to bf16 as the CPU mul_mat converts it, f32 accumulation;
+ *   y = W x in f32 (the weight format's products above);
  *   q_out     f32 [T][n_head][head_dim]      rms_norm * q_norm, IMRoPE at pos
  *   gate_out  f32 [T][n_head*head_dim]       the gate half of attn_q, raw
  *   q_idx_out f32 [T][idx_n_head][idx_dim]   rms_norm * q_idx_norm, IMRoPE at pos
  *   k_out     f32 [T][n_head_kv*head_dim]    rms_norm * k_norm, IMRoPE at pos
  *   v_out     f32 [T][n_head_kv*head_dim]    raw
  *   kidx_out  f32 [T][idx_dim]               raw (normed and roped when pooled)
- * which are qsa_decode's q (QSA_TYPE_F32), q_idx, k_new, v_new and kidx_new.  The workspace is
- * zeroed once (qsa_workspace_init); above 16 tokens it must be 256-byte aligned (QSA_ERR_WORKSPACE).  Replaces the projection, norm and rope nodes of
+ * which are qsa_decode's q (QSA_TYPE_F32), q_idx, k_new, v_new and kidx_new.  Up to 16 tokens the
+ * projections stream the weights (a matrix-vector kernel per group of 4 tokens); above, with
+ * rope_dim a multiple of 64, they run as one tcgen05 GEMM whose epilogue applies the norms and
+ * IMRoPE (f32 accumulation in the tensor cores; q8_0 weights and activations enter it as f16 of
+ * their d * q values, each rounded once).  The workspace is zeroed once (qsa_workspace_init) and
+ * 16-byte aligned (QSA_ERR_WORKSPACE).  Replaces the projection, norm and rope nodes of
  * src/qwfn_graph.cpp:465, 479-484, 505-518. */
 qsa_status qsa_front(const qsa_desc * d, const qsa_front_weights * w, int32_t T, const int32_t * pos,
                      const float * x, float * q_out, float * gate_out, float * q_idx_out,
@@ -319,13 +328,14 @@ qsa_status qsa_front(const qsa_desc * d, const qsa_front_weights * w, int32_t T,
 
 /* The output side of the node (src/qwfn_graph.cpp:543-545; prefill :406-407): for T tokens
  *   y = attn_output.weight * (attn * sigmoid(gate)),
- * sigmoid 1/(1+exp(-g)) in f32, the gated product rounded to bf16 as the CPU mul_mat converts it,
- * f32 accumulation.  wo: bf16 [n_embd][n_head*head_dim] (16-byte aligned); attn: f32
- * [T][n_head][head_dim] (qsa_decode's out); gate: f32 [T][n_head*head_dim] (qsa_front's gate);
- * y: f32 [T][n_embd].  Up to 16 tokens no workspace is used (ws may be NULL); above, the tokens
- * run as one cuBLAS GEMM and ws holds qsa_output_workspace_size(d, n_embd, T) bytes (256-byte
- * aligned, else QSA_ERR_WORKSPACE).  A device's first call above 16 tokens creates its cuBLAS handle. */
-size_t qsa_output_workspace_size(const qsa_desc * d, int32_t n_embd, int32_t T);
+ * sigmoid 1/(1+exp(-g)) in f32; the gated product enters the weight format's products as qsa_front's
+ * activations do.  wo: [n_embd][n_head*head_dim] in bf16 or q8_0 (w_type, 16-byte aligned); attn:
+ * f32 [T][n_head][head_dim] (qsa_decode's out); gate: f32 [T][n_head*head_dim] (qsa_front's gate);
+ * y: f32 [T][n_embd].  Up to 16 tokens no workspace is used (ws may be NULL); above, the tokens run
+ * as one tcgen05 GEMM and ws holds qsa_output_workspace_size(d, n_embd, w_type, T) bytes (16-byte
+ * aligned, zeroed once, else QSA_ERR_WORKSPACE); n_embd is then a multiple of 4 and y 16-byte
+ * aligned. */
+size_t qsa_output_workspace_size(const qsa_desc * d, int32_t n_embd, int32_t w_type, int32_t T);
 qsa_status qsa_output(const qsa_desc * d, const void * wo, int32_t n_embd, int32_t w_type, int32_t T,
                       const float * attn, const float * gate, float * y, void * ws, size_t ws_bytes,
                       qsa_stream_t stream);

@@ -49,6 +49,8 @@ def lib() -> ctypes.CDLL:
             "orc_node": (None, [D, VP, VP, VP, I64, VP, VP, I32, VP, VP, VP, VP, I32]),
             "orc_front": (None, [D, VP, VP, VP, VP, VP, VP, VP, VP, I64, I64, VP, VP, VP, VP, VP, VP, VP, VP]),
             "orc_output": (None, [D, VP, I64, I64, VP, VP, VP]),
+            "orc_front_w": (None, [D, I32, VP, VP, VP, VP, VP, VP, VP, VP, I64, I64, VP, VP, VP, VP, VP, VP, VP, VP]),
+            "orc_output_w": (None, [D, I32, VP, I64, I64, VP, VP, VP]),
         }
         for name, (res, args) in sigs.items():
             fn = getattr(L, name)
@@ -211,32 +213,35 @@ def cache_arrays(d: QsaDesc):
             np.zeros((n, d.idx_dim), np.uint16), np.zeros((n // d.ratio, d.idx_dim), np.uint16))
 
 
-def front(d: QsaDesc, w: dict, pos: np.ndarray, x: np.ndarray) -> dict:
-    """orc_front: the projections, norms and IMRoPE feeding the node for T tokens.
-    w: wq, wk, wv, wq_idx, wk_idx as uint16 bf16 bits [out][n_embd]; q_norm, k_norm, q_idx_norm f32
-    (or None).  pos int32 [T], x f32 [T][n_embd].  Returns q, gate, q_idx, k, v, kidx (f32)."""
+def front(d: QsaDesc, w: dict, pos: np.ndarray, x: np.ndarray, w_type: int = TYPE_BF16) -> dict:
+    """orc_front_w: the projections, norms and IMRoPE feeding the node for T tokens.
+    w: wq, wk, wv, wq_idx, wk_idx as uint16 bf16 bits [out][n_embd] (w_type TYPE_BF16), or as uint8
+    q8_0 rows [out][n_embd/32*34] (TYPE_Q8_0); q_norm, k_norm, q_idx_norm f32 (or None).
+    pos int32 [T], x f32 [T][n_embd].  Returns q, gate, q_idx, k, v, kidx (f32)."""
     T, n_embd = x.shape
     hd, nh, nkv, H, D = d.head_dim, d.n_head, d.n_head_kv, d.idx_n_head, d.idx_dim
     out = {"q": np.zeros((T, nh, hd), np.float32), "gate": np.zeros((T, nh * hd), np.float32),
            "q_idx": np.zeros((T, H, D), np.float32), "k": np.zeros((T, nkv * hd), np.float32),
            "v": np.zeros((T, nkv * hd), np.float32), "kidx": np.zeros((T, D), np.float32)}
-    ws = [np.ascontiguousarray(w[k], dtype=np.uint16) for k in ("wq", "wk", "wv", "wq_idx", "wk_idx")]
+    wdt = np.uint8 if w_type == TYPE_Q8_0 else np.uint16
+    ws = [np.ascontiguousarray(w[k], dtype=wdt) for k in ("wq", "wk", "wv", "wq_idx", "wk_idx")]
     ns = [None if w.get(k) is None else np.ascontiguousarray(w[k], dtype=np.float32)
           for k in ("q_norm", "k_norm", "q_idx_norm")]
     pos = np.ascontiguousarray(pos, dtype=np.int32)
     x = np.ascontiguousarray(x, dtype=np.float32)
-    lib().orc_front(ctypes.byref(d), *[_p(a) for a in ws], *[_p(a) for a in ns], n_embd, T, _p(pos), _p(x),
-                    *[_p(out[k]) for k in ("q", "gate", "q_idx", "k", "v", "kidx")])
+    lib().orc_front_w(ctypes.byref(d), w_type, *[_p(a) for a in ws], *[_p(a) for a in ns], n_embd, T, _p(pos), _p(x),
+                      *[_p(out[k]) for k in ("q", "gate", "q_idx", "k", "v", "kidx")])
     return out
 
 
-def output(d: QsaDesc, wo: np.ndarray, attn: np.ndarray, gate: np.ndarray) -> np.ndarray:
-    """orc_output: y = attn_output (attn * sigmoid(gate)); wo uint16 bf16 bits [n_embd][n_head*head_dim],
-    attn f32 [T][n_head][head_dim], gate f32 [T][n_head*head_dim] -> y f32 [T][n_embd]."""
-    wo = np.ascontiguousarray(wo, dtype=np.uint16)
+def output(d: QsaDesc, wo: np.ndarray, attn: np.ndarray, gate: np.ndarray, w_type: int = TYPE_BF16) -> np.ndarray:
+    """orc_output_w: y = attn_output (attn * sigmoid(gate)); wo uint16 bf16 bits [n_embd][n_head*head_dim]
+    (or uint8 q8_0 rows with w_type TYPE_Q8_0), attn f32 [T][n_head][head_dim], gate f32
+    [T][n_head*head_dim] -> y f32 [T][n_embd]."""
+    wo = np.ascontiguousarray(wo, dtype=np.uint8 if w_type == TYPE_Q8_0 else np.uint16)
     attn = np.ascontiguousarray(attn, dtype=np.float32)
     gate = np.ascontiguousarray(gate, dtype=np.float32)
     T, n_embd = attn.shape[0], wo.shape[0]
     y = np.zeros((T, n_embd), np.float32)
-    lib().orc_output(ctypes.byref(d), _p(wo), n_embd, T, _p(attn), _p(gate), _p(y))
+    lib().orc_output_w(ctypes.byref(d), w_type, _p(wo), n_embd, T, _p(attn), _p(gate), _p(y))
     return y

@@ -511,63 +511,109 @@ static void orc_norm_rope(const qsa_desc * d, float * v, int64_t D, const float 
 //   attn_q rows per head h: [2h*hd, 2h*hd+hd) the query, the next hd the gate (:505-510);
 //   Q = rms(Q_h)*q_norm, K = rms(K_h)*k_norm, q_idx = rms(q_h)*q_idx_norm, each then IMRoPE at the
 //   token's position; V, the gate and the raw indexer key as projected.
+// One projection row: bf16 weights (ggml's vec_dot_bf16: the activation rounded to bf16, exact
+// f32 products, here summed in double and rounded once), or q8_0 weights (ggml_vec_dot_q8_0_q8_0:
+// the activation row quantised to q8_0 with the reference rounding, per block the integer sum of
+// products times f32(d_w) * f32(d_x), the block terms summed in double and rounded once).
+struct ProjRow {
+    int32_t w_type;
+    int64_t n;                       // row length (n_embd or n_head*head_dim)
+    std::vector<float> xb;           // bf16 path: the activation's bf16 values
+    std::vector<uint8_t> xq;         // q8_0 path: the activation's q8_0 blocks
+    void set_x(const float * x) {
+        if (w_type == QSA_TYPE_Q8_0) {
+            xq.resize((size_t) n / QK8_0 * Q8_0_BYTES);
+            for (int64_t b = 0; b < n / QK8_0; b++) q8_0_quantize_block(x + b * QK8_0, xq.data() + b * Q8_0_BYTES);
+        } else {
+            xb.resize((size_t) n);
+            for (int64_t e = 0; e < n; e++) xb[e] = bf16_to_f32(f32_to_bf16(x[e]));
+        }
+    }
+    size_t row_bytes() const { return w_type == QSA_TYPE_Q8_0 ? (size_t) n / QK8_0 * Q8_0_BYTES : (size_t) n * 2; }
+    float dot(const void * w_base, int64_t row) const {
+        const uint8_t * w = static_cast<const uint8_t *>(w_base) + (size_t) row * row_bytes();
+        double acc = 0.0;
+        if (w_type == QSA_TYPE_Q8_0) {
+            for (int64_t b = 0; b < n / QK8_0; b++) {
+                const uint8_t * wb = w + b * Q8_0_BYTES, * xb8 = xq.data() + b * Q8_0_BYTES;
+                uint16_t dw, dx;
+                std::memcpy(&dw, wb, 2);
+                std::memcpy(&dx, xb8, 2);
+                int32_t sumi = 0;
+                for (int j = 0; j < QK8_0; j++) sumi += (int32_t) (int8_t) wb[2 + j] * (int32_t) (int8_t) xb8[2 + j];
+                acc += (double) ((float) sumi * (f16_to_f32(dw) * f16_to_f32(dx)));
+            }
+        } else {
+            const uint16_t * wr = reinterpret_cast<const uint16_t *>(w);
+            for (int64_t e = 0; e < n; e++) acc += (double) (bf16_to_f32(wr[e]) * xb[e]);
+        }
+        return (float) acc;
+    }
+};
+
+void orc_front_w(const qsa_desc * d, int32_t w_type, const void * wq, const void * wk, const void * wv,
+                 const void * wq_idx, const void * wk_idx, const float * q_norm, const float * k_norm,
+                 const float * q_idx_norm, int64_t n_embd, int64_t T, const int32_t * pos, const float * x,
+                 float * q_out, float * gate_out, float * q_idx_out, float * k_out, float * v_out, float * kidx_out) {
+    const int64_t hd = d->head_dim, nh = d->n_head, nkv = d->n_head_kv, H = d->idx_n_head, D = d->idx_dim;
+    #pragma omp parallel for schedule(static) if (T > 1)
+    for (int64_t t = 0; t < T; t++) {
+        ProjRow pr{w_type, n_embd, {}, {}};
+        pr.set_x(x + t * n_embd);
+        std::vector<float> v(hd);
+        const float p = (float) pos[t];
+        for (int64_t h = 0; h < nh; h++) {
+            for (int64_t e = 0; e < hd; e++) v[e] = pr.dot(wq, 2 * h * hd + e);
+            orc_norm_rope(d, v.data(), hd, q_norm, p);
+            std::memcpy(q_out + (t * nh + h) * hd, v.data(), (size_t) hd * 4);
+            for (int64_t e = 0; e < hd; e++) gate_out[(t * nh + h) * hd + e] = pr.dot(wq, (2 * h + 1) * hd + e);
+        }
+        for (int64_t j = 0; j < nkv; j++) {
+            for (int64_t e = 0; e < hd; e++) v[e] = pr.dot(wk, j * hd + e);
+            orc_norm_rope(d, v.data(), hd, k_norm, p);
+            std::memcpy(k_out + (t * nkv + j) * hd, v.data(), (size_t) hd * 4);
+            for (int64_t e = 0; e < hd; e++) v_out[(t * nkv + j) * hd + e] = pr.dot(wv, j * hd + e);
+        }
+        std::vector<float> qi(D);
+        for (int64_t h = 0; h < H; h++) {
+            for (int64_t e = 0; e < D; e++) qi[e] = pr.dot(wq_idx, h * D + e);
+            orc_norm_rope(d, qi.data(), D, q_idx_norm, p);
+            std::memcpy(q_idx_out + (t * H + h) * D, qi.data(), (size_t) D * 4);
+        }
+        for (int64_t e = 0; e < D; e++) kidx_out[t * D + e] = pr.dot(wk_idx, e);
+    }
+}
+
 void orc_front(const qsa_desc * d, const uint16_t * wq, const uint16_t * wk, const uint16_t * wv,
                const uint16_t * wq_idx, const uint16_t * wk_idx, const float * q_norm, const float * k_norm,
                const float * q_idx_norm, int64_t n_embd, int64_t T, const int32_t * pos, const float * x,
                float * q_out, float * gate_out, float * q_idx_out, float * k_out, float * v_out, float * kidx_out) {
-    const int64_t hd = d->head_dim, nh = d->n_head, nkv = d->n_head_kv, H = d->idx_n_head, D = d->idx_dim;
-    auto dot = [&](const uint16_t * w, const float * xb) {
-        double acc = 0.0;
-        for (int64_t e = 0; e < n_embd; e++) acc += (double) (bf16_to_f32(w[e]) * xb[e]);
-        return (float) acc;
-    };
-    #pragma omp parallel for schedule(static) if (T > 1)
-    for (int64_t t = 0; t < T; t++) {
-        std::vector<float> xb(n_embd), v(hd);
-        for (int64_t e = 0; e < n_embd; e++) xb[e] = bf16_to_f32(f32_to_bf16(x[t * n_embd + e]));
-        const float p = (float) pos[t];
-        for (int64_t h = 0; h < nh; h++) {
-            for (int64_t e = 0; e < hd; e++) v[e] = dot(wq + (2 * h * hd + e) * n_embd, xb.data());
-            orc_norm_rope(d, v.data(), hd, q_norm, p);
-            std::memcpy(q_out + (t * nh + h) * hd, v.data(), (size_t) hd * 4);
-            for (int64_t e = 0; e < hd; e++) gate_out[(t * nh + h) * hd + e] = dot(wq + ((2 * h + 1) * hd + e) * n_embd, xb.data());
-        }
-        for (int64_t j = 0; j < nkv; j++) {
-            for (int64_t e = 0; e < hd; e++) v[e] = dot(wk + (j * hd + e) * n_embd, xb.data());
-            orc_norm_rope(d, v.data(), hd, k_norm, p);
-            std::memcpy(k_out + (t * nkv + j) * hd, v.data(), (size_t) hd * 4);
-            for (int64_t e = 0; e < hd; e++) v_out[(t * nkv + j) * hd + e] = dot(wv + (j * hd + e) * n_embd, xb.data());
-        }
-        std::vector<float> qi(D);
-        for (int64_t h = 0; h < H; h++) {
-            for (int64_t e = 0; e < D; e++) qi[e] = dot(wq_idx + (h * D + e) * n_embd, xb.data());
-            orc_norm_rope(d, qi.data(), D, q_idx_norm, p);
-            std::memcpy(q_idx_out + (t * H + h) * D, qi.data(), (size_t) D * 4);
-        }
-        for (int64_t e = 0; e < D; e++) kidx_out[t * D + e] = dot(wk_idx + e * n_embd, xb.data());
-    }
+    orc_front_w(d, QSA_TYPE_BF16, wq, wk, wv, wq_idx, wk_idx, q_norm, k_norm, q_idx_norm, n_embd, T, pos, x,
+                q_out, gate_out, q_idx_out, k_out, v_out, kidx_out);
 }
 
 
 // The output side (src/qwfn_graph.cpp:543-545): z = attn * sigmoid(gate) in f32 (ggml_sigmoid:
-// 1/(1+expf(-g))), then mul_mat(attn_output bf16, z): z rounded to bf16, products exact in f32,
-// accumulated in double and rounded once.
-void orc_output(const qsa_desc * d, const uint16_t * wo, int64_t n_embd, int64_t T, const float * attn,
-                const float * gate, float * y) {
+// 1/(1+expf(-g))), then mul_mat(attn_output, z) as ProjRow computes it (bf16 or q8_0 weights).
+void orc_output_w(const qsa_desc * d, int32_t w_type, const void * wo, int64_t n_embd, int64_t T, const float * attn,
+                  const float * gate, float * y) {
     const int64_t n_in = (int64_t) d->n_head * d->head_dim;
     #pragma omp parallel for schedule(static) if (T > 1)
     for (int64_t t = 0; t < T; t++) {
         std::vector<float> z(n_in);
         for (int64_t e = 0; e < n_in; e++) {
             const float sg = 1.0f / (1.0f + expf(-gate[t * n_in + e]));
-            z[e] = bf16_to_f32(f32_to_bf16(attn[t * n_in + e] * sg));
+            z[e] = attn[t * n_in + e] * sg;
         }
-        for (int64_t r = 0; r < n_embd; r++) {
-            double acc = 0.0;
-            for (int64_t e = 0; e < n_in; e++) acc += (double) (bf16_to_f32(wo[r * n_in + e]) * z[e]);
-            y[t * n_embd + r] = (float) acc;
-        }
+        ProjRow pr{w_type, n_in, {}, {}};
+        pr.set_x(z.data());
+        for (int64_t r = 0; r < n_embd; r++) y[t * n_embd + r] = pr.dot(wo, r);
     }
+}
+
+void orc_output(const qsa_desc * d, const uint16_t * wo, int64_t n_embd, int64_t T, const float * attn,
+                const float * gate, float * y) {
+    orc_output_w(d, QSA_TYPE_BF16, wo, n_embd, T, attn, gate, y);
 }
 
 }  // extern "C"

@@ -144,7 +144,7 @@ def lib() -> ctypes.CDLL:
         "qsa_stage_copy": (I32, [VP, VP, SZ, VP]),
         "qsa_front_workspace_size": (SZ, [D, P(QsaFrontWeights), I32]),
         "qsa_front": (I32, [D, P(QsaFrontWeights), I32, VP, VP, VP, VP, VP, VP, VP, VP, VP, SZ, VP]),
-        "qsa_output_workspace_size": (SZ, [D, I32, I32]),
+        "qsa_output_workspace_size": (SZ, [D, I32, I32, I32]),
         "qsa_output": (I32, [D, VP, I32, I32, I32, VP, VP, VP, VP, SZ, VP]),
         "qsa_version": (I32, []),
     }

@@ -87,16 +87,18 @@ def token_inputs(d: QsaDesc, n: int, seed: int, q_dtype=torch.bfloat16, device="
 N_EMBD = 2560     # model width of the synthetic projection weights
 
 
-def front_weights(d: QsaDesc, n_embd: int = N_EMBD, seed: int = 0, gammas: bool = False, device="cuda") -> dict:
-    """Synthetic weights of the projection front (qsa_front): bf16 ~ N(0, 0.02) row-major
-    [out][n_embd] for attn_q (query and gate interleaved per head), attn_k, attn_v,
-    indexer.q_proj, indexer.k_proj; f32 norm weights, 1 (the stand-in) or with gammas=True
-    ~ 1 + N(0, 0.1) to exercise the multiply."""
+def front_weights(d: QsaDesc, n_embd: int = N_EMBD, seed: int = 0, gammas: bool = False, device="cuda",
+                  q8_0: bool = False) -> dict:
+    """Synthetic weights of the projection front (qsa_front): ~ N(0, 0.02) row-major [out][n_embd]
+    for attn_q (query and gate interleaved per head), attn_k, attn_v, indexer.q_proj,
+    indexer.k_proj, in bf16 or (q8_0=True) as q8_0 rows; f32 norm weights, 1 (the stand-in) or with
+    gammas=True ~ 1 + N(0, 0.1) to exercise the multiply."""
     g = torch.Generator(device=device).manual_seed(seed)
     hd = d.head_dim
 
     def w(rows):
-        return (torch.randn(rows, n_embd, generator=g, device=device) * 0.02).to(torch.bfloat16)
+        f = torch.randn(rows, n_embd, generator=g, device=device) * 0.02
+        return q8_0_rows(f) if q8_0 else f.to(torch.bfloat16)
 
     def gamma(n):
         if not gammas:
@@ -106,3 +108,27 @@ def front_weights(d: QsaDesc, n_embd: int = N_EMBD, seed: int = 0, gammas: bool 
     return {"wq": w(2 * hd * d.n_head), "wk": w(hd * d.n_head_kv), "wv": w(hd * d.n_head_kv),
             "wq_idx": w(d.idx_dim * d.idx_n_head), "wk_idx": w(d.idx_dim),
             "q_norm": gamma(hd), "k_norm": gamma(hd), "q_idx_norm": gamma(d.idx_dim)}
+
+
+def q8_0_rows(w: torch.Tensor) -> torch.Tensor:
+    """f32 [rows][n] (n % 32 == 0) -> q8_0 rows as bytes uint8 [rows][n/32*34], with ggml's reference
+    rounding (quantize_row_q8_0_ref): per block d = amax/127, id = 1/d (0 when d == 0), q = x*id
+    rounded half away from zero, d stored as f16 ahead of the block's 32 int8 values."""
+    rows, n = w.shape
+    x = w.float().reshape(rows, n // 32, 32)
+    d = x.abs().amax(dim=2, keepdim=True) / 127.0
+    inv = torch.where(d != 0, 1.0 / d, torch.zeros_like(d))
+    v = x * inv
+    q = (torch.sign(v) * torch.floor(v.abs() + 0.5)).to(torch.int8)
+    out = torch.empty(rows, n // 32, 34, dtype=torch.uint8, device=w.device)
+    out[:, :, :2] = d.half().view(torch.uint8).reshape(rows, n // 32, 2)
+    out[:, :, 2:] = q.view(torch.uint8)
+    return out.reshape(rows, n // 32 * 34)
+
+
+def q8_0_rows_dequant(q: torch.Tensor) -> torch.Tensor:
+    """q8_0 rows uint8 [rows][n/32*34] -> f32 [rows][n] (f32(d) * q)."""
+    rows = q.shape[0]
+    b = q.reshape(rows, -1, 34)
+    d = b[:, :, :2].contiguous().view(torch.float16).float()
+    return (d * b[:, :, 2:].contiguous().view(torch.int8).float()).reshape(rows, -1)

@@ -9,18 +9,11 @@
 namespace qsa {
 
 // ---------------------------------------------------------------------------------------------
-// One q8_0 block (32 values) per warp, lane = element.  ggml's reference rounding
-// (quantize_row_q8_0_ref): d = amax/127, id = 1/d (0 when d == 0), q = roundf(x*id), d -> f16.
+// One q8_0 block (32 values) per warp, lane = element (q8_0_quant_lane).
 __device__ __forceinline__ void quantize_q8_0_warp(const float * __restrict__ x, uint8_t * __restrict__ dst, int lane) {
-    const float v = x[lane];
-    float amax = fabsf(v);
-    #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    const float d  = __fdiv_rn(amax, 127.0f);
-    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-    const float q  = roundf(__fmul_rn(v, id));
-    dst[2 + lane] = (uint8_t) (int8_t) (int) q;
-    if (lane == 0) *reinterpret_cast<uint16_t *>(dst) = f32_to_f16_bits(d);   // q8_0 blocks are 2-byte aligned
+    uint16_t dbits;
+    dst[2 + lane] = (uint8_t) q8_0_quant_lane(x[lane], dbits);
+    if (lane == 0) *reinterpret_cast<uint16_t *>(dst) = dbits;   // q8_0 blocks are 2-byte aligned
 }
 
 // Write one token row of K (or V) with a whole CTA: kv_dim/32 q8_0 blocks, one per warp in turn.

@@ -78,6 +78,19 @@ __device__ __forceinline__ double warp_sum16_d(double v) {   // butterfly within
     return v;
 }
 
+// One q8_0 block (32 values) across a warp, lane = element, with ggml's reference rounding
+// (quantize_row_q8_0_ref): d = amax/127, id = 1/d (0 when d == 0), q = roundf(x*id), d stored as
+// f16.  Returns the lane's quantised value; dbits receives the f16 bits of d (in every lane).
+__device__ __forceinline__ int8_t q8_0_quant_lane(float v, uint16_t & dbits) {
+    float amax = fabsf(v);
+    #pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float d  = __fdiv_rn(amax, 127.0f);
+    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    dbits = f32_to_f16_bits(d);
+    return (int8_t) (int) roundf(__fmul_rn(v, id));
+}
+
 // Programmatic dependent launch: a kernel launched with programmatic stream serialization may
 // start while its predecessor runs; it must wait before touching what the predecessor writes.
 // Triggering lets the successor launch once every CTA of this grid has started or exited.

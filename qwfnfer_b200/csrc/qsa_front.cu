@@ -263,22 +263,46 @@ __device__ __forceinline__ void front_epilogue(const DevDesc & d, const FrontArg
     }
 }
 
-__global__ void __launch_bounds__(FR_THREADS, 2) front_kernel(DevDesc d, FrontArgs a) {
-    extern __shared__ __align__(16) float xs[];                 // [T][n_embd]
+// Arrival: the last CTA of a head group (of `chunks` CTAs) finishes it.  The barrier orders the
+// CTA's row stores before thread 0's release; its acquire orders the other CTAs' stores before our
+// reads.
+__device__ __forceinline__ void front_finish(const DevDesc & d, const FrontArgs & a, const FrontShape & sh, int kind,
+                                             int g, int chunks) {
     __shared__ bool is_last;
-    const FrontShape sh = front_shape(d);
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    // this CTA's kind, head group and 64-row chunk
-    int kind = 0, c = blockIdx.x;
+    __syncthreads();
+    const int gid = sh.gid0[kind] + g;
+    if (threadIdx.x == 0) {
+        unsigned prev;
+        asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], 1;" : "=r"(prev) : "l"(a.counters + gid) : "memory");
+        is_last = prev == (unsigned) chunks - 1;
+        if (is_last) a.counters[gid] = 0;                      // leave the counter at zero for the next call
+    }
+    __syncthreads();
+    if (!is_last) return;
+    front_epilogue(d, a, sh, kind, g);
+}
+
+// This CTA's kind, head group g and 32-row chunk of the group (chunks per group).
+__device__ __forceinline__ void front_cta_rows(const FrontShape & sh, int & kind, int & g, int & chunk, int & chunks) {
+    int c = blockIdx.x;
+    kind = 0;
     while (kind < FR_KINDS - 1 && c >= sh.groups[kind] * (sh.group_rows[kind] / FR_ROWS)) {
         c -= sh.groups[kind] * (sh.group_rows[kind] / FR_ROWS);
         kind++;
     }
-    const int chunks = sh.group_rows[kind] / FR_ROWS;
-    const int g = c / chunks, chunk = c % chunks;
+    chunks = sh.group_rows[kind] / FR_ROWS;
+    g = c / chunks;
+    chunk = c % chunks;
+}
+
+__global__ void __launch_bounds__(FR_THREADS, 2) front_kernel(DevDesc d, FrontArgs a) {
+    extern __shared__ __align__(16) float xs[];                 // [T][n_embd]
+    const FrontShape sh = front_shape(d);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    int kind, g, chunk, chunks;
+    front_cta_rows(sh, kind, g, chunk, chunks);
     const int row_in_kind = g * sh.group_rows[kind] + chunk * FR_ROWS;
     const int T = a.T, n = a.n_embd;
-
 
     gemv_stream<FR_UNROLL>(a.w[kind] + (size_t) (row_in_kind + warp * (FR_ROWS / 8)) * n, FR_ROWS / 8, n, xs, T, lane,
         [&] {   // the activations go to shared memory by cp.async ahead of the first weight loads' data;
@@ -300,20 +324,7 @@ __global__ void __launch_bounds__(FR_THREADS, 2) front_kernel(DevDesc d, FrontAr
         [&](int r, int t, float v) {
             a.y[(size_t) t * a.rows_total + sh.row0[kind] + row_in_kind + warp * (FR_ROWS / 8) + r] = v;
         });
-
-    // Arrival: the last CTA of the head group finishes it.  The barrier orders the CTA's row
-    // stores before thread 0's release; its acquire orders the other CTAs' stores before our reads.
-    __syncthreads();
-    const int gid = sh.gid0[kind] + g;
-    if (tid == 0) {
-        unsigned prev;
-        asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], 1;" : "=r"(prev) : "l"(a.counters + gid) : "memory");
-        is_last = prev == (unsigned) chunks - 1;
-        if (is_last) a.counters[gid] = 0;                      // leave the counter at zero for the next call
-    }
-    __syncthreads();
-    if (!is_last) return;
-    front_epilogue(d, a, sh, kind, g);
+    front_finish(d, a, sh, kind, g, chunks);
 }
 
 constexpr int OUT_ROWS = 16;               // attn_output rows per CTA (2 per warp)
@@ -341,6 +352,177 @@ __global__ void __launch_bounds__(FR_THREADS, 2) output_kernel(const uint16_t * 
             __syncthreads();
         },
         [&](int r, int t, float v) { y[(size_t) t * n_embd + row0 + r] = v; });
+}
+
+// ------------------------------------------------------------------ q8_0 weights
+// ggml's mul_mat over q8_0 weights quantises the activation row to q8_0 (its vec_dot_type) and
+// takes per 32-value block the integer sum of products times f32(d_w) * f32(d_x), accumulated in
+// f32 (ggml_vec_dot_q8_0_q8_0).  Here the activations are quantised with the reference rounding
+// (q8_0_quant_lane) and the integer sums are dp4a's.
+constexpr int Q8_CHUNK_BLOCKS = 64;                              // q8_0 blocks of a row per streaming step
+constexpr int Q8_CHUNK_BYTES  = Q8_CHUNK_BLOCKS * Q8_0_BYTES;    // 2176 bytes, 136 16-byte words
+constexpr int Q8_CHUNK_WORDS  = Q8_CHUNK_BYTES / 16;
+constexpr int Q8_WPL          = (Q8_CHUNK_WORDS + 31) / 32;      // words a lane loads per step
+
+// Shared memory of a q8_0 GEMV CTA for T tokens of n values: the tokens' q8_0 values and scales,
+// then every warp's two weight staging buffers.
+inline size_t q8_gemv_smem(int T, int n) {
+    return (size_t) T * n + (size_t) T * (n / QK8_0) * 4 + 8 * 2 * Q8_CHUNK_BYTES;
+}
+
+// One warp's q8_0 matrix-vector products: rows [0, wrows) of the q8_0 matrix at `wrow0` (rows of
+// n/32 blocks of 34 bytes; n a multiple of 256, so a row is a whole number of 16-byte words) times
+// the T token rows held as q8_0 in shared memory (xq int8 [T][n], xd f32 [T][n/32]).  A step is one
+// row's chunk of up to 64 blocks: the warp loads its 16-byte words (evict-first; the next step's
+// loads are issued before this step's products), stages them in one of its two shared buffers, and
+// lane = (block of 8, quarter) forms 8 products per token with two dp4a; the block's integer sum is
+// reduced over its 4 lanes and times f32(d_w) * f32(d_x) added to the lane's f32 accumulator; at
+// the row's end the 8 block slots are summed (fixed shuffle tree) and emit(r, t, sum) is called.
+template <typename Emit>
+__device__ __forceinline__ void gemv_stream_q8(const uint8_t * __restrict__ wrow0, int wrows, int n, const int8_t * xq,
+                                               const float * xd, int T, int lane, uint8_t * wbuf, Emit && emit) {
+    const int nb = n / QK8_0;
+    const size_t rb = (size_t) nb * Q8_0_BYTES;
+    const int chunks = (nb + Q8_CHUNK_BLOCKS - 1) / Q8_CHUNK_BLOCKS;
+    const int items = wrows * chunks;
+    auto load = [&](int it, uint4 (&v)[Q8_WPL]) {
+        const int row = it / chunks, c = it % chunks;
+        const int nwords = min(Q8_CHUNK_BLOCKS, nb - c * Q8_CHUNK_BLOCKS) * Q8_0_BYTES / 16;
+        const uint4 * p = reinterpret_cast<const uint4 *>(wrow0 + (size_t) row * rb + (size_t) c * Q8_CHUNK_BYTES);
+        #pragma unroll
+        for (int u = 0; u < Q8_WPL; u++) {
+            const int w = lane + 32 * u;
+            v[u] = w < nwords ? ld_stream(p + w) : make_uint4(0u, 0u, 0u, 0u);
+        }
+    };
+    uint4 cur[Q8_WPL], nxt[Q8_WPL];
+    float acc[FR_TOK];
+    #pragma unroll
+    for (int t = 0; t < FR_TOK; t++) acc[t] = 0.0f;
+    if (items > 0) load(0, cur);
+    const int part = lane & 3;
+    for (int it = 0; it < items; it++) {
+        if (it + 1 < items) load(it + 1, nxt);
+        const int c = it % chunks;
+        const int nblk = min(Q8_CHUNK_BLOCKS, nb - c * Q8_CHUNK_BLOCKS);     // a multiple of 8
+        uint8_t * buf = wbuf + (it & 1) * Q8_CHUNK_BYTES;
+        #pragma unroll
+        for (int u = 0; u < Q8_WPL; u++) {
+            const int w = lane + 32 * u;
+            if (w < Q8_CHUNK_WORDS) reinterpret_cast<uint4 *>(buf)[w] = cur[u];
+        }
+        __syncwarp();
+        for (int b = lane >> 2; b < nblk; b += 8) {
+            const uint8_t * blk = buf + b * Q8_0_BYTES;
+            const float dw = f16_bits_to_f32(*reinterpret_cast<const uint16_t *>(blk));
+            const uint32_t w0 = lds_u32_a2(blk + 2 + 8 * part), w1 = lds_u32_a2(blk + 6 + 8 * part);
+            const int gb = c * Q8_CHUNK_BLOCKS + b;
+            #pragma unroll
+            for (int t = 0; t < FR_TOK; t++) {
+                if (t >= T) break;
+                const uint2 xv = *reinterpret_cast<const uint2 *>(xq + (size_t) t * n + gb * QK8_0 + 8 * part);
+                int si = __dp4a((int) w0, (int) xv.x, 0);
+                si = __dp4a((int) w1, (int) xv.y, si);
+                si += __shfl_xor_sync(0xffffffffu, si, 1);
+                si += __shfl_xor_sync(0xffffffffu, si, 2);
+                acc[t] = __fadd_rn(acc[t], __fmul_rn((float) si, __fmul_rn(dw, xd[t * nb + gb])));
+            }
+        }
+        if (c == chunks - 1) {                                  // the row is complete
+            #pragma unroll
+            for (int t = 0; t < FR_TOK; t++) {
+                float sacc = acc[t];
+                #pragma unroll
+                for (int o = 4; o < 32; o <<= 1) sacc += __shfl_xor_sync(0xffffffffu, sacc, o);
+                if (lane == 0 && t < T) emit(it / chunks, t, sacc);
+                acc[t] = 0.0f;
+            }
+        }
+        #pragma unroll
+        for (int u = 0; u < Q8_WPL; u++) cur[u] = nxt[u];
+    }
+}
+
+// The T token rows (f32, n values each, from global) quantised to q8_0 into shared memory, one
+// block per warp in turn; with `gate` each value is first multiplied by sigmoid(gate) (the output
+// side's ggml_mul(attn, ggml_sigmoid(gate)) in f32, 1/(1+exp(-g))).
+__device__ __forceinline__ void stage_q8(const float * __restrict__ x, const float * __restrict__ gate, int T, int n,
+                                         int8_t * xq, float * xd) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nb = n / QK8_0;
+    for (int i = warp; i < T * nb; i += FR_THREADS / 32) {
+        float v = __ldg(x + (size_t) i * QK8_0 + lane);
+        if (gate) v = __fmul_rn(v, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-__ldg(gate + (size_t) i * QK8_0 + lane)))));
+        uint16_t db;
+        xq[(size_t) i * QK8_0 + lane] = q8_0_quant_lane(v, db);
+        if (lane == 0) xd[i] = f16_bits_to_f32(db);
+    }
+    __syncthreads();
+}
+
+// front_kernel over q8_0 weights (the same rows per CTA, finish and outputs).
+__global__ void __launch_bounds__(FR_THREADS, 2) front_kernel_q8(DevDesc d, FrontArgs a) {
+    extern __shared__ __align__(16) unsigned char fq_smem[];
+    const FrontShape sh = front_shape(d);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int kind, g, chunk, chunks;
+    front_cta_rows(sh, kind, g, chunk, chunks);
+    const int T = a.T, n = a.n_embd;
+    int8_t * xq = reinterpret_cast<int8_t *>(fq_smem);
+    float * xd = reinterpret_cast<float *>(fq_smem + (size_t) T * n);
+    uint8_t * wbuf = fq_smem + (size_t) T * n + (size_t) T * (n / QK8_0) * 4 + warp * 2 * Q8_CHUNK_BYTES;
+    const int row_in_kind = g * sh.group_rows[kind] + chunk * FR_ROWS;
+    const size_t rb = (size_t) (n / QK8_0) * Q8_0_BYTES;
+    stage_q8(a.x, nullptr, T, n, xq, xd);
+    gemv_stream_q8(reinterpret_cast<const uint8_t *>(a.w[kind]) + (size_t) (row_in_kind + warp * (FR_ROWS / 8)) * rb,
+                   FR_ROWS / 8, n, xq, xd, T, lane, wbuf, [&](int r, int t, float v) {
+        a.y[(size_t) t * a.rows_total + sh.row0[kind] + row_in_kind + warp * (FR_ROWS / 8) + r] = v;
+    });
+    front_finish(d, a, sh, kind, g, chunks);
+}
+
+// output_kernel over a q8_0 attn_output: z = attn * sigmoid(gate) in f32, quantised to q8_0.
+__global__ void __launch_bounds__(FR_THREADS, 2) output_kernel_q8(const uint8_t * __restrict__ wo, int n_embd, int n_in,
+        int T, const float * __restrict__ attn, const float * __restrict__ gate, float * __restrict__ y) {
+    extern __shared__ __align__(16) unsigned char oq_smem[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int8_t * zq = reinterpret_cast<int8_t *>(oq_smem);
+    float * zd = reinterpret_cast<float *>(oq_smem + (size_t) T * n_in);
+    uint8_t * wbuf = oq_smem + (size_t) T * n_in + (size_t) T * (n_in / QK8_0) * 4 + warp * 2 * Q8_CHUNK_BYTES;
+    const int row0 = blockIdx.x * OUT_ROWS + warp * (OUT_ROWS / 8);
+    const int wrows = max(0, min(OUT_ROWS / 8, n_embd - row0));
+    const size_t rb = (size_t) (n_in / QK8_0) * Q8_0_BYTES;
+    stage_q8(attn, gate, T, n_in, zq, zd);
+    gemv_stream_q8(wo + (size_t) row0 * rb, wrows, n_in, zq, zd, T, lane, wbuf,
+                   [&](int r, int t, float v) { y[(size_t) t * n_embd + row0 + r] = v; });
+}
+
+// GEMM-path operands of q8_0 weights: every q8_0 value as f16(f32(d) * q) (a thread per 8 values),
+// and activations (f32, optionally times sigmoid(gate)) quantised to q8_0 and stored the same way (a
+// warp per block).  The tensor-core products of these f16 values are exact; they differ from the
+// integer block sums of the reference only by the f16 rounding of each d * q.
+__global__ void q8_to_f16_kernel(const uint8_t * __restrict__ q, uint4 * __restrict__ out, size_t n8) {
+    for (size_t i = (size_t) blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (size_t) gridDim.x * blockDim.x) {
+        const uint8_t * blk = q + (i >> 2) * Q8_0_BYTES;
+        const float dd = f16_bits_to_f32(*reinterpret_cast<const uint16_t *>(blk));
+        const uint8_t * v = blk + 2 + (i & 3) * 8;
+        float f[8];
+        #pragma unroll
+        for (int k = 0; k < 8; k++) f[k] = __fmul_rn(dd, (float) (int8_t) v[k]);
+        out[i] = make_uint4(pack_f16x2(f[0], f[1]), pack_f16x2(f[2], f[3]), pack_f16x2(f[4], f[5]), pack_f16x2(f[6], f[7]));
+    }
+}
+
+__global__ void act_q8_f16_kernel(const float * __restrict__ x, const float * __restrict__ gate, uint16_t * __restrict__ out,
+                                  size_t n_blocks) {
+    const int lane = threadIdx.x & 31;
+    const size_t warps = (size_t) gridDim.x * (blockDim.x / 32);
+    for (size_t i = (size_t) blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5); i < n_blocks; i += warps) {
+        float v = x[i * QK8_0 + lane];
+        if (gate) v = __fmul_rn(v, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gate[i * QK8_0 + lane]))));
+        uint16_t db;
+        const int8_t qv = q8_0_quant_lane(v, db);
+        out[i * QK8_0 + lane] = f32_to_f16_bits(__fmul_rn(f16_bits_to_f32(db), (float) qv));
+    }
 }
 
 constexpr int FR_GEMV_MAX_T = 16;           // above: the projections run as tcgen05 GEMMs (qsa_proj_gemm.cu)
@@ -377,9 +559,10 @@ __global__ void rope_table_kernel(DevDesc d, const int * __restrict__ pos, int T
 }
 
 // The front's workspace.  Up to FR_GEMV_MAX_T tokens: the status word, the head-group counters and
-// FR_TOK tokens' projections.  Above: the status word, the tokens' activations in bf16 and their
-// rope table.
-struct FrontWs { size_t status, counters, y, xb, cs, total; bool gemm; };
+// FR_TOK tokens' projections.  Above: the status word, the tokens' activations as 16-bit GEMM
+// operands (bf16, or f16 of their q8_0 values), their rope table and, for q8_0 weights, the weights
+// as f16 GEMM operands.
+struct FrontWs { size_t status, counters, y, xb, cs, wdq, total; bool gemm; };
 
 size_t align256(size_t x) { return (x + 255) & ~(size_t) 255; }
 
@@ -387,20 +570,21 @@ size_t align256(size_t x) { return (x + 255) & ~(size_t) 255; }
 // 64 (other rope widths run through the GEMV path in token groups).
 bool front_gemm_path(const DevDesc & d, int T) { return T > FR_GEMV_MAX_T && d.rope_dim % 64 == 0; }
 
-FrontWs front_ws(const DevDesc & d, int T, int n_embd) {
-    const FrontShape sh = front_shape(d);
-    const int rows = sh.row0[FR_KINDS - 1] + MAX_IDX_DIM;
+size_t front_rows(const DevDesc & d) { const FrontShape sh = front_shape(d); return (size_t) sh.row0[FR_KINDS - 1] + MAX_IDX_DIM; }
+
+FrontWs front_ws(const DevDesc & d, int T, int n_embd, int w_type) {
     FrontWs w{};
     w.status = 0;
     w.counters = 16;
     w.gemm = front_gemm_path(d, T);
     if (!w.gemm) {
-        w.y = align256(w.counters + (size_t) sh.n_groups * 4);
-        w.total = w.y + (size_t) FR_TOK * rows * 4;
+        w.y = align256(w.counters + (size_t) front_shape(d).n_groups * 4);
+        w.total = w.y + (size_t) FR_TOK * front_rows(d) * 4;
     } else {
         w.xb = 256;
         w.cs = align256(w.xb + (size_t) T * n_embd * 2);
-        w.total = align256(w.cs + (size_t) T * (d.rope_dim / 2) * 8);
+        w.wdq = align256(w.cs + (size_t) T * (d.rope_dim / 2) * 8);
+        w.total = w_type == QSA_TYPE_Q8_0 ? align256(w.wdq + front_rows(d) * n_embd * 2) : w.wdq;
     }
     return w;
 }
@@ -409,26 +593,54 @@ unsigned grid_for(size_t n, int per_thread_block = 256) {
     return (unsigned) std::min<size_t>((n + per_thread_block - 1) / per_thread_block, 148 * 8);
 }
 
-// The GEMM path for T > FR_GEMV_MAX_T tokens: x to bf16, the rope table, then one tcgen05 GEMM over
-// the five weight matrices whose epilogue applies the norms and IMRoPE and stores the outputs.
-qsa_status front_gemm(const DevDesc & d, const FrontArgs & a, int T, const FrontWs & L, unsigned char * wsb,
+qsa_status gemm_status(cudaError_t e) {
+    return e == cudaSuccess ? QSA_OK : (e == cudaErrorNotSupported ? QSA_ERR_UNSUPPORTED : QSA_ERR_CUDA);
+}
+
+// The GEMM path for T > FR_GEMV_MAX_T tokens: the activations as 16-bit operands (bf16; for q8_0
+// weights f16 of their q8_0 values, and the weights as f16 of theirs), the rope table, then one
+// tcgen05 GEMM over the five weight matrices whose epilogue applies the norms and IMRoPE and stores
+// the outputs.
+qsa_status front_gemm(const DevDesc & d, const FrontArgs & a, int T, int w_type, const FrontWs & L, unsigned char * wsb,
                       cudaStream_t st) {
     const int n = a.n_embd;
     uint16_t * xb = reinterpret_cast<uint16_t *>(wsb + L.xb);
     float2 * cs = reinterpret_cast<float2 *>(wsb + L.cs);
-    const size_t n4 = (size_t) T * n / 4;
-    to_bf16_kernel<<<grid_for(n4), 256, 0, st>>>(reinterpret_cast<const float4 *>(a.x), reinterpret_cast<uint2 *>(xb), n4);
+    const bool q8 = w_type == QSA_TYPE_Q8_0;
+    const void * w[5] = {a.w[0], a.w[1], a.w[2], a.w[3], a.w[4]};
+    if (q8) {
+        const size_t nblk = (size_t) T * n / QK8_0;
+        act_q8_f16_kernel<<<grid_for(nblk * 32), 256, 0, st>>>(a.x, nullptr, xb, nblk);
+        const FrontShape sh = front_shape(d);
+        uint16_t * wdq = reinterpret_cast<uint16_t *>(wsb + L.wdq);
+        for (int k = 0; k < FR_KINDS; k++) {
+            const size_t rows = (size_t) sh.groups[k] * sh.group_rows[k];
+            uint16_t * dst = wdq + (size_t) sh.row0[k] * n;
+            q8_to_f16_kernel<<<grid_for(rows * n / 8), 256, 0, st>>>(static_cast<const uint8_t *>(w[k]),
+                                                                    reinterpret_cast<uint4 *>(dst), rows * n / 8);
+            w[k] = dst;
+        }
+    } else {
+        const size_t n4 = (size_t) T * n / 4;
+        to_bf16_kernel<<<grid_for(n4), 256, 0, st>>>(reinterpret_cast<const float4 *>(a.x), reinterpret_cast<uint2 *>(xb), n4);
+    }
     rope_table_kernel<<<grid_for((size_t) T * (d.rope_dim / 2)), 256, 0, st>>>(d, a.pos, T, cs);
     if (cudaGetLastError() != cudaSuccess) return QSA_ERR_CUDA;
-    const void * w[5] = {a.w[0], a.w[1], a.w[2], a.w[3], a.w[4]};
     const float * norm[3] = {a.norm[0], a.norm[1], a.norm[2]};
     float * out[6] = {a.q_out, a.gate_out, a.q_idx_out, a.k_out, a.v_out, a.kidx_out};
-    const cudaError_t e = launch_proj_gemm_front(d, st, T, n, xb, w, false, cs, norm, out,
-                                                 reinterpret_cast<uint32_t *>(wsb + L.status));
-    return e == cudaSuccess ? QSA_OK : (e == cudaErrorNotSupported ? QSA_ERR_UNSUPPORTED : QSA_ERR_CUDA);
+    return gemm_status(launch_proj_gemm_front(d, st, T, n, xb, w, q8, cs, norm, out,
+                                              reinterpret_cast<uint32_t *>(wsb + L.status)));
 }
 
 bool aligned16(const void * p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Weight formats of the projections: bf16 rows (n a multiple of 8), or q8_0 rows (n a multiple of
+// 256: whole 16-byte words per row, and whole 8-block groups for the GEMV's lane layout).
+bool weight_shape_ok(int w_type, int n) {
+    if (w_type == QSA_TYPE_BF16) return n % 8 == 0;
+    if (w_type == QSA_TYPE_Q8_0) return n % 256 == 0;
+    return false;
+}
 
 }  // namespace
 }  // namespace qsa
@@ -437,7 +649,7 @@ using namespace qsa;
 
 extern "C" size_t qsa_front_workspace_size(const qsa_desc * dd, const qsa_front_weights * w, int32_t T) {
     if (qsa_desc_check(dd) != QSA_OK || !w || T <= 0 || w->n_embd <= 0) return 0;
-    return front_ws(dev_desc(dd), T, w->n_embd).total;
+    return front_ws(dev_desc(dd), T, w->n_embd, w->w_type).total;
 }
 
 extern "C" qsa_status qsa_front(const qsa_desc * dd, const qsa_front_weights * w, int32_t T, const int32_t * pos,
@@ -449,20 +661,25 @@ extern "C" qsa_status qsa_front(const qsa_desc * dd, const qsa_front_weights * w
     if (!w || T <= 0 || !pos || !x || !q_out || !gate_out || !q_idx_out || !k_out || !v_out || !kidx_out)
         return QSA_ERR_INVALID;
     if (!w->wq || !w->wk || !w->wv || !w->wq_idx || !w->wk_idx) return QSA_ERR_INVALID;
-    if (w->w_type != QSA_TYPE_BF16) return QSA_ERR_UNSUPPORTED;
-    if (w->n_embd <= 0 || w->n_embd % 8 != 0 || w->n_embd > FR_MAX_EMBD) return QSA_ERR_UNSUPPORTED;
+    if (w->w_type != QSA_TYPE_BF16 && w->w_type != QSA_TYPE_Q8_0) return QSA_ERR_UNSUPPORTED;
+    if (w->n_embd <= 0 || !weight_shape_ok(w->w_type, w->n_embd) || w->n_embd > FR_MAX_EMBD) return QSA_ERR_UNSUPPORTED;
     if (dd->rope_dim % 16 != 0) return QSA_ERR_UNSUPPORTED;          // pairs at a lane distance for 8 values a lane
     const void * ptrs[] = {w->wq, w->wk, w->wv, w->wq_idx, w->wk_idx, x, q_out, gate_out, q_idx_out, k_out, v_out, kidx_out};
     for (const void * p : ptrs)
         if (!aligned16(p)) return QSA_ERR_INVALID;
+    const bool q8 = w->w_type == QSA_TYPE_Q8_0;
     const DevDesc d = dev_desc(dd);
-    const FrontWs L = front_ws(d, T, w->n_embd);
+    const FrontWs L = front_ws(d, T, w->n_embd, w->w_type);
     if (!ws || ws_bytes < L.total) return QSA_ERR_WORKSPACE;
     // the GEMM path's tensor maps want their base addresses 16-byte aligned (slices of ws at 256)
-    if (L.gemm && (reinterpret_cast<uintptr_t>(ws) & 15u)) return QSA_ERR_WORKSPACE;
+    if (L.gemm && !aligned16(ws)) return QSA_ERR_WORKSPACE;
     static std::atomic<uint64_t> attr{0};
     cudaError_t e = once_per_device(attr, [] {
-        return cudaFuncSetAttribute(front_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FR_TOK * FR_MAX_EMBD * 4);
+        cudaError_t r = cudaFuncSetAttribute(front_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FR_TOK * FR_MAX_EMBD * 4);
+        if (r == cudaSuccess)
+            r = cudaFuncSetAttribute(front_kernel_q8, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int) q8_gemv_smem(FR_TOK, FR_MAX_EMBD));
+        return r;
     });
     if (e != cudaSuccess) return QSA_ERR_CUDA;
     const FrontShape sh = front_shape(d);
@@ -477,12 +694,12 @@ extern "C" qsa_status qsa_front(const qsa_desc * dd, const qsa_front_weights * w
     a.counters = reinterpret_cast<unsigned *>(wsb + L.counters);
     a.y = reinterpret_cast<float *>(wsb + L.y);
     a.n_embd = w->n_embd;
-    a.rows_total = sh.row0[FR_KINDS - 1] + MAX_IDX_DIM;
+    a.rows_total = (int) front_rows(d);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     if (L.gemm) {
         a.pos = pos; a.x = x; a.q_out = q_out; a.gate_out = gate_out; a.q_idx_out = q_idx_out;
         a.k_out = k_out; a.v_out = v_out; a.kidx_out = kidx_out;
-        return front_gemm(d, a, T, L, wsb, st);
+        return front_gemm(d, a, T, w->w_type, L, wsb, st);
     }
     const size_t kv = (size_t) d.n_head_kv * HEAD_DIM;
     for (int t0 = 0; t0 < T; t0 += FR_TOK) {                   // token groups run one after another on the stream
@@ -495,24 +712,29 @@ extern "C" qsa_status qsa_front(const qsa_desc * dd, const qsa_front_weights * w
         a.k_out = k_out + t0 * kv;
         a.v_out = v_out + t0 * kv;
         a.kidx_out = kidx_out + (size_t) t0 * MAX_IDX_DIM;
-        front_kernel<<<sh.ctas, FR_THREADS, (size_t) a.T * w->n_embd * 4, st>>>(d, a);
+        if (q8) front_kernel_q8<<<sh.ctas, FR_THREADS, q8_gemv_smem(a.T, w->n_embd), st>>>(d, a);
+        else    front_kernel<<<sh.ctas, FR_THREADS, (size_t) a.T * w->n_embd * 4, st>>>(d, a);
         if ((e = cudaGetLastError()) != cudaSuccess) return QSA_ERR_CUDA;
     }
     return QSA_OK;
 }
 
-// The output side's workspace: none up to FR_GEMV_MAX_T tokens; above, the status word and the gated
-// activations in bf16 (the GEMM's A operand).
-size_t out_ws_bytes(const qsa_desc * d, int T, size_t * z_off) {
+// The output side's workspace: none up to FR_GEMV_MAX_T tokens; above, the status word, the gated
+// activations as the GEMM's 16-bit A operand (bf16, or f16 of their q8_0 values for q8_0 weights)
+// and, for q8_0 weights, attn_output as f16.
+size_t out_ws_bytes(const qsa_desc * d, int n_embd, int T, int w_type, size_t * z_off, size_t * w_off) {
     if (T <= FR_GEMV_MAX_T) return 0;
+    const size_t n_in = (size_t) d->n_head * d->head_dim;
     *z_off = 256;
-    return align256(*z_off + (size_t) T * d->n_head * d->head_dim * 2);
+    *w_off = align256(*z_off + (size_t) T * n_in * 2);
+    return w_type == QSA_TYPE_Q8_0 ? align256(*w_off + (size_t) n_embd * n_in * 2) : *w_off;
 }
 
-extern "C" size_t qsa_output_workspace_size(const qsa_desc * dd, int32_t n_embd, int32_t T) {
+extern "C" size_t qsa_output_workspace_size(const qsa_desc * dd, int32_t n_embd, int32_t w_type, int32_t T) {
     if (qsa_desc_check(dd) != QSA_OK || n_embd <= 0 || T <= 0) return 0;
-    size_t off = 0;
-    return out_ws_bytes(dd, T, &off);
+    if (w_type != QSA_TYPE_BF16 && w_type != QSA_TYPE_Q8_0) return 0;
+    size_t a = 0, b = 0;
+    return out_ws_bytes(dd, n_embd, T, w_type, &a, &b);
 }
 
 extern "C" qsa_status qsa_output(const qsa_desc * dd, const void * wo, int32_t n_embd, int32_t w_type, int32_t T,
@@ -521,39 +743,57 @@ extern "C" qsa_status qsa_output(const qsa_desc * dd, const void * wo, int32_t n
     qsa_status s = qsa_desc_check(dd);
     if (s != QSA_OK) return s;
     if (!wo || !attn || !gate || !y || T <= 0 || n_embd <= 0) return QSA_ERR_INVALID;
-    if (w_type != QSA_TYPE_BF16) return QSA_ERR_UNSUPPORTED;
+    if (w_type != QSA_TYPE_BF16 && w_type != QSA_TYPE_Q8_0) return QSA_ERR_UNSUPPORTED;
     if (!aligned16(wo) || !aligned16(attn) || !aligned16(gate) || (reinterpret_cast<uintptr_t>(y) & 3u))
         return QSA_ERR_INVALID;
     const int n_in = dd->n_head * dd->head_dim;
-    if (n_in > OUT_MAX_IN || n_in % 8 != 0) return QSA_ERR_UNSUPPORTED;
-    size_t z_off = 0;
-    const size_t need = out_ws_bytes(dd, T, &z_off);
+    if (n_in > OUT_MAX_IN || !weight_shape_ok(w_type, n_in)) return QSA_ERR_UNSUPPORTED;
+    const bool q8 = w_type == QSA_TYPE_Q8_0;
+    size_t z_off = 0, w_off = 0;
+    const size_t need = out_ws_bytes(dd, n_embd, T, w_type, &z_off, &w_off);
     if (need && (!ws || ws_bytes < need || !aligned16(ws))) return QSA_ERR_WORKSPACE;
-    if (T > FR_GEMV_MAX_T) {       // a prefill-sized batch: y = zb wo^T as one GEMM
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (T > FR_GEMV_MAX_T) {       // a prefill-sized batch: y = z wo^T as one GEMM
         if (n_embd % 4 != 0) return QSA_ERR_UNSUPPORTED;      // float4 rows of the epilogue's stores
         if (!aligned16(y)) return QSA_ERR_INVALID;
-        cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
         unsigned char * wsb = static_cast<unsigned char *>(ws);
         uint16_t * zb = reinterpret_cast<uint16_t *>(wsb + z_off);
-        const size_t n4 = (size_t) T * n_in / 4;
-        gate_bf16_kernel<<<grid_for(n4), 256, 0, st>>>(reinterpret_cast<const float4 *>(attn),
-                                                      reinterpret_cast<const float4 *>(gate), reinterpret_cast<uint2 *>(zb), n4);
+        const void * w16 = wo;
+        if (q8) {
+            const size_t nblk = (size_t) T * n_in / QK8_0;
+            act_q8_f16_kernel<<<grid_for(nblk * 32), 256, 0, st>>>(attn, gate, zb, nblk);
+            uint16_t * wdq = reinterpret_cast<uint16_t *>(wsb + w_off);
+            const size_t n8 = (size_t) n_embd * n_in / 8;
+            q8_to_f16_kernel<<<grid_for(n8), 256, 0, st>>>(static_cast<const uint8_t *>(wo), reinterpret_cast<uint4 *>(wdq), n8);
+            w16 = wdq;
+        } else {
+            const size_t n4 = (size_t) T * n_in / 4;
+            gate_bf16_kernel<<<grid_for(n4), 256, 0, st>>>(reinterpret_cast<const float4 *>(attn),
+                                                          reinterpret_cast<const float4 *>(gate), reinterpret_cast<uint2 *>(zb), n4);
+        }
         if (cudaGetLastError() != cudaSuccess) return QSA_ERR_CUDA;
-        const cudaError_t e = launch_proj_gemm_plain(st, T, n_in, n_embd, zb, wo, false, y, reinterpret_cast<uint32_t *>(wsb));
-        return e == cudaSuccess ? QSA_OK : (e == cudaErrorNotSupported ? QSA_ERR_UNSUPPORTED : QSA_ERR_CUDA);
+        return gemm_status(launch_proj_gemm_plain(st, T, n_in, n_embd, zb, w16, q8, y, reinterpret_cast<uint32_t *>(wsb)));
     }
     static std::atomic<uint64_t> attr{0};
     cudaError_t e = once_per_device(attr, [] {
-        return cudaFuncSetAttribute(output_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FR_TOK * OUT_MAX_IN * 4);
+        cudaError_t r = cudaFuncSetAttribute(output_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FR_TOK * OUT_MAX_IN * 4);
+        if (r == cudaSuccess)
+            r = cudaFuncSetAttribute(output_kernel_q8, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int) q8_gemv_smem(FR_TOK, OUT_MAX_IN));
+        return r;
     });
     if (e != cudaSuccess) return QSA_ERR_CUDA;
-    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     const unsigned grid = (unsigned) ((n_embd + OUT_ROWS - 1) / OUT_ROWS);
     for (int t0 = 0; t0 < T; t0 += FR_TOK) {
         const int Tg = std::min(FR_TOK, T - t0);
-        output_kernel<<<grid, FR_THREADS, (size_t) Tg * n_in * 4, st>>>(
-            static_cast<const uint16_t *>(wo), n_embd, n_in, Tg, attn + (size_t) t0 * n_in, gate + (size_t) t0 * n_in,
-            y + (size_t) t0 * n_embd);
+        if (q8)
+            output_kernel_q8<<<grid, FR_THREADS, q8_gemv_smem(Tg, n_in), st>>>(
+                static_cast<const uint8_t *>(wo), n_embd, n_in, Tg, attn + (size_t) t0 * n_in, gate + (size_t) t0 * n_in,
+                y + (size_t) t0 * n_embd);
+        else
+            output_kernel<<<grid, FR_THREADS, (size_t) Tg * n_in * 4, st>>>(
+                static_cast<const uint16_t *>(wo), n_embd, n_in, Tg, attn + (size_t) t0 * n_in, gate + (size_t) t0 * n_in,
+                y + (size_t) t0 * n_embd);
         if ((e = cudaGetLastError()) != cudaSuccess) return QSA_ERR_CUDA;
     }
     return QSA_OK;

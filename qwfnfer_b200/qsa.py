@@ -253,27 +253,39 @@ class QsaDecodeStep:
         return self.host_out
 
 
+def _weight_format(t: torch.Tensor) -> tuple[int, int]:
+    """(qsa type, row length in values) of a projection weight held as ggml holds it: bf16
+    [out][n], or q8_0 rows as bytes uint8 [out][n/32*34]."""
+    if t.dim() == 2 and t.dtype == torch.bfloat16:
+        return TYPE_BF16, int(t.shape[1])
+    if t.dim() == 2 and t.dtype == torch.uint8 and t.shape[1] % 34 == 0:
+        return _abi.TYPE_Q8_0, int(t.shape[1]) // 34 * 32
+    raise QsaError(_abi.QSA_ERR_INVALID, "projection weights: bf16 [out][n] or q8_0 bytes uint8 [out][n/32*34]")
+
+
 class QsaFront:
-    """The projections feeding the node of one layer (qsa_front): bf16 weights, row-major
-    [out][n_embd] as ggml holds them (attn_q with query and gate interleaved per head, attn_k,
-    attn_v, indexer.q_proj, indexer.k_proj) and the f32 norm weights.  project() returns
-    qsa_decode's inputs: q (f32, QSA_TYPE_F32), q_idx, k_new, v_new, kidx_new, and the gate."""
+    """The projections feeding the node of one layer (qsa_front): weights row-major [out][n_embd]
+    as ggml holds them (attn_q with query and gate interleaved per head, attn_k, attn_v,
+    indexer.q_proj, indexer.k_proj), bf16 or q8_0 (uint8 rows of n_embd/32 blocks of 34 bytes),
+    and the f32 norm weights.  project() returns qsa_decode's inputs: q (f32, QSA_TYPE_F32), q_idx,
+    k_new, v_new, kidx_new, and the gate."""
 
     def __init__(self, desc: QsaDesc, wq: torch.Tensor, wk: torch.Tensor, wv: torch.Tensor, wq_idx: torch.Tensor,
                  wk_idx: torch.Tensor, q_norm: torch.Tensor | None = None, k_norm: torch.Tensor | None = None,
                  q_idx_norm: torch.Tensor | None = None):
-        for t in (wq, wk, wv, wq_idx, wk_idx):
-            if t.dtype != torch.bfloat16 or t.dim() != 2 or t.shape[1] != wq.shape[1]:
-                raise QsaError(_abi.QSA_ERR_INVALID, "front weights: bf16 [out][n_embd]")
+        fmts = {_weight_format(t) for t in (wq, wk, wv, wq_idx, wk_idx)}
+        if len(fmts) != 1:
+            raise QsaError(_abi.QSA_ERR_INVALID, "front weights: one format and row length for all five")
+        (w_type, n_embd), = fmts
         for t in (q_norm, k_norm, q_idx_norm):
             if t is not None and t.dtype != torch.float32:
                 raise QsaError(_abi.QSA_ERR_INVALID, "front norm weights: f32")
-        self.desc, self.device, self.n_embd = desc, wq.device, int(wq.shape[1])
+        self.desc, self.device, self.n_embd, self.w_type = desc, wq.device, n_embd, w_type
         self._keep = (wq, wk, wv, wq_idx, wk_idx, q_norm, k_norm, q_idx_norm)
         w = QsaFrontWeights()
         w.wq, w.wk, w.wv, w.wq_idx, w.wk_idx = (_ptr(t) for t in (wq, wk, wv, wq_idx, wk_idx))
         w.q_norm, w.k_norm, w.q_idx_norm = (_ptr(t) for t in (q_norm, k_norm, q_idx_norm))
-        w.n_embd, w.w_type = self.n_embd, TYPE_BF16
+        w.n_embd, w.w_type = self.n_embd, w_type
         self.w = w
         self._ws: torch.Tensor | None = None
 
@@ -308,21 +320,23 @@ class QsaFront:
 
 class QsaOutput:
     """The output side of the node (qsa_output): y = attn_output.weight (attn * sigmoid(gate)), the
-    bf16 weight row-major [n_embd][n_head*head_dim]."""
+    weight row-major [n_embd][n_head*head_dim] in bf16, or q8_0 bytes uint8 [n_embd][n_head*head_dim/32*34]."""
 
     def __init__(self, desc: QsaDesc, wo: torch.Tensor):
-        if wo.dtype != torch.bfloat16 or wo.dim() != 2 or wo.shape[1] != desc.n_head * desc.head_dim:
-            raise QsaError(_abi.QSA_ERR_INVALID, "attn_output weight: bf16 [n_embd][n_head*head_dim]")
+        self.w_type, n_in = _weight_format(wo)
+        if n_in != desc.n_head * desc.head_dim:
+            raise QsaError(_abi.QSA_ERR_INVALID, "attn_output weight: [n_embd][n_head*head_dim]")
         self.desc, self.wo, self.n_embd = desc, wo, int(wo.shape[0])
         self._ws: torch.Tensor | None = None
 
-    def workspace(self, T: int) -> torch.Tensor | None:
+    def workspace(self, T: int, stream=None) -> torch.Tensor | None:
         """The workspace of a T-token call (none up to 16 tokens; above, the GEMM path's)."""
-        size = lib().qsa_output_workspace_size(ctypes.byref(self.desc), self.n_embd, T)
+        size = lib().qsa_output_workspace_size(ctypes.byref(self.desc), self.n_embd, self.w_type, T)
         if size == 0:
             return None
         if self._ws is None or self._ws.numel() < size:
             self._ws = torch.empty(size, dtype=torch.uint8, device=self.wo.device)
+            check(lib().qsa_workspace_init(self._ws.data_ptr(), size, _stream(stream)), "qsa_workspace_init")
         return self._ws
 
     def project(self, attn: torch.Tensor, gate: torch.Tensor, out: torch.Tensor | None = None, stream=None):
@@ -330,8 +344,8 @@ class QsaOutput:
         T = attn.shape[0]
         if out is None:
             out = torch.empty((T, self.n_embd), dtype=torch.float32, device=self.wo.device)
-        ws = self.workspace(T)
-        check(lib().qsa_output(ctypes.byref(self.desc), _ptr(self.wo), self.n_embd, TYPE_BF16, T, _ptr(attn), _ptr(gate),
+        ws = self.workspace(T, stream)
+        check(lib().qsa_output(ctypes.byref(self.desc), _ptr(self.wo), self.n_embd, self.w_type, T, _ptr(attn), _ptr(gate),
                                _ptr(out), None if ws is None else ws.data_ptr(), 0 if ws is None else ws.numel(),
                                _stream(stream)), "qsa_output")
         return out

@@ -112,8 +112,11 @@ def test_output_host_refusals():
     assert call(attn=A + 4) == _abi.QSA_ERR_INVALID
     assert call(n_embd=0) == _abi.QSA_ERR_INVALID
     assert call(T=0) == _abi.QSA_ERR_INVALID
-    assert L.qsa_output_workspace_size(ctypes.byref(d), 2560, 16) == 0           # the GEMV path needs none
-    need = L.qsa_output_workspace_size(ctypes.byref(d), 2560, 64)
+    assert L.qsa_output_workspace_size(ctypes.byref(d), 2560, _abi.TYPE_BF16, 16) == 0   # the GEMV path needs none
+    assert L.qsa_output_workspace_size(ctypes.byref(d), 2560, TYPE_F16, 64) == 0         # no such weight type
+    assert (L.qsa_output_workspace_size(ctypes.byref(d), 2560, _abi.TYPE_Q8_0, 64) >
+            L.qsa_output_workspace_size(ctypes.byref(d), 2560, _abi.TYPE_BF16, 64))      # + attn_output as f16
+    need = L.qsa_output_workspace_size(ctypes.byref(d), 2560, _abi.TYPE_BF16, 64)
     assert need >= 64 * 4096 * 2
     assert call(T=64) == _abi.QSA_ERR_WORKSPACE                                   # the GEMM path without one
     assert call(T=64, ws_bytes=need - 16) == _abi.QSA_ERR_WORKSPACE

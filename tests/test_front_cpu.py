@@ -127,3 +127,69 @@ def test_oracle_output_matches_numpy():
     ref = z @ W.T
     bound = 1e-6 * (np.abs(z) @ np.abs(W).T) + 2 ** -7 * np.max(np.abs(z)[:, None, :] * np.abs(W)[None], axis=2)
     assert np.all(np.abs(got - ref) <= bound)
+
+
+def q8_rows(a: np.ndarray) -> np.ndarray:
+    """f32 [rows][n] -> q8_0 rows uint8 [rows][n/32*34] with the pinned reference quantiser."""
+    return oracle.q8_0_quantize(np.ascontiguousarray(a, np.float32))
+
+
+def np_q8_dot_rows(wq: np.ndarray, x: np.ndarray) -> np.ndarray:
+    """ggml_vec_dot_q8_0_q8_0 of every q8_0 weight row with x quantised to q8_0 (numpy, float64 sums
+    of the f32 block terms): per block the integer sum of products times f32(d_w) * f32(d_x)."""
+    n = x.shape[-1]
+    nb = n // 32
+    xq = q8_rows(x[None])[0].reshape(nb, 34)
+    xd = xq[:, :2].copy().view(np.float16).astype(np.float32)[:, 0]
+    xi = xq[:, 2:].view(np.int8).astype(np.int64)
+    w = wq.reshape(wq.shape[0], nb, 34)
+    wd = w[:, :, :2].copy().view(np.float16).astype(np.float32)[:, :, 0]
+    wi = w[:, :, 2:].view(np.int8).astype(np.int64)
+    sumi = (wi * xi[None]).sum(axis=2).astype(np.float32)
+    terms = sumi * (wd * xd[None]).astype(np.float32)
+    return terms.astype(np.float64).sum(axis=1).astype(np.float32)
+
+
+def test_oracle_q8_0_weights_front_and_output():
+    """q8_0 projection weights (what quantised GGUF checkpoints carry): the oracle quantises the
+    activations to q8_0 and takes integer block dots scaled by both f16 scales, as ggml's CPU
+    mul_mat does; checked against an independent numpy restatement, rows exact to f32 rounding."""
+    d = make_desc(idx_n_head=2)
+    n_embd = 512
+    rng = np.random.default_rng(3)
+    hd = d.head_dim
+    wf = {k: rng.standard_normal((r, n_embd), dtype=np.float32) * 0.02
+          for k, r in (("wq", 2 * hd * d.n_head), ("wk", hd * d.n_head_kv), ("wv", hd * d.n_head_kv),
+                       ("wq_idx", d.idx_dim * d.idx_n_head), ("wk_idx", d.idx_dim))}
+    w = {k: q8_rows(v) for k, v in wf.items()}
+    x = rng.standard_normal((2, n_embd), dtype=np.float32)
+    pos = np.array([7, 150000], np.int32)
+    got = oracle.front(d, w, pos, x, w_type=8)
+    for t in range(2):
+        gate = np.concatenate([np_q8_dot_rows(w["wq"][(2 * h + 1) * hd:(2 * h + 2) * hd], x[t]) for h in range(d.n_head)])
+        np.testing.assert_allclose(got["gate"][t], gate, rtol=1e-6, atol=1e-6)
+        np.testing.assert_allclose(got["v"][t], np_q8_dot_rows(w["wv"], x[t]), rtol=1e-6, atol=1e-6)
+        np.testing.assert_allclose(got["kidx"][t], np_q8_dot_rows(w["wk_idx"], x[t]), rtol=1e-6, atol=1e-6)
+    # the q8_0 result tracks the f32 product to the quantisation error
+    exact = x @ wf["wv"].T
+    assert np.abs(got["v"] - exact).max() <= 0.02 * np.abs(exact).max()
+    # output side
+    wo32 = rng.standard_normal((96, d.n_head * hd), dtype=np.float32) * 0.02
+    attn = rng.standard_normal((2, d.n_head, hd), dtype=np.float32)
+    g = rng.standard_normal((2, d.n_head * hd), dtype=np.float32)
+    y = oracle.output(d, q8_rows(wo32), attn, g, w_type=8)
+    z = attn.reshape(2, -1) * (np.float32(1) / (np.float32(1) + np.exp(-g)))
+    for t in range(2):
+        np.testing.assert_allclose(y[t], np_q8_dot_rows(q8_rows(wo32), z[t].astype(np.float32)), rtol=1e-5, atol=1e-6)
+
+
+def test_synthetic_q8_0_weights_use_the_pinned_rounding():
+    """configs.q8_0_rows (the torch quantiser of the synthetic q8_0 weights) gives the bytes of the
+    oracle's quantiser, which the gguf-py golden vectors pin to ggml's reference rounding."""
+    from qwfnfer_b200.configs import q8_0_rows, q8_0_rows_dequant
+    x = torch.randn(48, 512, generator=torch.Generator().manual_seed(5)) * 0.02
+    x[3, :32] = 0.0                                     # an all-zero block (d = 0)
+    x[4, 40] = 1e-3                                     # a block with one large value
+    q = q8_0_rows(x).numpy()
+    assert np.array_equal(q, oracle.q8_0_quantize(x.numpy()))
+    assert np.array_equal(q8_0_rows_dequant(torch.from_numpy(q)).numpy(), oracle.q8_0_dequantize(q))

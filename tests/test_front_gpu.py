@@ -284,3 +284,69 @@ def test_projection_gemm_full_chunk_sampled(which):
         ref = oracle.output(d, wo.view(torch.int16).cpu().numpy().view(np.uint16), a_s.cpu().numpy(), g_s.cpu().numpy())
         err = np.abs(y[samples].cpu().numpy() - ref)
         assert np.all(err <= output_bound(wo, a_s, g_s, GEMM_PROJ_TOL)), float(err.max())
+
+
+# q8_0 projection weights.  GEMV path (up to 16 tokens): integer block dots (dp4a) of the q8_0
+# weights with the q8_0-quantised activations, f32 sums of the block terms, as ggml's mul_mat; bound
+# 1e-5 of the row's sum of |w x| over the dequantised operands.  GEMM path: the tensor-core products
+# of the f16 roundings of every d * q (2^-11 relative each), bound 2e-4 of that sum and 2e-3 of the
+# largest normed output (the q8_0 quantisation itself moves the result by ~1%).
+Q8_GEMV_TOL, Q8_GEMM_TOL, Q8_GEMM_NORMED_TOL = 1e-5, 2e-4, 2e-3
+
+
+def q8_abs_row_sums(wq8: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+    """[T][rows] sums of |w * x| over the dequantised q8_0 weight and q8_0-quantised activation."""
+    from qwfnfer_b200.configs import q8_0_rows, q8_0_rows_dequant
+    xd = q8_0_rows_dequant(q8_0_rows(x))
+    return xd.abs() @ q8_0_rows_dequant(wq8).abs().T
+
+
+@pytest.mark.parametrize("T", [1, 5, 40])
+def test_front_q8_0_weights_match_oracle(T):
+    d = make_desc(n_ctx=1 << 20, idx_n_head=1)
+    w = front_weights(d, seed=90 + T, gammas=True, q8_0=True)
+    front = QsaFront(d, **w)
+    assert front.n_embd == 2560
+    g = torch.Generator(device="cuda").manual_seed(91)
+    x = torch.randn(T, front.n_embd, generator=g, device="cuda")
+    pos_list = [int(p) for p in torch.randint(0, 163840, (T,), generator=torch.Generator().manual_seed(T))]
+    pos = torch.tensor(pos_list, dtype=torch.int32, device="cuda")
+    q, gate, q_idx, k, v, kidx = front.project(x, pos)
+    torch.cuda.synchronize()
+    hw = {kk: t.cpu().numpy() for kk, t in w.items()}
+    ref = oracle.front(d, hw, np.array(pos_list, np.int32), x.cpu().numpy(), w_type=TYPE_Q8_0)
+    gemm = T > 16
+    tol, ntol = (Q8_GEMM_TOL, Q8_GEMM_NORMED_TOL) if gemm else (Q8_GEMV_TOL, NORMED_TOL)
+    hd = d.head_dim
+    wq_gate = w["wq"].view(d.n_head, 2, hd, -1)[:, 1].reshape(d.n_head * hd, -1)
+    for name, got, wt in (("gate", gate, wq_gate), ("v", v, w["wv"]), ("kidx", kidx, w["wk_idx"])):
+        bound = tol * q8_abs_row_sums(wt, x).cpu().numpy()
+        err = np.abs(got.cpu().numpy() - ref[name])
+        assert np.all(err <= bound + 1e-30), (name, float(err.max()), float(bound.max()))
+    for name, got in (("q", q), ("k", k), ("q_idx", q_idx)):
+        e = np.abs(got.cpu().numpy() - ref[name]).max() / np.abs(ref[name]).max()
+        assert e <= ntol, (name, e)
+
+
+@pytest.mark.parametrize("T", [1, 3, 24])
+def test_output_q8_0_weights_match_oracle(T):
+    from qwfnfer_b200.configs import q8_0_rows
+    d = make_desc()
+    g = torch.Generator(device="cuda").manual_seed(95 + T)
+    n_in = d.n_head * d.head_dim
+    wo = q8_0_rows(torch.randn(2560, n_in, generator=g, device="cuda") * 0.02)
+    attn = torch.randn(T, d.n_head, d.head_dim, generator=g, device="cuda")
+    gate = 2 * torch.randn(T, n_in, generator=g, device="cuda")
+    y = QsaOutput(d, wo).project(attn, gate)
+    torch.cuda.synchronize()
+    ref = oracle.output(d, wo.cpu().numpy(), attn.cpu().numpy(), gate.cpu().numpy(), w_type=TYPE_Q8_0)
+    z = attn.reshape(T, -1) * torch.sigmoid(gate)
+    tol = Q8_GEMM_TOL if T > 16 else Q8_GEMV_TOL
+    # the device and host expf may round one gated value apart, which can move its q8_0 value one step
+    # (or its block's scale): one step of the largest quantised term per row on top of the bound
+    from qwfnfer_b200.configs import q8_0_rows_dequant
+    wd = q8_0_rows_dequant(wo).abs()
+    step = (z.abs().amax(dim=1, keepdim=True) / 127.0) @ wd.amax(dim=1, keepdim=True).T
+    bound = tol * q8_abs_row_sums(wo, z).cpu().numpy() + 2.0 * step.cpu().numpy()
+    err = np.abs(y.cpu().numpy() - ref)
+    assert np.all(err <= bound), float((err / bound).max())
