@@ -158,6 +158,19 @@ qsa_status qsa_decode(const qsa_desc * d, const qsa_decode_item * items, int32_t
                       float * out, int32_t * sel_out,
                       void * ws, size_t ws_bytes, qsa_stream_t stream);
 
+/* qsa_decode with the node's output gate applied where the attention stores its result: besides
+ * (or, with out NULL, instead of) the f32 output, the call writes the gated product
+ *   z = out * sigmoid(gate)        (ggml_mul(attn, ggml_sigmoid(gate)), f32, sigmoid 1/(1+exp(-g)))
+ * gate: f32 [batch][n_head*head_dim] (qsa_front's gate), z: [batch][n_head*head_dim] as bf16
+ * (z_type QSA_TYPE_BF16: rounded as the bf16 attn_output mul_mat converts it) or f32
+ * (QSA_TYPE_F32, for q8_0 attn_output weights, which quantise it).  qsa_output_z then projects z.
+ * Replaces graph_builder::sparse_attn_decode through the gate multiply (src/qwfn_graph.cpp:450-544). */
+qsa_status qsa_decode_gated(const qsa_desc * d, const qsa_decode_item * items, int32_t batch, int32_t max_n_kv,
+                            const void * q, int32_t q_type, const float * q_idx,
+                            const float * k_new, const float * v_new, const float * kidx_new,
+                            const float * gate, void * z, int32_t z_type, float * out /* optional */,
+                            int32_t * sel_out, void * ws, size_t ws_bytes, qsa_stream_t stream);
+
 /* The three stages of qsa_decode as separate calls (same arguments and workspace), for callers
  * that append elsewhere or time the stages: append (row n_past of each item, plus the pooled key
  * of a block it completes), select (scores + top-k into the workspace, optional sel_out),
@@ -282,6 +295,16 @@ qsa_status qsa_prefill(const qsa_desc * d, const qsa_layer_cache * cache /* host
                        float * out, int32_t * sel_out,
                        void * ws, size_t ws_bytes, qsa_stream_t stream);
 
+/* qsa_prefill with the output gate applied in the attention's final store, as qsa_decode_gated
+ * (arguments as there, `batch` replaced by T).  Replaces graph_builder::sparse_attn through the gate
+ * multiply (src/qwfn_graph.cpp:235-405). */
+qsa_status qsa_prefill_gated(const qsa_desc * d, const qsa_layer_cache * cache /* host struct */,
+                             int32_t n_past, int32_t T,
+                             const void * q, int32_t q_type, const float * q_idx,
+                             const float * k_new, const float * v_new, const float * kidx_new,
+                             const float * gate, void * z, int32_t z_type, float * out /* optional */,
+                             int32_t * sel_out, void * ws, size_t ws_bytes, qsa_stream_t stream);
+
 /* ------------------------------------------------------------------ projection front */
 /* The projections feeding the node, as graph_builder::sparse_attn_decode builds them
  * (src/qwfn_graph.cpp:465, 479-484, 505-518; prefill :324-347).  Weights are row-major
@@ -339,6 +362,12 @@ size_t qsa_output_workspace_size(const qsa_desc * d, int32_t n_embd, int32_t w_t
 qsa_status qsa_output(const qsa_desc * d, const void * wo, int32_t n_embd, int32_t w_type, int32_t T,
                       const float * attn, const float * gate, float * y, void * ws, size_t ws_bytes,
                       qsa_stream_t stream);
+/* The attn_output projection of a gated product written by qsa_decode_gated / qsa_prefill_gated:
+ * y = attn_output.weight * z, z [T][n_head*head_dim] bf16 (z_type QSA_TYPE_BF16, bf16 weights only:
+ * the GEMM path reads it as its operand, no gate pass) or f32 (QSA_TYPE_F32, either weight type).
+ * Workspace, alignment and paths as qsa_output (src/qwfn_graph.cpp:545; prefill :406-407). */
+qsa_status qsa_output_z(const qsa_desc * d, const void * wo, int32_t n_embd, int32_t w_type, int32_t T,
+                        const void * z, int32_t z_type, float * y, void * ws, size_t ws_bytes, qsa_stream_t stream);
 
 /* ------------------------------------------------------------------ staging */
 /* Copy `bytes` (a multiple of 16, both addresses 16-byte aligned) from src to dst with a kernel on

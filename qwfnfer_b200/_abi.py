@@ -125,6 +125,9 @@ def lib() -> ctypes.CDLL:
         "qsa_decode_select": (I32, [D, VP, I32, I32, VP, VP, VP, SZ, VP]),
         "qsa_decode_attend": (I32, [D, VP, I32, I32, VP, I32, VP, VP, SZ, VP]),
         "qsa_decode_noalloc": (I32, [D, VP, I32, I32, VP, I32, VP, VP, VP, VP, VP, VP, VP]),
+        "qsa_decode_gated": (I32, [D, VP, I32, I32, VP, I32, VP, VP, VP, VP, VP, VP, I32, VP, VP, VP, SZ, VP]),
+        "qsa_prefill_gated": (I32, [D, C, I32, I32, VP, I32, VP, VP, VP, VP, VP, VP, I32, VP, VP, VP, SZ, VP]),
+        "qsa_output_z": (I32, [D, VP, I32, I32, I32, VP, I32, VP, VP, SZ, VP]),
         "qsa_shard_state_floats": (SZ, [D]),
         "qsa_shard_append": (I32, [D, C, I32, I32, I32, I32, VP, VP, VP, VP]),
         "qsa_shard_append_ri": (I32, [D, C, I32, I32, I32, I32, VP, VP, VP, VP]),
@@ -170,6 +173,7 @@ HEADER_SYMBOLS = [
     "qsa_merge_states",
     "qsa_ipc_handle", "qsa_ipc_open", "qsa_ipc_close", "qsa_peer_buffer_bytes", "qsa_peer_push", "qsa_peer_wait",
     "qsa_prefill_workspace_size", "qsa_prefill", "qsa_front_workspace_size", "qsa_front", "qsa_output_workspace_size", "qsa_output",
+    "qsa_decode_gated", "qsa_prefill_gated", "qsa_output_z",
     "qsa_stage_copy",
     "qsa_check", "qsa_version",
 ]

@@ -136,7 +136,7 @@ qsa_status launch_select(const DevDesc & d, const WsLayout & w, int n_q, const q
 
 // Attention over the selection held in the workspace (and the merge of split queries).
 qsa_status launch_attend(const DevDesc & d, const WsLayout & w, int n_q, const qsa_decode_item * items,
-                         qsa_layer_cache cache0, int n_past0, const void * q, int q_type, float * out,
+                         qsa_layer_cache cache0, int n_past0, const void * q, int q_type, OutSpec out,
                          unsigned char * ws, cudaStream_t st, float * state_out = nullptr) {
     return cuda_status(launch_attn(d, st, n_q, items, cache0, n_past0, q, q_type,
                                    reinterpret_cast<const int *>(ws + w.sel), reinterpret_cast<const int *>(ws + w.nsel),
@@ -351,18 +351,34 @@ qsa_status qsa_decode_attend(const qsa_desc * dd, const qsa_decode_item * items,
     if (s != QSA_OK) return s;
     if (!q || !out || (q_type != QSA_TYPE_BF16 && q_type != QSA_TYPE_F32)) return QSA_ERR_INVALID;
     qsa_layer_cache none{};
-    return launch_attend(d, w, batch, items, none, 0, q, q_type, out, static_cast<unsigned char *>(ws),
+    return launch_attend(d, w, batch, items, none, 0, q, q_type, OutSpec{out, nullptr, nullptr, 0}, static_cast<unsigned char *>(ws),
                          reinterpret_cast<cudaStream_t>(stream));
 }
 
-qsa_status qsa_decode(const qsa_desc * dd, const qsa_decode_item * items, int32_t batch, int32_t max_n_kv,
-                      const void * q, int32_t q_type, const float * q_idx,
-                      const float * k_new, const float * v_new, const float * kidx_new,
-                      float * out, int32_t * sel_out, void * ws, size_t ws_bytes, qsa_stream_t stream) {
+namespace {
+// An output descriptor from the public arguments: out and/or the gated product z (gate and z both
+// given, z_type QSA_TYPE_BF16 or QSA_TYPE_F32, 8- or 16-byte aligned as its element type needs).
+bool out_spec(float * out, const float * gate, void * z, int32_t z_type, OutSpec & o) {
+    o = OutSpec{out, nullptr, nullptr, 0};
+    if ((gate != nullptr) != (z != nullptr)) return false;
+    if (z) {
+        if (z_type != QSA_TYPE_BF16 && z_type != QSA_TYPE_F32) return false;
+        if ((reinterpret_cast<uintptr_t>(gate) & 15u) || (reinterpret_cast<uintptr_t>(z) & (z_type == QSA_TYPE_BF16 ? 7u : 15u)))
+            return false;
+        o.gate = gate; o.z = z; o.z_bf16 = z_type == QSA_TYPE_BF16;
+    }
+    if (out && (reinterpret_cast<uintptr_t>(out) & 15u)) return false;
+    return out || z;
+}
+
+qsa_status decode_impl(const qsa_desc * dd, const qsa_decode_item * items, int32_t batch, int32_t max_n_kv,
+                       const void * q, int32_t q_type, const float * q_idx,
+                       const float * k_new, const float * v_new, const float * kidx_new,
+                       const OutSpec & out, int32_t * sel_out, void * ws, size_t ws_bytes, qsa_stream_t stream) {
     DevDesc d; WsLayout w;
     qsa_status s = decode_common(dd, items, batch, max_n_kv, ws, ws_bytes, d, w);
     if (s != QSA_OK) return s;
-    if (!q || !q_idx || !out || (q_type != QSA_TYPE_BF16 && q_type != QSA_TYPE_F32)) return QSA_ERR_INVALID;
+    if (!q || !q_idx || (q_type != QSA_TYPE_BF16 && q_type != QSA_TYPE_F32)) return QSA_ERR_INVALID;
     const bool any_new = k_new || v_new || kidx_new;
     if (any_new && !(k_new && v_new && kidx_new)) return QSA_ERR_INVALID;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
@@ -374,14 +390,36 @@ qsa_status qsa_decode(const qsa_desc * dd, const qsa_decode_item * items, int32_
     if ((s = launch_select(d, w, batch, items, none, 0, q_idx, sel_out, wsb, st)) != QSA_OK) return s;
     return launch_attend(d, w, batch, items, none, 0, q, q_type, out, wsb, st);
 }
+}  // namespace
 
-qsa_status qsa_prefill(const qsa_desc * dd, const qsa_layer_cache * cache, int32_t n_past, int32_t T,
-                       const void * q, int32_t q_type, const float * q_idx,
-                       const float * k_new, const float * v_new, const float * kidx_new,
-                       float * out, int32_t * sel_out, void * ws, size_t ws_bytes, qsa_stream_t stream) {
+qsa_status qsa_decode(const qsa_desc * dd, const qsa_decode_item * items, int32_t batch, int32_t max_n_kv,
+                      const void * q, int32_t q_type, const float * q_idx,
+                      const float * k_new, const float * v_new, const float * kidx_new,
+                      float * out, int32_t * sel_out, void * ws, size_t ws_bytes, qsa_stream_t stream) {
+    if (!out) return QSA_ERR_INVALID;
+    return decode_impl(dd, items, batch, max_n_kv, q, q_type, q_idx, k_new, v_new, kidx_new,
+                       OutSpec{out, nullptr, nullptr, 0}, sel_out, ws, ws_bytes, stream);
+}
+
+qsa_status qsa_decode_gated(const qsa_desc * dd, const qsa_decode_item * items, int32_t batch, int32_t max_n_kv,
+                            const void * q, int32_t q_type, const float * q_idx,
+                            const float * k_new, const float * v_new, const float * kidx_new,
+                            const float * gate, void * z, int32_t z_type, float * out,
+                            int32_t * sel_out, void * ws, size_t ws_bytes, qsa_stream_t stream) {
+    OutSpec o;
+    if (!gate || !z || !out_spec(out, gate, z, z_type, o)) return QSA_ERR_INVALID;
+    return decode_impl(dd, items, batch, max_n_kv, q, q_type, q_idx, k_new, v_new, kidx_new, o, sel_out, ws, ws_bytes,
+                       stream);
+}
+
+namespace {
+qsa_status prefill_impl(const qsa_desc * dd, const qsa_layer_cache * cache, int32_t n_past, int32_t T,
+                        const void * q, int32_t q_type, const float * q_idx,
+                        const float * k_new, const float * v_new, const float * kidx_new,
+                        const OutSpec & out, int32_t * sel_out, void * ws, size_t ws_bytes, qsa_stream_t stream) {
     qsa_status s = qsa_desc_check(dd);
     if (s != QSA_OK) return s;
-    if (!cache || n_past < 0 || T <= 0 || (int64_t) n_past + T > dd->n_ctx || !q || !q_idx || !out) return QSA_ERR_INVALID;
+    if (!cache || n_past < 0 || T <= 0 || (int64_t) n_past + T > dd->n_ctx || !q || !q_idx) return QSA_ERR_INVALID;
     if (!cache->k || !cache->v || !cache->idx || !cache->pool) return QSA_ERR_INVALID;
     if (q_type != QSA_TYPE_BF16 && q_type != QSA_TYPE_F32) return QSA_ERR_INVALID;
     const bool any_new = k_new || v_new || kidx_new;
@@ -418,6 +456,26 @@ qsa_status qsa_prefill(const qsa_desc * dd, const qsa_layer_cache * cache, int32
                                                   reinterpret_cast<const int *>(wsb + w.nsel), prefill_n_blocks(d, n_past + T),
                                                   wsb + w.total, out, reinterpret_cast<uint32_t *>(wsb + w.status)));
     return launch_attend(d, w, T, nullptr, *cache, n_past, q, q_type, out, wsb, st);
+}
+}  // namespace
+
+qsa_status qsa_prefill(const qsa_desc * dd, const qsa_layer_cache * cache, int32_t n_past, int32_t T,
+                       const void * q, int32_t q_type, const float * q_idx,
+                       const float * k_new, const float * v_new, const float * kidx_new,
+                       float * out, int32_t * sel_out, void * ws, size_t ws_bytes, qsa_stream_t stream) {
+    if (!out) return QSA_ERR_INVALID;
+    return prefill_impl(dd, cache, n_past, T, q, q_type, q_idx, k_new, v_new, kidx_new, OutSpec{out, nullptr, nullptr, 0},
+                        sel_out, ws, ws_bytes, stream);
+}
+
+qsa_status qsa_prefill_gated(const qsa_desc * dd, const qsa_layer_cache * cache, int32_t n_past, int32_t T,
+                             const void * q, int32_t q_type, const float * q_idx,
+                             const float * k_new, const float * v_new, const float * kidx_new,
+                             const float * gate, void * z, int32_t z_type, float * out,
+                             int32_t * sel_out, void * ws, size_t ws_bytes, qsa_stream_t stream) {
+    OutSpec o;
+    if (!gate || !z || !out_spec(out, gate, z, z_type, o)) return QSA_ERR_INVALID;
+    return prefill_impl(dd, cache, n_past, T, q, q_type, q_idx, k_new, v_new, kidx_new, o, sel_out, ws, ws_bytes, stream);
 }
 
 qsa_status qsa_check(void * ws, size_t ws_bytes, qsa_stream_t stream) {
@@ -495,7 +553,7 @@ qsa_status qsa_shard_attend(const qsa_desc * dd, const qsa_decode_item * items, 
     if (e == cudaErrorInvalidValue) return QSA_ERR_UNSUPPORTED;       // too many candidates for one CTA
     if (e != cudaSuccess) return QSA_ERR_CUDA;
     qsa_layer_cache none{};
-    return launch_attend(d, w, batch, items, none, 0, q, q_type, nullptr, wsb, st, state);
+    return launch_attend(d, w, batch, items, none, 0, q, q_type, OutSpec{nullptr, nullptr, nullptr, 0}, wsb, st, state);
 }
 
 // ---- KV-sharded decode with the indexer caches replicated on every rank
@@ -531,7 +589,7 @@ qsa_status qsa_shard_decode_ri(const qsa_desc * dd, const qsa_decode_item * item
                                       reinterpret_cast<uint32_t *>(wsb + w.status))) != QSA_OK) return s;
     qsa_layer_cache none{};
     if ((s = launch_select(d, w, batch, items, none, 0, q_idx, sel_out, wsb, st)) != QSA_OK) return s;
-    return launch_attend(d, w, batch, items, none, 0, q, q_type, nullptr, wsb, st, state);
+    return launch_attend(d, w, batch, items, none, 0, q, q_type, OutSpec{nullptr, nullptr, nullptr, 0}, wsb, st, state);
 }
 
 qsa_status qsa_merge_states(const qsa_desc * dd, int32_t n_parts, int32_t batch, const float * states, float * out,

@@ -98,7 +98,7 @@ __global__ void __launch_bounds__(ATT_THREADS, AttnCfg<KV_TYPE>::MIN_CTAS) attn_
         const void * __restrict__ q, int q_type,
         const int * __restrict__ sel_ws, const int * __restrict__ nsel_ws, int tiles_per_cta, int max_chunks,
         float * __restrict__ part_o, float * __restrict__ part_ml,
-        float * __restrict__ out, uint32_t * __restrict__ status, float * __restrict__ state_out) {
+        OutSpec outs, uint32_t * __restrict__ status, float * __restrict__ state_out) {
     using Cfg = AttnCfg<KV_TYPE>;
     constexpr int NS = Cfg::NSTAGE, HB = Cfg::HB, RB = attn_row_bytes<KV_TYPE>();
     extern __shared__ __align__(128) unsigned char smem[];
@@ -177,7 +177,7 @@ __global__ void __launch_bounds__(ATT_THREADS, AttnCfg<KV_TYPE>::MIN_CTAS) attn_
     const int n_cells = nsel * r;
     const int n_tiles = (n_cells + ATT_CELLS - 1) / ATT_CELLS;
     const int n_chunks = attn_n_chunks(d, nsel, tiles_per_cta);
-    float * outq = out ? out + (size_t) t * d.n_head * HEAD_DIM : nullptr;
+    const size_t outq = (size_t) t * d.n_head * HEAD_DIM;     // element offset of query t's output
     // sharded mode: the unnormalised state [M 16][L 16][O 16x256] of query t instead of the output
     float * stq = state_out ? state_out + (size_t) t * (2 * HROWS + HROWS * HEAD_DIM) : nullptr;
     if (n_chunks == 0) {                       // nothing selected (or a bad position): zero output
@@ -185,7 +185,8 @@ __global__ void __launch_bounds__(ATT_THREADS, AttnCfg<KV_TYPE>::MIN_CTAS) attn_
             if (stq)
                 for (int i = tid; i < 2 * HROWS + HROWS * HEAD_DIM; i += ATT_THREADS) stq[i] = i < HROWS ? -INFINITY : 0.0f;
             else
-                for (int i = tid; i < d.n_head * HEAD_DIM; i += ATT_THREADS) outq[i] = 0.0f;
+                for (int i = 4 * tid; i < d.n_head * HEAD_DIM; i += 4 * ATT_THREADS)
+                    out_store4(outs, outq + i, make_float4(0.f, 0.f, 0.f, 0.f));
         }
         return;
     }
@@ -552,8 +553,8 @@ __global__ void __launch_bounds__(ATT_THREADS, AttnCfg<KV_TYPE>::MIN_CTAS) attn_
         } else if (hr < n_rows && h < d.gqa) {
             const float L = cml[HROWS + hr];
             const float inv = L > 0.0f ? 1.0f / L : 0.0f;
-            reinterpret_cast<float4 *>(outq + (size_t) hh * d.gqa * HEAD_DIM + (size_t) h * HEAD_DIM)[d4] =
-                make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+            out_store4(outs, outq + (size_t) hh * d.gqa * HEAD_DIM + (size_t) h * HEAD_DIM + 4 * d4,
+                       make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv));
         }
     }
     if (tid < 2 * HROWS) {
@@ -575,7 +576,7 @@ template <int PRE>
 __global__ void __launch_bounds__(MERGE_THREADS) attn_merge_kernel(DevDesc d, const qsa_decode_item * __restrict__ items,
         int n_past0, const int * __restrict__ nsel_ws, int tiles_per_cta, int max_chunks,
         const float * __restrict__ part_o, const float * __restrict__ part_ml,
-        float * __restrict__ out, float * __restrict__ state_out) {
+        OutSpec outs, float * __restrict__ state_out) {
     extern __shared__ float wsh[];                    // [max_chunks] weights
     __shared__ float red[2][MERGE_THREADS / 32];
     __shared__ float4 racc[MERGE_GROUPS][MERGE_COLS];
@@ -653,8 +654,8 @@ __global__ void __launch_bounds__(MERGE_THREADS) attn_merge_kernel(DevDesc d, co
             if (blockIdx.z == 0 && tid == 0) { stq[hr] = M; stq[HROWS + hr] = L; }
         } else {
             const float inv = L > 0.0f ? 1.0f / L : 0.0f;
-            reinterpret_cast<float4 *>(out + ((size_t) t * d.n_head + g * d.gqa + h) * HEAD_DIM)[d4] =
-                make_float4(s.x * inv, s.y * inv, s.z * inv, s.w * inv);
+            out_store4(outs, ((size_t) t * d.n_head + g * d.gqa + h) * HEAD_DIM + 4 * d4,
+                       make_float4(s.x * inv, s.y * inv, s.z * inv, s.w * inv));
         }
     }
 }
@@ -683,7 +684,7 @@ int attn_resident_ctas(int type_k) {
 
 cudaError_t launch_attn(const DevDesc & d, cudaStream_t st, int n_q, const qsa_decode_item * items,
         qsa_layer_cache cache0, int n_past0, const void * q, int q_type, const int * sel_ws, const int * nsel_ws,
-        int tiles_per_cta, int max_chunks, float * part_o, float * part_ml, float * out, uint32_t * status,
+        int tiles_per_cta, int max_chunks, float * part_o, float * part_ml, OutSpec outs, uint32_t * status,
         float * state_out) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned) max_chunks, (unsigned) n_q);
@@ -697,7 +698,7 @@ cudaError_t launch_attn(const DevDesc & d, cudaStream_t st, int n_q, const qsa_d
     cudaError_t e;
     cfg.dynamicSmemBytes = d.type_k == QSA_TYPE_Q8_0 ? attn_smem_bytes<QSA_TYPE_Q8_0>(d.kb) : attn_smem_bytes<QSA_TYPE_F16>(d.kb);
 #define QSA_LAUNCH_ATTN(T, N) cudaLaunchKernelEx(&cfg, attn_kernel<T, N>, d, items, cache0, n_past0, q, q_type, sel_ws, \
-                                                 nsel_ws, tiles_per_cta, max_chunks, part_o, part_ml, out, status, state_out)
+                                                 nsel_ws, tiles_per_cta, max_chunks, part_o, part_ml, outs, status, state_out)
     if (d.type_k == QSA_TYPE_Q8_0) e = d.n_head_kv == 2 ? QSA_LAUNCH_ATTN(QSA_TYPE_Q8_0, 2) : QSA_LAUNCH_ATTN(QSA_TYPE_Q8_0, 1);
     else                           e = d.n_head_kv == 2 ? QSA_LAUNCH_ATTN(QSA_TYPE_F16, 2) : QSA_LAUNCH_ATTN(QSA_TYPE_F16, 1);
 #undef QSA_LAUNCH_ATTN
@@ -708,9 +709,9 @@ cudaError_t launch_attn(const DevDesc & d, cudaStream_t st, int n_q, const qsa_d
     mc.dynamicSmemBytes = (size_t) max_chunks * 4;
     if (max_chunks > 2 * MERGE_GROUPS)
         return cudaLaunchKernelEx(&mc, attn_merge_kernel<16>, d, items, n_past0, nsel_ws, tiles_per_cta, max_chunks,
-                                  (const float *) part_o, (const float *) part_ml, out, state_out);
+                                  (const float *) part_o, (const float *) part_ml, outs, state_out);
     return cudaLaunchKernelEx(&mc, attn_merge_kernel<2>, d, items, n_past0, nsel_ws, tiles_per_cta, max_chunks,
-                              (const float *) part_o, (const float *) part_ml, out, state_out);
+                              (const float *) part_o, (const float *) part_ml, outs, state_out);
 }
 
 }  // namespace qsa

@@ -101,6 +101,35 @@ __device__ __forceinline__ void set_status(uint32_t * status, uint32_t code) {
     if (status) atomicOr(status, code);
 }
 
+// ------------------------------------------------------------------ the node's output
+// Where the attention output goes: `out` (f32 [n_q][n_head][head_dim], optional) and, with a gate,
+// the gated product z = out * sigmoid(gate) of the node's output side (ggml_mul(attn,
+// ggml_sigmoid(gate)), f32, sigmoid 1/(1+exp(-g))), stored as bf16 (rounded as the bf16
+// attn_output mul_mat converts it) or as f32 (z_bf16 = 0); gate and z are [n_q][n_head*head_dim].
+struct OutSpec {
+    float * out;
+    const float * gate;
+    void * z;
+    int z_bf16;
+};
+
+// Four consecutive output values at element offset `off` (a multiple of 4).
+__device__ __forceinline__ void out_store4(const OutSpec & o, size_t off, float4 v) {
+    if (o.out) *reinterpret_cast<float4 *>(o.out + off) = v;
+    if (o.z) {
+        const float4 g = *reinterpret_cast<const float4 *>(o.gate + off);
+        auto gz = [](float a, float b) { return __fmul_rn(a, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-b)))); };
+        const float z0 = gz(v.x, g.x), z1 = gz(v.y, g.y), z2 = gz(v.z, g.z), z3 = gz(v.w, g.w);
+        if (o.z_bf16) {
+            auto b16 = [](float x) { return (uint32_t) __bfloat16_as_ushort(__float2bfloat16_rn(x)); };
+            *reinterpret_cast<uint2 *>(static_cast<uint16_t *>(o.z) + off) = make_uint2(b16(z0) | (b16(z1) << 16),
+                                                                                        b16(z2) | (b16(z3) << 16));
+        } else {
+            *reinterpret_cast<float4 *>(static_cast<float *>(o.z) + off) = make_float4(z0, z1, z2, z3);
+        }
+    }
+}
+
 // ------------------------------------------------------------------ mbarrier + bulk copy
 __device__ __forceinline__ uint32_t smem_u32(const void * p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));

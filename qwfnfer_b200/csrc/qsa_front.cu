@@ -330,9 +330,10 @@ __global__ void __launch_bounds__(FR_THREADS, 2) front_kernel(DevDesc d, FrontAr
 constexpr int OUT_ROWS = 16;               // attn_output rows per CTA (2 per warp)
 constexpr int OUT_MAX_IN = 4096;           // n_head * head_dim
 
-// y[t][row] = sum_e wo[row][e] * bf16(attn[t][e] * sigmoid(gate[t][e])) for the launch's T tokens.
+// y[t][row] = sum_e wo[row][e] * bf16(attn[t][e] * sigmoid(gate[t][e])) for the launch's T tokens; with
+// gate null, attn holds the gated product already (f32, or bf16 values when z_bf16).
 __global__ void __launch_bounds__(FR_THREADS, 2) output_kernel(const uint16_t * __restrict__ wo, int n_embd, int n_in,
-        int T, const float * __restrict__ attn, const float * __restrict__ gate, float * __restrict__ y) {
+        int T, const float * __restrict__ attn, const float * __restrict__ gate, int z_bf16, float * __restrict__ y) {
     extern __shared__ __align__(16) float zs[];                 // [T][n_in]
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int row0 = blockIdx.x * OUT_ROWS + warp * (OUT_ROWS / 8);
@@ -341,13 +342,21 @@ __global__ void __launch_bounds__(FR_THREADS, 2) output_kernel(const uint16_t * 
         [] {},
         [&] {   // ggml_sigmoid: 1 / (1 + exp(-g)) in f32; the product rounded to bf16 as mul_mat converts it
             for (int i = tid; i < T * n_in / 4; i += FR_THREADS) {
-                const float4 o = reinterpret_cast<const float4 *>(attn)[i];
-                const float4 g = reinterpret_cast<const float4 *>(gate)[i];
-                auto z = [](float a, float b) {
-                    const float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-b)));
-                    return __bfloat162float(__float2bfloat16_rn(__fmul_rn(a, sg)));
-                };
-                reinterpret_cast<float4 *>(zs)[i] = make_float4(z(o.x, g.x), z(o.y, g.y), z(o.z, g.z), z(o.w, g.w));
+                float4 zz;
+                if (z_bf16) {
+                    const uint2 b = reinterpret_cast<const uint2 *>(attn)[i];
+                    zz = make_float4(__uint_as_float(b.x << 16), __uint_as_float(b.x & 0xffff0000u),
+                                     __uint_as_float(b.y << 16), __uint_as_float(b.y & 0xffff0000u));
+                } else {
+                    const float4 o = reinterpret_cast<const float4 *>(attn)[i];
+                    const float4 g = gate ? reinterpret_cast<const float4 *>(gate)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+                    auto z = [&](float a, float b) {
+                        const float v = gate ? __fmul_rn(a, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-b)))) : a;
+                        return __bfloat162float(__float2bfloat16_rn(v));
+                    };
+                    zz = make_float4(z(o.x, g.x), z(o.y, g.y), z(o.z, g.z), z(o.w, g.w));
+                }
+                reinterpret_cast<float4 *>(zs)[i] = zz;
             }
             __syncthreads();
         },
@@ -793,7 +802,76 @@ extern "C" qsa_status qsa_output(const qsa_desc * dd, const void * wo, int32_t n
         else
             output_kernel<<<grid, FR_THREADS, (size_t) Tg * n_in * 4, st>>>(
                 static_cast<const uint16_t *>(wo), n_embd, n_in, Tg, attn + (size_t) t0 * n_in, gate + (size_t) t0 * n_in,
-                y + (size_t) t0 * n_embd);
+                0, y + (size_t) t0 * n_embd);
+        if ((e = cudaGetLastError()) != cudaSuccess) return QSA_ERR_CUDA;
+    }
+    return QSA_OK;
+}
+
+// The output projection over the gated product the attention already wrote (qsa_decode_gated /
+// qsa_prefill_gated): z bf16 (bf16 weights) or f32 (either weight type) [T][n_head*head_dim].
+extern "C" qsa_status qsa_output_z(const qsa_desc * dd, const void * wo, int32_t n_embd, int32_t w_type, int32_t T,
+                                   const void * z, int32_t z_type, float * y, void * ws, size_t ws_bytes,
+                                   qsa_stream_t stream) {
+    qsa_status s = qsa_desc_check(dd);
+    if (s != QSA_OK) return s;
+    if (!wo || !z || !y || T <= 0 || n_embd <= 0) return QSA_ERR_INVALID;
+    if (w_type != QSA_TYPE_BF16 && w_type != QSA_TYPE_Q8_0) return QSA_ERR_UNSUPPORTED;
+    if (z_type != QSA_TYPE_F32 && !(z_type == QSA_TYPE_BF16 && w_type == QSA_TYPE_BF16)) return QSA_ERR_INVALID;
+    if (!aligned16(wo) || !aligned16(z) || (reinterpret_cast<uintptr_t>(y) & 3u)) return QSA_ERR_INVALID;
+    const int n_in = dd->n_head * dd->head_dim;
+    if (n_in > OUT_MAX_IN || !weight_shape_ok(w_type, n_in)) return QSA_ERR_UNSUPPORTED;
+    const bool q8 = w_type == QSA_TYPE_Q8_0, zb16 = z_type == QSA_TYPE_BF16;
+    size_t z_off = 0, w_off = 0;
+    const size_t need = out_ws_bytes(dd, n_embd, T, w_type, &z_off, &w_off);
+    if (need && (!ws || ws_bytes < need || !aligned16(ws))) return QSA_ERR_WORKSPACE;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (T > FR_GEMV_MAX_T) {
+        if (n_embd % 4 != 0) return QSA_ERR_UNSUPPORTED;
+        if (!aligned16(y)) return QSA_ERR_INVALID;
+        unsigned char * wsb = static_cast<unsigned char *>(ws);
+        const void * a16 = z;                  // bf16 z enters the GEMM as it is
+        const void * w16 = wo;
+        if (!zb16) {
+            uint16_t * zb = reinterpret_cast<uint16_t *>(wsb + z_off);
+            if (q8) {
+                const size_t nblk = (size_t) T * n_in / QK8_0;
+                act_q8_f16_kernel<<<grid_for(nblk * 32), 256, 0, st>>>(static_cast<const float *>(z), nullptr, zb, nblk);
+            } else {
+                const size_t n4 = (size_t) T * n_in / 4;
+                to_bf16_kernel<<<grid_for(n4), 256, 0, st>>>(static_cast<const float4 *>(z), reinterpret_cast<uint2 *>(zb), n4);
+            }
+            a16 = zb;
+        }
+        if (q8) {
+            uint16_t * wdq = reinterpret_cast<uint16_t *>(wsb + w_off);
+            const size_t n8 = (size_t) n_embd * n_in / 8;
+            q8_to_f16_kernel<<<grid_for(n8), 256, 0, st>>>(static_cast<const uint8_t *>(wo), reinterpret_cast<uint4 *>(wdq), n8);
+            w16 = wdq;
+        }
+        if (cudaGetLastError() != cudaSuccess) return QSA_ERR_CUDA;
+        return gemm_status(launch_proj_gemm_plain(st, T, n_in, n_embd, a16, w16, q8, y, reinterpret_cast<uint32_t *>(wsb)));
+    }
+    static std::atomic<uint64_t> attr{0};
+    cudaError_t e = once_per_device(attr, [] {
+        cudaError_t r = cudaFuncSetAttribute(output_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FR_TOK * OUT_MAX_IN * 4);
+        if (r == cudaSuccess)
+            r = cudaFuncSetAttribute(output_kernel_q8, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int) q8_gemv_smem(FR_TOK, OUT_MAX_IN));
+        return r;
+    });
+    if (e != cudaSuccess) return QSA_ERR_CUDA;
+    const unsigned grid = (unsigned) ((n_embd + OUT_ROWS - 1) / OUT_ROWS);
+    const size_t zes = zb16 ? 2 : 4;
+    for (int t0 = 0; t0 < T; t0 += FR_TOK) {
+        const int Tg = std::min(FR_TOK, T - t0);
+        const float * zt = reinterpret_cast<const float *>(static_cast<const unsigned char *>(z) + (size_t) t0 * n_in * zes);
+        if (q8)
+            output_kernel_q8<<<grid, FR_THREADS, q8_gemv_smem(Tg, n_in), st>>>(
+                static_cast<const uint8_t *>(wo), n_embd, n_in, Tg, zt, nullptr, y + (size_t) t0 * n_embd);
+        else
+            output_kernel<<<grid, FR_THREADS, (size_t) Tg * n_in * 4, st>>>(
+                static_cast<const uint16_t *>(wo), n_embd, n_in, Tg, zt, nullptr, zb16 ? 1 : 0, y + (size_t) t0 * n_embd);
         if ((e = cudaGetLastError()) != cudaSuccess) return QSA_ERR_CUDA;
     }
     return QSA_OK;

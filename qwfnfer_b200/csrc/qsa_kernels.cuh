@@ -48,7 +48,7 @@ DevDesc dev_desc(const qsa_desc * d);
 // of the merge of their partials (defined beside the kernels).
 cudaError_t launch_attn(const DevDesc & d, cudaStream_t st, int n_q, const qsa_decode_item * items,
         qsa_layer_cache cache0, int n_past0, const void * q, int q_type, const int * sel_ws, const int * nsel_ws,
-        int tiles_per_cta, int max_chunks, float * part_o, float * part_ml, float * out, uint32_t * status,
+        int tiles_per_cta, int max_chunks, float * part_o, float * part_ml, OutSpec outs, uint32_t * status,
         float * state_out);
 cudaError_t attn_set_attrs();
 // Cells per attention tile.
@@ -72,7 +72,7 @@ bool prefill_kv_supported(const DevDesc & d, int T);
 size_t prefill_kv_workspace(const DevDesc & d, int T, int n_blocks);
 cudaError_t launch_prefill_attn_kv(const DevDesc & d, cudaStream_t st, qsa_layer_cache cache, int n_past0, int T,
                                    const void * q, int q_type, const int * sel, const int * nsel, int n_blocks,
-                                   unsigned char * ws, float * out, uint32_t * status);
+                                   unsigned char * ws, OutSpec outs, uint32_t * status);
 
 // The prefill-sized projections on tcgen05 (qsa_proj_gemm.cu).  Front: xb [T][n_embd] 16-bit
 // activations, w[5] the 16-bit weights (attn_q, attn_k, attn_v, indexer.q_proj, indexer.k_proj),

@@ -460,7 +460,7 @@ __global__ void __launch_bounds__(PA_THREADS, 1) prefill_attn_kv_kernel(
 // coalesced.
 __global__ void prefill_merge_kernel(DevDesc d, int T, int slots, const int * __restrict__ nsel,
         const int * __restrict__ entry_of, const __half * __restrict__ part_o, const float * __restrict__ part_ml,
-        float * __restrict__ out) {
+        OutSpec outs) {
     extern __shared__ float pm_smem[];                       // [n_head][kb] weights, [n_head][kb] rows
     const int t = blockIdx.x, h = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n = max(0, min(nsel[t], d.kb));
@@ -515,9 +515,9 @@ __global__ void prefill_merge_kernel(DevDesc d, int T, int slots, const int * __
     }
     for (; j < n; j++) add(load(j), w[j]);
     const float inv = Wl > 0.0f ? 1.0f / Wl : 0.0f;
-    float4 * dst = reinterpret_cast<float4 *>(out + ((size_t) t * d.n_head + h) * HEAD_DIM) + lane * 2;
-    dst[0] = make_float4(acc[0] * inv, acc[1] * inv, acc[2] * inv, acc[3] * inv);
-    dst[1] = make_float4(acc[4] * inv, acc[5] * inv, acc[6] * inv, acc[7] * inv);
+    const size_t off = ((size_t) t * d.n_head + h) * HEAD_DIM + lane * 8;
+    out_store4(outs, off, make_float4(acc[0] * inv, acc[1] * inv, acc[2] * inv, acc[3] * inv));
+    out_store4(outs, off + 4, make_float4(acc[4] * inv, acc[5] * inv, acc[6] * inv, acc[7] * inv));
 }
 
 bool prefill_kv_supported(const DevDesc & d, int T) {
@@ -597,7 +597,7 @@ size_t prefill_kv_workspace(const DevDesc & d, int T, int n_blocks) { return pre
 
 cudaError_t launch_prefill_attn_kv(const DevDesc & d, cudaStream_t st, qsa_layer_cache cache, int n_past0, int T,
                                    const void * q, int q_type, const int * sel, const int * nsel, int n_blocks,
-                                   unsigned char * ws, float * out, uint32_t * status) {
+                                   unsigned char * ws, OutSpec outs, uint32_t * status) {
     static std::atomic<uint64_t> attr{0};
     cudaError_t e = once_per_device(attr, [] {
         return cudaFuncSetAttribute(prefill_attn_kv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PA_SMEM);
@@ -637,7 +637,7 @@ cudaError_t launch_prefill_attn_kv(const DevDesc & d, cudaStream_t st, qsa_layer
         if (e != cudaSuccess) return e;
     }
     prefill_merge_kernel<<<(unsigned) T, 32 * d.n_head, merge_smem, st>>>(d, T, (int) slots, nsel, entry_of, part_o,
-                                                                          part_ml, out);
+                                                                          part_ml, outs);
     return cudaGetLastError();
 }
 

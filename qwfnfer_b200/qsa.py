@@ -140,6 +140,43 @@ class QsaNode:
                                ws.data_ptr(), ws.numel(), _stream(stream)), "qsa_decode")
         return out
 
+    def sparse_attn_decode_gated(self, items: torch.Tensor, batch: int, max_n_kv: int, q: torch.Tensor,
+                                 q_idx: torch.Tensor, gate: torch.Tensor, k_new=None, v_new=None, kidx_new=None,
+                                 z_dtype=torch.bfloat16, out: torch.Tensor | None = None,
+                                 sel_out: torch.Tensor | None = None, ws: torch.Tensor | None = None,
+                                 stream=None) -> torch.Tensor:
+        """qsa_decode_gated: the decode with the output gate applied in the attention's final store;
+        returns z = out * sigmoid(gate) [batch][n_head*head_dim] in z_dtype (bf16 or f32); `out`
+        (optional) also receives the ungated f32 output."""
+        d = self.desc
+        z = torch.empty((batch, d.n_head * d.head_dim), dtype=z_dtype, device=self.device)
+        q_type = TYPE_BF16 if q.dtype == torch.bfloat16 else TYPE_F32
+        if ws is None:
+            ws = self.workspace("decode", batch, max_n_kv, stream)
+        check(lib().qsa_decode_gated(ctypes.byref(d), _ptr(items), batch, max_n_kv, _ptr(q), q_type, _ptr(q_idx),
+                                     _ptr(k_new), _ptr(v_new), _ptr(kidx_new), _ptr(gate), _ptr(z), _z_type(z_dtype),
+                                     _ptr(out), _ptr(sel_out), ws.data_ptr(), ws.numel(), _stream(stream)),
+              "qsa_decode_gated")
+        return z
+
+    def sparse_attn_gated(self, cache: QsaLayerCache, n_past: int, q: torch.Tensor, q_idx: torch.Tensor,
+                          gate: torch.Tensor, k_new=None, v_new=None, kidx_new=None, z_dtype=torch.bfloat16,
+                          out: torch.Tensor | None = None, sel_out: torch.Tensor | None = None,
+                          ws: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+        """qsa_prefill_gated: a prefill chunk with the output gate applied in the final store (see
+        sparse_attn_decode_gated)."""
+        d = self.desc
+        T = q.shape[0]
+        z = torch.empty((T, d.n_head * d.head_dim), dtype=z_dtype, device=self.device)
+        q_type = TYPE_BF16 if q.dtype == torch.bfloat16 else TYPE_F32
+        if ws is None:
+            ws = self.workspace("prefill", T, n_past + T, stream)
+        check(lib().qsa_prefill_gated(ctypes.byref(d), ctypes.byref(cache), n_past, T, _ptr(q), q_type, _ptr(q_idx),
+                                      _ptr(k_new), _ptr(v_new), _ptr(kidx_new), _ptr(gate), _ptr(z), _z_type(z_dtype),
+                                      _ptr(out), _ptr(sel_out), ws.data_ptr(), ws.numel(), _stream(stream)),
+              "qsa_prefill_gated")
+        return z
+
     def sparse_attn(self, cache: QsaLayerCache, n_past: int, q: torch.Tensor, q_idx: torch.Tensor,
                     k_new=None, v_new=None, kidx_new=None, out: torch.Tensor | None = None,
                     sel_out: torch.Tensor | None = None, ws: torch.Tensor | None = None, stream=None) -> torch.Tensor:
@@ -163,6 +200,14 @@ class QsaNode:
                     sel_out: bool = False) -> "QsaDecodeStep":
         """A captured decode step of these caches (one token per cache, at most max_n_kv cells)."""
         return QsaDecodeStep(self, caches, max_n_kv, q_dtype, sel_out)
+
+
+def _z_type(dtype) -> int:
+    if dtype == torch.bfloat16:
+        return TYPE_BF16
+    if dtype == torch.float32:
+        return TYPE_F32
+    raise QsaError(_abi.QSA_ERR_INVALID, "gated output: bfloat16 or float32")
 
 
 class QsaDecodeStep:
@@ -348,4 +393,16 @@ class QsaOutput:
         check(lib().qsa_output(ctypes.byref(self.desc), _ptr(self.wo), self.n_embd, self.w_type, T, _ptr(attn), _ptr(gate),
                                _ptr(out), None if ws is None else ws.data_ptr(), 0 if ws is None else ws.numel(),
                                _stream(stream)), "qsa_output")
+        return out
+
+    def project_z(self, z: torch.Tensor, out: torch.Tensor | None = None, stream=None):
+        """qsa_output_z: y = attn_output.weight z for a gated product z [T][n_head*head_dim] (bf16 with
+        bf16 weights, or f32) written by the gated decode / prefill -> y f32 [T][n_embd]."""
+        T = z.shape[0]
+        if out is None:
+            out = torch.empty((T, self.n_embd), dtype=torch.float32, device=self.wo.device)
+        ws = self.workspace(T, stream)
+        check(lib().qsa_output_z(ctypes.byref(self.desc), _ptr(self.wo), self.n_embd, self.w_type, T, _ptr(z),
+                                 _z_type(z.dtype), _ptr(out), None if ws is None else ws.data_ptr(),
+                                 0 if ws is None else ws.numel(), _stream(stream)), "qsa_output_z")
         return out
