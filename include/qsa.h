@@ -91,7 +91,18 @@ typedef struct qsa_desc {
     float   rms_eps;         /* rms_eps                                                           */
     float   rope_freq_base;  /* rope_freq_base                                                    */
     const float * k_norm_w;  /* device [idx_dim], indexer.k_norm.weight; NULL means all ones      */
+    uint32_t placement;      /* where the caches live (state_config's kv_host / idx_host,
+                                src/qwfn_state.h:31-36): 0 = device memory, or QSA_KV_HOST and/or
+                                QSA_IDX_HOST: pinned host memory mapped into the device's address
+                                space (device-accessible at its host address), read and written by
+                                the device over the bus.  The pooled keys stay in device memory.    */
 } qsa_desc;
+
+/* qsa_desc.placement bits. */
+enum {
+    QSA_KV_HOST  = 1u << 0,  /* K and V caches in pinned host memory */
+    QSA_IDX_HOST = 1u << 1   /* raw indexer-key cache in pinned host memory */
+};
 
 /* One layer's caches of one sequence (device pointers, reference layouts above). */
 typedef struct qsa_layer_cache {
@@ -368,6 +379,40 @@ qsa_status qsa_output(const qsa_desc * d, const void * wo, int32_t n_embd, int32
  * Workspace, alignment and paths as qsa_output (src/qwfn_graph.cpp:545; prefill :406-407). */
 qsa_status qsa_output_z(const qsa_desc * d, const void * wo, int32_t n_embd, int32_t w_type, int32_t T,
                         const void * z, int32_t z_type, float * y, void * ws, size_t ws_bytes, qsa_stream_t stream);
+
+/* ------------------------------------------------------------------ descriptors from GGUF metadata */
+/* The node's hyper-parameters of a GGUF file, read as model_index::read_metadata reads them
+ * (src/qwfn_model.cpp:111-152): keys under "<arch>." with the same defaults; integer keys of any
+ * integer type, f32 keys only as F32, arrays of 32/64-bit integers.  Only "qwen4exp" files are
+ * accepted (QSA_ERR_UNSUPPORTED otherwise), as the reference loader does. */
+#define QSA_GGUF_MAX_LAYERS 256
+typedef struct qsa_gguf_hparams {
+    char    arch[64];
+    int32_t n_layer, n_embd, n_ctx_train;
+    int32_t n_head, n_head_kv, head_dim;
+    float   rms_eps;
+    int32_t full_attention_interval;
+    int32_t n_compress;                               /* entries of attention.compress_ratios */
+    int32_t compress_ratios[QSA_GGUF_MAX_LAYERS];     /* per layer; 0 = a dense attention layer */
+    float   rope_freq_base;
+    int32_t rope_dim;
+    int32_t sections[4];
+    int32_t idx_n_head, idx_dim, idx_top_k;
+} qsa_gguf_hparams;
+
+/* Read the metadata of the GGUF file at `path` (host path; tensor data is not read).  err (host,
+ * err_len bytes, optional) receives a message on failure. */
+qsa_status qsa_gguf_read_hparams(const char * path, qsa_gguf_hparams * hp, char * err, size_t err_len);
+/* 1 when layer il runs the node: an attention layer ((il + 1) % full_attention_interval == 0,
+ * hparams::is_attn_layer) with compress_ratios[il] > 0; 0 otherwise. */
+int32_t qsa_gguf_is_qsa_layer(const qsa_gguf_hparams * hp, int32_t il);
+/* The descriptor of sparse-attention layer il for a cache of n_ctx cells (rounded up to whole
+ * blocks): ratio compress_ratios[il], top_k_blocks = ceil((idx_top_k + r - 1) / r) - 1 with the
+ * window rule given (0 = the reference's: its incomplete block forced, engine::init,
+ * src/qwfn_engine.cpp:384-431).  Returns qsa_desc_check's verdict on it (the descriptor is filled
+ * in either way); QSA_ERR_INVALID when il is not such a layer. */
+qsa_status qsa_gguf_layer_desc(const qsa_gguf_hparams * hp, int32_t il, int32_t n_ctx, int32_t window,
+                               int32_t type_k, int32_t type_v, const float * k_norm_w, qsa_desc * out);
 
 /* ------------------------------------------------------------------ staging */
 /* Copy `bytes` (a multiple of 16, both addresses 16-byte aligned) from src to dst with a kernel on

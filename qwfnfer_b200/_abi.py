@@ -20,6 +20,7 @@ STATUS_NAMES = {
 }
 
 TYPE_F32, TYPE_F16, TYPE_Q8_0, TYPE_BF16 = 0, 1, 8, 30
+KV_HOST, IDX_HOST = 1, 2          # qsa_desc.placement bits
 
 
 class QsaDesc(ctypes.Structure):
@@ -30,7 +31,7 @@ class QsaDesc(ctypes.Structure):
         ("top_k_blocks", ctypes.c_int32), ("window", ctypes.c_int32), ("n_ctx", ctypes.c_int32),
         ("type_k", ctypes.c_int32), ("type_v", ctypes.c_int32), ("rope_dim", ctypes.c_int32),
         ("sections", ctypes.c_int32 * 4), ("rms_eps", ctypes.c_float),
-        ("rope_freq_base", ctypes.c_float), ("k_norm_w", ctypes.c_void_p),
+        ("rope_freq_base", ctypes.c_float), ("k_norm_w", ctypes.c_void_p), ("placement", ctypes.c_uint32),
     ]
 
     def copy(self) -> "QsaDesc":
@@ -59,10 +60,25 @@ class QsaFrontWeights(ctypes.Structure):
                 ("n_embd", ctypes.c_int32), ("w_type", ctypes.c_int32)]
 
 
+GGUF_MAX_LAYERS = 256
+
+
+class QsaGgufHparams(ctypes.Structure):
+    """struct qsa_gguf_hparams (include/qsa.h)."""
+    _fields_ = [
+        ("arch", ctypes.c_char * 64), ("n_layer", ctypes.c_int32), ("n_embd", ctypes.c_int32),
+        ("n_ctx_train", ctypes.c_int32), ("n_head", ctypes.c_int32), ("n_head_kv", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32), ("rms_eps", ctypes.c_float), ("full_attention_interval", ctypes.c_int32),
+        ("n_compress", ctypes.c_int32), ("compress_ratios", ctypes.c_int32 * GGUF_MAX_LAYERS),
+        ("rope_freq_base", ctypes.c_float), ("rope_dim", ctypes.c_int32), ("sections", ctypes.c_int32 * 4),
+        ("idx_n_head", ctypes.c_int32), ("idx_dim", ctypes.c_int32), ("idx_top_k", ctypes.c_int32),
+    ]
+
+
 def make_desc(n_head=16, n_head_kv=2, head_dim=256, idx_n_head=1, idx_dim=128, ratio=64,
               top_k_blocks=64, window=128, n_ctx=4096, type_k=TYPE_Q8_0, type_v=TYPE_Q8_0,
               rope_dim=64, sections=(11, 11, 10, 0), rms_eps=1e-6, rope_freq_base=1e7,
-              k_norm_w=None) -> QsaDesc:
+              k_norm_w=None, kv_host=False, idx_host=False) -> QsaDesc:
     d = QsaDesc()
     d.n_head, d.n_head_kv, d.head_dim = n_head, n_head_kv, head_dim
     d.idx_n_head, d.idx_dim, d.ratio = idx_n_head, idx_dim, ratio
@@ -72,6 +88,7 @@ def make_desc(n_head=16, n_head_kv=2, head_dim=256, idx_n_head=1, idx_dim=128, r
         d.sections[i] = sections[i]
     d.rms_eps, d.rope_freq_base = rms_eps, rope_freq_base
     d.k_norm_w = k_norm_w
+    d.placement = (KV_HOST if kv_host else 0) | (IDX_HOST if idx_host else 0)
     return d
 
 
@@ -150,6 +167,9 @@ def lib() -> ctypes.CDLL:
         "qsa_output_workspace_size": (SZ, [D, I32, I32, I32]),
         "qsa_output": (I32, [D, VP, I32, I32, I32, VP, VP, VP, VP, SZ, VP]),
         "qsa_version": (I32, []),
+        "qsa_gguf_read_hparams": (I32, [ctypes.c_char_p, P(QsaGgufHparams), ctypes.c_char_p, SZ]),
+        "qsa_gguf_is_qsa_layer": (I32, [P(QsaGgufHparams), I32]),
+        "qsa_gguf_layer_desc": (I32, [P(QsaGgufHparams), I32, I32, I32, I32, I32, VP, D]),
     }
     for name, (res, args) in sigs.items():
         fn = getattr(L, name)
@@ -174,6 +194,7 @@ HEADER_SYMBOLS = [
     "qsa_ipc_handle", "qsa_ipc_open", "qsa_ipc_close", "qsa_peer_buffer_bytes", "qsa_peer_push", "qsa_peer_wait",
     "qsa_prefill_workspace_size", "qsa_prefill", "qsa_front_workspace_size", "qsa_front", "qsa_output_workspace_size", "qsa_output",
     "qsa_decode_gated", "qsa_prefill_gated", "qsa_output_z",
+    "qsa_gguf_read_hparams", "qsa_gguf_is_qsa_layer", "qsa_gguf_layer_desc",
     "qsa_stage_copy",
     "qsa_check", "qsa_version",
 ]

@@ -17,7 +17,7 @@ import sys
 PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
-SOURCES = ["qsa_api.cu", "qsa_append.cu", "qsa_select.cu", "qsa_attn.cu", "qsa_shard.cu", "qsa_prefill_tc.cu", "qsa_prefill_attn.cu", "qsa_peer.cu", "qsa_static_ws.cu", "qsa_stage.cu", "qsa_front.cu", "qsa_proj_gemm.cu"]
+SOURCES = ["qsa_api.cu", "qsa_append.cu", "qsa_select.cu", "qsa_attn.cu", "qsa_shard.cu", "qsa_prefill_tc.cu", "qsa_prefill_attn.cu", "qsa_peer.cu", "qsa_static_ws.cu", "qsa_stage.cu", "qsa_front.cu", "qsa_proj_gemm.cu", "qsa_gguf.cpp"]
 OUT = os.path.join(PKG, "libqsa.so")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -43,7 +43,7 @@ def build_lib(verbose: bool = False) -> str:
     if verbose:
         flags += ["-Xptxas", "-v"]
     for src in SOURCES:
-        obj = os.path.join(bdir, src.replace(".cu", ".o"))
+        obj = os.path.join(bdir, os.path.splitext(src)[0] + ".o")
         objs.append(obj)
         path = os.path.join(CSRC, src)
         deps = [path] + [os.path.join(CSRC, h) for h in os.listdir(CSRC) if h.endswith(".cuh")] + \

@@ -39,6 +39,7 @@ DevDesc make_dev(const qsa_desc * d) {
     x.hb_v = (int) kv_row_bytes(d->type_v, d->head_dim);
     x.shard_blk0 = 0;
     x.shard_blk1 = INT_MAX;
+    x.kv_host = (d->placement & QSA_KV_HOST) ? 1 : 0;
     return x;
 }
 
@@ -189,6 +190,7 @@ qsa_status qsa_desc_check(const qsa_desc * d) {
     if (d->idx_dim != MAX_IDX_DIM || d->idx_n_head > 4 || d->rope_dim % 8 != 0) return QSA_ERR_UNSUPPORTED;
     if (d->type_k != d->type_v) return QSA_ERR_UNSUPPORTED;
     if (d->top_k_blocks + n_force_of(d) > MAX_KB) return QSA_ERR_UNSUPPORTED;
+    if (d->placement & ~(uint32_t) (QSA_KV_HOST | QSA_IDX_HOST)) return QSA_ERR_INVALID;
     if (d->ratio > 256) return QSA_ERR_UNSUPPORTED;        // a block of raw keys is staged in shared memory
     return QSA_OK;
 }
@@ -427,7 +429,7 @@ qsa_status prefill_impl(const qsa_desc * dd, const qsa_layer_cache * cache, int3
     const DevDesc d = make_dev(dd);
     const WsLayout w = ws_layout(d, T, n_past + T);
     // the block-grouped path reads the caches with TMA, which wants 16-byte aligned rows
-    const bool kv_path = prefill_kv_path(d, T) && reinterpret_cast<uintptr_t>(cache->k) % 16 == 0 &&
+    const bool kv_path = prefill_kv_path(d, T) && !d.kv_host && reinterpret_cast<uintptr_t>(cache->k) % 16 == 0 &&
                          reinterpret_cast<uintptr_t>(cache->v) % 16 == 0;
     const size_t need = kv_path ? w.total + prefill_kv_workspace(d, T, prefill_n_blocks(d, n_past + T)) : w.total;
     if (!ws || ws_bytes < need) return QSA_ERR_WORKSPACE;

@@ -295,6 +295,35 @@ __global__ void __launch_bounds__(ATT_THREADS, AttnCfg<KV_TYPE>::MIN_CTAS) attn_
             // r a multiple of the tile: the whole tile lies in block j_lo (no per-lane division)
             const int cell = (r % ATT_CELLS == 0) ? sel[j_lo] * r + (e_lo - j_lo * r) + lane : list_cell(sel, r, ea);
             const unsigned vm = __ballot_sync(0xffffffffu, ea < n_cells && cell <= qpos);
+            if (d.kv_host) {
+                // K and V in pinned host memory: the warp copies each run's rows with ordinary 16-byte
+                // loads (bulk copies are not used on host memory), then one release arrive completes
+                // the stage
+                for (int j = j_lo; j <= j_hi; j++) {
+                    const int a = max(e_lo, j * r), b = min(e_hi, (j + 1) * r);
+                    const int cs = sel[j] * r + (a - j * r);
+                    const int nv = max(0, min(b - a, qpos - cs + 1));
+                    const int n16 = nv * RBr / 16;
+                    const uint4 * sk = reinterpret_cast<const uint4 *>(kbase + (size_t) cs * d.rb_k);
+                    const uint4 * sv = reinterpret_cast<const uint4 *>(vbase + (size_t) cs * d.rb_v);
+                    uint4 * dk = reinterpret_cast<uint4 *>(stage_k(s) + (a - e_lo) * RBr);
+                    uint4 * dv = reinterpret_cast<uint4 *>(stage_v(s) + (a - e_lo) * RBr);
+                    for (int w = lane; w < n16; w += 64) {
+                        const bool two = w + 32 < n16;
+                        const uint4 k0 = sk[w], v0 = sv[w];
+                        uint4 k1 = make_uint4(0u, 0u, 0u, 0u), v1 = k1;
+                        if (two) { k1 = sk[w + 32]; v1 = sv[w + 32]; }
+                        dk[w] = k0; dv[w] = v0;
+                        if (two) { dk[w + 32] = k1; dv[w + 32] = v1; }
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) {
+                    vmask[s] = vm;
+                    mbar_arrive(&full_bar[s]);
+                }
+                continue;
+            }
             if (lane == 0) {
                 vmask[s] = vm;
                 mbar_arrive_expect_tx(&full_bar[s], bytes);

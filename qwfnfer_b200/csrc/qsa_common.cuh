@@ -40,6 +40,9 @@ struct DevDesc {
     // Replicated indexer caches: with shard_ri set only K and V are local to the shard; the raw
     // keys and pooled keys of every block are held (global rows) and every rank selects globally.
     int shard_ri;
+    // K and V in pinned host memory (qsa_desc.placement & QSA_KV_HOST): read with ordinary loads,
+    // never by bulk or tensor copies.
+    int kv_host;
 };
 
 // Local address of global row `row` of a sharded cache array with `row_bytes` per row; rows

@@ -42,7 +42,9 @@ class QsaState:
 
     blocks=(lo, hi): a shard's caches, holding blocks [lo, hi) only (row 0 = cell lo*ratio);
     with index_full the raw-key and pooled-key caches still cover every block (the sharded decode
-    with replicated indexer caches)."""
+    with replicated indexer caches).  The descriptor's placement puts K/V (KV_HOST) and/or the raw
+    indexer keys (IDX_HOST) in pinned host memory, as state_config's kv_host / idx_host do
+    (src/qwfn_state.h:31-36); the pooled keys stay on the device."""
 
     def __init__(self, desc: QsaDesc, n_layers: int = 1, device: str | torch.device = "cuda", zero: bool = False,
                  blocks: tuple[int, int] | None = None, index_full: bool = False):
@@ -52,10 +54,16 @@ class QsaState:
         self.blocks = blocks if blocks is not None else (0, desc.n_ctx // desc.ratio)
         n = (self.blocks[1] - self.blocks[0]) * desc.ratio
         ni = desc.n_ctx if index_full else n
-        alloc = torch.zeros if zero else torch.empty
-        self.k = [alloc((n, row_bytes(desc, 0)), dtype=torch.uint8, device=self.device) for _ in range(n_layers)]
-        self.v = [alloc((n, row_bytes(desc, 1)), dtype=torch.uint8, device=self.device) for _ in range(n_layers)]
-        self.idx = [alloc((ni, desc.idx_dim), dtype=torch.int16, device=self.device) for _ in range(n_layers)]
+        def alloc(shape, dtype, host):
+            if host:                       # pinned, mapped into the device's address space (UVA)
+                t = torch.empty(shape, dtype=dtype, pin_memory=True)
+                return t.zero_() if zero else t
+            return (torch.zeros if zero else torch.empty)(shape, dtype=dtype, device=self.device)
+
+        kv_host, idx_host = bool(desc.placement & _abi.KV_HOST), bool(desc.placement & _abi.IDX_HOST)
+        self.k = [alloc((n, row_bytes(desc, 0)), torch.uint8, kv_host) for _ in range(n_layers)]
+        self.v = [alloc((n, row_bytes(desc, 1)), torch.uint8, kv_host) for _ in range(n_layers)]
+        self.idx = [alloc((ni, desc.idx_dim), torch.int16, idx_host) for _ in range(n_layers)]
         self.pool = [torch.zeros((ni // desc.ratio, desc.idx_dim), dtype=torch.int16, device=self.device)
                      for _ in range(n_layers)]
 

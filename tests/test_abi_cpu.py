@@ -67,7 +67,8 @@ def test_struct_layouts_match_header():
     assert ctypes.sizeof(_abi.QsaLayerCache) == 32
     assert ctypes.sizeof(_abi.QsaDecodeItem) == 48
     assert _abi.QsaDecodeItem.n_past.offset == 32
-    assert ctypes.sizeof(_abi.QsaDesc) == 4 * 12 + 16 + 8 + 8
+    assert ctypes.sizeof(_abi.QsaDesc) == 4 * 12 + 16 + 8 + 8 + 8      # + placement (and tail padding)
+    assert _abi.QsaDesc.placement.offset == 80
 
 
 def test_front_weights_layout():

@@ -83,3 +83,62 @@ def test_checkpoint_shape_is_refused_cleanly(tmp_path):
     with pytest.raises(QsaError) as e:
         layer_desc(hp, 7, n_ctx=262144)
     assert e.value.status == QSA_ERR_UNSUPPORTED
+
+
+def test_c_reader_typed_getters(tmp_path):
+    """The library's C reader follows the reference loader's getters: integer keys of any integer
+    width, f32 keys only when stored as F32 (an F64 value falls back to the default), integer
+    arrays of 64-bit elements, a partial sections array completed from the defaults."""
+    from gguf import GGUFValueType, GGUFWriter
+
+    p = tmp_path / "typed.gguf"
+    w = GGUFWriter(str(p), "qwen4exp")
+    A = "qwen4exp."
+    w.add_uint64(A + "block_count", 4)
+    w.add_uint16(A + "attention.head_count", 16)
+    w.add_int32(A + "attention.head_count_kv", 2)
+    w.add_uint32(A + "attention.key_length", 256)
+    w.add_uint32(A + "embedding_length", 2560)
+    w.add_float64(A + "attention.layer_norm_rms_epsilon", 1e-5)      # not F32: the default 1e-6 holds
+    w.add_array(A + "attention.compress_ratios", [0, 0, 0, 64])
+    w.add_key_value(A + "rope.dimension_sections", [12, 12], GGUFValueType.ARRAY, sub_type=GGUFValueType.INT64)
+    w.add_uint8(A + "attention.indexer.head_count", 1)
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    hp = read_hparams(str(p))
+    assert (hp["n_layer"], hp["n_head"], hp["n_head_kv"], hp["idx_n_head"]) == (4, 16, 2, 1)
+    assert abs(hp["rms_eps"] - 1e-6) < 1e-12
+    assert hp["compress_ratios"] == [0, 0, 0, 64]
+    assert hp["sections"] == [12, 12, 10, 0]
+    assert qsa_layers(hp) == [3]
+
+
+def test_c_reader_refusals(tmp_path):
+    """Another architecture is refused as the reference loader refuses it; a file that is not GGUF
+    or is cut short is reported, not read past its end."""
+    from gguf import GGUFWriter
+
+    p = tmp_path / "other.gguf"
+    w = GGUFWriter(str(p), "llama")
+    w.add_uint32("llama.block_count", 2)
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    with pytest.raises(QsaError) as e:
+        read_hparams(str(p))
+    assert e.value.status == QSA_ERR_UNSUPPORTED and "architecture" in str(e.value)
+    junk = tmp_path / "junk.gguf"
+    junk.write_bytes(b"not a gguf file at all")
+    with pytest.raises(QsaError):
+        read_hparams(str(junk))
+    good = tmp_path / "standin.gguf"
+    write_gguf(good, STANDIN)
+    cut = tmp_path / "cut.gguf"
+    cut.write_bytes(good.read_bytes()[:100])
+    with pytest.raises(QsaError):
+        read_hparams(str(cut))
+    with pytest.raises(QsaError):
+        read_hparams(str(tmp_path / "missing.gguf"))
