@@ -265,6 +265,27 @@ qsa_status qsa_shard_attend(const qsa_desc * d, const qsa_decode_item * items, i
 qsa_status qsa_merge_states(const qsa_desc * d, int32_t n_parts, int32_t batch, const float * states, float * out,
                             qsa_stream_t stream);
 
+/* The whole sharded step on one rank, the two exchanges done with the caller's NCCL communicator
+ * (the ncclComm_t of the ranks holding the shards; shard order = rank order in it, n_ranks its size):
+ *   index_replicated 0: qsa_shard_candidates -> ncclAllGather -> qsa_shard_attend
+ *   index_replicated 1: qsa_shard_decode_ri (indexer caches replicated on every rank)
+ * then ncclAllGather of the states and qsa_merge_states into out (f32 [batch][n_head][head_dim],
+ * identical on every rank; sel_out optional).  All work is stream-ordered on `stream`.  NCCL is
+ * not linked by the library: the entry points come from the libnccl.so.2 already loaded in the
+ * process (QSA_ERR_UNSUPPORTED if none is).  The workspace (qsa_decode_sharded_workspace_size,
+ * zeroed once) holds the shard calls' workspace and the gathered candidates and states.
+ * Replaces graph_builder::sparse_attn_decode (src/qwfn_graph.cpp:450-541) for a sequence whose
+ * cells are split over ranks; the exchange itself has no counterpart in the reference. */
+typedef struct ncclComm * qsa_nccl_comm_t;      /* ncclComm_t */
+size_t qsa_decode_sharded_workspace_size(const qsa_desc * d, int32_t batch, int32_t max_n_kv,
+                                         int32_t blk_lo, int32_t blk_hi, int32_t n_ranks);
+qsa_status qsa_decode_sharded(const qsa_desc * d, const qsa_decode_item * items, int32_t batch, int32_t max_n_kv,
+                              int32_t blk_lo, int32_t blk_hi, int32_t index_replicated,
+                              qsa_nccl_comm_t comm, int32_t n_ranks,
+                              const void * q, int32_t q_type, const float * q_idx,
+                              const float * k_new, const float * v_new, const float * kidx_new,
+                              float * out, int32_t * sel_out, void * ws, size_t ws_bytes, qsa_stream_t stream);
+
 /* ------------------------------------------------------------------ all-gather over peer memory
  * The two exchanges of the sharded decode without a collective library: every rank owns a gather
  * buffer of qsa_peer_buffer_bytes(n_ranks, slot_bytes) bytes ([n_ranks][slot_bytes] + flags,

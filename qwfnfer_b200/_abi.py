@@ -152,6 +152,8 @@ def lib() -> ctypes.CDLL:
         "qsa_shard_candidates": (I32, [D, VP, I32, I32, I32, I32, VP, VP, VP, VP, VP, VP, SZ, VP]),
         "qsa_shard_attend": (I32, [D, VP, I32, I32, I32, I32, I32, VP, I32, VP, I32, VP, VP, VP, SZ, VP]),
         "qsa_merge_states": (I32, [D, I32, I32, VP, VP, VP]),
+        "qsa_decode_sharded_workspace_size": (SZ, [D, I32, I32, I32, I32, I32]),
+        "qsa_decode_sharded": (I32, [D, VP, I32, I32, I32, I32, I32, VP, I32, VP, I32, VP, VP, VP, VP, VP, VP, VP, SZ, VP]),
         "qsa_ipc_handle": (I32, [VP, VP, P(SZ)]),
         "qsa_ipc_open": (I32, [VP, P(VP)]),
         "qsa_ipc_close": (I32, [VP]),
@@ -190,7 +192,7 @@ HEADER_SYMBOLS = [
     "qsa_decode", "qsa_decode_append", "qsa_decode_select", "qsa_decode_attend", "qsa_decode_noalloc",
     "qsa_shard_state_floats", "qsa_shard_workspace_size", "qsa_shard_append", "qsa_shard_candidates", "qsa_shard_attend",
     "qsa_shard_append_ri", "qsa_shard_decode_ri",
-    "qsa_merge_states",
+    "qsa_merge_states", "qsa_decode_sharded_workspace_size", "qsa_decode_sharded",
     "qsa_ipc_handle", "qsa_ipc_open", "qsa_ipc_close", "qsa_peer_buffer_bytes", "qsa_peer_push", "qsa_peer_wait",
     "qsa_prefill_workspace_size", "qsa_prefill", "qsa_front_workspace_size", "qsa_front", "qsa_output_workspace_size", "qsa_output",
     "qsa_decode_gated", "qsa_prefill_gated", "qsa_output_z",

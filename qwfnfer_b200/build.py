@@ -17,7 +17,7 @@ import sys
 PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
-SOURCES = ["qsa_api.cu", "qsa_append.cu", "qsa_select.cu", "qsa_attn.cu", "qsa_shard.cu", "qsa_prefill_tc.cu", "qsa_prefill_attn.cu", "qsa_peer.cu", "qsa_static_ws.cu", "qsa_stage.cu", "qsa_front.cu", "qsa_proj_gemm.cu", "qsa_gguf.cpp"]
+SOURCES = ["qsa_api.cu", "qsa_append.cu", "qsa_select.cu", "qsa_attn.cu", "qsa_shard.cu", "qsa_prefill_tc.cu", "qsa_prefill_attn.cu", "qsa_peer.cu", "qsa_static_ws.cu", "qsa_stage.cu", "qsa_front.cu", "qsa_proj_gemm.cu", "qsa_gguf.cpp", "qsa_shard_nccl.cu"]
 OUT = os.path.join(PKG, "libqsa.so")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -56,7 +56,7 @@ def build_lib(verbose: bool = False) -> str:
             sys.stderr.write(r.stdout + r.stderr)
         if r.returncode != 0:
             raise RuntimeError(f"nvcc failed on {src}")
-    cmd = [nvcc(), "-shared", "-o", OUT] + objs + ARCH + ["-ccbin", host_cxx(), "-cudart", "static"]
+    cmd = [nvcc(), "-shared", "-o", OUT] + objs + ARCH + ["-ccbin", host_cxx(), "-cudart", "static", "-ldl"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         sys.stderr.write(r.stdout + r.stderr)

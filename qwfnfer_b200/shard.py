@@ -27,7 +27,7 @@ import ctypes
 import torch
 import torch.distributed as dist
 
-from ._abi import QsaDesc, QsaLayerCache, TYPE_BF16, TYPE_F32, check, k_blocks, lib
+from ._abi import QsaDesc, QsaError, QsaLayerCache, TYPE_BF16, TYPE_F32, check, k_blocks, lib
 
 
 def shard_blocks(n_blocks: int, world: int, rank: int) -> tuple[int, int]:
@@ -225,8 +225,10 @@ class ShardedDecoder:
 
     def __init__(self, desc: QsaDesc, backend=None, group=None, rank: int | None = None,
                  world: int | None = None, exchange: str = "nccl", batch: int = 1, index: str = "sharded"):
-        """exchange: "nccl" (all-gathers of the process group) or "peer" (libqsa's all-gather over
-        NVLink peer memory, GPUs of one node; sized for `batch` queries per step).  index: "sharded"
+        """exchange: "nccl" (all-gathers of the process group), "nccl_capi" (the whole step in libqsa's
+        qsa_decode_sharded with the process group's NCCL communicator) or "peer" (libqsa's
+        all-gather over NVLink peer memory, GPUs of one node; sized for `batch` queries per step).
+        index: "sharded"
         (each rank holds its blocks' raw and pooled keys; candidates are exchanged) or "replicated"
         (every rank holds all of them, QsaState(index_full=True), and selects globally itself: one
         exchange per step)."""
@@ -243,6 +245,14 @@ class ShardedDecoder:
         self.kb = k_blocks(desc)
         self.peer = None
         self._steps = 0
+        self.comm = 0
+        if exchange == "nccl_capi":
+            pg = group if group is not None else dist.group.WORLD
+            dev = self.backend.device
+            dist.all_reduce(torch.zeros(1, device=dev), group=pg)        # the communicator exists after a collective
+            self.comm = pg._get_backend(dev)._comm_ptr()
+            if not self.comm:
+                raise QsaError(1, "no NCCL communicator behind the process group")
         if exchange == "peer" and self.world > 1:
             # Channels: 0 candidates, 1 and 2 states.  A push overwrites the peers' slots without
             # waiting for them to finish reading the last round, so consecutive pushes into one
@@ -285,6 +295,8 @@ class ShardedDecoder:
              sel_out: torch.Tensor | None = None) -> torch.Tensor:
         """One decode step of one layer for `batch` queries (items: this rank's device item table,
         global n_past, local caches).  Returns f32 [batch, n_head, head_dim] on every rank."""
+        if self.comm:
+            return self._step_capi(items, batch, max_n_kv, q, q_idx, k_new, v_new, kidx_new, sel_out)
         if self.index_replicated:
             state = self.backend.decode_ri(items, batch, max_n_kv, self.blocks, q, q_idx, k_new, v_new, kidx_new,
                                            sel_out=sel_out)
@@ -298,3 +310,36 @@ class ShardedDecoder:
                                     n_shards=self.world, cand_stride=cstride)
         states, _ = self._all_gather(state, 1)
         return self.backend.merge(states.view(self.world, batch, -1))
+
+    def _step_capi(self, items, batch, max_n_kv, q, q_idx, k_new, v_new, kidx_new, sel_out):
+        """The step as one qsa_decode_sharded call (its all-gathers on the NCCL communicator)."""
+        d = self.desc
+        L = lib()
+        size = L.qsa_decode_sharded_workspace_size(ctypes.byref(d), batch, max_n_kv, self.blocks[0], self.blocks[1],
+                                                    self.world)
+        if size == 0:
+            raise QsaError(1, "invalid sharded decode shape")
+        ws = self.backend._ws.get(("capi", size))
+        stream = torch.cuda.current_stream(self.backend.device).cuda_stream
+        if ws is None:
+            ws = torch.empty(size, dtype=torch.uint8, device=self.backend.device)
+            check(L.qsa_workspace_init(ws.data_ptr(), size, stream), "qsa_workspace_init")
+            self.backend._ws[("capi", size)] = ws
+        out = torch.empty((batch, d.n_head, d.head_dim), dtype=torch.float32, device=self.backend.device)
+        q_type = TYPE_BF16 if q.dtype == torch.bfloat16 else TYPE_F32
+        check(L.qsa_decode_sharded(ctypes.byref(d), _ptr(items), batch, max_n_kv, self.blocks[0], self.blocks[1],
+                                   1 if self.index_replicated else 0, self.comm, self.world, _ptr(q), q_type,
+                                   _ptr(q_idx), _ptr(k_new), _ptr(v_new), _ptr(kidx_new), out.data_ptr(), _ptr(sel_out),
+                                   ws.data_ptr(), ws.numel(), stream), "qsa_decode_sharded")
+        return out
+
+    def check(self, batch: int, max_n_kv: int) -> int:
+        """qsa_check of the workspace this decoder's steps used (synchronises the stream)."""
+        if self.comm:
+            size = lib().qsa_decode_sharded_workspace_size(ctypes.byref(self.desc), batch, max_n_kv, self.blocks[0],
+                                                          self.blocks[1], self.world)
+            ws = self.backend._ws.get(("capi", size))
+            if ws is None:
+                return 0
+            return lib().qsa_check(ws.data_ptr(), ws.numel(), torch.cuda.current_stream(self.backend.device).cuda_stream)
+        return self.backend.check(batch, max_n_kv, self.blocks)

@@ -86,7 +86,7 @@ def main() -> int:
     step_outs = [dec.step(items, B, max_n_kv, q, q_idx, k, v, ki, sel_out=sel).clone() for _ in range(3 if delay else 1)]
     out = step_outs[-1]
     steps_equal = all(torch.equal(o, out) for o in step_outs)
-    st_code = dec.backend.check(B, max_n_kv)
+    st_code = dec.check(B, max_n_kv)
     if dec.peer is not None and st_code == QSA_OK:
         st_code = dec.peer.check()
     status = torch.tensor([st_code], dtype=torch.int32, device=dev)

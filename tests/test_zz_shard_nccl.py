@@ -28,14 +28,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("exchange,index,delay", [("nccl", "sharded", ""), ("peer", "sharded", ""),
-                                                 ("peer", "replicated", ""), ("peer", "replicated", "delay"),
-                                                 ("peer", "sharded", "delay")])
-def test_sharded_decode_over_ranks(exchange, index, delay):
-    """`delay`: three steps back to back, the last rank's host sleeping between each peer push and
-    its wait (later rounds published before its wait launches)."""
-    n = min(4, torch.cuda.device_count())
+def _run(n, exchange, index, delay=""):
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes", "1",
            "--nproc-per-node", str(n), "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
            os.path.join(TESTS, "shard_nccl_worker.py"), exchange, index] + ([delay] if delay else [])
@@ -44,3 +37,24 @@ def test_sharded_decode_over_ranks(exchange, index, delay):
     assert r.returncode == 0 and lines, r.stdout[-3000:] + r.stderr[-3000:]
     res = json.loads(lines[-1][len("SHARD_NCCL "):])
     assert res["ok"] and res["world"] == n, res
+
+
+@pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU")
+@pytest.mark.parametrize("index", ["sharded", "replicated"])
+def test_sharded_decode_c_entry_one_rank(index):
+    """qsa_decode_sharded (the step with its NCCL all-gathers behind the C ABI) on a one-rank
+    communicator: the same selection as qsa_decode and the output within the parity tolerance."""
+    _run(1, "nccl_capi", index)
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("exchange,index,delay", [("nccl", "sharded", ""), ("peer", "sharded", ""),
+                                                 ("peer", "replicated", ""), ("peer", "replicated", "delay"),
+                                                 ("peer", "sharded", "delay"), ("nccl_capi", "sharded", ""),
+                                                 ("nccl_capi", "replicated", "")])
+def test_sharded_decode_over_ranks(exchange, index, delay):
+    """`delay`: three steps back to back, the last rank's host sleeping between each peer push and
+    its wait (later rounds published before its wait launches).  nccl_capi: qsa_decode_sharded with
+    the process group's communicator."""
+    n = min(4, torch.cuda.device_count())
+    _run(n, exchange, index, delay)
