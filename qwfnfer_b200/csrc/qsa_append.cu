@@ -73,18 +73,16 @@ __device__ void pool_block_warp(const DevDesc & d, const uint16_t * __restrict__
         x[e] = __fmul_rn(x[e], scale);
         if (d.k_norm_w) x[e] = __fmul_rn(x[e], d.k_norm_w[4 * lane + e]);
     }
-    // IMRoPE: pair i rotates dims (i, i + rope_dim/2), i < rope_dim/2.
+    // IMRoPE: pair i rotates dims (i, i + rope_dim/2), i < rope_dim/2.  Lane i evaluates pair i's
+    // angle (pairs 32.. by further rounds), and every dim of the pair takes it by shuffle.
     const int half = d.rope_dim / 2;
     float y[4] = {x[0], x[1], x[2], x[3]};
     const int sect_dims = d.sections[0] + d.sections[1] + d.sections[2] + d.sections[3];
     const float p = (float) (b * r);
-    #pragma unroll
-    for (int e = 0; e < 4; e++) {
-        const int dim = 4 * lane + e;
-        const bool first = dim < half, second = dim >= half && dim < d.rope_dim;
-        const int i = first ? dim : dim - half;                 // pair index
-        float partner = __shfl_sync(0xffffffffu, x[e], first ? lane + half / 4 : (lane - half / 4) & 31);
-        if (first || second) {
+    for (int i0 = 0; i0 < half; i0 += 32) {
+        const int i = i0 + lane;                                // this lane's pair
+        float c_i = 1.0f, s_i = 0.0f;
+        if (i < half) {
             float th = p;
             for (int k = 0; k < i; k++) th = __fmul_rn(th, d.theta_scale);
             const int sector = i % sect_dims;
@@ -101,9 +99,20 @@ __device__ void pool_block_warp(const DevDesc & d, const uint16_t * __restrict__
             rr = fma(-k, 2.4492935982947064e-16, rr);                       // 2 pi - high part
             double sd, cd;
             sincos(rr, &sd, &cd);
-            const float c = (float) cd, s = (float) sd;
-            if (first) y[e] = __fsub_rn(__fmul_rn(x[e], c), __fmul_rn(partner, s));     // x0*c - x1*s
-            else       y[e] = __fadd_rn(__fmul_rn(partner, s), __fmul_rn(x[e], c));     // x0*s + x1*c
+            c_i = (float) cd;
+            s_i = (float) sd;
+        }
+        #pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const int dim = 4 * lane + e;
+            const bool first = dim < half, second = dim >= half && dim < d.rope_dim;
+            const int pi = first ? dim : dim - half;                         // pair index of this dim
+            const float partner = __shfl_sync(0xffffffffu, x[e], first ? lane + half / 4 : (lane - half / 4) & 31);
+            const float c = __shfl_sync(0xffffffffu, c_i, pi & 31), s = __shfl_sync(0xffffffffu, s_i, pi & 31);
+            if ((first || second) && pi >= i0 && pi < i0 + 32) {
+                if (first) y[e] = __fsub_rn(__fmul_rn(x[e], c), __fmul_rn(partner, s));     // x0*c - x1*s
+                else       y[e] = __fadd_rn(__fmul_rn(partner, s), __fmul_rn(x[e], c));     // x0*s + x1*c
+            }
         }
     }
     uint2 o;

@@ -96,7 +96,7 @@ template <int KV_TYPE, int NKV>
 __global__ void __launch_bounds__(ATT_THREADS, AttnCfg<KV_TYPE>::MIN_CTAS) attn_kernel(
         DevDesc d, const qsa_decode_item * __restrict__ items, qsa_layer_cache cache0, int n_past0,
         const void * __restrict__ q, int q_type,
-        const int * __restrict__ sel_ws, const int * __restrict__ nsel_ws, int tiles_per_cta, int max_chunks,
+        const int * sel_ws, const int * nsel_ws, int tiles_per_cta, int max_chunks,
         float * __restrict__ part_o, float * __restrict__ part_ml,
         OutSpec outs, uint32_t * __restrict__ status, float * __restrict__ state_out) {
     using Cfg = AttnCfg<KV_TYPE>;
@@ -167,36 +167,6 @@ __global__ void __launch_bounds__(ATT_THREADS, AttnCfg<KV_TYPE>::MIN_CTAS) attn_
             *reinterpret_cast<uint4 *>(qs + i * 8) = o4;
         }
     }
-    pdl_wait();                                // the selection of this step is complete
-    const int nsel_raw = nsel_ws[t];
-    for (int i = tid; i < d.kb; i += ATT_THREADS) sel[i] = sel_ws[(size_t) t * d.kb + i];
-    const bool pos_ok = qpos >= 0 && qpos < d.n_ctx;
-    const int nsel = pos_ok ? max(0, min(nsel_raw, d.kb)) : 0;
-    const int r = d.ratio;
-    constexpr int RBr = NKV * HB;                        // cache row bytes: the run copies' row pitch
-    const int n_cells = nsel * r;
-    const int n_tiles = (n_cells + ATT_CELLS - 1) / ATT_CELLS;
-    const int n_chunks = attn_n_chunks(d, nsel, tiles_per_cta);
-    const size_t outq = (size_t) t * d.n_head * HEAD_DIM;     // element offset of query t's output
-    // sharded mode: the unnormalised state [M 16][L 16][O 16x256] of query t instead of the output
-    float * stq = state_out ? state_out + (size_t) t * (2 * HROWS + HROWS * HEAD_DIM) : nullptr;
-    if (n_chunks == 0) {                       // nothing selected (or a bad position): zero output
-        if (chunk == 0) {
-            if (stq)
-                for (int i = tid; i < 2 * HROWS + HROWS * HEAD_DIM; i += ATT_THREADS) stq[i] = i < HROWS ? -INFINITY : 0.0f;
-            else
-                for (int i = 4 * tid; i < d.n_head * HEAD_DIM; i += 4 * ATT_THREADS)
-                    out_store4(outs, outq + i, make_float4(0.f, 0.f, 0.f, 0.f));
-        }
-        return;
-    }
-    if (chunk >= n_chunks) return;             // the grid covers the longest query of the batch
-    if ((smem_u32(smem) & 15u) != 0) {        // bulk copies need 16-byte aligned destinations
-        if (tid == 0) set_status(status, DEV_BAD_SEL);
-        return;
-    }
-    const int tile0 = chunk * tiles_per_cta;
-    const int n_local = min(tiles_per_cta, n_tiles - tile0);
     if (tid == 0) {
         for (int s = 0; s < NS; s++) {
             mbar_init(&full_bar[s], 1);
@@ -205,7 +175,7 @@ __global__ void __launch_bounds__(ATT_THREADS, AttnCfg<KV_TYPE>::MIN_CTAS) attn_
         abort_wait = 0;
         fence_mbar_init();
     }
-    __syncthreads();                                  // staged Q, sel and the barriers are visible
+    __syncthreads();                                  // staged Q and the barriers are visible
     // Q fragments (mma B operand) of each KV head, packed in lane order into shared memory (over
     // the staged Q, which only these two builders read): head n = r8 of the 8-head tile.
     uint32_t qf[16][2];
@@ -250,6 +220,37 @@ __global__ void __launch_bounds__(ATT_THREADS, AttnCfg<KV_TYPE>::MIN_CTAS) attn_
         for (int k = 0; k < 8; k++) qreg[k] = qfrag[(hs * 16 + 8 * dh + k) * 32 + lane];
     }
     __syncthreads();
+    // Everything above depends on Q only, so it runs while the selection of this step is still in
+    // progress (this grid is launched programmatically behind it).
+    pdl_wait();                                // the selection of this step is complete
+    const int nsel_raw = ld_dep(nsel_ws + t);
+    const bool pos_ok = qpos >= 0 && qpos < d.n_ctx;
+    const int nsel = pos_ok ? max(0, min(nsel_raw, d.kb)) : 0;
+    const int r = d.ratio;
+    constexpr int RBr = NKV * HB;                        // cache row bytes: the run copies' row pitch
+    const int n_cells = nsel * r;
+    const int n_tiles = (n_cells + ATT_CELLS - 1) / ATT_CELLS;
+    const int n_chunks = attn_n_chunks(d, nsel, tiles_per_cta);
+    const size_t outq = (size_t) t * d.n_head * HEAD_DIM;     // element offset of query t's output
+    // sharded mode: the unnormalised state [M 16][L 16][O 16x256] of query t instead of the output
+    float * stq = state_out ? state_out + (size_t) t * (2 * HROWS + HROWS * HEAD_DIM) : nullptr;
+    if (n_chunks == 0) {                       // nothing selected (or a bad position): zero output
+        if (chunk == 0) {
+            if (stq)
+                for (int i = tid; i < 2 * HROWS + HROWS * HEAD_DIM; i += ATT_THREADS) stq[i] = i < HROWS ? -INFINITY : 0.0f;
+            else
+                for (int i = 4 * tid; i < d.n_head * HEAD_DIM; i += 4 * ATT_THREADS)
+                    out_store4(outs, outq + i, make_float4(0.f, 0.f, 0.f, 0.f));
+        }
+        return;
+    }
+    if (chunk >= n_chunks) return;             // the grid covers the longest query of the batch
+    if ((smem_u32(smem) & 15u) != 0) {        // bulk copies need 16-byte aligned destinations
+        if (tid == 0) set_status(status, DEV_BAD_SEL);
+        return;
+    }
+    const int tile0 = chunk * tiles_per_cta;
+    const int n_local = min(tiles_per_cta, n_tiles - tile0);
 
     auto stage_k = [&](int s) { return smem + s * attn_stage_bytes<KV_TYPE>(); };
     auto stage_v = [&](int s) { return smem + s * attn_stage_bytes<KV_TYPE>() + ATT_CELLS * RB; };  // RB >= row bytes
@@ -270,6 +271,9 @@ __global__ void __launch_bounds__(ATT_THREADS, AttnCfg<KV_TYPE>::MIN_CTAS) attn_
     float m0 = -1e30f, m1 = -1e30f, l0 = 0.0f, l1 = 0.0f;
 
     if (producer) {
+        // only the producer reads the selected list: its lanes copy it (no CTA barrier)
+        for (int i = lane; i < nsel; i += 32) sel[i] = ld_dep(sel_ws + (size_t) t * d.kb + i);
+        __syncwarp();
         // Tile i goes to stage i % NS: one copy per block-run of valid rows (cells <= the query
         // position) for K and V, and the tile's 32-bit row-validity mask (written before the
         // release of the arrive).  Lane = tile entry.
@@ -603,8 +607,8 @@ constexpr int MERGE_GROUPS = MERGE_THREADS / MERGE_COLS;
 // 134 chunks; 2 for batched decode, whose few chunks per query need few registers)
 template <int PRE>
 __global__ void __launch_bounds__(MERGE_THREADS) attn_merge_kernel(DevDesc d, const qsa_decode_item * __restrict__ items,
-        int n_past0, const int * __restrict__ nsel_ws, int tiles_per_cta, int max_chunks,
-        const float * __restrict__ part_o, const float * __restrict__ part_ml,
+        int n_past0, const int * nsel_ws, int tiles_per_cta, int max_chunks,
+        const float * part_o, const float * part_ml,
         OutSpec outs, float * __restrict__ state_out) {
     extern __shared__ float wsh[];                    // [max_chunks] weights
     __shared__ float red[2][MERGE_THREADS / 32];
@@ -619,7 +623,7 @@ __global__ void __launch_bounds__(MERGE_THREADS) attn_merge_kernel(DevDesc d, co
     if (!state_out && !live) return;
     pdl_wait();                                       // attn_kernel has completed: partials are written
     const bool pos_ok = qpos >= 0 && qpos < d.n_ctx;
-    const int nsel = pos_ok ? max(0, min(nsel_ws[t], d.kb)) : 0;
+    const int nsel = pos_ok ? max(0, min(ld_dep(nsel_ws + t), d.kb)) : 0;
     const int n_chunks = attn_n_chunks(d, nsel, tiles_per_cta);
     if (n_chunks <= 1) return;                        // written by the attention CTA itself
     // the partial rows do not depend on the weights: this thread's (up to PRE) loads go out
@@ -630,11 +634,11 @@ __global__ void __launch_bounds__(MERGE_THREADS) attn_merge_kernel(DevDesc d, co
     #pragma unroll
     for (int k = 0; k < PRE; k++) {
         const int c = grp + k * MERGE_GROUPS;
-        pre[k] = c < n_chunks ? __ldcg(po + (size_t) c * cstride) : make_float4(0.f, 0.f, 0.f, 0.f);
+        pre[k] = c < n_chunks ? ld_dep(po + (size_t) c * cstride) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     const float * ml = part_ml + (size_t) t * max_chunks * 2 * HROWS;
     float M = -INFINITY;
-    for (int c = tid; c < n_chunks; c += MERGE_THREADS) M = fmaxf(M, __ldcg(ml + c * 2 * HROWS + hr));
+    for (int c = tid; c < n_chunks; c += MERGE_THREADS) M = fmaxf(M, ld_dep(ml + c * 2 * HROWS + hr));
     M = warp_max(M);
     if (lane == 0) red[0][warp] = M;
     __syncthreads();
@@ -644,9 +648,9 @@ __global__ void __launch_bounds__(MERGE_THREADS) attn_merge_kernel(DevDesc d, co
     const float Mu = M == -INFINITY ? 0.0f : M;
     float L = 0.0f;
     for (int c = tid; c < n_chunks; c += MERGE_THREADS) {
-        const float w = exp2f(__ldcg(ml + c * 2 * HROWS + hr) - Mu);
+        const float w = exp2f(ld_dep(ml + c * 2 * HROWS + hr) - Mu);
         wsh[c] = w;
-        L += __ldcg(ml + c * 2 * HROWS + HROWS + hr) * w;
+        L += ld_dep(ml + c * 2 * HROWS + HROWS + hr) * w;
     }
     #pragma unroll
     for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
@@ -664,7 +668,7 @@ __global__ void __launch_bounds__(MERGE_THREADS) attn_merge_kernel(DevDesc d, co
     }
     #pragma unroll 4
     for (int c = grp + PRE * MERGE_GROUPS; c < n_chunks; c += MERGE_GROUPS) {   // longer splits
-        const float4 v = __ldcg(po + (size_t) c * cstride);
+        const float4 v = ld_dep(po + (size_t) c * cstride);
         const float w = wsh[c];
         acc.x += w * v.x; acc.y += w * v.y; acc.z += w * v.z; acc.w += w * v.w;
     }

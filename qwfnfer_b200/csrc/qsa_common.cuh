@@ -100,6 +100,31 @@ __device__ __forceinline__ int8_t q8_0_quant_lane(float v, uint16_t & dbits) {
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// Loads of data that the preceding grid of a programmatic chain writes, issued after pdl_wait():
+// volatile asm with a memory clobber is never moved above the wait (through a const __restrict__
+// pointer the compiler may treat the data as unchanging for the whole kernel and hoist its loads),
+// and .cg reads the lines from L2.
+__device__ __forceinline__ int ld_dep(const int * p) {
+    int v;
+    asm volatile("ld.global.cg.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ float ld_dep(const float * p) {
+    float v;
+    asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ float4 ld_dep(const float4 * p) {
+    float4 v;
+    asm volatile("ld.global.cg.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ uint4 ld_dep(const uint4 * p) {
+    uint4 v;
+    asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p) : "memory");
+    return v;
+}
+
 __device__ __forceinline__ void set_status(uint32_t * status, uint32_t code) {
     if (status) atomicOr(status, code);
 }

@@ -23,7 +23,7 @@ static_assert(MAX_KB <= SEL_THREADS, "one kept block per selection thread");
 // Score blocks [b_begin, b_end) of one query: 16 lanes per block row (8 dims = 16 bytes each).
 // Products of two f16 values are exact in f32; they are summed in double (exact for these
 // magnitudes) and rounded once, so the result does not depend on the summation order.
-__device__ __forceinline__ void score_range(const DevDesc & d, const uint16_t * __restrict__ pool,
+__device__ __forceinline__ void score_range(const DevDesc & d, const uint16_t * pool,
         const float (&qf)[4][8], int b_begin, int b_end, float * __restrict__ scores) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     const int half = lane >> 4, sub = lane & 15;
@@ -31,7 +31,8 @@ __device__ __forceinline__ void score_range(const DevDesc & d, const uint16_t * 
         const int b = b0 + half;
         const bool ok = b < b_end;
         uint4 w = make_uint4(0, 0, 0, 0);
-        if (ok) w = __ldg(reinterpret_cast<const uint4 *>(pool + (size_t) b * MAX_IDX_DIM + 8 * sub));
+        // pooled keys the append before this grid may have written (read after its pdl_wait)
+        if (ok) w = ld_dep(reinterpret_cast<const uint4 *>(pool + (size_t) b * MAX_IDX_DIM + 8 * sub));
         const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
         float pk[8];
         #pragma unroll

@@ -19,11 +19,11 @@ constexpr int STAGE_THREADS = 256;
 // 16-byte pieces, one per thread and grid-stride beyond that.  The wait comes first: the bytes
 // may be the output of the kernel before this one in the stream.
 __global__ void __launch_bounds__(STAGE_THREADS) stage_copy_kernel(uint4 * __restrict__ dst,
-                                                                   const uint4 * __restrict__ src, size_t n16) {
+                                                                   const uint4 * src, size_t n16) {
     pdl_wait();
     pdl_trigger();
     const size_t stride = (size_t) gridDim.x * blockDim.x;
-    for (size_t i = (size_t) blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += stride) dst[i] = src[i];
+    for (size_t i = (size_t) blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += stride) dst[i] = ld_dep(src + i);
 }
 
 // Device memory of the current device, managed memory, or pinned host memory that kernels can
