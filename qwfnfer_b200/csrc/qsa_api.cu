@@ -112,13 +112,14 @@ qsa_status launch_select(const DevDesc & d, const WsLayout & w, int n_q, const q
                          unsigned char * ws, cudaStream_t st, float * cand_scores = nullptr) {
     uint32_t * status = reinterpret_cast<uint32_t *>(ws + w.status);
     // blocks per scoring CTA: one row pair per warp while the grid fits one wave, more once it
-    // would not (a 1024-thread CTA holds a whole SM's registers: one wave is 148 CTAs)
+    // would not (a CTA holds a whole SM's registers: one wave is 148 CTAs)
     const int lo = d.shard_ri ? 0 : d.shard_blk0, hi = d.shard_ri ? INT_MAX : d.shard_blk1;
     const int n_blk = std::max(1, std::min(w.scores_stride, hi) - lo);   // blocks scored
     int bpc = 2 * (SEL_THREADS_HOST / 32);                 // one row pair per warp
     while (bpc < 1024 && (int64_t) ceil_div(n_blk, bpc) * n_q > 148) bpc *= 2;
     const int score_ctas = ceil_div(n_blk, bpc);
-    const size_t sel_smem = (size_t) w.scores_stride * 5;       // scores + selection flags
+    // the scores, then one ballot word per 32 candidates (and per selecting warp, its last round)
+    const size_t sel_smem = (size_t) w.scores_stride * 4 + ((size_t) ceil_div(w.scores_stride, 32) + SEL_THREADS_HOST / 32) * 4;
     if (sel_smem > 160 * 1024) return QSA_ERR_UNSUPPORTED;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(score_ctas, n_q);

@@ -224,6 +224,17 @@ __global__ void __launch_bounds__(ATT_THREADS, AttnCfg<KV_TYPE>::MIN_CTAS) attn_
     // progress (this grid is launched programmatically behind it).
     pdl_wait();                                // the selection of this step is complete
     const int nsel_raw = ld_dep(nsel_ws + t);
+    // the producer requests the first entries of the list together with its length (one round
+    // trip instead of two; entries past the length are never used)
+    constexpr int SEL_PRE = 4;
+    int sel_pre[SEL_PRE];
+    if (producer) {
+        #pragma unroll
+        for (int k = 0; k < SEL_PRE; k++) {
+            const int i = lane + 32 * k;
+            sel_pre[k] = i < d.kb ? ld_dep(sel_ws + (size_t) t * d.kb + i) : -1;
+        }
+    }
     const bool pos_ok = qpos >= 0 && qpos < d.n_ctx;
     const int nsel = pos_ok ? max(0, min(nsel_raw, d.kb)) : 0;
     const int r = d.ratio;
@@ -272,7 +283,10 @@ __global__ void __launch_bounds__(ATT_THREADS, AttnCfg<KV_TYPE>::MIN_CTAS) attn_
 
     if (producer) {
         // only the producer reads the selected list: its lanes copy it (no CTA barrier)
-        for (int i = lane; i < nsel; i += 32) sel[i] = ld_dep(sel_ws + (size_t) t * d.kb + i);
+        #pragma unroll
+        for (int k = 0; k < SEL_PRE; k++)
+            if (lane + 32 * k < nsel) sel[lane + 32 * k] = sel_pre[k];
+        for (int i = lane + 32 * SEL_PRE; i < nsel; i += 32) sel[i] = ld_dep(sel_ws + (size_t) t * d.kb + i);
         __syncwarp();
         // Tile i goes to stage i % NS: one copy per block-run of valid rows (cells <= the query
         // position) for K and V, and the tile's 32-bit row-validity mask (written before the

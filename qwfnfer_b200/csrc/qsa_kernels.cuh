@@ -24,7 +24,7 @@ cudaError_t once_per_device(std::atomic<uint64_t> & done, F && set) {
 }
 
 constexpr int MAX_KB = 1024;          // blocks kept per query that the kernels can hold
-constexpr int SEL_THREADS_HOST = 1024;      // threads of a scoring/selection CTA
+constexpr int SEL_THREADS_HOST = 512;       // threads of a scoring/selection CTA
 
 __global__ void append_rows_kernel(DevDesc d, qsa_layer_cache c, int pos0,
         const float * k, const float * v, const float * kidx);
