@@ -4,8 +4,8 @@ The scores are exact functions of the pooled keys (f16 x f16 products are exact 
 double, rounded once), so the GPU and the oracle score every block identically and the selected
 lists must be equal entry for entry, ties included (ties go to the lower block).  The pooled keys
 are written directly (the selection reads nothing else), so contexts of any length are cheap:
-  - random keys at every candidate count the selecting threads are laid out for (4 to 64 blocks
-    per thread, the last beyond 16,384 blocks);
+  - random keys from 70 to 20,000 blocks (1 to 16 selecting warps, one to several rounds of
+    candidates per warp);
   - every score equal (equal keys; all-zero keys), a few distinct scores (ties at the cut), fewer
     positive scores than wanted (the cut falls among the zeros), a cut inside one f32 exponent.
 """
