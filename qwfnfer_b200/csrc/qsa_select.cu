@@ -17,39 +17,59 @@ namespace qsa {
 
 constexpr int SEL_THREADS = SEL_THREADS_HOST;
 
-// Score blocks [b_begin, b_end) of one query: 16 lanes per block row (8 dims = 16 bytes each).
-// Products of two f16 values are exact in f32; they are summed in double (exact for these
-// magnitudes) and rounded once, so the result does not depend on the summation order.
+// Score blocks [b_begin, b_end) of one query: 16 lanes per block row (8 dims = 16 bytes each), a
+// warp on SCORE_U row pairs at a time (their loads in flight together).  Products of two f16
+// values are exact in f32; they are summed in double (exact for these magnitudes) and rounded
+// once, so the result does not depend on the summation order.
+constexpr int SCORE_U = 4;
+
+// This warp's rows of the batch at b0 (rows b0 + u*step + half); pooled keys the append before
+// this grid may have written, read after its pdl_wait.
+__device__ __forceinline__ void score_load(const uint16_t * pool, int b0, int b_end, int step, uint4 (&w)[SCORE_U]) {
+    const int half = (threadIdx.x >> 4) & 1, sub = threadIdx.x & 15;
+    #pragma unroll
+    for (int u = 0; u < SCORE_U; u++) {
+        const int b = b0 + u * step + half;
+        w[u] = b < b_end ? ld_dep(reinterpret_cast<const uint4 *>(pool + (size_t) b * MAX_IDX_DIM + 8 * sub))
+                         : make_uint4(0, 0, 0, 0);
+    }
+}
+
 __device__ __forceinline__ void score_range(const DevDesc & d, const uint16_t * pool,
-        const float (&qf)[4][8], int b_begin, int b_end, float * __restrict__ scores, uint4 first) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    const int half = lane >> 4, sub = lane & 15;
-    for (int b0 = b_begin + 2 * warp; b0 < b_end; b0 += 2 * nw) {
-        const int b = b0 + half;
-        const bool ok = b < b_end;
-        uint4 w = first;                       // the first pair was loaded by the caller
-        first = make_uint4(0, 0, 0, 0);
-        // pooled keys the append before this grid may have written (read after its pdl_wait)
-        if (b0 != b_begin + 2 * warp && ok) w = ld_dep(reinterpret_cast<const uint4 *>(pool + (size_t) b * MAX_IDX_DIM + 8 * sub));
-        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-        float pk[8];
+        const float (&qf)[4][8], int b_begin, int b_end, float * __restrict__ scores, const uint4 (&first)[SCORE_U]) {
+    const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int half = (threadIdx.x >> 4) & 1, sub = threadIdx.x & 15;
+    const int step = 2 * nw;
+    uint4 w[SCORE_U];
+    #pragma unroll
+    for (int u = 0; u < SCORE_U; u++) w[u] = first[u];      // the first batch was loaded by the caller
+    #pragma unroll 1
+    for (int b0 = b_begin + 2 * warp; b0 < b_end; b0 += SCORE_U * step) {
+        if (b0 != b_begin + 2 * warp) score_load(pool, b0, b_end, step, w);
         #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            pk[2 * i]     = f16_bits_to_f32((uint16_t) (ws[i] & 0xffff));
-            pk[2 * i + 1] = f16_bits_to_f32((uint16_t) (ws[i] >> 16));
-        }
-        double hs = 0.0;
-        #pragma unroll
-        for (int h = 0; h < 4; h++) {
-            if (h >= d.idx_n_head) break;
-            double acc = 0.0;
+        for (int u = 0; u < SCORE_U; u++) {
+            if (b0 + u * step >= b_end) break;           // this warp's remaining rows are past the range
+            const int b = b0 + u * step + half;
+            const uint32_t ws[4] = {w[u].x, w[u].y, w[u].z, w[u].w};
+            float pk[8];
             #pragma unroll
-            for (int e = 0; e < 8; e++) acc += (double) __fmul_rn(pk[e], qf[h][e]);
-            acc = warp_sum16_d(acc);
-            const float dot = (float) acc;
-            hs += (double) (dot > 0.0f ? dot : 0.0f);
+            for (int i = 0; i < 4; i++) {
+                pk[2 * i]     = f16_bits_to_f32((uint16_t) (ws[i] & 0xffff));
+                pk[2 * i + 1] = f16_bits_to_f32((uint16_t) (ws[i] >> 16));
+            }
+            double hs = 0.0;
+            #pragma unroll
+            for (int h = 0; h < 4; h++) {
+                if (h >= d.idx_n_head) break;
+                double acc = 0.0;
+                #pragma unroll
+                for (int e = 0; e < 8; e++) acc += (double) __fmul_rn(pk[e], qf[h][e]);
+                acc = warp_sum16_d(acc);
+                const float dot = (float) acc;
+                hs += (double) (dot > 0.0f ? dot : 0.0f);
+            }
+            if (b < b_end && sub == 0) scores[b] = (float) hs;
         }
-        if (ok && sub == 0) scores[b] = (float) hs;
     }
 }
 
@@ -62,7 +82,7 @@ __device__ __forceinline__ void forced_range(const DevDesc & d, int q, int & f_l
 }
 
 constexpr int SEL_BINS = 256;      // one radix digit: 8 bits
-constexpr int LIST_MAX = 1024;     // entries of a cut bin collected for the later digits
+constexpr int LIST_MAX = 4096;     // entries of a cut bin collected for the later digits
 constexpr int RANK_MAX = 32;       // a cut bin this small is ranked directly
 
 // Selection scratch of the last CTA of a query.  The digit histograms are triple-buffered: a
@@ -144,28 +164,42 @@ __device__ void select_blocks(const DevDesc & d, const float * sc_g, float * ssc
     auto comp = [&](int b) -> unsigned long long {
         return ((unsigned long long) __float_as_uint(ssc[b]) << 32) | (unsigned) (c_end - 1 - b);
     };
-    // 1. the candidates' scores into shared memory (16-byte loads, two in flight per thread: score
+    // 1. the candidates' scores into shared memory (16-byte loads, four in flight per thread: score
     //    rows are 16-byte aligned; written by the other CTAs of this grid, read after the arrival's
-    //    acquire), with the histogram of the first digit (score bits 30..23).  Zero scores (every
-    //    head cut by the relu, about half of the keys) are counted per warp.
+    //    acquire), with the histogram of the first digit (score bits 30..23), counted from shared
+    //    memory by a short loop.  Zero scores (every head cut by the relu, about half of the keys)
+    //    are counted per warp.
     {
+        constexpr int U = 4;
         const int i0 = lo_c >> 2, i1 = (c_end + 3) >> 2;
         #pragma unroll 1
-        for (int base = i0; base < i1; base += 2 * ns) {
-            const int ia = base + tid, ibb = base + ns + tid;
-            const float4 va = ia < i1 ? __ldcg(reinterpret_cast<const float4 *>(sc_g) + ia) : make_float4(0.f, 0.f, 0.f, 0.f);
-            const float4 vb = ibb < i1 ? __ldcg(reinterpret_cast<const float4 *>(sc_g) + ibb) : make_float4(0.f, 0.f, 0.f, 0.f);
-            if (ia < i1) reinterpret_cast<float4 *>(ssc)[ia] = va;
-            if (ibb < i1) reinterpret_cast<float4 *>(ssc)[ibb] = vb;
-            const float e[8] = {va.x, va.y, va.z, va.w, vb.x, vb.y, vb.z, vb.w};
-            int n_zero = 0;
+        for (int base = i0; base < i1; base += U * ns) {
+            float4 v[U];
             #pragma unroll
-            for (int k = 0; k < 8; k++) {
-                const int b = 4 * (k < 4 ? ia : ibb) + (k & 3);
-                const unsigned key = __float_as_uint(e[k]);
-                if (b < lo_c || b >= c_end) continue;
-                if (key) atomicAdd(&sm.hist[0][(key >> 23) & 0xffu], 1u);
-                else n_zero++;
+            for (int u = 0; u < U; u++) {
+                const int i = base + u * ns + tid;
+                v[u] = i < i1 ? __ldcg(reinterpret_cast<const float4 *>(sc_g) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+            #pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int i = base + u * ns + tid;
+                if (i < i1) reinterpret_cast<float4 *>(ssc)[i] = v[u];
+            }
+            int n_zero = 0;
+            #pragma unroll 1
+            for (int u = 0; u < U; u++) {
+                const int i = base + u * ns + tid;
+                if (i >= i1) break;
+                const float4 x = reinterpret_cast<const float4 *>(ssc)[i];
+                const float e[4] = {x.x, x.y, x.z, x.w};
+                #pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    const int b = 4 * i + k;
+                    const unsigned key = __float_as_uint(e[k]);
+                    if (b < lo_c || b >= c_end) continue;
+                    if (key) atomicAdd(&sm.hist[0][(key >> 23) & 0xffu], 1u);
+                    else n_zero++;
+                }
             }
             #pragma unroll
             for (int o = 16; o > 0; o >>= 1) n_zero += __shfl_xor_sync(0xffffffffu, n_zero, o);
@@ -333,11 +367,10 @@ __global__ void __launch_bounds__(SEL_THREADS, 1) score_select_kernel(DevDesc d,
         const int b0 = blo + blockIdx.x * blocks_per_cta;
         const int b1 = min(min(cand_hi, bhi), b0 + blocks_per_cta);
         if (!defer_wait) pdl_wait();             // the append of this step (pooled keys) is complete
-        // this warp's first row pair is requested before the query is read: the two loads overlap
+        // this warp's first batch of rows is requested before the query is read: the loads overlap
         const int sub = threadIdx.x & 15;
-        const int bf = b0 + 2 * (threadIdx.x >> 5) + ((threadIdx.x >> 4) & 1);
-        uint4 first = make_uint4(0, 0, 0, 0);
-        if (bf < b1) first = ld_dep(reinterpret_cast<const uint4 *>(pool + (size_t) bf * MAX_IDX_DIM + 8 * sub));
+        uint4 first[SCORE_U];
+        score_load(pool, b0 + 2 * (int) (threadIdx.x >> 5), b1, 2 * (int) (blockDim.x >> 5), first);
         float qf[4][8];
         #pragma unroll
         for (int h = 0; h < 4; h++)
