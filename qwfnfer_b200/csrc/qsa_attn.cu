@@ -707,6 +707,66 @@ __global__ void __launch_bounds__(MERGE_THREADS) attn_merge_kernel(DevDesc d, co
     }
 }
 
+// The merge for queries split over at most MERGE_SMALL_CHUNKS chunks (batched decode, short
+// prefill chunks): CTA = query, thread = (row hr, float4 column); every thread loads its row's
+// (m, l) and its column of every partial at once and forms the same M, weights and L as
+// attn_merge_kernel.  Launched programmatically behind attn_kernel.
+constexpr int MERGE_SMALL_CHUNKS = 8;
+constexpr int MERGE_SMALL_THREADS = HROWS * HEAD_DIM / 4;
+
+__global__ void __launch_bounds__(MERGE_SMALL_THREADS) attn_merge_small_kernel(DevDesc d,
+        const qsa_decode_item * __restrict__ items, int n_past0, const int * nsel_ws, int tiles_per_cta, int max_chunks,
+        const float * part_o, const float * part_ml, OutSpec outs, float * __restrict__ state_out) {
+    const int t = blockIdx.x, tid = threadIdx.x;
+    const int hr = tid / (HEAD_DIM / 4), d4 = tid % (HEAD_DIM / 4);
+    const int g = hr >> 3, h = hr & 7;
+    const int qpos = items ? items[t].n_past : n_past0 + t;
+    const bool live = g < d.n_head_kv && h < d.gqa;
+    if (!state_out && !live) return;
+    pdl_wait();                                       // attn_kernel has completed: partials are written
+    const bool pos_ok = qpos >= 0 && qpos < d.n_ctx;
+    const int nsel = pos_ok ? max(0, min(ld_dep(nsel_ws + t), d.kb)) : 0;
+    const int n_chunks = min(attn_n_chunks(d, nsel, tiles_per_cta), MERGE_SMALL_CHUNKS);
+    if (n_chunks <= 1) return;                        // written by the attention CTA itself
+    const float * ml = part_ml + (size_t) t * max_chunks * 2 * HROWS;
+    const float4 * po = reinterpret_cast<const float4 *>(part_o + ((size_t) t * max_chunks * HROWS + hr) * HEAD_DIM) + d4;
+    const size_t cstride = (size_t) HROWS * HEAD_DIM / 4;         // float4s between chunks
+    float mc[MERGE_SMALL_CHUNKS], lc[MERGE_SMALL_CHUNKS];
+    float4 oc[MERGE_SMALL_CHUNKS];
+    #pragma unroll
+    for (int c = 0; c < MERGE_SMALL_CHUNKS; c++) {
+        if (c < n_chunks) {
+            mc[c] = ld_dep(ml + c * 2 * HROWS + hr);
+            lc[c] = ld_dep(ml + c * 2 * HROWS + HROWS + hr);
+            oc[c] = ld_dep(po + (size_t) c * cstride);
+        } else {
+            mc[c] = -INFINITY; lc[c] = 0.0f; oc[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
+    float M = -INFINITY;
+    #pragma unroll
+    for (int c = 0; c < MERGE_SMALL_CHUNKS; c++) M = fmaxf(M, mc[c]);
+    const float Mu = M == -INFINITY ? 0.0f : M;
+    float L = 0.0f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    #pragma unroll
+    for (int c = 0; c < MERGE_SMALL_CHUNKS; c++) {
+        if (c >= n_chunks) break;
+        const float w = exp2f(mc[c] - Mu);
+        L += lc[c] * w;
+        acc.x += w * oc[c].x; acc.y += w * oc[c].y; acc.z += w * oc[c].z; acc.w += w * oc[c].w;
+    }
+    if (state_out) {
+        float * stq = state_out + (size_t) t * (2 * HROWS + HROWS * HEAD_DIM);
+        reinterpret_cast<float4 *>(stq + 2 * HROWS + hr * HEAD_DIM)[d4] = acc;
+        if (d4 == 0) { stq[hr] = M; stq[HROWS + hr] = L; }
+    } else {
+        const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+        out_store4(outs, ((size_t) t * d.n_head + g * d.gqa + h) * HEAD_DIM + 4 * d4,
+                   make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv));
+    }
+}
+
 template <int KV_TYPE, int NKV>
 cudaError_t attn_set_attr_one() {
     return cudaFuncSetAttribute(attn_kernel<KV_TYPE, NKV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -751,6 +811,13 @@ cudaError_t launch_attn(const DevDesc & d, cudaStream_t st, int n_q, const qsa_d
 #undef QSA_LAUNCH_ATTN
     if (e != cudaSuccess || max_chunks <= 1) return e;
     cudaLaunchConfig_t mc = cfg;
+    if (max_chunks <= MERGE_SMALL_CHUNKS) {
+        mc.gridDim = dim3((unsigned) n_q);
+        mc.blockDim = dim3(MERGE_SMALL_THREADS);
+        mc.dynamicSmemBytes = 0;
+        return cudaLaunchKernelEx(&mc, attn_merge_small_kernel, d, items, n_past0, nsel_ws, tiles_per_cta, max_chunks,
+                                  (const float *) part_o, (const float *) part_ml, outs, state_out);
+    }
     mc.gridDim = dim3((unsigned) n_q, HROWS, HEAD_DIM / (4 * MERGE_COLS));
     mc.blockDim = dim3(MERGE_THREADS);
     mc.dynamicSmemBytes = (size_t) max_chunks * 4;
