@@ -240,8 +240,32 @@ __device__ void select_blocks(const DevDesc & d, const float * sc_g, float * ssc
                 for (int i = tid; i < SEL_BINS; i += ns) hnext[i] = 0u;
             }
             const int n = from_list ? nlist : n_c;
+            // over many candidates the keys of four iterations are read ahead (this loop then runs
+            // long enough for its wider code to pay); short passes keep the compact loop
+            const int p_fast = (!from_list && n > 4096) ? n - n % (4 * ns) : 0;
             #pragma unroll 1
-            for (int p = tid; p < n; p += ns) {
+            for (int p0 = tid; p0 < p_fast; p0 += 4 * ns) {
+                unsigned long long Cs[4];
+                #pragma unroll
+                for (int u = 0; u < 4; u++) Cs[u] = comp(lo_c + p0 + u * ns);
+                #pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const unsigned long long C = Cs[u];
+                    if ((C & pmask) != prefix) continue;
+                    if (rank) {
+                        const int slot = atomicAdd(&sm.nstage, 1);
+                        if (slot < RANK_MAX) sm.stage[slot] = C;
+                        continue;
+                    }
+                    if (collect) {
+                        const int slot = atomicAdd(&sm.nlist, 1);
+                        if (slot < LIST_MAX) sm.list[slot] = lo_c + p0 + u * ns;
+                    }
+                    atomicAdd(hcur + ((unsigned) (C >> dshift) & dmask), 1u);
+                }
+            }
+            #pragma unroll 1
+            for (int p = p_fast + tid; p < n; p += ns) {
                 const int b = from_list ? sm.list[p] : lo_c + p;
                 const unsigned long long C = comp(b);
                 if ((C & pmask) != prefix) continue;
@@ -277,8 +301,24 @@ __device__ void select_blocks(const DevDesc & d, const float * sc_g, float * ssc
     const int R = (n_c + ns - 1) / ns;
     const int start = lo_c + w * R * 32, end = min(c_end, start + R * 32);
     int cnt = 0;
+    const int r_fast = R >= 8 ? R - R % 4 : 0;        // many rounds: four in flight
     #pragma unroll 1
-    for (int r = 0; r < R; r++) {
+    for (int r0 = 0; r0 < r_fast; r0 += 4) {
+        bool tk[4];
+        #pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int b = start + 32 * (r0 + u) + lane;
+            tk[u] = b < end && comp(b) >= K;
+        }
+        #pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const unsigned m = __ballot_sync(0xffffffffu, tk[u]);
+            if (lane == 0) balls[w * R + r0 + u] = m;
+            cnt += __popc(m);
+        }
+    }
+    #pragma unroll 1
+    for (int r = r_fast; r < R; r++) {
         const int b = start + 32 * r + lane;
         const unsigned m = __ballot_sync(0xffffffffu, b < end && comp(b) >= K);
         if (lane == 0) balls[w * R + r] = m;
