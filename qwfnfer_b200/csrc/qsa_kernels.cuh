@@ -92,9 +92,5 @@ cudaError_t launch_shard_select(const DevDesc & d, cudaStream_t st, const qsa_de
         uint32_t * status);
 cudaError_t launch_merge_states(const DevDesc & d, cudaStream_t st, int n_parts, int batch, const float * states,
         float * out);
-// CTAs per thread-block cluster of the attention launch (partials are per cluster).
-int attn_cluster_size(int max_chunks);
-// Rows (KV head x query head) of the attention state: a partial is rows x head_dim floats.
-int attn_state_rows();
 
 }  // namespace qsa

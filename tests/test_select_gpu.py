@@ -4,8 +4,9 @@ The scores are exact functions of the pooled keys (f16 x f16 products are exact 
 double, rounded once), so the GPU and the oracle score every block identically and the selected
 lists must be equal entry for entry, ties included (ties go to the lower block).  The pooled keys
 are written directly (the selection reads nothing else), so contexts of any length are cheap:
-  - random keys from 70 to 20,000 blocks (1 to 16 selecting warps, one to several rounds of
-    candidates per warp);
+  - random keys from 70 to 33,000 blocks (1 to 16 selecting warps, one to several rounds of
+    candidates per warp, passes that read four keys per thread ahead beyond 4,096 candidates);
+  - 128 to 512 blocks kept, up to 36,000 blocks (close to the 160 KB of scores one CTA holds);
   - every score equal (equal keys; all-zero keys), a few distinct scores (ties at the cut), fewer
     positive scores than wanted (the cut falls among the zeros), a cut inside one f32 exponent.
 """
@@ -63,11 +64,20 @@ def _f16(a) -> np.ndarray:
     return np.ascontiguousarray(np.asarray(a, np.float32).astype(np.float16))
 
 
-@pytest.mark.parametrize("n_blocks", [70, 900, 1900, 2560, 4000, 8100, 16384, 20000])
+@pytest.mark.parametrize("n_blocks", [70, 900, 1900, 2560, 4000, 8100, 8192, 16384, 20000, 33000])
 def test_random_keys_every_layout(n_blocks):
     rng = np.random.default_rng(n_blocks)
     rows = _f16(rng.normal(0, 1.012 / 8, (n_blocks, 128)))
     _run(n_blocks, rows, seed=n_blocks)
+
+
+@pytest.mark.parametrize("top_k,n_blocks", [(128, 16384), (256, 20000), (512, 36000), (512, 30000)])
+def test_wider_selections(top_k, n_blocks):
+    """More blocks kept, over long contexts: a cut bin larger than the collected list at the first
+    digits, ranks from a deeper level."""
+    rng = np.random.default_rng(top_k + n_blocks)
+    rows = _f16(rng.normal(0, 1.012 / 8, (n_blocks, 128)))
+    _run(n_blocks, rows, top_k=top_k, seed=top_k)
 
 
 @pytest.mark.parametrize("n_blocks", [500, 2560, 20000])
