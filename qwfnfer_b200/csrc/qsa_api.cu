@@ -105,11 +105,18 @@ qsa_status set_attrs() {
     }));
 }
 
+// Launch chaining.  Kernels after the first of a call are launched programmatically: they may
+// start before the kernel ahead of them ends, and read what it writes only after pdl_wait, but
+// read the call's inputs (items, q, q_idx, caches) at once.  That is safe because the first kernel
+// of every call is an ordinary launch, which starts only once all earlier work in the stream is
+// complete, whatever that work is (the caller's kernels, qsa_stage_copy, another call).
+// `chained`: a kernel of the same call precedes this launch.
+
 // Scores + selection into the workspace (and sel_out).  Sharded (cand_scores != null): scores of
 // the shard's blocks only, and its candidates with their scores in sel_out / cand_scores.
 qsa_status launch_select(const DevDesc & d, const WsLayout & w, int n_q, const qsa_decode_item * items,
                          qsa_layer_cache cache0, int n_past0, const float * q_idx, int32_t * sel_out,
-                         unsigned char * ws, cudaStream_t st, float * cand_scores = nullptr) {
+                         unsigned char * ws, cudaStream_t st, bool chained, float * cand_scores = nullptr) {
     uint32_t * status = reinterpret_cast<uint32_t *>(ws + w.status);
     // blocks per scoring CTA: one row pair per warp while the grid fits one wave, more once it
     // would not (a CTA holds a whole SM's registers: one wave is 148 CTAs)
@@ -130,7 +137,7 @@ qsa_status launch_select(const DevDesc & d, const WsLayout & w, int n_q, const q
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;      // overlaps the append's tail
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = chained ? 1 : 0;
     return cuda_status(cudaLaunchKernelEx(&cfg, score_select_kernel, d, items, cache0.pool, n_past0, q_idx, bpc,
         reinterpret_cast<float *>(ws + w.scores), w.scores_stride, reinterpret_cast<unsigned *>(ws + w.cnt_sel),
         reinterpret_cast<int *>(ws + w.sel), reinterpret_cast<int *>(ws + w.nsel), sel_out, status, cand_scores));
@@ -139,8 +146,8 @@ qsa_status launch_select(const DevDesc & d, const WsLayout & w, int n_q, const q
 // Attention over the selection held in the workspace (and the merge of split queries).
 qsa_status launch_attend(const DevDesc & d, const WsLayout & w, int n_q, const qsa_decode_item * items,
                          qsa_layer_cache cache0, int n_past0, const void * q, int q_type, OutSpec out,
-                         unsigned char * ws, cudaStream_t st, float * state_out = nullptr) {
-    return cuda_status(launch_attn(d, st, n_q, items, cache0, n_past0, q, q_type,
+                         unsigned char * ws, cudaStream_t st, bool chained, float * state_out = nullptr) {
+    return cuda_status(launch_attn(d, st, chained, n_q, items, cache0, n_past0, q, q_type,
                                    reinterpret_cast<const int *>(ws + w.sel), reinterpret_cast<const int *>(ws + w.nsel),
                                    w.tiles_per_cta, w.max_chunks, reinterpret_cast<float *>(ws + w.part_o),
                                    reinterpret_cast<float *>(ws + w.part_ml), out,
@@ -343,7 +350,7 @@ qsa_status qsa_decode_select(const qsa_desc * dd, const qsa_decode_item * items,
     if (!q_idx) return QSA_ERR_INVALID;
     qsa_layer_cache none{};
     return launch_select(d, w, batch, items, none, 0, q_idx, sel_out, static_cast<unsigned char *>(ws),
-                         reinterpret_cast<cudaStream_t>(stream));
+                         reinterpret_cast<cudaStream_t>(stream), false);
 }
 
 qsa_status qsa_decode_attend(const qsa_desc * dd, const qsa_decode_item * items, int32_t batch, int32_t max_n_kv,
@@ -355,7 +362,7 @@ qsa_status qsa_decode_attend(const qsa_desc * dd, const qsa_decode_item * items,
     if (!q || !out || (q_type != QSA_TYPE_BF16 && q_type != QSA_TYPE_F32)) return QSA_ERR_INVALID;
     qsa_layer_cache none{};
     return launch_attend(d, w, batch, items, none, 0, q, q_type, OutSpec{out, nullptr, nullptr, 0}, static_cast<unsigned char *>(ws),
-                         reinterpret_cast<cudaStream_t>(stream));
+                         reinterpret_cast<cudaStream_t>(stream), false);
 }
 
 namespace {
@@ -390,8 +397,8 @@ qsa_status decode_impl(const qsa_desc * dd, const qsa_decode_item * items, int32
         if ((s = launch_append_decode(d, st, batch, items, k_new, v_new, kidx_new,
                                       reinterpret_cast<uint32_t *>(wsb + w.status))) != QSA_OK) return s;
     qsa_layer_cache none{};
-    if ((s = launch_select(d, w, batch, items, none, 0, q_idx, sel_out, wsb, st)) != QSA_OK) return s;
-    return launch_attend(d, w, batch, items, none, 0, q, q_type, out, wsb, st);
+    if ((s = launch_select(d, w, batch, items, none, 0, q_idx, sel_out, wsb, st, any_new)) != QSA_OK) return s;
+    return launch_attend(d, w, batch, items, none, 0, q, q_type, out, wsb, st, true);
 }
 }  // namespace
 
@@ -451,14 +458,14 @@ qsa_status prefill_impl(const qsa_desc * dd, const qsa_layer_cache * cache, int3
             e = launch_select_scores_warp(d, st, n_past, T, scores, w.scores_stride, reinterpret_cast<int *>(wsb + w.sel),
                                           reinterpret_cast<int *>(wsb + w.nsel), sel_out, status);
         if (e != cudaSuccess) return QSA_ERR_CUDA;
-    } else if ((s = launch_select(d, w, T, nullptr, *cache, n_past, q_idx, sel_out, wsb, st)) != QSA_OK) {
+    } else if ((s = launch_select(d, w, T, nullptr, *cache, n_past, q_idx, sel_out, wsb, st, any_new)) != QSA_OK) {
         return s;
     }
     if (kv_path)
         return cuda_status(launch_prefill_attn_kv(d, st, *cache, n_past, T, q, q_type, reinterpret_cast<const int *>(wsb + w.sel),
                                                   reinterpret_cast<const int *>(wsb + w.nsel), prefill_n_blocks(d, n_past + T),
                                                   wsb + w.total, out, reinterpret_cast<uint32_t *>(wsb + w.status)));
-    return launch_attend(d, w, T, nullptr, *cache, n_past, q, q_type, out, wsb, st);
+    return launch_attend(d, w, T, nullptr, *cache, n_past, q, q_type, out, wsb, st, true);
 }
 }  // namespace
 
@@ -534,7 +541,7 @@ qsa_status qsa_shard_candidates(const qsa_desc * dd, const qsa_decode_item * ite
         if ((s = launch_append_decode(d, st, batch, items, k_new, v_new, kidx_new,
                                       reinterpret_cast<uint32_t *>(wsb + w.status))) != QSA_OK) return s;
     qsa_layer_cache none{};
-    return launch_select(d, w, batch, items, none, 0, q_idx, cand, wsb, st,
+    return launch_select(d, w, batch, items, none, 0, q_idx, cand, wsb, st, any_new,
                          reinterpret_cast<float *>(cand + (size_t) batch * d.kb));
 }
 
@@ -556,7 +563,8 @@ qsa_status qsa_shard_attend(const qsa_desc * dd, const qsa_decode_item * items, 
     if (e == cudaErrorInvalidValue) return QSA_ERR_UNSUPPORTED;       // too many candidates for one CTA
     if (e != cudaSuccess) return QSA_ERR_CUDA;
     qsa_layer_cache none{};
-    return launch_attend(d, w, batch, items, none, 0, q, q_type, OutSpec{nullptr, nullptr, nullptr, 0}, wsb, st, state);
+    return launch_attend(d, w, batch, items, none, 0, q, q_type, OutSpec{nullptr, nullptr, nullptr, 0}, wsb, st, true,
+                         state);
 }
 
 // ---- KV-sharded decode with the indexer caches replicated on every rank
@@ -591,8 +599,9 @@ qsa_status qsa_shard_decode_ri(const qsa_desc * dd, const qsa_decode_item * item
         if ((s = launch_append_decode(d, st, batch, items, k_new, v_new, kidx_new,
                                       reinterpret_cast<uint32_t *>(wsb + w.status))) != QSA_OK) return s;
     qsa_layer_cache none{};
-    if ((s = launch_select(d, w, batch, items, none, 0, q_idx, sel_out, wsb, st)) != QSA_OK) return s;
-    return launch_attend(d, w, batch, items, none, 0, q, q_type, OutSpec{nullptr, nullptr, nullptr, 0}, wsb, st, state);
+    if ((s = launch_select(d, w, batch, items, none, 0, q_idx, sel_out, wsb, st, any_new)) != QSA_OK) return s;
+    return launch_attend(d, w, batch, items, none, 0, q, q_type, OutSpec{nullptr, nullptr, nullptr, 0}, wsb, st, true,
+                         state);
 }
 
 qsa_status qsa_merge_states(const qsa_desc * dd, int32_t n_parts, int32_t batch, const float * states, float * out,

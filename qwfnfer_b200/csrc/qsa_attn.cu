@@ -789,7 +789,7 @@ int attn_resident_ctas(int type_k) {
     return 148 * (type_k == QSA_TYPE_Q8_0 ? AttnCfg<QSA_TYPE_Q8_0>::MIN_CTAS : AttnCfg<QSA_TYPE_F16>::MIN_CTAS);
 }
 
-cudaError_t launch_attn(const DevDesc & d, cudaStream_t st, int n_q, const qsa_decode_item * items,
+cudaError_t launch_attn(const DevDesc & d, cudaStream_t st, bool chained, int n_q, const qsa_decode_item * items,
         qsa_layer_cache cache0, int n_past0, const void * q, int q_type, const int * sel_ws, const int * nsel_ws,
         int tiles_per_cta, int max_chunks, float * part_o, float * part_ml, OutSpec outs, uint32_t * status,
         float * state_out) {
@@ -801,7 +801,7 @@ cudaError_t launch_attn(const DevDesc & d, cudaStream_t st, int n_q, const qsa_d
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;   // prologue overlaps the select
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = chained ? 1 : 0;     // the first kernel of a call waits for all earlier work
     cudaError_t e;
     cfg.dynamicSmemBytes = d.type_k == QSA_TYPE_Q8_0 ? attn_smem_bytes<QSA_TYPE_Q8_0>(d.kb) : attn_smem_bytes<QSA_TYPE_F16>(d.kb);
 #define QSA_LAUNCH_ATTN(T, N) cudaLaunchKernelEx(&cfg, attn_kernel<T, N>, d, items, cache0, n_past0, q, q_type, sel_ws, \
@@ -811,6 +811,7 @@ cudaError_t launch_attn(const DevDesc & d, cudaStream_t st, int n_q, const qsa_d
 #undef QSA_LAUNCH_ATTN
     if (e != cudaSuccess || max_chunks <= 1) return e;
     cudaLaunchConfig_t mc = cfg;
+    mc.numAttrs = 1;                    // the merge follows the attention of this call
     if (max_chunks <= MERGE_SMALL_CHUNKS) {
         mc.gridDim = dim3((unsigned) n_q);
         mc.blockDim = dim3(MERGE_SMALL_THREADS);

@@ -45,8 +45,10 @@ size_t decode_workspace_zero_prefix(const qsa_desc * d, int32_t batch, int32_t m
 DevDesc dev_desc(const qsa_desc * d);
 
 // Host launcher of the attention kernel and, when a query spans several CTAs (max_chunks > 1),
-// of the merge of their partials (defined beside the kernels).
-cudaError_t launch_attn(const DevDesc & d, cudaStream_t st, int n_q, const qsa_decode_item * items,
+// of the merge of their partials (defined beside the kernels).  chained: a kernel of the same call
+// precedes the attention, which may then start early (programmatic launch); otherwise it is an
+// ordinary launch that waits for all earlier work in the stream.
+cudaError_t launch_attn(const DevDesc & d, cudaStream_t st, bool chained, int n_q, const qsa_decode_item * items,
         qsa_layer_cache cache0, int n_past0, const void * q, int q_type, const int * sel_ws, const int * nsel_ws,
         int tiles_per_cta, int max_chunks, float * part_o, float * part_ml, OutSpec outs, uint32_t * status,
         float * state_out);
