@@ -108,9 +108,10 @@ qsa_status set_attrs() {
 // Launch chaining.  Kernels after the first of a call are launched programmatically: they may
 // start before the kernel ahead of them ends, and read what it writes only after pdl_wait, but
 // read the call's inputs (items, q, q_idx, caches) at once.  That is safe because the first kernel
-// of every call is an ordinary launch, which starts only once all earlier work in the stream is
-// complete, whatever that work is (the caller's kernels, qsa_stage_copy, another call).
-// `chained`: a kernel of the same call precedes this launch.
+// of every call starts its dependents only once all earlier work in the stream is complete,
+// whatever that work is (the caller's kernels, qsa_stage_copy, another call): it is an ordinary
+// launch, or (the decode append) it waits for the kernel ahead before it reads anything or
+// triggers.  `chained`: a kernel of the same call precedes this launch.
 
 // Scores + selection into the workspace (and sel_out).  Sharded (cand_scores != null): scores of
 // the shard's blocks only, and its candidates with their scores in sel_out / cand_scores.
@@ -312,11 +313,23 @@ namespace {
 // before it in the stream (whatever wrote the items, q_idx and the new rows) is then complete
 // when the chain starts, which the selection relies on: launched behind the append, it reads
 // the items and q_idx before its own griddepcontrol.wait.
+// The first kernel of its call, yet a programmatic launch: its launch overlaps the kernel ahead,
+// and it waits for that kernel before it reads anything.  Waiting on the kernel ahead covers all
+// earlier work in the stream, as that kernel completes only after its own predecessors (an
+// ordinary launch starts after them; a programmatic one waits for them before it exits).
 qsa_status launch_append_decode(const DevDesc & d, cudaStream_t st, int batch, const qsa_decode_item * items,
                                 const float * k_new, const float * v_new, const float * kidx_new, uint32_t * status) {
-    append_decode_kernel<<<batch, APPEND_DECODE_THREADS, append_decode_smem(d), st>>>(d, items, k_new, v_new, kidx_new,
-                                                                                     status);
-    return cuda_status(cudaGetLastError());
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(batch);
+    cfg.blockDim = dim3(APPEND_DECODE_THREADS);
+    cfg.dynamicSmemBytes = append_decode_smem(d);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cuda_status(cudaLaunchKernelEx(&cfg, append_decode_kernel, d, items, k_new, v_new, kidx_new, status));
 }
 
 qsa_status decode_common(const qsa_desc * dd, const qsa_decode_item * items, int32_t batch, int32_t max_n_kv,

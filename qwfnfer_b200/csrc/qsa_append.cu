@@ -159,10 +159,14 @@ __global__ void __launch_bounds__(256) pool_blocks_kernel(DevDesc d, const uint1
 // pooled key is ever read, an incomplete block being forced by the bias).  The block's raw-key
 // rows are staged into shared memory in one round of loads, then summed in order by one warp.
 constexpr int APPEND_THREADS = 1024;
-__global__ void __launch_bounds__(APPEND_THREADS) append_decode_kernel(DevDesc d, const qsa_decode_item * __restrict__ items,
-        const float * __restrict__ k, const float * __restrict__ v, const float * __restrict__ kidx,
-        uint32_t * __restrict__ status) {
+// The inputs are plain pointers (no __restrict__): loads through a const __restrict__ pointer may
+// be hoisted above the wait.
+__global__ void __launch_bounds__(APPEND_THREADS) append_decode_kernel(DevDesc d, const qsa_decode_item * items,
+        const float * k, const float * v, const float * kidx, uint32_t * __restrict__ status) {
     extern __shared__ __align__(16) unsigned char dyn_smem[];
+    // Launched programmatically behind whatever precedes the call: nothing is read before the
+    // kernel ahead has completed (it, in turn, completes only after everything before it).
+    pdl_wait();
     pdl_trigger();
     const int s = blockIdx.x;
     qsa_decode_item it = items[s];

@@ -223,9 +223,9 @@ class QsaDecodeStep:
     the engine submits one compute graph per step to its backend (src/qwfn_engine.cpp:814).
 
     A replay is qsa_stage_copy of the step's packed pinned host buffer to the device (the item
-    table with this token's positions, then q, q_idx, k_new, v_new, kidx_new), qsa_decode, and
-    qsa_stage_copy of the output to pinned host memory: kernels on the compute engine at both ends,
-    no copy-engine hand-over.  Between replays: wait(), write the inputs (the views in `host`,
+    table with this token's positions, then q, q_idx, k_new, v_new, kidx_new) and qsa_decode,
+    whose last kernel stores the output straight into pinned host memory (mapped at its host
+    address): kernels on the compute engine only, no copy-engine hand-over.  Between replays: wait(), write the inputs (the views in `host`,
     or a packed row through load()) and the positions (set_positions()), run(), then read
     `host_out` once the stream has synchronised (run(sync=True) does that)."""
 
@@ -259,7 +259,6 @@ class QsaDecodeStep:
             table[i].cache = c
         self.host["items"].copy_(torch.frombuffer(bytearray(bytes(table)), dtype=torch.uint8))
         self._n_past = self.host["items"].view(torch.int32).view(B, item_bytes // 4)[:, QsaDecodeItem.n_past.offset // 4]
-        self.out = torch.empty((B, d.n_head, d.head_dim), dtype=torch.float32, device=node.device)
         self.host_out = torch.empty((B, d.n_head, d.head_dim), dtype=torch.float32).pin_memory()
         self.sel = torch.empty((B, node.kb), dtype=torch.int32, device=node.device) if sel_out else None
         self.ws = node.workspace("decode", B, self.max_n_kv)
@@ -288,10 +287,8 @@ class QsaDecodeStep:
         q_type = TYPE_BF16 if self.q_dtype == torch.bfloat16 else TYPE_F32
         check(lib().qsa_decode(ctypes.byref(d), self.dev_in.data_ptr(), self.batch, self.max_n_kv,
                                dv["q"].data_ptr(), q_type, dv["q_idx"].data_ptr(), dv["k_new"].data_ptr(),
-                               dv["v_new"].data_ptr(), dv["kidx_new"].data_ptr(), self.out.data_ptr(),
+                               dv["v_new"].data_ptr(), dv["kidx_new"].data_ptr(), self.host_out.data_ptr(),
                                _ptr(self.sel), self.ws.data_ptr(), self.ws.numel(), st), "qsa_decode")
-        check(lib().qsa_stage_copy(self.host_out.data_ptr(), self.out.data_ptr(),
-                                   self.out.numel() * self.out.element_size(), st), "qsa_stage_copy (output)")
 
     def run(self, sync: bool = False) -> torch.Tensor:
         """Replay the step on the current stream (captured on first use); returns host_out."""
