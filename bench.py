@@ -610,27 +610,37 @@ def run_ours_config3(args, ws, rank, local):
     torch.cuda.synchronize()
     clocks.mark("t1")
     attn_us = _timed_replays(g_attn, K, before)
-    # e2e: the public call with this rank's inputs copied from pinned host memory and the outputs back
-    hins = [tuple(x.cpu().pin_memory() for x in t) for t in ins]
-    hout = torch.empty(B, d.n_head, d.head_dim).pin_memory()
-    stream = torch.cuda.current_stream()
+    # e2e through the public QsaDecodeStep: per step, this rank's packed pinned host rows (item
+    # table with the positions, q, q_idx, k, v, kidx of every sequence) staged in by a kernel,
+    # qsa_decode, and the output stored by its last kernel into pinned host memory
+    dstep = node.decode_step([st.layer() for st in states], max_n_kv)
+    dstep.set_positions(positions)
+    rows = []
+    for s_ in range(S):
+        for name, x in zip(("q", "q_idx", "k_new", "v_new", "kidx_new"), ins[s_]):
+            dstep.host[name].copy_(x.cpu())
+        rows.append(dstep.host_in[dstep.input_offset:].clone().pin_memory())
+    for s_ in range(max(args.warmup, 3)):
+        dstep.wait()
+        dstep.load(rows[s_ % S])
+        dstep.run()
     e2e = []
     for i in range(K):
+        dstep.wait()
+        dstep.load(rows[i % S])
         flush.zero_()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
-        for dst, src in zip((sq, sqi, sk, sv, ski), hins[i % S]):
-            dst.copy_(src, non_blocking=True)
-        step_api(stream.cuda_stream)
-        hout.copy_(out, non_blocking=True)
+        dstep.run()
         b.record()
         e2e.append((a, b))
     torch.cuda.synchronize()
     e2e_us = [a.elapsed_time(b) * 1e3 for a, b in e2e]
     clocks.stop()
     check(node.check(wsb), "qsa_check")
-    h2d = sum(x.numel() * x.element_size() for x in ins[0])
-    d2h = out.numel() * out.element_size()
+    check(node.check(dstep.ws), "qsa_check (e2e step)")
+    h2d = dstep.row_bytes
+    d2h = dstep.host_out.numel() * dstep.host_out.element_size()
     sel_h = sel.cpu().numpy()
     cells = sum(attended_cells(sel_h[t], positions[t], d.ratio) for t in range(B))
     attn_bytes = cells * 2 * 544 + sum(x.numel() * x.element_size() for x in (sq, out)) + B * KB * 4
