@@ -292,26 +292,27 @@ class ShardedDecoder:
                             None if kidx is None else kidx[sl])
 
     def step(self, items, batch: int, max_n_kv: int, q, q_idx, k_new=None, v_new=None, kidx_new=None,
-             sel_out: torch.Tensor | None = None) -> torch.Tensor:
+             sel_out: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
         """One decode step of one layer for `batch` queries (items: this rank's device item table,
-        global n_past, local caches).  Returns f32 [batch, n_head, head_dim] on every rank."""
+        global n_past, local caches).  Returns f32 [batch, n_head, head_dim] on every rank, in `out`
+        when given (device memory, or pinned host memory: the last kernel stores into it)."""
         if self.comm:
-            return self._step_capi(items, batch, max_n_kv, q, q_idx, k_new, v_new, kidx_new, sel_out)
+            return self._step_capi(items, batch, max_n_kv, q, q_idx, k_new, v_new, kidx_new, sel_out, out)
         if self.index_replicated:
             state = self.backend.decode_ri(items, batch, max_n_kv, self.blocks, q, q_idx, k_new, v_new, kidx_new,
                                            sel_out=sel_out)
             channel = 1 + (self._steps & 1)
             self._steps += 1
             states, _ = self._all_gather(state, channel)
-            return self.backend.merge(states.view(self.world, batch, -1))
+            return self.backend.merge(states.view(self.world, batch, -1), out)
         cand = self.backend.candidates(items, batch, max_n_kv, self.blocks, q_idx, k_new, v_new, kidx_new)
         gathered, cstride = self._all_gather(cand, 0)
         state = self.backend.attend(items, batch, max_n_kv, self.blocks, gathered, q, sel_out=sel_out,
                                     n_shards=self.world, cand_stride=cstride)
         states, _ = self._all_gather(state, 1)
-        return self.backend.merge(states.view(self.world, batch, -1))
+        return self.backend.merge(states.view(self.world, batch, -1), out)
 
-    def _step_capi(self, items, batch, max_n_kv, q, q_idx, k_new, v_new, kidx_new, sel_out):
+    def _step_capi(self, items, batch, max_n_kv, q, q_idx, k_new, v_new, kidx_new, sel_out, out=None):
         """The step as one qsa_decode_sharded call (its all-gathers on the NCCL communicator)."""
         d = self.desc
         L = lib()
@@ -325,7 +326,8 @@ class ShardedDecoder:
             ws = torch.empty(size, dtype=torch.uint8, device=self.backend.device)
             check(L.qsa_workspace_init(ws.data_ptr(), size, stream), "qsa_workspace_init")
             self.backend._ws[("capi", size)] = ws
-        out = torch.empty((batch, d.n_head, d.head_dim), dtype=torch.float32, device=self.backend.device)
+        if out is None:
+            out = torch.empty((batch, d.n_head, d.head_dim), dtype=torch.float32, device=self.backend.device)
         q_type = TYPE_BF16 if q.dtype == torch.bfloat16 else TYPE_F32
         check(L.qsa_decode_sharded(ctypes.byref(d), _ptr(items), batch, max_n_kv, self.blocks[0], self.blocks[1],
                                    1 if self.index_replicated else 0, self.comm, self.world, _ptr(q), q_type,

@@ -91,5 +91,9 @@ class OracleShardBackend:
             states[t] = oracle.attend_state(d, self.kc, self.vc, [qp - lo * r], local, q_np[t:t + 1], q_type)[0]
         return torch.from_numpy(states)
 
-    def merge(self, states):
-        return torch.from_numpy(oracle.merge_states(self.d, states.numpy()))
+    def merge(self, states, out=None):
+        merged = torch.from_numpy(oracle.merge_states(self.d, states.numpy()))
+        if out is None:
+            return merged
+        out.copy_(merged.view_as(out))
+        return out
