@@ -119,12 +119,14 @@ qsa_status launch_select(const DevDesc & d, const WsLayout & w, int n_q, const q
                          qsa_layer_cache cache0, int n_past0, const float * q_idx, int32_t * sel_out,
                          unsigned char * ws, cudaStream_t st, bool chained, float * cand_scores = nullptr) {
     uint32_t * status = reinterpret_cast<uint32_t *>(ws + w.status);
-    // blocks per scoring CTA: one row pair per warp while the grid fits one wave, more once it
-    // would not (a CTA holds a whole SM's registers: one wave is 148 CTAs)
+    // blocks per scoring CTA: the fewest (whole row pairs of every warp, at least one) that keep
+    // the batch's scoring grid within one wave (a CTA holds a whole SM's registers: one wave is
+    // 148 CTAs); a second wave would start its CTAs only when the first leaves
     const int lo = d.shard_ri ? 0 : d.shard_blk0, hi = d.shard_ri ? INT_MAX : d.shard_blk1;
     const int n_blk = std::max(1, std::min(w.scores_stride, hi) - lo);   // blocks scored
-    int bpc = 2 * (SEL_THREADS_HOST / 32);                 // one row pair per warp
-    while (bpc < 1024 && (int64_t) ceil_div(n_blk, bpc) * n_q > 148) bpc *= 2;
+    constexpr int PAIRS = 2 * (SEL_THREADS_HOST / 32);                   // one row pair per warp
+    const int per_q = std::max(1, 148 / n_q);                            // CTAs per query
+    const int bpc = std::max(PAIRS, ceil_div(ceil_div(n_blk, per_q), PAIRS) * PAIRS);
     const int score_ctas = ceil_div(n_blk, bpc);
     // the scores, then one ballot word per 32 candidates (and per selecting warp, its last round)
     const size_t sel_smem = (size_t) w.scores_stride * 4 + ((size_t) ceil_div(w.scores_stride, 32) + SEL_THREADS_HOST / 32) * 4;

@@ -21,7 +21,7 @@ constexpr int SEL_THREADS = SEL_THREADS_HOST;
 // warp on SCORE_U row pairs at a time (their loads in flight together).  Products of two f16
 // values are exact in f32; they are summed in double (exact for these magnitudes) and rounded
 // once, so the result does not depend on the summation order.
-constexpr int SCORE_U = 4;
+constexpr int SCORE_U = 8;
 
 // This warp's rows of the batch at b0 (rows b0 + u*step + half); pooled keys the append before
 // this grid may have written, read after its pdl_wait.
