@@ -721,13 +721,20 @@ def run_ours_config5(args, ws, rank, local):
             dec.step(items[il], 1, n_past + 1, q[il:il + 1], qi[il:il + 1], k[il:il + 1], v[il:il + 1],
                      ki[il:il + 1], sel_out=sel[il:il + 1], out=None if out is None else out[il:il + 1])
 
+    # Tokens per graph replay.  The replicated-index step's state exchange alternates two peer
+    # channels per step, so that a rank's push of step s+1 lands only after the peer read step s;
+    # a graph fixes the channel of every step it holds, so one of a single step would reuse one
+    # channel every replay.  The 12 layers after one another already alternate inside the graph;
+    # the batched step is captured twice.
+    reps = 2 if lb else 1
     for s in range(args.warmup):
         load(s)
         step()
     torch.cuda.synchronize()
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g, capture_error_mode="thread_local"):
-        step()
+        for _ in range(reps):
+            step()
     # the attention stage alone (the dominant kernel), on this rank's share: layer 0, or all 12
     # layers in one launch with --layer-batch (with replicated indexer caches: selection + attention)
     a_items, a_b = (items_all, NL) if lb else (items[0], 1)
@@ -773,22 +780,25 @@ def run_ours_config5(args, ws, rank, local):
     for x in ins[0]:
         offs.append(o)
         o += (x.numel() * x.element_size() + 15) // 16 * 16
-    dev_in = torch.empty(o, dtype=torch.uint8, device=dev)
-    host_in = torch.empty(o, dtype=torch.uint8).pin_memory()
-    e_slots = [dev_in[off:off + x.numel() * x.element_size()].view(x.dtype).view(x.shape) for x, off in zip(ins[0], offs)]
+    dev_in = torch.empty(reps, o, dtype=torch.uint8, device=dev)
+    host_in = torch.empty(reps, o, dtype=torch.uint8).pin_memory()
+    e_slots = [[dev_in[r_, off:off + x.numel() * x.element_size()].view(x.dtype).view(x.shape)
+                for x, off in zip(ins[0], offs)] for r_ in range(reps)]
     rows = []
     for t_ in ins:
         r = torch.zeros(o, dtype=torch.uint8)
         for x, off in zip(t_, offs):
             r[off:off + x.numel() * x.element_size()].copy_(x.contiguous().view(torch.uint8).reshape(-1).cpu())
         rows.append(r.pin_memory())
-    hout = torch.empty(NL, d.n_head, d.head_dim).pin_memory()
+    hout = torch.empty(reps, NL, d.n_head, d.head_dim).pin_memory()
 
     def step_e2e():
-        check(L.qsa_stage_copy(dev_in.data_ptr(), host_in.data_ptr(), o, _stream(None)), "qsa_stage_copy")
-        step(e_slots, hout)
+        for r_ in range(reps):               # each token's row staged, its step, its outputs stored to the host
+            check(L.qsa_stage_copy(dev_in[r_].data_ptr(), host_in[r_].data_ptr(), o, _stream(None)), "qsa_stage_copy")
+            step(e_slots[r_], hout[r_])
 
-    host_in.copy_(rows[0])
+    for r_ in range(reps):
+        host_in[r_].copy_(rows[r_])
     step_e2e()
     torch.cuda.synchronize()
     g_e2e = torch.cuda.CUDAGraph()
@@ -797,7 +807,8 @@ def run_ours_config5(args, ws, rank, local):
     e2e = []
     for i in range(K):
         torch.cuda.synchronize()               # the previous token's output is back before its successor is written
-        host_in.copy_(rows[i % S])
+        for r_ in range(reps):
+            host_in[r_].copy_(rows[(reps * i + r_) % S])
         flush.zero_()
         if ws > 1:
             torch.distributed.barrier()
@@ -823,8 +834,8 @@ def run_ours_config5(args, ws, rank, local):
     attn_mean = statistics.mean(attn_us)
     hbm, _, src = peaks()
     achieved = attn_bytes / (attn_mean * 1e-6) / 1e9
-    total_us = max_over_ranks(statistics.mean(step_us), ws)
-    e2e_max = max_over_ranks(statistics.mean(e2e_us), ws)
+    total_us = max_over_ranks(statistics.mean(step_us), ws) / reps
+    e2e_max = max_over_ranks(statistics.mean(e2e_us), ws) / reps
     res = {
         "metric": "sparse-attn decode us/layer @1M q8_0, 12 layers, KV-sequence-sharded",
         "value": round(total_us / NL, 3), "unit": "us/layer-token", "n_gpus": ws, "steps": K,
@@ -841,14 +852,15 @@ def run_ours_config5(args, ws, rank, local):
                                    + (", indexer caches replicated" if dec.index_replicated else "")
                                    + ")") if ws > 1 else "1 GPU",
                    "blocks_per_gpu": hi - lo,
-                   "l2": "flushed (256 MB write) before every timed step", "cuda_graph": True},
+                   "l2": "flushed (256 MB write) before every timed step", "cuda_graph": True,
+                   "tokens_per_replay": reps},
         "roofline": {"bound": "hbm", "kernel": "attn_kernel<q8_0> (qsa_shard_attend), "
                                + ("all 12 layers in one launch" if lb else "layer 0") + ", rank 0",
                      "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
                      "peak_source": f"{src} hbm_gbs (burst)", "traffic": None,
                      "algorithmic_bytes_per_launch": attn_bytes, "launch_us": round(attn_mean, 3)},
         "step_roofline": {"algorithmic_bytes_per_gpu": step_bytes,
-                          "achieved_gbs": round(step_bytes / (statistics.mean(step_us) * 1e-6) / 1e9, 1)},
+                          "achieved_gbs": round(step_bytes / (statistics.mean(step_us) / reps * 1e-6) / 1e9, 1)},
         "e2e": {"value": round(e2e_max / NL, 3), "unit": "us/layer-token",
                 "h2d_bytes_per_step": sum(x.numel() * x.element_size() for x in ins[0]),
                 "d2h_bytes_per_step": NL * d.n_head * d.head_dim * 4},

@@ -231,7 +231,12 @@ class ShardedDecoder:
         index: "sharded"
         (each rank holds its blocks' raw and pooled keys; candidates are exchanged) or "replicated"
         (every rank holds all of them, QsaState(index_full=True), and selects globally itself: one
-        exchange per step)."""
+        exchange per step).
+
+        With the peer exchange and replicated indexer caches, consecutive steps alternate two state
+        channels (a rank's push of step s+1 lands only after its peers read step s).  A CUDA graph
+        fixes each captured step's channel, so a graph replayed back to back must hold an even
+        number of steps."""
         if index not in ("sharded", "replicated"):
             raise ValueError("index is 'sharded' or 'replicated'")
         self.index_replicated = index == "replicated"
