@@ -848,7 +848,10 @@ def run_ours_config5(args, ws, rank, local):
                                   "exchange per token for all layers)" if lb else ", layer after layer"),
                    "global_batch": 1, "seq_len": n_past + 1, "layers": NL,
                    "parallelism": (f"KV-sequence-sharded x{ws} ("
-                                   + ("NVLink peer-memory all-gathers" if args.exchange == "peer" else "NCCL all-gathers")
+                                   + {"peer": "NVLink peer memory: states stored by the attention, published by flag"
+                                      if dec.index_replicated else "NVLink peer-memory all-gathers",
+                                      "peer_push": "NVLink peer-memory all-gathers",
+                                      "nccl": "NCCL all-gathers"}[args.exchange]
                                    + (", indexer caches replicated" if dec.index_replicated else "")
                                    + ")") if ws > 1 else "1 GPU",
                    "blocks_per_gpu": hi - lo,
@@ -1088,7 +1091,7 @@ def main():
     ap.add_argument("--index", default="replicated", choices=["sharded", "replicated"],
                     help="config 5: the indexer caches replicated on every rank (one state exchange per layer) or "
                          "sharded with the K/V (candidates exchanged too)")
-    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+    ap.add_argument("--exchange", default="peer", choices=["peer", "peer_push", "nccl"],
                     help="config 5 with N > 1: the shards' exchanges over NVLink peer memory or NCCL")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)

@@ -310,6 +310,33 @@ qsa_status qsa_peer_push(void * const * bufs, int32_t n_ranks, int32_t rank, con
 qsa_status qsa_peer_wait(const void * local_buf, int32_t n_ranks, size_t slot_bytes, const uint32_t * epoch,
                          void * ws, size_t ws_bytes, qsa_stream_t stream);
 
+/* The replicated-index step with its state exchange fused into the kernels (no push or wait
+ * launch): one channel of the peer buffers above, as this rank sees it.  region[p] is rank p's
+ * gather buffer of the channel (this rank's own, or its CUDA IPC mapping), laid out as
+ * qsa_peer_buffer_bytes(n_ranks, slot_bytes) with slot_bytes = batch * qsa_shard_state_floats * 4;
+ * epoch is this rank's zeroed device counter of the channel.  At most 8 ranks. */
+typedef struct qsa_peer_slots {
+    void * region[8];
+    int32_t n_ranks;
+    int32_t rank;
+    uint32_t * epoch;
+} qsa_peer_slots;
+
+/* qsa_shard_decode_ri whose attention (or its merge) stores this rank's state into slot `rank` of
+ * every region over NVLink, after which a one-warp kernel publishes it (the channel's next epoch,
+ * a system-scope release flag in every region).  qsa_merge_states_peer then waits (bounded:
+ * QSA_ERR_TIMEOUT through the status word of `ws`, at least 16 bytes, read by qsa_check) until
+ * every rank's state of the round is in this rank's region and merges them in rank order into out
+ * (f32 [batch][n_head][head_dim]).  Consecutive steps alternate two channels, as for
+ * qsa_peer_push: a rank stores into a channel again only after every peer has read it. */
+qsa_status qsa_shard_decode_ri_peer(const qsa_desc * d, const qsa_decode_item * items, int32_t batch, int32_t max_n_kv,
+                                    int32_t blk_lo, int32_t blk_hi, const void * q, int32_t q_type, const float * q_idx,
+                                    const float * k_new, const float * v_new, const float * kidx_new,
+                                    const qsa_peer_slots * slots, int32_t * sel_out, void * ws, size_t ws_bytes,
+                                    qsa_stream_t stream);
+qsa_status qsa_merge_states_peer(const qsa_desc * d, const qsa_peer_slots * slots, int32_t batch, float * out,
+                                 void * ws, size_t ws_bytes, qsa_stream_t stream);
+
 /* ------------------------------------------------------------------ prefill */
 size_t qsa_prefill_workspace_size(const qsa_desc * d, int32_t T, int32_t max_n_kv);
 

@@ -191,9 +191,13 @@ def shard5(argv: list[str]) -> None:
     for _ in range(3):
         step()
     torch.cuda.synchronize()
+    # the batched step twice per replay: the replicated-index state exchange alternates two peer
+    # channels per step, which a graph of one step would fix to one
+    reps = 2 if lb else 1
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g, capture_error_mode="thread_local"):
-        step()
+        for _ in range(reps):
+            step()
     for _ in range(5):
         g.replay()
     torch.cuda.synchronize()
@@ -222,7 +226,7 @@ def shard5(argv: list[str]) -> None:
         for i, (n, a, b) in enumerate(s_):
             rows.setdefault(f"{i:02d} {n.split('(')[0]}", []).append((a - t0, b - a))
     lines = [f"rank {rank} of {ws}, exchange {exchange}, {'12 layers as one batch' if lb else 'layer after layer'}: "
-             f"step {statistics.median(spans):.1f} us (median of {len(spans)})"]
+             f"replay of {reps} token(s) {statistics.median(spans):.1f} us (median of {len(spans)})"]
     for key, vals in list(rows.items())[:64]:
         lines.append(f"  {key:48s} start {statistics.median([x for x, _ in vals]):8.1f} us  "
                      f"duration {statistics.median([y for _, y in vals]):7.1f} us")

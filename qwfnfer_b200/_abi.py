@@ -52,6 +52,13 @@ class QsaDecodeItem(ctypes.Structure):
                 ("reserved", ctypes.c_int32 * 3)]
 
 
+class QsaPeerSlots(ctypes.Structure):
+    """struct qsa_peer_slots: one channel of the NVLink peer exchange (every rank's gather region
+    of it in this process, the rank count and index, this rank's epoch counter of the channel)."""
+    _fields_ = [("region", ctypes.c_void_p * 8), ("n_ranks", ctypes.c_int32), ("rank", ctypes.c_int32),
+                ("epoch", ctypes.c_void_p)]
+
+
 class QsaFrontWeights(ctypes.Structure):
     """struct qsa_front_weights (include/qsa.h)."""
     _fields_ = [("wq", ctypes.c_void_p), ("wk", ctypes.c_void_p), ("wv", ctypes.c_void_p),
@@ -160,6 +167,9 @@ def lib() -> ctypes.CDLL:
         "qsa_peer_buffer_bytes": (SZ, [I32, SZ]),
         "qsa_peer_push": (I32, [VP, I32, I32, VP, SZ, VP, VP, VP]),
         "qsa_peer_wait": (I32, [VP, I32, SZ, VP, VP, SZ, VP]),
+        "qsa_shard_decode_ri_peer": (I32, [D, VP, I32, I32, I32, I32, VP, I32, VP, VP, VP, VP, P(QsaPeerSlots), VP, VP,
+                                           SZ, VP]),
+        "qsa_merge_states_peer": (I32, [D, P(QsaPeerSlots), I32, VP, VP, SZ, VP]),
         "qsa_prefill_workspace_size": (SZ, [D, I32, I32]),
         "qsa_prefill": (I32, [D, C, I32, I32, VP, I32, VP, VP, VP, VP, VP, VP, VP, SZ, VP]),
         "qsa_check": (I32, [VP, SZ, VP]),
@@ -194,6 +204,7 @@ HEADER_SYMBOLS = [
     "qsa_shard_append_ri", "qsa_shard_decode_ri",
     "qsa_merge_states", "qsa_decode_sharded_workspace_size", "qsa_decode_sharded",
     "qsa_ipc_handle", "qsa_ipc_open", "qsa_ipc_close", "qsa_peer_buffer_bytes", "qsa_peer_push", "qsa_peer_wait",
+    "qsa_shard_decode_ri_peer", "qsa_merge_states_peer",
     "qsa_prefill_workspace_size", "qsa_prefill", "qsa_front_workspace_size", "qsa_front", "qsa_output_workspace_size", "qsa_output",
     "qsa_decode_gated", "qsa_prefill_gated", "qsa_output_z",
     "qsa_gguf_read_hparams", "qsa_gguf_is_qsa_layer", "qsa_gguf_layer_desc",

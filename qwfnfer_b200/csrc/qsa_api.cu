@@ -146,15 +146,22 @@ qsa_status launch_select(const DevDesc & d, const WsLayout & w, int n_q, const q
         reinterpret_cast<int *>(ws + w.sel), reinterpret_cast<int *>(ws + w.nsel), sel_out, status, cand_scores));
 }
 
+// The states of a sharded step in one array (null: none, the output instead).
+StateDst local_states(float * p) {
+    StateDst s{};
+    if (p) { s.base[0] = p; s.n = 1; }
+    return s;
+}
+
 // Attention over the selection held in the workspace (and the merge of split queries).
 qsa_status launch_attend(const DevDesc & d, const WsLayout & w, int n_q, const qsa_decode_item * items,
                          qsa_layer_cache cache0, int n_past0, const void * q, int q_type, OutSpec out,
-                         unsigned char * ws, cudaStream_t st, bool chained, float * state_out = nullptr) {
+                         unsigned char * ws, cudaStream_t st, bool chained, const StateDst & sdst = StateDst{}) {
     return cuda_status(launch_attn(d, st, chained, n_q, items, cache0, n_past0, q, q_type,
                                    reinterpret_cast<const int *>(ws + w.sel), reinterpret_cast<const int *>(ws + w.nsel),
                                    w.tiles_per_cta, w.max_chunks, reinterpret_cast<float *>(ws + w.part_o),
                                    reinterpret_cast<float *>(ws + w.part_ml), out,
-                                   reinterpret_cast<uint32_t *>(ws + w.status), state_out));
+                                   reinterpret_cast<uint32_t *>(ws + w.status), sdst));
 }
 
 }  // namespace
@@ -579,7 +586,7 @@ qsa_status qsa_shard_attend(const qsa_desc * dd, const qsa_decode_item * items, 
     if (e != cudaSuccess) return QSA_ERR_CUDA;
     qsa_layer_cache none{};
     return launch_attend(d, w, batch, items, none, 0, q, q_type, OutSpec{nullptr, nullptr, nullptr, 0}, wsb, st, true,
-                         state);
+                         local_states(state));
 }
 
 // ---- KV-sharded decode with the indexer caches replicated on every rank
@@ -616,7 +623,71 @@ qsa_status qsa_shard_decode_ri(const qsa_desc * dd, const qsa_decode_item * item
     qsa_layer_cache none{};
     if ((s = launch_select(d, w, batch, items, none, 0, q_idx, sel_out, wsb, st, any_new)) != QSA_OK) return s;
     return launch_attend(d, w, batch, items, none, 0, q, q_type, OutSpec{nullptr, nullptr, nullptr, 0}, wsb, st, true,
-                         state);
+                         local_states(state));
+}
+
+// ---- the replicated-index step with its state exchange fused into the kernels
+namespace {
+// This rank's slot and flag in every region of the channel, for `batch` states.
+bool peer_targets(const qsa_peer_slots * ps, int batch, StateDst & sd, uint32_t * flag[MAX_STATE_DST],
+                  size_t & stride) {
+    if (!ps || ps->n_ranks <= 0 || ps->n_ranks > MAX_STATE_DST || ps->rank < 0 || ps->rank >= ps->n_ranks || !ps->epoch)
+        return false;
+    stride = ((size_t) batch * attn_state_rows() * (2 + HEAD_DIM) * 4 + 15) & ~(size_t) 15;
+    sd = StateDst{};
+    for (int p = 0; p < ps->n_ranks; p++) {
+        unsigned char * r = static_cast<unsigned char *>(ps->region[p]);
+        if (!r || reinterpret_cast<uintptr_t>(r) % 16 != 0) return false;
+        sd.base[p] = reinterpret_cast<float *>(r + (size_t) ps->rank * stride);
+        flag[p] = reinterpret_cast<uint32_t *>(r + (size_t) ps->n_ranks * stride) + ps->rank;
+    }
+    sd.n = ps->n_ranks;
+    return true;
+}
+}  // namespace
+
+qsa_status qsa_shard_decode_ri_peer(const qsa_desc * dd, const qsa_decode_item * items, int32_t batch, int32_t max_n_kv,
+                                    int32_t blk_lo, int32_t blk_hi, const void * q, int32_t q_type, const float * q_idx,
+                                    const float * k_new, const float * v_new, const float * kidx_new,
+                                    const qsa_peer_slots * slots, int32_t * sel_out, void * ws, size_t ws_bytes,
+                                    qsa_stream_t stream) {
+    DevDesc d; WsLayout w;
+    qsa_status s = shard_common(dd, items, batch, max_n_kv, blk_lo, blk_hi, ws, ws_bytes, d, w);
+    if (s != QSA_OK) return s;
+    d.shard_ri = 1;
+    StateDst sd;
+    uint32_t * flag[MAX_STATE_DST];
+    size_t stride = 0;
+    if (!peer_targets(slots, batch, sd, flag, stride)) return QSA_ERR_INVALID;
+    if (!q || !q_idx || (q_type != QSA_TYPE_BF16 && q_type != QSA_TYPE_F32)) return QSA_ERR_INVALID;
+    const bool any_new = k_new || v_new || kidx_new;
+    if (any_new && !(k_new && v_new && kidx_new)) return QSA_ERR_INVALID;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    unsigned char * wsb = static_cast<unsigned char *>(ws);
+    if (any_new)
+        if ((s = launch_append_decode(d, st, batch, items, k_new, v_new, kidx_new,
+                                      reinterpret_cast<uint32_t *>(wsb + w.status))) != QSA_OK) return s;
+    qsa_layer_cache none{};
+    if ((s = launch_select(d, w, batch, items, none, 0, q_idx, sel_out, wsb, st, any_new)) != QSA_OK) return s;
+    if ((s = launch_attend(d, w, batch, items, none, 0, q, q_type, OutSpec{nullptr, nullptr, nullptr, 0}, wsb, st, true,
+                           sd)) != QSA_OK) return s;
+    return cuda_status(launch_peer_publish(st, flag, slots->n_ranks, slots->epoch));
+}
+
+qsa_status qsa_merge_states_peer(const qsa_desc * dd, const qsa_peer_slots * slots, int32_t batch, float * out,
+                                 void * ws, size_t ws_bytes, qsa_stream_t stream) {
+    qsa_status s = qsa_desc_check(dd);
+    if (s != QSA_OK) return s;
+    StateDst sd;
+    uint32_t * flag[MAX_STATE_DST];
+    size_t stride = 0;
+    if (batch <= 0 || !out || !peer_targets(slots, batch, sd, flag, stride)) return QSA_ERR_INVALID;
+    if (!ws || ws_bytes < 16) return QSA_ERR_WORKSPACE;
+    const unsigned char * local = static_cast<const unsigned char *>(slots->region[slots->rank]);
+    return cuda_status(launch_merge_states(make_dev(dd), reinterpret_cast<cudaStream_t>(stream), slots->n_ranks, batch,
+                                           reinterpret_cast<const float *>(local),
+                                           out, reinterpret_cast<const uint32_t *>(local + (size_t) slots->n_ranks * stride),
+                                           slots->epoch, static_cast<uint32_t *>(ws)));
 }
 
 qsa_status qsa_merge_states(const qsa_desc * dd, int32_t n_parts, int32_t batch, const float * states, float * out,

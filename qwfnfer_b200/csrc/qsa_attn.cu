@@ -98,7 +98,7 @@ __global__ void __launch_bounds__(ATT_THREADS, AttnCfg<KV_TYPE>::MIN_CTAS) attn_
         const void * __restrict__ q, int q_type,
         const int * sel_ws, const int * nsel_ws, int tiles_per_cta, int max_chunks,
         float * __restrict__ part_o, float * __restrict__ part_ml,
-        OutSpec outs, uint32_t * __restrict__ status, float * __restrict__ state_out) {
+        OutSpec outs, uint32_t * __restrict__ status, StateDst sdst) {
     using Cfg = AttnCfg<KV_TYPE>;
     constexpr int NS = Cfg::NSTAGE, HB = Cfg::HB, RB = attn_row_bytes<KV_TYPE>();
     extern __shared__ __align__(128) unsigned char smem[];
@@ -244,12 +244,14 @@ __global__ void __launch_bounds__(ATT_THREADS, AttnCfg<KV_TYPE>::MIN_CTAS) attn_
     const int n_chunks = attn_n_chunks(d, nsel, tiles_per_cta);
     const size_t outq = (size_t) t * d.n_head * HEAD_DIM;     // element offset of query t's output
     // sharded mode: the unnormalised state [M 16][L 16][O 16x256] of query t instead of the output
-    float * stq = state_out ? state_out + (size_t) t * (2 * HROWS + HROWS * HEAD_DIM) : nullptr;
+    const bool stq = sdst.n > 0;
+    const size_t sq0 = (size_t) t * (2 * HROWS + HROWS * HEAD_DIM);      // its offset in the state arrays
     if (n_chunks == 0) {                       // nothing selected (or a bad position): zero output
         if (chunk == 0) {
-            if (stq)
-                for (int i = tid; i < 2 * HROWS + HROWS * HEAD_DIM; i += ATT_THREADS) stq[i] = i < HROWS ? -INFINITY : 0.0f;
-            else
+            if (stq) {
+                for (int i = tid; i < 2 * HROWS + HROWS * HEAD_DIM; i += ATT_THREADS)
+                    state_put(sdst, sq0 + i, i < HROWS ? -INFINITY : 0.0f);
+            } else
                 for (int i = 4 * tid; i < d.n_head * HEAD_DIM; i += 4 * ATT_THREADS)
                     out_store4(outs, outq + i, make_float4(0.f, 0.f, 0.f, 0.f));
         }
@@ -596,7 +598,7 @@ __global__ void __launch_bounds__(ATT_THREADS, AttnCfg<KV_TYPE>::MIN_CTAS) attn_
         if (!single) {
             reinterpret_cast<float4 *>(po)[e4] = acc;
         } else if (stq) {
-            reinterpret_cast<float4 *>(stq + 2 * HROWS)[e4] = acc;
+            state_put4(sdst, sq0 + 2 * HROWS + 4 * (size_t) e4, acc);
         } else if (hr < n_rows && h < d.gqa) {
             const float L = cml[HROWS + hr];
             const float inv = L > 0.0f ? 1.0f / L : 0.0f;
@@ -606,7 +608,7 @@ __global__ void __launch_bounds__(ATT_THREADS, AttnCfg<KV_TYPE>::MIN_CTAS) attn_
     }
     if (tid < 2 * HROWS) {
         if (!single) part_ml[((size_t) t * max_chunks + chunk) * 2 * HROWS + tid] = cml[tid];
-        else if (stq) stq[tid] = cml[tid];
+        else if (stq) state_put(sdst, sq0 + tid, cml[tid]);
     }
 }
 
@@ -623,7 +625,7 @@ template <int PRE>
 __global__ void __launch_bounds__(MERGE_THREADS) attn_merge_kernel(DevDesc d, const qsa_decode_item * __restrict__ items,
         int n_past0, const int * nsel_ws, int tiles_per_cta, int max_chunks,
         const float * part_o, const float * part_ml,
-        OutSpec outs, float * __restrict__ state_out) {
+        OutSpec outs, StateDst sdst) {
     extern __shared__ float wsh[];                    // [max_chunks] weights
     __shared__ float red[2][MERGE_THREADS / 32];
     __shared__ float4 racc[MERGE_GROUPS][MERGE_COLS];
@@ -634,7 +636,7 @@ __global__ void __launch_bounds__(MERGE_THREADS) attn_merge_kernel(DevDesc d, co
     const int qpos = items ? items[t].n_past : n_past0 + t;
     const int g = hr >> 3, h = hr & 7;
     const bool live = g < d.n_head_kv && h < d.gqa;
-    if (!state_out && !live) return;
+    if (sdst.n == 0 && !live) return;
     pdl_wait();                                       // attn_kernel has completed: partials are written
     const bool pos_ok = qpos >= 0 && qpos < d.n_ctx;
     const int nsel = pos_ok ? max(0, min(ld_dep(nsel_ws + t), d.kb)) : 0;
@@ -695,10 +697,10 @@ __global__ void __launch_bounds__(MERGE_THREADS) attn_merge_kernel(DevDesc d, co
             const float4 v = racc[k][tid];
             s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
         }
-        if (state_out) {
-            float * stq = state_out + (size_t) t * (2 * HROWS + HROWS * HEAD_DIM);
-            reinterpret_cast<float4 *>(stq + 2 * HROWS + hr * HEAD_DIM)[d4] = s;
-            if (blockIdx.z == 0 && tid == 0) { stq[hr] = M; stq[HROWS + hr] = L; }
+        if (sdst.n > 0) {
+            const size_t sq0 = (size_t) t * (2 * HROWS + HROWS * HEAD_DIM);
+            state_put4(sdst, sq0 + 2 * HROWS + (size_t) hr * HEAD_DIM + 4 * d4, s);
+            if (blockIdx.z == 0 && tid == 0) { state_put(sdst, sq0 + hr, M); state_put(sdst, sq0 + HROWS + hr, L); }
         } else {
             const float inv = L > 0.0f ? 1.0f / L : 0.0f;
             out_store4(outs, ((size_t) t * d.n_head + g * d.gqa + h) * HEAD_DIM + 4 * d4,
@@ -716,13 +718,13 @@ constexpr int MERGE_SMALL_THREADS = HROWS * HEAD_DIM / 4;
 
 __global__ void __launch_bounds__(MERGE_SMALL_THREADS) attn_merge_small_kernel(DevDesc d,
         const qsa_decode_item * __restrict__ items, int n_past0, const int * nsel_ws, int tiles_per_cta, int max_chunks,
-        const float * part_o, const float * part_ml, OutSpec outs, float * __restrict__ state_out) {
+        const float * part_o, const float * part_ml, OutSpec outs, StateDst sdst) {
     const int t = blockIdx.x, tid = threadIdx.x;
     const int hr = tid / (HEAD_DIM / 4), d4 = tid % (HEAD_DIM / 4);
     const int g = hr >> 3, h = hr & 7;
     const int qpos = items ? items[t].n_past : n_past0 + t;
     const bool live = g < d.n_head_kv && h < d.gqa;
-    if (!state_out && !live) return;
+    if (sdst.n == 0 && !live) return;
     pdl_wait();                                       // attn_kernel has completed: partials are written
     const bool pos_ok = qpos >= 0 && qpos < d.n_ctx;
     const int nsel = pos_ok ? max(0, min(ld_dep(nsel_ws + t), d.kb)) : 0;
@@ -756,10 +758,10 @@ __global__ void __launch_bounds__(MERGE_SMALL_THREADS) attn_merge_small_kernel(D
         L += lc[c] * w;
         acc.x += w * oc[c].x; acc.y += w * oc[c].y; acc.z += w * oc[c].z; acc.w += w * oc[c].w;
     }
-    if (state_out) {
-        float * stq = state_out + (size_t) t * (2 * HROWS + HROWS * HEAD_DIM);
-        reinterpret_cast<float4 *>(stq + 2 * HROWS + hr * HEAD_DIM)[d4] = acc;
-        if (d4 == 0) { stq[hr] = M; stq[HROWS + hr] = L; }
+    if (sdst.n > 0) {
+        const size_t sq0 = (size_t) t * (2 * HROWS + HROWS * HEAD_DIM);
+        state_put4(sdst, sq0 + 2 * HROWS + (size_t) hr * HEAD_DIM + 4 * d4, acc);
+        if (d4 == 0) { state_put(sdst, sq0 + hr, M); state_put(sdst, sq0 + HROWS + hr, L); }
     } else {
         const float inv = L > 0.0f ? 1.0f / L : 0.0f;
         out_store4(outs, ((size_t) t * d.n_head + g * d.gqa + h) * HEAD_DIM + 4 * d4,
@@ -792,7 +794,7 @@ int attn_resident_ctas(int type_k) {
 cudaError_t launch_attn(const DevDesc & d, cudaStream_t st, bool chained, int n_q, const qsa_decode_item * items,
         qsa_layer_cache cache0, int n_past0, const void * q, int q_type, const int * sel_ws, const int * nsel_ws,
         int tiles_per_cta, int max_chunks, float * part_o, float * part_ml, OutSpec outs, uint32_t * status,
-        float * state_out) {
+        const StateDst & sdst) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned) max_chunks, (unsigned) n_q);
     cfg.blockDim = dim3(ATT_THREADS);
@@ -805,7 +807,7 @@ cudaError_t launch_attn(const DevDesc & d, cudaStream_t st, bool chained, int n_
     cudaError_t e;
     cfg.dynamicSmemBytes = d.type_k == QSA_TYPE_Q8_0 ? attn_smem_bytes<QSA_TYPE_Q8_0>(d.kb) : attn_smem_bytes<QSA_TYPE_F16>(d.kb);
 #define QSA_LAUNCH_ATTN(T, N) cudaLaunchKernelEx(&cfg, attn_kernel<T, N>, d, items, cache0, n_past0, q, q_type, sel_ws, \
-                                                 nsel_ws, tiles_per_cta, max_chunks, part_o, part_ml, outs, status, state_out)
+                                                 nsel_ws, tiles_per_cta, max_chunks, part_o, part_ml, outs, status, sdst)
     if (d.type_k == QSA_TYPE_Q8_0) e = d.n_head_kv == 2 ? QSA_LAUNCH_ATTN(QSA_TYPE_Q8_0, 2) : QSA_LAUNCH_ATTN(QSA_TYPE_Q8_0, 1);
     else                           e = d.n_head_kv == 2 ? QSA_LAUNCH_ATTN(QSA_TYPE_F16, 2) : QSA_LAUNCH_ATTN(QSA_TYPE_F16, 1);
 #undef QSA_LAUNCH_ATTN
@@ -817,16 +819,16 @@ cudaError_t launch_attn(const DevDesc & d, cudaStream_t st, bool chained, int n_
         mc.blockDim = dim3(MERGE_SMALL_THREADS);
         mc.dynamicSmemBytes = 0;
         return cudaLaunchKernelEx(&mc, attn_merge_small_kernel, d, items, n_past0, nsel_ws, tiles_per_cta, max_chunks,
-                                  (const float *) part_o, (const float *) part_ml, outs, state_out);
+                                  (const float *) part_o, (const float *) part_ml, outs, sdst);
     }
     mc.gridDim = dim3((unsigned) n_q, HROWS, HEAD_DIM / (4 * MERGE_COLS));
     mc.blockDim = dim3(MERGE_THREADS);
     mc.dynamicSmemBytes = (size_t) max_chunks * 4;
     if (max_chunks > 2 * MERGE_GROUPS)
         return cudaLaunchKernelEx(&mc, attn_merge_kernel<16>, d, items, n_past0, nsel_ws, tiles_per_cta, max_chunks,
-                                  (const float *) part_o, (const float *) part_ml, outs, state_out);
+                                  (const float *) part_o, (const float *) part_ml, outs, sdst);
     return cudaLaunchKernelEx(&mc, attn_merge_kernel<2>, d, items, n_past0, nsel_ws, tiles_per_cta, max_chunks,
-                              (const float *) part_o, (const float *) part_ml, outs, state_out);
+                              (const float *) part_o, (const float *) part_ml, outs, sdst);
 }
 
 }  // namespace qsa

@@ -141,6 +141,27 @@ struct OutSpec {
     int z_bf16;
 };
 
+// Where a sharded decode's unnormalised states go: query t's state at base[p] + t x the state
+// floats, for every p < n (n = 0: no state, the output instead; n = 1: this rank's workspace; with
+// the NVLink peer exchange, this rank's slot in every rank's gather region, remote ones included).
+// The writers do not fence: the kernel that publishes the states waits for the writing grid to
+// complete (griddepcontrol.wait: its stores performed and visible to the waiting thread), and its
+// system-scope release of the flag carries them to the peers.  A fence in every writing thread
+// waited for its own NVLink acknowledgements and lengthened the merge from 24 to 42 us (batched).
+constexpr int MAX_STATE_DST = 8;
+struct StateDst {
+    float * base[MAX_STATE_DST];
+    int n;
+};
+__device__ __forceinline__ void state_put4(const StateDst & s, size_t off, float4 v) {
+    #pragma unroll 1
+    for (int p = 0; p < s.n; p++) *reinterpret_cast<float4 *>(s.base[p] + off) = v;
+}
+__device__ __forceinline__ void state_put(const StateDst & s, size_t off, float v) {
+    #pragma unroll 1
+    for (int p = 0; p < s.n; p++) s.base[p][off] = v;
+}
+
 // Four consecutive output values at element offset `off` (a multiple of 4).
 __device__ __forceinline__ void out_store4(const OutSpec & o, size_t off, float4 v) {
     if (o.out) *reinterpret_cast<float4 *>(o.out + off) = v;

@@ -51,7 +51,7 @@ DevDesc dev_desc(const qsa_desc * d);
 cudaError_t launch_attn(const DevDesc & d, cudaStream_t st, bool chained, int n_q, const qsa_decode_item * items,
         qsa_layer_cache cache0, int n_past0, const void * q, int q_type, const int * sel_ws, const int * nsel_ws,
         int tiles_per_cta, int max_chunks, float * part_o, float * part_ml, OutSpec outs, uint32_t * status,
-        float * state_out);
+        const StateDst & sdst);
 cudaError_t attn_set_attrs();
 // Cells per attention tile.
 int attn_tile_cells();
@@ -92,7 +92,13 @@ cudaError_t launch_proj_gemm_plain(cudaStream_t st, int T, int K, int N, const v
 cudaError_t launch_shard_select(const DevDesc & d, cudaStream_t st, const qsa_decode_item * items, int n_shards,
         int batch, const int * cand, size_t cand_stride, int blo, int bhi, int * sel_out, int * sel_ws, int * nsel_ws,
         uint32_t * status);
+// flags != null: first wait (bounded; DEV_TIMEOUT in status) until flags[0..n_parts) reach *epoch
+// (the peer exchange's publication), then read the states through L2.
 cudaError_t launch_merge_states(const DevDesc & d, cudaStream_t st, int n_parts, int batch, const float * states,
-        float * out);
+        float * out, const uint32_t * flags = nullptr, const uint32_t * epoch = nullptr, uint32_t * status = nullptr);
+// Publication of states stored into every rank's gather region (qsa_peer.cu): launched
+// programmatically behind the kernel that stored them, it advances *epoch and sets this rank's
+// flag in every region (flag[p], p < n) to it with a system-scope release.
+cudaError_t launch_peer_publish(cudaStream_t st, uint32_t * const * flag, int n, uint32_t * epoch);
 
 }  // namespace qsa

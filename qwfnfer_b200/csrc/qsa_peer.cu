@@ -92,6 +92,42 @@ __global__ void peer_wait_kernel(const void * __restrict__ local_buf, int n_rank
     __threadfence_system();
 }
 
+// Publication of states that the kernel ahead stored into every rank's region (StateDst with the
+// regions' slots of this rank): once that grid has completed (its stores performed), the channel's
+// next epoch goes into this rank's flag of every region with a system-scope release.
+struct PeerFlags {
+    uint32_t * flag[MAX_STATE_DST];
+};
+__global__ void peer_publish_kernel(PeerFlags f, int n, uint32_t * __restrict__ epoch) {
+    pdl_wait();                              // the grid that stored the states has completed
+    __shared__ uint32_t e;
+    if (threadIdx.x == 0) {
+        e = *epoch + 1;
+        *epoch = e;
+    }
+    __syncthreads();
+    if ((int) threadIdx.x < n) {
+        __threadfence_system();
+        st_release_sys(f.flag[threadIdx.x], e);
+    }
+}
+
+cudaError_t launch_peer_publish(cudaStream_t st, uint32_t * const * flag, int n, uint32_t * epoch) {
+    if (n <= 0 || n > MAX_STATE_DST) return cudaErrorInvalidValue;
+    PeerFlags f{};
+    for (int p = 0; p < n; p++) f.flag[p] = flag[p];
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(32);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;      // its launch overlaps the writer
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, peer_publish_kernel, f, n, epoch);
+}
+
 cudaError_t launch_peer_push(cudaStream_t st, void * const * bufs, int n_ranks, int rank, const void * src,
                              size_t slot_bytes, uint32_t * epoch, unsigned * counter) {
     // about 32 KB of peer stores per CTA

@@ -290,21 +290,48 @@ __global__ void __launch_bounds__(1024) shard_select_sort_kernel(DevDesc d, cons
 
 // out[t][h][d] from the gathered states [n_parts][batch][M 16 | L 16 | O 16x256], merged in rank
 // order: M = max_p m_p, out = sum_p 2^(m_p - M) O_p / sum_p 2^(m_p - M) l_p.
+// flags != null: the states were stored into this rank's region by every rank and published by
+// flag; each CTA first waits (bounded by 2 s of %globaltimer, then DEV_TIMEOUT, so the context
+// stays usable) until every flag has reached *epoch, and reads the states from L2.
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t * p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
 __global__ void __launch_bounds__(256) merge_states_kernel(DevDesc d, int n_parts, int batch,
-        const float * __restrict__ states, float * __restrict__ out) {
+        const float * states, float * __restrict__ out, const uint32_t * flags, const uint32_t * epoch,
+        uint32_t * status) {
     constexpr int ROWS = 16, SF = 2 * ROWS + ROWS * HEAD_DIM;
     const int t = blockIdx.x, hr = blockIdx.y, dim = threadIdx.x;
     const int g = hr >> 3, h = hr & 7;
     if (g >= d.n_head_kv || h >= d.gqa) return;
+    if (flags) {
+        if ((int) threadIdx.x < n_parts) {
+            const uint32_t e = *reinterpret_cast<const volatile uint32_t *>(epoch);
+            const uint32_t * f = flags + threadIdx.x;
+            // a flag at or past this round's epoch: the rank's states of this round have landed
+            if ((int32_t) (ld_acquire_sys_u32(f) - e) < 0) {
+                const uint64_t t0 = global_timer_ns();
+                while ((int32_t) (ld_acquire_sys_u32(f) - e) < 0) {
+                    if (global_timer_ns() - t0 > 2000000000ull) {
+                        set_status(status, DEV_TIMEOUT);
+                        break;
+                    }
+                }
+            }
+        }
+        __syncthreads();
+    }
+    auto ld = [&](size_t i) { return flags ? __ldcg(states + i) : states[i]; };
     float M = -INFINITY;
-    for (int p = 0; p < n_parts; p++) M = fmaxf(M, states[((size_t) p * batch + t) * SF + hr]);
+    for (int p = 0; p < n_parts; p++) M = fmaxf(M, ld(((size_t) p * batch + t) * SF + hr));
     const float Mu = M == -INFINITY ? 0.0f : M;
     float L = 0.0f, acc = 0.0f;
     for (int p = 0; p < n_parts; p++) {
-        const float * st = states + ((size_t) p * batch + t) * SF;
-        const float w = exp2f(st[hr] - Mu);
-        L += st[ROWS + hr] * w;
-        acc += st[2 * ROWS + hr * HEAD_DIM + dim] * w;
+        const size_t st = ((size_t) p * batch + t) * SF;
+        const float w = exp2f(ld(st + hr) - Mu);
+        L += ld(st + ROWS + hr) * w;
+        acc += ld(st + 2 * ROWS + (size_t) hr * HEAD_DIM + dim) * w;
     }
     out[((size_t) t * d.n_head + g * d.gqa + h) * HEAD_DIM + dim] = L > 0.0f ? acc / L : 0.0f;
 }
@@ -340,8 +367,9 @@ cudaError_t launch_shard_select(const DevDesc & d, cudaStream_t st, const qsa_de
 }
 
 cudaError_t launch_merge_states(const DevDesc & d, cudaStream_t st, int n_parts, int batch, const float * states,
-                                float * out) {
-    merge_states_kernel<<<dim3(batch, 16), HEAD_DIM, 0, st>>>(d, n_parts, batch, states, out);
+                                float * out, const uint32_t * flags, const uint32_t * epoch, uint32_t * status) {
+    if (flags && (!epoch || !status || n_parts > HEAD_DIM)) return cudaErrorInvalidValue;
+    merge_states_kernel<<<dim3(batch, 16), HEAD_DIM, 0, st>>>(d, n_parts, batch, states, out, flags, epoch, status);
     return cudaGetLastError();
 }
 

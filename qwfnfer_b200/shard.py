@@ -27,7 +27,7 @@ import ctypes
 import torch
 import torch.distributed as dist
 
-from ._abi import QsaDesc, QsaError, QsaLayerCache, TYPE_BF16, TYPE_F32, check, k_blocks, lib
+from ._abi import QsaDesc, QsaError, QsaLayerCache, QsaPeerSlots, TYPE_BF16, TYPE_F32, check, k_blocks, lib
 
 
 def shard_blocks(n_blocks: int, world: int, rank: int) -> tuple[int, int]:
@@ -101,6 +101,28 @@ class LibShardBackend:
                                         state.data_ptr(), _ptr(sel_out), ws.data_ptr(), ws.numel(), self._stream()),
               "qsa_shard_decode_ri")
         return state
+
+    def decode_ri_peer(self, items, batch: int, max_n_kv: int, blocks: tuple[int, int], q, q_idx, slots: QsaPeerSlots,
+                       k_new=None, v_new=None, kidx_new=None, sel_out: torch.Tensor | None = None) -> None:
+        """decode_ri whose state goes straight into slot `rank` of every rank's region of one peer
+        channel (`slots`), published there by a release flag: no push or wait launch."""
+        q_type = TYPE_BF16 if q.dtype == torch.bfloat16 else TYPE_F32
+        ws = self.workspace(batch, max_n_kv, blocks)
+        check(lib().qsa_shard_decode_ri_peer(ctypes.byref(self.desc), _ptr(items), batch, max_n_kv, blocks[0],
+                                             blocks[1], _ptr(q), q_type, _ptr(q_idx), _ptr(k_new), _ptr(v_new),
+                                             _ptr(kidx_new), ctypes.byref(slots), _ptr(sel_out), ws.data_ptr(),
+                                             ws.numel(), self._stream()), "qsa_shard_decode_ri_peer")
+
+    def merge_peer(self, slots: QsaPeerSlots, batch: int, status: torch.Tensor,
+                   out: torch.Tensor | None = None) -> torch.Tensor:
+        """Wait (bounded; the status word of `status`) for every rank's state of the round in this
+        rank's region of the channel, then merge them into out f32 [batch, n_head, head_dim]."""
+        d = self.desc
+        if out is None:
+            out = torch.empty((batch, d.n_head, d.head_dim), dtype=torch.float32, device=self.device)
+        check(lib().qsa_merge_states_peer(ctypes.byref(d), ctypes.byref(slots), batch, out.data_ptr(),
+                                          status.data_ptr(), status.numel(), self._stream()), "qsa_merge_states_peer")
+        return out
 
     def candidates(self, items, batch: int, max_n_kv: int, blocks: tuple[int, int], q_idx,
                    k_new=None, v_new=None, kidx_new=None, out: torch.Tensor | None = None) -> torch.Tensor:
@@ -182,9 +204,10 @@ class PeerExchange:
             check(L.qsa_ipc_open(hb, ctypes.byref(base)), "qsa_ipc_open")
             self._opened.append(base.value)
             bases.append(base.value + o)
-        # per channel, the device array of every rank's region address
-        self.ptrs = [torch.tensor([b + off_c for b in bases], dtype=torch.int64, device=self.device)
-                     for off_c in self.offsets]
+        # per channel, every rank's region address (host list, and a device array for the push)
+        self.regions = [[b + off_c for b in bases] for off_c in self.offsets]
+        self.ptrs = [torch.tensor(r, dtype=torch.int64, device=self.device) for r in self.regions]
+        self._slots: dict[int, QsaPeerSlots] = {}
         self.status = torch.zeros(64, dtype=torch.uint8, device=self.device)   # status word of the waits
         torch.cuda.synchronize(self.device)
         dist.barrier(group=group)
@@ -209,6 +232,20 @@ class PeerExchange:
             return flat.view((self.world,) + tuple(src.shape)), stride
         return flat, stride
 
+    def slots(self, channel: int) -> QsaPeerSlots:
+        """The channel as qsa_shard_decode_ri_peer / qsa_merge_states_peer see it (at most 8 ranks)."""
+        s = self._slots.get(channel)
+        if s is None:
+            if self.world > 8:
+                raise QsaError(1, "the fused peer exchange serves at most 8 ranks")
+            s = QsaPeerSlots()
+            for r, a in enumerate(self.regions[channel]):
+                s.region[r] = a
+            s.n_ranks, s.rank = self.world, self.rank
+            s.epoch = self.sync[channel].data_ptr()
+            self._slots[channel] = s
+        return s
+
     def check(self) -> int:
         return lib().qsa_check(self.status.data_ptr(), self.status.numel(),
                                torch.cuda.current_stream(self.device).cuda_stream)
@@ -226,8 +263,11 @@ class ShardedDecoder:
     def __init__(self, desc: QsaDesc, backend=None, group=None, rank: int | None = None,
                  world: int | None = None, exchange: str = "nccl", batch: int = 1, index: str = "sharded"):
         """exchange: "nccl" (all-gathers of the process group), "nccl_capi" (the whole step in libqsa's
-        qsa_decode_sharded with the process group's NCCL communicator) or "peer" (libqsa's
-        all-gather over NVLink peer memory, GPUs of one node; sized for `batch` queries per step).
+        qsa_decode_sharded with the process group's NCCL communicator), "peer" (libqsa's all-gather
+        over NVLink peer memory, GPUs of one node; sized for `batch` queries per step; with
+        replicated indexer caches and at most 8 ranks, the states are stored into the peers by the
+        attention itself and published by flag) or "peer_push" (the same buffers, every exchange by
+        a push and a wait launch).
         index: "sharded"
         (each rank holds its blocks' raw and pooled keys; candidates are exchanged) or "replicated"
         (every rank holds all of them, QsaState(index_full=True), and selects globally itself: one
@@ -258,7 +298,8 @@ class ShardedDecoder:
             self.comm = pg._get_backend(dev)._comm_ptr()
             if not self.comm:
                 raise QsaError(1, "no NCCL communicator behind the process group")
-        if exchange == "peer" and self.world > 1:
+        self.fused = exchange == "peer"
+        if exchange in ("peer", "peer_push") and self.world > 1:
             # Channels: 0 candidates, 1 and 2 states.  A push overwrites the peers' slots without
             # waiting for them to finish reading the last round, so consecutive pushes into one
             # channel are always separated by a wait on another: the sharded-index step alternates
@@ -304,10 +345,19 @@ class ShardedDecoder:
         if self.comm:
             return self._step_capi(items, batch, max_n_kv, q, q_idx, k_new, v_new, kidx_new, sel_out, out)
         if self.index_replicated:
-            state = self.backend.decode_ri(items, batch, max_n_kv, self.blocks, q, q_idx, k_new, v_new, kidx_new,
-                                           sel_out=sel_out)
             channel = 1 + (self._steps & 1)
             self._steps += 1
+            if self.peer is not None and self.fused and self.world <= 8:
+                # the attention stores the state into every rank's region itself and publishes it;
+                # the merge waits for the flags (no push or wait launch)
+                if batch * self.backend.state_floats * 4 != self.peer.slot[channel]:
+                    raise QsaError(1, "batch differs from the one the peer exchange was sized for")
+                slots = self.peer.slots(channel)
+                self.backend.decode_ri_peer(items, batch, max_n_kv, self.blocks, q, q_idx, slots, k_new, v_new,
+                                            kidx_new, sel_out=sel_out)
+                return self.backend.merge_peer(slots, batch, self.peer.status, out)
+            state = self.backend.decode_ri(items, batch, max_n_kv, self.blocks, q, q_idx, k_new, v_new, kidx_new,
+                                           sel_out=sel_out)
             states, _ = self._all_gather(state, channel)
             return self.backend.merge(states.view(self.world, batch, -1), out)
         cand = self.backend.candidates(items, batch, max_n_kv, self.blocks, q_idx, k_new, v_new, kidx_new)

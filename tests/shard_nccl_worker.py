@@ -12,10 +12,11 @@ unsharded caches on its GPU and runs qsa_decode on them; every rank's output and
 gathered to rank 0 and compared with it.  Rank 0 prints one line `SHARD_NCCL {...}`; the exit
 code is 0 only if every check passed.
 
-With `delay`, the step runs three times back to back and the last rank's host sleeps between
-launching each peer push and the wait behind it, so the other ranks publish later rounds while
-its wait has not been launched yet: the exchange must neither time out nor let a later round's
-push overwrite slots still being read (every step's output is checked).
+With `delay`, the step runs three times back to back and the last rank's host sleeps before
+launching each wait for the peers (the wait of a push, or the state merge that waits for the
+states the other ranks' kernels stored into its region), so the other ranks publish later rounds
+while its wait has not been launched yet: the exchange must neither time out nor let a later
+round overwrite slots still being read (every step's output is checked).
 """
 from __future__ import annotations
 
@@ -40,14 +41,14 @@ ATTN_TOL = 2e-3
 
 
 def _delay_waits(peer, seconds):
-    """Make this rank's host sleep between launching each push and its wait."""
+    """Make this rank's host sleep before launching each wait for the peers."""
     import qwfnfer_b200.shard as shard_mod
     real = shard_mod.lib
 
     class Slow:
         def __getattr__(self, name):
             fn = getattr(real(), name)
-            if name != "qsa_peer_wait":
+            if name not in ("qsa_peer_wait", "qsa_merge_states_peer"):
                 return fn
 
             def wait(*a):
