@@ -153,13 +153,17 @@ struct StateDst {
     float * base[MAX_STATE_DST];
     int n;
 };
+// (unrolled over the fixed slots: a runtime index into the kernel parameter would copy it to the
+// stack)
 __device__ __forceinline__ void state_put4(const StateDst & s, size_t off, float4 v) {
-    #pragma unroll 1
-    for (int p = 0; p < s.n; p++) *reinterpret_cast<float4 *>(s.base[p] + off) = v;
+    #pragma unroll
+    for (int p = 0; p < MAX_STATE_DST; p++)
+        if (p < s.n) *reinterpret_cast<float4 *>(s.base[p] + off) = v;
 }
 __device__ __forceinline__ void state_put(const StateDst & s, size_t off, float v) {
-    #pragma unroll 1
-    for (int p = 0; p < s.n; p++) s.base[p][off] = v;
+    #pragma unroll
+    for (int p = 0; p < MAX_STATE_DST; p++)
+        if (p < s.n) s.base[p][off] = v;
 }
 
 // Four consecutive output values at element offset `off` (a multiple of 4).
