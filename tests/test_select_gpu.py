@@ -128,3 +128,36 @@ def test_cut_inside_one_exponent():
     rows[:, 0] = rng.uniform(1.0, 1.99, n_blocks)
     sc, _ = _run(n_blocks, _f16(rows), q_idx=q)
     assert np.all((sc[:n_blocks - 3] >= 1) & (sc[:n_blocks - 3] < 2))
+
+
+def test_batch_of_long_queries():
+    """Eight queries at different positions over one long cache: the batch's scoring grid (18
+    CTAs of 448 blocks per query, in one wave) and eight selecting CTAs; each query's selection
+    equals the oracle's."""
+    n_blocks, B = 9000, 8
+    rng = np.random.default_rng(11)
+    rows = _f16(rng.normal(0, 1.012 / 8, (n_blocks, 128)))
+    n_ctx = 64 * (n_blocks + 2)
+    d = make_desc(n_ctx=n_ctx, top_k_blocks=64, window=128)
+    pool = torch.zeros(n_ctx // 64, d.idx_dim, dtype=torch.int16, device="cuda")
+    pool[:n_blocks] = torch.from_numpy(rows.view(np.int16)).cuda()
+    positions = [64 * (n_blocks - 37 * i) - 1 for i in range(B)]
+    q_idx = rng.normal(0, 1.0, (B, 1, d.idx_dim)).astype(np.float32)
+    node = QsaNode(d)
+    c = QsaLayerCache()
+    c.pool = pool.data_ptr()
+    c.k = c.v = c.idx = pool.data_ptr()
+    items = decode_items([c] * B, positions)
+    max_n_kv = max(positions) + 1
+    ws = node.workspace("decode", B, max_n_kv)
+    sel = torch.full((B, k_blocks(d)), -7, dtype=torch.int32, device="cuda")
+    qd = torch.from_numpy(q_idx).cuda()
+    check(lib().qsa_decode_select(ctypes.byref(d), items.data_ptr(), B, max_n_kv, qd.data_ptr(), sel.data_ptr(),
+                                  ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream), "select")
+    assert node.check(ws) == QSA_OK
+    got = sel.cpu().numpy()
+    for i, q_pos in enumerate(positions):
+        nb = (q_pos + 1) // 64
+        sc = oracle.scores(d, rows[:nb].view(np.uint16), nb, q_idx[i, 0])[0]
+        want, _ = oracle.select(d, sc, q_pos)
+        assert np.array_equal(got[i], want), f"query {i}"
