@@ -11,6 +11,10 @@
 //   qsa_peer_wait: spin (bounded: 2 s of %globaltimer, then DEV_TIMEOUT in the status word) until
 //     every flag of this rank's buffer carries the current epoch; kernels launched after it read
 //     the gathered slots.
+//   qsa_shard_decode_ri_peer's publication (peer_publish_kernel): the attention (or its merge)
+//     has stored this rank's states into slot `rank` of every buffer itself; once that grid has
+//     completed, one warp advances the epoch and sets flag[rank] in every buffer with a
+//     system-scope release, and qsa_merge_states_peer waits for the flags.
 // No multicast and no NVLS: only ordinary stores to peer memory and loads of local memory.
 #include <cstring>
 
