@@ -655,15 +655,15 @@ qsa_status qsa_shard_decode_ri_peer(const qsa_desc * dd, const qsa_decode_item *
                                     const float * k_new, const float * v_new, const float * kidx_new,
                                     const qsa_peer_slots * slots, int32_t * sel_out, void * ws, size_t ws_bytes,
                                     qsa_stream_t stream) {
+    StateDst sd;
+    uint32_t * flag[MAX_STATE_DST];
+    size_t stride = 0;
+    if (batch <= 0 || !peer_targets(slots, batch, sd, flag, stride)) return QSA_ERR_INVALID;
+    if (!q || !q_idx || (q_type != QSA_TYPE_BF16 && q_type != QSA_TYPE_F32)) return QSA_ERR_INVALID;
     DevDesc d; WsLayout w;
     qsa_status s = shard_common(dd, items, batch, max_n_kv, blk_lo, blk_hi, ws, ws_bytes, d, w);
     if (s != QSA_OK) return s;
     d.shard_ri = 1;
-    StateDst sd;
-    uint32_t * flag[MAX_STATE_DST];
-    size_t stride = 0;
-    if (!peer_targets(slots, batch, sd, flag, stride)) return QSA_ERR_INVALID;
-    if (!q || !q_idx || (q_type != QSA_TYPE_BF16 && q_type != QSA_TYPE_F32)) return QSA_ERR_INVALID;
     const bool any_new = k_new || v_new || kidx_new;
     if (any_new && !(k_new && v_new && kidx_new)) return QSA_ERR_INVALID;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);

@@ -71,6 +71,11 @@ def test_struct_layouts_match_header():
     assert _abi.QsaDesc.placement.offset == 80
 
 
+def test_peer_slots_layout():
+    assert ctypes.sizeof(_abi.QsaPeerSlots) == 8 * 8 + 4 + 4 + 8
+    assert _abi.QsaPeerSlots.epoch.offset == 72
+
+
 def test_front_weights_layout():
     assert ctypes.sizeof(_abi.QsaFrontWeights) == 8 * 8 + 2 * 4
     assert _abi.QsaFrontWeights.n_embd.offset == 64
@@ -129,3 +134,30 @@ def test_stage_copy_host_refusals():
     assert L.qsa_stage_copy(A, A, 20, None) == _abi.QSA_ERR_INVALID          # not a multiple of 16 bytes
     assert L.qsa_stage_copy(A + 8, A, 16, None) == _abi.QSA_ERR_INVALID      # misaligned
     assert L.qsa_stage_copy(A, A, 0, None) == _abi.QSA_ERR_INVALID
+
+
+def _slots(n=2, rank=0, epoch=A, regions=None):
+    s = _abi.QsaPeerSlots()
+    for r in range(min(n, 8)):
+        s.region[r] = regions[r] if regions else A + r * (1 << 24)
+    s.n_ranks, s.rank, s.epoch = n, rank, epoch
+    return s
+
+
+def test_fused_peer_exchange_host_refusals():
+    """qsa_shard_decode_ri_peer / qsa_merge_states_peer refuse bad channel descriptions on the host:
+    more than 8 ranks, a rank outside them, no epoch word, a region off 16 bytes; and the merge a
+    batch of 0 or a status word under 16 bytes."""
+    d = make_desc(n_ctx=4096)
+    L = lib()
+    dec = lambda s, batch=1: L.qsa_shard_decode_ri_peer(ctypes.byref(d), A, batch, 4096, 0, 32, A, _abi.TYPE_BF16, A,
+                                                        None, None, None, ctypes.byref(s), None, A, 1 << 30, None)
+    mrg = lambda s, batch=1, ws_bytes=64: L.qsa_merge_states_peer(ctypes.byref(d), ctypes.byref(s), batch, A, A,
+                                                                  ws_bytes, None)
+    for bad in (_slots(n=9), _slots(n=0), _slots(rank=2), _slots(rank=-1), _slots(epoch=None),
+                _slots(regions=[A, A + 4])):
+        assert dec(bad) == _abi.QSA_ERR_INVALID
+        assert mrg(bad) == _abi.QSA_ERR_INVALID
+    assert dec(_slots(), batch=0) == _abi.QSA_ERR_INVALID
+    assert mrg(_slots(), batch=0) == _abi.QSA_ERR_INVALID
+    assert mrg(_slots(), ws_bytes=8) == _abi.QSA_ERR_WORKSPACE
