@@ -14,8 +14,9 @@ T tokens at N_PAST of a q8_0 cache and runs the whole chunk (T=4096 at 77824 kee
 with about 2.5 GB on the device).  Each step is preceded by a 256 MB L2 flush; the device time of every step is printed.
 `front` projects T tokens through the layer's 48.5 MB of bf16 projection weights (the config-2 descriptor), each
 step after the 256 MB L2 flush, so the weights come from DRAM.
-`shard5` replays the config-5 sharded decode step (one layer after another, or with `lb` the 12 layers as one batch;
-`ri`: indexer caches replicated)
+`shard5` replays the config-5 sharded decode step (one layer after another, or with `lb` the 12 layers as one batch,
+captured twice per replay so that the state exchange's two channels alternate; `ri`: indexer caches replicated;
+exchange `peer` (states stored by the attention into every rank's buffer), `peer_push` or `nccl`)
 from a CUDA graph under torch.profiler and prints, per rank, each kernel's median start offset and duration within
 the step (CUPTI activity records; a breakdown, not a bench value).
 """
