@@ -21,8 +21,12 @@
 //     multiplies the f32 partial dot of each 32-dim group, the V scale multiplies P;
 //   - online softmax in the exp2 domain with warp shuffles; the two cell halves of a KV head
 //     merge in shared memory; a query split over several CTAs leaves one unnormalised partial per CTA in
-//     the workspace, merged by attn_merge_kernel (launched programmatically behind the
-//     attention grid, it waits for it with griddepcontrol.wait).
+//     the workspace, merged by attn_merge_kernel, or attn_merge_small_kernel when no query has more
+//     than 8 partials (launched programmatically behind the attention grid, they wait for it with
+//     griddepcontrol.wait);
+//   - sharded decode: the result is the unnormalised state (M, L, O) instead of the output, stored
+//     to every destination of a StateDst (this rank's workspace, or its slot in every rank's
+//     gather region over NVLink, published afterwards by peer_publish_kernel).
 #include "qsa_kernels.cuh"
 
 namespace qsa {
