@@ -8,6 +8,9 @@
 // a radix select over the gathered scores, one warp per query);
 // each rank attends its own selected blocks into an unnormalised state (attn_kernel, state mode);
 // the states are all-gathered and merge_states_kernel combines them by log-sum-exp in rank order.
+// With the indexer caches replicated every rank selects globally itself, and the fused peer
+// exchange has the attention store the states into every rank's region; merge_states_kernel then
+// waits for the ranks' flags before it reads them.
 #include "qsa_kernels.cuh"
 
 namespace qsa {
