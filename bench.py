@@ -50,7 +50,7 @@ def peaks():
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the config-2 decode
 # attention, from one ncu capture of this kernel (not measured by this run; the capture's command
 # and figures are in profiles/attn_decode_config2.md).
-ATTN_CONFIG2_NCU_TRAFFIC = 4706560
+ATTN_CONFIG2_NCU_TRAFFIC = 4716288
 
 
 NVML_SAMPLER = r"""
