@@ -810,6 +810,11 @@ cudaError_t launch_attn(const DevDesc & d, cudaStream_t st, bool chained, int n_
     cfg.numAttrs = chained ? 1 : 0;     // the first kernel of a call waits for all earlier work
     cudaError_t e;
     cfg.dynamicSmemBytes = d.type_k == QSA_TYPE_Q8_0 ? attn_smem_bytes<QSA_TYPE_Q8_0>(d.kb) : attn_smem_bytes<QSA_TYPE_F16>(d.kb);
+    // A grid of at most one CTA per SM asks for the most shared memory the kernel allows, so that no
+    // SM takes two of its CTAs: launched behind the selection, whose CTAs hold most SMs, two q8_0
+    // CTAs would otherwise pair up on the SMs that come free first.
+    if ((int64_t) max_chunks * n_q <= 148 && d.type_k == QSA_TYPE_Q8_0)
+        cfg.dynamicSmemBytes = attn_smem_bytes<QSA_TYPE_Q8_0>(MAX_KB);
 #define QSA_LAUNCH_ATTN(T, N) cudaLaunchKernelEx(&cfg, attn_kernel<T, N>, d, items, cache0, n_past0, q, q_type, sel_ws, \
                                                  nsel_ws, tiles_per_cta, max_chunks, part_o, part_ml, outs, status, sdst)
     if (d.type_k == QSA_TYPE_Q8_0) e = d.n_head_kv == 2 ? QSA_LAUNCH_ATTN(QSA_TYPE_Q8_0, 2) : QSA_LAUNCH_ATTN(QSA_TYPE_Q8_0, 1);
